@@ -1,0 +1,1180 @@
+// Decode-step kernels and the model runtime behind the runner seam.
+//
+// One decode step of one sequence slot is a chain of kernels launched with
+// programmatic dependent launch (PDL) and captured once into a CUDA graph:
+//   embed -> [qkv+head-norm+RoPE+KV append -> attention -> o_proj+residual
+//             -> post-norm+gate/up+SwiGLU -> down+residual] x layers
+//   -> final-norm+LM head+argmax (or a position advance during prefill)
+// Each kernel prefetches its weight slice into L2 before it waits on the
+// previous kernel, so weight traffic overlaps the dependency.  Position,
+// token and score live in device memory, so successive replays feed the
+// argmax back without a host round trip.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <cmath>
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "q4_gemv.cuh"
+#include "q4gpu_internal.h"
+
+namespace q4 {
+
+// ---------------------------------------------------------------------------
+// Device-side views
+// ---------------------------------------------------------------------------
+struct KvView {
+  int32_t* pool;         // [n_pages][layers][2][8][64][128] int32
+  const int32_t* pages;  // this slot's page table: logical page -> physical page
+  int64_t page_elems;    // layers * 2 * 8 * 64 * 128
+  __device__ __forceinline__ int32_t* at(int layer, int kind, int head, int pos) const {
+    return pool + (int64_t)pages[pos >> 6] * page_elems +
+           ((((int64_t)layer * 2 + kind) * kKvHeads + head) * kKvPage + (pos & (kKvPage - 1))) * kHeadDim;
+  }
+};
+
+struct ArgBestD {
+  int64_t score;
+  int32_t idx;
+  int32_t pad;
+};
+
+struct SlotState {
+  int32_t* pos;     // [1] position of the next step
+  int32_t* tokens;  // [max_ctx + 1] input token per position; argmax written at pos+1
+  int64_t* scores;  // [max_ctx + 1]
+  int32_t* hidden;  // [1024] Q14.10 layer input / output
+  int32_t* qrope;   // [2048] Q12.12
+  int32_t* attn;    // [2048] Q12.12
+  int32_t* post;    // [1024] Q14.10
+  int32_t* mlp;     // [3072] Q12.12
+  ArgBestD* lm_partial;
+  unsigned int* lm_counter;
+  KvView kv;
+};
+
+struct LayerW {
+  const uint8_t* wqkv;  // [4096, 512]: q rows 0..2047, k 2048..3071, v 3072..4095
+  const uint16_t* sqkv;
+  const uint8_t* wo;  // [1024, 1024]
+  const uint16_t* so;
+  const uint8_t* wgate;  // [3072, 512]
+  const uint16_t* sgate;
+  const uint8_t* wup;
+  const uint16_t* sup;
+  const uint8_t* wdown;  // [1024, 1536]
+  const uint16_t* sdown;
+  const int32_t* g_in;
+  const int32_t* g_post;
+  const int32_t* g_q;
+  const int32_t* g_k;
+};
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Hidden-size RMSNorm of `src` (Q14.10) into `dst` (Q12.12), block-wide.
+__device__ __forceinline__ void hidden_norm_to(const int32_t* __restrict__ src, const int32_t* __restrict__ gamma,
+                                               int32_t* dst, int64_t* red) {
+  int64_t ss = 0;
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    const int32_t v = src[i];
+    dst[i] = v;
+    ss += (int64_t)v * v;
+  }
+  ss = block_sum_i64(ss, red);
+  const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) dst[i] = norm_apply(dst[i], inv, gamma[i], kHiddenNorm);
+}
+
+// ---------------------------------------------------------------------------
+// Step kernels
+// ---------------------------------------------------------------------------
+__global__ void embed_step_kernel(SlotState st, const uint8_t* __restrict__ W, const uint16_t* __restrict__ S) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int t = st.tokens[*st.pos];
+  const uint8_t* row = W + (size_t)t * (kHidden / 2);
+  const uint16_t* sc = S + (size_t)t * (kHidden / kGroup);
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    const uint8_t b = row[i >> 1];
+    const int q = (int)((i & 1) ? (b >> 4) : (b & 0xF));
+    st.hidden[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
+  }
+}
+
+// One CTA per head: 16 q heads, 8 k heads, 8 v heads (128 rows each).
+__global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, int layer,
+                                                       const int32_t* __restrict__ cos_tab,
+                                                       const int32_t* __restrict__ sin_tab) {
+  __shared__ __align__(16) int32_t a[kHidden];
+  __shared__ __align__(16) uint32_t limbs[limb_words(kHidden)];
+  __shared__ int64_t bias8[kHidden / 32];
+  __shared__ int64_t red[8];
+  __shared__ int32_t y[kHeadDim], z[kHeadDim];
+  const int head = blockIdx.x;
+  const int row0 = head * kHeadDim;
+  if (threadIdx.x == 0) {
+    prefetch_l2(w.wqkv + (size_t)row0 * 512, kHeadDim * 512);
+    prefetch_l2(w.sqkv + (size_t)row0 * 16, kHeadDim * 32);
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  hidden_norm_to(st.hidden, w.g_in, a, red);
+  __syncthreads();
+  stage_limbs(a, kHidden, limbs, bias8);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    int64_t acc[4] = {0, 0, 0, 0};
+    const int r0 = warp * 16 + pass * 4;
+    gemv_slice<kHidden, 4>(w.wqkv, w.sqkv, row0 + r0, kQRows + 2 * kKvRows, 0, limbs, bias8, acc);
+    warp_reduce_rows<4>(acc);
+    if (lane < 4) y[r0 + lane] = sat24(acc[lane] >> 14);
+  }
+  __syncthreads();
+  const int pos = *st.pos;
+  const int d = threadIdx.x;
+  if (head < kQHeads + kKvHeads) {
+    const int32_t* gamma = head < kQHeads ? w.g_q : w.g_k;
+    int64_t ss = d < kHeadDim ? (int64_t)y[d] * y[d] : 0;
+    ss = block_sum_i64(ss, red);
+    const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
+    if (d < kHeadDim) z[d] = norm_apply(y[d], inv, gamma[d], kHeadNorm);
+    __syncthreads();
+    if (d < kHeadDim) {
+      const int64_t rot = d < 64 ? -(int64_t)z[d + 64] : (int64_t)z[d - 64];
+      const int32_t r = sat24(((int64_t)z[d] * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
+      if (head < kQHeads)
+        st.qrope[head * kHeadDim + d] = r;
+      else
+        st.kv.at(layer, 0, head - kQHeads, pos)[d] = r;
+    }
+  } else if (d < kHeadDim) {
+    st.kv.at(layer, 1, head - kQHeads - kKvHeads, pos)[d] = y[d];
+  }
+}
+
+// One CTA per KV head (its two query heads) of one slot.  Exact two-pass
+// softmax: scores of every position are kept in shared memory, then the
+// row max, the LUT index, exp sum, per-index probabilities and sum(prob*v).
+__global__ void __launch_bounds__(256) attn_step_kernel(SlotState st, int layer, const int32_t* __restrict__ exp_lut,
+                                                        int64_t scale_q0_31) {
+  extern __shared__ int64_t sc[];  // [2][ctx] scores, then LUT indices
+  __shared__ int32_t q[2][kHeadDim];
+  __shared__ uint64_t probtab[2][kExpLut];
+  __shared__ int64_t red[8];
+  __shared__ int64_t half_acc[2][kHeadDim];
+  const int kv = blockIdx.x;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int ctx = *st.pos + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int i = threadIdx.x; i < 2 * kHeadDim; i += blockDim.x) q[i / kHeadDim][i % kHeadDim] = st.qrope[2 * kv * kHeadDim + i];
+  __syncthreads();
+  for (int p = warp; p < ctx; p += nw) {
+    const int4 k4 = reinterpret_cast<const int4*>(st.kv.at(layer, 0, kv, p))[lane];
+    const int d = lane * 4;
+    int64_t s0 = (int64_t)q[0][d] * k4.x + (int64_t)q[0][d + 1] * k4.y + (int64_t)q[0][d + 2] * k4.z +
+                 (int64_t)q[0][d + 3] * k4.w;
+    int64_t s1 = (int64_t)q[1][d] * k4.x + (int64_t)q[1][d + 1] * k4.y + (int64_t)q[1][d + 2] * k4.z +
+                 (int64_t)q[1][d + 3] * k4.w;
+    s0 = warp_sum_i64(s0);
+    s1 = warp_sum_i64(s1);
+    if (lane == 0) {
+      sc[p] = scale_score(s0, scale_q0_31);
+      sc[ctx + p] = scale_score(s1, scale_q0_31);
+    }
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int h = 0; h < 2; ++h) {
+    int64_t* s = sc + h * ctx;
+    int64_t mx = INT64_MIN;
+    for (int p = threadIdx.x; p < ctx; p += blockDim.x) mx = s[p] > mx ? s[p] : mx;
+    mx = block_max_i64(mx, red);
+    int64_t sum = 0;
+    for (int p = threadIdx.x; p < ctx; p += blockDim.x) {
+      const int ix = lut_index(mx, s[p]);
+      s[p] = ix;
+      sum += exp_lut[ix];
+    }
+    sum = block_sum_i64(sum, red);
+    for (int i = threadIdx.x; i < kExpLut; i += blockDim.x) probtab[h][i] = ((uint64_t)exp_lut[i] << 16) / (uint64_t)sum;
+  }
+  __syncthreads();
+  const int d = threadIdx.x & (kHeadDim - 1);
+  const int par = threadIdx.x >> 7;  // 0 or 1: even / odd positions
+  int64_t acc0 = 0, acc1 = 0;
+  for (int p = par; p < ctx; p += 2) {
+    const int64_t v = st.kv.at(layer, 1, kv, p)[d];
+    acc0 += (int64_t)probtab[0][sc[p]] * v;
+    acc1 += (int64_t)probtab[1][sc[ctx + p]] * v;
+  }
+  if (par == 1) {
+    half_acc[0][d] = acc0;
+    half_acc[1][d] = acc1;
+  }
+  __syncthreads();
+  if (par == 0) {
+    acc0 += half_acc[0][d];
+    acc1 += half_acc[1][d];
+    st.attn[(2 * kv) * kHeadDim + d] = sat24(acc0 >> 16);
+    st.attn[(2 * kv + 1) * kHeadDim + d] = sat24(acc1 >> 16);
+  }
+}
+
+// o_proj (K = 2048) + residual: post = sat24(hidden + (sat24(q26 >> 14) >> 2)).
+// 8 warps = 2 K-slices x 4 row groups of 2 rows -> 8 rows per CTA.
+__global__ void __launch_bounds__(256) oproj_step_kernel(SlotState st, LayerW w) {
+  constexpr int K = 2 * kHidden, R = 2, RPB = 8;
+  __shared__ __align__(16) int32_t a[K];
+  __shared__ __align__(16) uint32_t limbs[limb_words(K)];
+  __shared__ int64_t bias8[K / 32];
+  __shared__ int64_t part[2][RPB];
+  const int row0 = blockIdx.x * RPB;
+  if (threadIdx.x == 0) {
+    prefetch_l2(w.wo + (size_t)row0 * (K / 2), RPB * (K / 2));
+    prefetch_l2(w.so + (size_t)row0 * (K / 64), RPB * (K / 64) * 2);
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  for (int i = threadIdx.x; i < K; i += blockDim.x) a[i] = st.attn[i];
+  __syncthreads();
+  stage_limbs(a, K, limbs, bias8);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = warp & 1, rg = warp >> 1;
+  int64_t acc[R] = {0, 0};
+  gemv_slice<K, R>(w.wo, w.so, row0 + rg * R, kHidden, ks, limbs, bias8, acc);
+  warp_reduce_rows<R>(acc);
+  if (lane < R) part[ks][rg * R + lane] = acc[lane];
+  __syncthreads();
+  if (threadIdx.x < RPB) {
+    const int r = row0 + threadIdx.x;
+    const int32_t o = sat24((part[0][threadIdx.x] + part[1][threadIdx.x]) >> 14);
+    st.post[r] = sat24((int64_t)st.hidden[r] + (o >> 2));
+  }
+}
+
+// post-attention norm + gate/up + SwiGLU.  CTA: gate rows [r0, r0+16) by
+// warps 0-3 and up rows [r0, r0+16) by warps 4-7.
+__global__ void __launch_bounds__(256) gateup_step_kernel(SlotState st, LayerW w, const int32_t* __restrict__ sig_lut) {
+  constexpr int R = 4, RPB = 16;
+  __shared__ __align__(16) int32_t a[kHidden];
+  __shared__ __align__(16) uint32_t limbs[limb_words(kHidden)];
+  __shared__ int64_t bias8[kHidden / 32];
+  __shared__ int64_t red[8];
+  __shared__ int32_t gu[2][RPB];
+  const int row0 = blockIdx.x * RPB;
+  if (threadIdx.x == 0) {
+    prefetch_l2(w.wgate + (size_t)row0 * 512, RPB * 512);
+    prefetch_l2(w.wup + (size_t)row0 * 512, RPB * 512);
+    prefetch_l2(w.sgate + (size_t)row0 * 16, RPB * 32);
+    prefetch_l2(w.sup + (size_t)row0 * 16, RPB * 32);
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  hidden_norm_to(st.post, w.g_post, a, red);
+  __syncthreads();
+  stage_limbs(a, kHidden, limbs, bias8);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int which = warp >> 2;
+  int64_t acc[R] = {0, 0, 0, 0};
+  gemv_slice<kHidden, R>(which ? w.wup : w.wgate, which ? w.sup : w.sgate, row0 + (warp & 3) * R, kInter, 0, limbs,
+                         bias8, acc);
+  warp_reduce_rows<R>(acc);
+  if (lane < R) gu[which][(warp & 3) * R + lane] = sat24(acc[lane] >> 14);
+  __syncthreads();
+  if (threadIdx.x < RPB) {
+    const int32_t g = gu[0][threadIdx.x], u = gu[1][threadIdx.x];
+    const int32_t gc = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
+    int ix = (gc + 32768 + 32) >> 6;
+    ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
+    const int32_t silu = sat24(((int64_t)g * sig_lut[ix]) >> 16);
+    st.mlp[row0 + threadIdx.x] = sat24(((int64_t)silu * u) >> 12);
+  }
+}
+
+// down (K = 3072) + residual: hidden = sat24(post + (sat24(q26 >> 14) >> 2)).
+// 6 warps = 3 K-slices x 2 row groups of 4 rows -> 8 rows per CTA.
+__global__ void __launch_bounds__(192) down_step_kernel(SlotState st, LayerW w) {
+  constexpr int K = kInter, R = 4, RPB = 8;
+  __shared__ __align__(16) int32_t a[K];
+  __shared__ __align__(16) uint32_t limbs[limb_words(K)];
+  __shared__ int64_t bias8[K / 32];
+  __shared__ int64_t part[3][RPB];
+  const int row0 = blockIdx.x * RPB;
+  if (threadIdx.x == 0) {
+    prefetch_l2(w.wdown + (size_t)row0 * (K / 2), RPB * (K / 2));
+    prefetch_l2(w.sdown + (size_t)row0 * (K / 64), RPB * (K / 64) * 2);
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  for (int i = threadIdx.x; i < K; i += blockDim.x) a[i] = st.mlp[i];
+  __syncthreads();
+  stage_limbs(a, K, limbs, bias8);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = warp % 3, rg = warp / 3;
+  int64_t acc[R] = {0, 0, 0, 0};
+  gemv_slice<K, R>(w.wdown, w.sdown, row0 + rg * R, kHidden, ks, limbs, bias8, acc);
+  warp_reduce_rows<R>(acc);
+  if (lane < R) part[ks][rg * R + lane] = acc[lane];
+  __syncthreads();
+  if (threadIdx.x < RPB) {
+    const int r = row0 + threadIdx.x;
+    const int32_t dn = sat24((part[0][threadIdx.x] + part[1][threadIdx.x] + part[2][threadIdx.x]) >> 14);
+    st.hidden[r] = sat24((int64_t)st.post[r] + (dn >> 2));
+  }
+}
+
+__device__ __forceinline__ bool better_d(int64_t s, int32_t i, int64_t bs, int32_t bi) {
+  return s > bs || (s == bs && i < bi);
+}
+
+// Final norm + tied LM head + exact argmax; writes tokens[pos+1],
+// scores[pos+1] and advances pos.  Persistent grid over row blocks.
+__global__ void __launch_bounds__(256) lmhead_step_kernel(SlotState st, const uint8_t* __restrict__ W,
+                                                          const uint16_t* __restrict__ S, int rows,
+                                                          const int32_t* __restrict__ g_final) {
+  constexpr int R = 4;
+  __shared__ __align__(16) int32_t a[kHidden];
+  __shared__ __align__(16) uint32_t limbs[limb_words(kHidden)];
+  __shared__ int64_t bias8[kHidden / 32];
+  __shared__ int64_t red[8];
+  __shared__ ArgBestD wbest[8];
+  __shared__ bool last;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int pos = *st.pos;
+  hidden_norm_to(st.hidden, g_final, a, red);
+  __syncthreads();
+  stage_limbs(a, kHidden, limbs, bias8);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int64_t best_s = INT64_MIN;
+  int32_t best_i = INT32_MAX;
+  for (int base = (blockIdx.x * nw + warp) * R; base < rows; base += gridDim.x * nw * R) {
+    int64_t acc[R] = {0, 0, 0, 0};
+    gemv_slice<kHidden, R>(W, S, base, rows, 0, limbs, bias8, acc);
+    warp_reduce_rows<R>(acc);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (base + r < rows && acc[r] > best_s) {
+        best_s = acc[r];
+        best_i = base + r;
+      }
+  }
+  if ((threadIdx.x & 31) == 0) wbest[warp] = ArgBestD{best_s, best_i, 0};
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ArgBestD b = wbest[0];
+    for (int i = 1; i < nw; ++i)
+      if (better_d(wbest[i].score, wbest[i].idx, b.score, b.idx)) b = wbest[i];
+    st.lm_partial[blockIdx.x] = b;
+    __threadfence();
+    last = atomicAdd(st.lm_counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    ArgBestD b = st.lm_partial[0];
+    for (int i = 1; i < (int)gridDim.x; ++i) {
+      const ArgBestD c{*((volatile int64_t*)&st.lm_partial[i].score), *((volatile int32_t*)&st.lm_partial[i].idx), 0};
+      if (better_d(c.score, c.idx, b.score, b.idx)) b = c;
+    }
+    st.tokens[pos + 1] = b.idx;
+    st.scores[pos + 1] = b.score;
+    *st.pos = pos + 1;
+    *st.lm_counter = 0;
+  }
+}
+
+__global__ void advance_step_kernel(SlotState st) {
+  grid_dep_wait();
+  grid_dep_launch();
+  if (threadIdx.x == 0) *st.pos += 1;
+}
+
+// Scatter a KV pool page range to/from the reference order [pos][head][128].
+__global__ void kv_copy_kernel(KvView kv, int layer, int kind, int positions, int32_t* flat, int to_pool) {
+  const int p = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  if (p >= positions) return;
+  int32_t* slot = kv.at(layer, kind, h, p) + d;
+  int32_t* f = flat + ((size_t)p * kKvHeads + h) * kHeadDim + d;
+  if (to_pool)
+    *slot = *f;
+  else
+    *f = *slot;
+}
+
+}  // namespace q4
+
+// ===========================================================================
+// Host runtime
+// ===========================================================================
+using namespace q4;
+
+namespace {
+thread_local std::string g_last_error = "no error";
+}
+
+int q4gpu_fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int q4gpu_check_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "CUDA launch failed: %s", cudaGetErrorString(e));
+  return Q4GPU_OK;
+}
+
+#define Q4_CUDA(call)                                                                                  \
+  do {                                                                                                 \
+    const cudaError_t e_ = (call);                                                                     \
+    if (e_ != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+namespace {
+
+constexpr int kMaxLayers = 28;
+
+struct GraphKey {
+  int slot, layer_start, layer_count, embed, tail;
+  bool operator<(const GraphKey& o) const {
+    return std::tie(slot, layer_start, layer_count, embed, tail) <
+           std::tie(o.slot, o.layer_start, o.layer_count, o.embed, o.tail);
+  }
+};
+
+struct HostResult {
+  int32_t token;
+  int32_t pos;
+  int64_t score;
+};
+
+}  // namespace
+
+struct q4gpu_model {
+  q4gpu_model_config cfg{};
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  // weights
+  LayerW layers[kMaxLayers]{};
+  uint8_t* w_layers = nullptr;  // per layer: qkv, o, gate, up, down (packed)
+  uint16_t* s_layers = nullptr;
+  int32_t* gammas = nullptr;  // per layer: in[1024], post[1024], q[128], k[128]
+  uint8_t* emb = nullptr;
+  uint16_t* semb = nullptr;
+  int32_t* g_final = nullptr;
+  int32_t* cos_tab = nullptr;
+  int32_t* sin_tab = nullptr;
+  int32_t* exp_lut = nullptr;
+  int32_t* sig_lut = nullptr;
+  // KV pool
+  int32_t* kv_pool = nullptr;
+  int64_t page_elems = 0;
+  int pages_per_seq = 0;
+  int32_t* page_tables = nullptr;
+  // slots
+  std::vector<SlotState> slots;
+  HostResult* h_res = nullptr;  // pinned, one per slot
+  int32_t* h_in = nullptr;      // pinned staging: [token, pos] per slot
+  std::vector<cudaEvent_t> done;
+  std::vector<int> busy;
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+
+  template <class T>
+  int alloc(T** p, size_t count) {
+    void* v = nullptr;
+    Q4_CUDA(cudaMalloc(&v, count * sizeof(T) + 256));
+    Q4_CUDA(cudaMemset(v, 0, count * sizeof(T) + 256));
+    allocs.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return Q4GPU_OK;
+  }
+};
+
+namespace {
+
+constexpr size_t kQkvBytes = (size_t)(kQRows + 2 * kKvRows) * 512;
+constexpr size_t kOBytes = (size_t)kHidden * 1024;
+constexpr size_t kGateBytes = (size_t)kInter * 512;
+constexpr size_t kDownBytes = (size_t)kHidden * 1536;
+constexpr size_t kLayerWBytes = kQkvBytes + kOBytes + 2 * kGateBytes + kDownBytes;
+constexpr size_t kQkvScales = (size_t)(kQRows + 2 * kKvRows) * 16;
+constexpr size_t kOScales = (size_t)kHidden * 32;
+constexpr size_t kGateScales = (size_t)kInter * 16;
+constexpr size_t kDownScales = (size_t)kHidden * 48;
+constexpr size_t kLayerScales = kQkvScales + kOScales + 2 * kGateScales + kDownScales;
+constexpr size_t kLayerGammas = 2 * kHidden + 2 * kHeadDim;
+
+// (packed pointer, scale pointer, rows, cols) of one weight tensor
+struct TensorRef {
+  uint8_t* w;
+  uint16_t* s;
+  int64_t rows;
+  int cols;
+};
+
+TensorRef layer_tensor(q4gpu_model* m, int layer, int which) {
+  uint8_t* w = m->w_layers + (size_t)layer * kLayerWBytes;
+  uint16_t* s = m->s_layers + (size_t)layer * kLayerScales;
+  switch (which) {
+    case Q4GPU_T_Q: return {w, s, kQRows, kHidden};
+    case Q4GPU_T_K: return {w + (size_t)kQRows * 512, s + (size_t)kQRows * 16, kKvRows, kHidden};
+    case Q4GPU_T_V:
+      return {w + (size_t)(kQRows + kKvRows) * 512, s + (size_t)(kQRows + kKvRows) * 16, kKvRows, kHidden};
+    case Q4GPU_T_O: return {w + kQkvBytes, s + kQkvScales, kHidden, 2 * kHidden};
+    case Q4GPU_T_GATE: return {w + kQkvBytes + kOBytes, s + kQkvScales + kOScales, kInter, kHidden};
+    case Q4GPU_T_UP:
+      return {w + kQkvBytes + kOBytes + kGateBytes, s + kQkvScales + kOScales + kGateScales, kInter, kHidden};
+    case Q4GPU_T_DOWN:
+      return {w + kQkvBytes + kOBytes + 2 * kGateBytes, s + kQkvScales + kOScales + 2 * kGateScales, kHidden, kInter};
+    default: return {nullptr, nullptr, 0, 0};
+  }
+}
+
+int32_t* layer_gamma(q4gpu_model* m, int layer, int which, int* n) {
+  int32_t* g = m->gammas + (size_t)layer * kLayerGammas;
+  switch (which) {
+    case Q4GPU_T_INPUT_GAMMA: *n = kHidden; return g;
+    case Q4GPU_T_POST_GAMMA: *n = kHidden; return g + kHidden;
+    case Q4GPU_T_Q_GAMMA: *n = kHeadDim; return g + 2 * kHidden;
+    case Q4GPU_T_K_GAMMA: *n = kHeadDim; return g + 2 * kHidden + kHeadDim;
+    default: *n = 0; return nullptr;
+  }
+}
+
+// exp LUT (257 x UQ0.20) and sigmoid LUT (1025 x UQ0.16); round-half-even on
+// the double value as Python's round() does.
+void build_luts(int32_t* exp_lut, int32_t* sig_lut) {
+  for (int i = 0; i < kExpLut; ++i) exp_lut[i] = (int32_t)std::nearbyint(std::exp(-(double)i / 16.0) * 1048576.0);
+  for (int i = 0; i < kSigLut; ++i) {
+    const double x = -8.0 + (double)i / 64.0;
+    double y = std::nearbyint(1.0 / (1.0 + std::exp(-x)) * 65536.0);
+    y = y < 0 ? 0 : (y > 65535 ? 65535 : y);
+    sig_lut[i] = (int32_t)y;
+  }
+}
+
+// HF default RoPE inverse frequencies for head_dim 128, theta 1e6, as the
+// float32 values 1 / (1e6 ** (2i / 128)) that torch produces (torch's float32
+// pow differs from libm powf in the last bit for some i, so the values are
+// data here, not recomputed).
+constexpr float kInvFreq[64] = {
+    0x1.0000000000000p+0f, 0x1.9c975a0000000p-1f, 0x1.4c7bc00000000p-1f, 0x1.0bedde0000000p-1f,
+    0x1.afd1360000000p-2f, 0x1.5bf9fe0000000p-2f, 0x1.186a080000000p-2f, 0x1.c3f06a0000000p-3f,
+    0x1.6c310e0000000p-3f, 0x1.257b220000000p-3f, 0x1.d8ffac0000000p-4f, 0x1.7d298c0000000p-4f,
+    0x1.33281a0000000p-4f, 0x1.ef0a260000000p-5f, 0x1.8eec7e0000000p-5f, 0x1.41783a0000000p-5f,
+    0x1.030dc60000000p-5f, 0x1.a183500000000p-6f, 0x1.5073160000000p-6f, 0x1.0f20100000000p-6f,
+    0x1.b4f7e40000000p-7f, 0x1.6020a40000000p-7f, 0x1.1bc25a0000000p-7f, 0x1.c9548c0000000p-8f,
+    0x1.7089380000000p-8f, 0x1.28fb5c0000000p-8f, 0x1.dea41c0000000p-9f, 0x1.81b58a0000000p-9f,
+    0x1.36d21a0000000p-9f, 0x1.f4f1e00000000p-10f, 0x1.93aeb80000000p-10f, 0x1.454dee0000000p-10f,
+    0x1.0624de0000000p-10f, 0x1.a67e500000000p-11f, 0x1.5476880000000p-11f, 0x1.125c040000000p-11f,
+    0x1.ba2e4a0000000p-12f, 0x1.6453f60000000p-12f, 0x1.1f24e40000000p-12f, 0x1.cec9240000000p-13f,
+    0x1.74eea60000000p-13f, 0x1.2c86480000000p-13f, 0x1.e459c40000000p-14f, 0x1.864f6a0000000p-14f,
+    0x1.3a87480000000p-14f, 0x1.faeba80000000p-15f, 0x1.987f7c0000000p-15f, 0x1.492f560000000p-15f,
+    0x1.0945640000000p-15f, 0x1.ab88820000000p-16f, 0x1.58863a0000000p-16f, 0x1.15a1da0000000p-16f,
+    0x1.bf749e0000000p-17f, 0x1.68941c0000000p-17f, 0x1.2291c60000000p-17f, 0x1.d44e640000000p-18f,
+    0x1.7961820000000p-18f, 0x1.301c040000000p-18f, 0x1.ea20e00000000p-19f, 0x1.8af7560000000p-19f,
+    0x1.3e47c80000000p-19f, 0x1.007bd80000000p-19f, 0x1.9d5ef20000000p-20f, 0x1.4d1c980000000p-20f};
+
+// Q1.15 RoPE table: freqs and cos/sin in float32, rint(x * 2^15) clipped.
+void build_rope(int positions, int32_t* cos_t, int32_t* sin_t) {
+  const float* inv = kInvFreq;
+  for (int p = 0; p < positions; ++p)
+    for (int d = 0; d < kHeadDim; ++d) {
+      const float f = inv[d & 63] * (float)p;
+      double c = std::nearbyint((double)std::cos(f) * 32768.0), s = std::nearbyint((double)std::sin(f) * 32768.0);
+      c = c > 32767 ? 32767 : (c < -32768 ? -32768 : c);
+      s = s > 32767 ? 32767 : (s < -32768 ? -32768 : s);
+      cos_t[p * kHeadDim + d] = (int32_t)c;
+      sin_t[p * kHeadDim + d] = (int32_t)s;
+    }
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g;
+  cfg.blockDim = b;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+size_t attn_smem(int max_ctx) { return (size_t)2 * max_ctx * sizeof(int64_t); }
+
+// Enqueue one step of `slot` (no capture logic here).
+int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int embed, int tail) {
+  const SlotState& st = m->slots[slot];
+  cudaStream_t s = m->stream;
+  if (embed) Q4_CUDA(launch_k(embed_step_kernel, dim3(1), dim3(256), 0, s, st, (const uint8_t*)m->emb,
+                              (const uint16_t*)m->semb));
+  const int64_t scale = 189812531LL;  // round(128^-0.5 * 2^31)
+  for (int l = layer_start; l < layer_start + layer_count; ++l) {
+    const LayerW& w = m->layers[l];
+    Q4_CUDA(launch_k(qkv_step_kernel, dim3(kQHeads + 2 * kKvHeads), dim3(256), 0, s, st, w, l,
+                     (const int32_t*)m->cos_tab, (const int32_t*)m->sin_tab));
+    Q4_CUDA(launch_k(attn_step_kernel, dim3(kKvHeads), dim3(256), attn_smem(m->cfg.max_context), s, st, l,
+                     (const int32_t*)m->exp_lut, scale));
+    Q4_CUDA(launch_k(oproj_step_kernel, dim3(kHidden / 8), dim3(256), 0, s, st, w));
+    Q4_CUDA(launch_k(gateup_step_kernel, dim3(kInter / 16), dim3(256), 0, s, st, w, (const int32_t*)m->sig_lut));
+    Q4_CUDA(launch_k(down_step_kernel, dim3(kHidden / 8), dim3(192), 0, s, st, w));
+  }
+  if (tail)
+    Q4_CUDA(launch_k(lmhead_step_kernel, dim3(Q4GPU_LM_HEAD_BLOCKS), dim3(256), 0, s, st, (const uint8_t*)m->emb,
+                     (const uint16_t*)m->semb, m->cfg.vocab, (const int32_t*)m->g_final));
+  else
+    Q4_CUDA(launch_k(advance_step_kernel, dim3(1), dim3(32), 0, s, st));
+  return Q4GPU_OK;
+}
+
+int get_graph(q4gpu_model* m, const GraphKey& k, cudaGraphExec_t* out) {
+  auto it = m->graphs.find(k);
+  if (it != m->graphs.end()) {
+    *out = it->second;
+    return Q4GPU_OK;
+  }
+  cudaGraph_t g = nullptr;
+  Q4_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = enqueue_step(m, k.slot, k.layer_start, k.layer_count, k.embed, k.tail);
+  const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+  if (rc != Q4GPU_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+  cudaGraphExec_t e = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ie));
+  m->graphs[k] = e;
+  *out = e;
+  return Q4GPU_OK;
+}
+
+int set_device(q4gpu_model* m) {
+  Q4_CUDA(cudaSetDevice(m->cfg.device));
+  return Q4GPU_OK;
+}
+
+// Wait for the slot's last work, polling at most max_polls times (0 = block).
+int poll_slot(q4gpu_model* m, int slot, uint32_t max_polls) {
+  if (max_polls == 0) {
+    if (cudaEventSynchronize(m->done[slot]) != cudaSuccess) return QOT_ERR_STATUS;
+    m->busy[slot] = 0;
+    return QOT_OK;
+  }
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    const cudaError_t e = cudaEventQuery(m->done[slot]);
+    if (e == cudaSuccess) {
+      m->busy[slot] = 0;
+      return QOT_OK;
+    }
+    if (e != cudaErrorNotReady) return QOT_ERR_STATUS;
+  }
+  return QOT_ERR_TIMEOUT;
+}
+
+bool slot_busy(q4gpu_model* m, int slot) {
+  if (!m->busy[slot]) return false;
+  if (cudaEventQuery(m->done[slot]) == cudaSuccess) m->busy[slot] = 0;
+  return m->busy[slot] != 0;
+}
+
+uint64_t step_bytes(const q4gpu_model* m, int layers, int ctx, int tail) {
+  const uint64_t per_layer = kLayerWBytes + 2 * kLayerScales + (uint64_t)2 * kKvRows * 4 * ctx;
+  return per_layer * layers + (tail ? (uint64_t)m->cfg.vocab * (512 + 32) : 0);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* q4gpu_last_error(void) { return g_last_error.c_str(); }
+const char* q4gpu_version(void) { return "q4gpu 0.1 sm_100a"; }
+
+int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
+  if (!cfg || !out) return q4gpu_fail(Q4GPU_ERR_ARG, "null config/out");
+  *out = nullptr;
+  if (cfg->n_layers < 1 || cfg->n_layers > kMaxLayers || cfg->vocab < 1 || cfg->max_context < 1 ||
+      cfg->max_context > 16384 || cfg->max_seqs < 1 || cfg->max_seqs > 1024)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad model config");
+  auto* m = new q4gpu_model();
+  m->cfg = *cfg;
+  int rc = Q4GPU_OK;
+  auto fail = [&](int code) {
+    q4gpu_model_destroy(m);
+    return code;
+  };
+  if ((rc = set_device(m))) return fail(rc);
+  if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "stream create"));
+  const int L = cfg->n_layers;
+  if ((rc = m->alloc(&m->w_layers, kLayerWBytes * L))) return fail(rc);
+  if ((rc = m->alloc(&m->s_layers, kLayerScales * L))) return fail(rc);
+  if ((rc = m->alloc(&m->gammas, kLayerGammas * L))) return fail(rc);
+  if ((rc = m->alloc(&m->emb, (size_t)cfg->vocab * 512))) return fail(rc);
+  if ((rc = m->alloc(&m->semb, (size_t)cfg->vocab * 16))) return fail(rc);
+  if ((rc = m->alloc(&m->g_final, kHidden))) return fail(rc);
+  if ((rc = m->alloc(&m->cos_tab, (size_t)cfg->max_context * kHeadDim))) return fail(rc);
+  if ((rc = m->alloc(&m->sin_tab, (size_t)cfg->max_context * kHeadDim))) return fail(rc);
+  if ((rc = m->alloc(&m->exp_lut, kExpLut))) return fail(rc);
+  if ((rc = m->alloc(&m->sig_lut, kSigLut))) return fail(rc);
+  for (int l = 0; l < L; ++l) {
+    LayerW& w = m->layers[l];
+    const TensorRef q = layer_tensor(m, l, Q4GPU_T_Q), o = layer_tensor(m, l, Q4GPU_T_O),
+                    g = layer_tensor(m, l, Q4GPU_T_GATE), u = layer_tensor(m, l, Q4GPU_T_UP),
+                    d = layer_tensor(m, l, Q4GPU_T_DOWN);
+    w.wqkv = q.w;
+    w.sqkv = q.s;
+    w.wo = o.w;
+    w.so = o.s;
+    w.wgate = g.w;
+    w.sgate = g.s;
+    w.wup = u.w;
+    w.sup = u.s;
+    w.wdown = d.w;
+    w.sdown = d.s;
+    int n;
+    w.g_in = layer_gamma(m, l, Q4GPU_T_INPUT_GAMMA, &n);
+    w.g_post = layer_gamma(m, l, Q4GPU_T_POST_GAMMA, &n);
+    w.g_q = layer_gamma(m, l, Q4GPU_T_Q_GAMMA, &n);
+    w.g_k = layer_gamma(m, l, Q4GPU_T_K_GAMMA, &n);
+  }
+  // default tables: gammas 1.0, LUTs, RoPE (float32 host build)
+  {
+    std::vector<int32_t> ones(kLayerGammas * L, 128), e(kExpLut), sg(kSigLut);
+    if (cudaMemcpy(m->gammas, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->g_final, ones.data(), kHidden * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "gamma init"));
+    build_luts(e.data(), sg.data());
+    if (cudaMemcpy(m->exp_lut, e.data(), kExpLut * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->sig_lut, sg.data(), kSigLut * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "lut init"));
+    std::vector<int32_t> c((size_t)cfg->max_context * kHeadDim), s(c.size());
+    build_rope(cfg->max_context, c.data(), s.data());
+    if (cudaMemcpy(m->cos_tab, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(m->sin_tab, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "rope init"));
+  }
+  // paged KV pool: every slot owns ceil(max_context / 64) pages
+  m->page_elems = (int64_t)L * 2 * kKvHeads * kKvPage * kHeadDim;
+  m->pages_per_seq = (cfg->max_context + kKvPage - 1) / kKvPage;
+  const int64_t n_pages = (int64_t)m->pages_per_seq * cfg->max_seqs;
+  if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
+  if ((rc = m->alloc(&m->page_tables, (size_t)n_pages))) return fail(rc);
+  {
+    std::vector<int32_t> pt(n_pages);
+    for (int64_t i = 0; i < n_pages; ++i) pt[i] = (int32_t)i;
+    if (cudaMemcpy(m->page_tables, pt.data(), n_pages * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "page table init"));
+  }
+  // per-slot state
+  const int S = cfg->max_seqs;
+  int32_t *pos, *tokens, *hidden, *qrope, *attn, *post, *mlp;
+  int64_t* scores;
+  ArgBestD* part;
+  unsigned int* ctr;
+  const int T = cfg->max_context + 2;
+  if ((rc = m->alloc(&pos, (size_t)S * 4))) return fail(rc);
+  if ((rc = m->alloc(&tokens, (size_t)S * T))) return fail(rc);
+  if ((rc = m->alloc(&scores, (size_t)S * T))) return fail(rc);
+  if ((rc = m->alloc(&hidden, (size_t)S * kHidden))) return fail(rc);
+  if ((rc = m->alloc(&qrope, (size_t)S * kQRows))) return fail(rc);
+  if ((rc = m->alloc(&attn, (size_t)S * kQRows))) return fail(rc);
+  if ((rc = m->alloc(&post, (size_t)S * kHidden))) return fail(rc);
+  if ((rc = m->alloc(&mlp, (size_t)S * kInter))) return fail(rc);
+  if ((rc = m->alloc(&part, (size_t)S * Q4GPU_LM_HEAD_BLOCKS))) return fail(rc);
+  if ((rc = m->alloc(&ctr, (size_t)S * 32))) return fail(rc);
+  for (int i = 0; i < S; ++i) {
+    SlotState st{};
+    st.pos = pos + i * 4;
+    st.tokens = tokens + (size_t)i * T;
+    st.scores = scores + (size_t)i * T;
+    st.hidden = hidden + (size_t)i * kHidden;
+    st.qrope = qrope + (size_t)i * kQRows;
+    st.attn = attn + (size_t)i * kQRows;
+    st.post = post + (size_t)i * kHidden;
+    st.mlp = mlp + (size_t)i * kInter;
+    st.lm_partial = part + (size_t)i * Q4GPU_LM_HEAD_BLOCKS;
+    st.lm_counter = ctr + (size_t)i * 32;
+    st.kv = KvView{m->kv_pool, m->page_tables + (size_t)i * m->pages_per_seq, m->page_elems};
+    m->slots.push_back(st);
+  }
+  if (cudaMallocHost(&m->h_res, sizeof(HostResult) * S) != cudaSuccess ||
+      cudaMallocHost(&m->h_in, sizeof(int32_t) * 2 * S) != cudaSuccess)
+    return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "pinned alloc"));
+  m->done.resize(S);
+  m->busy.assign(S, 0);
+  for (int i = 0; i < S; ++i)
+    if (cudaEventCreateWithFlags(&m->done[i], cudaEventDisableTiming) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "event create"));
+  const size_t asmem = attn_smem(cfg->max_context);
+  if (cudaFuncSetAttribute(attn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem) != cudaSuccess)
+    return fail(q4gpu_fail(Q4GPU_ERR_SHAPE, "max_context %d needs %zu B of shared memory", cfg->max_context, asmem));
+  *out = m;
+  return Q4GPU_OK;
+}
+
+void q4gpu_model_destroy(q4gpu_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->cfg.device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto e : m->done)
+    if (e) cudaEventDestroy(e);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->h_res) cudaFreeHost(m->h_res);
+  if (m->h_in) cudaFreeHost(m->h_in);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+void* q4gpu_model_stream(q4gpu_model* m) { return m ? (void*)m->stream : nullptr; }
+
+int q4gpu_model_init_synthetic(q4gpu_model* m, uint64_t seed, float std_dev, float gamma_std) {
+  if (!m) return q4gpu_fail(Q4GPU_ERR_ARG, "null model");
+  int rc = set_device(m);
+  if (rc) return rc;
+  const size_t max_elems = std::max<size_t>((size_t)m->cfg.vocab * kHidden, (size_t)kInter * kHidden);
+  float* tmp = nullptr;
+  int32_t* err = nullptr;
+  Q4_CUDA(cudaMalloc(&tmp, max_elems * sizeof(float)));
+  Q4_CUDA(cudaMalloc(&err, sizeof(int32_t)));
+  Q4_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), m->stream));
+  auto gen_quant = [&](uint64_t tid, const TensorRef& t) -> int {
+    int r = q4gpu_synth_f32(seed, tid, 0, t.rows * t.cols, std_dev, 1, tmp, m->stream);
+    if (r) return r;
+    return q4gpu_quantize_q4(tmp, t.rows, t.cols, t.w, t.s, err, m->stream);
+  };
+  // tensor ids: embedding 0, final norm 15, layer l tensor w -> 16 + 16 l + w
+  rc = gen_quant(0, TensorRef{m->emb, m->semb, m->cfg.vocab, kHidden});
+  for (int l = 0; l < m->cfg.n_layers && !rc; ++l)
+    for (int wi = Q4GPU_T_Q; wi <= Q4GPU_T_DOWN && !rc; ++wi)
+      rc = gen_quant(16 + 16 * (uint64_t)l + wi, layer_tensor(m, l, wi));
+  if (!rc && gamma_std > 0.f) {
+    std::vector<float> hv(kHidden);
+    std::vector<int32_t> q(kHidden);
+    auto gamma = [&](uint64_t tid, int32_t* dst, int n) -> int {
+      int r = q4gpu_synth_f32(seed, tid, 0, n, gamma_std, 1, tmp, m->stream);
+      if (r) return r;
+      Q4_CUDA(cudaMemcpyAsync(hv.data(), tmp, n * 4, cudaMemcpyDeviceToHost, m->stream));
+      Q4_CUDA(cudaStreamSynchronize(m->stream));
+      for (int i = 0; i < n; ++i) {
+        const float g = 1.0f + hv[i];
+        double v = std::nearbyint((double)g * 128.0);
+        v = v > 32767 ? 32767 : (v < -32768 ? -32768 : v);
+        q[i] = (int32_t)v;
+      }
+      Q4_CUDA(cudaMemcpyAsync(dst, q.data(), n * 4, cudaMemcpyHostToDevice, m->stream));
+      Q4_CUDA(cudaStreamSynchronize(m->stream));
+      return Q4GPU_OK;
+    };
+    for (int l = 0; l < m->cfg.n_layers && !rc; ++l)
+      for (int wi = Q4GPU_T_INPUT_GAMMA; wi <= Q4GPU_T_K_GAMMA && !rc; ++wi) {
+        int n;
+        int32_t* dst = layer_gamma(m, l, wi, &n);
+        rc = gamma(16 + 16 * (uint64_t)l + wi, dst, n);
+      }
+    if (!rc) rc = gamma(15, m->g_final, kHidden);
+  }
+  int32_t herr = 0;
+  if (!rc && cudaMemcpyAsync(&herr, err, 4, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess)
+    rc = q4gpu_fail(Q4GPU_ERR_CUDA, "err readback");
+  if (cudaStreamSynchronize(m->stream) != cudaSuccess && !rc) rc = q4gpu_fail(Q4GPU_ERR_CUDA, "init sync");
+  cudaFree(tmp);
+  cudaFree(err);
+  if (!rc && herr) rc = q4gpu_fail(Q4GPU_ERR_QUANT, "a Q4 scale overflowed unsigned Q2.14");
+  return rc;
+}
+
+static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, size_t data_bytes, uint16_t* scale,
+                     size_t scale_bytes, bool to_device) {
+  if (!m || !data) return q4gpu_fail(Q4GPU_ERR_ARG, "null model/data");
+  int rc = set_device(m);
+  if (rc) return rc;
+  const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+  auto cp = [&](void* dev, void* host, size_t n) -> int {
+    Q4_CUDA(to_device ? cudaMemcpy(dev, host, n, kind) : cudaMemcpy(host, dev, n, kind));
+    return Q4GPU_OK;
+  };
+  if (which >= Q4GPU_T_Q && which <= Q4GPU_T_DOWN) {
+    if (layer < 0 || layer >= m->cfg.n_layers) return q4gpu_fail(Q4GPU_ERR_ARG, "bad layer");
+    const TensorRef t = layer_tensor(m, layer, which);
+    if (data_bytes != (size_t)t.rows * t.cols / 2 || !scale || scale_bytes != (size_t)t.rows * (t.cols / 64) * 2)
+      return q4gpu_fail(Q4GPU_ERR_SHAPE, "tensor %d expects %lld x %d", which, (long long)t.rows, t.cols);
+    if ((rc = cp(t.w, data, data_bytes))) return rc;
+    return cp(t.s, scale, scale_bytes);
+  }
+  if (which >= Q4GPU_T_INPUT_GAMMA && which <= Q4GPU_T_K_GAMMA) {
+    if (layer < 0 || layer >= m->cfg.n_layers) return q4gpu_fail(Q4GPU_ERR_ARG, "bad layer");
+    int n;
+    int32_t* g = layer_gamma(m, layer, which, &n);
+    if (data_bytes != (size_t)n * 4) return q4gpu_fail(Q4GPU_ERR_SHAPE, "gamma expects %d int32", n);
+    return cp(g, data, data_bytes);
+  }
+  switch (which) {
+    case Q4GPU_T_EMBED:
+      if (data_bytes != (size_t)m->cfg.vocab * 512 || !scale || scale_bytes != (size_t)m->cfg.vocab * 32)
+        return q4gpu_fail(Q4GPU_ERR_SHAPE, "embedding expects %d x 1024", m->cfg.vocab);
+      if ((rc = cp(m->emb, data, data_bytes))) return rc;
+      return cp(m->semb, scale, scale_bytes);
+    case Q4GPU_T_FINAL_GAMMA:
+      if (data_bytes != kHidden * 4) return q4gpu_fail(Q4GPU_ERR_SHAPE, "final gamma expects 1024 int32");
+      return cp(m->g_final, data, data_bytes);
+    case Q4GPU_T_ROPE_COS:
+    case Q4GPU_T_ROPE_SIN:
+      if (data_bytes != (size_t)m->cfg.max_context * kHeadDim * 4)
+        return q4gpu_fail(Q4GPU_ERR_SHAPE, "rope table expects [%d, 128] int32", m->cfg.max_context);
+      return cp(which == Q4GPU_T_ROPE_COS ? m->cos_tab : m->sin_tab, data, data_bytes);
+    case Q4GPU_T_EXP_LUT:
+      if (data_bytes != kExpLut * 4) return q4gpu_fail(Q4GPU_ERR_SHAPE, "exp LUT expects 257 int32");
+      return cp(m->exp_lut, data, data_bytes);
+    case Q4GPU_T_SIGMOID_LUT:
+      if (data_bytes != kSigLut * 4) return q4gpu_fail(Q4GPU_ERR_SHAPE, "sigmoid LUT expects 1025 int32");
+      return cp(m->sig_lut, data, data_bytes);
+    default: return q4gpu_fail(Q4GPU_ERR_ARG, "unknown tensor id %d", which);
+  }
+}
+
+int q4gpu_model_set_tensor(q4gpu_model* m, int32_t layer, int32_t which, const void* data, size_t data_bytes,
+                           const uint16_t* scale, size_t scale_bytes) {
+  return tensor_io(m, layer, which, const_cast<void*>(data), data_bytes, const_cast<uint16_t*>(scale), scale_bytes,
+                   true);
+}
+
+int q4gpu_model_get_tensor(q4gpu_model* m, int32_t layer, int32_t which, void* data, size_t data_bytes,
+                           uint16_t* scale, size_t scale_bytes) {
+  return tensor_io(m, layer, which, data, data_bytes, scale, scale_bytes, false);
+}
+
+// Validation shared by the runner and the decode API (reference order:
+// qmap_one_token_runtime.h:249-283).
+static int validate_run(q4gpu_model* m, uintptr_t base, const qot_run_config_t* c, uint32_t position) {
+  if (!c) return QOT_ERR_NULL;
+  if (c->layer_count == 0u || c->layer_start >= (uint32_t)m->cfg.n_layers) return QOT_ERR_BAD_LAYER;
+  const uint32_t end = c->layer_start + c->layer_count;
+  if (end > (uint32_t)m->cfg.n_layers || end < c->layer_start) return QOT_ERR_BAD_LAYER;
+  if (position >= (uint32_t)m->cfg.max_context) return QOT_ERR_CONTEXT;
+  if (base >= (uintptr_t)m->cfg.max_seqs) return QOT_ERR_BAD_ADDR;
+  return QOT_OK;
+}
+
+int q4gpu_run_token(void* runner_context, uintptr_t base, const qot_run_config_t* config, uint32_t input_token_id,
+                    uint32_t position, uint32_t max_polls, qot_result_t* result) {
+  q4gpu_model* m = static_cast<q4gpu_model*>(runner_context);
+  if (!m || !config || !result) return QOT_ERR_NULL;
+  int rc = validate_run(m, base, config, position);
+  if (rc != QOT_OK) return rc;
+  if (config->embedding_enable && input_token_id >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
+  if (set_device(m)) return QOT_ERR_STATUS;
+  const int slot = (int)base;
+  if (slot_busy(m, slot)) return QOT_ERR_BUSY;
+  cudaGraphExec_t g;
+  if (get_graph(m, GraphKey{slot, (int)config->layer_start, (int)config->layer_count,
+                            config->embedding_enable ? 1 : 0, 1},
+                &g) != Q4GPU_OK)
+    return QOT_ERR_STATUS;
+  const SlotState& st = m->slots[slot];
+  int32_t* hin = m->h_in + 2 * slot;
+  hin[0] = (int32_t)input_token_id;
+  hin[1] = (int32_t)position;
+  HostResult* hr = m->h_res + slot;
+  if (cudaMemcpyAsync(st.tokens + position, &hin[0], 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess ||
+      cudaMemcpyAsync(st.pos, &hin[1], 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess ||
+      cudaGraphLaunch(g, m->stream) != cudaSuccess ||
+      cudaMemcpyAsync(&hr->token, st.tokens + position + 1, 4, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess ||
+      cudaMemcpyAsync(&hr->score, st.scores + position + 1, 8, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess ||
+      cudaEventRecord(m->done[slot], m->stream) != cudaSuccess) {
+    q4gpu_fail(Q4GPU_ERR_CUDA, "run_token enqueue: %s", cudaGetErrorString(cudaGetLastError()));
+    return QOT_ERR_STATUS;
+  }
+  m->busy[slot] = 1;
+  memset(result, 0, sizeof(*result));
+  rc = poll_slot(m, slot, max_polls);
+  if (rc != QOT_OK) return rc;
+  result->status = 1u;  // done
+  result->token_id = (uint32_t)hr->token;
+  result->score_q26 = hr->score;
+  result->layers_started = config->layer_count;
+  result->layers_completed = config->layer_count;
+  result->layer_done_mask =
+      (uint32_t)((config->layer_count >= 32 ? 0xFFFFFFFFull : ((1ull << config->layer_count) - 1)) << config->layer_start);
+  result->tail_tiles_started = result->tail_tiles_completed = (uint32_t)((m->cfg.vocab + 15) / 16);
+  const uint64_t rd = step_bytes(m, config->layer_count, position + 1, 1) / 4;
+  result->mem_read_words = (uint32_t)std::min<uint64_t>(rd, 0xFFFFFFFFull);
+  result->mem_write_words = (uint32_t)(config->layer_count * 2 * kKvRows);
+  return QOT_OK;
+}
+
+int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_t* cfg,
+                           const uint32_t* prompt_token_ids, uint32_t prompt_token_count, uint32_t max_new_tokens,
+                           uint32_t* generated_token_ids, uint32_t generated_token_capacity,
+                           uint32_t max_polls_per_token, uint32_t* generated_token_count, qot_result_t* last_result) {
+  if (generated_token_count) *generated_token_count = 0u;
+  if (!m || !cfg || !prompt_token_ids || !generated_token_ids || !last_result) return QOT_ERR_NULL;
+  if (prompt_token_count == 0u || max_new_tokens == 0u) return QOT_ERR_CAPACITY;
+  if (generated_token_capacity < max_new_tokens) return QOT_ERR_CAPACITY;
+  if (cfg->runtime_context_enable == 0u || cfg->embedding_enable == 0u) return QOT_ERR_CONTEXT;
+  if (cfg->final_hidden_override_valid != 0u) return QOT_ERR_CONTEXT;
+  for (uint32_t i = 0; i < prompt_token_count; ++i)
+    if (prompt_token_ids[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
+  const uint32_t run_count = prompt_token_count + max_new_tokens - 1u;
+  if (run_count < prompt_token_count || cfg->position >= (uint32_t)m->cfg.max_context ||
+      run_count > (uint32_t)m->cfg.max_context - cfg->position)
+    return QOT_ERR_CONTEXT;
+  int rc = validate_run(m, base, cfg, cfg->position);
+  if (rc != QOT_OK) return rc;
+  if (set_device(m)) return QOT_ERR_STATUS;
+  const int slot = (int)base;
+  if (slot_busy(m, slot)) return QOT_ERR_BUSY;
+  cudaGraphExec_t gpre, gstep;
+  if (get_graph(m, GraphKey{slot, (int)cfg->layer_start, (int)cfg->layer_count, 1, 0}, &gpre) != Q4GPU_OK ||
+      get_graph(m, GraphKey{slot, (int)cfg->layer_start, (int)cfg->layer_count, 1, 1}, &gstep) != Q4GPU_OK)
+    return QOT_ERR_STATUS;
+  const SlotState& st = m->slots[slot];
+  std::vector<int32_t> toks(prompt_token_ids, prompt_token_ids + prompt_token_count);
+  int32_t* hin = m->h_in + 2 * slot;
+  hin[1] = (int32_t)cfg->position;
+  std::vector<int32_t> gen(max_new_tokens);
+  std::vector<int64_t> gsc(max_new_tokens);
+  bool ok = cudaMemcpyAsync(st.tokens + cfg->position, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice,
+                            m->stream) == cudaSuccess &&
+            cudaMemcpyAsync(st.pos, &hin[1], 4, cudaMemcpyHostToDevice, m->stream) == cudaSuccess;
+  for (uint32_t i = 0; ok && i + 1 < prompt_token_count; ++i) ok = cudaGraphLaunch(gpre, m->stream) == cudaSuccess;
+  for (uint32_t i = 0; ok && i < max_new_tokens; ++i) ok = cudaGraphLaunch(gstep, m->stream) == cudaSuccess;
+  const uint32_t first = cfg->position + prompt_token_count;
+  ok = ok &&
+       cudaMemcpyAsync(gen.data(), st.tokens + first, max_new_tokens * 4, cudaMemcpyDeviceToHost, m->stream) ==
+           cudaSuccess &&
+       cudaMemcpyAsync(gsc.data(), st.scores + first, max_new_tokens * 8, cudaMemcpyDeviceToHost, m->stream) ==
+           cudaSuccess &&
+       cudaEventRecord(m->done[slot], m->stream) == cudaSuccess;
+  if (!ok) {
+    q4gpu_fail(Q4GPU_ERR_CUDA, "decode enqueue: %s", cudaGetErrorString(cudaGetLastError()));
+    return QOT_ERR_STATUS;
+  }
+  m->busy[slot] = 1;
+  // The poll budget covers the whole run.
+  const uint64_t polls = (uint64_t)max_polls_per_token * run_count;
+  rc = poll_slot(m, slot, (uint32_t)std::min<uint64_t>(polls, 0xFFFFFFFFull));
+  memset(last_result, 0, sizeof(*last_result));
+  if (rc != QOT_OK) return rc;
+  for (uint32_t i = 0; i < max_new_tokens; ++i) {
+    if ((uint32_t)gen[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
+    generated_token_ids[i] = (uint32_t)gen[i];
+  }
+  if (generated_token_count) *generated_token_count = max_new_tokens;
+  last_result->status = 1u;
+  last_result->token_id = (uint32_t)gen[max_new_tokens - 1];
+  last_result->score_q26 = gsc[max_new_tokens - 1];
+  last_result->layers_started = last_result->layers_completed = cfg->layer_count;
+  return QOT_OK;
+}
+
+int q4gpu_decode_batch(q4gpu_model* m, int32_t n_seq, const uint32_t* prompts, const uint32_t* prompt_lens,
+                       uint32_t max_new_tokens, uint32_t* generated, int64_t* scores) {
+  if (!m || !prompts || !prompt_lens || !generated || n_seq <= 0) return QOT_ERR_NULL;
+  if (n_seq > m->cfg.max_seqs) return QOT_ERR_CAPACITY;
+  qot_run_config_t cfg{};
+  cfg.layer_start = 0;
+  cfg.layer_count = (uint32_t)m->cfg.n_layers;
+  cfg.runtime_context_enable = 1;
+  cfg.embedding_enable = 1;
+  size_t off = 0;
+  for (int s = 0; s < n_seq; ++s) {
+    uint32_t cnt = 0;
+    qot_result_t res;
+    const int rc = q4gpu_decode_token_ids(m, (uintptr_t)s, &cfg, prompts + off, prompt_lens[s], max_new_tokens,
+                                          generated + (size_t)s * max_new_tokens, max_new_tokens, 0, &cnt, &res);
+    if (rc != QOT_OK) return rc;
+    if (scores) {
+      // per-token scores of this sequence
+      const uint32_t first = prompt_lens[s];
+      if (cudaMemcpy(scores + (size_t)s * max_new_tokens, m->slots[s].scores + first, max_new_tokens * 8,
+                     cudaMemcpyDeviceToHost) != cudaSuccess)
+        return QOT_ERR_STATUS;
+    }
+    off += prompt_lens[s];
+  }
+  return QOT_OK;
+}
+
+int q4gpu_model_read_hidden(q4gpu_model* m, uintptr_t base, int32_t* hidden) {
+  if (!m || !hidden || base >= (uintptr_t)m->cfg.max_seqs) return Q4GPU_ERR_ARG;
+  int rc = set_device(m);
+  if (rc) return rc;
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  Q4_CUDA(cudaMemcpy(hidden, m->slots[base].hidden, kHidden * 4, cudaMemcpyDeviceToHost));
+  return Q4GPU_OK;
+}
+
+static int kv_io(q4gpu_model* m, uintptr_t base, int32_t layer, int32_t kind, int32_t positions, int32_t* data,
+                 bool to_pool) {
+  if (!m || !data || base >= (uintptr_t)m->cfg.max_seqs || layer < 0 || layer >= m->cfg.n_layers || kind < 0 ||
+      kind > 1 || positions <= 0 || positions > m->cfg.max_context)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad kv request");
+  int rc = set_device(m);
+  if (rc) return rc;
+  const size_t n = (size_t)positions * kKvRows;
+  int32_t* dev = nullptr;
+  Q4_CUDA(cudaMalloc(&dev, n * 4));
+  bool ok = true;
+  if (to_pool) ok = cudaMemcpy(dev, data, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok) {
+    kv_copy_kernel<<<dim3(positions, kKvHeads), kHeadDim, 0, m->stream>>>(m->slots[base].kv, layer, kind, positions,
+                                                                          dev, to_pool ? 1 : 0);
+    ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(m->stream) == cudaSuccess;
+  }
+  if (ok && !to_pool) ok = cudaMemcpy(data, dev, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(dev);
+  return ok ? Q4GPU_OK : q4gpu_fail(Q4GPU_ERR_CUDA, "kv copy failed");
+}
+
+int q4gpu_model_read_kv(q4gpu_model* m, uintptr_t base, int32_t layer, int32_t kind, int32_t positions,
+                        int32_t* out) {
+  return kv_io(m, base, layer, kind, positions, out, false);
+}
+
+int q4gpu_model_write_kv(q4gpu_model* m, uintptr_t base, int32_t layer, int32_t kind, int32_t positions,
+                         const int32_t* data) {
+  return kv_io(m, base, layer, kind, positions, const_cast<int32_t*>(data), true);
+}
+
+int q4gpu_model_write_hidden(q4gpu_model* m, uintptr_t base, const int32_t* hidden) {
+  if (!m || !hidden || base >= (uintptr_t)m->cfg.max_seqs) return Q4GPU_ERR_ARG;
+  int rc = set_device(m);
+  if (rc) return rc;
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  Q4_CUDA(cudaMemcpy(m->slots[base].hidden, hidden, kHidden * 4, cudaMemcpyHostToDevice));
+  return Q4GPU_OK;
+}
+
+void q4gpu_build_tables(int32_t* exp_lut, int32_t* sigmoid_lut) { build_luts(exp_lut, sigmoid_lut); }
+
+void q4gpu_build_rope_table(int32_t positions, int32_t* cos_q1_15, int32_t* sin_q1_15) {
+  build_rope(positions, cos_q1_15, sin_q1_15);
+}
+
+}  // extern "C"

@@ -1,0 +1,187 @@
+"""Host-side model context: device-resident Q4 weights, paged KV cache and
+the decode graphs of libq4gpu, driven through the reference's runner seam.
+
+``Q4Model.run_token`` is ``qot_run_token`` (one full-model invocation per
+call, ``FPGA_Project/software/qmap_one_token_runtime/qmap_one_token_runtime.h:369-392``)
+and ``Q4Model.decode`` is ``qot_decode_token_ids`` (``:399-500``); both return
+the reference's ``QOT_*`` status codes through ``QotError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _native
+from . import tables
+from ._native import QotResult, QotRunConfig
+
+HIDDEN = 1024
+VOCAB = 151936
+LAYERS = 28
+
+QOT_NAMES = {0: "OK", -1: "BUSY", -2: "BAD_LAYER", -3: "BAD_TABLE", -4: "BAD_ADDR", -5: "TIMEOUT",
+             -6: "STATUS", -7: "NULL", -8: "BAD_TOKEN", -9: "CAPACITY", -10: "CONTEXT"}
+
+WEIGHT_SHAPES = {_native.T_Q: (2048, 1024), _native.T_K: (1024, 1024), _native.T_V: (1024, 1024),
+                 _native.T_O: (1024, 2048), _native.T_GATE: (3072, 1024), _native.T_UP: (3072, 1024),
+                 _native.T_DOWN: (1024, 3072)}
+GAMMA_SIZES = {_native.T_INPUT_GAMMA: 1024, _native.T_POST_GAMMA: 1024, _native.T_Q_GAMMA: 128,
+               _native.T_K_GAMMA: 128}
+
+
+class QotError(RuntimeError):
+    def __init__(self, code: int, what: str):
+        super().__init__(f"{what}: QOT_ERR_{QOT_NAMES.get(code, code)} ({code})")
+        self.code = code
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return a.ctypes.data_as(C.c_void_p)
+
+
+@dataclass
+class RunResult:
+    token_id: int
+    score_q26: int
+    raw: QotResult
+
+
+class Q4Model:
+    """One B200 model context (weights + KV for ``max_seqs`` sequence slots)."""
+
+    def __init__(self, n_layers: int = LAYERS, vocab: int = VOCAB, max_context: int = 256, max_seqs: int = 1,
+                 device: int = 0):
+        self.lib = _native.load()
+        cfg = _native.ModelConfig(n_layers=n_layers, vocab=vocab, max_context=max_context, max_seqs=max_seqs,
+                                  device=device)
+        h = C.c_void_p()
+        _native.check(self.lib.q4gpu_model_create(C.byref(cfg), C.byref(h)), "q4gpu_model_create")
+        self.handle = h
+        self.n_layers, self.vocab, self.max_context, self.max_seqs = n_layers, vocab, max_context, max_seqs
+        self.install_rope_tables()
+
+    # -- lifecycle ---------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.q4gpu_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        return int(self.lib.q4gpu_model_stream(self.handle) or 0)
+
+    # -- weights -----------------------------------------------------------
+    def init_synthetic(self, seed: int = 0, std: float = 0.02, gamma_std: float = 0.0) -> None:
+        """Seeded random-init weights quantised on the device."""
+        _native.check(self.lib.q4gpu_model_init_synthetic(self.handle, seed, std, gamma_std),
+                      "q4gpu_model_init_synthetic")
+
+    def install_rope_tables(self) -> None:
+        cos, sin = tables.rope_tables(self.max_context)
+        self.set_table(_native.T_ROPE_COS, cos)
+        self.set_table(_native.T_ROPE_SIN, sin)
+
+    def set_table(self, which: int, values: np.ndarray, layer: int = 0) -> None:
+        v = np.ascontiguousarray(values, dtype=np.int32)
+        _native.check(self.lib.q4gpu_model_set_tensor(self.handle, layer, which, _ptr(v), v.nbytes, None, 0),
+                      "q4gpu_model_set_tensor")
+
+    def set_weight(self, layer: int, which: int, packed: np.ndarray, scale: np.ndarray) -> None:
+        p = np.ascontiguousarray(packed, dtype=np.uint8)
+        s = np.ascontiguousarray(scale, dtype=np.uint16)
+        _native.check(self.lib.q4gpu_model_set_tensor(self.handle, layer, which, _ptr(p), p.nbytes, _ptr(s),
+                                                      s.nbytes), "q4gpu_model_set_tensor")
+
+    def get_weight(self, layer: int, which: int) -> tuple[np.ndarray, np.ndarray]:
+        rows, cols = (self.vocab, HIDDEN) if which == _native.T_EMBED else WEIGHT_SHAPES[which]
+        p = np.empty((rows, cols // 2), dtype=np.uint8)
+        s = np.empty((rows, cols // 64), dtype=np.uint16)
+        _native.check(self.lib.q4gpu_model_get_tensor(self.handle, layer, which, _ptr(p), p.nbytes, _ptr(s),
+                                                      s.nbytes), "q4gpu_model_get_tensor")
+        return p, s
+
+    def get_gamma(self, layer: int, which: int) -> np.ndarray:
+        n = HIDDEN if which == _native.T_FINAL_GAMMA else GAMMA_SIZES[which]
+        g = np.empty(n, dtype=np.int32)
+        _native.check(self.lib.q4gpu_model_get_tensor(self.handle, layer, which, _ptr(g), g.nbytes, None, 0),
+                      "q4gpu_model_get_tensor")
+        return g
+
+    # -- runner seam -------------------------------------------------------
+    def run_config(self, layer_start: int = 0, layer_count: int | None = None, embedding: bool = True,
+                   position: int = 0) -> QotRunConfig:
+        c = QotRunConfig()
+        c.layer_start = layer_start
+        c.layer_count = self.n_layers - layer_start if layer_count is None else layer_count
+        c.position = position
+        c.runtime_context_enable = 1
+        c.embedding_enable = 1 if embedding else 0
+        return c
+
+    def run_token(self, token: int, position: int, slot: int = 0, layer_start: int = 0,
+                  layer_count: int | None = None, embedding: bool = True, max_polls: int = 0) -> RunResult:
+        cfg = self.run_config(layer_start, layer_count, embedding, position)
+        res = QotResult()
+        rc = self.lib.q4gpu_run_token(self.handle, slot, C.byref(cfg), token, position, max_polls, C.byref(res))
+        if rc != 0:
+            raise QotError(rc, "q4gpu_run_token")
+        return RunResult(res.token_id, res.score_q26, res)
+
+    def decode(self, prompt, max_new_tokens: int, slot: int = 0, position: int = 0,
+               max_polls_per_token: int = 0) -> tuple[list[int], QotResult]:
+        p = np.ascontiguousarray(np.asarray(prompt, dtype=np.uint32))
+        out = np.zeros(max(max_new_tokens, 1), dtype=np.uint32)
+        cnt = C.c_uint32(0)
+        res = QotResult()
+        cfg = self.run_config(position=position)
+        rc = self.lib.q4gpu_decode_token_ids(self.handle, slot, C.byref(cfg), _ptr(p), p.size, max_new_tokens,
+                                             _ptr(out), out.size, max_polls_per_token, C.byref(cnt), C.byref(res))
+        if rc != 0:
+            raise QotError(rc, "q4gpu_decode_token_ids")
+        return out[: cnt.value].astype(np.int64).tolist(), res
+
+    def decode_batch(self, prompts, max_new_tokens: int) -> tuple[np.ndarray, np.ndarray]:
+        lens = np.asarray([len(p) for p in prompts], dtype=np.uint32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.uint32) for p in prompts]))
+        gen = np.zeros((len(prompts), max_new_tokens), dtype=np.uint32)
+        scores = np.zeros((len(prompts), max_new_tokens), dtype=np.int64)
+        rc = self.lib.q4gpu_decode_batch(self.handle, len(prompts), _ptr(flat), _ptr(lens), max_new_tokens,
+                                         _ptr(gen), _ptr(scores))
+        if rc != 0:
+            raise QotError(rc, "q4gpu_decode_batch")
+        return gen.astype(np.int64), scores
+
+    # -- state access ------------------------------------------------------
+    def read_hidden(self, slot: int = 0) -> np.ndarray:
+        h = np.empty(HIDDEN, dtype=np.int32)
+        _native.check(self.lib.q4gpu_model_read_hidden(self.handle, slot, _ptr(h)), "q4gpu_model_read_hidden")
+        return h.astype(np.int64)
+
+    def write_hidden(self, hidden, slot: int = 0) -> None:
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.int32))
+        _native.check(self.lib.q4gpu_model_write_hidden(self.handle, slot, _ptr(h)), "q4gpu_model_write_hidden")
+
+    def read_kv(self, layer: int, kind: int, positions: int, slot: int = 0) -> np.ndarray:
+        out = np.empty((positions, 8, 128), dtype=np.int32)
+        _native.check(self.lib.q4gpu_model_read_kv(self.handle, slot, layer, kind, positions, _ptr(out)),
+                      "q4gpu_model_read_kv")
+        return out.astype(np.int64)
+
+    def write_kv(self, layer: int, kind: int, data, slot: int = 0) -> None:
+        d = np.ascontiguousarray(np.asarray(data, dtype=np.int32))
+        _native.check(self.lib.q4gpu_model_write_kv(self.handle, slot, layer, kind, d.shape[0], _ptr(d)),
+                      "q4gpu_model_write_kv")
