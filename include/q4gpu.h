@@ -314,6 +314,33 @@ int q4gpu_model_write_kv(q4gpu_model *m, uintptr_t base, int32_t layer, int32_t 
 void q4gpu_build_tables(int32_t *exp_lut, int32_t *sigmoid_lut);
 void q4gpu_build_rope_table(int32_t positions, int32_t *cos_q1_15, int32_t *sin_q1_15);
 
+/* Continue a greedy decode of slot `base` on the device: enqueue n_steps
+ * replays of the full-model step graph (embedding of tokens[pos], all layers,
+ * LM head writing tokens[pos+1] and advancing pos).  Returns without waiting;
+ * q4gpu_model_sync waits.  The caller keeps pos + n_steps < max_context. */
+int q4gpu_decode_steps(q4gpu_model *m, uintptr_t base, int32_t n_steps);
+/* Set slot's next position, stream-ordered after the slot's queued work. */
+int q4gpu_model_set_position(q4gpu_model *m, uintptr_t base, int32_t position);
+int q4gpu_model_sync(q4gpu_model *m);
+
+/* Read tokens[start, start+n) and their argmax scores (scores[p] is the score
+ * of the argmax that produced tokens[p]) and the slot's next position. */
+int q4gpu_model_read_tokens(q4gpu_model *m, uintptr_t base, int32_t start, int32_t n, int32_t *tokens,
+                            int64_t *scores, int32_t *position);
+
+/* Kernel kinds of one decode step, for q4gpu_model_time_kernels. */
+enum {
+    Q4GPU_K_EMBED = 0, Q4GPU_K_QKV, Q4GPU_K_ATTN, Q4GPU_K_OPROJ, Q4GPU_K_GATEUP, Q4GPU_K_DOWN,
+    Q4GPU_K_LMHEAD, Q4GPU_K_ADVANCE, Q4GPU_K_COUNT
+};
+
+/* Run `reps` decode steps of slot `base` (continuing its greedy decode) as
+ * plain launches with a CUDA event between consecutive kernels, and return the
+ * mean device time of one launch of each kernel kind (ms_per_launch[8]) and
+ * the launches of each kind in one step (launches_per_step[8]). */
+int q4gpu_model_time_kernels(q4gpu_model *m, uintptr_t base, int32_t reps, double *ms_per_launch,
+                             int32_t *launches_per_step);
+
 /* Stream the context launches on (a cudaStream_t), for timing. */
 void *q4gpu_model_stream(q4gpu_model *m);
 

@@ -23,6 +23,10 @@ T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN = range(7)
 T_INPUT_GAMMA, T_POST_GAMMA, T_Q_GAMMA, T_K_GAMMA = range(7, 11)
 T_EMBED, T_FINAL_GAMMA, T_ROPE_COS, T_ROPE_SIN, T_EXP_LUT, T_SIGMOID_LUT = range(100, 106)
 
+# kernel kinds of one decode step (q4gpu_model_time_kernels)
+KERNEL_KINDS = ["embed", "qkv_norm_rope_kv", "attention", "o_proj_residual", "post_norm_gate_up_swiglu",
+                "down_residual", "final_norm_lm_head_argmax", "advance"]
+
 
 class QotLayerQmapBases(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in ("qkv", "input_norm", "attn_frontend", "attn_score_value", "o_proj",
@@ -93,6 +97,11 @@ SIGNATURES = {
     "q4gpu_build_tables": (None, [P, P]),
     "q4gpu_build_rope_table": (None, [I32, P, P]),
     "q4gpu_model_stream": (P, [P]),
+    "q4gpu_decode_steps": (C.c_int, [P, C.c_size_t, I32]),
+    "q4gpu_model_sync": (C.c_int, [P]),
+    "q4gpu_model_set_position": (C.c_int, [P, C.c_size_t, I32]),
+    "q4gpu_model_read_tokens": (C.c_int, [P, C.c_size_t, I32, I32, P, P, P]),
+    "q4gpu_model_time_kernels": (C.c_int, [P, C.c_size_t, I32, P, P]),
 }
 
 _lib = None

@@ -403,6 +403,12 @@ __global__ void advance_step_kernel(SlotState st) {
   if (threadIdx.x == 0) *st.pos += 1;
 }
 
+__global__ void set_pos_kernel(SlotState st, int position) {
+  grid_dep_wait();
+  grid_dep_launch();
+  if (threadIdx.x == 0) *st.pos = position;
+}
+
 // Scatter a KV pool page range to/from the reference order [pos][head][128].
 __global__ void kv_copy_kernel(KvView kv, int layer, int kind, int positions, int32_t* flat, int to_pool) {
   const int p = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
@@ -624,29 +630,61 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStrea
 
 size_t attn_smem(int max_ctx) { return (size_t)2 * max_ctx * sizeof(int64_t); }
 
-// Enqueue one step of `slot` (no capture logic here).
-int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int embed, int tail) {
+// Per-kernel event marks for q4gpu_model_time_kernels (kinds as in q4gpu.h).
+struct KernelMarks {
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> kind;
+  int mark(cudaStream_t s, int k) {
+    cudaEvent_t e;
+    Q4_CUDA(cudaEventCreate(&e));
+    ev.push_back(e);
+    kind.push_back(k);
+    Q4_CUDA(cudaEventRecord(e, s));
+    return Q4GPU_OK;
+  }
+  ~KernelMarks() {
+    for (auto e : ev) cudaEventDestroy(e);
+  }
+};
+
+// Enqueue one step of `slot` (no capture logic here).  With `marks`, an
+// event is recorded before every kernel and after the last one.
+int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int embed, int tail,
+                 KernelMarks* marks = nullptr) {
   const SlotState& st = m->slots[slot];
   cudaStream_t s = m->stream;
-  if (embed) Q4_CUDA(launch_k(embed_step_kernel, dim3(1), dim3(256), 0, s, st, (const uint8_t*)m->emb,
-                              (const uint16_t*)m->semb));
+  auto mark = [&](int k) { return marks ? marks->mark(s, k) : Q4GPU_OK; };
+  int rc;
+  if (embed) {
+    if ((rc = mark(Q4GPU_K_EMBED))) return rc;
+    Q4_CUDA(launch_k(embed_step_kernel, dim3(1), dim3(256), 0, s, st, (const uint8_t*)m->emb,
+                     (const uint16_t*)m->semb));
+  }
   const int64_t scale = 189812531LL;  // round(128^-0.5 * 2^31)
   for (int l = layer_start; l < layer_start + layer_count; ++l) {
     const LayerW& w = m->layers[l];
+    if ((rc = mark(Q4GPU_K_QKV))) return rc;
     Q4_CUDA(launch_k(qkv_step_kernel, dim3(kQHeads + 2 * kKvHeads), dim3(256), 0, s, st, w, l,
                      (const int32_t*)m->cos_tab, (const int32_t*)m->sin_tab));
+    if ((rc = mark(Q4GPU_K_ATTN))) return rc;
     Q4_CUDA(launch_k(attn_step_kernel, dim3(kKvHeads), dim3(256), attn_smem(m->cfg.max_context), s, st, l,
                      (const int32_t*)m->exp_lut, scale));
+    if ((rc = mark(Q4GPU_K_OPROJ))) return rc;
     Q4_CUDA(launch_k(oproj_step_kernel, dim3(kHidden / 8), dim3(256), 0, s, st, w));
+    if ((rc = mark(Q4GPU_K_GATEUP))) return rc;
     Q4_CUDA(launch_k(gateup_step_kernel, dim3(kInter / 16), dim3(256), 0, s, st, w, (const int32_t*)m->sig_lut));
+    if ((rc = mark(Q4GPU_K_DOWN))) return rc;
     Q4_CUDA(launch_k(down_step_kernel, dim3(kHidden / 8), dim3(192), 0, s, st, w));
   }
-  if (tail)
+  if (tail) {
+    if ((rc = mark(Q4GPU_K_LMHEAD))) return rc;
     Q4_CUDA(launch_k(lmhead_step_kernel, dim3(Q4GPU_LM_HEAD_BLOCKS), dim3(256), 0, s, st, (const uint8_t*)m->emb,
                      (const uint16_t*)m->semb, m->cfg.vocab, (const int32_t*)m->g_final));
-  else
+  } else {
+    if ((rc = mark(Q4GPU_K_ADVANCE))) return rc;
     Q4_CUDA(launch_k(advance_step_kernel, dim3(1), dim3(32), 0, s, st));
-  return Q4GPU_OK;
+  }
+  return mark(-1);
 }
 
 int get_graph(q4gpu_model* m, const GraphKey& k, cudaGraphExec_t* out) {
@@ -1119,6 +1157,75 @@ int q4gpu_decode_batch(q4gpu_model* m, int32_t n_seq, const uint32_t* prompts, c
     off += prompt_lens[s];
   }
   return QOT_OK;
+}
+
+int q4gpu_decode_steps(q4gpu_model* m, uintptr_t base, int32_t n_steps) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || n_steps < 0) return q4gpu_fail(Q4GPU_ERR_ARG, "bad decode_steps");
+  int rc = set_device(m);
+  if (rc) return rc;
+  cudaGraphExec_t g;
+  if ((rc = get_graph(m, GraphKey{(int)base, 0, m->cfg.n_layers, 1, 1}, &g))) return rc;
+  for (int i = 0; i < n_steps; ++i) Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  return Q4GPU_OK;
+}
+
+int q4gpu_model_set_position(q4gpu_model* m, uintptr_t base, int32_t position) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || position < 0 || position >= m->cfg.max_context)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad set_position");
+  int rc = set_device(m);
+  if (rc) return rc;
+  // a one-thread kernel keeps this stream-ordered without a host round trip
+  Q4_CUDA(launch_k(set_pos_kernel, dim3(1), dim3(32), 0, m->stream, m->slots[base], (int)position));
+  return Q4GPU_OK;
+}
+
+int q4gpu_model_sync(q4gpu_model* m) {
+  if (!m) return q4gpu_fail(Q4GPU_ERR_ARG, "null model");
+  int rc = set_device(m);
+  if (rc) return rc;
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  for (size_t i = 0; i < m->busy.size(); ++i) m->busy[i] = 0;
+  return Q4GPU_OK;
+}
+
+int q4gpu_model_read_tokens(q4gpu_model* m, uintptr_t base, int32_t start, int32_t n, int32_t* tokens,
+                            int64_t* scores, int32_t* position) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || start < 0 || n < 0 || start + n > m->cfg.max_context + 2)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad read_tokens");
+  int rc = set_device(m);
+  if (rc) return rc;
+  const SlotState& st = m->slots[base];
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  if (n && tokens) Q4_CUDA(cudaMemcpy(tokens, st.tokens + start, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  if (n && scores) Q4_CUDA(cudaMemcpy(scores, st.scores + start, (size_t)n * 8, cudaMemcpyDeviceToHost));
+  if (position) Q4_CUDA(cudaMemcpy(position, st.pos, 4, cudaMemcpyDeviceToHost));
+  return Q4GPU_OK;
+}
+
+int q4gpu_model_time_kernels(q4gpu_model* m, uintptr_t base, int32_t reps, double* ms_per_launch,
+                             int32_t* launches_per_step) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || reps <= 0 || !ms_per_launch || !launches_per_step)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad time_kernels");
+  int rc = set_device(m);
+  if (rc) return rc;
+  double tot[Q4GPU_K_COUNT] = {0};
+  int cnt[Q4GPU_K_COUNT] = {0};
+  for (int r = 0; r < reps; ++r) {
+    KernelMarks mk;
+    if ((rc = enqueue_step(m, (int)base, 0, m->cfg.n_layers, 1, 1, &mk))) return rc;
+    Q4_CUDA(cudaStreamSynchronize(m->stream));
+    for (size_t i = 0; i + 1 < mk.ev.size(); ++i) {
+      float ms = 0.f;
+      Q4_CUDA(cudaEventElapsedTime(&ms, mk.ev[i], mk.ev[i + 1]));
+      tot[mk.kind[i]] += ms;
+      cnt[mk.kind[i]] += 1;
+    }
+  }
+  for (int k = 0; k < Q4GPU_K_COUNT; ++k) {
+    ms_per_launch[k] = cnt[k] ? tot[k] / cnt[k] : 0.0;
+    launches_per_step[k] = cnt[k] / reps;
+  }
+  return Q4GPU_OK;
 }
 
 int q4gpu_model_read_hidden(q4gpu_model* m, uintptr_t base, int32_t* hidden) {

@@ -165,6 +165,33 @@ class Q4Model:
             raise QotError(rc, "q4gpu_decode_batch")
         return gen.astype(np.int64), scores
 
+    # -- device-resident decode loop ----------------------------------------
+    def decode_steps(self, n_steps: int, slot: int = 0) -> None:
+        """Enqueue n greedy steps continuing slot's decode on the device (async)."""
+        _native.check(self.lib.q4gpu_decode_steps(self.handle, slot, n_steps), "q4gpu_decode_steps")
+
+    def set_position(self, position: int, slot: int = 0) -> None:
+        _native.check(self.lib.q4gpu_model_set_position(self.handle, slot, position), "q4gpu_model_set_position")
+
+    def sync(self) -> None:
+        _native.check(self.lib.q4gpu_model_sync(self.handle), "q4gpu_model_sync")
+
+    def read_tokens(self, start: int, n: int, slot: int = 0) -> tuple[np.ndarray, np.ndarray, int]:
+        t = np.zeros(max(n, 1), dtype=np.int32)
+        s = np.zeros(max(n, 1), dtype=np.int64)
+        pos = C.c_int32(0)
+        _native.check(self.lib.q4gpu_model_read_tokens(self.handle, slot, start, n, _ptr(t), _ptr(s),
+                                                       C.byref(pos)), "q4gpu_model_read_tokens")
+        return t[:n].astype(np.int64), s[:n], pos.value
+
+    def time_kernels(self, reps: int = 3, slot: int = 0) -> dict[str, tuple[float, int]]:
+        """Mean device ms per launch and launches per step of each kernel kind."""
+        ms = np.zeros(8, dtype=np.float64)
+        cnt = np.zeros(8, dtype=np.int32)
+        _native.check(self.lib.q4gpu_model_time_kernels(self.handle, slot, reps, _ptr(ms), _ptr(cnt)),
+                      "q4gpu_model_time_kernels")
+        return {k: (float(ms[i]), int(cnt[i])) for i, k in enumerate(_native.KERNEL_KINDS) if cnt[i]}
+
     # -- state access ------------------------------------------------------
     def read_hidden(self, slot: int = 0) -> np.ndarray:
         h = np.empty(HIDDEN, dtype=np.int32)

@@ -169,3 +169,25 @@ def test_full_model_matches_reference_golden(refmodel):
         gen, res = gm.decode(prompt, len(refmodel["generated"]), slot=1)
         assert gen == refmodel["generated"].tolist()
         assert res.score_q26 == int(refmodel["generated_scores"][-1])
+
+
+def test_device_decode_loop_matches_oracle(small):
+    """decode_steps / set_position / read_tokens / time_kernels: the
+    device-resident greedy loop used by bench.py, cycled back to a position."""
+    gm, om = small
+    prompt = [9, 8, 7]
+    gen, _ = gm.decode(prompt, 1, slot=0)
+    gm.decode_steps(5, slot=0)
+    toks, scores, pos = gm.read_tokens(3, 6, slot=0)
+    ref, ref_scores = O.greedy_decode(om, prompt, 6, max_ctx=128)
+    assert toks.tolist() == ref and scores.tolist() == ref_scores and pos == 8
+    gm.set_position(3, slot=0)  # replay the same five steps: identical tokens
+    gm.decode_steps(5, slot=0)
+    toks2, _, pos2 = gm.read_tokens(3, 6, slot=0)
+    assert toks2.tolist() == ref and pos2 == 8
+    gm.set_position(3, slot=0)
+    kt = gm.time_kernels(reps=2, slot=0)
+    assert kt["qkv_norm_rope_kv"][1] == 2 and kt["final_norm_lm_head_argmax"][1] == 1
+    assert all(v[0] > 0 for v in kt.values())
+    toks3, _, _ = gm.read_tokens(3, 3, slot=0)
+    assert toks3.tolist() == ref[:3]
