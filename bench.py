@@ -253,7 +253,7 @@ def run_ours(args, ws, rank, local):
     enqueue(warm, state)
     m.sync()
     # parity spot check of the cycle: the device must reproduce the first cycle's tokens
-    toks, _, _ = m.read_tokens(PROMPT_LEN, min(warm, CYCLE) + 1)
+    toks = m.read_tokens(PROMPT_LEN, min(warm, CYCLE) + 1)[0].tolist()
 
     sampler = ClockSampler(local)
     sampler.start()
