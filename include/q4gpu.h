@@ -144,6 +144,30 @@ int q4gpu_lm_head_argmax(const int32_t *act, const uint8_t *packed, const uint16
                          int32_t rows, int64_t *logits, void *workspace, size_t workspace_bytes,
                          int32_t *out_token, int64_t *out_score, void *stream);
 
+/* The LM head + argmax above for callers that cannot allocate device memory.
+ * No counterpart in the reference.  It allocates nothing: its scratch (the
+ * per-CTA partial results and a completion counter, 7120 bytes) is a static
+ * device array inside libq4gpu, present on every GPU that loads the library
+ * until the process exits.  It serves callers whose device memory belongs to
+ * someone else — a serving framework's pre-reserved pool, or a host ported
+ * from the reference's bare-metal runtime that only owns the buffers it
+ * passes in — and latency-critical loops that must not call cudaMalloc, which
+ * synchronises the device.  The caller still passes inputs and outputs (all
+ * device pointers, as above).
+ * - rows must be 1..Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS; anything else returns
+ *   Q4GPU_ERR_ARG before any device work.
+ * - The first call on a device looks up the scratch's device address with that
+ *   device current (cudaGetSymbolAddress); make that first call before any
+ *   stream capture.
+ * - Every call on a device shares the one scratch array and it keeps the last
+ *   call's contents (the completion counter is cleared on each call): calls
+ *   that overlap on the GPU race with each other and must be serialised by
+ *   the caller, e.g. by issuing them on one stream. */
+#define Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS 16777216
+int q4gpu_lm_head_argmax_noalloc(const int32_t *act, const uint8_t *packed, const uint16_t *scale,
+                                 int32_t rows, int64_t *logits, int32_t *out_token, int64_t *out_score,
+                                 void *stream);
+
 /* =========================================================================
  * Runner seam: types of the reference's host runtime
  * (FPGA_Project/software/qmap_one_token_runtime/qmap_one_token_runtime.h:17-82),

@@ -81,6 +81,7 @@ SIGNATURES = {
     "q4gpu_embedding": (C.c_int, [P, I32, P, P, P, P]),
     "q4gpu_lm_head_workspace_bytes": (SZ, [I32]),
     "q4gpu_lm_head_argmax": (C.c_int, [P, P, P, I32, P, P, SZ, P, P, P]),
+    "q4gpu_lm_head_argmax_noalloc": (C.c_int, [P, P, P, I32, P, P, P, P]),
     "q4gpu_model_create": (C.c_int, [C.POINTER(ModelConfig), C.POINTER(P)]),
     "q4gpu_model_destroy": (None, [P]),
     "q4gpu_model_init_synthetic": (C.c_int, [P, U64, C.c_float, C.c_float]),

@@ -2,6 +2,8 @@
 // reference's fixed-point decode path, exposed through the C ABI in
 // include/q4gpu.h so each stage can be checked bit-exactly on its own.
 // The decode-step kernels (q4_decode.cu) fuse these same stages.
+#include <mutex>
+
 #include "q4_gemv.cuh"
 #include "q4gpu_internal.h"
 
@@ -362,6 +364,16 @@ __global__ void __launch_bounds__(256) lm_head_kernel(const int32_t* __restrict_
   }
 }
 
+// Scratch of q4gpu_lm_head_argmax_noalloc: the per-CTA best (score, row) of
+// the LM-head grid and its completion counter, 444 * 16 + 16 = 7120 bytes,
+// resident on every device that loads this library.
+struct LmHeadStaticScratch {
+  ArgBest partial[Q4GPU_LM_HEAD_BLOCKS];
+  unsigned int counter;
+  unsigned int pad[3];
+};
+static __device__ __align__(256) LmHeadStaticScratch g_lm_head_static_scratch;
+
 }  // namespace q4
 
 // ===========================================================================
@@ -501,6 +513,48 @@ int q4gpu_lm_head_argmax(const int32_t* act, const uint8_t* packed, const uint16
   cudaMemsetAsync(counter, 0, sizeof(unsigned int), as_stream(stream));
   lm_head_kernel<4><<<Q4GPU_LM_HEAD_BLOCKS, 256, 0, as_stream(stream)>>>(act, packed, scale, rows, logits, partial,
                                                                           counter, out_token, out_score);
+  return q4gpu_check_launch();
+}
+
+// Device address of g_lm_head_static_scratch, looked up once per device (with
+// that device current) on the first no-alloc call there.  In host code the
+// symbol itself is only a host-side stand-in; kernels get this address.
+static int lm_head_static_scratch(q4::LmHeadStaticScratch** out) {
+  static std::mutex mu;
+  static q4::LmHeadStaticScratch* addr[Q4GPU_MAX_DEVICES] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= Q4GPU_MAX_DEVICES) return q4gpu_fail(Q4GPU_ERR_ARG, "device ordinal %d too large", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, q4::g_lm_head_static_scratch);
+    if (e != cudaSuccess)
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cudaGetSymbolAddress(lm-head scratch): %s", cudaGetErrorString(e));
+    addr[dev] = static_cast<q4::LmHeadStaticScratch*>(p);
+  }
+  *out = addr[dev];
+  return Q4GPU_OK;
+}
+
+int q4gpu_lm_head_argmax_noalloc(const int32_t* act, const uint8_t* packed, const uint16_t* scale, int32_t rows,
+                                 int64_t* logits, int32_t* out_token, int64_t* out_score, void* stream) {
+  if (!act || !packed || !scale || !out_token || !out_score) return q4gpu_fail(Q4GPU_ERR_ARG, "null argument");
+  if (rows <= 0 || rows > Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "rows %d outside 1..%d supported by the static LM-head scratch", rows,
+                      Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS);
+  if (((uintptr_t)packed) & 15) return q4gpu_fail(Q4GPU_ERR_ALIGN, "packed weights must be 16-byte aligned");
+  q4::LmHeadStaticScratch* sc = nullptr;
+  int rc = lm_head_static_scratch(&sc);
+  if (rc) return rc;
+  // the completion counter must start at zero (the kernel leaves it at zero,
+  // but an earlier call may have been cut short)
+  const cudaError_t e = cudaMemsetAsync(&sc->counter, 0, sizeof(unsigned int), as_stream(stream));
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "scratch clear: %s", cudaGetErrorString(e));
+  lm_head_kernel<4><<<Q4GPU_LM_HEAD_BLOCKS, 256, 0, as_stream(stream)>>>(act, packed, scale, rows, logits,
+                                                                          sc->partial, &sc->counter, out_token,
+                                                                          out_score);
   return q4gpu_check_launch();
 }
 

@@ -9,6 +9,8 @@
 
 // Blocks of the persistent LM-head kernel (3 resident CTAs on each of 148 SMs).
 #define Q4GPU_LM_HEAD_BLOCKS 444
+// Devices the library keeps per-device state for.
+#define Q4GPU_MAX_DEVICES 64
 
 // Record an error message for q4gpu_last_error() and return `code`.
 int q4gpu_fail(int code, const char* fmt, ...);
