@@ -145,6 +145,28 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
 
 
+def stage_timeline(m, n_steps: int) -> dict:
+    """Mean per-stage work and barrier latency (us) of persistent decode steps."""
+    st = m.trace_persistent(n_steps).astype(np.int64)
+    per_step = 5 * LAYERS + 1
+    names = ["qkv", "attention", "o_proj", "gate_up", "down"]
+    work = {k: [] for k in names + ["lm_head"]}
+    wait = {k: [] for k in names + ["lm_head"]}
+    for s in range(1, n_steps):
+        base = s * per_step
+        prev = st[base - 1, 1]
+        for i in range(per_step):
+            arr, rel = st[base + i]
+            k = "lm_head" if i == per_step - 1 else names[i % 5]
+            work[k].append(arr - prev)
+            wait[k].append(rel - arr)
+            prev = rel
+    out = {k: {"work": round(float(np.mean(work[k])) / 1e3, 3), "barrier": round(float(np.mean(wait[k])) / 1e3, 3)}
+           for k in work}
+    out["step"] = round(float(st[n_steps * per_step - 1, 1] - st[per_step - 1, 1]) / (n_steps - 1) / 1e3, 2)
+    return out
+
+
 def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -293,21 +315,35 @@ def run_ours(args, ws, rank, local):
         e2e_s = float(t.item())
     e2e = ws * e2e_steps / e2e_s
 
-    # per-kernel device times (plain launches with events between kernels)
+    # timeline of the persistent kernel: per stage, work (previous release to
+    # the last CTA's arrival) and barrier latency (last arrival to release)
+    m.set_position(PROMPT_LEN)
+    m.sync()
+    tl = stage_timeline(m, 4) if m.mode == 1 else None
+    # per-kernel device times of the per-stage kernels (mode 0, events between kernels)
     m.set_position(PROMPT_LEN)
     m.sync()
     kt = m.time_kernels(reps=3)
-    share = {k: v[0] * v[1] for k, v in kt.items()}
-    tot = sum(share.values())
-    dom = max(share, key=share.get)
-    ctx_mid = PROMPT_LEN + 2  # time_kernels ran at positions 128..130
-    dom_bytes = kernel_bytes(dom, ctx_mid)
     peaks = measured_peaks()
-    achieved = dom_bytes / (kt[dom][0] * 1e-3) / 1e9
     lm = "final_norm_lm_head_argmax"
     lm_gbs = kernel_bytes(lm, 0) / (kt[lm][0] * 1e-3) / 1e9
-    step_gb = step_bytes(PROMPT_LEN + CYCLE // 2) / 1e9
-    launches = sum(v[1] for v in kt.values())
+    step_b = step_bytes(PROMPT_LEN + CYCLE // 2)
+    step_gb = step_b / 1e9
+    if m.mode == 1:
+        # one persistent launch per 128-step cycle: its bytes over its device time
+        dom = "decode_persistent_kernel"
+        dom_bytes = step_b * CYCLE
+        dom_ms = ms_max / steps * CYCLE
+        launches = -(-steps // CYCLE) * 2  # the persistent kernel + a position reset per cycle
+    else:
+        share = {k: v[0] * v[1] for k, v in kt.items()}
+        dom = max(share, key=share.get)
+        dom_bytes = kernel_bytes(dom, PROMPT_LEN + 2)
+        dom_ms = kt[dom][0]
+        launches = sum(v[1] for v in kt.values()) * steps
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    share = {k: v[0] * v[1] for k, v in kt.items()}
+    tot = sum(share.values())
 
     if rank == 0:
         line = {
@@ -322,15 +358,17 @@ def run_ours(args, ws, rank, local):
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"], "traffic": profiled_traffic(dom),
-                         "bytes_per_launch": dom_bytes, "ms_per_launch": round(kt[dom][0], 5)},
+                         "bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5)},
+            "mode": "persistent cooperative kernel" if m.mode == 1 else "per-stage kernels in CUDA graphs",
+            "stage_timeline_us": tl,
             "step_roofline": {"bytes_per_step": int(step_gb * 1e9),
                               "achieved_gbs": round(step_gb / (ms_max / steps / 1000.0), 1),
                               "frac": round(step_gb / (ms_max / steps / 1000.0) / peaks["hbm_gbs"], 4)},
             "gemv": {"kernel": "lm head 151936x1024 Q4 GEMV + argmax", "gbs": round(lm_gbs, 1),
                      "frac": round(lm_gbs / peaks["hbm_gbs"], 4)},
-            "kernels": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
-                            "share": round(share[k] / tot, 4)} for k, v in kt.items()},
-            "gpu_launches": launches * steps,
+            "stage_kernels_mode0": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
+                                        "share": round(share[k] / tot, 4)} for k, v in kt.items()},
+            "gpu_launches": launches,
             "clocks": clocks,
         }
         if ws == 1 and not args.no_cpu_baseline:

@@ -343,6 +343,22 @@ void q4gpu_build_rope_table(int32_t positions, int32_t *cos_q1_15, int32_t *sin_
  * LM head writing tokens[pos+1] and advancing pos).  Returns without waiting;
  * q4gpu_model_sync waits.  The caller keeps pos + n_steps < max_context. */
 int q4gpu_decode_steps(q4gpu_model *m, uintptr_t base, int32_t n_steps);
+/* Execution mode of q4gpu_decode_steps / q4gpu_decode_token_ids / decode_batch:
+ * 0 = one CUDA graph of per-stage kernels per step (PDL-chained);
+ * 1 = the persistent cooperative kernel, many steps per launch (default when
+ *     its shared memory fits; q4gpu_run_token always uses mode 0).
+ * A persistent launch whose grid barrier wait runs out reports through
+ * q4gpu_model_sync (Q4GPU_ERR_CUDA) or QOT_ERR_TIMEOUT from the decode API. */
+int q4gpu_model_set_mode(q4gpu_model *m, int32_t mode);
+int32_t q4gpu_model_get_mode(q4gpu_model *m);
+
+/* Diagnostics: run n_steps persistent decode steps of slot `base` (the LM head
+ * where p + 1 >= lm_from) and return, for each of the first n_barriers grid
+ * barriers, {last CTA's arrival, release} in %globaltimer ns (uint64 [n_barriers, 2]).
+ * Per step there are 5 barriers per layer, then one after the LM head. */
+int q4gpu_model_trace_persistent(q4gpu_model *m, uintptr_t base, int32_t n_steps, int32_t lm_from,
+                                 uint64_t *stamps, int32_t n_barriers);
+
 /* Set slot's next position, stream-ordered after the slot's queued work. */
 int q4gpu_model_set_position(q4gpu_model *m, uintptr_t base, int32_t position);
 int q4gpu_model_sync(q4gpu_model *m);

@@ -100,6 +100,9 @@ SIGNATURES = {
     "q4gpu_model_stream": (P, [P]),
     "q4gpu_decode_steps": (C.c_int, [P, C.c_size_t, I32]),
     "q4gpu_model_sync": (C.c_int, [P]),
+    "q4gpu_model_set_mode": (C.c_int, [P, I32]),
+    "q4gpu_model_get_mode": (I32, [P]),
+    "q4gpu_model_trace_persistent": (C.c_int, [P, C.c_size_t, I32, I32, P, I32]),
     "q4gpu_model_set_position": (C.c_int, [P, C.c_size_t, I32]),
     "q4gpu_model_read_tokens": (C.c_int, [P, C.c_size_t, I32, I32, P, P, P]),
     "q4gpu_model_time_kernels": (C.c_int, [P, C.c_size_t, I32, P, P]),

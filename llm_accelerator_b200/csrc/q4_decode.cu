@@ -9,6 +9,8 @@
 // previous kernel, so weight traffic overlaps the dependency.  Position,
 // token and score live in device memory, so successive replays feed the
 // argmax back without a host round trip.
+#include <cudaTypedefs.h>
+
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -19,63 +21,10 @@
 #include <vector>
 
 #include "q4_gemv.cuh"
+#include "q4_state.cuh"
 #include "q4gpu_internal.h"
 
 namespace q4 {
-
-// ---------------------------------------------------------------------------
-// Device-side views
-// ---------------------------------------------------------------------------
-struct KvView {
-  int32_t* pool;         // [n_pages][layers][2][8][64][128] int32
-  const int32_t* pages;  // this slot's page table: logical page -> physical page
-  int64_t page_elems;    // layers * 2 * 8 * 64 * 128
-  __device__ __forceinline__ int32_t* at(int layer, int kind, int head, int pos) const {
-    return pool + (int64_t)pages[pos >> 6] * page_elems +
-           ((((int64_t)layer * 2 + kind) * kKvHeads + head) * kKvPage + (pos & (kKvPage - 1))) * kHeadDim;
-  }
-};
-
-struct ArgBestD {
-  int64_t score;
-  int32_t idx;
-  int32_t pad;
-};
-
-struct SlotState {
-  int32_t* pos;     // [1] position of the next step
-  int32_t* tokens;  // [max_ctx + 1] input token per position; argmax written at pos+1
-  int64_t* scores;  // [max_ctx + 1]
-  int32_t* hidden;  // [1024] Q14.10 layer input / output
-  int32_t* qrope;   // [2048] Q12.12
-  int32_t* attn;    // [2048] Q12.12
-  int32_t* post;    // [1024] Q14.10
-  int32_t* mlp;     // [3072] Q12.12
-  ArgBestD* lm_partial;
-  unsigned int* lm_counter;
-  KvView kv;
-};
-
-struct LayerW {
-  const uint8_t* wqkv;  // [4096, 512]: q rows 0..2047, k 2048..3071, v 3072..4095
-  const uint16_t* sqkv;
-  const uint8_t* wo;  // [1024, 1024]
-  const uint16_t* so;
-  const uint8_t* wgate;  // [3072, 512]
-  const uint16_t* sgate;
-  const uint8_t* wup;
-  const uint16_t* sup;
-  const uint8_t* wdown;  // [1024, 1536]
-  const uint16_t* sdown;
-  const int32_t* g_in;
-  const int32_t* g_post;
-  const int32_t* g_q;
-  const int32_t* g_k;
-};
-
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 // Hidden-size RMSNorm of `src` (Q14.10) into `dst` (Q12.12), block-wide.
 __device__ __forceinline__ void hidden_norm_to(const int32_t* __restrict__ src, const int32_t* __restrict__ gamma,
@@ -97,6 +46,7 @@ __device__ __forceinline__ void hidden_norm_to(const int32_t* __restrict__ src, 
 __global__ void embed_step_kernel(SlotState st, const uint8_t* __restrict__ W, const uint16_t* __restrict__ S) {
   grid_dep_wait();
   grid_dep_launch();
+  if (*st.pos >= st.max_ctx) return;  // stepping past the context does nothing
   const int t = st.tokens[*st.pos];
   const uint8_t* row = W + (size_t)t * (kHidden / 2);
   const uint16_t* sc = S + (size_t)t * (kHidden / kGroup);
@@ -124,6 +74,7 @@ __global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, i
   }
   grid_dep_wait();
   grid_dep_launch();
+  if (*st.pos >= st.max_ctx) return;
   hidden_norm_to(st.hidden, w.g_in, a, red);
   __syncthreads();
   stage_limbs(a, kHidden, limbs, bias8);
@@ -173,6 +124,7 @@ __global__ void __launch_bounds__(256) attn_step_kernel(SlotState st, int layer,
   const int kv = blockIdx.x;
   grid_dep_wait();
   grid_dep_launch();
+  if (*st.pos >= st.max_ctx) return;
   const int ctx = *st.pos + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   for (int i = threadIdx.x; i < 2 * kHeadDim; i += blockDim.x) q[i / kHeadDim][i % kHeadDim] = st.qrope[2 * kv * kHeadDim + i];
@@ -354,6 +306,7 @@ __global__ void __launch_bounds__(256) lmhead_step_kernel(SlotState st, const ui
   grid_dep_wait();
   grid_dep_launch();
   const int pos = *st.pos;
+  if (pos >= st.max_ctx) return;
   hidden_norm_to(st.hidden, g_final, a, red);
   __syncthreads();
   stage_limbs(a, kHidden, limbs, bias8);
@@ -400,7 +353,7 @@ __global__ void __launch_bounds__(256) lmhead_step_kernel(SlotState st, const ui
 __global__ void advance_step_kernel(SlotState st) {
   grid_dep_wait();
   grid_dep_launch();
-  if (threadIdx.x == 0) *st.pos += 1;
+  if (threadIdx.x == 0 && *st.pos < st.max_ctx) *st.pos += 1;
 }
 
 __global__ void set_pos_kernel(SlotState st, int position) {
@@ -502,6 +455,16 @@ struct q4gpu_model {
   std::vector<cudaEvent_t> done;
   std::vector<int> busy;
   std::map<GraphKey, cudaGraphExec_t> graphs;
+  // persistent decode kernel (mode 1)
+  int mode = 0;
+  int p_grid = 0;
+  size_t p_smem = 0;
+  LayerW* layers_dev = nullptr;
+  int32_t* p_qkv = nullptr;
+  ArgBestD* p_lm_part = nullptr;
+  unsigned int* p_bar = nullptr;
+  int* p_err = nullptr;
+  CUtensorMap vmap{};
 
   template <class T>
   int alloc(T** p, size_t count) {
@@ -687,6 +650,81 @@ int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int
   return mark(-1);
 }
 
+// 2-D tensor map over the KV pool for the persistent kernel's V-slice loads:
+// rows of 128 int32 (one position of one (page, layer, kind, head)), box of
+// 64 positions x 16 dims.
+int encode_kv_map(q4gpu_model* m, int64_t n_pages) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q) !=
+          cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !encode)
+    return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t rows = (cuuint64_t)n_pages * m->cfg.n_layers * 2 * kKvHeads * kKvPage;
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 4};
+  const cuuint32_t box[2] = {16, (cuuint32_t)kKvPage};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(&m->vmap, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, m->kv_pool, dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q4GPU_OK;
+}
+
+// n_steps decode steps of `slot` in one persistent launch, continuing from
+// the slot's device position; the LM head runs where p + 1 >= lm_from.
+int run_persistent(q4gpu_model* m, int slot, int n_steps, int lm_from, unsigned long long* trace = nullptr,
+                   int trace_cap = 0) {
+  if (n_steps <= 0) return Q4GPU_OK;
+  PersistArgs a{};
+  a.vmap = m->vmap;
+  a.st = m->slots[slot];
+  a.layers = m->layers_dev;
+  a.n_layers = m->cfg.n_layers;
+  a.emb = m->emb;
+  a.semb = m->semb;
+  a.vocab = m->cfg.vocab;
+  a.g_final = m->g_final;
+  a.cos_tab = m->cos_tab;
+  a.sin_tab = m->sin_tab;
+  a.exp_lut = m->exp_lut;
+  a.sig_lut = m->sig_lut;
+  a.qkv = m->p_qkv;
+  a.lm_part = m->p_lm_part;
+  a.bar = m->p_bar;
+  a.err = m->p_err;
+  a.n_steps = n_steps;
+  a.lm_from = lm_from;
+  a.score_cap = m->cfg.max_context;
+  a.trace = trace;
+  a.trace_cap = trace_cap;
+  // the arrival counter of one launch counts (5 L + 1) G per step: split very
+  // long runs so it stays below 2^32
+  const int per_launch = (int)std::min<int64_t>(
+      (int64_t)0xF0000000 / ((int64_t)m->p_grid * (5 * m->cfg.n_layers + 1)), 1 << 20);
+  int rc = Q4GPU_OK;
+  for (int done = 0; done < n_steps && rc == Q4GPU_OK; done += per_launch) {
+    a.n_steps = std::min(per_launch, n_steps - done);
+    Q4_CUDA(cudaMemsetAsync(m->p_bar, 0, 2 * sizeof(unsigned int), m->stream));
+    rc = q4gpu_launch_persistent(a, m->p_grid, m->p_smem, m->stream);
+    a.trace = nullptr;
+  }
+  return rc;
+}
+
+int check_persistent_error(q4gpu_model* m) {
+  if (!m->p_err) return Q4GPU_OK;
+  int e = 0;
+  Q4_CUDA(cudaMemcpy(&e, m->p_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(m->p_err, 0, sizeof(int));
+    return q4gpu_fail(Q4GPU_ERR_CUDA, e == 2 ? "persistent decode kernel: stepped past max_context"
+                                             : "persistent decode kernel: a grid barrier wait ran out");
+  }
+  return Q4GPU_OK;
+}
+
 int get_graph(q4gpu_model* m, const GraphKey& k, cudaGraphExec_t* out) {
   auto it = m->graphs.find(k);
   if (it != m->graphs.end()) {
@@ -858,6 +896,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
     st.lm_partial = part + (size_t)i * Q4GPU_LM_HEAD_BLOCKS;
     st.lm_counter = ctr + (size_t)i * 32;
     st.kv = KvView{m->kv_pool, m->page_tables + (size_t)i * m->pages_per_seq, m->page_elems};
+    st.max_ctx = cfg->max_context;
     m->slots.push_back(st);
   }
   if (cudaMallocHost(&m->h_res, sizeof(HostResult) * S) != cudaSuccess ||
@@ -871,6 +910,19 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   const size_t asmem = attn_smem(cfg->max_context);
   if (cudaFuncSetAttribute(attn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem) != cudaSuccess)
     return fail(q4gpu_fail(Q4GPU_ERR_SHAPE, "max_context %d needs %zu B of shared memory", cfg->max_context, asmem));
+  // persistent kernel: available when its shared memory fits (score buffer of max_context)
+  if ((rc = m->alloc(&m->layers_dev, (size_t)L))) return fail(rc);
+  if (cudaMemcpy(m->layers_dev, m->layers, sizeof(LayerW) * L, cudaMemcpyHostToDevice) != cudaSuccess)
+    return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "layer table upload"));
+  if ((rc = m->alloc(&m->p_qkv, (size_t)kQRows + 2 * kKvRows))) return fail(rc);
+  if ((rc = m->alloc(&m->p_lm_part, 1024))) return fail(rc);
+  if ((rc = m->alloc(&m->p_bar, 16))) return fail(rc);
+  if ((rc = m->alloc(&m->p_err, 16))) return fail(rc);
+  if (q4gpu_persistent_setup(cfg->max_context, &m->p_smem, &m->p_grid) == Q4GPU_OK && m->p_grid <= 1024 &&
+      encode_kv_map(m, n_pages) == Q4GPU_OK)
+    m->mode = 1;
+  else
+    m->p_grid = 0;
   *out = m;
   return Q4GPU_OK;
 }
@@ -1100,8 +1152,12 @@ int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_
   bool ok = cudaMemcpyAsync(st.tokens + cfg->position, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice,
                             m->stream) == cudaSuccess &&
             cudaMemcpyAsync(st.pos, &hin[1], 4, cudaMemcpyHostToDevice, m->stream) == cudaSuccess;
-  for (uint32_t i = 0; ok && i + 1 < prompt_token_count; ++i) ok = cudaGraphLaunch(gpre, m->stream) == cudaSuccess;
-  for (uint32_t i = 0; ok && i < max_new_tokens; ++i) ok = cudaGraphLaunch(gstep, m->stream) == cudaSuccess;
+  if (m->mode == 1) {
+    ok = ok && run_persistent(m, slot, (int)run_count, (int)(cfg->position + prompt_token_count)) == Q4GPU_OK;
+  } else {
+    for (uint32_t i = 0; ok && i + 1 < prompt_token_count; ++i) ok = cudaGraphLaunch(gpre, m->stream) == cudaSuccess;
+    for (uint32_t i = 0; ok && i < max_new_tokens; ++i) ok = cudaGraphLaunch(gstep, m->stream) == cudaSuccess;
+  }
   const uint32_t first = cfg->position + prompt_token_count;
   ok = ok &&
        cudaMemcpyAsync(gen.data(), st.tokens + first, max_new_tokens * 4, cudaMemcpyDeviceToHost, m->stream) ==
@@ -1119,6 +1175,7 @@ int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_
   rc = poll_slot(m, slot, (uint32_t)std::min<uint64_t>(polls, 0xFFFFFFFFull));
   memset(last_result, 0, sizeof(*last_result));
   if (rc != QOT_OK) return rc;
+  if (m->mode == 1 && check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
   for (uint32_t i = 0; i < max_new_tokens; ++i) {
     if ((uint32_t)gen[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
     generated_token_ids[i] = (uint32_t)gen[i];
@@ -1163,11 +1220,39 @@ int q4gpu_decode_steps(q4gpu_model* m, uintptr_t base, int32_t n_steps) {
   if (!m || base >= (uintptr_t)m->cfg.max_seqs || n_steps < 0) return q4gpu_fail(Q4GPU_ERR_ARG, "bad decode_steps");
   int rc = set_device(m);
   if (rc) return rc;
+  if (m->mode == 1) return run_persistent(m, (int)base, n_steps, 0);
   cudaGraphExec_t g;
   if ((rc = get_graph(m, GraphKey{(int)base, 0, m->cfg.n_layers, 1, 1}, &g))) return rc;
   for (int i = 0; i < n_steps; ++i) Q4_CUDA(cudaGraphLaunch(g, m->stream));
   return Q4GPU_OK;
 }
+
+int q4gpu_model_trace_persistent(q4gpu_model* m, uintptr_t base, int32_t n_steps, int32_t lm_from,
+                                 uint64_t* stamps, int32_t n_barriers) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || n_steps <= 0 || !stamps || n_barriers <= 0)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad trace request");
+  if (m->p_grid == 0) return q4gpu_fail(Q4GPU_ERR_SHAPE, "persistent kernel unavailable");
+  int rc = set_device(m);
+  if (rc) return rc;
+  unsigned long long* dev = nullptr;
+  Q4_CUDA(cudaMalloc(&dev, (size_t)n_barriers * 2 * sizeof(unsigned long long)));
+  bool ok = cudaMemsetAsync(dev, 0, (size_t)n_barriers * 16, m->stream) == cudaSuccess &&
+            run_persistent(m, (int)base, n_steps, lm_from, dev, n_barriers) == Q4GPU_OK &&
+            cudaStreamSynchronize(m->stream) == cudaSuccess &&
+            cudaMemcpy(stamps, dev, (size_t)n_barriers * 16, cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(dev);
+  if (!ok) return q4gpu_fail(Q4GPU_ERR_CUDA, "trace run failed");
+  return check_persistent_error(m);
+}
+
+int q4gpu_model_set_mode(q4gpu_model* m, int32_t mode) {
+  if (!m || (mode != 0 && mode != 1)) return q4gpu_fail(Q4GPU_ERR_ARG, "mode must be 0 or 1");
+  if (mode == 1 && m->p_grid == 0) return q4gpu_fail(Q4GPU_ERR_SHAPE, "persistent kernel unavailable");
+  m->mode = mode;
+  return Q4GPU_OK;
+}
+
+int32_t q4gpu_model_get_mode(q4gpu_model* m) { return m ? m->mode : -1; }
 
 int q4gpu_model_set_position(q4gpu_model* m, uintptr_t base, int32_t position) {
   if (!m || base >= (uintptr_t)m->cfg.max_seqs || position < 0 || position >= m->cfg.max_context)
@@ -1185,7 +1270,7 @@ int q4gpu_model_sync(q4gpu_model* m) {
   if (rc) return rc;
   Q4_CUDA(cudaStreamSynchronize(m->stream));
   for (size_t i = 0; i < m->busy.size(); ++i) m->busy[i] = 0;
-  return Q4GPU_OK;
+  return check_persistent_error(m);
 }
 
 int q4gpu_model_read_tokens(q4gpu_model* m, uintptr_t base, int32_t start, int32_t n, int32_t* tokens,

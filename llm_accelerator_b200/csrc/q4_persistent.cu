@@ -1,0 +1,876 @@
+// Persistent cooperative decode kernel: many batch-1 greedy decode steps of
+// one sequence slot in a single launch.
+//
+// One CTA per SM (512 threads) walks every step through the stages
+//   S1  input norm + QKV GEMV (rows split over the grid)      -> qkv (raw Q12.12)
+//   S2  q/k head norm + RoPE, KV append, attention            -> attn
+//   S3  o_proj + residual                                     -> post
+//   S4  post-attention norm + gate/up + SwiGLU                -> mlp
+//   S5  down + residual                                       -> hidden
+//   ... x layers, then final norm + LM head + argmax           -> next token
+// separated by grid-wide barriers.  Nothing that does not depend on this
+// step's activations waits behind a barrier: every CTA prefetches into L2 its
+// weight slices of the layer ahead, loads its weights of the next stage into
+// registers before arriving at the barrier, and copies the K rows and V slice
+// of its attention head into shared memory with TMA bulk copies (mbarrier
+// completion) while the QKV stage runs.  Attention assigns each KV head to
+// kAttnSplit CTAs, each owning a slice of head_dim: every CTA of a head
+// recomputes the (cheap) scores, max and exp sum from its shared-memory copy
+// of K, so no cross-CTA exchange is needed.
+// The argmax is reduced redundantly by every CTA after a barrier, so the
+// next step's embedding starts without another one.
+//
+// Inter-CTA data is read with ld.global.cg (L2) after acquire/release
+// barriers; weights use the read-only path.  Every barrier wait is bounded:
+// on timeout the kernel sets an error word and all CTAs leave.
+#include "q4_gemv.cuh"
+#include "q4_state.cuh"
+#include "q4gpu_internal.h"
+
+namespace q4 {
+
+constexpr int kPThreads = 512;
+constexpr int kPWarps = kPThreads / 32;
+constexpr int kAttnSplit = 8;  // CTAs per KV head (head_dim slices of 16)
+constexpr int kSliceDims = kHeadDim / kAttnSplit;
+constexpr uint32_t kSpinLimit = 1u << 22;
+constexpr int kKvWindow = 256;  // cached positions staged in shared memory
+
+// ---- memory-model helpers ---------------------------------------------------
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int32_t ldcg(const int32_t* p) { return __ldcg(p); }
+__device__ __forceinline__ int4 ldcg4(const int32_t* p) { return __ldcg(reinterpret_cast<const int4*>(p)); }
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier / bulk-copy helpers (shared memory of this CTA) --------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(b))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Bounded wait for phase `parity` of *b; false if it ran out (error word set,
+// then one more bounded wait so no copy is still landing when the CTA exits).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* err) {
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 1023) == 1023 && *((volatile int*)err) != 0) break;
+  }
+  atomicCAS(err, 0, 3);
+  for (uint32_t it = 0; it < kSpinLimit && !mbar_try_wait(b, parity); ++it) {
+  }
+  return false;
+}
+
+// Grid-wide barrier: arrivals count in bar[0]; the last CTA to arrive resets
+// it and bumps the generation word bar[1], which the others poll (acquire).
+// `hook` runs on warp 1 between arrival and release (work that needs no
+// result of this stage, e.g. L2 prefetches).  Returns false when the wait ran
+// out or another CTA reported an error; the caller then returns.
+struct Barrier {
+  unsigned* bar;
+  int* err;
+  int* s_flag;
+  unsigned long long* trace;
+  int trace_cap;
+  unsigned index;
+};
+
+struct NoHook {
+  __device__ void operator()() const {}
+};
+
+template <class Hook = NoHook>
+__device__ __forceinline__ bool grid_sync(Barrier& b, Hook hook = Hook()) {
+  __syncthreads();
+  const unsigned idx = b.index++;
+  if (threadIdx.x == 0) {
+    if (b.trace && (int)idx < b.trace_cap) atomicMax(&b.trace[2 * idx], globaltimer());
+    const unsigned gen = ld_acquire_u32(b.bar + 1);
+    __threadfence();
+    const unsigned arrived = atomicAdd(b.bar, 1u);
+    int ok = 1;
+    if (arrived == gridDim.x - 1) {
+      atomicExch(b.bar, 0u);
+      __threadfence();
+      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(b.bar + 1), "r"(gen + 1) : "memory");
+    } else {
+      uint32_t it = 0;
+      while (ld_acquire_u32(b.bar + 1) == gen) {
+        if (++it > kSpinLimit || ((it & 255) == 0 && *((volatile int*)b.err) != 0)) {
+          atomicCAS(b.err, 0, 1);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    if (b.trace && blockIdx.x == 0 && (int)idx < b.trace_cap) b.trace[2 * idx + 1] = globaltimer();
+    *b.s_flag = ok;
+  } else if (threadIdx.x == 32) {
+    hook();
+  }
+  __syncthreads();
+  return *b.s_flag != 0;
+}
+
+__device__ __forceinline__ int part_of(int n, int i, int g) { return (int)(((int64_t)n * i) / g); }
+
+// Limbs of K activations in shared memory, one 8-element chunk per thread.
+__device__ __forceinline__ void stage_limbs_par(const int32_t* act, int K, uint32_t* limbs, int64_t* bias8) {
+  const int c = threadIdx.x;
+  int64_t s = 0;
+  if (c < K / 8) {
+    make_limbs8(act + 8 * c, limbs + (c >> 2) * kLimbStride + (c & 3) * 6);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += act[8 * c + e];
+  }
+  s += shfl_xor_i64(s, 1);
+  s += shfl_xor_i64(s, 2);
+  if (c < K / 8 && (c & 3) == 0) bias8[c >> 2] = 8 * s;
+}
+
+// Hidden-size RMSNorm of act[] in place (Q14.10 -> Q12.12).
+__device__ __forceinline__ void hidden_norm_inplace(int32_t* act, const int32_t* __restrict__ gamma, int64_t* red) {
+  int64_t ss = 0;
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) ss += (int64_t)act[i] * act[i];
+  ss = block_sum_i64(ss, red);
+  const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) act[i] = norm_apply(act[i], inv, gamma[i], kHiddenNorm);
+}
+
+// Block-wide max (and sum) of two int64 values at once; red needs 32 slots.
+__device__ __forceinline__ void block_max2(int64_t& x, int64_t& y, int64_t* red) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const int64_t ox = shfl_xor_i64(x, m), oy = shfl_xor_i64(y, m);
+    x = ox > x ? ox : x;
+    y = oy > y ? oy : y;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    red[2 * warp] = x;
+    red[2 * warp + 1] = y;
+  }
+  __syncthreads();
+  x = red[0];
+  y = red[1];
+  for (int i = 1; i < nw; ++i) {
+    x = red[2 * i] > x ? red[2 * i] : x;
+    y = red[2 * i + 1] > y ? red[2 * i + 1] : y;
+  }
+}
+
+__device__ __forceinline__ void block_sum2(int64_t& x, int64_t& y, int64_t* red) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    x += shfl_xor_i64(x, m);
+    y += shfl_xor_i64(y, m);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    red[2 * warp] = x;
+    red[2 * warp + 1] = y;
+  }
+  __syncthreads();
+  x = 0;
+  y = 0;
+  for (int i = 0; i < nw; ++i) {
+    x += red[2 * i];
+    y += red[2 * i + 1];
+  }
+}
+
+// ---- GEMV items with weights preloaded into registers -----------------------
+// Item `it` is row row_of(it / KS) of a matrix at K-slice it % KS; warp w owns
+// items w, w + 16, ..., (RMAX of them).  The preload runs before a barrier,
+// the compute after it.
+template <int K, int RMAX>
+struct Pre {
+  uint4 w[RMAX];
+  uint32_t sc[RMAX];
+};
+
+template <int K, int RMAX, class RowFn>
+__device__ __forceinline__ void preload_items(int n_items, RowFn row_of, Pre<K, RMAX>& pre) {
+  constexpr int KS = K / 1024;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < RMAX; ++j) {
+    const int it = warp + j * kPWarps;
+    if (it < n_items) {
+      const uint8_t* W;
+      const uint16_t* S;
+      row_of(it / KS, W, S);
+      const int hg = (it % KS) * 32 + lane;
+      pre.w[j] = ldg_stream(W + (size_t)hg * 16);
+      pre.sc[j] = __ldg(S + (hg >> 1));
+    } else {
+      pre.w[j] = make_uint4(0, 0, 0, 0);
+      pre.sc[j] = 0;
+    }
+  }
+}
+
+template <int K, int RMAX>
+__device__ __forceinline__ void compute_items(int n_items, const Pre<K, RMAX>& pre, const uint32_t* limbs,
+                                              const int64_t* bias8, int64_t* part) {
+  constexpr int KS = K / 1024;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < RMAX; ++j) {
+    const int it = warp + j * kPWarps;
+    if (it < n_items) {
+      const int hg = (it % KS) * 32 + lane;
+      const uint32_t* l = limbs + hg * kLimbStride;
+      uint32_t l24[24];
+#pragma unroll
+      for (int i = 0; i < 6; ++i) {
+        const uint4 t = reinterpret_cast<const uint4*>(l)[i];
+        l24[4 * i] = t.x;
+        l24[4 * i + 1] = t.y;
+        l24[4 * i + 2] = t.z;
+        l24[4 * i + 3] = t.w;
+      }
+      const int64_t v = warp_sum_i64(lane_span(pre.w[j], l24, bias8[hg], pre.sc[j]));
+      if (lane == 0) part[it] = v;
+    }
+  }
+}
+
+struct PSmem {
+  int32_t* act;       // [3072]
+  uint32_t* limbs;    // [96 * 28]
+  int64_t* bias8;     // [96]
+  int64_t* part;      // [256]
+  int64_t* red;       // [32]
+  int64_t* sc;        // [2 * score_cap]
+  uint64_t* probtab;  // [2 * 257]
+  int32_t* hv;        // [4 * 128]: q0, q1, k, v of the attention head
+  int64_t* vacc;      // [32 * kSliceDims * 2]
+  int32_t* kwin;      // [kKvWindow * 128]: cached K rows of the attention head
+  int32_t* vwin;      // [kKvWindow * kSliceDims]: cached V of this CTA's dims
+  uint64_t* mbar;     // [5]: KV copy completion, then 4 LM-head ring slots
+  int32_t* own;       // [16]: this CTA's rows of hidden (0..7) and post (8..15)
+  int* flag;
+};
+
+constexpr int kLmChunkRows = 64;  // LM-head rows per ring slot (32 KB + 2 KB)
+constexpr int kLmRing = 4;
+
+// ---- prefetch of the weights this CTA reads later ---------------------------
+// L2 prefetch of a byte range in pieces of at most 32 KB.
+__device__ __forceinline__ void prefetch_range(const void* p, size_t bytes) {
+  const char* c = static_cast<const char*>(p);
+  for (size_t off = 0; off < bytes; off += 32768)
+    prefetch_l2(c + off, (uint32_t)(bytes - off < 32768 ? bytes - off : 32768));
+}
+
+__device__ __forceinline__ void prefetch_rows(const uint8_t* W, const uint16_t* S, int K, int r0, int r1) {
+  if (r1 > r0) {
+    prefetch_range(W + (size_t)r0 * (K / 2), (size_t)(r1 - r0) * (K / 2));
+    prefetch_range(S + (size_t)r0 * (K / 64), (size_t)(r1 - r0) * (K / 64) * 2);
+  }
+}
+
+__device__ void prefetch_layer(const LayerW& w, int cta, int G) {
+  prefetch_rows(w.wqkv, w.sqkv, kHidden, part_of(4096, cta, G), part_of(4096, cta + 1, G));
+  prefetch_rows(w.wo, w.so, 2 * kHidden, part_of(kHidden, cta, G), part_of(kHidden, cta + 1, G));
+  const int g0 = part_of(kInter, cta, G), g1 = part_of(kInter, cta + 1, G);
+  prefetch_rows(w.wgate, w.sgate, kHidden, g0, g1);
+  prefetch_rows(w.wup, w.sup, kHidden, g0, g1);
+  prefetch_rows(w.wdown, w.sdown, kInter, part_of(kHidden, cta, G), part_of(kHidden, cta + 1, G));
+}
+
+// TMA copies of head h's cached K rows [0, n) (1-D bulk, one per page) and
+// V dims [d0, d0+16) (2-D tensor map, one 64 x 16 box per page) of `layer`
+// into shared memory; completion on sm.mbar[0] (one phase).
+__device__ void issue_kv_copies(const PersistArgs& a, const PSmem& sm, int layer, int n) {
+  const int h = blockIdx.x / kAttnSplit, d0 = (blockIdx.x % kAttnSplit) * kSliceDims;
+  // order earlier generic reads of the windows and the (acquired) generic
+  // writes of the KV rows by other CTAs before the async-proxy copies
+  fence_proxy_async();
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int pages = (n + kKvPage - 1) / kKvPage;
+    mbar_arrive_expect_tx(sm.mbar, (unsigned)n * kHeadDim * 4 + (unsigned)pages * kKvPage * kSliceDims * 4);
+    for (int pg = 0; pg < pages; ++pg) {
+      const int p0 = pg * kKvPage;
+      bulk_g2s(sm.kwin + p0 * kHeadDim, a.st.kv.at(layer, 0, h, p0), (unsigned)min(kKvPage, n - p0) * kHeadDim * 4,
+               sm.mbar);
+      const int row = (int)((((int64_t)a.st.kv.pages[pg] * a.n_layers + layer) * 2 + 1) * kKvHeads + h) * kKvPage;
+      tma_load_2d(sm.vwin + p0 * kSliceDims, &a.vmap, d0, row, sm.mbar);
+    }
+  }
+}
+
+// LM-head chunk `j` of this CTA's rows into ring slot j % kLmRing.
+__device__ __forceinline__ void issue_lm_chunk(const PersistArgs& a, const PSmem& sm, int r0, int r1, int j) {
+  const int c0 = r0 + j * kLmChunkRows;
+  if (c0 >= r1) return;
+  const int rows = min(kLmChunkRows, r1 - c0);
+  const int slot = j % kLmRing;
+  uint64_t* mb = sm.mbar + 1 + slot;
+  mbar_arrive_expect_tx(mb, (unsigned)rows * (512 + 32));
+  bulk_g2s(reinterpret_cast<uint8_t*>(sm.kwin) + (size_t)slot * kLmChunkRows * 512, a.emb + (size_t)c0 * 512,
+           (unsigned)rows * 512, mb);
+  bulk_g2s(reinterpret_cast<uint8_t*>(sm.vwin) + (size_t)slot * kLmChunkRows * 32, a.semb + (size_t)c0 * 16,
+           (unsigned)rows * 32, mb);
+}
+
+// ---- stages -----------------------------------------------------------------
+using PreQkv = Pre<kHidden, 2>;
+using PreO = Pre<2 * kHidden, 1>;
+using PreGU = Pre<kHidden, 3>;
+using PreDown = Pre<kInter, 2>;
+
+__device__ __forceinline__ void preload_qkv(const LayerW& w, PreQkv& pre) {
+  const int r0 = part_of(4096, blockIdx.x, gridDim.x), r1 = part_of(4096, blockIdx.x + 1, gridDim.x);
+  preload_items(r1 - r0, [&](int r, const uint8_t*& W, const uint16_t*& S) {
+    W = w.wqkv + (size_t)(r0 + r) * 512;
+    S = w.sqkv + (size_t)(r0 + r) * 16;
+  }, pre);
+}
+__device__ __forceinline__ void preload_oproj(const LayerW& w, PreO& pre) {
+  const int r0 = part_of(kHidden, blockIdx.x, gridDim.x), r1 = part_of(kHidden, blockIdx.x + 1, gridDim.x);
+  preload_items((r1 - r0) * 2, [&](int r, const uint8_t*& W, const uint16_t*& S) {
+    W = w.wo + (size_t)(r0 + r) * 1024;
+    S = w.so + (size_t)(r0 + r) * 32;
+  }, pre);
+}
+__device__ __forceinline__ void preload_gateup(const LayerW& w, PreGU& pre) {
+  const int r0 = part_of(kInter, blockIdx.x, gridDim.x), r1 = part_of(kInter, blockIdx.x + 1, gridDim.x);
+  const int n = r1 - r0;
+  preload_items(2 * n, [&](int r, const uint8_t*& W, const uint16_t*& S) {
+    const bool up = r >= n;
+    const int row = r0 + (up ? r - n : r);
+    W = (up ? w.wup : w.wgate) + (size_t)row * 512;
+    S = (up ? w.sup : w.sgate) + (size_t)row * 16;
+  }, pre);
+}
+__device__ __forceinline__ void preload_down(const LayerW& w, PreDown& pre) {
+  const int r0 = part_of(kHidden, blockIdx.x, gridDim.x), r1 = part_of(kHidden, blockIdx.x + 1, gridDim.x);
+  preload_items((r1 - r0) * 3, [&](int r, const uint8_t*& W, const uint16_t*& S) {
+    W = w.wdown + (size_t)(r0 + r) * 1536;
+    S = w.sdown + (size_t)(r0 + r) * 48;
+  }, pre);
+}
+
+__device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm, bool first_layer,
+                          const PreQkv& pre) {
+  const int G = gridDim.x, cta = blockIdx.x;
+  // the layer input: the embedding (already in act) or the previous layer's output
+  if (!first_layer)
+    for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
+      *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
+  __syncthreads();
+  hidden_norm_inplace(sm.act, w.g_in, sm.red);
+  __syncthreads();
+  stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
+  __syncthreads();
+  const int r0 = part_of(4096, cta, G), r1 = part_of(4096, cta + 1, G);
+  compute_items(r1 - r0, pre, sm.limbs, sm.bias8, sm.part);
+  __syncthreads();
+  for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) a.qkv[r0 + i] = sat24(sm.part[i] >> 14);
+}
+
+// returns false on a copy timeout
+__device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSmem& sm, int layer, int pos,
+                                unsigned& mbar_phase) {
+  const int cta = blockIdx.x;
+  if (cta >= kKvHeads * kAttnSplit) return true;
+  const int h = cta / kAttnSplit, sl = cta % kAttnSplit, d0 = sl * kSliceDims;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int ctx = pos + 1;
+  int32_t* q0 = sm.hv;
+  int32_t* q1 = sm.hv + kHeadDim;
+  int32_t* kc = sm.hv + 2 * kHeadDim;
+  int32_t* vc = sm.hv + 3 * kHeadDim;
+  // raw q (2 heads), k, v of this KV head; then per-head norm and RoPE
+  int32_t raw = 0;
+  if (t < 3 * kHeadDim) {
+    const int which = t / kHeadDim, d = t % kHeadDim;
+    const int row = which < 2 ? (2 * h + which) * kHeadDim + d : kQRows + h * kHeadDim + d;
+    raw = ldcg(a.qkv + row);
+  } else if (t < 4 * kHeadDim) {
+    vc[t - 3 * kHeadDim] = ldcg(a.qkv + kQRows + kKvRows + h * kHeadDim + (t - 3 * kHeadDim));
+  }
+  int64_t sq = t < 3 * kHeadDim ? (int64_t)raw * raw : 0;
+  sq = warp_sum_i64(sq);
+  if (lane == 0) sm.red[warp] = sq;
+  __syncthreads();
+  if (t < 3 * kHeadDim) {
+    const int which = t / kHeadDim, d = t % kHeadDim;
+    const int64_t ss = sm.red[which * 4] + sm.red[which * 4 + 1] + sm.red[which * 4 + 2] + sm.red[which * 4 + 3];
+    const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
+    const int32_t* gamma = which < 2 ? w.g_q : w.g_k;
+    sm.hv[which * kHeadDim + d] = norm_apply(raw, inv, gamma[d], kHeadNorm);
+  }
+  __syncthreads();
+  int32_t rot_v = 0;
+  if (t < 3 * kHeadDim) {
+    const int which = t / kHeadDim, d = t % kHeadDim;
+    const int32_t* x = sm.hv + which * kHeadDim;
+    const int64_t rot = d < 64 ? -(int64_t)x[d + 64] : (int64_t)x[d - 64];
+    rot_v = sat24(((int64_t)x[d] * a.cos_tab[pos * kHeadDim + d] + rot * a.sin_tab[pos * kHeadDim + d]) >> 15);
+  }
+  __syncthreads();
+  if (t < 3 * kHeadDim) sm.hv[t] = rot_v;
+  if (sl == 0 && t >= 3 * kHeadDim && t < 4 * kHeadDim) {
+    // this position's V goes to the cache (K below, after RoPE is in smem)
+    a.st.kv.at(layer, 1, h, pos)[t - 3 * kHeadDim] = vc[t - 3 * kHeadDim];
+  }
+  __syncthreads();
+  if (sl == 0 && t < kHeadDim) a.st.kv.at(layer, 0, h, pos)[t] = kc[t];
+  // the cached K rows and V slice were copied into shared memory during QKV
+  if (!mbar_wait(sm.mbar, mbar_phase, a.err)) return false;
+  mbar_phase ^= 1u;
+  // scores: 8 threads per position, thread c owns dims {4c + 32j + e}
+  {
+    const int pp = t >> 3, c = t & 7;
+    int32_t qa[16], qb[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        qa[4 * j + e] = q0[4 * c + 32 * j + e];
+        qb[4 * j + e] = q1[4 * c + 32 * j + e];
+      }
+    const int64_t scale = 189812531LL;
+    for (int p0 = 0; p0 < ctx; p0 += kPThreads / 8) {
+      const int p = p0 + pp;
+      int64_t s0 = 0, s1 = 0;
+      if (p < ctx) {
+        const int32_t* krow = p == pos ? kc : sm.kwin + p * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * c + 32 * j);
+          s0 += (int64_t)qa[4 * j] * k4.x + (int64_t)qa[4 * j + 1] * k4.y + (int64_t)qa[4 * j + 2] * k4.z +
+                (int64_t)qa[4 * j + 3] * k4.w;
+          s1 += (int64_t)qb[4 * j] * k4.x + (int64_t)qb[4 * j + 1] * k4.y + (int64_t)qb[4 * j + 2] * k4.z +
+                (int64_t)qb[4 * j + 3] * k4.w;
+        }
+      }
+#pragma unroll
+      for (int m = 1; m < 8; m <<= 1) {
+        s0 += shfl_xor_i64(s0, m);
+        s1 += shfl_xor_i64(s1, m);
+      }
+      if (c == 0 && p < ctx) {
+        sm.sc[p] = scale_score(s0, scale);
+        sm.sc[a.score_cap + p] = scale_score(s1, scale);
+      }
+    }
+  }
+  __syncthreads();
+  {
+    int64_t* s0 = sm.sc;
+    int64_t* s1 = sm.sc + a.score_cap;
+    int64_t m0 = INT64_MIN, m1 = INT64_MIN;
+    for (int p = t; p < ctx; p += blockDim.x) {
+      m0 = s0[p] > m0 ? s0[p] : m0;
+      m1 = s1[p] > m1 ? s1[p] : m1;
+    }
+    block_max2(m0, m1, sm.red);
+    int64_t e0 = 0, e1 = 0;
+    for (int p = t; p < ctx; p += blockDim.x) {
+      const int i0 = lut_index(m0, s0[p]), i1 = lut_index(m1, s1[p]);
+      s0[p] = i0;
+      s1[p] = i1;
+      e0 += a.exp_lut[i0];
+      e1 += a.exp_lut[i1];
+    }
+    block_sum2(e0, e1, sm.red);
+    for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
+      const int hh = i / kExpLut, k = i % kExpLut;
+      sm.probtab[i] = ((uint64_t)a.exp_lut[k] << 16) / (uint64_t)(hh ? e1 : e0);
+    }
+  }
+  __syncthreads();
+  // sum(prob * v) over this CTA's head_dim slice: thread = (dim, position lane)
+  {
+    const int dl = t % kSliceDims, pl = t / kSliceDims;  // pl in [0, 32)
+    int64_t acc0 = 0, acc1 = 0;
+    for (int p = pl; p < ctx; p += kPThreads / kSliceDims) {
+      const int64_t v = p == pos ? (int64_t)vc[d0 + dl] : (int64_t)sm.vwin[p * kSliceDims + dl];
+      acc0 += (int64_t)sm.probtab[sm.sc[p]] * v;
+      acc1 += (int64_t)sm.probtab[kExpLut + sm.sc[a.score_cap + p]] * v;
+    }
+    sm.vacc[(pl * kSliceDims + dl) * 2] = acc0;
+    sm.vacc[(pl * kSliceDims + dl) * 2 + 1] = acc1;
+  }
+  __syncthreads();
+  if (t < 2 * kSliceDims) {
+    const int dl = t % kSliceDims, hh = t / kSliceDims;
+    int64_t acc = 0;
+    for (int pl = 0; pl < kPThreads / kSliceDims; ++pl) acc += sm.vacc[(pl * kSliceDims + dl) * 2 + hh];
+    a.st.attn[(2 * h + hh) * kHeadDim + d0 + dl] = sat24(acc >> 16);
+  }
+  return true;
+}
+
+__device__ void stage_oproj(const PersistArgs& a, const PSmem& sm, const PreO& pre) {
+  const int G = gridDim.x, cta = blockIdx.x;
+  constexpr int K = 2 * kHidden;
+  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
+    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.attn + i);
+  __syncthreads();
+  stage_limbs_par(sm.act, K, sm.limbs, sm.bias8);
+  __syncthreads();
+  const int r0 = part_of(kHidden, cta, G), r1 = part_of(kHidden, cta + 1, G);
+  compute_items((r1 - r0) * 2, pre, sm.limbs, sm.bias8, sm.part);
+  __syncthreads();
+  for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) {
+    const int32_t o = sat24((sm.part[2 * i] + sm.part[2 * i + 1]) >> 14);
+    const int32_t post = sat24((int64_t)sm.own[i] + (o >> 2));
+    a.st.post[r0 + i] = post;
+    sm.own[8 + i] = post;
+  }
+}
+
+__device__ void stage_gateup(const PersistArgs& a, const LayerW& w, const PSmem& sm, const PreGU& pre) {
+  const int G = gridDim.x, cta = blockIdx.x;
+  for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
+    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.post + i);
+  __syncthreads();
+  hidden_norm_inplace(sm.act, w.g_post, sm.red);
+  __syncthreads();
+  stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
+  __syncthreads();
+  const int r0 = part_of(kInter, cta, G), r1 = part_of(kInter, cta + 1, G), n = r1 - r0;
+  compute_items(2 * n, pre, sm.limbs, sm.bias8, sm.part);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int32_t g = sat24(sm.part[i] >> 14), u = sat24(sm.part[n + i] >> 14);
+    const int32_t gc = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
+    int ix = (gc + 32768 + 32) >> 6;
+    ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
+    const int32_t silu = sat24(((int64_t)g * a.sig_lut[ix]) >> 16);
+    a.st.mlp[r0 + i] = sat24(((int64_t)silu * u) >> 12);
+  }
+}
+
+__device__ void stage_down(const PersistArgs& a, const PSmem& sm, const PreDown& pre) {
+  const int G = gridDim.x, cta = blockIdx.x;
+  constexpr int K = kInter;
+  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
+    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.mlp + i);
+  __syncthreads();
+  stage_limbs_par(sm.act, K, sm.limbs, sm.bias8);
+  __syncthreads();
+  const int r0 = part_of(kHidden, cta, G), r1 = part_of(kHidden, cta + 1, G);
+  compute_items((r1 - r0) * 3, pre, sm.limbs, sm.bias8, sm.part);
+  __syncthreads();
+  for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) {
+    const int32_t dn = sat24((sm.part[3 * i] + sm.part[3 * i + 1] + sm.part[3 * i + 2]) >> 14);
+    const int32_t hid = sat24((int64_t)sm.own[8 + i] + (dn >> 2));
+    a.st.hidden[r0 + i] = hid;
+    sm.own[i] = hid;
+  }
+}
+
+// final norm + this CTA's LM-head rows (streamed through the shared-memory
+// ring; chunks 0..kLmRing-1 were issued before the barrier) + local argmax
+// -> lm_part[cta].  Bit s of `ring_phase` is the phase parity ring slot s waits
+// on next (each slot alternates strictly between one issue and one use).
+__device__ void stage_lmhead(const PersistArgs& a, const PSmem& sm, unsigned& ring_phase) {
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
+    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
+  __syncthreads();
+  hidden_norm_inplace(sm.act, a.g_final, sm.red);
+  __syncthreads();
+  stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
+  __syncthreads();
+  const int r0 = part_of(a.vocab, cta, G), r1 = part_of(a.vocab, cta + 1, G);
+  const int n_chunks = (r1 - r0 + kLmChunkRows - 1) / kLmChunkRows;
+  int64_t best_s = INT64_MIN;
+  int32_t best_i = INT32_MAX;
+  // limbs of this lane's half-group stay in registers for every row
+  uint32_t l24[24];
+  {
+    const uint4* lp = reinterpret_cast<const uint4*>(sm.limbs + lane * kLimbStride);
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint4 t = lp[i];
+      l24[4 * i] = t.x;
+      l24[4 * i + 1] = t.y;
+      l24[4 * i + 2] = t.z;
+      l24[4 * i + 3] = t.w;
+    }
+  }
+  const int64_t b8 = sm.bias8[lane];
+  for (int j = 0; j < n_chunks; ++j) {
+    const int slot = j % kLmRing;
+    if (!mbar_wait(sm.mbar + 1 + slot, (ring_phase >> slot) & 1u, a.err)) return;
+    ring_phase ^= 1u << slot;
+    const int c0 = r0 + j * kLmChunkRows;
+    const int rows = min(kLmChunkRows, r1 - c0);
+    const uint8_t* wbuf = reinterpret_cast<const uint8_t*>(sm.kwin) + (size_t)slot * kLmChunkRows * 512;
+    const uint16_t* sbuf =
+        reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(sm.vwin) + (size_t)slot * kLmChunkRows * 32);
+    constexpr int RW = kLmChunkRows / kPWarps;  // rows per warp per chunk
+    int64_t acc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+      const int row = warp * RW + r;
+      acc[r] = 0;
+      if (row < rows) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(wbuf + (size_t)row * 512 + lane * 16);
+        acc[r] = lane_span(wv, l24, b8, sbuf[row * 16 + (lane >> 1)]);
+      }
+    }
+    warp_reduce_rows<RW>(acc);
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+      const int row = warp * RW + r;
+      if (row < rows && acc[r] > best_s) {  // ascending rows within a warp
+        best_s = acc[r];
+        best_i = c0 + row;
+      }
+    }
+    __syncthreads();  // every warp is done with this slot
+    if (threadIdx.x == 0 && j + kLmRing < n_chunks) issue_lm_chunk(a, sm, r0, r1, j + kLmRing);
+  }
+  if (lane == 0) {
+    sm.part[2 * warp] = best_s;
+    sm.part[2 * warp + 1] = best_i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t bs = sm.part[0];
+    int32_t bi = (int32_t)sm.part[1];
+    for (int i = 1; i < kPWarps; ++i) {
+      const int64_t sv = sm.part[2 * i];
+      const int32_t idx = (int32_t)sm.part[2 * i + 1];
+      if (sv > bs || (sv == bs && idx < bi)) {
+        bs = sv;
+        bi = idx;
+      }
+    }
+    __stcg(&a.lm_part[cta].score, bs);
+    __stcg(&a.lm_part[cta].idx, bi);
+  }
+}
+
+// Reduce the per-CTA bests with warp 0 (lowest row wins ties); result in sm.part[0..1].
+__device__ void reduce_lm_parts(const PersistArgs& a, const PSmem& sm) {
+  if (threadIdx.x < 32) {
+    int64_t bs = INT64_MIN;
+    int32_t bi = INT32_MAX;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += 32) {
+      const int64_t s = __ldcg(&a.lm_part[i].score);
+      const int32_t idx = __ldcg(&a.lm_part[i].idx);
+      if (s > bs || (s == bs && idx < bi)) {
+        bs = s;
+        bi = idx;
+      }
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      const int64_t os = shfl_xor_i64(bs, m);
+      const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, m);
+      if (os > bs || (os == bs && oi < bi)) {
+        bs = os;
+        bi = oi;
+      }
+    }
+    if (threadIdx.x == 0) {
+      sm.part[0] = bi;
+      sm.part[1] = bs;
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const __grid_constant__ PersistArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  PSmem sm;
+  {
+    unsigned char* p = smem_raw;
+    auto take = [&](size_t bytes) {
+      unsigned char* r = p;
+      p += (bytes + 127) & ~(size_t)127;
+      return r;
+    };
+    sm.kwin = reinterpret_cast<int32_t*>(take((size_t)kKvWindow * kHeadDim * 4));
+    sm.vwin = reinterpret_cast<int32_t*>(take((size_t)kKvWindow * kSliceDims * 4));
+    sm.act = reinterpret_cast<int32_t*>(take(kInter * 4));
+    sm.limbs = reinterpret_cast<uint32_t*>(take(limb_words(kInter) * 4));
+    sm.bias8 = reinterpret_cast<int64_t*>(take((kInter / 32) * 8));
+    sm.part = reinterpret_cast<int64_t*>(take(256 * 8));
+    sm.red = reinterpret_cast<int64_t*>(take(32 * 8));
+    sm.probtab = reinterpret_cast<uint64_t*>(take(2 * kExpLut * 8));
+    sm.hv = reinterpret_cast<int32_t*>(take(4 * kHeadDim * 4));
+    sm.vacc = reinterpret_cast<int64_t*>(take((size_t)kPThreads * 2 * 8));
+    sm.mbar = reinterpret_cast<uint64_t*>(take(8 * 8));
+    sm.own = reinterpret_cast<int32_t*>(take(16 * 4));
+    sm.flag = reinterpret_cast<int*>(take(16));
+    sm.sc = reinterpret_cast<int64_t*>(take((size_t)2 * a.score_cap * 8));
+  }
+  const int G = gridDim.x, cta = blockIdx.x;
+  const bool attn_cta = cta < kKvHeads * kAttnSplit;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 1 + kLmRing; ++i) mbar_init(sm.mbar + i, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  Barrier bar{a.bar, a.err, sm.flag, a.trace, a.trace_cap, 0u};
+  unsigned mbar_phase = 0;
+  unsigned ring_phase = 0;
+  int pos = ldcg(a.st.pos);
+  int next_tok = -1;
+  const int h0 = part_of(kHidden, cta, G), h1 = part_of(kHidden, cta + 1, G);
+  const int v0 = part_of(a.vocab, cta, G), v1 = part_of(a.vocab, cta + 1, G);
+  PreQkv pq;
+  PreO po;
+  PreGU pg;
+  PreDown pd;
+  for (int step = 0; step < a.n_steps; ++step) {
+    if (pos >= a.st.max_ctx) {  // every CTA sees the same pos: all stop here
+      if (cta == 0 && threadIdx.x == 0) atomicCAS(a.err, 0, 2);
+      break;
+    }
+    const bool lm = pos + 1 >= a.lm_from;
+    const int tok = next_tok >= 0 ? next_tok : ldcg(a.st.tokens + pos);
+    // tied embedding: the whole vector for the first norm, and this CTA's
+    // rows of the residual stream
+    {
+      const uint8_t* row = a.emb + (size_t)tok * (kHidden / 2);
+      const uint16_t* sc = a.semb + (size_t)tok * (kHidden / kGroup);
+      for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+        const uint8_t b = row[i >> 1];
+        const int q = (int)((i & 1) ? (b >> 4) : (b & 0xF));
+        sm.act[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < h1 - h0; i += blockDim.x) {
+        a.st.hidden[h0 + i] = sm.act[h0 + i];
+        sm.own[i] = sm.act[h0 + i];
+      }
+    }
+    preload_qkv(a.layers[0], pq);
+    for (int l = 0; l < a.n_layers; ++l) {
+      const LayerW w = a.layers[l];
+      const bool last = l + 1 == a.n_layers;
+      if (attn_cta) issue_kv_copies(a, sm, l, pos);
+      preload_oproj(w, po);
+      stage_qkv(a, w, sm, l == 0, pq);
+      // L2 prefetch of the next layer's weight slices while waiting
+      if (!grid_sync(bar, [&] {
+            if (!last) prefetch_layer(a.layers[l + 1], cta, G);
+          }))
+        return;
+      if (!stage_attention(a, w, sm, l, pos, mbar_phase)) return;
+      if (!grid_sync(bar)) return;
+      preload_gateup(w, pg);
+      stage_oproj(a, sm, po);
+      if (!grid_sync(bar)) return;
+      preload_down(w, pd);
+      stage_gateup(a, w, sm, pg);
+      if (!grid_sync(bar)) return;
+      if (!last) preload_qkv(a.layers[l + 1], pq);
+      stage_down(a, sm, pd);
+      if (last && lm) {
+        // the first LM-head chunks stream in while the layer barrier resolves
+        fence_proxy_async();
+        __syncthreads();
+        if (threadIdx.x == 0)
+          for (int j = 0; j < kLmRing; ++j) issue_lm_chunk(a, sm, v0, v1, j);
+      }
+      if (!grid_sync(bar)) return;
+    }
+    next_tok = -1;
+    if (lm) {
+      stage_lmhead(a, sm, ring_phase);
+      if (!grid_sync(bar)) return;
+      reduce_lm_parts(a, sm);
+      if (cta == 0 && threadIdx.x == 0) {
+        a.st.tokens[pos + 1] = (int32_t)sm.part[0];
+        a.st.scores[pos + 1] = sm.part[1];
+      }
+      next_tok = (int)sm.part[0];
+      __syncthreads();
+      // lm_part is rewritten only after the next step's 5 x layers barriers
+    }
+    ++pos;
+  }
+  if (cta == 0 && threadIdx.x == 0) *a.st.pos = pos;
+}
+
+size_t persistent_smem_bytes(int score_cap) {
+  auto r = [](size_t b) { return (b + 127) & ~(size_t)127; };
+  return r((size_t)kKvWindow * kHeadDim * 4) + r((size_t)kKvWindow * kSliceDims * 4) + r(kInter * 4) +
+         r(limb_words(kInter) * 4) + r((kInter / 32) * 8) + r(256 * 8) + r(32 * 8) + r(2 * kExpLut * 8) +
+         r(4 * kHeadDim * 4) + r((size_t)kPThreads * 2 * 8) + r(64) + r(64) + r(16) + r((size_t)2 * score_cap * 8) +
+         128;
+}
+
+}  // namespace q4
+
+// Host launcher, called by the runtime in q4_decode.cu.
+int q4gpu_launch_persistent(const q4::PersistArgs& args, int grid, size_t smem, cudaStream_t stream) {
+  void* params[] = {const_cast<q4::PersistArgs*>(&args)};
+  const cudaError_t e = cudaLaunchCooperativeKernel((const void*)q4::decode_persistent_kernel, dim3(grid),
+                                                    dim3(q4::kPThreads), params, smem, stream);
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
+  return Q4GPU_OK;
+}
+
+int q4gpu_persistent_setup(int score_cap, size_t* smem, int* grid) {
+  // attention stages at most kKvWindow cached positions in shared memory
+  if (score_cap > q4::kKvWindow + 1)
+    return q4gpu_fail(Q4GPU_ERR_SHAPE, "persistent kernel supports max_context <= %d", q4::kKvWindow + 1);
+  *smem = q4::persistent_smem_bytes(score_cap);
+  cudaError_t e = cudaFuncSetAttribute(q4::decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)*smem);
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "persistent smem %zu: %s", *smem, cudaGetErrorString(e));
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, q4::decode_persistent_kernel, q4::kPThreads, *smem);
+  if (e != cudaSuccess || per_sm < 1)
+    return q4gpu_fail(Q4GPU_ERR_CUDA, "persistent kernel does not fit one CTA per SM");
+  // one CTA per SM; the register preloads cover one pass when the grid has >= 128 CTAs
+  *grid = sms;
+  if (*grid < 128) return q4gpu_fail(Q4GPU_ERR_SHAPE, "persistent kernel needs >= 128 SMs (%d)", sms);
+  return Q4GPU_OK;
+}

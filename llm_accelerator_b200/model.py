@@ -170,6 +170,23 @@ class Q4Model:
         """Enqueue n greedy steps continuing slot's decode on the device (async)."""
         _native.check(self.lib.q4gpu_decode_steps(self.handle, slot, n_steps), "q4gpu_decode_steps")
 
+    @property
+    def mode(self) -> int:
+        """0: per-stage kernels in CUDA graphs; 1: persistent cooperative kernel."""
+        return int(self.lib.q4gpu_model_get_mode(self.handle))
+
+    @mode.setter
+    def mode(self, value: int) -> None:
+        _native.check(self.lib.q4gpu_model_set_mode(self.handle, value), "q4gpu_model_set_mode")
+
+    def trace_persistent(self, n_steps: int, lm_from: int = 0, slot: int = 0) -> np.ndarray:
+        """[barriers, 2] (last arrival, release) ns of a persistent run."""
+        n = n_steps * (5 * self.n_layers + 1)
+        st = np.zeros((n, 2), dtype=np.uint64)
+        _native.check(self.lib.q4gpu_model_trace_persistent(self.handle, slot, n_steps, lm_from, _ptr(st), n),
+                      "q4gpu_model_trace_persistent")
+        return st
+
     def set_position(self, position: int, slot: int = 0) -> None:
         _native.check(self.lib.q4gpu_model_set_position(self.handle, slot, position), "q4gpu_model_set_position")
 

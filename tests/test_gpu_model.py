@@ -191,3 +191,42 @@ def test_device_decode_loop_matches_oracle(small):
     assert all(v[0] > 0 for v in kt.values())
     toks3, _, _ = gm.read_tokens(3, 3, slot=0)
     assert toks3.tolist() == ref[:3]
+
+
+def test_persistent_and_graph_modes_agree(small):
+    """Mode 1 (persistent cooperative kernel, the default) and mode 0
+    (per-stage kernels in CUDA graphs) give the oracle's tokens and scores."""
+    gm, om = small
+    assert gm.mode == 1, "persistent kernel should be available for this shape"
+    prompt = [11, 2222, 3333, 44, 5555, 6]
+    ref, ref_scores = O.greedy_decode(om, prompt, 9, max_ctx=128)
+    for mode in (1, 0, 1):
+        gm.mode = mode
+        toks, res = gm.decode(prompt, 9, slot=1)
+        assert toks == ref, mode
+        assert res.score_q26 == ref_scores[-1]
+        _, scores, pos = gm.read_tokens(len(prompt), 9, slot=1)
+        assert scores.tolist() == ref_scores and pos == len(prompt) + 8
+    gm.mode = 1
+
+
+def test_stepping_past_max_context_is_refused(small):
+    gm, om = small
+    prompt = [1, 2, 3]
+    gm.decode(prompt, 1, slot=0)
+    gm.set_position(126, slot=0)
+    for mode in (1, 0):
+        gm.mode = mode
+        gm.set_position(126, slot=0)
+        gm.decode_steps(4, slot=0)  # 126, 127 are valid; 128 and 129 are not
+        if mode == 1:
+            with pytest.raises(_native.Q4GpuError):
+                gm.sync()
+        else:
+            gm.sync()
+        _, _, pos = gm.read_tokens(0, 0, slot=0)
+        assert pos == 128
+    gm.mode = 1
+    # the context is still usable afterwards
+    toks, _ = gm.decode([5, 6], 3, slot=0)
+    assert toks == O.greedy_decode(om, [5, 6], 3, max_ctx=128)[0]
