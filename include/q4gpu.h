@@ -306,11 +306,37 @@ int q4gpu_decode_token_ids(q4gpu_model *m, uintptr_t base, const qot_run_config_
                            uint32_t *generated_token_count, qot_result_t *last_result);
 
 /* Batched greedy decode of independent sequences (slots 0..n_seq-1), each
- * with its own prompt (prompts concatenated; prompt_lens[n_seq]).
- * generated: uint32 [n_seq, max_new_tokens]; scores (optional) int64 same shape. */
+ * with its own prompt (prompts concatenated; prompt_lens[n_seq]), every prompt
+ * starting at position 0.  Up to 64 sequences advance together per step
+ * (groups of 64 run one after another), sharing each weight read; results are
+ * identical to decoding each sequence alone with q4gpu_decode_token_ids.
+ * generated: uint32 [n_seq, max_new_tokens]; scores (optional) int64 same shape.
+ * Returns QOT_* codes: QOT_ERR_CAPACITY (n_seq, an empty prompt, no tokens),
+ * QOT_ERR_CONTEXT (prompt_len + max_new_tokens - 1 > max_context),
+ * QOT_ERR_BAD_TOKEN, QOT_ERR_BUSY, QOT_ERR_STATUS. */
 int q4gpu_decode_batch(q4gpu_model *m, int32_t n_seq, const uint32_t *prompts,
                        const uint32_t *prompt_lens, uint32_t max_new_tokens, uint32_t *generated,
                        int64_t *scores);
+
+/* Batched decode, device-resident loop (no reference counterpart: the
+ * reference decodes one sequence at a time).  Slots [first_slot, first_slot +
+ * n_seq), 1 <= n_seq <= 64.  Each step feeds every sequence the token stored
+ * at its position, runs all layers and the LM head for all of them at once,
+ * stores the argmax at position + 1 (when position + 1 >= its lm_from) and
+ * advances the position.  Asynchronous on the model stream. */
+int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t n_steps);
+
+/* Every slot of the range to `position`; lm_from (>= 0) sets the position
+ * from which argmax tokens are stored, -1 keeps it.  Stream-ordered. */
+int q4gpu_batch_set_position(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t position,
+                             int32_t lm_from);
+
+/* One batched step with host buffers: sequence i of the range takes
+ * token_ids[i] at positions[i] and returns the argmax (and its Q26 score,
+ * optional) of the next position.  Blocks until the results are on the host. */
+int q4gpu_batch_run_step(q4gpu_model *m, int32_t first_slot, int32_t n_seq,
+                         const uint32_t *token_ids, const uint32_t *positions, uint32_t *out_tokens,
+                         int64_t *out_scores);
 
 /* Read back the Q14.10 hidden state after the last layer of slot `base`
  * (int32 [1024]) and the retained K or V entries of one layer in the

@@ -91,6 +91,9 @@ SIGNATURES = {
     "q4gpu_decode_token_ids": (C.c_int, [P, C.c_size_t, C.POINTER(QotRunConfig), P, U32, U32, P, U32, U32,
                                          C.POINTER(U32), C.POINTER(QotResult)]),
     "q4gpu_decode_batch": (C.c_int, [P, I32, P, P, U32, P, P]),
+    "q4gpu_batch_steps": (C.c_int, [P, I32, I32, I32]),
+    "q4gpu_batch_set_position": (C.c_int, [P, I32, I32, I32, I32]),
+    "q4gpu_batch_run_step": (C.c_int, [P, I32, I32, P, P, P, P]),
     "q4gpu_model_read_hidden": (C.c_int, [P, C.c_size_t, P]),
     "q4gpu_model_read_kv": (C.c_int, [P, C.c_size_t, I32, I32, I32, P]),
     "q4gpu_model_write_hidden": (C.c_int, [P, C.c_size_t, P]),

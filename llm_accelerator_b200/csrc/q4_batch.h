@@ -1,0 +1,69 @@
+// Batched decode (q4_batch.cu): device layout and launch interface.
+#pragma once
+#include "q4_state.cuh"
+
+namespace q4 {
+
+constexpr int kBatchSeqMax = 64;  // sequences one batched step advances
+constexpr int kBatchOnes = 8;     // B rows of ones after the 3 SP limb rows
+constexpr int kScoreScale = 189812531;  // round(128^-0.5 * 2^31)
+
+// int8 copies of one layer's Q4 matrices (row-major [rows, K], one byte per
+// weight), with the model's Q2.14 group scales.
+struct BatchLayerW {
+  const int8_t* wqkv;  // [4096, 1024]: q, k, v rows
+  const uint16_t* sqkv;
+  const int8_t* wo;  // [1024, 2048]
+  const uint16_t* so;
+  const int8_t* wgu;  // [6144, 1024]: 32-row blocks, gate rows 32b.. then up rows 32b..
+  const uint16_t* sgu;  // [6144, 16], same row order
+  const int8_t* wdown;  // [1024, 3072]
+  const uint16_t* sdown;
+  const int32_t* g_in;
+  const int32_t* g_post;
+  const int32_t* g_q;
+  const int32_t* g_k;
+};
+
+struct BatchPlan {
+  const SlotState* slots;  // device array [S]: sequence m is slot m
+  int S;                   // live sequences (1..64)
+  int SP;                  // padded sequence count: 8, 16, 24, 32 or 64
+  int32_t* qkv_raw;        // [64, 4096]
+  uint8_t* bt1;            // [3 SP + 8, 1024] limbs of the normed hidden / post vectors
+  uint8_t* bt2;            // [3 SP + 8, 2048] limbs of the attention output
+  uint8_t* bt3;            // [3 SP + 8, 3072] limbs of the SwiGLU output
+  const int32_t* lm_from;  // [S] the argmax is stored at positions p with p + 1 >= lm_from
+  const uint8_t* emb;      // packed Q4 embedding [vocab, 512]
+  const uint16_t* semb;    // [vocab, 16]
+  const int8_t* emb8;      // int8 embedding [vocab, 1024] (LM head)
+  const BatchLayerW* layers;  // host array [n_layers]
+  int n_layers;
+  int max_ctx;
+  int vocab;
+  const int32_t* cos_tab;
+  const int32_t* sin_tab;
+  const int32_t* exp_lut;
+  const int32_t* sig_lut;
+  const int32_t* g_final;
+  ArgBestD* lm_partial;  // [ceil(vocab / 256), 64]
+};
+
+}  // namespace q4
+
+int q4gpu_batch_padded(int S);
+int q4gpu_batch_setup(const q4::BatchPlan& p);
+// One decode position for all S sequences (embedding .. argmax), stream-ordered.
+int q4gpu_enqueue_batch_step(const q4::BatchPlan& p, cudaStream_t s);
+// packed int4 (two per byte, even index in the low nibble) -> int8
+int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s);
+// gate/up packed rows -> the interleaved int8 layout of BatchLayerW::wgu / sgu
+int q4gpu_expand_gu(const uint8_t* gate, const uint8_t* up, const uint16_t* sg, const uint16_t* su, int8_t* out,
+                    uint16_t* sout, cudaStream_t s);
+// in: device [S][2] (token, position); lm_from[m] = 0
+int q4gpu_batch_load(const q4::SlotState* slots, int S, const int32_t* in, int32_t* lm_from, cudaStream_t s);
+// out: device [S][4] int32 = (token, 0, score as int64) at position in[m][1] + 1
+int q4gpu_batch_gather(const q4::SlotState* slots, int S, const int32_t* in, int32_t* out, cudaStream_t s);
+// every sequence to `pos`; lm_from[m] = lm_value unless lm_value < 0
+int q4gpu_batch_set_positions(const q4::SlotState* slots, int S, int pos, int32_t* lm_from, int lm_value,
+                              cudaStream_t s);

@@ -20,6 +20,7 @@
 #include <tuple>
 #include <vector>
 
+#include "q4_batch.h"
 #include "q4_gemv.cuh"
 #include "q4_state.cuh"
 #include "q4gpu_internal.h"
@@ -465,6 +466,23 @@ struct q4gpu_model {
   unsigned int* p_bar = nullptr;
   int* p_err = nullptr;
   CUtensorMap vmap{};
+  // batched decode (q4_batch.cu), set up on first use
+  int8_t* b_w8 = nullptr;     // per layer: qkv [4096,1024], o [1024,2048], gate/up [6144,1024], down [1024,3072]
+  uint16_t* b_sgu = nullptr;  // per layer: gate/up scales [6144,16] in the interleaved row order
+  int8_t* b_emb8 = nullptr;   // [vocab, 1024]
+  int32_t* b_qkv = nullptr;
+  uint8_t* b_bt1 = nullptr;
+  uint8_t* b_bt2 = nullptr;
+  uint8_t* b_bt3 = nullptr;
+  SlotState* b_slots = nullptr;  // device copy of slots
+  int32_t* b_lm_from = nullptr;  // [max_seqs]
+  ArgBestD* b_lm_part = nullptr;
+  int32_t* b_io = nullptr;   // device [64][2] inputs, then [64][4] outputs
+  int32_t* h_bio = nullptr;  // pinned mirror of b_io
+  BatchLayerW b_layers[kMaxLayers]{};
+  bool b_stale = true;  // int8 copies out of date with the Q4 weights
+  int b_ones_sp = 0;    // SP whose ones rows the B matrices hold
+  std::map<std::pair<int, int>, cudaGraphExec_t> b_graphs;  // (first slot, S)
 
   template <class T>
   int alloc(T** p, size_t count) {
@@ -783,6 +801,142 @@ uint64_t step_bytes(const q4gpu_model* m, int layers, int ctx, int tail) {
   return per_layer * layers + (tail ? (uint64_t)m->cfg.vocab * (512 + 32) : 0);
 }
 
+// ---- batched decode (q4_batch.cu) ------------------------------------------
+constexpr size_t kB8Qkv = (size_t)(kQRows + 2 * kKvRows) * kHidden;
+constexpr size_t kB8O = (size_t)kHidden * 2 * kHidden;
+constexpr size_t kB8Gu = (size_t)2 * kInter * kHidden;
+constexpr size_t kB8Down = (size_t)kHidden * kInter;
+constexpr size_t kB8Layer = kB8Qkv + kB8O + kB8Gu + kB8Down;
+constexpr int kBtRows = 3 * kBatchSeqMax + kBatchOnes;
+
+int batch_lm_ctas(int vocab) { return (vocab + 255) / 256; }
+
+// Allocate the batched-decode buffers once and refresh the int8 weight copies
+// when the Q4 weights changed since the last batched call.
+int batch_prepare(q4gpu_model* m) {
+  if (m->cfg.vocab < 64) return q4gpu_fail(Q4GPU_ERR_SHAPE, "batched decode needs a vocabulary of at least 64");
+  const int L = m->cfg.n_layers;
+  int rc;
+  if (!m->b_w8) {
+    if ((rc = m->alloc(&m->b_w8, kB8Layer * L))) return rc;
+    if ((rc = m->alloc(&m->b_sgu, (size_t)2 * kInter * (kHidden / kGroup) * L))) return rc;
+    if ((rc = m->alloc(&m->b_emb8, (size_t)m->cfg.vocab * kHidden))) return rc;
+    if ((rc = m->alloc(&m->b_qkv, (size_t)kBatchSeqMax * (kQRows + 2 * kKvRows)))) return rc;
+    if ((rc = m->alloc(&m->b_bt1, (size_t)kBtRows * kHidden))) return rc;
+    if ((rc = m->alloc(&m->b_bt2, (size_t)kBtRows * 2 * kHidden))) return rc;
+    if ((rc = m->alloc(&m->b_bt3, (size_t)kBtRows * kInter))) return rc;
+    if ((rc = m->alloc(&m->b_slots, m->slots.size()))) return rc;
+    Q4_CUDA(cudaMemcpy(m->b_slots, m->slots.data(), sizeof(SlotState) * m->slots.size(), cudaMemcpyHostToDevice));
+    if ((rc = m->alloc(&m->b_lm_from, (size_t)m->cfg.max_seqs))) return rc;
+    if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
+    if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
+    Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
+    for (int l = 0; l < L; ++l) {
+      int8_t* w = m->b_w8 + kB8Layer * l;
+      const LayerW& q = m->layers[l];
+      BatchLayerW& b = m->b_layers[l];
+      b.wqkv = w;
+      b.sqkv = q.sqkv;
+      b.wo = w + kB8Qkv;
+      b.so = q.so;
+      b.wgu = w + kB8Qkv + kB8O;
+      b.sgu = m->b_sgu + (size_t)2 * kInter * (kHidden / kGroup) * l;
+      b.wdown = w + kB8Qkv + kB8O + kB8Gu;
+      b.sdown = q.sdown;
+      b.g_in = q.g_in;
+      b.g_post = q.g_post;
+      b.g_q = q.g_q;
+      b.g_k = q.g_k;
+    }
+  }
+  if (m->b_stale) {
+    for (int l = 0; l < L; ++l) {
+      const LayerW& q = m->layers[l];
+      BatchLayerW& b = m->b_layers[l];
+      if ((rc = q4gpu_expand_int4(q.wqkv, (int64_t)kB8Qkv / 2, const_cast<int8_t*>(b.wqkv), m->stream))) return rc;
+      if ((rc = q4gpu_expand_int4(q.wo, (int64_t)kB8O / 2, const_cast<int8_t*>(b.wo), m->stream))) return rc;
+      if ((rc = q4gpu_expand_gu(q.wgate, q.wup, q.sgate, q.sup, const_cast<int8_t*>(b.wgu),
+                                const_cast<uint16_t*>(b.sgu), m->stream)))
+        return rc;
+      if ((rc = q4gpu_expand_int4(q.wdown, (int64_t)kB8Down / 2, const_cast<int8_t*>(b.wdown), m->stream))) return rc;
+    }
+    if ((rc = q4gpu_expand_int4(m->emb, (int64_t)m->cfg.vocab * (kHidden / 2), m->b_emb8, m->stream))) return rc;
+    m->b_stale = false;
+  }
+  return Q4GPU_OK;
+}
+
+BatchPlan batch_plan(q4gpu_model* m, int first, int S) {
+  BatchPlan p{};
+  p.slots = m->b_slots + first;
+  p.S = S;
+  p.SP = q4gpu_batch_padded(S);
+  p.qkv_raw = m->b_qkv;
+  p.bt1 = m->b_bt1;
+  p.bt2 = m->b_bt2;
+  p.bt3 = m->b_bt3;
+  p.lm_from = m->b_lm_from + first;
+  p.emb = m->emb;
+  p.semb = m->semb;
+  p.emb8 = m->b_emb8;
+  p.layers = m->b_layers;
+  p.n_layers = m->cfg.n_layers;
+  p.max_ctx = m->cfg.max_context;
+  p.vocab = m->cfg.vocab;
+  p.cos_tab = m->cos_tab;
+  p.sin_tab = m->sin_tab;
+  p.exp_lut = m->exp_lut;
+  p.sig_lut = m->sig_lut;
+  p.g_final = m->g_final;
+  p.lm_partial = m->b_lm_part;
+  return p;
+}
+
+// Graph of one batched step over slots [first, first + S), with the B
+// matrices' ones rows set for its padded size.
+int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out) {
+  int rc = batch_prepare(m);
+  if (rc) return rc;
+  const BatchPlan p = batch_plan(m, first, S);
+  if (m->b_ones_sp != p.SP) {
+    Q4_CUDA(cudaMemsetAsync(m->b_bt1 + (size_t)3 * p.SP * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
+    Q4_CUDA(cudaMemsetAsync(m->b_bt2 + (size_t)3 * p.SP * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden, m->stream));
+    Q4_CUDA(cudaMemsetAsync(m->b_bt3 + (size_t)3 * p.SP * kInter, 1, (size_t)kBatchOnes * kInter, m->stream));
+    m->b_ones_sp = p.SP;
+  }
+  const auto key = std::make_pair(first, S);
+  auto it = m->b_graphs.find(key);
+  if (it != m->b_graphs.end()) {
+    *out = it->second;
+    return Q4GPU_OK;
+  }
+  if ((rc = q4gpu_batch_setup(p))) return rc;
+  cudaGraph_t g = nullptr;
+  Q4_CUDA(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+  rc = q4gpu_enqueue_batch_step(p, m->stream);
+  const cudaError_t ce = cudaStreamEndCapture(m->stream, &g);
+  if (rc != Q4GPU_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "batch graph capture: %s", cudaGetErrorString(ce));
+  cudaGraphExec_t e = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&e, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "batch graph instantiate: %s", cudaGetErrorString(ie));
+  m->b_graphs[key] = e;
+  *out = e;
+  return Q4GPU_OK;
+}
+
+int batch_range_ok(q4gpu_model* m, int first, int n_seq) {
+  if (!m || first < 0 || n_seq < 1 || n_seq > kBatchSeqMax || first + n_seq > m->cfg.max_seqs)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "batch needs 1..%d slots inside max_seqs", kBatchSeqMax);
+  for (int s = first; s < first + n_seq; ++s)
+    if (slot_busy(m, s)) return q4gpu_fail(Q4GPU_ERR_ARG, "slot %d still has work queued", s);
+  return set_device(m);
+}
+
 }  // namespace
 
 extern "C" {
@@ -932,6 +1086,8 @@ void q4gpu_model_destroy(q4gpu_model* m) {
   cudaSetDevice(m->cfg.device);
   if (m->stream) cudaStreamSynchronize(m->stream);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : m->b_graphs) cudaGraphExecDestroy(kv.second);
+  if (m->h_bio) cudaFreeHost(m->h_bio);
   for (auto e : m->done)
     if (e) cudaEventDestroy(e);
   for (void* p : m->allocs) cudaFree(p);
@@ -953,6 +1109,7 @@ int q4gpu_model_init_synthetic(q4gpu_model* m, uint64_t seed, float std_dev, flo
   Q4_CUDA(cudaMalloc(&tmp, max_elems * sizeof(float)));
   Q4_CUDA(cudaMalloc(&err, sizeof(int32_t)));
   Q4_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), m->stream));
+  m->b_stale = true;
   auto gen_quant = [&](uint64_t tid, const TensorRef& t) -> int {
     int r = q4gpu_synth_f32(seed, tid, 0, t.rows * t.cols, std_dev, 1, tmp, m->stream);
     if (r) return r;
@@ -1005,6 +1162,7 @@ static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, s
   int rc = set_device(m);
   if (rc) return rc;
   const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+  if (to_device) m->b_stale = true;
   auto cp = [&](void* dev, void* host, size_t n) -> int {
     Q4_CUDA(to_device ? cudaMemcpy(dev, host, n, kind) : cudaMemcpy(host, dev, n, kind));
     return Q4GPU_OK;
@@ -1190,30 +1348,107 @@ int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_
 
 int q4gpu_decode_batch(q4gpu_model* m, int32_t n_seq, const uint32_t* prompts, const uint32_t* prompt_lens,
                        uint32_t max_new_tokens, uint32_t* generated, int64_t* scores) {
-  if (!m || !prompts || !prompt_lens || !generated || n_seq <= 0) return QOT_ERR_NULL;
-  if (n_seq > m->cfg.max_seqs) return QOT_ERR_CAPACITY;
-  qot_run_config_t cfg{};
-  cfg.layer_start = 0;
-  cfg.layer_count = (uint32_t)m->cfg.n_layers;
-  cfg.runtime_context_enable = 1;
-  cfg.embedding_enable = 1;
-  size_t off = 0;
+  if (!m || !prompts || !prompt_lens || !generated) return QOT_ERR_NULL;
+  if (n_seq <= 0 || n_seq > m->cfg.max_seqs || max_new_tokens == 0u) return QOT_ERR_CAPACITY;
+  std::vector<size_t> off(n_seq + 1, 0);
   for (int s = 0; s < n_seq; ++s) {
-    uint32_t cnt = 0;
-    qot_result_t res;
-    const int rc = q4gpu_decode_token_ids(m, (uintptr_t)s, &cfg, prompts + off, prompt_lens[s], max_new_tokens,
-                                          generated + (size_t)s * max_new_tokens, max_new_tokens, 0, &cnt, &res);
-    if (rc != QOT_OK) return rc;
-    if (scores) {
-      // per-token scores of this sequence
-      const uint32_t first = prompt_lens[s];
-      if (cudaMemcpy(scores + (size_t)s * max_new_tokens, m->slots[s].scores + first, max_new_tokens * 8,
-                     cudaMemcpyDeviceToHost) != cudaSuccess)
-        return QOT_ERR_STATUS;
-    }
-    off += prompt_lens[s];
+    const uint32_t len = prompt_lens[s];
+    if (len == 0u) return QOT_ERR_CAPACITY;
+    if ((uint64_t)len + max_new_tokens - 1u > (uint64_t)m->cfg.max_context) return QOT_ERR_CONTEXT;
+    off[s + 1] = off[s] + len;
+    for (uint32_t i = 0; i < len; ++i)
+      if (prompts[off[s] + i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
   }
+  for (int first = 0; first < n_seq; first += kBatchSeqMax) {
+    const int S = std::min(kBatchSeqMax, n_seq - first);
+    if (batch_range_ok(m, first, S) != Q4GPU_OK) return QOT_ERR_BUSY;
+    cudaGraphExec_t g;
+    if (batch_graph(m, first, S, &g) != Q4GPU_OK) return QOT_ERR_STATUS;
+    // prompts at positions 0.., every sequence from position 0; the argmax of
+    // sequence s lands from position prompt_len[s] on
+    std::vector<int32_t> lm(S);
+    uint32_t longest = 0;
+    bool ok = true;
+    for (int i = 0; i < S && ok; ++i) {
+      const int s = first + i;
+      lm[i] = (int32_t)prompt_lens[s];
+      longest = std::max(longest, prompt_lens[s]);
+      ok = cudaMemcpyAsync(m->slots[s].tokens, prompts + off[s], (size_t)prompt_lens[s] * 4, cudaMemcpyHostToDevice,
+                           m->stream) == cudaSuccess;
+    }
+    ok = ok &&
+         cudaMemcpyAsync(m->b_lm_from + first, lm.data(), (size_t)S * 4, cudaMemcpyHostToDevice, m->stream) ==
+             cudaSuccess &&
+         q4gpu_batch_set_positions(m->b_slots + first, S, 0, m->b_lm_from + first, -1, m->stream) == Q4GPU_OK;
+    const uint32_t steps = longest + max_new_tokens - 1u;
+    for (uint32_t i = 0; ok && i < steps; ++i) ok = cudaGraphLaunch(g, m->stream) == cudaSuccess;
+    for (int i = 0; ok && i < S; ++i) {
+      const int s = first + i;
+      ok = cudaMemcpyAsync(generated + (size_t)s * max_new_tokens, m->slots[s].tokens + prompt_lens[s],
+                           (size_t)max_new_tokens * 4, cudaMemcpyDeviceToHost, m->stream) == cudaSuccess &&
+           (!scores || cudaMemcpyAsync(scores + (size_t)s * max_new_tokens, m->slots[s].scores + prompt_lens[s],
+                                       (size_t)max_new_tokens * 8, cudaMemcpyDeviceToHost, m->stream) == cudaSuccess);
+    }
+    ok = ok && cudaStreamSynchronize(m->stream) == cudaSuccess;
+    if (!ok) {
+      q4gpu_fail(Q4GPU_ERR_CUDA, "batched decode: %s", cudaGetErrorString(cudaGetLastError()));
+      return QOT_ERR_STATUS;
+    }
+  }
+  for (size_t i = 0; i < (size_t)n_seq * max_new_tokens; ++i)
+    if (generated[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
   return QOT_OK;
+}
+
+int q4gpu_batch_steps(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t n_steps) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (n_steps < 0) return q4gpu_fail(Q4GPU_ERR_ARG, "negative step count");
+  cudaGraphExec_t g;
+  if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
+  for (int i = 0; i < n_steps; ++i) Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  return Q4GPU_OK;
+}
+
+int q4gpu_batch_set_position(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t position, int32_t lm_from) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (position < 0 || position >= m->cfg.max_context || lm_from < -1)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad batch position %d / lm_from %d", position, lm_from);
+  if ((rc = batch_prepare(m))) return rc;
+  return q4gpu_batch_set_positions(m->b_slots + first_slot, n_seq, position, m->b_lm_from + first_slot, lm_from,
+                                   m->stream);
+}
+
+int q4gpu_batch_run_step(q4gpu_model* m, int32_t first_slot, int32_t n_seq, const uint32_t* token_ids,
+                         const uint32_t* positions, uint32_t* out_tokens, int64_t* out_scores) {
+  if (!m || !token_ids || !positions || !out_tokens) return q4gpu_fail(Q4GPU_ERR_ARG, "null argument");
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  for (int i = 0; i < n_seq; ++i)
+    if (token_ids[i] >= (uint32_t)m->cfg.vocab || positions[i] >= (uint32_t)m->cfg.max_context)
+      return q4gpu_fail(Q4GPU_ERR_ARG, "sequence %d: token %u / position %u out of range", i, token_ids[i],
+                        positions[i]);
+  cudaGraphExec_t g;
+  if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
+  int32_t* hin = m->h_bio;
+  int32_t* hout = m->h_bio + 2 * kBatchSeqMax;
+  for (int i = 0; i < n_seq; ++i) {
+    hin[2 * i] = (int32_t)token_ids[i];
+    hin[2 * i + 1] = (int32_t)positions[i];
+  }
+  const SlotState* slots = m->b_slots + first_slot;
+  Q4_CUDA(cudaMemcpyAsync(m->b_io, hin, (size_t)n_seq * 8, cudaMemcpyHostToDevice, m->stream));
+  if ((rc = q4gpu_batch_load(slots, n_seq, m->b_io, m->b_lm_from + first_slot, m->stream))) return rc;
+  Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  if ((rc = q4gpu_batch_gather(slots, n_seq, m->b_io, m->b_io + 2 * kBatchSeqMax, m->stream))) return rc;
+  Q4_CUDA(cudaMemcpyAsync(hout, m->b_io + 2 * kBatchSeqMax, (size_t)n_seq * 16, cudaMemcpyDeviceToHost, m->stream));
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  for (int i = 0; i < n_seq; ++i) {
+    out_tokens[i] = (uint32_t)hout[4 * i];
+    if (out_scores) memcpy(&out_scores[i], &hout[4 * i + 2], 8);
+  }
+  return Q4GPU_OK;
 }
 
 int q4gpu_decode_steps(q4gpu_model* m, uintptr_t base, int32_t n_steps) {

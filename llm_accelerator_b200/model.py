@@ -165,6 +165,25 @@ class Q4Model:
             raise QotError(rc, "q4gpu_decode_batch")
         return gen.astype(np.int64), scores
 
+    # -- batched decode (up to 64 slots per step) ------------------------------
+    def batch_steps(self, n_steps: int, n_seq: int, first_slot: int = 0) -> None:
+        """Enqueue n batched steps for slots [first_slot, first_slot + n_seq) (async)."""
+        _native.check(self.lib.q4gpu_batch_steps(self.handle, first_slot, n_seq, n_steps), "q4gpu_batch_steps")
+
+    def batch_set_position(self, position: int, n_seq: int, first_slot: int = 0, lm_from: int = -1) -> None:
+        _native.check(self.lib.q4gpu_batch_set_position(self.handle, first_slot, n_seq, position, lm_from),
+                      "q4gpu_batch_set_position")
+
+    def batch_run_step(self, tokens, positions, first_slot: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        """One batched step with host buffers: (next tokens, Q26 scores) per sequence."""
+        t = np.ascontiguousarray(tokens, dtype=np.uint32)
+        p = np.ascontiguousarray(positions, dtype=np.uint32)
+        out = np.zeros(t.size, dtype=np.uint32)
+        sc = np.zeros(t.size, dtype=np.int64)
+        _native.check(self.lib.q4gpu_batch_run_step(self.handle, first_slot, t.size, _ptr(t), _ptr(p), _ptr(out),
+                                                    _ptr(sc)), "q4gpu_batch_run_step")
+        return out.astype(np.int64), sc
+
     # -- device-resident decode loop ----------------------------------------
     def decode_steps(self, n_steps: int, slot: int = 0) -> None:
         """Enqueue n greedy steps continuing slot's decode on the device (async)."""
