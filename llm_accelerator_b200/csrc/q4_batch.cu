@@ -1,32 +1,28 @@
 // Batched greedy decode: up to 64 independent sequences advance one position
 // per step together, sharing every weight read.
 //
-// GEMMs run on the tensor cores with exact integer arithmetic.  Weights are
-// expanded once to int8 (row-major [rows, K]).  Each sequence's activation a
-// (signed 24-bit) is fed as the three unsigned byte limbs of a + 2^23, and
-// eight B rows of ones yield sum(w) per row and 64-group.  Per group,
-// mma.sync m16n8k32 (s8 x u8 -> s32) accumulates P0, P1, P2 and W1 exactly
-// (|P| < 2^17), and
+// GEMMs run on the tensor cores (tcgen05.mma, kind::i8) with exact integer
+// arithmetic.  Weights are expanded once to int8 (row-major [rows, K]).  Each
+// sequence's activation a (signed 24-bit) is fed as the three unsigned byte
+// limbs of a + 2^23, and eight B rows of ones yield sum(w) per row and
+// 64-group, so that per scale group
 //     sum(w * a) = P0 + 256 P1 + 65536 P2 - 2^23 W1
-// is formed in int64 and multiplied by the group's Q2.14 scale.  The B tile
-// columns are ordered [limb][sequence], so the three limbs of one (row,
-// sequence) land in the same thread's accumulator fragment.
+// with every Pj an exact int32 tensor-core sum (|Pj| < 2^17).
 //
-// B ("limb") matrices are stored transposed, Bt[n][k] u8 with n = limb * SP + m
+// B ("limb") matrices are stored as Bt[n][k] u8 with n = limb * SP + m
 // (SP = padded sequence count) and n = 3 SP .. 3 SP + 7 the ones rows.
 // Producers write them directly: a norm kernel for the norm-fed GEMMs, the
-// attention epilogue for o_proj, the SwiGLU epilogue for down.  Both GEMM
-// operands stream through a 4-stage cp.async pipeline per 64-column group.
+// attention epilogue for o_proj, the SwiGLU epilogue for down.
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 
 #include "q4_batch.h"
 #include "q4_gemv.cuh"
+#include "q4_umma.cuh"
 #include "q4gpu_internal.h"
 
 namespace q4 {
-
-constexpr int kBStride = 80;  // bytes per row of a 64-byte k-chunk in shared memory (bank-conflict free)
-constexpr int kNStage = 4;
 
 struct BatchCtx {
   const SlotState* slots;  // [S]
@@ -36,24 +32,8 @@ struct BatchCtx {
   uint8_t* bt2;            // [N, 2048]
   uint8_t* bt3;            // [N, 3072]
   const int32_t* lm_from;  // [S]
+  int* err;                // set when a pipeline wait runs out
 };
-
-__device__ __forceinline__ void mma_s8u8(int32_t (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
 
 // limbs of the unsigned offset value a + 2^23
 __device__ __forceinline__ void write_limbs(uint8_t* bt, int SP, int K, int m, int k, int32_t a) {
@@ -61,92 +41,6 @@ __device__ __forceinline__ void write_limbs(uint8_t* bt, int SP, int K, int m, i
   bt[(size_t)(0 * SP + m) * K + k] = (uint8_t)(u & 0xFF);
   bt[(size_t)(1 * SP + m) * K + k] = (uint8_t)((u >> 8) & 0xFF);
   bt[(size_t)(2 * SP + m) * K + k] = (uint8_t)((u >> 16) & 0xFF);
-}
-
-template <int J>
-struct WarpAcc {
-  int64_t v[2][2 * J];  // [row half][2j + c]
-};
-
-// Exact batched GEMV of one CTA: rows [row0, row0 + 16 RT) of A (int8
-// [rows, K], scales [rows, K/64]) against all SP sequences of bt.  Warps:
-// RT row tiles x SH sequence blocks of 8 J sequences (SH * 8 J == SP).
-// acc.v[h][2j+c]: row row0 + 16 rt + lane/4 + 8h, sequence 8 J sb + 8j + 2(lane%4) + c.
-template <int K, int J, int SH, int RT>
-__device__ __forceinline__ void bgemm_cta(const int8_t* __restrict__ A, const uint16_t* __restrict__ Sc, int row0,
-                                          const uint8_t* __restrict__ bt, uint8_t* smem, WarpAcc<J>& acc) {
-  constexpr int G = K / 64;
-  constexpr int SP = SH * 8 * J;
-  constexpr int N = 3 * SP + 8;
-  constexpr int ROWS = 16 * RT;
-  constexpr int A_BYTES = ROWS * kBStride, B_BYTES = N * kBStride;
-  constexpr int STAGE = A_BYTES + B_BYTES;
-  constexpr int NT = 32 * RT * SH;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-  const int rt = warp % RT, sb = warp / RT;
-  auto issue = [&](int g) {
-    if (g < G) {
-      uint8_t* st = smem + (g % kNStage) * STAGE;
-      for (int i = threadIdx.x; i < (ROWS + N) * 4; i += NT) {
-        const int r = i >> 2, part = i & 3;
-        if (r < ROWS)
-          cp_async16(st + r * kBStride + part * 16, A + (size_t)(row0 + r) * K + g * 64 + part * 16);
-        else
-          cp_async16(st + A_BYTES + (r - ROWS) * kBStride + part * 16,
-                     bt + (size_t)(r - ROWS) * K + g * 64 + part * 16);
-      }
-    }
-    cp_async_commit();
-  };
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int q = 0; q < 2 * J; ++q) acc.v[h][q] = 0;
-#pragma unroll
-  for (int s = 0; s < kNStage - 1; ++s) issue(s);
-  const int arow = (rt * 16 + gid) * kBStride + tig * 4;
-  for (int g = 0; g < G; ++g) {
-    cp_async_wait<kNStage - 2>();
-    __syncthreads();
-    issue(g + kNStage - 1);
-    const uint8_t* st = smem + (g % kNStage) * STAGE;
-    int32_t d[3 * J + 1][4];
-#pragma unroll
-    for (int t = 0; t < 3 * J + 1; ++t) d[t][0] = d[t][1] = d[t][2] = d[t][3] = 0;
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      uint32_t a[4];
-      a[0] = *reinterpret_cast<const uint32_t*>(st + arow + ks * 32);
-      a[1] = *reinterpret_cast<const uint32_t*>(st + arow + 8 * kBStride + ks * 32);
-      a[2] = *reinterpret_cast<const uint32_t*>(st + arow + ks * 32 + 16);
-      a[3] = *reinterpret_cast<const uint32_t*>(st + arow + 8 * kBStride + ks * 32 + 16);
-#pragma unroll
-      for (int t = 0; t < 3 * J + 1; ++t) {
-        const int n0 = t < 3 * J ? (t / J) * SP + sb * 8 * J + 8 * (t % J) : 3 * SP;
-        const uint8_t* bp = st + A_BYTES + (n0 + gid) * kBStride + ks * 32 + tig * 4;
-        mma_s8u8(d[t], a, *reinterpret_cast<const uint32_t*>(bp), *reinterpret_cast<const uint32_t*>(bp + 16));
-      }
-    }
-    const int r0 = row0 + rt * 16 + gid;
-    const int64_t s0 = __ldg(Sc + (size_t)r0 * G + g), s1 = __ldg(Sc + (size_t)(r0 + 8) * G + g);
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int r = 2 * h + c;
-          const int64_t gsum = ((int64_t)d[2 * J + j][r] << 16) + ((int64_t)d[J + j][r] << 8) + (int64_t)d[j][r] -
-                               ((int64_t)d[3 * J][r] << 23);
-          acc.v[h][2 * j + c] += gsum * (h ? s1 : s0);
-        }
-  }
-  cp_async_wait<0>();
-}
-
-template <int J, int SH, int RT>
-__host__ __device__ constexpr size_t bgemm_smem() {
-  return (size_t)kNStage * (16 * RT + 3 * SH * 8 * J + 8) * kBStride;
 }
 
 // ---------------------------------------------------------------------------
@@ -162,20 +56,21 @@ __global__ void expand_int4_kernel(const uint8_t* __restrict__ packed, int64_t n
 }
 
 // gate [3072, 1024] and up [3072, 1024] (packed, with scales) -> int8 [6144,
-// 1024] in 32-row blocks: out rows 64 b .. 64 b + 31 = gate rows 32 b .., out
-// rows 64 b + 32 .. 64 b + 63 = up rows 32 b ..
+// 1024] in 64-row blocks: out rows 128 b .. 128 b + 63 = gate rows 64 b ..,
+// out rows 128 b + 64 .. 128 b + 127 = up rows 64 b ..
 __global__ void expand_gu_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up,
                                  const uint16_t* __restrict__ sg, const uint16_t* __restrict__ su,
                                  int8_t* __restrict__ out, uint16_t* __restrict__ sout) {
   constexpr int64_t kBytes = (int64_t)2 * kInter * (kHidden / 2);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < kBytes; i += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / (kHidden / 2)), col = (int)(i % (kHidden / 2));
-    const int src = 32 * (r / 64) + (r & 31);
-    const uint8_t b = ((r & 32) ? up : gate)[(size_t)src * (kHidden / 2) + col];
+    const int src = 64 * (r / 128) + (r & 63);
+    const bool is_up = (r & 64) != 0;
+    const uint8_t b = (is_up ? up : gate)[(size_t)src * (kHidden / 2) + col];
     const int lo = b & 0xF, hi = b >> 4;
     out[2 * i] = (int8_t)(lo >= 8 ? lo - 16 : lo);
     out[2 * i + 1] = (int8_t)(hi >= 8 ? hi - 16 : hi);
-    if (col < kHidden / kGroup) sout[(size_t)r * (kHidden / kGroup) + col] = ((r & 32) ? su : sg)[(size_t)src * 16 + col];
+    if (col < kHidden / kGroup) sout[(size_t)r * (kHidden / kGroup) + col] = (is_up ? su : sg)[(size_t)src * 16 + col];
   }
 }
 
@@ -241,32 +136,6 @@ __global__ void batch_norm_limbs_kernel(BatchCtx c, int which, const int32_t* __
   const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
   for (int i = threadIdx.x; i < kHidden; i += blockDim.x)
     write_limbs(c.bt1, c.SP, kHidden, m, i, norm_apply(x[i], inv, gamma[i], kHiddenNorm));
-}
-
-template <int J>
-__device__ __forceinline__ int acc_seq(int sb, int q, int lane) {
-  return sb * 8 * J + 8 * (q >> 1) + 2 * (lane & 3) + (q & 1);
-}
-
-// QKV projection: raw Q12.12 rows into qkv_raw (64 rows per CTA).
-template <int J, int SH>
-__global__ void __launch_bounds__(128 * SH) batch_qkv_kernel(BatchCtx c, const int8_t* __restrict__ W,
-                                                             const uint16_t* __restrict__ Sc) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int RT = 4;
-  grid_dep_wait();
-  grid_dep_launch();
-  const int row0 = blockIdx.x * 16 * RT;
-  WarpAcc<J> acc;
-  bgemm_cta<kHidden, J, SH, RT>(W, Sc, row0, c.bt1, smem, acc);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp % RT, sb = warp / RT;
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int q = 0; q < 2 * J; ++q) {
-      const int m = acc_seq<J>(sb, q, lane);
-      if (m < c.S) c.qkv_raw[(size_t)m * 4096 + row0 + rt * 16 + (lane >> 2) + 8 * h] = sat24(acc.v[h][q] >> 14);
-    }
 }
 
 // Attention for one (KV head, sequence): q/k head RMSNorm + RoPE, KV append,
@@ -437,146 +306,293 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchCtx c, int layer, 
   }
 }
 
-// o_proj (mode 0: post = sat24(hidden + (o >> 2))) or down (mode 1: hidden =
-// sat24(post + (d >> 2))); 64 rows per CTA x all sequences.
-template <int K, int J, int SH>
-__global__ void __launch_bounds__(128 * SH) batch_resid_kernel(BatchCtx c, const int8_t* __restrict__ W,
-                                                               const uint16_t* __restrict__ Sc, int mode) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int RT = 4;
-  grid_dep_wait();
-  grid_dep_launch();
-  const int row0 = blockIdx.x * 16 * RT;
-  WarpAcc<J> acc;
-  bgemm_cta<K, J, SH, RT>(W, Sc, row0, mode == 0 ? c.bt2 : c.bt3, smem, acc);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp % RT, sb = warp / RT;
-#pragma unroll
-  for (int h = 0; h < 2; ++h)
-#pragma unroll
-    for (int q = 0; q < 2 * J; ++q) {
-      const int m = acc_seq<J>(sb, q, lane);
-      if (m >= c.S) continue;
-      const SlotState& st = c.slots[m];
-      if (*st.pos >= st.max_ctx) continue;
-      const int r = row0 + rt * 16 + (lane >> 2) + 8 * h;
-      const int32_t o = sat24(acc.v[h][q] >> 14);
-      if (mode == 0)
-        st.post[r] = sat24((int64_t)st.hidden[r] + (o >> 2));
-      else
-        st.hidden[r] = sat24((int64_t)st.post[r] + (o >> 2));
+// ---------------------------------------------------------------------------
+// Exact batched GEMM on the 5th-generation tensor cores.
+//
+// CTA tile: 128 weight rows x NB limb columns (NB = 3 SP + 8 rounded up to
+// 16), K streamed in 128-byte tiles (two 64-column scale groups) through a
+// 3-stage TMA ring.  Warp 0 issues the TMA loads, warp 1 owns TMEM and issues
+// tcgen05.mma (kind::i8, s8 x u8 -> s32), warps 2-17 are the epilogue.  Each
+// scale group accumulates into its own TMEM buffer (two, alternating), so the
+// MMAs of one group overlap the epilogue of the previous: the epilogue reads
+// the limb sums P0, P1, P2 and the weight sum W1 of (row, sequence) with
+// tcgen05.ld and folds them into an int64 accumulator exactly,
+//     sum(w a) s = (P0 + 256 P1) s + (2 P2 - 256 W1) (s << 15),
+// two 32 x 32 -> 64-bit multiply-adds per (row, sequence, group).
+// K may be split over the CTAs of a cluster (gridDim.y = splits <= 8); the
+// partial sums then meet in the owning CTA's shared memory over DSMEM.
+// ---------------------------------------------------------------------------
+enum GemmKind { kGemmQkv = 0, kGemmO = 1, kGemmGu = 2, kGemmDown = 3, kGemmLm = 4 };
+
+constexpr int kUThreads = 576;  // 18 warps
+constexpr int kUStages = 3;
+
+template <int SP>
+struct UCfg {
+  static constexpr int NB = (3 * SP + kBatchOnes + 15) / 16 * 16;
+  static constexpr int Q = SP / 4;  // sequences per epilogue thread
+  static constexpr int A_BYTES = 128 * 128;
+  static constexpr int B_BYTES = NB * 128;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int TCOLS = 2 * NB <= 32 ? 32 : 2 * NB <= 64 ? 64 : 2 * NB <= 128 ? 128 : 2 * NB <= 256 ? 256 : 512;
+  static constexpr int BUF = TCOLS / 2;  // TMEM columns of one accumulator buffer
+  static constexpr int RED_BYTES = 128 * SP * 8;
+  static constexpr size_t SMEM = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 256;
+  static constexpr uint32_t IDESC = umma::i8_idesc(128, NB);
+};
+
+struct UGemm {
+  BatchCtx c;
+  const uint16_t* scales;  // [rows, K / 64]
+  int rows;                // rows of A (the LM head's may end inside the last tile)
+  int K;
+  int kt_per_split;        // 128-wide K tiles each CTA of a cluster covers
+  const int32_t* sig_lut;
+  ArgBestD* partial;       // LM head: [tiles, 64]
+};
+
+template <int SP, int KIND>
+__global__ void __launch_bounds__(kUThreads, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, UGemm g) {
+  using C = UCfg<SP>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = umma::smem_addr(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  int64_t* red = reinterpret_cast<int64_t*>(sm + kUStages * C::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kUStages * C::STAGE + C::RED_BYTES);
+  uint64_t* empty = full + kUStages;
+  uint64_t* tfull = empty + kUStages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  const int nkt = g.kt_per_split, kt0 = split * nkt;
+  const int row0 = tile * 128;
+  const int G = g.K / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kUStages; ++s) {
+      umma::bar_init(full + s, 1);
+      umma::bar_init(empty + s, 1);
     }
-}
-
-// gate/up + SwiGLU: CTA = 32 gate rows and the same 32 up rows (row tiles
-// 0-1 gate, 2-3 up) x all sequences; writes mlp and its limbs (down's B).
-template <int J, int SH>
-__global__ void __launch_bounds__(128 * SH) batch_gateup_kernel(BatchCtx c, const int8_t* __restrict__ Wgu,
-                                                                const uint16_t* __restrict__ Sgu,
-                                                                const int32_t* __restrict__ sig_lut) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int RT = 4;
-  constexpr int SP = SH * 8 * J;
-  int32_t* gsm = reinterpret_cast<int32_t*>(smem + bgemm_smem<J, SH, RT>());  // [32][SP]
-  grid_dep_wait();
-  grid_dep_launch();
-  // Wgu interleaves 32-row blocks: block b = gate rows [32b, 32b+32), then up rows
-  const int row0 = blockIdx.x * 64;
-  WarpAcc<J> acc;
-  bgemm_cta<kHidden, J, SH, RT>(Wgu, Sgu, row0, c.bt1, smem, acc);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp % RT, sb = warp / RT;
-  const bool up = rt >= 2;
-  if (!up) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int q = 0; q < 2 * J; ++q) {
-        const int r = rt * 16 + (lane >> 2) + 8 * h;
-        gsm[r * SP + acc_seq<J>(sb, q, lane)] = sat24(acc.v[h][q] >> 14);
-      }
+    for (int h = 0; h < 2; ++h) {
+      umma::bar_init(tfull + h, 1);
+      umma::bar_init(tempty + h, 16);
+    }
+    *abort_flag = 0;
+    umma::bar_init_fence();
+    umma::prefetch_map(&amap);
+    umma::prefetch_map(&bmap);
   }
+  if (warp == 1) umma::tmem_alloc(tmem_slot, C::TCOLS);
+  umma::fence_before_sync();
   __syncthreads();
-  if (up) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-#pragma unroll
-      for (int q = 0; q < 2 * J; ++q) {
-        const int m = acc_seq<J>(sb, q, lane);
-        if (m >= c.S) continue;
-        const SlotState& st = c.slots[m];
-        if (*st.pos >= st.max_ctx) continue;
-        const int r = (rt - 2) * 16 + (lane >> 2) + 8 * h;
-        const int32_t g = gsm[r * SP + m], u = sat24(acc.v[h][q] >> 14);
-        const int32_t gc = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
-        int ix = (gc + 32768 + 32) >> 6;
-        ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
-        const int32_t silu = sat24(((int64_t)g * sig_lut[ix]) >> 16);
-        const int32_t hv = sat24(((int64_t)silu * u) >> 12);
-        const int i = blockIdx.x * 32 + r;
-        st.mlp[i] = hv;
-        write_limbs(c.bt3, SP, kInter, m, i, hv);
-      }
-  }
-}
+  umma::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicExch(g.c.err, 3);
+  };
 
-// LM head: 256 rows per CTA x all sequences -> per-CTA best (score, row) per sequence.
-template <int J, int SH>
-__global__ void __launch_bounds__(128 * SH) batch_lmhead_kernel(BatchCtx c, const int8_t* __restrict__ W,
-                                                                const uint16_t* __restrict__ Sc, int rows,
-                                                                ArgBestD* __restrict__ partial) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  constexpr int RT = 4;
-  constexpr int SP = SH * 8 * J;
-  ArgBestD* best = reinterpret_cast<ArgBestD*>(smem + bgemm_smem<J, SH, RT>());  // [RT][SP]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, rt = warp % RT, sb = warp / RT;
-  grid_dep_wait();
-  grid_dep_launch();
-  int64_t bs[2 * J];
-  int32_t bi[2 * J];
+  if (warp == 0) {
+    if (lane == 0) {
+      // the weights do not depend on the previous kernel: their first tiles
+      // stream in while it finishes
+      const int pre = nkt < kUStages ? nkt : kUStages;
+      for (int kt = 0; kt < pre; ++kt) {
+        umma::bar_expect_tx(full + kt, C::STAGE);
+        umma::tma_load(sm + kt * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + kt);
+      }
+      grid_dep_wait();
+      for (int kt = 0; kt < pre; ++kt)
+        umma::tma_load(sm + kt * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, 0, full + kt);
+      for (int kt = pre; kt < nkt && !*abort_flag; ++kt) {
+        const int s = kt % kUStages;
+        if (!umma::bar_wait(empty + s, ((kt / kUStages) & 1) ^ 1)) {
+          fail();
+          break;
+        }
+        umma::bar_expect_tx(full + s, C::STAGE);
+        umma::tma_load(sm + s * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + s);
+        umma::tma_load(sm + s * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, 0, full + s);
+      }
+    } else {
+      grid_dep_wait();
+    }
+  } else if (warp == 1) {
+    grid_dep_wait();
+    if (lane == 0) {
+      for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
+        const int s = kt % kUStages;
+        if (!umma::bar_wait(full + s, (kt / kUStages) & 1)) {
+          fail();
+          break;
+        }
+        umma::fence_after_sync();
+        const uint32_t a0 = umma::smem_addr(sm + s * C::STAGE), b0 = a0 + C::A_BYTES;
+        for (int h = 0; h < 2; ++h) {
+          if (!umma::bar_wait(tempty + h, (kt & 1) ^ 1)) {
+            fail();
+            break;
+          }
+          umma::fence_after_sync();
+          const uint32_t d = tmem + (uint32_t)(h * C::BUF);
 #pragma unroll
-  for (int q = 0; q < 2 * J; ++q) {
-    bs[q] = INT64_MIN;
-    bi[q] = INT32_MAX;
-  }
-  for (int sub = 0; sub < 4; ++sub) {  // 4 x 64 rows
-    const int row0 = blockIdx.x * 256 + sub * 64;
-    if (row0 >= rows) break;  // uniform per CTA
-    // the last, partial tile reads a clamped (valid) window and drops the extra rows
-    const int row_eff = row0 + 64 <= rows ? row0 : rows - 64;
-    WarpAcc<J> acc;
-    bgemm_cta<kHidden, J, SH, RT>(W, Sc, row_eff, c.bt1, smem, acc);
+          for (int j = 0; j < 2; ++j) {
+            const uint32_t off = (uint32_t)(64 * h + 32 * j);
+            umma::mma_i8(d, umma::sw128_desc(a0 + off), umma::sw128_desc(b0 + off), C::IDESC, (uint32_t)j);
+          }
+          umma::mma_commit(tfull + h);
+        }
+        umma::mma_commit(empty + s);
+      }
+    }
+  } else {
+    grid_dep_wait();
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (its sub-partition);
+    // the four warps of one sub-partition take a quarter of the sequences each
+    const int sp = warp & 3, q = (warp - 2) >> 2;
+    const int r = 32 * sp + lane;
+    const int grow = row0 + r < g.rows ? row0 + r : g.rows - 1;
+    const uint16_t* srow = g.scales + (size_t)grow * G + 2 * kt0;
+    int64_t acc[C::Q];
 #pragma unroll
-    for (int q = 0; q < 2 * J; ++q)
-#pragma unroll
+    for (int j = 0; j < C::Q; ++j) acc[j] = 0;
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * sp) << 16);
+    for (int kt = 0; kt < nkt; ++kt) {
+      const uint32_t s2 = *reinterpret_cast<const uint32_t*>(srow + 2 * kt);
       for (int h = 0; h < 2; ++h) {
-        const int r = row_eff + rt * 16 + (lane >> 2) + 8 * h;
-        if (r >= row0 && (acc.v[h][q] > bs[q] || (acc.v[h][q] == bs[q] && r < bi[q]))) {
-          bs[q] = acc.v[h][q];
-          bi[q] = r;
+        if (!umma::bar_wait(tfull + h, kt & 1)) {
+          fail();
+          kt = nkt;
+          break;
+        }
+        umma::fence_after_sync();
+        int32_t d0[C::Q], d1[C::Q], d2[C::Q], w1[1];
+        const uint32_t ta = lane_base + (uint32_t)(h * C::BUF + q * C::Q);
+        umma::tmem_ld_any<C::Q>(ta, d0);
+        umma::tmem_ld_any<C::Q>(ta + SP, d1);
+        umma::tmem_ld_any<C::Q>(ta + 2 * SP, d2);
+        umma::tmem_ld<1>(lane_base + (uint32_t)(h * C::BUF + 3 * SP), w1);
+        umma::tmem_ld_wait();
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) umma::bar_arrive(tempty + h);
+        const int32_t s = (int32_t)(h ? (s2 >> 16) : (s2 & 0xFFFFu));
+        const int32_t s15 = s << 15, w256 = w1[0] * 256;
+#pragma unroll
+        for (int j = 0; j < C::Q; ++j) {
+          const int32_t lo = d0[j] + d1[j] * 256;
+          const int32_t t2 = 2 * d2[j] - w256;
+          acc[j] += (int64_t)t2 * s15 + (int64_t)lo * s;
         }
       }
-    __syncthreads();
+    }
+    // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
+    // so each owner holds matching rows of both 64-row halves (gate and up)
+    const int rows_per = 64 / splits;
+    const int owner = (r & 63) / rows_per;
+    const int local = (r >> 6) * rows_per + (r & 63) % rows_per;
+    const int nl = 128 / splits;
+    int64_t* dst = red + ((size_t)split * nl + local) * SP + q * C::Q;
+    if (splits == 1) {
+#pragma unroll
+      for (int j = 0; j < C::Q; ++j) dst[j] = acc[j];
+    } else {
+      const uint32_t ca = umma::cluster_map(umma::smem_addr(dst), (uint32_t)owner);
+#pragma unroll
+      for (int j = 0; j < C::Q; ++j) umma::cluster_st64(ca + 8 * j, acc[j]);
+    }
   }
-#pragma unroll
-  for (int q = 0; q < 2 * J; ++q) {
-#pragma unroll
-    for (int msk = 4; msk < 32; msk <<= 1) {  // across lanes with the same lane & 3
-      const int64_t os = shfl_xor_i64(bs[q], msk);
-      const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi[q], msk);
-      if (os > bs[q] || (os == bs[q] && oi < bi[q])) {
-        bs[q] = os;
-        bi[q] = oi;
+  grid_dep_launch();
+  __syncwarp();
+  if (splits > 1)
+    umma::cluster_sync();
+  else
+    __syncthreads();
+
+  // final epilogue over the rows this CTA owns
+  const int rows_per = 64 / splits, nl = 128 / splits;
+  const int et = threadIdx.x;
+  auto row_of = [&](int local) { return (local / rows_per) * 64 + split * rows_per + local % rows_per; };
+  auto sum_of = [&](int local, int m) {
+    int64_t v = 0;
+    for (int src = 0; src < splits; ++src) v += red[((size_t)src * nl + local) * SP + m];
+    return v;
+  };
+  if (!*abort_flag) {
+    if constexpr (KIND == kGemmQkv) {
+      for (int i = et; i < nl * SP; i += kUThreads) {
+        const int local = i / SP, m = i % SP;
+        if (m < g.c.S) g.c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
+      }
+    } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
+      for (int i = et; i < nl * SP; i += kUThreads) {
+        const int local = i / SP, m = i % SP;
+        if (m >= g.c.S) continue;
+        const SlotState& st = g.c.slots[m];
+        if (*st.pos >= st.max_ctx) continue;
+        const int row = row0 + row_of(local);
+        const int32_t o = sat24(sum_of(local, m) >> 14);
+        if (KIND == kGemmO)
+          st.post[row] = sat24((int64_t)st.hidden[row] + (o >> 2));
+        else
+          st.hidden[row] = sat24((int64_t)st.post[row] + (o >> 2));
+      }
+    } else if constexpr (KIND == kGemmGu) {
+      // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
+      for (int i = et; i < rows_per * SP; i += kUThreads) {
+        const int j = i / SP, m = i % SP;
+        if (m >= g.c.S) continue;
+        const SlotState& st = g.c.slots[m];
+        if (*st.pos >= st.max_ctx) continue;
+        const int32_t gv = sat24(sum_of(j, m) >> 14), uv = sat24(sum_of(rows_per + j, m) >> 14);
+        const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
+        int ix = (gc + 32768 + 32) >> 6;
+        ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
+        const int32_t silu = sat24(((int64_t)gv * g.sig_lut[ix]) >> 16);
+        const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
+        const int idx = tile * 64 + split * rows_per + j;
+        st.mlp[idx] = hv;
+        write_limbs(g.c.bt3, SP, kInter, m, idx, hv);
+      }
+    } else {
+      // LM head (no split): best (score, row) of each sequence over the tile
+      ArgBestD* cand = reinterpret_cast<ArgBestD*>(sm);  // the TMA stages are free now
+      constexpr int kParts = kUThreads / SP;
+      for (int i = et; i < kParts * SP; i += kUThreads) {
+        const int m = i % SP, part = i / SP;
+        int64_t bs = INT64_MIN;
+        int32_t bi = INT32_MAX;
+        for (int lr = part; lr < 128; lr += kParts) {
+          const int row = row0 + lr;
+          if (row >= g.rows) break;
+          const int64_t v = red[(size_t)lr * SP + m];
+          if (v > bs) {  // rows ascend within a part: strict '>' keeps the lowest index
+            bs = v;
+            bi = row;
+          }
+        }
+        cand[part * SP + m] = ArgBestD{bs, bi, 0};
+      }
+      __syncthreads();
+      for (int m = et; m < SP; m += kUThreads) {
+        ArgBestD b = cand[m];
+        for (int part = 1; part < kParts; ++part) {
+          const ArgBestD o = cand[part * SP + m];
+          if (o.score > b.score || (o.score == b.score && o.idx < b.idx)) b = o;
+        }
+        g.partial[(size_t)tile * kBatchSeqMax + m] = b;
       }
     }
-    if (lane < 4) best[rt * SP + acc_seq<J>(sb, q, lane)] = ArgBestD{bs[q], bi[q], 0};
   }
+  umma::fence_before_sync();
   __syncthreads();
-  for (int m = threadIdx.x; m < c.S; m += blockDim.x) {
-    ArgBestD b = best[m];
-    for (int r = 1; r < RT; ++r) {
-      const ArgBestD o = best[r * SP + m];
-      if (o.score > b.score || (o.score == b.score && o.idx < b.idx)) b = o;
-    }
-    partial[(size_t)blockIdx.x * kBatchSeqMax + m] = b;
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, C::TCOLS);
   }
 }
 
@@ -640,18 +656,32 @@ using namespace q4;
 namespace {
 
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, Args... args) {
+cudaError_t launch_ex(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, int cluster_y,
+                      Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = g;
   cfg.blockDim = b;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_y > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = (unsigned)cluster_y;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, Args... args) {
+  return launch_ex(k, g, b, smem, s, 1, args...);
 }
 
 #define BQ(call)                                                                                        \
@@ -660,45 +690,53 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStr
     if (e_ != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
-template <int J, int SH>
+// K splits of each batched GEMM (a cluster of that many CTAs per row tile)
+constexpr int kSplitQkv = 4, kSplitO = 8, kSplitGu = 2, kSplitDown = 8;
+
+template <int SP, int KIND>
+cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const BatchCtx& c, const uint16_t* scales,
+                        int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s) {
+  UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial};
+  const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)splits);
+  return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
+}
+
+template <int SP>
 int enqueue_t(const BatchPlan& p, cudaStream_t s) {
-  const BatchCtx c{p.slots, p.S, p.SP, p.qkv_raw, p.bt1, p.bt2, p.bt3, p.lm_from};
-  constexpr size_t sm = bgemm_smem<J, SH, 4>();
-  constexpr int SP = SH * 8 * J;
-  const dim3 blk(128 * SH);
+  const BatchCtx c{p.slots, p.S, p.SP, p.qkv_raw, p.bt1, p.bt2, p.bt3, p.lm_from, p.err};
   BQ(launch_pdl(batch_embed_kernel, dim3(p.S), dim3(256), 0, s, c, p.emb, p.semb));
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in));
-    BQ(launch_pdl(batch_qkv_kernel<J, SH>, dim3(4096 / 64), blk, sm, s, c, w.wqkv, w.sqkv));
+    BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
+                                  nullptr, s)));
     BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), (size_t)2 * p.max_ctx * 8, s, c, l, w.g_q, w.g_k,
                   p.cos_tab, p.sin_tab, p.exp_lut));
-    BQ(launch_pdl(batch_resid_kernel<2 * kHidden, J, SH>, dim3(kHidden / 64), blk, sm, s, c, w.wo, w.so, 0));
+    BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s)));
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post));
-    BQ(launch_pdl(batch_gateup_kernel<J, SH>, dim3(kInter / 32), blk, sm + (size_t)32 * SP * 4, s, c, w.wgu, w.sgu,
-                  p.sig_lut));
-    BQ(launch_pdl(batch_resid_kernel<kInter, J, SH>, dim3(kHidden / 64), blk, sm, s, c, w.wdown, w.sdown, 1));
+    BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s)));
+    BQ((launch_gemm<SP, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr, s)));
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final));
-  const int lm_ctas = (p.vocab + 255) / 256;
-  BQ(launch_pdl(batch_lmhead_kernel<J, SH>, dim3(lm_ctas), blk, sm + (size_t)4 * SP * sizeof(ArgBestD), s, c, p.emb8,
-                p.semb, p.vocab, p.lm_partial));
-  BQ(launch_pdl(batch_argmax_kernel, dim3(p.S), dim3(256), 0, s, c, (const ArgBestD*)p.lm_partial, lm_ctas));
+  BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s)));
+  BQ(launch_pdl(batch_argmax_kernel, dim3(p.S), dim3(256), 0, s, c, (const ArgBestD*)p.lm_partial,
+                (p.vocab + 127) / 128));
   return Q4GPU_OK;
 }
 
-template <int J, int SH>
+template <int SP, int KIND>
+int set_smem() {
+  BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)UCfg<SP>::SMEM));
+  return Q4GPU_OK;
+}
+
+template <int SP>
 int setup_t(const BatchPlan& p) {
-  constexpr size_t sm = bgemm_smem<J, SH, 4>();
-  constexpr int SP = SH * 8 * J;
-  BQ(cudaFuncSetAttribute(batch_qkv_kernel<J, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-  BQ(cudaFuncSetAttribute(batch_resid_kernel<2 * kHidden, J, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)sm));
-  BQ(cudaFuncSetAttribute(batch_resid_kernel<kInter, J, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-  BQ(cudaFuncSetAttribute(batch_gateup_kernel<J, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)(sm + (size_t)32 * SP * 4)));
-  BQ(cudaFuncSetAttribute(batch_lmhead_kernel<J, SH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)(sm + (size_t)4 * SP * sizeof(ArgBestD))));
+  int rc;
+  if ((rc = set_smem<SP, kGemmQkv>()) || (rc = set_smem<SP, kGemmO>()) || (rc = set_smem<SP, kGemmGu>()) ||
+      (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
+    return rc;
   BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           (int)((size_t)2 * p.max_ctx * 8)));
   return Q4GPU_OK;
@@ -708,28 +746,50 @@ int setup_t(const BatchPlan& p) {
 
 int q4gpu_batch_padded(int S) { return S <= 8 ? 8 : S <= 16 ? 16 : S <= 24 ? 24 : S <= 32 ? 32 : 64; }
 
-// SP <= 32: one warp block of J = SP / 8 sequence groups; SP == 64: two blocks of 4.
 int q4gpu_batch_setup(const BatchPlan& p) {
   switch (p.SP) {
-    case 8: return setup_t<1, 1>(p);
-    case 16: return setup_t<2, 1>(p);
-    case 24: return setup_t<3, 1>(p);
-    case 32: return setup_t<4, 1>(p);
-    case 64: return setup_t<4, 2>(p);
+    case 8: return setup_t<8>(p);
+    case 16: return setup_t<16>(p);
+    case 24: return setup_t<24>(p);
+    case 32: return setup_t<32>(p);
+    case 64: return setup_t<64>(p);
     default: return q4gpu_fail(Q4GPU_ERR_SHAPE, "padded batch %d", p.SP);
   }
 }
 
 int q4gpu_enqueue_batch_step(const BatchPlan& p, cudaStream_t s) {
   switch (p.SP) {
-    case 8: return enqueue_t<1, 1>(p, s);
-    case 16: return enqueue_t<2, 1>(p, s);
-    case 24: return enqueue_t<3, 1>(p, s);
-    case 32: return enqueue_t<4, 1>(p, s);
-    case 64: return enqueue_t<4, 2>(p, s);
+    case 8: return enqueue_t<8>(p, s);
+    case 16: return enqueue_t<16>(p, s);
+    case 24: return enqueue_t<24>(p, s);
+    case 32: return enqueue_t<32>(p, s);
+    case 64: return enqueue_t<64>(p, s);
     default: return q4gpu_fail(Q4GPU_ERR_SHAPE, "padded batch %d", p.SP);
   }
 }
+
+int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !encode)
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)inner_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)inner_bytes};
+  const cuuint32_t box[2] = {128, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q4GPU_OK;
+}
+
+int q4gpu_batch_limb_rows(int SP) { return 3 * SP + kBatchOnes; }
+int q4gpu_batch_box_rows(int SP) { return (3 * SP + kBatchOnes + 15) / 16 * 16; }
 
 int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s) {
   const int blocks = (int)std::min<int64_t>((n_bytes + 255) / 256, 148 * 32);

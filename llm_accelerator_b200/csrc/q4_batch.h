@@ -11,11 +11,16 @@ constexpr int kScoreScale = 189812531;  // round(128^-0.5 * 2^31)
 // int8 copies of one layer's Q4 matrices (row-major [rows, K], one byte per
 // weight), with the model's Q2.14 group scales.
 struct BatchLayerW {
+  // TMA maps of the int8 matrices (128-byte x 128-row boxes, 128-byte swizzle)
+  alignas(64) CUtensorMap mqkv;
+  CUtensorMap mo;
+  CUtensorMap mgu;
+  CUtensorMap mdown;
   const int8_t* wqkv;  // [4096, 1024]: q, k, v rows
   const uint16_t* sqkv;
   const int8_t* wo;  // [1024, 2048]
   const uint16_t* so;
-  const int8_t* wgu;  // [6144, 1024]: 32-row blocks, gate rows 32b.. then up rows 32b..
+  const int8_t* wgu;  // [6144, 1024]: 128-row blocks, gate rows 64b.. then up rows 64b..
   const uint16_t* sgu;  // [6144, 16], same row order
   const int8_t* wdown;  // [1024, 3072]
   const uint16_t* sdown;
@@ -26,6 +31,10 @@ struct BatchLayerW {
 };
 
 struct BatchPlan {
+  alignas(64) CUtensorMap mb1;  // TMA maps of bt1 / bt2 / bt3 ([3 SP + 8] rows)
+  CUtensorMap mb2;
+  CUtensorMap mb3;
+  CUtensorMap mlm;  // int8 embedding (LM head)
   const SlotState* slots;  // device array [S]: sequence m is slot m
   int S;                   // live sequences (1..64)
   int SP;                  // padded sequence count: 8, 16, 24, 32 or 64
@@ -46,12 +55,17 @@ struct BatchPlan {
   const int32_t* exp_lut;
   const int32_t* sig_lut;
   const int32_t* g_final;
-  ArgBestD* lm_partial;  // [ceil(vocab / 256), 64]
+  ArgBestD* lm_partial;  // [ceil(vocab / 128), 64]
+  int* err;              // device flag: a GEMM pipeline wait ran out
 };
 
 }  // namespace q4
 
 int q4gpu_batch_padded(int S);
+int q4gpu_batch_limb_rows(int SP);  // rows of a limb matrix: 3 SP + 8
+int q4gpu_batch_box_rows(int SP);   // the same rounded up to the MMA's N granule (16)
+// 2-D TMA map of a row-major u8 matrix [rows, inner_bytes], 128 x box_rows boxes, 128-byte swizzle
+int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows);
 int q4gpu_batch_setup(const q4::BatchPlan& p);
 // One decode position for all S sequences (embedding .. argmax), stream-ordered.
 int q4gpu_enqueue_batch_step(const q4::BatchPlan& p, cudaStream_t s);

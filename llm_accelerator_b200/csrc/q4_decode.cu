@@ -16,6 +16,7 @@
 #include <cstring>
 #include <cmath>
 #include <map>
+#include <memory>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -479,6 +480,8 @@ struct q4gpu_model {
   ArgBestD* b_lm_part = nullptr;
   int32_t* b_io = nullptr;   // device [64][2] inputs, then [64][4] outputs
   int32_t* h_bio = nullptr;  // pinned mirror of b_io
+  int* b_err = nullptr;      // set by a batched GEMM whose pipeline wait ran out
+  CUtensorMap b_mlm{};       // TMA map of b_emb8
   BatchLayerW b_layers[kMaxLayers]{};
   bool b_stale = true;  // int8 copies out of date with the Q4 weights
   int b_ones_sp = 0;    // SP whose ones rows the B matrices hold
@@ -809,7 +812,7 @@ constexpr size_t kB8Down = (size_t)kHidden * kInter;
 constexpr size_t kB8Layer = kB8Qkv + kB8O + kB8Gu + kB8Down;
 constexpr int kBtRows = 3 * kBatchSeqMax + kBatchOnes;
 
-int batch_lm_ctas(int vocab) { return (vocab + 255) / 256; }
+int batch_lm_ctas(int vocab) { return (vocab + 127) / 128; }
 
 // Allocate the batched-decode buffers once and refresh the int8 weight copies
 // when the Q4 weights changed since the last batched call.
@@ -830,6 +833,7 @@ int batch_prepare(q4gpu_model* m) {
     if ((rc = m->alloc(&m->b_lm_from, (size_t)m->cfg.max_seqs))) return rc;
     if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
     if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
+    if ((rc = m->alloc(&m->b_err, 4))) return rc;
     Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
     for (int l = 0; l < L; ++l) {
       int8_t* w = m->b_w8 + kB8Layer * l;
@@ -847,7 +851,13 @@ int batch_prepare(q4gpu_model* m) {
       b.g_post = q.g_post;
       b.g_q = q.g_q;
       b.g_k = q.g_k;
+      if ((rc = q4gpu_encode_u8_map(&b.mqkv, b.wqkv, kHidden, kQRows + 2 * kKvRows, 128)) ||
+          (rc = q4gpu_encode_u8_map(&b.mo, b.wo, 2 * kHidden, kHidden, 128)) ||
+          (rc = q4gpu_encode_u8_map(&b.mgu, b.wgu, kHidden, 2 * kInter, 128)) ||
+          (rc = q4gpu_encode_u8_map(&b.mdown, b.wdown, kInter, kHidden, 128)))
+        return rc;
     }
+    if ((rc = q4gpu_encode_u8_map(&m->b_mlm, m->b_emb8, kHidden, (uint64_t)m->cfg.vocab, 128))) return rc;
   }
   if (m->b_stale) {
     for (int l = 0; l < L; ++l) {
@@ -866,8 +876,8 @@ int batch_prepare(q4gpu_model* m) {
   return Q4GPU_OK;
 }
 
-BatchPlan batch_plan(q4gpu_model* m, int first, int S) {
-  BatchPlan p{};
+int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
+  p = BatchPlan{};
   p.slots = m->b_slots + first;
   p.S = S;
   p.SP = q4gpu_batch_padded(S);
@@ -889,7 +899,27 @@ BatchPlan batch_plan(q4gpu_model* m, int first, int S) {
   p.sig_lut = m->sig_lut;
   p.g_final = m->g_final;
   p.lm_partial = m->b_lm_part;
-  return p;
+  p.err = m->b_err;
+  p.mlm = m->b_mlm;
+  const uint64_t nrows = (uint64_t)q4gpu_batch_limb_rows(p.SP);
+  const uint32_t box = (uint32_t)q4gpu_batch_box_rows(p.SP);
+  int rc;
+  if ((rc = q4gpu_encode_u8_map(&p.mb1, p.bt1, kHidden, nrows, box)) ||
+      (rc = q4gpu_encode_u8_map(&p.mb2, p.bt2, 2 * kHidden, nrows, box)) ||
+      (rc = q4gpu_encode_u8_map(&p.mb3, p.bt3, kInter, nrows, box)))
+    return rc;
+  return Q4GPU_OK;
+}
+
+int batch_check_error(q4gpu_model* m) {
+  if (!m->b_err) return Q4GPU_OK;
+  int e = 0;
+  Q4_CUDA(cudaMemcpy(&e, m->b_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e) {
+    cudaMemset(m->b_err, 0, sizeof(int));
+    return q4gpu_fail(Q4GPU_ERR_CUDA, "batched GEMM: a pipeline wait ran out");
+  }
+  return Q4GPU_OK;
 }
 
 // Graph of one batched step over slots [first, first + S), with the B
@@ -897,7 +927,9 @@ BatchPlan batch_plan(q4gpu_model* m, int first, int S) {
 int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out) {
   int rc = batch_prepare(m);
   if (rc) return rc;
-  const BatchPlan p = batch_plan(m, first, S);
+  auto pp = std::make_unique<BatchPlan>();
+  BatchPlan& p = *pp;
+  if ((rc = batch_plan(m, first, S, p))) return rc;
   if (m->b_ones_sp != p.SP) {
     Q4_CUDA(cudaMemsetAsync(m->b_bt1 + (size_t)3 * p.SP * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
     Q4_CUDA(cudaMemsetAsync(m->b_bt2 + (size_t)3 * p.SP * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden, m->stream));
@@ -1394,6 +1426,7 @@ int q4gpu_decode_batch(q4gpu_model* m, int32_t n_seq, const uint32_t* prompts, c
       q4gpu_fail(Q4GPU_ERR_CUDA, "batched decode: %s", cudaGetErrorString(cudaGetLastError()));
       return QOT_ERR_STATUS;
     }
+    if (batch_check_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
   }
   for (size_t i = 0; i < (size_t)n_seq * max_new_tokens; ++i)
     if (generated[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
@@ -1444,6 +1477,7 @@ int q4gpu_batch_run_step(q4gpu_model* m, int32_t first_slot, int32_t n_seq, cons
   if ((rc = q4gpu_batch_gather(slots, n_seq, m->b_io, m->b_io + 2 * kBatchSeqMax, m->stream))) return rc;
   Q4_CUDA(cudaMemcpyAsync(hout, m->b_io + 2 * kBatchSeqMax, (size_t)n_seq * 16, cudaMemcpyDeviceToHost, m->stream));
   Q4_CUDA(cudaStreamSynchronize(m->stream));
+  if ((rc = batch_check_error(m))) return rc;
   for (int i = 0; i < n_seq; ++i) {
     out_tokens[i] = (uint32_t)hout[4 * i];
     if (out_scores) memcpy(&out_scores[i], &hout[4 * i + 2], 8);
@@ -1505,6 +1539,7 @@ int q4gpu_model_sync(q4gpu_model* m) {
   if (rc) return rc;
   Q4_CUDA(cudaStreamSynchronize(m->stream));
   for (size_t i = 0; i < m->busy.size(); ++i) m->busy[i] = 0;
+  if ((rc = batch_check_error(m))) return rc;
   return check_persistent_error(m);
 }
 
