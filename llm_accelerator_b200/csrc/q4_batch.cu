@@ -33,6 +33,11 @@ struct BatchCtx {
   uint8_t* bt3;            // [N, 3072]
   const int32_t* lm_from;  // [S]
   int* err;                // set when a pipeline wait runs out
+  // the range's slots are consecutive in the model's state arrays
+  const int32_t* pos0;     // position of sequence m at pos0[4 m]
+  int32_t* hidden0;        // [S, 1024]
+  int32_t* post0;          // [S, 1024]
+  int max_ctx;
 };
 
 // limbs of the unsigned offset value a + 2^23
@@ -109,57 +114,101 @@ __global__ void batch_set_pos_kernel(const SlotState* __restrict__ slots, int S,
 __global__ void batch_embed_kernel(BatchCtx c, const uint8_t* __restrict__ W, const uint16_t* __restrict__ S) {
   grid_dep_wait();
   grid_dep_launch();
-  const SlotState& st = c.slots[blockIdx.x];
-  const int pos = *st.pos;
-  if (pos >= st.max_ctx) return;
-  const int t = st.tokens[pos];
+  const int m = blockIdx.x;
+  const int pos = c.pos0[4 * m];
+  if (pos >= c.max_ctx) return;
+  const int t = c.slots[m].tokens[pos];
   const uint8_t* row = W + (size_t)t * (kHidden / 2);
   const uint16_t* sc = S + (size_t)t * (kHidden / kGroup);
+  int32_t* h = c.hidden0 + (size_t)m * kHidden;
   for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
     const uint8_t b = row[i >> 1];
     const int q = (int)((i & 1) ? (b >> 4) : (b & 0xF));
-    st.hidden[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
+    h[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
   }
 }
 
-// RMSNorm of one sequence's hidden (which 0) or post (which 1) vector -> limbs in bt1
-__global__ void batch_norm_limbs_kernel(BatchCtx c, int which, const int32_t* __restrict__ gamma) {
+// RMSNorm of one sequence's hidden (which 0) or post (which 1) vector -> limbs
+// in bt1.  256 threads x 4 consecutive elements.
+__global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int which,
+                                                               const int32_t* __restrict__ gamma) {
   __shared__ int64_t red[32];
   grid_dep_wait();
   grid_dep_launch();
-  const int m = blockIdx.x;
-  const SlotState& st = c.slots[m];
-  const int32_t* x = which == 0 ? st.hidden : st.post;
-  int64_t ss = 0;
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) ss += (int64_t)x[i] * x[i];
+  const int m = blockIdx.x, k = 4 * threadIdx.x;
+  const int4 x = *reinterpret_cast<const int4*>((which == 0 ? c.hidden0 : c.post0) + (size_t)m * kHidden + k);
+  const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
+  int64_t ss = (int64_t)x.x * x.x + (int64_t)x.y * x.y + (int64_t)x.z * x.z + (int64_t)x.w * x.w;
   ss = block_sum_i64(ss, red);
   const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x)
-    write_limbs(c.bt1, c.SP, kHidden, m, i, norm_apply(x[i], inv, gamma[i], kHiddenNorm));
+  const uint32_t u0 = (uint32_t)(norm_apply(x.x, inv, gm.x, kHiddenNorm) + (1 << 23));
+  const uint32_t u1 = (uint32_t)(norm_apply(x.y, inv, gm.y, kHiddenNorm) + (1 << 23));
+  const uint32_t u2 = (uint32_t)(norm_apply(x.z, inv, gm.z, kHiddenNorm) + (1 << 23));
+  const uint32_t u3 = (uint32_t)(norm_apply(x.w, inv, gm.w, kHiddenNorm) + (1 << 23));
+#pragma unroll
+  for (int limb = 0; limb < 3; ++limb) {
+    const int sh = 8 * limb;
+    const uint32_t word = ((u0 >> sh) & 0xFF) | (((u1 >> sh) & 0xFF) << 8) | (((u2 >> sh) & 0xFF) << 16) |
+                          (((u3 >> sh) & 0xFF) << 24);
+    *reinterpret_cast<uint32_t*>(c.bt1 + (size_t)(limb * c.SP + m) * kHidden + k) = word;
+  }
 }
 
 // Attention for one (KV head, sequence): q/k head RMSNorm + RoPE, KV append,
 // exact two-pass LUT softmax for the two query heads of the group; writes the
-// output and its limbs (the o_proj B matrix).  256 threads.
-__global__ void __launch_bounds__(256) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
-                                                         const int32_t* __restrict__ g_k,
-                                                         const int32_t* __restrict__ cos_tab,
-                                                         const int32_t* __restrict__ sin_tab,
-                                                         const int32_t* __restrict__ exp_lut) {
-  extern __shared__ int64_t sc[];  // [2][ctx] scaled scores, then LUT indices
-  __shared__ __align__(16) int32_t hv[2][kHeadDim];  // roped q of the two heads
+// output and its limbs (the o_proj B matrix).  256 threads.  K, then V, of the
+// earlier positions stream through a 3-slot ring of 32-position chunks (16 KB
+// bulk copies, contiguous inside a KV page); the current position's K/V row
+// is taken from shared memory.
+constexpr int kAttnChunk = 32;
+constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
+constexpr int kAttnRing = 3;
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   umma::smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(umma::smem_addr(bar))
+               : "memory");
+}
+
+__global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
+                                                            const int32_t* __restrict__ g_k,
+                                                            const int32_t* __restrict__ cos_tab,
+                                                            const int32_t* __restrict__ sin_tab,
+                                                            const int32_t* __restrict__ exp_lut) {
+  extern __shared__ __align__(128) uint8_t attn_smem[];
+  int32_t* ring = reinterpret_cast<int32_t*>(attn_smem);                            // [3][32][128]
+  int64_t* sc = reinterpret_cast<int64_t*>(attn_smem + kAttnRing * kAttnChunkBytes);  // [2][ctx]
+  __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v
   __shared__ uint64_t probtab[2][kExpLut];
   __shared__ int64_t red[32];
-  __shared__ int64_t part[8][2][kHeadDim];
+  __shared__ uint64_t bars[kAttnRing];
   const int kv = blockIdx.x, m = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   grid_dep_wait();
   grid_dep_launch();
-  const SlotState& st = c.slots[m];
-  const int pos = *st.pos;
-  if (pos >= st.max_ctx) return;
+  const int pos = c.pos0[m * 4];
+  if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
-  const int32_t* raw = c.qkv_raw + (size_t)m * 4096;
+  const KvView kvv = c.slots[m].kv;
+  // chunks 0 .. nk-1: K, nk .. 2 nk-1: V, positions [32 j, min(32 j + 32, pos))
+  const int nk = (ctx + kAttnChunk - 1) / kAttnChunk, total = 2 * nk;
+  auto issue = [&](int i) {
+    const int kind = i < nk ? 0 : 1, j = i < nk ? i : i - nk;
+    const int p0 = j * kAttnChunk;
+    const int n = (pos - p0) < kAttnChunk ? (pos - p0) : kAttnChunk;
+    uint64_t* b = bars + i % kAttnRing;
+    umma::bar_expect_tx(b, n > 0 ? (uint32_t)n * kHeadDim * 4 : 0u);
+    if (n > 0)
+      bulk_load(ring + (i % kAttnRing) * kAttnChunk * kHeadDim, kvv.at(layer, kind, kv, p0), (uint32_t)n * kHeadDim * 4,
+                b);
+  };
+  if (t == 0) {
+    for (int s = 0; s < kAttnRing; ++s) umma::bar_init(bars + s, 1);
+    umma::bar_init_fence();
+    for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
+  }
+  const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
   // warp 0: q head 2kv, warp 1: q head 2kv+1, warp 2: k (normed, roped);
   // warp 3: v.  A lane owns dims 4 lane .. 4 lane + 3; the RoPE partner
   // d +- 64 sits 16 lanes away.
@@ -183,18 +232,17 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchCtx c, int layer, 
       o[e] = sat24(((int64_t)n * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
     }
     const int4 o4 = make_int4(o[0], o[1], o[2], o[3]);
-    if (warp < 2)
-      *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
-    else
-      reinterpret_cast<int4*>(st.kv.at(layer, 0, kv, pos))[lane] = o4;
+    *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
+    if (warp == 2) reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = o4;
   } else if (warp == 3) {
-    reinterpret_cast<int4*>(st.kv.at(layer, 1, kv, pos))[lane] =
-        *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim + 4 * lane);
+    const int4 v4 = *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim + 4 * lane);
+    *reinterpret_cast<int4*>(&hv[3][4 * lane]) = v4;
+    reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
   }
-  // block barrier: makes this position's K/V (global) and q (shared) visible
   __syncthreads();
-  // scores: 8 lanes per position, 4 positions per warp, 32 per pass; lane
-  // `sub` holds dims 4 (sub + 8 j) .. +3, j = 0..3 (128-byte coalesced rows)
+  bool ok = true;
+  // scores: chunk of 32 positions, 4 per warp, 8 lanes per position; lane
+  // `sub` holds dims 4 (sub + 8 j) .. +3, j = 0..3
   {
     const int sub = lane & 7, quad = lane >> 3;
     int32_t q0[16], q1[16];
@@ -205,47 +253,36 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchCtx c, int layer, 
       q0[4 * j] = a.x; q0[4 * j + 1] = a.y; q0[4 * j + 2] = a.z; q0[4 * j + 3] = a.w;
       q1[4 * j] = b.x; q1[4 * j + 1] = b.y; q1[4 * j + 2] = b.z; q1[4 * j + 3] = b.w;
     }
-    // the trip count is uniform across the warp (the shuffles need all lanes)
-    for (int base = warp * 4; base < ctx; base += 64) {
-      int4 k4[2][4];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int p = base + quad + 32 * u;
-        if (p < ctx) {
-          const int4* kr = reinterpret_cast<const int4*>(st.kv.at(layer, 0, kv, p));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) k4[u][j] = kr[sub + 8 * j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 4; ++j) k4[u][j] = make_int4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int p = base + quad + 32 * u;
-        int64_t s0 = 0, s1 = 0;
+    for (int i = 0; i < nk; ++i) {
+      if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+      const int p = i * kAttnChunk + warp * 4 + quad;
+      const int32_t* krow = p == pos ? hv[2] : ring + ((i % kAttnRing) * kAttnChunk + warp * 4 + quad) * kHeadDim;
+      int64_t s0 = 0, s1 = 0;
+      if (p < ctx) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const int32_t kk[4] = {k4[u][j].x, k4[u][j].y, k4[u][j].z, k4[u][j].w};
+          const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * (sub + 8 * j));
+          const int32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             s0 += (int64_t)q0[4 * j + e] * kk[e];
             s1 += (int64_t)q1[4 * j + e] * kk[e];
           }
         }
-#pragma unroll
-        for (int msk = 1; msk < 8; msk <<= 1) {
-          s0 += shfl_xor_i64(s0, msk);
-          s1 += shfl_xor_i64(s1, msk);
-        }
-        if (sub == 0 && p < ctx) {
-          sc[p] = scale_score(s0, kScoreScale);
-          sc[ctx + p] = scale_score(s1, kScoreScale);
-        }
       }
+#pragma unroll
+      for (int msk = 1; msk < 8; msk <<= 1) {
+        s0 += shfl_xor_i64(s0, msk);
+        s1 += shfl_xor_i64(s1, msk);
+      }
+      if (sub == 0 && p < ctx) {
+        sc[p] = scale_score(s0, kScoreScale);
+        sc[ctx + p] = scale_score(s1, kScoreScale);
+      }
+      __syncthreads();  // slot i % 3 is free again
+      if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
     }
   }
-  __syncthreads();
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
     int64_t* s = sc + h * ctx;
@@ -262,46 +299,47 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(BatchCtx c, int layer, 
     for (int i = t; i < kExpLut; i += blockDim.x) probtab[h][i] = ((uint64_t)exp_lut[i] << 16) / (uint64_t)sum;
   }
   __syncthreads();
-  // values: thread (pg = warp, lane) accumulates dims 4 lane .. +3 of
-  // positions p = pg (mod 8), two heads
-  {
-    int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-    for (int p0 = warp; p0 < ctx; p0 += 32) {
-      int4 v4[4];
+  // values: thread (warp, lane) accumulates dims 4 lane .. +3 of the chunk's
+  // positions warp, warp + 8, warp + 16, warp + 24 for both heads
+  int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+  for (int i = nk; i < total; ++i) {
+    if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+    const int base = (i - nk) * kAttnChunk;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int p = p0 + 8 * u;
-        if (p < ctx) v4[u] = reinterpret_cast<const int4*>(st.kv.at(layer, 1, kv, p))[lane];
-      }
+    for (int u = 0; u < 4; ++u) {
+      const int p = base + warp + 8 * u;
+      if (p < ctx) {
+        const int32_t* vrow =
+            p == pos ? hv[3] : ring + ((i % kAttnRing) * kAttnChunk + warp + 8 * u) * kHeadDim;
+        const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
+        const int64_t pr0 = (int64_t)probtab[0][sc[p]], pr1 = (int64_t)probtab[1][sc[ctx + p]];
+        const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int p = p0 + 8 * u;
-        if (p < ctx) {
-          const int64_t pr0 = (int64_t)probtab[0][sc[p]], pr1 = (int64_t)probtab[1][sc[ctx + p]];
-          const int32_t vv[4] = {v4[u].x, v4[u].y, v4[u].z, v4[u].w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            a0[e] += pr0 * vv[e];
-            a1[e] += pr1 * vv[e];
-          }
+        for (int e = 0; e < 4; ++e) {
+          a0[e] += pr0 * vv[e];
+          a1[e] += pr1 * vv[e];
         }
       }
     }
+    __syncthreads();
+    if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+  }
+  if (!ok) atomicExch(c.err, 4);
+  // the ring is idle now: reuse it for the cross-warp sums [8][2][128]
+  int64_t* part = reinterpret_cast<int64_t*>(attn_smem);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      part[warp][0][4 * lane + e] = a0[e];
-      part[warp][1][4 * lane + e] = a1[e];
-    }
+  for (int e = 0; e < 4; ++e) {
+    part[(warp * 2 + 0) * kHeadDim + 4 * lane + e] = a0[e];
+    part[(warp * 2 + 1) * kHeadDim + 4 * lane + e] = a1[e];
   }
   __syncthreads();
   {
     const int h = t >> 7, d = t & (kHeadDim - 1);
     int64_t acc = 0;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) acc += part[w][h][d];
+    for (int w = 0; w < 8; ++w) acc += part[(w * 2 + h) * kHeadDim + d];
     const int32_t o = sat24(acc >> 16);
     const int k = (2 * kv + h) * kHeadDim + d;
-    st.attn[k] = o;
     write_limbs(c.bt2, c.SP, 2 * kHidden, m, k, o);
   }
 }
@@ -337,7 +375,7 @@ struct UCfg {
   static constexpr int TCOLS = 2 * NB <= 32 ? 32 : 2 * NB <= 64 ? 64 : 2 * NB <= 128 ? 128 : 2 * NB <= 256 ? 256 : 512;
   static constexpr int BUF = TCOLS / 2;  // TMEM columns of one accumulator buffer
   static constexpr int RED_BYTES = 128 * SP * 8;
-  static constexpr size_t SMEM = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 512;
   static constexpr uint32_t IDESC = umma::i8_idesc(128, NB);
 };
 
@@ -365,6 +403,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* live = reinterpret_cast<int*>(tmem_slot + 2);  // [64]: sequence m takes part in this step
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
@@ -423,7 +462,9 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
   } else if (warp == 1) {
     grid_dep_wait();
-    if (lane == 0) {
+    if (lane != 0) {
+      for (int m = lane - 1; m < SP; m += 31) live[m] = m < g.c.S && g.c.pos0[4 * m] < g.c.max_ctx;
+    } else {
       for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
         const int s = kt % kUStages;
         if (!umma::bar_wait(full + s, (kt / kUStages) & 1)) {
@@ -457,12 +498,18 @@ __global__ void __launch_bounds__(kUThreads, 1)
     const int r = 32 * sp + lane;
     const int grow = row0 + r < g.rows ? row0 + r : g.rows - 1;
     const uint16_t* srow = g.scales + (size_t)grow * G + 2 * kt0;
+    uint32_t s2all[8];  // this row's scale pairs for the CTA's K tiles (nkt <= 8)
+#pragma unroll
+    for (int kt = 0; kt < 8; ++kt) s2all[kt] = kt < nkt ? *reinterpret_cast<const uint32_t*>(srow + 2 * kt) : 0u;
     int64_t acc[C::Q];
 #pragma unroll
     for (int j = 0; j < C::Q; ++j) acc[j] = 0;
     const uint32_t lane_base = tmem + ((uint32_t)(32 * sp) << 16);
+#pragma unroll 1
     for (int kt = 0; kt < nkt; ++kt) {
-      const uint32_t s2 = *reinterpret_cast<const uint32_t*>(srow + 2 * kt);
+      uint32_t s2 = s2all[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) s2 = kt == i ? s2all[i] : s2;
       for (int h = 0; h < 2; ++h) {
         if (!umma::bar_wait(tfull + h, kt & 1)) {
           fail();
@@ -496,14 +543,15 @@ __global__ void __launch_bounds__(kUThreads, 1)
     const int owner = (r & 63) / rows_per;
     const int local = (r >> 6) * rows_per + (r & 63) % rows_per;
     const int nl = 128 / splits;
-    int64_t* dst = red + ((size_t)split * nl + local) * SP + q * C::Q;
+    // red[src][m][local]: a warp's 32 rows land contiguously
+    int64_t* dst = red + ((size_t)split * SP + q * C::Q) * nl + local;
     if (splits == 1) {
 #pragma unroll
-      for (int j = 0; j < C::Q; ++j) dst[j] = acc[j];
+      for (int j = 0; j < C::Q; ++j) dst[(size_t)j * nl] = acc[j];
     } else {
       const uint32_t ca = umma::cluster_map(umma::smem_addr(dst), (uint32_t)owner);
 #pragma unroll
-      for (int j = 0; j < C::Q; ++j) umma::cluster_st64(ca + 8 * j, acc[j]);
+      for (int j = 0; j < C::Q; ++j) umma::cluster_st64(ca + 8 * j * nl, acc[j]);
     }
   }
   grid_dep_launch();
@@ -519,57 +567,52 @@ __global__ void __launch_bounds__(kUThreads, 1)
   auto row_of = [&](int local) { return (local / rows_per) * 64 + split * rows_per + local % rows_per; };
   auto sum_of = [&](int local, int m) {
     int64_t v = 0;
-    for (int src = 0; src < splits; ++src) v += red[((size_t)src * nl + local) * SP + m];
+    for (int src = 0; src < splits; ++src) v += red[((size_t)src * SP + m) * nl + local];
     return v;
   };
   if (!*abort_flag) {
     if constexpr (KIND == kGemmQkv) {
       for (int i = et; i < nl * SP; i += kUThreads) {
-        const int local = i / SP, m = i % SP;
-        if (m < g.c.S) g.c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
+        const int local = i % nl, m = i / nl;
+        if (m < g.c.S)
+          g.c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
       }
     } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
       for (int i = et; i < nl * SP; i += kUThreads) {
-        const int local = i / SP, m = i % SP;
-        if (m >= g.c.S) continue;
-        const SlotState& st = g.c.slots[m];
-        if (*st.pos >= st.max_ctx) continue;
-        const int row = row0 + row_of(local);
+        const int local = i % nl, m = i / nl;
+        if (!live[m]) continue;
+        const size_t at = (size_t)m * kHidden + row0 + row_of(local);
         const int32_t o = sat24(sum_of(local, m) >> 14);
         if (KIND == kGemmO)
-          st.post[row] = sat24((int64_t)st.hidden[row] + (o >> 2));
+          g.c.post0[at] = sat24((int64_t)g.c.hidden0[at] + (o >> 2));
         else
-          st.hidden[row] = sat24((int64_t)st.post[row] + (o >> 2));
+          g.c.hidden0[at] = sat24((int64_t)g.c.post0[at] + (o >> 2));
       }
     } else if constexpr (KIND == kGemmGu) {
       // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
       for (int i = et; i < rows_per * SP; i += kUThreads) {
-        const int j = i / SP, m = i % SP;
-        if (m >= g.c.S) continue;
-        const SlotState& st = g.c.slots[m];
-        if (*st.pos >= st.max_ctx) continue;
+        const int j = i % rows_per, m = i / rows_per;
+        if (!live[m]) continue;
         const int32_t gv = sat24(sum_of(j, m) >> 14), uv = sat24(sum_of(rows_per + j, m) >> 14);
         const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
         int ix = (gc + 32768 + 32) >> 6;
         ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
         const int32_t silu = sat24(((int64_t)gv * g.sig_lut[ix]) >> 16);
         const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
-        const int idx = tile * 64 + split * rows_per + j;
-        st.mlp[idx] = hv;
-        write_limbs(g.c.bt3, SP, kInter, m, idx, hv);
+        write_limbs(g.c.bt3, SP, kInter, m, tile * 64 + split * rows_per + j, hv);
       }
     } else {
       // LM head (no split): best (score, row) of each sequence over the tile
       ArgBestD* cand = reinterpret_cast<ArgBestD*>(sm);  // the TMA stages are free now
       constexpr int kParts = kUThreads / SP;
       for (int i = et; i < kParts * SP; i += kUThreads) {
-        const int m = i % SP, part = i / SP;
+        const int part = i % kParts, m = i / kParts;
         int64_t bs = INT64_MIN;
         int32_t bi = INT32_MAX;
         for (int lr = part; lr < 128; lr += kParts) {
           const int row = row0 + lr;
           if (row >= g.rows) break;
-          const int64_t v = red[(size_t)lr * SP + m];
+          const int64_t v = red[(size_t)m * 128 + lr];
           if (v > bs) {  // rows ascend within a part: strict '>' keeps the lowest index
             bs = v;
             bi = row;
@@ -703,15 +746,17 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
 
 template <int SP>
 int enqueue_t(const BatchPlan& p, cudaStream_t s) {
-  const BatchCtx c{p.slots, p.S, p.SP, p.qkv_raw, p.bt1, p.bt2, p.bt3, p.lm_from, p.err};
+  const BatchCtx c{p.slots, p.S,   p.SP,      p.qkv_raw, p.bt1,  p.bt2,     p.bt3,
+                   p.lm_from, p.err, p.pos0, p.hidden0, p.post0, p.max_ctx};
+  const size_t attn_smem = (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8;
   BQ(launch_pdl(batch_embed_kernel, dim3(p.S), dim3(256), 0, s, c, p.emb, p.semb));
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in));
     BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
                                   nullptr, s)));
-    BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), (size_t)2 * p.max_ctx * 8, s, c, l, w.g_q, w.g_k,
-                  p.cos_tab, p.sin_tab, p.exp_lut));
+    BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), attn_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
+                  p.sin_tab, p.exp_lut));
     BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s)));
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post));
     BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s)));
@@ -738,7 +783,7 @@ int setup_t(const BatchPlan& p) {
       (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
     return rc;
   BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)((size_t)2 * p.max_ctx * 8)));
+                          (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
   return Q4GPU_OK;
 }
 

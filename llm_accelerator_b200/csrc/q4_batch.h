@@ -56,7 +56,11 @@ struct BatchPlan {
   const int32_t* sig_lut;
   const int32_t* g_final;
   ArgBestD* lm_partial;  // [ceil(vocab / 128), 64]
-  int* err;              // device flag: a GEMM pipeline wait ran out
+  int* err;              // device flag: a pipeline wait ran out
+  // slots [first, first + S) are consecutive in the model's state arrays
+  const int32_t* pos0;   // position of sequence m at pos0[4 m]
+  int32_t* hidden0;      // [S, 1024]
+  int32_t* post0;        // [S, 1024]
 };
 
 }  // namespace q4

@@ -900,6 +900,9 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.g_final = m->g_final;
   p.lm_partial = m->b_lm_part;
   p.err = m->b_err;
+  p.pos0 = m->slots[first].pos;
+  p.hidden0 = m->slots[first].hidden;
+  p.post0 = m->slots[first].post;
   p.mlm = m->b_mlm;
   const uint64_t nrows = (uint64_t)q4gpu_batch_limb_rows(p.SP);
   const uint32_t box = (uint32_t)q4gpu_batch_box_rows(p.SP);
