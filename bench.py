@@ -2,20 +2,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: the 28-layer, 151936-vocabulary Qwen3-0.6B with
-seeded synthetic Q4 weights (seed 0), batch 1, a 128-token prompt of uniform
-random ids, greedy decode.  One step = one generated token (embedding, 28
-layers, final norm, LM head + argmax) with the decode positions cycling
-through 128..255 (the generated half of config 3; every cycle repeats the
-same tokens).  Weights are 316 MB per step, larger than L2.
+Headline workload: the 28-layer, 151936-vocabulary
+Qwen3-0.6B with seeded synthetic Q4 weights (seed 0); 64 independent
+sequences per GPU, each with its own 256-token prompt of uniform random ids,
+greedy generation of 256 tokens, context up to 512.  The prompts are
+prefilled position by position through the same batched step (the
+reference's serial prefill).  One timed step = one batched decode step: 64
+tokens, one per sequence (embedding, 28 layers, final norm, LM head,
+argmax), at decode positions cycling through 256..510 (the generated half;
+a cycle replays the same tokens).  Per step the weights (420 MB of int8
+copies) and the KV cache of 64 sequences (~5.6 GB at the mean context 384)
+stream from HBM: far larger than L2, so no flush is needed.
 
-N > 1 (torchrun, one rank per GPU): every rank decodes its own independent
-sequence (prompt seed = rank); no collective on the data path; value is the
-total tokens/s over ranks with the max-over-ranks device time (weak scaling).
+Secondary: batch 1, prompt 128, decode positions
+128..255, on the persistent cooperative kernel.
+
+N > 1 (torchrun, one rank per GPU): every rank decodes its own 64 sequences
+(prompt seeds depend on the rank); no collective on the data path; value is
+the total tokens/s over ranks with the max-over-ranks device time (weak
+scaling).
 
 `--impl reference` times the reference's arithmetic on the host CPU (the C
 restatement of the reference's Python Q4 path, all host threads) on the
-same workload; under torchrun only rank 0 runs it.
+same workload, one sequence at a time as the reference runs; under torchrun
+only rank 0 runs it.
 """
 from __future__ import annotations
 
@@ -34,41 +44,47 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-METRIC = "decode tokens/sec (batch 1), Qwen3-0.6B Q4 greedy decode"
+METRIC = "decode tokens/sec (batch 64), Qwen3-0.6B Q4 greedy decode"
 UNIT = "tokens/s"
-PROMPT_LEN = 128
-CYCLE = 128  # decode positions 128..255
 VOCAB = 151936
 LAYERS = 28
-WORKLOAD = ("cfg3: Qwen3-0.6B 28-layer Q4 (int4 + Q2.14 group scales) greedy decode, batch 1, tied "
-            "151936-vocab LM head, prompt 128 uniform ids (seed = rank), decode positions 128..255 cycled")
+BATCH = 64
+PROMPT = 256
+GEN = 256
+MAX_CTX = 512
+CYCLE = GEN - 1  # decode steps of one generation: positions 256..510
+WORKLOAD = ("cfg4: Qwen3-0.6B 28-layer Q4 (int4 + Q2.14 group scales) greedy decode, 64 sequences per GPU, "
+            "prompt 256 uniform ids each, 256 generated tokens, context up to 512, decode positions 256..510 cycled")
+B1_PROMPT, B1_CYCLE = 128, 128
+HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 
-# bytes one launch of each kernel kind reads/writes (algorithmic)
-QKV_ROWS, O_ROWS, INTER = 4096, 1024, 3072
 
-
-def kernel_bytes(kind: str, ctx: int) -> int:
+# ---------------------------------------------------------------------------
+# algorithmic bytes of one launch of each batched kernel (S sequences, the
+# attention at context `ctx`): what the kernel must move at least
+# ---------------------------------------------------------------------------
+def batch_kernel_bytes(kind: str, S: int, ctx: int) -> int:
+    limbs = 3 * S  # limb rows of a B matrix (u8)
     if kind == "embed":
-        return 512 + 32 + 4096
-    if kind == "qkv_norm_rope_kv":
-        return QKV_ROWS * (512 + 32) + 4096 + 2 * 4096 + 2 * 128 * 4 * 2 + 8192
+        return S * (512 + 32 + 4 * HIDDEN)
+    if kind == "norm_limbs":
+        return S * (4 * HIDDEN + limbs // S * HIDDEN) + 4 * HIDDEN
+    if kind == "qkv_gemm":
+        return QKV_ROWS * HIDDEN + QKV_ROWS * 32 + limbs * HIDDEN + S * QKV_ROWS * 4
     if kind == "attention":
-        return 2 * 8 * 128 * 4 * ctx + 8192 + 8192
-    if kind == "o_proj_residual":
-        return O_ROWS * (1024 + 64) + 8192 + 4096 + 4096
-    if kind == "post_norm_gate_up_swiglu":
-        return 2 * INTER * (512 + 32) + 4096 + INTER * 4
-    if kind == "down_residual":
-        return O_ROWS * (1536 + 96) + INTER * 4 + 4096 + 4096
-    if kind == "final_norm_lm_head_argmax":
-        return VOCAB * (512 + 32) + 4096 + 16
+        kv_read = 8 * 2 * (ctx - 1) * 128 * 4
+        return S * (kv_read + 8 * 2 * 128 * 4 + QKV_ROWS * 4 + 3 * 2 * HIDDEN)
+    if kind == "o_proj_gemm":
+        return HIDDEN * 2 * HIDDEN + HIDDEN * 64 + limbs * 2 * HIDDEN + S * 3 * HIDDEN * 4
+    if kind == "gate_up_gemm":
+        return 2 * INTER * HIDDEN + 2 * INTER * 32 + limbs * HIDDEN + limbs * INTER
+    if kind == "down_gemm":
+        return HIDDEN * INTER + HIDDEN * 96 + limbs * INTER + S * 3 * HIDDEN * 4
+    if kind == "lm_head_gemm":
+        return VOCAB * HIDDEN + VOCAB * 32 + limbs * HIDDEN + (VOCAB + 127) // 128 * 64 * 16
+    if kind == "argmax":
+        return S * ((VOCAB + 127) // 128 * 16 + 16)
     return 0
-
-
-def step_bytes(ctx: int) -> int:
-    per_layer = sum(kernel_bytes(k, ctx) for k in ("qkv_norm_rope_kv", "attention", "o_proj_residual",
-                                                   "post_norm_gate_up_swiglu", "down_residual"))
-    return kernel_bytes("embed", ctx) + LAYERS * per_layer + kernel_bytes("final_norm_lm_head_argmax", ctx)
 
 
 def measured_peaks() -> dict:
@@ -145,28 +161,6 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
 
 
-def stage_timeline(m, n_steps: int) -> dict:
-    """Mean per-stage work and barrier latency (us) of persistent decode steps."""
-    st = m.trace_persistent(n_steps).astype(np.int64)
-    per_step = 5 * LAYERS + 1
-    names = ["qkv", "attention", "o_proj", "gate_up", "down"]
-    work = {k: [] for k in names + ["lm_head"]}
-    wait = {k: [] for k in names + ["lm_head"]}
-    for s in range(1, n_steps):
-        base = s * per_step
-        prev = st[base - 1, 1]
-        for i in range(per_step):
-            arr, rel = st[base + i]
-            k = "lm_head" if i == per_step - 1 else names[i % 5]
-            work[k].append(arr - prev)
-            wait[k].append(rel - arr)
-            prev = rel
-    out = {k: {"work": round(float(np.mean(work[k])) / 1e3, 3), "barrier": round(float(np.mean(wait[k])) / 1e3, 3)}
-           for k in work}
-    out["step"] = round(float(st[n_steps * per_step - 1, 1] - st[per_step - 1, 1]) / (n_steps - 1) / 1e3, 2)
-    return out
-
-
 def dist_setup():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -174,29 +168,31 @@ def dist_setup():
     return ws, rank, local
 
 
-def prompt_for(rank: int) -> list[int]:
-    return np.random.default_rng(rank).integers(0, VOCAB, PROMPT_LEN).tolist()
+def prompts_for(rank: int) -> list[list[int]]:
+    return [np.random.default_rng(1000 * rank + i).integers(0, VOCAB, PROMPT).tolist() for i in range(BATCH)]
 
 
 # ---------------------------------------------------------------------------
-# CPU arm: the C restatement of the reference path
+# CPU arm: the C restatement of the reference path, one sequence at a time
 # ---------------------------------------------------------------------------
 def cpu_decode(n_steps: int, warmup: int, threads: int = 0) -> dict:
+    """Sequence 0 of rank 0: serial prefill of its 256-token prompt, then
+    warm-up + n_steps greedy decode steps (one token each) from position 256."""
     from oracle import c_oracle as CO
     cores = CO.set_threads(threads)
-    m = CO.CModel(LAYERS, VOCAB, PROMPT_LEN + CYCLE, seed=0)
-    prompt = prompt_for(0)
+    m = CO.CModel(LAYERS, VOCAB, MAX_CTX, seed=0)
+    prompt = prompts_for(0)[0]
     tok = 0
     for p, t in enumerate(prompt):
-        tok, _ = m.run_token(t, p, want_logits=(p == PROMPT_LEN - 1))
+        tok, _ = m.run_token(t, p, want_logits=(p == PROMPT - 1))
     first = tok
     toks = []
-    pos = PROMPT_LEN
+    pos = PROMPT
 
     def step():
         nonlocal tok, pos
-        if pos >= PROMPT_LEN + CYCLE:
-            pos, tok = PROMPT_LEN, first
+        if pos >= PROMPT + CYCLE:
+            pos, tok = PROMPT, first
         tok, _ = m.run_token(tok, pos)
         toks.append(tok)
         pos += 1
@@ -220,11 +216,12 @@ def run_reference(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 * r["seconds"] / steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": 1, "prompt": PROMPT_LEN, "parallelism": "host CPU"},
+        "config": {"workload": WORKLOAD, "batch": BATCH, "prompt": PROMPT, "generate": GEN,
+                   "parallelism": "host CPU, one sequence at a time"},
         "cpu_baseline": {"value": round(r["value"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
-                         "sample": f"{steps} decode steps after {warm} warm-up steps and the 128-token prefill, "
-                                   "C restatement of the reference's Python Q4 path (oracle/q4_oracle.c), "
-                                   "OpenMP over all host threads"},
+                         "sample": f"sequence 0: {steps} decode steps (one token each) after {warm} warm-up steps "
+                                   "and the serial 256-token prefill, C restatement of the reference's Python Q4 "
+                                   "path (oracle/q4_oracle.c), OpenMP over all host threads"},
         "e2e": {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -233,6 +230,45 @@ def run_reference(args, ws, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def batch1_secondary(device: int, steps: int) -> dict:
+    """Config 3 on the persistent kernel: batch 1, prompt 128, positions 128..255."""
+    import torch
+
+    from llm_accelerator_b200.model import Q4Model
+
+    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=B1_PROMPT + B1_CYCLE, max_seqs=1, device=device)
+    m.init_synthetic(seed=0)
+    slot = 0
+    prompt = np.random.default_rng(7).integers(0, VOCAB, B1_PROMPT).tolist()
+    gen, _ = m.decode(prompt, 1, slot=slot)
+    first = gen[0]
+    stream = torch.cuda.ExternalStream(m.stream)
+    m.decode_steps(8, slot=slot)
+    m.set_position(B1_PROMPT, slot=slot)
+    m.sync()
+    steps = min(steps, B1_CYCLE)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    m.decode_steps(steps, slot=slot)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    n_e2e = 32
+    tok, pos = first, B1_PROMPT
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        tok = m.run_token(tok, pos, slot=slot).token_id
+        pos += 1
+    e2e_s = time.perf_counter() - t0
+    mode = m.mode
+    m.close()
+    return {"workload": "cfg3: batch 1, prompt 128 uniform ids, decode positions 128..255",
+            "value": round(steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
+            "steps": steps, "mode": "persistent cooperative kernel" if mode == 1 else "per-stage CUDA graphs",
+            "e2e": {"value": round(n_e2e / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 12, "api": "q4gpu_run_token (qot_session_runner_fn)"}}
+
+
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -250,32 +286,47 @@ def run_ours(args, ws, rank, local):
         if dist is not None:
             dist.barrier()
 
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     steps, warm = args.steps, args.warmup
-    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=PROMPT_LEN + CYCLE + 1, max_seqs=1, device=local)
+    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=MAX_CTX, max_seqs=BATCH, device=local)
     m.init_synthetic(seed=0)
-    prompt = prompt_for(rank)
-    gen, _ = m.decode(prompt, 1)  # serial prefill of the prompt; pos is now 128
-    first = gen[0]
+    prompts = prompts_for(rank)
     stream = torch.cuda.ExternalStream(m.stream)
 
-    def enqueue(n: int, state: dict):
-        """n decode steps, cycling positions 128..255."""
+    # serial prefill of the 64 prompts through the batched step; the argmax
+    # after position 255 is each sequence's first generated token
+    t0 = time.perf_counter()
+    gen0, _ = m.decode_batch(prompts, 1)
+    prefill_s = time.perf_counter() - t0
+    first = gen0[:, 0].copy()
+
+    def enqueue(n: int, state: dict) -> int:
+        """n batched decode steps cycling positions 256..510; returns launches of the resets."""
+        resets = 0
         while n > 0:
-            room = PROMPT_LEN + CYCLE - state["pos"]
+            room = PROMPT + CYCLE - state["pos"]
             if room == 0:
-                m.set_position(PROMPT_LEN)
-                state["pos"] = PROMPT_LEN
+                m.batch_set_position(PROMPT, BATCH)
+                state["pos"] = PROMPT
                 room = CYCLE
+                resets += 1
             k = min(n, room)
-            m.decode_steps(k)
+            m.batch_steps(k, BATCH)
             state["pos"] += k
             n -= k
+        return resets
 
-    state = {"pos": PROMPT_LEN}
+    state = {"pos": PROMPT}
     enqueue(warm, state)
+    m.batch_set_position(PROMPT, BATCH)
+    state["pos"] = PROMPT
     m.sync()
-    # parity spot check of the cycle: the device must reproduce the first cycle's tokens
-    toks = m.read_tokens(PROMPT_LEN, min(warm, CYCLE) + 1)[0].tolist()
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -283,103 +334,83 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    enqueue(steps, state)
+    resets = enqueue(steps, state)
     e1.record(stream)
     e1.synchronize()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
-    ms = e0.elapsed_time(e1)
-    ms_max = ms
-    if dist is not None:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_max = float(t.item())
-    value = ws * steps / (ms_max / 1000.0)
+    m.sync()
+    ms_max = max_over_ranks(e0.elapsed_time(e1))
+    value = ws * BATCH * steps / (ms_max / 1000.0)
+    n_check = min(steps, CYCLE, 16)
+    toks0 = m.read_tokens(PROMPT, n_check + 1, slot=0)[0].tolist()
 
-    # end to end through the runner seam (qot_session_runner_fn): per step the
-    # host passes (token, position) from pinned memory and reads (token, score)
-    e2e_steps = steps
-    tok, pos = first, PROMPT_LEN
+    # end to end through the public C ABI with host buffers: per step the host
+    # sends (token, position) of every sequence and reads back (token, score)
+    e2e_steps = min(steps, CYCLE)
+    tok = first.copy()
+    pos = np.full(BATCH, PROMPT, dtype=np.int64)
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
-        if pos >= PROMPT_LEN + CYCLE:
-            tok, pos = first, PROMPT_LEN
-        tok = m.run_token(tok, pos).token_id
+        tok, _ = m.batch_run_step(tok, pos)
         pos += 1
-    e2e_s = time.perf_counter() - t0
-    if dist is not None:
-        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = ws * e2e_steps / e2e_s
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e = ws * BATCH * e2e_steps / e2e_s
 
-    # timeline of the persistent kernel: per stage, work (previous release to
-    # the last CTA's arrival) and barrier latency (last arrival to release)
-    m.set_position(PROMPT_LEN)
+    # per-kernel device times at the middle of the cycle (kernels serialised by events)
+    mid = PROMPT + CYCLE // 2
+    m.batch_set_position(mid, BATCH)
     m.sync()
-    tl = stage_timeline(m, 4) if m.mode == 1 else None
-    # per-kernel device times of the per-stage kernels (mode 0, events between kernels)
-    m.set_position(PROMPT_LEN)
-    m.sync()
-    kt = m.time_kernels(reps=3)
-    peaks = measured_peaks()
-    lm = "final_norm_lm_head_argmax"
-    lm_gbs = kernel_bytes(lm, 0) / (kt[lm][0] * 1e-3) / 1e9
-    step_b = step_bytes(PROMPT_LEN + CYCLE // 2)
-    step_gb = step_b / 1e9
-    if m.mode == 1:
-        # one persistent launch per 128-step cycle: its bytes over its device time
-        dom = "decode_persistent_kernel"
-        dom_bytes = step_b * CYCLE
-        dom_ms = ms_max / steps * CYCLE
-        launches = -(-steps // CYCLE) * 2  # the persistent kernel + a position reset per cycle
-    else:
-        share = {k: v[0] * v[1] for k, v in kt.items()}
-        dom = max(share, key=share.get)
-        dom_bytes = kernel_bytes(dom, PROMPT_LEN + 2)
-        dom_ms = kt[dom][0]
-        launches = sum(v[1] for v in kt.values()) * steps
-    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    reps = 3
+    kt = m.batch_time_kernels(BATCH, reps=reps)
+    ctx_mean = mid + (reps + 1) / 2.0
     share = {k: v[0] * v[1] for k, v in kt.items()}
     tot = sum(share.values())
+    dom = max(share, key=share.get)
+    peaks = measured_peaks()
+
+    def gbs(kind: str) -> float:
+        return batch_kernel_bytes(kind, BATCH, int(round(ctx_mean))) / (kt[kind][0] * 1e-3) / 1e9
+
+    launches_per_step = sum(v[1] for v in kt.values())
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": ws, "steps": steps,
             "warmup": warm, "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch": 1, "prompt": PROMPT_LEN, "seq_len": PROMPT_LEN + CYCLE,
-                       "parallelism": f"independent sequences x{ws}" if ws > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (316 MB of Q4 weights per step)"},
-            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 12,
-                    "api": "q4gpu_run_token (qot_session_runner_fn signature), one host round trip per token"},
-            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1),
-                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "prompt": PROMPT, "generate": GEN,
+                       "max_context": MAX_CTX,
+                       "parallelism": f"independent sequences, {BATCH} per GPU x{ws}" if ws > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (420 MB int8 weights + ~5.6 GB KV cache per step)"},
+            "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": BATCH * 8,
+                    "d2h_bytes_per_step": BATCH * 16,
+                    "api": "q4gpu_batch_run_step: host (token, position) in, host (token, score) out, every step"},
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(gbs(dom), 1), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(gbs(dom) / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"], "traffic": profiled_traffic(dom),
-                         "bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5)},
-            "mode": "persistent cooperative kernel" if m.mode == 1 else "per-stage kernels in CUDA graphs",
-            "stage_timeline_us": tl,
-            "step_roofline": {"bytes_per_step": int(step_gb * 1e9),
-                              "achieved_gbs": round(step_gb / (ms_max / steps / 1000.0), 1),
-                              "frac": round(step_gb / (ms_max / steps / 1000.0) / peaks["hbm_gbs"], 4)},
-            "gemv": {"kernel": "lm head 151936x1024 Q4 GEMV + argmax", "gbs": round(lm_gbs, 1),
-                     "frac": round(lm_gbs / peaks["hbm_gbs"], 4)},
-            "stage_kernels_mode0": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
-                                        "share": round(share[k] / tot, 4)} for k, v in kt.items()},
-            "gpu_launches": launches,
+                         "bytes_per_launch": batch_kernel_bytes(dom, BATCH, int(round(ctx_mean))),
+                         "ms_per_launch": round(kt[dom][0], 5), "context": round(ctx_mean, 1)},
+            "kernels": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
+                            "share": round(share[k] / tot, 4), "gbs": round(gbs(k), 1)} for k, v in kt.items()},
+            "prefill_s": round(prefill_s, 3),
+            "gpu_launches": launches_per_step * steps + resets,
             "clocks": clocks,
         }
-        if ws == 1 and not args.no_cpu_baseline:
-            c = cpu_decode(args.cpu_steps, 2)
-            line["cpu_baseline"] = {
-                "value": round(c["value"], 3), "unit": UNIT, "cores": c["cores"], "kind": "port",
-                "sample": f"{args.cpu_steps} decode steps at positions 130.. after the same 128-token prefill, "
-                          "C restatement of the reference's Python Q4 path (oracle/q4_oracle.c), all host threads"}
-            n = min(len(c["tokens"]), len(toks))
-            line["parity"] = "tokens identical to CPU oracle" if c["tokens"][:n] == toks[:n] else \
-                f"MISMATCH gpu={toks[:n]} cpu={c['tokens'][:n]}"
+        if ws == 1:
+            line["batch1"] = batch1_secondary(local, 128)
+            if not args.no_cpu_baseline:
+                c = cpu_decode(args.cpu_steps, 2)
+                line["cpu_baseline"] = {
+                    "value": round(c["value"], 3), "unit": UNIT, "cores": c["cores"], "kind": "port",
+                    "sample": f"sequence 0: {args.cpu_steps} decode steps at positions 258.. after its serial "
+                              "256-token prefill, C restatement of the reference's Python Q4 path "
+                              "(oracle/q4_oracle.c), all host threads"}
+                n = min(len(c["tokens"]), len(toks0))
+                line["parity"] = "sequence 0 tokens identical to the CPU oracle" if c["tokens"][:n] == toks0[:n] \
+                    else f"MISMATCH gpu={toks0[:n]} cpu={c['tokens'][:n]}"
         print(json.dumps(line), flush=True)
     m.close()
     if dist is not None:
@@ -390,8 +421,8 @@ def run_ours(args, ws, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1024)
-    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--steps", type=int, default=255)
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -331,6 +331,25 @@ int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t
 int q4gpu_batch_set_position(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t position,
                              int32_t lm_from);
 
+/* Kernel kinds of a batched step (q4gpu_batch_time_kernels). */
+#define Q4GPU_BK_EMBED 0
+#define Q4GPU_BK_NORM 1
+#define Q4GPU_BK_QKV_GEMM 2
+#define Q4GPU_BK_ATTENTION 3
+#define Q4GPU_BK_O_GEMM 4
+#define Q4GPU_BK_GATE_UP_GEMM 5
+#define Q4GPU_BK_DOWN_GEMM 6
+#define Q4GPU_BK_LM_HEAD_GEMM 7
+#define Q4GPU_BK_ARGMAX 8
+#define Q4GPU_BK_COUNT 9
+
+/* Runs `reps` batched steps (advancing the positions) with an event after
+ * every kernel, so the kernels run back to back without overlap; returns the
+ * mean device ms per launch and the launches per step of each kind
+ * (arrays of Q4GPU_BK_COUNT). */
+int q4gpu_batch_time_kernels(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t reps,
+                             double *ms_per_launch, int32_t *launches_per_step);
+
 /* One batched step with host buffers: sequence i of the range takes
  * token_ids[i] at positions[i] and returns the argmax (and its Q26 score,
  * optional) of the next position.  Blocks until the results are on the host. */

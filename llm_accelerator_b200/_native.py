@@ -26,6 +26,9 @@ T_EMBED, T_FINAL_GAMMA, T_ROPE_COS, T_ROPE_SIN, T_EXP_LUT, T_SIGMOID_LUT = range
 # kernel kinds of one decode step (q4gpu_model_time_kernels)
 KERNEL_KINDS = ["embed", "qkv_norm_rope_kv", "attention", "o_proj_residual", "post_norm_gate_up_swiglu",
                 "down_residual", "final_norm_lm_head_argmax", "advance"]
+# kernels of a batched step (Q4GPU_BK_*)
+BATCH_KERNEL_KINDS = ["embed", "norm_limbs", "qkv_gemm", "attention", "o_proj_gemm", "gate_up_gemm", "down_gemm",
+                      "lm_head_gemm", "argmax"]
 
 
 class QotLayerQmapBases(C.Structure):
@@ -94,6 +97,7 @@ SIGNATURES = {
     "q4gpu_batch_steps": (C.c_int, [P, I32, I32, I32]),
     "q4gpu_batch_set_position": (C.c_int, [P, I32, I32, I32, I32]),
     "q4gpu_batch_run_step": (C.c_int, [P, I32, I32, P, P, P, P]),
+    "q4gpu_batch_time_kernels": (C.c_int, [P, I32, I32, I32, P, P]),
     "q4gpu_model_read_hidden": (C.c_int, [P, C.c_size_t, P]),
     "q4gpu_model_read_kv": (C.c_int, [P, C.c_size_t, I32, I32, I32, P]),
     "q4gpu_model_write_hidden": (C.c_int, [P, C.c_size_t, P]),

@@ -745,27 +745,52 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
 }
 
 template <int SP>
-int enqueue_t(const BatchPlan& p, cudaStream_t s) {
+int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
+  auto mark = [&](int kind) -> int {
+    if (!mk) return Q4GPU_OK;
+    cudaEvent_t e;
+    BQ(cudaEventCreate(&e));
+    mk->ev.push_back(e);
+    mk->kind.push_back(kind);
+    BQ(cudaEventRecord(e, s));
+    return Q4GPU_OK;
+  };
+  int rc;
+#define BMARK(k) \
+  if ((rc = mark(k))) return rc
   const BatchCtx c{p.slots, p.S,   p.SP,      p.qkv_raw, p.bt1,  p.bt2,     p.bt3,
                    p.lm_from, p.err, p.pos0, p.hidden0, p.post0, p.max_ctx};
   const size_t attn_smem = (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8;
+  BMARK(-1);
   BQ(launch_pdl(batch_embed_kernel, dim3(p.S), dim3(256), 0, s, c, p.emb, p.semb));
+  BMARK(kBkEmbed);
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in));
+    BMARK(kBkNorm);
     BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
                                   nullptr, s)));
+    BMARK(kBkQkv);
     BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), attn_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
                   p.sin_tab, p.exp_lut));
+    BMARK(kBkAttn);
     BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s)));
+    BMARK(kBkO);
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post));
+    BMARK(kBkNorm);
     BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s)));
+    BMARK(kBkGu);
     BQ((launch_gemm<SP, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr, s)));
+    BMARK(kBkDown);
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final));
+  BMARK(kBkNorm);
   BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s)));
+  BMARK(kBkLm);
   BQ(launch_pdl(batch_argmax_kernel, dim3(p.S), dim3(256), 0, s, c, (const ArgBestD*)p.lm_partial,
                 (p.vocab + 127) / 128));
+  BMARK(kBkArgmax);
+#undef BMARK
   return Q4GPU_OK;
 }
 
@@ -802,13 +827,13 @@ int q4gpu_batch_setup(const BatchPlan& p) {
   }
 }
 
-int q4gpu_enqueue_batch_step(const BatchPlan& p, cudaStream_t s) {
+int q4gpu_enqueue_batch_step(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   switch (p.SP) {
-    case 8: return enqueue_t<8>(p, s);
-    case 16: return enqueue_t<16>(p, s);
-    case 24: return enqueue_t<24>(p, s);
-    case 32: return enqueue_t<32>(p, s);
-    case 64: return enqueue_t<64>(p, s);
+    case 8: return enqueue_t<8>(p, s, mk);
+    case 16: return enqueue_t<16>(p, s, mk);
+    case 24: return enqueue_t<24>(p, s, mk);
+    case 32: return enqueue_t<32>(p, s, mk);
+    case 64: return enqueue_t<64>(p, s, mk);
     default: return q4gpu_fail(Q4GPU_ERR_SHAPE, "padded batch %d", p.SP);
   }
 }

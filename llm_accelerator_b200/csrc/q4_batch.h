@@ -1,5 +1,7 @@
 // Batched decode (q4_batch.cu): device layout and launch interface.
 #pragma once
+#include <vector>
+
 #include "q4_state.cuh"
 
 namespace q4 {
@@ -71,8 +73,15 @@ int q4gpu_batch_box_rows(int SP);   // the same rounded up to the MMA's N granul
 // 2-D TMA map of a row-major u8 matrix [rows, inner_bytes], 128 x box_rows boxes, 128-byte swizzle
 int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows);
 int q4gpu_batch_setup(const q4::BatchPlan& p);
+// Kernel kinds of a batched step (q4gpu.h Q4GPU_BK_*), for per-kernel timing.
+enum { kBkEmbed = 0, kBkNorm, kBkQkv, kBkAttn, kBkO, kBkGu, kBkDown, kBkLm, kBkArgmax, kBkCount };
+struct BatchMarks {
+  std::vector<cudaEvent_t> ev;  // an event after each launch (the first before the step)
+  std::vector<int> kind;        // kind of the launch the event closes (-1: start)
+};
 // One decode position for all S sequences (embedding .. argmax), stream-ordered.
-int q4gpu_enqueue_batch_step(const q4::BatchPlan& p, cudaStream_t s);
+// With marks, an event is recorded after every launch (no overlap between kernels).
+int q4gpu_enqueue_batch_step(const q4::BatchPlan& p, cudaStream_t s, BatchMarks* marks = nullptr);
 // packed int4 (two per byte, even index in the low nibble) -> int8
 int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s);
 // gate/up packed rows -> the interleaved int8 layout of BatchLayerW::wgu / sgu

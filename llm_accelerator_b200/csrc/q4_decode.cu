@@ -1586,6 +1586,41 @@ int q4gpu_model_time_kernels(q4gpu_model* m, uintptr_t base, int32_t reps, doubl
   return Q4GPU_OK;
 }
 
+int q4gpu_batch_time_kernels(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t reps, double* ms_per_launch,
+                             int32_t* launches_per_step) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (reps <= 0 || !ms_per_launch || !launches_per_step) return q4gpu_fail(Q4GPU_ERR_ARG, "bad batch_time_kernels");
+  cudaGraphExec_t g;  // makes the buffers, maps and ones rows ready
+  if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
+  auto pp = std::make_unique<BatchPlan>();
+  if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
+  double tot[kBkCount] = {0};
+  int cnt[kBkCount] = {0};
+  for (int r = 0; r < reps && rc == Q4GPU_OK; ++r) {
+    BatchMarks mk;
+    rc = q4gpu_enqueue_batch_step(*pp, m->stream, &mk);
+    if (rc == Q4GPU_OK && cudaStreamSynchronize(m->stream) != cudaSuccess)
+      rc = q4gpu_fail(Q4GPU_ERR_CUDA, "batch_time_kernels sync");
+    for (size_t i = 0; rc == Q4GPU_OK && i + 1 < mk.ev.size(); ++i) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, mk.ev[i], mk.ev[i + 1]) != cudaSuccess) {
+        rc = q4gpu_fail(Q4GPU_ERR_CUDA, "event timing");
+        break;
+      }
+      tot[mk.kind[i + 1]] += ms;
+      cnt[mk.kind[i + 1]] += 1;
+    }
+    for (cudaEvent_t e : mk.ev) cudaEventDestroy(e);
+  }
+  if (rc) return rc;
+  for (int k = 0; k < kBkCount; ++k) {
+    ms_per_launch[k] = cnt[k] ? tot[k] / cnt[k] : 0.0;
+    launches_per_step[k] = cnt[k] / reps;
+  }
+  return batch_check_error(m);
+}
+
 int q4gpu_model_read_hidden(q4gpu_model* m, uintptr_t base, int32_t* hidden) {
   if (!m || !hidden || base >= (uintptr_t)m->cfg.max_seqs) return Q4GPU_ERR_ARG;
   int rc = set_device(m);

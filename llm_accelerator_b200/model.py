@@ -184,6 +184,16 @@ class Q4Model:
                                                     _ptr(sc)), "q4gpu_batch_run_step")
         return out.astype(np.int64), sc
 
+    def batch_time_kernels(self, n_seq: int, reps: int = 2, first_slot: int = 0) -> dict[str, tuple[float, int]]:
+        """Mean device ms per launch and launches per step of each batched kernel
+        (kernels serialised by events; advances the positions by `reps`)."""
+        k = len(_native.BATCH_KERNEL_KINDS)
+        ms = np.zeros(k, dtype=np.float64)
+        cnt = np.zeros(k, dtype=np.int32)
+        _native.check(self.lib.q4gpu_batch_time_kernels(self.handle, first_slot, n_seq, reps, _ptr(ms), _ptr(cnt)),
+                      "q4gpu_batch_time_kernels")
+        return {name: (float(ms[i]), int(cnt[i])) for i, name in enumerate(_native.BATCH_KERNEL_KINDS) if cnt[i]}
+
     # -- device-resident decode loop ----------------------------------------
     def decode_steps(self, n_steps: int, slot: int = 0) -> None:
         """Enqueue n greedy steps continuing slot's decode on the device (async)."""
