@@ -265,8 +265,8 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
           const int32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            s0 += (int64_t)q0[4 * j + e] * kk[e];
-            s1 += (int64_t)q1[4 * j + e] * kk[e];
+            s0 = mad_wide(q0[4 * j + e], kk[e], s0);
+            s1 = mad_wide(q1[4 * j + e], kk[e], s1);
           }
         }
       }
@@ -296,7 +296,15 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
       sum += exp_lut[ix];
     }
     sum = block_sum_i64(sum, red);
-    for (int i = t; i < kExpLut; i += blockDim.x) probtab[h][i] = ((uint64_t)exp_lut[i] << 16) / (uint64_t)sum;
+    for (int i = t; i < kExpLut; i += blockDim.x)
+      probtab[h][i] = udiv_exact((uint64_t)exp_lut[i] << 16, (uint64_t)sum);
+  }
+  __syncthreads();
+  // per-position probabilities of both heads, packed over the index array
+  int2* prs = reinterpret_cast<int2*>(sc);
+  for (int p = t; p < ctx; p += blockDim.x) {
+    const int i0 = (int)sc[p], i1 = (int)sc[ctx + p];
+    prs[p] = make_int2((int)probtab[0][i0], (int)probtab[1][i1]);
   }
   __syncthreads();
   // values: thread (warp, lane) accumulates dims 4 lane .. +3 of the chunk's
@@ -312,12 +320,12 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
         const int32_t* vrow =
             p == pos ? hv[3] : ring + ((i % kAttnRing) * kAttnChunk + warp + 8 * u) * kHeadDim;
         const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
-        const int64_t pr0 = (int64_t)probtab[0][sc[p]], pr1 = (int64_t)probtab[1][sc[ctx + p]];
+        const int2 pr = prs[p];
         const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          a0[e] += pr0 * vv[e];
-          a1[e] += pr1 * vv[e];
+          a0[e] = mad_wide(pr.x, vv[e], a0[e]);
+          a1[e] = mad_wide(pr.y, vv[e], a1[e]);
         }
       }
     }
@@ -430,6 +438,9 @@ __global__ void __launch_bounds__(kUThreads, 1)
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // every CTA is resident now: the next kernel may launch and run its
+  // prologue; it waits (griddepcontrol.wait) for this grid to complete
+  grid_dep_launch();
   auto fail = [&]() {
     *abort_flag = 1;
     atomicExch(g.c.err, 3);
@@ -533,7 +544,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         for (int j = 0; j < C::Q; ++j) {
           const int32_t lo = d0[j] + d1[j] * 256;
           const int32_t t2 = 2 * d2[j] - w256;
-          acc[j] += (int64_t)t2 * s15 + (int64_t)lo * s;
+          acc[j] = mad_wide(lo, s, mad_wide(t2, s15, acc[j]));
         }
       }
     }
@@ -554,7 +565,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
       for (int j = 0; j < C::Q; ++j) umma::cluster_st64(ca + 8 * j * nl, acc[j]);
     }
   }
-  grid_dep_launch();
   __syncwarp();
   if (splits > 1)
     umma::cluster_sync();

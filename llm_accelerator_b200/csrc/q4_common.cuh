@@ -136,6 +136,24 @@ __device__ __forceinline__ int64_t combine_limbs(uint32_t p0, uint32_t p1, int32
   return ((int64_t)p2 << 16) + (int64_t)(p0 + (p1 << 8)) - bias8;
 }
 
+// acc + (int64)a * b as one widening multiply-add
+__device__ __forceinline__ int64_t mad_wide(int32_t a, int32_t b, int64_t acc) {
+  int64_t d;
+  asm("mad.wide.s32 %0, %1, %2, %3;" : "=l"(d) : "r"(a), "r"(b), "l"(acc));
+  return d;
+}
+
+// floor(n / d) for n, d < 2^53, d > 0: the IEEE double quotient of the exact
+// operands is within one of the true quotient, fixed up with integer products.
+__device__ __forceinline__ uint64_t udiv_exact(uint64_t n, uint64_t d) {
+  uint64_t q = (uint64_t)((double)n / (double)d);
+  if (q * d > n)
+    --q;
+  else if ((q + 1) * d <= n)
+    ++q;
+  return q;
+}
+
 __device__ __forceinline__ int64_t shfl_xor_i64(int64_t v, int m) {
   return (int64_t)__shfl_xor_sync(0xFFFFFFFFu, (unsigned long long)v, m);
 }
