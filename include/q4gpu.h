@@ -76,6 +76,17 @@ int q4gpu_gemv_q26(const int32_t *act, int32_t k, const uint8_t *packed, const u
                    int32_t rows, int64_t *out_q26, int32_t *out_q12_12, int32_t *sat_count,
                    void *stream);
 
+/* `count` independent Q4 GEMVs of one shape [rows, k] whose operands sit at
+ * fixed strides: matrix i uses act + i * act_stride (elements; 0 = one shared
+ * activation), packed + i * packed_stride (bytes, a multiple of 16), scale +
+ * i * scale_stride (elements) and writes out_q26 / out_q12_12 + i * out_stride.
+ * One launch streams all matrices.  No reference counterpart: the reference
+ * calls compute_q4_gemv_q26 once per matrix; results equal `count` such calls. */
+int q4gpu_gemv_q26_strided(const int32_t *act, int64_t act_stride, int32_t k, const uint8_t *packed,
+                           int64_t packed_stride, const uint16_t *scale, int64_t scale_stride,
+                           int32_t rows, int32_t count, int64_t *out_q26, int32_t *out_q12_12,
+                           int64_t out_stride, int32_t *sat_count, void *stream);
+
 /* Q26 -> Q12.12 words, sat24(q26 >> 14); replaces q26_to_q12_12
  * (H/28_...:136-138) and q26_to_q12_12_words (H/21_...:157-160). */
 int q4gpu_q26_to_q12_12(const int64_t *in_q26, int32_t n, int32_t *out_q12_12, int32_t *sat_count,

@@ -73,6 +73,8 @@ SIGNATURES = {
     "q4gpu_synth_f32": (C.c_int, [U64, U64, I64, I64, C.c_float, C.c_int, P, P]),
     "q4gpu_quantize_q4": (C.c_int, [P, I64, I32, P, P, P, P]),
     "q4gpu_gemv_q26": (C.c_int, [P, I32, P, P, I32, P, P, P, P]),
+    "q4gpu_gemv_q26_strided": (C.c_int, [P, C.c_int64, I32, P, C.c_int64, P, C.c_int64, I32, I32, P, P,
+                                         C.c_int64, P, P]),
     "q4gpu_q26_to_q12_12": (C.c_int, [P, I32, P, P, P]),
     "q4gpu_rmsnorm": (C.c_int, [P, P, I32, I32, I32, P, P, P]),
     "q4gpu_rope": (C.c_int, [P, I32, P, P, P, P, P]),

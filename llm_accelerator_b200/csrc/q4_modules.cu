@@ -96,58 +96,6 @@ __global__ void quantize_q4_kernel(const float* __restrict__ w, int64_t rows, in
 }
 
 // ---------------------------------------------------------------------------
-// GEMV -> Q26 row sums (+ optional Q12.12 words).  One warp per R rows per
-// 1024-column slice; K slices of a row are combined in shared memory.
-// ---------------------------------------------------------------------------
-template <int K, int R>
-__global__ void __launch_bounds__(256) gemv_q26_kernel(const int32_t* __restrict__ act, const uint8_t* __restrict__ W,
-                                                       const uint16_t* __restrict__ S, int rows,
-                                                       int64_t* __restrict__ out_q26, int32_t* __restrict__ out_q12,
-                                                       int32_t* __restrict__ sat) {
-  constexpr int KS = K / 1024;
-  constexpr int NW = 8;
-  constexpr int ROW_GROUPS = NW / KS > 0 ? NW / KS : 1;  // warps per K-slice
-  extern __shared__ __align__(16) unsigned char smem[];
-  int32_t* a = reinterpret_cast<int32_t*>(smem);
-  uint32_t* limbs = reinterpret_cast<uint32_t*>(a + K);
-  int64_t* bias8 = reinterpret_cast<int64_t*>(limbs + limb_words(K));
-  int64_t* part = bias8 + K / 32;  // [KS][ROW_GROUPS*R]
-  for (int i = threadIdx.x; i < K; i += blockDim.x) a[i] = act[i];
-  __syncthreads();
-  stage_limbs(a, K, limbs, bias8);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ks = warp % KS;
-  const int rg = warp / KS;
-  const int rows_per_block = ROW_GROUPS * R;
-  for (int base = blockIdx.x * rows_per_block; base < rows; base += gridDim.x * rows_per_block) {
-    int64_t acc[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0;
-    if (rg < ROW_GROUPS) {
-      gemv_slice<K, R>(W, S, base + rg * R, rows, ks, limbs, bias8, acc);
-      warp_reduce_rows<R>(acc);
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) part[ks * rows_per_block + rg * R + r] = acc[r];
-      }
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < rows_per_block; i += blockDim.x) {
-      const int row = base + i;
-      if (row < rows) {
-        int64_t s = 0;
-#pragma unroll
-        for (int k = 0; k < KS; ++k) s += part[k * rows_per_block + i];
-        out_q26[row] = s;
-        if (out_q12) out_q12[row] = sat24c(s >> 14, sat);
-      }
-    }
-    __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------------
 // RMSNorm over `rows` vectors of length n (hidden norm or per-head norm).
 // stats (optional) receives per row: sum_squares, mean_square, radicand, rms, inv_rms.
 // ---------------------------------------------------------------------------
@@ -292,6 +240,19 @@ __global__ void embedding_kernel(const int32_t* __restrict__ tokens, const uint8
 // ascending row order: lowest index wins ties).  Per-block bests go to the
 // workspace; the last block to finish reduces them.
 // ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// Streaming Q4 GEMV (batch 1): rows stream from HBM through a 4-slot shared-
+// memory ring by bulk copies (stages of SR consecutive rows, ~16 KB, one
+// cp.async.bulk each), so every CTA keeps up to 64 KB of weights in flight.
+// A warp owns RW = SR / 8 rows of a stage; lane j covers half-group j of
+// each 1024-column slice (16 bytes, 32 nibbles) against the activation byte
+// limbs staged once per CTA.  The RW per-lane partial sums meet in a
+// transposing butterfly (each exchange halves the values a lane holds).
+// Work units are (matrix, stage) over `count` matrices of the same shape at
+// fixed strides; each CTA takes a contiguous range of units.
+// MODE 0 writes Q26 row sums (and Q12.12); MODE 1 reduces a greedy argmax
+// (strict '>' in ascending row order, lowest index on ties).
+// ---------------------------------------------------------------------------
 struct ArgBest {
   int64_t score;
   int32_t idx;
@@ -302,65 +263,346 @@ __device__ __forceinline__ bool better(int64_t s, int32_t i, int64_t bs, int32_t
   return s > bs || (s == bs && i < bi);
 }
 
-template <int R>
-__global__ void __launch_bounds__(256) lm_head_kernel(const int32_t* __restrict__ act, const uint8_t* __restrict__ W,
-                                                      const uint16_t* __restrict__ S, int rows,
-                                                      int64_t* __restrict__ logits, ArgBest* __restrict__ partial,
-                                                      unsigned int* __restrict__ counter, int32_t* __restrict__ out_tok,
-                                                      int64_t* __restrict__ out_score) {
-  constexpr int K = kHidden;
-  __shared__ __align__(16) int32_t a[K];
-  __shared__ __align__(16) uint32_t limbs[limb_words(K)];
-  __shared__ int64_t bias8[K / 32];
-  __shared__ ArgBest wbest[8];
+struct GemvArgs {
+  const int32_t* act;
+  int64_t act_stride;  // elements between the activations of consecutive matrices (0: shared)
+  const uint8_t* W;
+  int64_t w_stride;    // bytes between matrices
+  const uint16_t* S;
+  int64_t s_stride;    // elements between matrices
+  int rows;            // rows per matrix
+  int count;           // matrices
+  int64_t* out;        // [count, rows] Q26 (MODE 0), or logits (MODE 1, optional)
+  int64_t out_stride;
+  int32_t* out12;      // [count, rows] Q12.12 (optional)
+  int32_t* sat;        // saturation counter (optional)
+  ArgBest* partial;    // MODE 1: [gridDim.x]
+  unsigned int* counter;
+  int32_t* out_tok;
+  int64_t* out_score;
+};
+
+constexpr int kGvConsumers = 8;                    // consumer warps; one more warp issues the copies
+constexpr int kGvThreads = (kGvConsumers + 1) * 32;
+
+template <int K>
+struct GvCfg {
+  static constexpr int SR = K == 1024 ? 32 : 16;  // rows per stage (a multiple of 8)
+  static constexpr int RW = SR / kGvConsumers;    // rows per consumer warp per stage
+  static constexpr int KS = K / 1024;
+  static constexpr int ROWB = K / 2;   // packed bytes per row
+  static constexpr int SROWB = K / 32;  // scale bytes per row
+  static constexpr int STAGE = SR * ROWB + SR * SROWB;
+  static constexpr int NS = K == 1024 ? 4 : (K == 2048 ? 6 : (K == 3072 ? 3 : 2));  // ring slots
+  static constexpr size_t SMEM =
+      128 + (size_t)NS * STAGE + (size_t)limb_words(K) * 4 + (size_t)(K / 32) * 4 + 2 * NS * 8 + 64;
+};
+
+__device__ __forceinline__ void gv_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(bytes), "r"((uint32_t)__cvta_generic_to_shared(bar))
+               : "memory");
+}
+__device__ __forceinline__ void gv_bar_init(uint64_t* b) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"((uint32_t)__cvta_generic_to_shared(b)) : "memory");
+}
+__device__ __forceinline__ void gv_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(b)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool gv_try(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"((uint32_t)__cvta_generic_to_shared(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait (about 0.2 s), false when it ran out
+__device__ __forceinline__ bool gv_wait(uint64_t* b, unsigned parity) {
+  if (gv_try(b, parity)) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 1;; ++it) {
+    if (gv_try(b, parity)) return true;
+    if ((it & 255u) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 200000000ull) return false;
+    }
+  }
+}
+
+// Limb words of K activations (read from global) and, per half-group of 32,
+// bias = 8 * sum(a) as int32 (|sum| <= 32 * 2^23, so 8 * sum fits).  One
+// thread per 8-element chunk; the four chunks of a half-group sit in
+// consecutive lanes.  Follow with __syncthreads().
+__device__ __forceinline__ void gv_stage_limbs(const int32_t* __restrict__ act, int K, uint32_t* limbs, int32_t* bias,
+                                               int nthreads) {
+  for (int c = threadIdx.x; c < K / 8; c += nthreads) {
+    const int4 x0 = *reinterpret_cast<const int4*>(act + 8 * c);
+    const int4 x1 = *reinterpret_cast<const int4*>(act + 8 * c + 4);
+    const int32_t v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    make_limbs8(v, limbs + (c >> 2) * kLimbStride + 6 * (c & 3));
+    int32_t sum = v[0] + v[1] + v[2] + v[3] + v[4] + v[5] + v[6] + v[7];  // |sum| < 2^26
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+    if ((c & 3) == 0) bias[c >> 2] = 8 * sum;
+  }
+}
+
+// sum(w * a) * s over one lane's 32 elements as three widening multiply-adds:
+// (P0 + 256 P1) s + 2 P2 (s << 15) - bias s, with Pj the limb partial sums.
+__device__ __forceinline__ int64_t gv_span(const uint4& w, const uint32_t* l24, int32_t bias, int32_t s, int64_t acc) {
+  uint32_t p0 = 0, p1 = 0;
+  int32_t p2 = 0;
+  dot8(w.x, l24 + 0, p0, p1, p2);
+  dot8(w.y, l24 + 6, p0, p1, p2);
+  dot8(w.z, l24 + 12, p0, p1, p2);
+  dot8(w.w, l24 + 18, p0, p1, p2);
+  acc = mad_wide((int32_t)(p0 + (p1 << 8)), s, acc);
+  acc = mad_wide(2 * p2, s << 15, acc);
+  return mad_wide(bias, -s, acc);
+}
+
+// Butterfly over the warp: the RW lane-partial row sums become full sums;
+// every lane ends with the sum of row gv_lane_row<RW>(lane).
+template <int RW>
+__device__ __forceinline__ int gv_lane_row(int lane) {
+  if constexpr (RW == 4) return 2 * ((lane >> 4) & 1) + ((lane >> 3) & 1);
+  if constexpr (RW == 2) return (lane >> 4) & 1;
+  return 0;
+}
+template <int RW>
+__device__ __forceinline__ int64_t gv_reduce(const int64_t (&acc)[RW], int lane) {
+  int64_t v;
+  if constexpr (RW == 4) {
+    const bool h4 = lane & 16;
+    int64_t k0 = h4 ? acc[2] : acc[0], k1 = h4 ? acc[3] : acc[1];
+    k0 += shfl_xor_i64(h4 ? acc[0] : acc[2], 16);
+    k1 += shfl_xor_i64(h4 ? acc[1] : acc[3], 16);
+    const bool h3 = lane & 8;
+    v = (h3 ? k1 : k0) + shfl_xor_i64(h3 ? k0 : k1, 8);
+    v += shfl_xor_i64(v, 4);
+    v += shfl_xor_i64(v, 2);
+    v += shfl_xor_i64(v, 1);
+  } else if constexpr (RW == 2) {
+    const bool h4 = lane & 16;
+    v = (h4 ? acc[1] : acc[0]) + shfl_xor_i64(h4 ? acc[0] : acc[1], 16);
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) v += shfl_xor_i64(v, m);
+  } else {
+    v = warp_sum_i64(acc[0]);
+  }
+  return v;
+}
+
+// SBULK: scales travel with the weights by bulk copy (16-byte aligned scale
+// rows); otherwise each lane loads its scales from global memory.
+__device__ __forceinline__ void gv_bar_init_n(uint64_t* b, unsigned n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(b)), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void gv_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"((uint32_t)__cvta_generic_to_shared(b)) : "memory");
+}
+__device__ __forceinline__ void gv_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kGvConsumers * 32) : "memory");
+}
+
+template <int K, int MODE, bool SBULK>
+__global__ void __launch_bounds__(kGvThreads) gemv_stream_kernel(GemvArgs g) {
+  using C = GvCfg<K>;
+  extern __shared__ __align__(128) unsigned char gv_smem[];
+  uint8_t* ring = gv_smem;
+  uint32_t* limbs = reinterpret_cast<uint32_t*>(gv_smem + C::NS * C::STAGE);
+  int32_t* bias = reinterpret_cast<int32_t*>(limbs + limb_words(K));
+  uint64_t* full = reinterpret_cast<uint64_t*>(bias + K / 32);
+  uint64_t* empty = full + C::NS;
+  __shared__ ArgBest wbest[kGvConsumers];
   __shared__ bool last;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) a[i] = act[i];
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int spm = (g.rows + C::SR - 1) / C::SR;  // stages per matrix
+  const int64_t total = (int64_t)spm * g.count;
+  const int64_t u0 = total * blockIdx.x / gridDim.x, u1 = total * (blockIdx.x + 1) / gridDim.x;
+  const int n = (int)(u1 - u0);
+  if (t == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      gv_bar_init(full + s);
+      gv_bar_init_n(empty + s, kGvConsumers);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   __syncthreads();
-  stage_limbs(a, K, limbs, bias8);
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   int64_t best_s = INT64_MIN;
   int32_t best_i = INT32_MAX;
-  for (int base = (blockIdx.x * nw + warp) * R; base < rows; base += gridDim.x * nw * R) {
-    int64_t acc[R];
+  if (warp == kGvConsumers) {
+    // producer: one lane streams the CTA's stages through the ring
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        const int s = i % C::NS;
+        if (i >= C::NS && !gv_wait(empty + s, ((i / C::NS) - 1) & 1)) break;
+        const int64_t u = u0 + i;
+        const int m = (int)(u / spm), j = (int)(u % spm);
+        const int nr = min(C::SR, g.rows - j * C::SR);
+        uint8_t* dst = ring + s * C::STAGE;
+        gv_expect(full + s, (uint32_t)nr * (C::ROWB + (SBULK ? C::SROWB : 0)));
+        gv_bulk(dst, g.W + m * g.w_stride + (int64_t)j * C::SR * C::ROWB, (uint32_t)nr * C::ROWB, full + s);
+        if constexpr (SBULK)
+          gv_bulk(dst + C::SR * C::ROWB, g.S + m * g.s_stride + (int64_t)j * C::SR * (K / 64), (uint32_t)nr * C::SROWB,
+                  full + s);
+      }
+    }
+  } else {
+    int cur_m = -1;
+    uint32_t l24[24];  // this lane's limbs when K is one slice
+    int32_t b32 = 0;
+    for (int i = 0; i < n; ++i) {
+      const int64_t u = u0 + i;
+      const int m = (int)(u / spm), j = (int)(u % spm);
+      if (m != cur_m && (cur_m < 0 || g.act_stride != 0)) {
+        gv_consumer_sync();
+        gv_stage_limbs(g.act + m * g.act_stride, K, limbs, bias, kGvConsumers * 32);
+        gv_consumer_sync();
+        if constexpr (C::KS == 1) {
+          const uint4* lp = reinterpret_cast<const uint4*>(limbs + lane * kLimbStride);
 #pragma unroll
-    for (int r = 0; r < R; ++r) acc[r] = 0;
-    gemv_slice<K, R>(W, S, base, rows, 0, limbs, bias8, acc);
-    warp_reduce_rows<R>(acc);
+          for (int q = 0; q < 6; ++q) {
+            const uint4 v = lp[q];
+            l24[4 * q] = v.x;
+            l24[4 * q + 1] = v.y;
+            l24[4 * q + 2] = v.z;
+            l24[4 * q + 3] = v.w;
+          }
+          b32 = bias[lane];
+        }
+      }
+      cur_m = m;
+      const int row0 = j * C::SR;
+      const int s = i % C::NS;
+      uint32_t sc[C::RW][C::KS];
+      if constexpr (!SBULK) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = base + r;
-      if (row < rows) {
-        if (logits && lane == r) logits[row] = acc[r];
-        if (acc[r] > best_s) {  // rows visited in ascending order within a warp
-          best_s = acc[r];
-          best_i = row;
+        for (int r = 0; r < C::RW; ++r) {
+          const int row = row0 + warp * C::RW + r;
+          const uint16_t* srow = g.S + m * g.s_stride + (int64_t)min(row, g.rows - 1) * (K / 64);
+#pragma unroll
+          for (int ks = 0; ks < C::KS; ++ks) sc[r][ks] = __ldg(srow + ((ks * 32 + lane) >> 1));
+        }
+      }
+      const bool ok = gv_wait(full + s, (i / C::NS) & 1);
+      const uint8_t* st = ring + s * C::STAGE;
+      if constexpr (SBULK) {
+        const uint16_t* ss = reinterpret_cast<const uint16_t*>(st + C::SR * C::ROWB);
+#pragma unroll
+        for (int r = 0; r < C::RW; ++r)
+#pragma unroll
+          for (int ks = 0; ks < C::KS; ++ks) sc[r][ks] = ss[(warp * C::RW + r) * (K / 64) + ((ks * 32 + lane) >> 1)];
+      }
+      int64_t acc[C::RW];
+#pragma unroll
+      for (int r = 0; r < C::RW; ++r) acc[r] = 0;
+#pragma unroll
+      for (int ks = 0; ks < C::KS; ++ks) {
+        if constexpr (C::KS > 1) {
+          const int hg = ks * 32 + lane;
+          const uint4* lp = reinterpret_cast<const uint4*>(limbs + hg * kLimbStride);
+#pragma unroll
+          for (int q = 0; q < 6; ++q) {
+            const uint4 v = lp[q];
+            l24[4 * q] = v.x;
+            l24[4 * q + 1] = v.y;
+            l24[4 * q + 2] = v.z;
+            l24[4 * q + 3] = v.w;
+          }
+          b32 = bias[hg];
+        }
+#pragma unroll
+        for (int r = 0; r < C::RW; ++r) {
+          const int lr = warp * C::RW + r;
+          if (row0 + lr < g.rows && ok) {
+            const uint4 w = *reinterpret_cast<const uint4*>(st + lr * C::ROWB + ks * 512 + lane * 16);
+            acc[r] = gv_span(w, l24, b32, (int32_t)sc[r][ks], acc[r]);
+          }
+        }
+      }
+      // the stage's bytes are in registers: hand the slot back
+      __syncwarp();
+      if (lane == 0) gv_arrive(empty + s);
+      const int64_t v = gv_reduce<C::RW>(acc, lane);
+      const int row = row0 + warp * C::RW + gv_lane_row<C::RW>(lane);
+      if ((lane & (32 / C::RW - 1)) == 0 && row < g.rows) {
+        if constexpr (MODE == 0) {
+          g.out[m * g.out_stride + row] = v;
+          if (g.out12) g.out12[m * g.out_stride + row] = sat24c(v >> 14, g.sat);
+        } else {
+          if (g.out) g.out[row] = v;
+          if (better(v, row, best_s, best_i)) {
+            best_s = v;
+            best_i = row;
+          }
         }
       }
     }
   }
-  if (lane == 0) wbest[warp] = ArgBest{best_s, best_i, 0};
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    ArgBest b = wbest[0];
-    for (int w = 1; w < nw; ++w)
-      if (better(wbest[w].score, wbest[w].idx, b.score, b.idx)) b = wbest[w];
-    partial[blockIdx.x] = b;
-    __threadfence();
-    const unsigned int done = atomicAdd(counter, 1u);
-    last = (done == gridDim.x - 1);
-  }
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    __threadfence();
-    ArgBest b = partial[0];
-    for (int i = 1; i < (int)gridDim.x; ++i) {
-      const ArgBest c{*((volatile int64_t*)&partial[i].score), *((volatile int32_t*)&partial[i].idx), 0};
-      if (better(c.score, c.idx, b.score, b.idx)) b = c;
+  if constexpr (MODE == 1) {
+    auto warp_best = [&](int64_t& bs, int32_t& bi) {
+#pragma unroll
+      for (int msk = 1; msk < 32; msk <<= 1) {
+        const int64_t os = shfl_xor_i64(bs, msk);
+        const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, msk);
+        if (better(os, oi, bs, bi)) {
+          bs = os;
+          bi = oi;
+        }
+      }
+    };
+    __syncwarp();
+    warp_best(best_s, best_i);
+    if (lane == 0 && warp < kGvConsumers) wbest[warp] = ArgBest{best_s, best_i, 0};
+    __syncthreads();
+    if (t == 0) {
+      ArgBest b = wbest[0];
+      for (int w = 1; w < kGvConsumers; ++w)
+        if (better(wbest[w].score, wbest[w].idx, b.score, b.idx)) b = wbest[w];
+      g.partial[blockIdx.x] = b;
+      __threadfence();
+      const unsigned int done = atomicAdd(g.counter, 1u);
+      last = (done == gridDim.x - 1);
     }
-    *out_tok = b.idx;
-    *out_score = b.score;
-    *counter = 0;  // ready for the next launch
+    __syncthreads();
+    if (last) {  // the last CTA reduces all partials, every thread a strided share
+      __threadfence();
+      int64_t bs = INT64_MIN;
+      int32_t bi = INT32_MAX;
+      for (int i = t; i < (int)gridDim.x; i += kGvThreads) {
+        const int64_t cs = *((volatile int64_t*)&g.partial[i].score);
+        const int32_t ci = *((volatile int32_t*)&g.partial[i].idx);
+        if (better(cs, ci, bs, bi)) {
+          bs = cs;
+          bi = ci;
+        }
+      }
+      warp_best(bs, bi);
+      __syncthreads();
+      if (lane == 0 && warp < kGvConsumers) wbest[warp] = ArgBest{bs, bi, 0};
+      // the producer warp's share (partials kGvConsumers*32 ..) joins through warp 0's slot
+      __syncthreads();
+      if (lane == 0 && warp == kGvConsumers && better(bs, bi, wbest[0].score, wbest[0].idx))
+        wbest[0] = ArgBest{bs, bi, 0};
+      __syncthreads();
+      if (t == 0) {
+        ArgBest b = wbest[0];
+        for (int w = 1; w < kGvConsumers; ++w)
+          if (better(wbest[w].score, wbest[w].idx, b.score, b.idx)) b = wbest[w];
+        *g.out_tok = b.idx;
+        *g.out_score = b.score;
+        *g.counter = 0;  // ready for the next launch
+      }
+    }
   }
 }
 
@@ -405,27 +647,88 @@ int q4gpu_quantize_q4(const float* w, int64_t rows, int32_t cols, uint8_t* packe
   return q4gpu_check_launch();
 }
 
+}  // extern "C"
+
+namespace {
+
+template <int K, int MODE>
+int gv_launch(const GemvArgs& g, int grid_cap, cudaStream_t s) {
+  using C = GvCfg<K>;
+  static_assert(C::SMEM < 227 * 1024, "GEMV stage ring too large");
+  // scales ride with the weights when every stage's scale rows start 16-byte aligned
+  const bool sbulk = ((uintptr_t)g.S & 15) == 0 && ((g.s_stride * 2) & 15) == 0;
+  auto kern = sbulk ? gemv_stream_kernel<K, MODE, true> : gemv_stream_kernel<K, MODE, false>;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "GEMV shared memory: %s", cudaGetErrorString(e));
+  const int64_t units = (int64_t)((g.rows + C::SR - 1) / C::SR) * g.count;
+  const int grid = (int)std::min<int64_t>(units, grid_cap);
+  kern<<<grid, kGvThreads, C::SMEM, s>>>(g);
+  return q4gpu_check_launch();
+}
+
+// CTAs per SM that fit the stage ring (x148 SMs), capped by the LM-head partial array
+int gv_grid_cap(int K) { return (K == 1024 ? 3 : 2) * 148; }
+
+template <int MODE>
+int gv_dispatch(int K, const GemvArgs& g, int grid_cap, cudaStream_t s) {
+  switch (K) {
+    case 1024: return gv_launch<1024, MODE>(g, grid_cap, s);
+    case 2048: return gv_launch<2048, MODE>(g, grid_cap, s);
+    case 3072: return gv_launch<3072, MODE>(g, grid_cap, s);
+    case 4096: return gv_launch<4096, MODE>(g, grid_cap, s);
+    default: return q4gpu_fail(Q4GPU_ERR_SHAPE, "GEMV K must be 1024, 2048, 3072 or 4096 (got %d)", K);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
 int q4gpu_gemv_q26(const int32_t* act, int32_t k, const uint8_t* packed, const uint16_t* scale, int32_t rows,
                    int64_t* out_q26, int32_t* out_q12_12, int32_t* sat_count, void* stream) {
   if (!act || !packed || !scale || !out_q26 || rows <= 0) return Q4GPU_ERR_ARG;
-  if ((((uintptr_t)packed) & 15) || (((uintptr_t)scale) & 1)) return Q4GPU_ERR_ALIGN;
-  constexpr int R = 4;
-  auto launch = [&](auto kern, int K) {
-    const int KS = K / 1024;
-    const int rows_per_block = (8 / KS) * R;
-    const size_t smem = K * 4 + limb_words(K) * 4 + (K / 32) * 8 + KS * rows_per_block * 8;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const int blocks = std::min((rows + rows_per_block - 1) / rows_per_block, 148 * 8);
-    kern<<<blocks, 256, smem, as_stream(stream)>>>(act, packed, scale, rows, out_q26, out_q12_12, sat_count);
-  };
-  switch (k) {
-    case 1024: launch(gemv_q26_kernel<1024, R>, 1024); break;
-    case 2048: launch(gemv_q26_kernel<2048, R>, 2048); break;
-    case 3072: launch(gemv_q26_kernel<3072, R>, 3072); break;
-    case 4096: launch(gemv_q26_kernel<4096, R>, 4096); break;
-    default: return Q4GPU_ERR_SHAPE;
-  }
-  return q4gpu_check_launch();
+  if ((((uintptr_t)packed) & 15) || (((uintptr_t)scale) & 1) || (((uintptr_t)act) & 15)) return Q4GPU_ERR_ALIGN;
+  if (k != 1024 && k != 2048 && k != 3072 && k != 4096) return Q4GPU_ERR_SHAPE;
+  GemvArgs g{};
+  g.act = act;
+  g.W = packed;
+  g.S = scale;
+  g.rows = rows;
+  g.count = 1;
+  g.out = out_q26;
+  g.out12 = out_q12_12;
+  g.sat = sat_count;
+  return gv_dispatch<0>(k, g, gv_grid_cap(k), as_stream(stream)) == Q4GPU_OK ? Q4GPU_OK : Q4GPU_ERR_CUDA;
+}
+
+int q4gpu_gemv_q26_strided(const int32_t* act, int64_t act_stride, int32_t k, const uint8_t* packed,
+                           int64_t packed_stride, const uint16_t* scale, int64_t scale_stride, int32_t rows,
+                           int32_t count, int64_t* out_q26, int32_t* out_q12_12, int64_t out_stride,
+                           int32_t* sat_count, void* stream) {
+  if (!act || !packed || !scale || !out_q26 || rows <= 0 || count <= 0 || act_stride < 0 ||
+      out_stride < (count > 1 ? rows : 0))
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad strided GEMV arguments");
+  if ((((uintptr_t)packed) & 15) || (packed_stride & 15) || (((uintptr_t)scale) & 1) || (((uintptr_t)act) & 15) ||
+      (act_stride & 3))
+    return q4gpu_fail(Q4GPU_ERR_ALIGN, "activations, packed weights and their strides must be 16-byte aligned");
+  if (k != 1024 && k != 2048 && k != 3072 && k != 4096)
+    return q4gpu_fail(Q4GPU_ERR_SHAPE, "GEMV K must be 1024, 2048, 3072 or 4096 (got %d)", k);
+  if (count > 1 && (packed_stride < (int64_t)rows * k / 2 || scale_stride < (int64_t)rows * k / 64))
+    return q4gpu_fail(Q4GPU_ERR_ARG, "matrix strides overlap");
+  GemvArgs g{};
+  g.act = act;
+  g.act_stride = act_stride;
+  g.W = packed;
+  g.w_stride = packed_stride;
+  g.S = scale;
+  g.s_stride = scale_stride;
+  g.rows = rows;
+  g.count = count;
+  g.out = out_q26;
+  g.out_stride = out_stride;
+  g.out12 = out_q12_12;
+  g.sat = sat_count;
+  return gv_dispatch<0>(k, g, gv_grid_cap(k), as_stream(stream));
 }
 
 int q4gpu_rmsnorm(const int32_t* x, const int32_t* gamma, int32_t rows, int32_t n, int32_t mode, int32_t* out,
@@ -506,14 +809,23 @@ int q4gpu_lm_head_argmax(const int32_t* act, const uint8_t* packed, const uint16
                          int64_t* out_score, void* stream) {
   if (!act || !packed || !scale || rows <= 0 || !workspace || !out_token || !out_score) return Q4GPU_ERR_ARG;
   if (workspace_bytes < q4gpu_lm_head_workspace_bytes(rows)) return Q4GPU_ERR_WORKSPACE;
-  if ((((uintptr_t)packed) & 15) || (((uintptr_t)workspace) & 15)) return Q4GPU_ERR_ALIGN;
+  if ((((uintptr_t)packed) & 15) || (((uintptr_t)workspace) & 15) || (((uintptr_t)act) & 15)) return Q4GPU_ERR_ALIGN;
   ArgBest* partial = reinterpret_cast<ArgBest*>(workspace);
   unsigned int* counter =
       reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + Q4GPU_LM_HEAD_BLOCKS * sizeof(ArgBest));
   cudaMemsetAsync(counter, 0, sizeof(unsigned int), as_stream(stream));
-  lm_head_kernel<4><<<Q4GPU_LM_HEAD_BLOCKS, 256, 0, as_stream(stream)>>>(act, packed, scale, rows, logits, partial,
-                                                                          counter, out_token, out_score);
-  return q4gpu_check_launch();
+  GemvArgs g{};
+  g.act = act;
+  g.W = packed;
+  g.S = scale;
+  g.rows = rows;
+  g.count = 1;
+  g.out = logits;
+  g.partial = partial;
+  g.counter = counter;
+  g.out_tok = out_token;
+  g.out_score = out_score;
+  return gv_dispatch<1>(kHidden, g, gv_grid_cap(kHidden), as_stream(stream)) == Q4GPU_OK ? Q4GPU_OK : Q4GPU_ERR_CUDA;
 }
 
 // Device address of g_lm_head_static_scratch, looked up once per device (with
@@ -544,7 +856,8 @@ int q4gpu_lm_head_argmax_noalloc(const int32_t* act, const uint8_t* packed, cons
   if (rows <= 0 || rows > Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS)
     return q4gpu_fail(Q4GPU_ERR_ARG, "rows %d outside 1..%d supported by the static LM-head scratch", rows,
                       Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS);
-  if (((uintptr_t)packed) & 15) return q4gpu_fail(Q4GPU_ERR_ALIGN, "packed weights must be 16-byte aligned");
+  if ((((uintptr_t)packed) & 15) || (((uintptr_t)act) & 15))
+    return q4gpu_fail(Q4GPU_ERR_ALIGN, "activation and packed weights must be 16-byte aligned");
   q4::LmHeadStaticScratch* sc = nullptr;
   int rc = lm_head_static_scratch(&sc);
   if (rc) return rc;
@@ -552,10 +865,18 @@ int q4gpu_lm_head_argmax_noalloc(const int32_t* act, const uint8_t* packed, cons
   // but an earlier call may have been cut short)
   const cudaError_t e = cudaMemsetAsync(&sc->counter, 0, sizeof(unsigned int), as_stream(stream));
   if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "scratch clear: %s", cudaGetErrorString(e));
-  lm_head_kernel<4><<<Q4GPU_LM_HEAD_BLOCKS, 256, 0, as_stream(stream)>>>(act, packed, scale, rows, logits,
-                                                                          sc->partial, &sc->counter, out_token,
-                                                                          out_score);
-  return q4gpu_check_launch();
+  GemvArgs g{};
+  g.act = act;
+  g.W = packed;
+  g.S = scale;
+  g.rows = rows;
+  g.count = 1;
+  g.out = logits;
+  g.partial = sc->partial;
+  g.counter = &sc->counter;
+  g.out_tok = out_token;
+  g.out_score = out_score;
+  return gv_dispatch<1>(kHidden, g, gv_grid_cap(kHidden), as_stream(stream));
 }
 
 }  // extern "C"

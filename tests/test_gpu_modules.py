@@ -201,3 +201,37 @@ def test_embedding_rows():
     got = R.embedding_hidden(toks, O.pack_int4(q), s)
     for i, t in enumerate(toks):
         assert np.array_equal(got[i], O.embedding_hidden(q[t], s[t]))
+
+
+@pytest.mark.parametrize("k,rows,count,shared", [(1024, 3072, 4, False), (2048, 100, 5, True), (3072, 37, 3, False),
+                                                 (4096, 9, 2, True)])
+def test_gemv_strided_many(k, rows, count, shared):
+    """q4gpu_gemv_q26_strided: `count` GEMVs in one launch equal `count`
+    separate oracle GEMVs (distinct or one shared activation)."""
+    from llm_accelerator_b200 import _native
+    lib = _native.load()
+    rng = np.random.default_rng(k * 7 + rows)
+    q = rng.integers(-8, 8, (count, rows, k)).astype(np.int8)
+    s = rng.integers(0, 1 << 16, (count, rows, k // 64)).astype(np.uint16)
+    a = rng.integers(-(1 << 23), 1 << 23, (1 if shared else count, k)).astype(np.int32)
+    packed = np.stack([O.pack_int4(q[i]) for i in range(count)])
+    dev = torch.device("cuda")
+    ta = torch.from_numpy(a).to(dev)
+    tw = torch.from_numpy(packed).to(dev)
+    ts = torch.from_numpy(s.view(np.int16)).to(dev)
+    out = torch.zeros((count, rows), dtype=torch.int64, device=dev)
+    o12 = torch.zeros((count, rows), dtype=torch.int32, device=dev)
+    sat = torch.zeros(1, dtype=torch.int32, device=dev)
+    rc = lib.q4gpu_gemv_q26_strided(ta.data_ptr(), 0 if shared else k, k, tw.data_ptr(), rows * k // 2, ts.data_ptr(),
+                                    rows * k // 64, rows, count, out.data_ptr(), o12.data_ptr(), rows, sat.data_ptr(),
+                                    None)
+    assert rc == 0, lib.q4gpu_last_error()
+    torch.cuda.synchronize()
+    n_sat = 0
+    for i in range(count):
+        ref = O.gemv_q26(a[0 if shared else i].astype(np.int64), q[i], s[i])
+        assert np.array_equal(out[i].cpu().numpy(), ref), i
+        r12, ns = O.q26_to_q12_12(ref)
+        assert np.array_equal(o12[i].cpu().numpy().astype(np.int64), r12), i
+        n_sat += ns
+    assert int(sat.item()) == n_sat
