@@ -169,7 +169,8 @@ def dist_setup():
 
 
 def prompts_for(rank: int) -> list[list[int]]:
-    return [np.random.default_rng(1000 * rank + i).integers(0, VOCAB, PROMPT).tolist() for i in range(BATCH)]
+    from llm_accelerator_b200.sharding import rank_prompts
+    return rank_prompts(rank, BATCH, PROMPT, VOCAB)
 
 
 # ---------------------------------------------------------------------------
@@ -286,12 +287,10 @@ def run_ours(args, ws, rank, local):
         if dist is not None:
             dist.barrier()
 
+    from llm_accelerator_b200.sharding import max_over_ranks as _max_over_ranks
+
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return _max_over_ranks(x, device=torch.device("cuda", local))
 
     steps, warm = args.steps, args.warmup
     m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=MAX_CTX, max_seqs=BATCH, device=local)
