@@ -38,7 +38,18 @@ struct BatchCtx {
   int32_t* hidden0;        // [S, 1024]
   int32_t* post0;          // [S, 1024]
   int max_ctx;
+  // optional timeline (nullptr = off): attention CTA (m, kv) of layer l writes
+  // %globaltimer stamps at its phase boundaries to trace[((l * S + m) * 8 + kv) * 8 + k]
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void attn_stamp(const BatchCtx& c, int layer, int m, int kv, int k) {
+  if (c.trace && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    c.trace[(((size_t)layer * c.S + m) * kKvHeads + kv) * 8 + k] = t;
+  }
+}
 
 // limbs of the unsigned offset value a + 2^23
 __device__ __forceinline__ void write_limbs(uint8_t* bt, int SP, int K, int m, int k, int32_t a) {
@@ -154,15 +165,33 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
   }
 }
 
-// Attention for one (KV head, sequence): q/k head RMSNorm + RoPE, KV append,
-// exact two-pass LUT softmax for the two query heads of the group; writes the
-// output and its limbs (the o_proj B matrix).  256 threads.  K, then V, of the
-// earlier positions stream through a 3-slot ring of 32-position chunks (16 KB
-// bulk copies, contiguous inside a KV page); the current position's K/V row
-// is taken from shared memory.
-constexpr int kAttnChunk = 32;
-constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
-constexpr int kAttnRing = 3;
+// ---------------------------------------------------------------------------
+// Split-KV attention: one CTA per (sequence m, KV head h, page c of 64
+// positions), so the work spreads evenly over the GPU whatever the batch and
+// context.  The exact two-pass LUT softmax is resolved across the pages of a
+// (m, h) pair by the CTA that finishes last:
+//   scores kernel: q head norm + RoPE (both query heads of the group), the new
+//     position's k (norm + RoPE) and v appended to the cache, scaled scores
+//     of the page to S, page maxima folded into M by atomicMax; the last page
+//     turns S into probabilities P (LUT index, sum, one division per LUT entry)
+//     and re-arms M.
+//   values kernel: sum over the page of P * V into O by 64-bit atomic adds;
+//     the last page writes sat24(O >> 16) as limbs of the o_proj input and
+//     re-arms O.
+// Integer sums are order independent, so the result equals the serial one.
+// ---------------------------------------------------------------------------
+constexpr int kPage = kKvPage;  // 64 positions per unit
+constexpr int kPageBytes = kPage * kHeadDim * 4;
+
+struct AttnScratch {
+  int64_t* S;         // [64 seqs][16 heads][max_ctx] scaled scores
+  uint32_t* P;        // [64][16][max_ctx] probabilities (UQ0.16, <= 65536)
+  int64_t* M;         // [64][16] running maxima, INT64_MIN when armed
+  int64_t* O;         // [64][16][128] value sums, 0 when armed
+  unsigned* cnt_s;    // [64][8] pages done, scores kernel
+  unsigned* cnt_v;    // [64][8] pages done, values kernel
+  int max_ctx;
+};
 
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -171,7 +200,249 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-__global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
+__device__ __forceinline__ int64_t ld_cg64(const int64_t* p) {
+  return (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
+}
+
+__global__ void __launch_bounds__(256) batch_attn_scores_kernel(BatchCtx c, AttnScratch a, int layer,
+                                                                const int32_t* __restrict__ g_q,
+                                                                const int32_t* __restrict__ g_k,
+                                                                const int32_t* __restrict__ cos_tab,
+                                                                const int32_t* __restrict__ sin_tab,
+                                                                const int32_t* __restrict__ exp_lut) {
+  __shared__ __align__(128) int32_t kpage[kPage * kHeadDim];  // 32 KB
+  __shared__ __align__(16) int32_t hv[3][kHeadDim];           // roped q0, q1, k of the new position
+  __shared__ int64_t red[32];
+  __shared__ int64_t wmax[8][2];
+  __shared__ uint32_t probtab[2][kExpLut];
+  __shared__ uint64_t bar;
+  __shared__ bool last;
+  const int pg = blockIdx.x, h = blockIdx.y, m = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int pos = c.pos0[4 * m];
+  if (pos >= c.max_ctx || pg * kPage > pos) return;
+  const int ctx = pos + 1, nch = (ctx + kPage - 1) / kPage;
+  const KvView kvv = c.slots[m].kv;
+  const int p0 = pg * kPage;
+  const int nold = min(kPage, pos - p0);  // rows of this page written by earlier steps
+  if (t == 0) {
+    umma::bar_init(&bar, 1);
+    umma::bar_init_fence();
+    umma::bar_expect_tx(&bar, nold > 0 ? (uint32_t)nold * kHeadDim * 4 : 0u);
+    if (nold > 0) bulk_load(kpage, kvv.at(layer, 0, h, p0), (uint32_t)nold * kHeadDim * 4, &bar);
+  }
+  const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
+  const bool has_new = pos < p0 + kPage;
+  // warps 0/1: q heads 2h, 2h+1; warp 2: k of the new position; warp 3: its v
+  if (warp < 3 && (warp < 2 || has_new)) {
+    const int row = warp < 2 ? (2 * h + warp) * kHeadDim : kQRows + h * kHeadDim;
+    const int4 x = *reinterpret_cast<const int4*>(raw + row + 4 * lane);
+    const int32_t xs[4] = {x.x, x.y, x.z, x.w};
+    int64_t ss = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += (int64_t)xs[e] * xs[e];
+    ss = warp_sum_i64(ss);
+    const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
+    const int32_t* gm = warp < 2 ? g_q : g_k;
+    int32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = 4 * lane + e;
+      const int32_t n = norm_apply(xs[e], inv, gm[d], kHeadNorm);
+      const int32_t partner = __shfl_xor_sync(0xFFFFFFFFu, n, 16);
+      const int64_t rot = lane < 16 ? -(int64_t)partner : (int64_t)partner;
+      o[e] = sat24(((int64_t)n * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
+    }
+    const int4 o4 = make_int4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
+    if (warp == 2) {
+      reinterpret_cast<int4*>(kvv.at(layer, 0, h, pos))[lane] = o4;
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // later bulk copies read this row
+    }
+  } else if (warp == 3 && has_new) {
+    reinterpret_cast<int4*>(kvv.at(layer, 1, h, pos))[lane] =
+        *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + h * kHeadDim + 4 * lane);
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  __syncthreads();
+  if (!umma::bar_wait(&bar, 0)) atomicExch(c.err, 4);
+  // 64 positions: warp w takes 8, four at a time (8 lanes per position; lane
+  // `sub` holds dims 4 (sub + 8 j) .. +3)
+  const int sub = lane & 7, quad = lane >> 3;
+  int32_t q0[16], q1[16];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int4 u = *reinterpret_cast<const int4*>(&hv[0][4 * (sub + 8 * j)]);
+    const int4 v = *reinterpret_cast<const int4*>(&hv[1][4 * (sub + 8 * j)]);
+    q0[4 * j] = u.x; q0[4 * j + 1] = u.y; q0[4 * j + 2] = u.z; q0[4 * j + 3] = u.w;
+    q1[4 * j] = v.x; q1[4 * j + 1] = v.y; q1[4 * j + 2] = v.z; q1[4 * j + 3] = v.w;
+  }
+  int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
+  int64_t* S0 = a.S + ((size_t)m * kQHeads + 2 * h) * a.max_ctx;
+  int64_t* S1 = S0 + a.max_ctx;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int lp = warp * 8 + r * 4 + quad;
+    const int p = p0 + lp;
+    const int32_t* krow = p == pos ? hv[2] : kpage + lp * kHeadDim;
+    int64_t s0 = 0, s1 = 0;
+    if (p < ctx) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * (sub + 8 * j));
+        const int32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          s0 = mad_wide(q0[4 * j + e], kk[e], s0);
+          s1 = mad_wide(q1[4 * j + e], kk[e], s1);
+        }
+      }
+    }
+#pragma unroll
+    for (int msk = 1; msk < 8; msk <<= 1) {
+      s0 += shfl_xor_i64(s0, msk);
+      s1 += shfl_xor_i64(s1, msk);
+    }
+    if (p < ctx) {
+      const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
+      if (sub == 0) {
+        S0[p] = v0;
+        S1[p] = v1;
+      }
+      mx0 = v0 > mx0 ? v0 : mx0;
+      mx1 = v1 > mx1 ? v1 : mx1;
+    }
+  }
+#pragma unroll
+  for (int msk = 8; msk < 32; msk <<= 1) {
+    const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
+    mx0 = o0 > mx0 ? o0 : mx0;
+    mx1 = o1 > mx1 ? o1 : mx1;
+  }
+  if (lane == 0) {
+    wmax[warp][0] = mx0;
+    wmax[warp][1] = mx1;
+  }
+  __syncthreads();
+  int64_t* Mh = a.M + (size_t)m * kQHeads + 2 * h;
+  if (t < 2) {
+    int64_t b = wmax[0][t];
+    for (int w = 1; w < 8; ++w) b = wmax[w][t] > b ? wmax[w][t] : b;
+    atomicMax(reinterpret_cast<long long*>(Mh + t), (long long)b);
+  }
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    unsigned* cnt = a.cnt_s + m * kKvHeads + h;
+    last = atomicAdd(cnt, 1u) == (unsigned)nch - 1;
+    if (last) *cnt = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  // last page of (m, h): scores -> probabilities for both heads
+  __threadfence();
+  uint32_t* P0 = a.P + ((size_t)m * kQHeads + 2 * h) * a.max_ctx;
+#pragma unroll 1
+  for (int hh = 0; hh < 2; ++hh) {
+    const int64_t mx = ld_cg64(Mh + hh);
+    const int64_t* Sh = hh ? S1 : S0;
+    int64_t sum = 0;
+    for (int p = t; p < ctx; p += blockDim.x) sum += exp_lut[lut_index(mx, ld_cg64(Sh + p))];
+    sum = block_sum_i64(sum, red);
+    for (int i = t; i < kExpLut; i += blockDim.x)
+      probtab[hh][i] = (uint32_t)udiv_exact((uint64_t)exp_lut[i] << 16, (uint64_t)sum);
+    __syncthreads();
+    uint32_t* Ph = P0 + (size_t)hh * a.max_ctx;
+    for (int p = t; p < ctx; p += blockDim.x) Ph[p] = probtab[hh][lut_index(mx, ld_cg64(Sh + p))];
+  }
+  if (t < 2) Mh[t] = INT64_MIN;
+}
+
+__global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, AttnScratch a, int layer) {
+  __shared__ __align__(128) int32_t vpage[kPage * kHeadDim];  // 32 KB
+  __shared__ int2 pr[kPage];
+  __shared__ uint64_t bar;
+  __shared__ bool last;
+  const int pg = blockIdx.x, h = blockIdx.y, m = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  grid_dep_wait();
+  grid_dep_launch();
+  const int pos = c.pos0[4 * m];
+  if (pos >= c.max_ctx || pg * kPage > pos) return;
+  const int ctx = pos + 1, nch = (ctx + kPage - 1) / kPage;
+  const int p0 = pg * kPage;
+  const int n = min(kPage, ctx - p0);
+  if (t == 0) {
+    umma::bar_init(&bar, 1);
+    umma::bar_init_fence();
+    umma::bar_expect_tx(&bar, (uint32_t)n * kHeadDim * 4);
+    bulk_load(vpage, c.slots[m].kv.at(layer, 1, h, p0), (uint32_t)n * kHeadDim * 4, &bar);
+  }
+  const uint32_t* P0 = a.P + ((size_t)m * kQHeads + 2 * h) * a.max_ctx;
+  if (t < kPage) pr[t] = t < n ? make_int2((int)P0[p0 + t], (int)P0[a.max_ctx + p0 + t]) : make_int2(0, 0);
+  __syncthreads();
+  if (!umma::bar_wait(&bar, 0)) atomicExch(c.err, 4);
+  int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+#pragma unroll 4
+  for (int u = 0; u < 8; ++u) {
+    const int lp = warp + 8 * u;
+    if (lp < n) {
+      const int4 v4 = *reinterpret_cast<const int4*>(vpage + lp * kHeadDim + 4 * lane);
+      const int2 p = pr[lp];
+      const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        a0[e] = mad_wide(p.x, vv[e], a0[e]);
+        a1[e] = mad_wide(p.y, vv[e], a1[e]);
+      }
+    }
+  }
+  // the page is consumed: its buffer takes the cross-warp sums [8][2][128]
+  __syncthreads();
+  int64_t* part = reinterpret_cast<int64_t*>(vpage);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    part[(warp * 2 + 0) * kHeadDim + 4 * lane + e] = a0[e];
+    part[(warp * 2 + 1) * kHeadDim + 4 * lane + e] = a1[e];
+  }
+  __syncthreads();
+  const int hh = t >> 7, d = t & (kHeadDim - 1);
+  int64_t acc = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) acc += part[(w * 2 + hh) * kHeadDim + d];
+  int64_t* Oh = a.O + ((size_t)m * kQHeads + 2 * h + hh) * kHeadDim;
+  atomicAdd(reinterpret_cast<unsigned long long*>(Oh + d), (unsigned long long)acc);
+  __threadfence();
+  __syncthreads();
+  if (t == 0) {
+    unsigned* cnt = a.cnt_v + m * kKvHeads + h;
+    last = atomicAdd(cnt, 1u) == (unsigned)nch - 1;
+    if (last) *cnt = 0;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int64_t sum = ld_cg64(Oh + d);
+  Oh[d] = 0;
+  write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * h + hh) * kHeadDim + d, sat24(sum >> 16));
+}
+
+// Attention for one (KV head, sequence): q/k head RMSNorm + RoPE, KV append,
+// exact two-pass LUT softmax for the two query heads of the group; writes the
+// output and its limbs (the o_proj B matrix).  256 threads.  K, then V, of the
+// earlier positions stream through a 2-slot ring of 32-position chunks (16 KB
+// bulk copies, contiguous inside a KV page); the current position's K/V row
+// is taken from shared memory.  The score maxima are kept while the scores
+// are made, so the softmax is one pass over the (shared-memory) scores.
+// Used when the batch has enough (KV head, sequence) pairs to fill the GPU;
+// small batches and long contexts use the split-KV kernels above.
+constexpr int kAttnChunk = 32;
+constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
+constexpr int kAttnRing = 2;
+
+__global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
                                                             const int32_t* __restrict__ cos_tab,
                                                             const int32_t* __restrict__ sin_tab,
@@ -180,14 +451,15 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
   int32_t* ring = reinterpret_cast<int32_t*>(attn_smem);                            // [3][32][128]
   int64_t* sc = reinterpret_cast<int64_t*>(attn_smem + kAttnRing * kAttnChunkBytes);  // [2][ctx]
   __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v
-  __shared__ uint64_t probtab[2][kExpLut];
-  __shared__ int64_t red[32];
+  __shared__ uint32_t probtab[2][kExpLut];
+  __shared__ int64_t red[2][8];
   __shared__ uint64_t bars[kAttnRing];
   const int kv = blockIdx.x, m = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   grid_dep_wait();
   grid_dep_launch();
-  const int pos = c.pos0[m * 4];
+  attn_stamp(c, layer, m, kv, 0);
+  const int pos = c.pos0[4 * m];
   if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
   const KvView kvv = c.slots[m].kv;
@@ -215,21 +487,23 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
   if (warp < 3) {
     const int row = warp < 2 ? (2 * kv + warp) * kHeadDim : kQRows + kv * kHeadDim;
     const int4 x = *reinterpret_cast<const int4*>(raw + row + 4 * lane);
-    const int32_t xs[4] = {x.x, x.y, x.z, x.w};
+    const int4 cs = *reinterpret_cast<const int4*>(cos_tab + pos * kHeadDim + 4 * lane);
+    const int4 sn = *reinterpret_cast<const int4*>(sin_tab + pos * kHeadDim + 4 * lane);
+    const int4 gm = *reinterpret_cast<const int4*>((warp < 2 ? g_q : g_k) + 4 * lane);
+    const int32_t xs[4] = {x.x, x.y, x.z, x.w}, cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+    const int32_t gv[4] = {gm.x, gm.y, gm.z, gm.w};
     int64_t ss = 0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ss += (int64_t)xs[e] * xs[e];
+    for (int e = 0; e < 4; ++e) ss = mad_wide(xs[e], xs[e], ss);
     ss = warp_sum_i64(ss);
     const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
-    const int32_t* g = warp < 2 ? g_q : g_k;
     int32_t o[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int d = 4 * lane + e;
-      const int32_t n = norm_apply(xs[e], inv, g[d], kHeadNorm);
+      const int32_t n = norm_apply(xs[e], inv, gv[e], kHeadNorm);
       const int32_t partner = __shfl_xor_sync(0xFFFFFFFFu, n, 16);
       const int64_t rot = lane < 16 ? -(int64_t)partner : (int64_t)partner;
-      o[e] = sat24(((int64_t)n * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
+      o[e] = sat24(((int64_t)n * cv[e] + rot * sv[e]) >> 15);
     }
     const int4 o4 = make_int4(o[0], o[1], o[2], o[3]);
     *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
@@ -240,9 +514,11 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
     reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
   }
   __syncthreads();
+  attn_stamp(c, layer, m, kv, 1);
   bool ok = true;
   // scores: chunk of 32 positions, 4 per warp, 8 lanes per position; lane
   // `sub` holds dims 4 (sub + 8 j) .. +3, j = 0..3
+  int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
   {
     const int sub = lane & 7, quad = lane >> 3;
     int32_t q0[16], q1[16];
@@ -275,29 +551,66 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
         s0 += shfl_xor_i64(s0, msk);
         s1 += shfl_xor_i64(s1, msk);
       }
-      if (sub == 0 && p < ctx) {
-        sc[p] = scale_score(s0, kScoreScale);
-        sc[ctx + p] = scale_score(s1, kScoreScale);
+      if (p < ctx) {
+        const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
+        if (sub == 0) {
+          sc[p] = v0;
+          sc[ctx + p] = v1;
+        }
+        mx0 = v0 > mx0 ? v0 : mx0;
+        mx1 = v1 > mx1 ? v1 : mx1;
       }
       __syncthreads();  // slot i % 3 is free again
       if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
     }
   }
-#pragma unroll 1
-  for (int h = 0; h < 2; ++h) {
-    int64_t* s = sc + h * ctx;
-    int64_t mx = INT64_MIN;
-    for (int p = t; p < ctx; p += blockDim.x) mx = s[p] > mx ? s[p] : mx;
-    mx = block_max_i64(mx, red);
-    int64_t sum = 0;
-    for (int p = t; p < ctx; p += blockDim.x) {
-      const int ix = lut_index(mx, s[p]);
-      s[p] = ix;
-      sum += exp_lut[ix];
-    }
-    sum = block_sum_i64(sum, red);
-    for (int i = t; i < kExpLut; i += blockDim.x)
-      probtab[h][i] = udiv_exact((uint64_t)exp_lut[i] << 16, (uint64_t)sum);
+  attn_stamp(c, layer, m, kv, 2);
+  // maxima of both heads (one block reduction)
+#pragma unroll
+  for (int msk = 8; msk < 32; msk <<= 1) {
+    const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
+    mx0 = o0 > mx0 ? o0 : mx0;
+    mx1 = o1 > mx1 ? o1 : mx1;
+  }
+  if (lane == 0) {
+    red[0][warp] = mx0;
+    red[1][warp] = mx1;
+  }
+  __syncthreads();
+  mx0 = red[0][0];
+  mx1 = red[1][0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) {
+    mx0 = red[0][w] > mx0 ? red[0][w] : mx0;
+    mx1 = red[1][w] > mx1 ? red[1][w] : mx1;
+  }
+  // LUT indices and exp sums of both heads (one block reduction)
+  int64_t sum0 = 0, sum1 = 0;
+  for (int p = t; p < ctx; p += blockDim.x) {
+    const int i0 = lut_index(mx0, sc[p]), i1 = lut_index(mx1, sc[ctx + p]);
+    sc[p] = i0;
+    sc[ctx + p] = i1;
+    sum0 += exp_lut[i0];
+    sum1 += exp_lut[i1];
+  }
+  sum0 = warp_sum_i64(sum0);
+  sum1 = warp_sum_i64(sum1);
+  __syncthreads();  // red reused
+  if (lane == 0) {
+    red[0][warp] = sum0;
+    red[1][warp] = sum1;
+  }
+  __syncthreads();
+  sum0 = 0;
+  sum1 = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    sum0 += red[0][w];
+    sum1 += red[1][w];
+  }
+  for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
+    const int h = i >= kExpLut, e = i - h * kExpLut;
+    probtab[h][e] = (uint32_t)udiv_exact((uint64_t)exp_lut[e] << 16, (uint64_t)(h ? sum1 : sum0));
   }
   __syncthreads();
   // per-position probabilities of both heads, packed over the index array
@@ -307,6 +620,7 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
     prs[p] = make_int2((int)probtab[0][i0], (int)probtab[1][i1]);
   }
   __syncthreads();
+  attn_stamp(c, layer, m, kv, 3);
   // values: thread (warp, lane) accumulates dims 4 lane .. +3 of the chunk's
   // positions warp, warp + 8, warp + 16, warp + 24 for both heads
   int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
@@ -332,6 +646,7 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
     __syncthreads();
     if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
   }
+  attn_stamp(c, layer, m, kv, 4);
   if (!ok) atomicExch(c.err, 4);
   // the ring is idle now: reuse it for the cross-warp sums [8][2][128]
   int64_t* part = reinterpret_cast<int64_t*>(attn_smem);
@@ -346,10 +661,9 @@ __global__ void __launch_bounds__(256, 3) batch_attn_kernel(BatchCtx c, int laye
     int64_t acc = 0;
 #pragma unroll
     for (int w = 0; w < 8; ++w) acc += part[(w * 2 + h) * kHeadDim + d];
-    const int32_t o = sat24(acc >> 16);
-    const int k = (2 * kv + h) * kHeadDim + d;
-    write_limbs(c.bt2, c.SP, 2 * kHidden, m, k, o);
+    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
   }
+  attn_stamp(c, layer, m, kv, 5);
 }
 
 // ---------------------------------------------------------------------------
@@ -754,6 +1068,8 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
   return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
 }
 
+bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 2 * 148 && p.max_ctx <= 1024; }
+
 template <int SP>
 int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   auto mark = [&](int kind) -> int {
@@ -768,9 +1084,14 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   int rc;
 #define BMARK(k) \
   if ((rc = mark(k))) return rc
-  const BatchCtx c{p.slots, p.S,   p.SP,      p.qkv_raw, p.bt1,  p.bt2,     p.bt3,
-                   p.lm_from, p.err, p.pos0, p.hidden0, p.post0, p.max_ctx};
-  const size_t attn_smem = (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8;
+  const BatchCtx c{p.slots, p.S,    p.SP,      p.qkv_raw, p.bt1,   p.bt2,     p.bt3,
+                   p.lm_from, p.err, p.pos0, p.hidden0, p.post0, p.max_ctx, p.trace};
+  const AttnScratch as{p.att_S, p.att_P, p.att_M, p.att_O, p.att_cnt_s, p.att_cnt_v, p.max_ctx};
+  const dim3 attn_grid((unsigned)((p.max_ctx + kPage - 1) / kPage), kKvHeads, (unsigned)p.S);
+  // enough (KV head, sequence) pairs to fill the GPU in one wave: one CTA per
+  // pair; otherwise split each pair's context over pages
+  const bool one_cta_per_head = attn_one_cta_per_head(p);
+  const size_t ring_smem = (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8;
   BMARK(-1);
   BQ(launch_pdl(batch_embed_kernel, dim3(p.S), dim3(256), 0, s, c, p.emb, p.semb));
   BMARK(kBkEmbed);
@@ -781,8 +1102,14 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
                                   nullptr, s)));
     BMARK(kBkQkv);
-    BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), attn_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
-                  p.sin_tab, p.exp_lut));
+    if (one_cta_per_head) {
+      BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
+                    p.sin_tab, p.exp_lut));
+    } else {
+      BQ(launch_pdl(batch_attn_scores_kernel, attn_grid, dim3(256), 0, s, c, as, l, w.g_q, w.g_k, p.cos_tab,
+                    p.sin_tab, p.exp_lut));
+      BQ(launch_pdl(batch_attn_values_kernel, attn_grid, dim3(256), 0, s, c, as, l));
+    }
     BMARK(kBkAttn);
     BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s)));
     BMARK(kBkO);
@@ -817,8 +1144,9 @@ int setup_t(const BatchPlan& p) {
   if ((rc = set_smem<SP, kGemmQkv>()) || (rc = set_smem<SP, kGemmO>()) || (rc = set_smem<SP, kGemmGu>()) ||
       (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
     return rc;
-  BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
+  if (attn_one_cta_per_head(p))
+    BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
   return Q4GPU_OK;
 }
 

@@ -63,6 +63,14 @@ struct BatchPlan {
   const int32_t* pos0;   // position of sequence m at pos0[4 m]
   int32_t* hidden0;      // [S, 1024]
   int32_t* post0;        // [S, 1024]
+  // split-KV attention scratch (re-armed by the kernels after each use)
+  int64_t* att_S;        // [64, 16, max_ctx] scaled scores
+  uint32_t* att_P;       // [64, 16, max_ctx] probabilities
+  int64_t* att_M;        // [64, 16] maxima (INT64_MIN when armed)
+  int64_t* att_O;        // [64, 16, 128] value sums (0 when armed)
+  unsigned* att_cnt_s;   // [64, 8]
+  unsigned* att_cnt_v;   // [64, 8]
+  unsigned long long* trace;  // optional attention timeline, [layers, S, 8, 8] (nullptr = off)
 };
 
 }  // namespace q4

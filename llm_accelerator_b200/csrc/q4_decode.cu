@@ -14,6 +14,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <climits>
 #include <cmath>
 #include <map>
 #include <memory>
@@ -480,7 +481,12 @@ struct q4gpu_model {
   ArgBestD* b_lm_part = nullptr;
   int32_t* b_io = nullptr;   // device [64][2] inputs, then [64][4] outputs
   int32_t* h_bio = nullptr;  // pinned mirror of b_io
-  int* b_err = nullptr;      // set by a batched GEMM whose pipeline wait ran out
+  int* b_err = nullptr;      // set by a batched kernel whose pipeline wait ran out
+  int64_t* b_att_S = nullptr;  // split-KV attention scratch
+  uint32_t* b_att_P = nullptr;
+  int64_t* b_att_M = nullptr;
+  int64_t* b_att_O = nullptr;
+  unsigned* b_att_cnt = nullptr;  // [2][64][8]
   CUtensorMap b_mlm{};       // TMA map of b_emb8
   BatchLayerW b_layers[kMaxLayers]{};
   bool b_stale = true;  // int8 copies out of date with the Q4 weights
@@ -834,6 +840,16 @@ int batch_prepare(q4gpu_model* m) {
     if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
     if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
     if ((rc = m->alloc(&m->b_err, 4))) return rc;
+    const size_t sp = (size_t)kBatchSeqMax * kQHeads * m->cfg.max_context;
+    if ((rc = m->alloc(&m->b_att_S, sp))) return rc;
+    if ((rc = m->alloc(&m->b_att_P, sp))) return rc;
+    if ((rc = m->alloc(&m->b_att_M, (size_t)kBatchSeqMax * kQHeads))) return rc;
+    if ((rc = m->alloc(&m->b_att_O, (size_t)kBatchSeqMax * kQHeads * kHeadDim))) return rc;
+    if ((rc = m->alloc(&m->b_att_cnt, (size_t)2 * kBatchSeqMax * kKvHeads))) return rc;
+    {
+      std::vector<int64_t> armed((size_t)kBatchSeqMax * kQHeads, INT64_MIN);
+      Q4_CUDA(cudaMemcpy(m->b_att_M, armed.data(), armed.size() * 8, cudaMemcpyHostToDevice));
+    }
     Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
     for (int l = 0; l < L; ++l) {
       int8_t* w = m->b_w8 + kB8Layer * l;
@@ -903,6 +919,12 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.pos0 = m->slots[first].pos;
   p.hidden0 = m->slots[first].hidden;
   p.post0 = m->slots[first].post;
+  p.att_S = m->b_att_S;
+  p.att_P = m->b_att_P;
+  p.att_M = m->b_att_M;
+  p.att_O = m->b_att_O;
+  p.att_cnt_s = m->b_att_cnt;
+  p.att_cnt_v = m->b_att_cnt + kBatchSeqMax * kKvHeads;
   p.mlm = m->b_mlm;
   const uint64_t nrows = (uint64_t)q4gpu_batch_limb_rows(p.SP);
   const uint32_t box = (uint32_t)q4gpu_batch_box_rows(p.SP);
@@ -1618,6 +1640,27 @@ int q4gpu_batch_time_kernels(q4gpu_model* m, int32_t first_slot, int32_t n_seq, 
     ms_per_launch[k] = cnt[k] ? tot[k] / cnt[k] : 0.0;
     launches_per_step[k] = cnt[k] / reps;
   }
+  return batch_check_error(m);
+}
+
+int q4gpu_batch_trace_attention(q4gpu_model* m, int32_t first_slot, int32_t n_seq, uint64_t* stamps,
+                                int64_t n_stamps) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  const int64_t need = (int64_t)m->cfg.n_layers * n_seq * kKvHeads * 8;
+  if (!stamps || n_stamps != need) return q4gpu_fail(Q4GPU_ERR_ARG, "trace needs %lld stamps", (long long)need);
+  cudaGraphExec_t g;  // makes the buffers, maps and ones rows ready
+  if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
+  auto pp = std::make_unique<BatchPlan>();
+  if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
+  unsigned long long* dev = nullptr;
+  Q4_CUDA(cudaMalloc(&dev, (size_t)need * 8));
+  pp->trace = dev;
+  bool ok = cudaMemsetAsync(dev, 0, (size_t)need * 8, m->stream) == cudaSuccess &&
+            q4gpu_enqueue_batch_step(*pp, m->stream) == Q4GPU_OK && cudaStreamSynchronize(m->stream) == cudaSuccess &&
+            cudaMemcpy(stamps, dev, (size_t)need * 8, cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(dev);
+  if (!ok) return q4gpu_fail(Q4GPU_ERR_CUDA, "attention trace step failed");
   return batch_check_error(m);
 }
 
