@@ -361,13 +361,19 @@ int q4gpu_batch_set_position(q4gpu_model *m, int32_t first_slot, int32_t n_seq, 
 int q4gpu_batch_time_kernels(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t reps,
                              double *ms_per_launch, int32_t *launches_per_step);
 
-/* Runs one batched step (advancing the positions) with the one-CTA-per-head
- * attention kernel writing %globaltimer stamps (ns) at its phase boundaries:
- * stamps[((layer * n_seq + m) * 8 + kv_head) * 8 + k], k = 0 start, 1 q/k
- * ready, 2 scores done, 3 probabilities ready, 4 values done, 5 end (zeros
- * where the split-KV kernels ran instead).  n_stamps = layers * n_seq * 64. */
-int q4gpu_batch_trace_attention(q4gpu_model *m, int32_t first_slot, int32_t n_seq, uint64_t *stamps,
-                                int64_t n_stamps);
+/* Runs one batched step (advancing the positions) with timelines on
+ * (%globaltimer ns; either array may be NULL):
+ * attn_stamps[((layer * n_seq + m) * 8 + kv_head) * 8 + k] from the
+ * one-CTA-per-head attention kernel, k = 0 start, 1 q/k ready, 2 scores done,
+ * 3 probabilities ready, 4 values done, 5 end (zeros where the split-KV kernels
+ * ran); n_attn = layers * n_seq * 64.
+ * gemm_stamps[((4 * layer + g) * 1200 + cta) * 8 + k] for GEMM g = qkv, o_proj,
+ * gate/up, down (the LM head at 4 * layers), cta = split * tiles + tile, k = 0
+ * entry, 1 set-up done, 2 dependency released, 3 first accumulator ready,
+ * 4 last scale group folded, 5 partial sums exchanged, 6 epilogue done;
+ * n_gemm = (4 * layers + 1) * 1200 * 8. */
+int q4gpu_batch_trace(q4gpu_model *m, int32_t first_slot, int32_t n_seq, uint64_t *attn_stamps,
+                      int64_t n_attn, uint64_t *gemm_stamps, int64_t n_gemm);
 
 /* One batched step with host buffers: sequence i of the range takes
  * token_ids[i] at positions[i] and returns the argmax (and its Q26 score,

@@ -100,7 +100,7 @@ SIGNATURES = {
     "q4gpu_batch_set_position": (C.c_int, [P, I32, I32, I32, I32]),
     "q4gpu_batch_run_step": (C.c_int, [P, I32, I32, P, P, P, P]),
     "q4gpu_batch_time_kernels": (C.c_int, [P, I32, I32, I32, P, P]),
-    "q4gpu_batch_trace_attention": (C.c_int, [P, I32, I32, P, C.c_int64]),
+    "q4gpu_batch_trace": (C.c_int, [P, I32, I32, P, C.c_int64, P, C.c_int64]),
     "q4gpu_model_read_hidden": (C.c_int, [P, C.c_size_t, P]),
     "q4gpu_model_read_kv": (C.c_int, [P, C.c_size_t, I32, I32, I32, P]),
     "q4gpu_model_write_hidden": (C.c_int, [P, C.c_size_t, P]),

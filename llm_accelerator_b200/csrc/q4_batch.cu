@@ -709,7 +709,19 @@ struct UGemm {
   int kt_per_split;        // 128-wide K tiles each CTA of a cluster covers
   const int32_t* sig_lut;
   ArgBestD* partial;       // LM head: [tiles, 64]
+  unsigned long long* trace;  // optional: [CTA][8] %globaltimer stamps of this launch (nullptr = off)
 };
+
+// GEMM timeline points: 0 entry, 1 set-up done, 2 dependency released (TMA
+// warp), 3 first accumulator ready, 4 last group folded, 5 partial sums
+// exchanged, 6 epilogue done (epilogue warp 2 records 3-4, thread 0 the rest)
+__device__ __forceinline__ void gemm_stamp(const UGemm& g, int k) {
+  if (g.trace) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + k] = t;
+  }
+}
 
 template <int SP, int KIND>
 __global__ void __launch_bounds__(kUThreads, 1)
@@ -733,6 +745,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   const int row0 = tile * 128;
   const int G = g.K / 64;
 
+  if (threadIdx.x == 0) gemm_stamp(g, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < kUStages; ++s) {
       umma::bar_init(full + s, 1);
@@ -752,6 +765,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) gemm_stamp(g, 1);
   // every CTA is resident now: the next kernel may launch and run its
   // prologue; it waits (griddepcontrol.wait) for this grid to complete
   grid_dep_launch();
@@ -770,6 +784,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         umma::tma_load(sm + kt * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + kt);
       }
       grid_dep_wait();
+      gemm_stamp(g, 2);
       for (int kt = 0; kt < pre; ++kt)
         umma::tma_load(sm + kt * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, 0, full + kt);
       for (int kt = pre; kt < nkt && !*abort_flag; ++kt) {
@@ -842,6 +857,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
           break;
         }
         umma::fence_after_sync();
+        if (kt == 0 && h == 0 && warp == 2 && lane == 0) gemm_stamp(g, 3);
         int32_t d0[C::Q], d1[C::Q], d2[C::Q], w1[1];
         const uint32_t ta = lane_base + (uint32_t)(h * C::BUF + q * C::Q);
         umma::tmem_ld_any<C::Q>(ta, d0);
@@ -862,6 +878,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         }
       }
     }
+    if (warp == 2 && lane == 0) gemm_stamp(g, 4);
     // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
     // so each owner holds matching rows of both 64-row halves (gate and up)
     const int rows_per = 64 / splits;
@@ -884,6 +901,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
     umma::cluster_sync();
   else
     __syncthreads();
+  if (threadIdx.x == 0) gemm_stamp(g, 5);
 
   // final epilogue over the rows this CTA owns
   const int rows_per = 64 / splits, nl = 128 / splits;
@@ -957,6 +975,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   }
   umma::fence_before_sync();
   __syncthreads();
+  if (threadIdx.x == 0) gemm_stamp(g, 6);
   if (warp == 1) {
     umma::fence_after_sync();
     umma::tmem_dealloc(tmem, C::TCOLS);
@@ -1062,13 +1081,14 @@ constexpr int kSplitQkv = 4, kSplitO = 8, kSplitGu = 2, kSplitDown = 8;
 
 template <int SP, int KIND>
 cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const BatchCtx& c, const uint16_t* scales,
-                        int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s) {
-  UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial};
+                        int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s,
+                        unsigned long long* trace = nullptr) {
+  UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial, trace};
   const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)splits);
   return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
 }
 
-bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 2 * 148 && p.max_ctx <= 1024; }
+bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
 
 template <int SP>
 int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
@@ -1082,6 +1102,10 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     return Q4GPU_OK;
   };
   int rc;
+  // GEMM launch i records into its own slice of the trace (kGemmTraceCtas CTAs x 8 stamps)
+  auto gtrace = [&](int i) -> unsigned long long* {
+    return p.gemm_trace ? p.gemm_trace + (size_t)i * kGemmTraceCtas * 8 : nullptr;
+  };
 #define BMARK(k) \
   if ((rc = mark(k))) return rc
   const BatchCtx c{p.slots, p.S,    p.SP,      p.qkv_raw, p.bt1,   p.bt2,     p.bt3,
@@ -1100,7 +1124,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in));
     BMARK(kBkNorm);
     BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
-                                  nullptr, s)));
+                                  nullptr, s, gtrace(4 * l + 0))));
     BMARK(kBkQkv);
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
@@ -1111,18 +1135,22 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
       BQ(launch_pdl(batch_attn_values_kernel, attn_grid, dim3(256), 0, s, c, as, l));
     }
     BMARK(kBkAttn);
-    BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s)));
+    BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s,
+                                gtrace(4 * l + 1))));
     BMARK(kBkO);
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post));
     BMARK(kBkNorm);
-    BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s)));
+    BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s,
+                                 gtrace(4 * l + 2))));
     BMARK(kBkGu);
-    BQ((launch_gemm<SP, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr, s)));
+    BQ((launch_gemm<SP, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr, s,
+                                   gtrace(4 * l + 3))));
     BMARK(kBkDown);
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final));
   BMARK(kBkNorm);
-  BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s)));
+  BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s,
+                               gtrace(4 * p.n_layers))));
   BMARK(kBkLm);
   BQ(launch_pdl(batch_argmax_kernel, dim3(p.S), dim3(256), 0, s, c, (const ArgBestD*)p.lm_partial,
                 (p.vocab + 127) / 128));

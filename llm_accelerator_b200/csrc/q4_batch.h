@@ -71,7 +71,10 @@ struct BatchPlan {
   unsigned* att_cnt_s;   // [64, 8]
   unsigned* att_cnt_v;   // [64, 8]
   unsigned long long* trace;  // optional attention timeline, [layers, S, 8, 8] (nullptr = off)
+  unsigned long long* gemm_trace;  // optional GEMM timeline, [4 layers + 1, kGemmTraceCtas, 8]
 };
+
+constexpr int kGemmTraceCtas = 1200;  // CTAs one GEMM launch can record (the LM head has 1187)
 
 }  // namespace q4
 

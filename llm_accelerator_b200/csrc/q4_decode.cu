@@ -1643,24 +1643,30 @@ int q4gpu_batch_time_kernels(q4gpu_model* m, int32_t first_slot, int32_t n_seq, 
   return batch_check_error(m);
 }
 
-int q4gpu_batch_trace_attention(q4gpu_model* m, int32_t first_slot, int32_t n_seq, uint64_t* stamps,
-                                int64_t n_stamps) {
+int q4gpu_batch_trace(q4gpu_model* m, int32_t first_slot, int32_t n_seq, uint64_t* attn_stamps, int64_t n_attn,
+                      uint64_t* gemm_stamps, int64_t n_gemm) {
   int rc = batch_range_ok(m, first_slot, n_seq);
   if (rc) return rc;
-  const int64_t need = (int64_t)m->cfg.n_layers * n_seq * kKvHeads * 8;
-  if (!stamps || n_stamps != need) return q4gpu_fail(Q4GPU_ERR_ARG, "trace needs %lld stamps", (long long)need);
+  const int64_t need_a = (int64_t)m->cfg.n_layers * n_seq * kKvHeads * 8;
+  const int64_t need_g = (int64_t)(4 * m->cfg.n_layers + 1) * kGemmTraceCtas * 8;
+  if ((attn_stamps && n_attn != need_a) || (gemm_stamps && n_gemm != need_g))
+    return q4gpu_fail(Q4GPU_ERR_ARG, "trace needs %lld attention and %lld GEMM stamps", (long long)need_a,
+                      (long long)need_g);
   cudaGraphExec_t g;  // makes the buffers, maps and ones rows ready
   if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
   auto pp = std::make_unique<BatchPlan>();
   if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
   unsigned long long* dev = nullptr;
-  Q4_CUDA(cudaMalloc(&dev, (size_t)need * 8));
-  pp->trace = dev;
-  bool ok = cudaMemsetAsync(dev, 0, (size_t)need * 8, m->stream) == cudaSuccess &&
+  Q4_CUDA(cudaMalloc(&dev, (size_t)(need_a + need_g) * 8));
+  pp->trace = attn_stamps ? dev : nullptr;
+  pp->gemm_trace = gemm_stamps ? dev + need_a : nullptr;
+  bool ok = cudaMemsetAsync(dev, 0, (size_t)(need_a + need_g) * 8, m->stream) == cudaSuccess &&
             q4gpu_enqueue_batch_step(*pp, m->stream) == Q4GPU_OK && cudaStreamSynchronize(m->stream) == cudaSuccess &&
-            cudaMemcpy(stamps, dev, (size_t)need * 8, cudaMemcpyDeviceToHost) == cudaSuccess;
+            (!attn_stamps || cudaMemcpy(attn_stamps, dev, (size_t)need_a * 8, cudaMemcpyDeviceToHost) == cudaSuccess) &&
+            (!gemm_stamps ||
+             cudaMemcpy(gemm_stamps, dev + need_a, (size_t)need_g * 8, cudaMemcpyDeviceToHost) == cudaSuccess);
   cudaFree(dev);
-  if (!ok) return q4gpu_fail(Q4GPU_ERR_CUDA, "attention trace step failed");
+  if (!ok) return q4gpu_fail(Q4GPU_ERR_CUDA, "traced batch step failed");
   return batch_check_error(m);
 }
 

@@ -194,12 +194,14 @@ class Q4Model:
                       "q4gpu_batch_time_kernels")
         return {name: (float(ms[i]), int(cnt[i])) for i, name in enumerate(_native.BATCH_KERNEL_KINDS) if cnt[i]}
 
-    def batch_trace_attention(self, n_seq: int, first_slot: int = 0) -> np.ndarray:
-        """One batched step; [layers, n_seq, 8 kv heads, 8] attention phase stamps (ns)."""
-        st = np.zeros((self.n_layers, n_seq, 8, 8), dtype=np.uint64)
-        _native.check(self.lib.q4gpu_batch_trace_attention(self.handle, first_slot, n_seq, _ptr(st), st.size),
-                      "q4gpu_batch_trace_attention")
-        return st
+    def batch_trace(self, n_seq: int, first_slot: int = 0) -> tuple[np.ndarray, np.ndarray]:
+        """One batched step with timelines on: attention stamps [layers, n_seq, 8, 8] and
+        GEMM stamps [4 * layers + 1, 1200, 8] (ns; see q4gpu_batch_trace)."""
+        at = np.zeros((self.n_layers, n_seq, 8, 8), dtype=np.uint64)
+        gt = np.zeros((4 * self.n_layers + 1, 1200, 8), dtype=np.uint64)
+        _native.check(self.lib.q4gpu_batch_trace(self.handle, first_slot, n_seq, _ptr(at), at.size, _ptr(gt), gt.size),
+                      "q4gpu_batch_trace")
+        return at, gt
 
     # -- device-resident decode loop ----------------------------------------
     def decode_steps(self, n_steps: int, slot: int = 0) -> None:
