@@ -337,6 +337,31 @@ int q4gpu_decode_batch(q4gpu_model *m, int32_t n_seq, const uint32_t *prompts,
  * advances the position.  Asynchronous on the model stream. */
 int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t n_steps);
 
+/* Vocabulary-sharded LM head (no reference counterpart; the reference scans the
+ * whole vocabulary on one device).  A step becomes: q4gpu_batch_forward_hidden
+ * on each rank's own sequences -> exchange of the final vectors -> each rank's
+ * q4gpu_lm_head_shard over its rows for all vectors -> exchange of the
+ * (score, row) winners, reduced with highest score / lowest row ->
+ * q4gpu_batch_commit on each rank's sequences.  All asynchronous on the model
+ * stream; pointers are device memory.
+ *
+ * forward_hidden: embedding, all layers and the final RMSNorm of one position
+ * for slots [first_slot, first_slot + n_seq); final_act receives the normed
+ * Q12.12 vectors (int32 [n_seq, 1024]).  Positions do not advance. */
+int q4gpu_batch_forward_hidden(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t *final_act);
+
+/* LM head over vocabulary rows [row_begin, row_end) for n_act (1..64) vectors
+ * acts (int32 [n_act, 1024], 16-byte aligned): best_score / best_row (int64
+ * [n_act]) get each vector's highest Q26 logit in the shard and its global row
+ * (lowest row on ties). */
+int q4gpu_lm_head_shard(q4gpu_model *m, const int32_t *acts, int32_t n_act, int32_t row_begin,
+                        int32_t row_end, int64_t *best_score, int64_t *best_row);
+
+/* Store tokens[i] (with scores[i]; int64 [n_seq]) at position + 1 of slot
+ * first_slot + i (from its lm_from on) and advance the positions. */
+int q4gpu_batch_commit(q4gpu_model *m, int32_t first_slot, int32_t n_seq, const int64_t *tokens,
+                       const int64_t *scores);
+
 /* Every slot of the range to `position`; lm_from (>= 0) sets the position
  * from which argmax tokens are stored, -1 keeps it.  Stream-ordered. */
 int q4gpu_batch_set_position(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t position,

@@ -142,7 +142,8 @@ __global__ void batch_embed_kernel(BatchCtx c, const uint8_t* __restrict__ W, co
 // RMSNorm of one sequence's hidden (which 0) or post (which 1) vector -> limbs
 // in bt1.  256 threads x 4 consecutive elements.
 __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int which,
-                                                               const int32_t* __restrict__ gamma) {
+                                                               const int32_t* __restrict__ gamma,
+                                                               int32_t* __restrict__ out_act) {
   __shared__ int64_t red[32];
   grid_dep_wait();
   grid_dep_launch();
@@ -152,10 +153,13 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
   int64_t ss = (int64_t)x.x * x.x + (int64_t)x.y * x.y + (int64_t)x.z * x.z + (int64_t)x.w * x.w;
   ss = block_sum_i64(ss, red);
   const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
-  const uint32_t u0 = (uint32_t)(norm_apply(x.x, inv, gm.x, kHiddenNorm) + (1 << 23));
-  const uint32_t u1 = (uint32_t)(norm_apply(x.y, inv, gm.y, kHiddenNorm) + (1 << 23));
-  const uint32_t u2 = (uint32_t)(norm_apply(x.z, inv, gm.z, kHiddenNorm) + (1 << 23));
-  const uint32_t u3 = (uint32_t)(norm_apply(x.w, inv, gm.w, kHiddenNorm) + (1 << 23));
+  const int4 nv = make_int4(norm_apply(x.x, inv, gm.x, kHiddenNorm), norm_apply(x.y, inv, gm.y, kHiddenNorm),
+                            norm_apply(x.z, inv, gm.z, kHiddenNorm), norm_apply(x.w, inv, gm.w, kHiddenNorm));
+  if (out_act) *reinterpret_cast<int4*>(out_act + (size_t)m * kHidden + k) = nv;
+  const uint32_t u0 = (uint32_t)(nv.x + (1 << 23));
+  const uint32_t u1 = (uint32_t)(nv.y + (1 << 23));
+  const uint32_t u2 = (uint32_t)(nv.z + (1 << 23));
+  const uint32_t u3 = (uint32_t)(nv.w + (1 << 23));
 #pragma unroll
   for (int limb = 0; limb < 3; ++limb) {
     const int sh = 8 * limb;
@@ -803,7 +807,9 @@ __global__ void __launch_bounds__(kUThreads, 1)
   } else if (warp == 1) {
     grid_dep_wait();
     if (lane != 0) {
-      for (int m = lane - 1; m < SP; m += 31) live[m] = m < g.c.S && g.c.pos0[4 * m] < g.c.max_ctx;
+      // which sequences take part in this step (the epilogues that update slot state)
+      if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
+        for (int m = lane - 1; m < SP; m += 31) live[m] = m < g.c.S && g.c.pos0[4 * m] < g.c.max_ctx;
     } else {
       for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
         const int s = kt % kUStages;
@@ -982,6 +988,82 @@ __global__ void __launch_bounds__(kUThreads, 1)
   }
 }
 
+// Limb matrix of already-normed Q12.12 vectors (the input of a vocab-shard LM
+// head): acts [n][1024] -> bt rows limb * SP + m.
+__global__ void __launch_bounds__(256) act_limbs_kernel(const int32_t* __restrict__ acts, uint8_t* __restrict__ bt,
+                                                        int SP) {
+  const int m = blockIdx.x, k = 4 * threadIdx.x;
+  const int4 v = *reinterpret_cast<const int4*>(acts + (size_t)m * kHidden + k);
+  const uint32_t u[4] = {(uint32_t)(v.x + (1 << 23)), (uint32_t)(v.y + (1 << 23)), (uint32_t)(v.z + (1 << 23)),
+                         (uint32_t)(v.w + (1 << 23))};
+#pragma unroll
+  for (int limb = 0; limb < 3; ++limb) {
+    const int sh = 8 * limb;
+    const uint32_t word = ((u[0] >> sh) & 0xFF) | (((u[1] >> sh) & 0xFF) << 8) | (((u[2] >> sh) & 0xFF) << 16) |
+                          (((u[3] >> sh) & 0xFF) << 24);
+    *reinterpret_cast<uint32_t*>(bt + (size_t)(limb * SP + m) * kHidden + k) = word;
+  }
+}
+
+// Best (score, row) of vector blockIdx.x over the LM-head tile partials of a
+// vocabulary shard starting at row_offset; the reference's rule (highest
+// score, lowest row on ties).
+__global__ void shard_argmax_kernel(const ArgBestD* __restrict__ partial, int n_parts, int row_offset,
+                                    int64_t* __restrict__ best_score, int64_t* __restrict__ best_row) {
+  __shared__ int64_t ss[32];
+  __shared__ int32_t si[32];
+  const int m = blockIdx.x;
+  int64_t bs = INT64_MIN;
+  int32_t bi = INT32_MAX;
+  for (int i = threadIdx.x; i < n_parts; i += blockDim.x) {
+    const ArgBestD o = partial[(size_t)i * kBatchSeqMax + m];
+    if (o.score > bs || (o.score == bs && o.idx < bi)) {
+      bs = o.score;
+      bi = o.idx;
+    }
+  }
+#pragma unroll
+  for (int msk = 16; msk > 0; msk >>= 1) {
+    const int64_t os = shfl_xor_i64(bs, msk);
+    const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, msk);
+    if (os > bs || (os == bs && oi < bi)) {
+      bs = os;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    ss[warp] = bs;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+      if (ss[w] > bs || (ss[w] == bs && si[w] < bi)) {
+        bs = ss[w];
+        bi = si[w];
+      }
+    best_score[m] = bs;
+    best_row[m] = (int64_t)bi + row_offset;
+  }
+}
+
+// Chosen next tokens of sequences 0..S-1: stored at position + 1 (from
+// lm_from on) with their scores; positions advance.
+__global__ void batch_commit_kernel(BatchCtx c, const int64_t* __restrict__ tokens,
+                                    const int64_t* __restrict__ scores) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= c.S) return;
+  const SlotState& st = c.slots[m];
+  const int pos = *st.pos;
+  if (pos >= st.max_ctx) return;
+  if (pos + 1 >= c.lm_from[m]) {
+    st.tokens[pos + 1] = (int32_t)tokens[m];
+    st.scores[pos + 1] = scores[m];
+  }
+  *st.pos = pos + 1;
+}
+
 // Reduce the LM-head partials of sequence blockIdx.x; write the argmax where
 // the sequence has left its prompt, and advance its position.
 __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ partial, int n_parts) {
@@ -1121,7 +1203,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   BMARK(kBkEmbed);
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
-    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in));
+    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
     BMARK(kBkNorm);
     BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
                                   nullptr, s, gtrace(4 * l + 0))));
@@ -1138,7 +1220,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s,
                                 gtrace(4 * l + 1))));
     BMARK(kBkO);
-    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post));
+    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
     BMARK(kBkNorm);
     BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s,
                                  gtrace(4 * l + 2))));
@@ -1147,8 +1229,9 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
                                    gtrace(4 * l + 3))));
     BMARK(kBkDown);
   }
-  BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final));
+  BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final, p.final_act));
   BMARK(kBkNorm);
+  if (p.final_act) return Q4GPU_OK;  // hidden-only step: the LM head runs per vocabulary shard
   BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s,
                                gtrace(4 * p.n_layers))));
   BMARK(kBkLm);
@@ -1230,6 +1313,42 @@ int q4gpu_batch_box_rows(int SP) { return (3 * SP + kBatchOnes + 15) / 16 * 16; 
 int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s) {
   const int blocks = (int)std::min<int64_t>((n_bytes + 255) / 256, 148 * 32);
   expand_int4_kernel<<<blocks, 256, 0, s>>>(packed, n_bytes, out);
+  return q4gpu_check_launch();
+}
+
+template <int SP>
+int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
+  BatchCtx c{};
+  c.S = q.n_act;
+  c.SP = SP;
+  c.err = q.err;
+  act_limbs_kernel<<<q.n_act, 256, 0, s>>>(q.acts, q.bt, SP);
+  BQ(cudaGetLastError());
+  BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, kGemmLm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)UCfg<SP>::SMEM));
+  const int rows = q.row_end - q.row_begin;
+  BQ((launch_gemm<SP, kGemmLm>(q.amap, q.bmap, c, q.scales, rows, kHidden, 1, nullptr, q.partial, s)));
+  shard_argmax_kernel<<<q.n_act, 256, 0, s>>>(q.partial, (rows + 127) / 128, q.row_begin, q.best_score, q.best_row);
+  BQ(cudaGetLastError());
+  return Q4GPU_OK;
+}
+
+int q4gpu_enqueue_lm_shard(const LmShardPlan& q, cudaStream_t s) {
+  switch (q4gpu_batch_padded(q.n_act)) {
+    case 8: return lm_shard_t<8>(q, s);
+    case 16: return lm_shard_t<16>(q, s);
+    case 24: return lm_shard_t<24>(q, s);
+    case 32: return lm_shard_t<32>(q, s);
+    default: return lm_shard_t<64>(q, s);
+  }
+}
+
+int q4gpu_enqueue_batch_commit(const BatchPlan& p, const int64_t* tokens, const int64_t* scores, cudaStream_t s) {
+  BatchCtx c{};
+  c.slots = p.slots;
+  c.S = p.S;
+  c.lm_from = p.lm_from;
+  batch_commit_kernel<<<(p.S + 63) / 64, 64, 0, s>>>(c, tokens, scores);
   return q4gpu_check_launch();
 }
 

@@ -72,6 +72,22 @@ struct BatchPlan {
   unsigned* att_cnt_v;   // [64, 8]
   unsigned long long* trace;  // optional attention timeline, [layers, S, 8, 8] (nullptr = off)
   unsigned long long* gemm_trace;  // optional GEMM timeline, [4 layers + 1, kGemmTraceCtas, 8]
+  int32_t* final_act;    // hidden-only step when set: final-norm Q12.12 [S, 1024], no LM head / argmax
+};
+
+// LM head over one vocabulary shard [row_begin, row_end) for n_act vectors.
+struct LmShardPlan {
+  alignas(64) CUtensorMap amap;  // int8 embedding rows of the shard
+  CUtensorMap bmap;              // limbs of the vectors
+  const int32_t* acts;           // [n_act, 1024] Q12.12
+  int n_act;
+  int row_begin, row_end;
+  const uint16_t* scales;        // scales of the shard's first row
+  uint8_t* bt;                   // [3 SP + 8, 1024] limb matrix
+  ArgBestD* partial;             // [ceil(rows / 128), 64]
+  int64_t* best_score;           // [n_act]
+  int64_t* best_row;             // [n_act] global rows
+  int* err;
 };
 
 constexpr int kGemmTraceCtas = 1200;  // CTAs one GEMM launch can record (the LM head has 1187)
@@ -105,3 +121,6 @@ int q4gpu_batch_gather(const q4::SlotState* slots, int S, const int32_t* in, int
 // every sequence to `pos`; lm_from[m] = lm_value unless lm_value < 0
 int q4gpu_batch_set_positions(const q4::SlotState* slots, int S, int pos, int32_t* lm_from, int lm_value,
                               cudaStream_t s);
+int q4gpu_enqueue_lm_shard(const q4::LmShardPlan& q, cudaStream_t s);
+// tokens / scores: device int64 [S]; stores them at position + 1 and advances positions
+int q4gpu_enqueue_batch_commit(const q4::BatchPlan& p, const int64_t* tokens, const int64_t* scores, cudaStream_t s);

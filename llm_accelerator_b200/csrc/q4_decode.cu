@@ -491,7 +491,11 @@ struct q4gpu_model {
   BatchLayerW b_layers[kMaxLayers]{};
   bool b_stale = true;  // int8 copies out of date with the Q4 weights
   int b_ones_sp = 0;    // SP whose ones rows the B matrices hold
-  std::map<std::pair<int, int>, cudaGraphExec_t> b_graphs;  // (first slot, S)
+  std::map<std::tuple<int, int, int>, cudaGraphExec_t> b_graphs;  // (first slot, S, hidden-only)
+  int32_t* b_final_act = nullptr;   // [64, 1024] final-norm vectors of a hidden-only step
+  uint8_t* b_lm_bt = nullptr;       // limb matrix of a vocabulary-shard LM head
+  ArgBestD* b_lm_shard_part = nullptr;
+  int b_lm_ones_sp = 0;
 
   template <class T>
   int alloc(T** p, size_t count) {
@@ -840,6 +844,9 @@ int batch_prepare(q4gpu_model* m) {
     if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
     if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
     if ((rc = m->alloc(&m->b_err, 4))) return rc;
+    if ((rc = m->alloc(&m->b_final_act, (size_t)kBatchSeqMax * kHidden))) return rc;
+    if ((rc = m->alloc(&m->b_lm_bt, (size_t)kBtRows * kHidden))) return rc;
+    if ((rc = m->alloc(&m->b_lm_shard_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
     const size_t sp = (size_t)kBatchSeqMax * kQHeads * m->cfg.max_context;
     if ((rc = m->alloc(&m->b_att_S, sp))) return rc;
     if ((rc = m->alloc(&m->b_att_P, sp))) return rc;
@@ -949,7 +956,7 @@ int batch_check_error(q4gpu_model* m) {
 
 // Graph of one batched step over slots [first, first + S), with the B
 // matrices' ones rows set for its padded size.
-int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out) {
+int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out, bool hidden_only = false) {
   int rc = batch_prepare(m);
   if (rc) return rc;
   auto pp = std::make_unique<BatchPlan>();
@@ -961,7 +968,8 @@ int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out) {
     Q4_CUDA(cudaMemsetAsync(m->b_bt3 + (size_t)3 * p.SP * kInter, 1, (size_t)kBatchOnes * kInter, m->stream));
     m->b_ones_sp = p.SP;
   }
-  const auto key = std::make_pair(first, S);
+  if (hidden_only) p.final_act = m->b_final_act;
+  const auto key = std::make_tuple(first, S, hidden_only ? 1 : 0);
   auto it = m->b_graphs.find(key);
   if (it != m->b_graphs.end()) {
     *out = it->second;
@@ -1466,6 +1474,62 @@ int q4gpu_batch_steps(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t
   if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
   for (int i = 0; i < n_steps; ++i) Q4_CUDA(cudaGraphLaunch(g, m->stream));
   return Q4GPU_OK;
+}
+
+int q4gpu_batch_forward_hidden(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t* final_act) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (!final_act) return q4gpu_fail(Q4GPU_ERR_ARG, "null final_act");
+  cudaGraphExec_t g;
+  if ((rc = batch_graph(m, first_slot, n_seq, &g, true))) return rc;
+  Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  Q4_CUDA(cudaMemcpyAsync(final_act, m->b_final_act, (size_t)n_seq * kHidden * 4, cudaMemcpyDeviceToDevice,
+                          m->stream));
+  return Q4GPU_OK;
+}
+
+int q4gpu_lm_head_shard(q4gpu_model* m, const int32_t* acts, int32_t n_act, int32_t row_begin, int32_t row_end,
+                        int64_t* best_score, int64_t* best_row) {
+  if (!m || !acts || !best_score || !best_row) return q4gpu_fail(Q4GPU_ERR_ARG, "null argument");
+  if (n_act < 1 || n_act > kBatchSeqMax || row_begin < 0 || row_end <= row_begin || row_end > m->cfg.vocab)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad LM-head shard: %d vectors, rows [%d, %d)", n_act, row_begin, row_end);
+  if (((uintptr_t)acts) & 15) return q4gpu_fail(Q4GPU_ERR_ALIGN, "acts must be 16-byte aligned");
+  int rc = set_device(m);
+  if (rc) return rc;
+  if ((rc = batch_prepare(m))) return rc;
+  const int SP = q4gpu_batch_padded(n_act);
+  if (m->b_lm_ones_sp != SP) {
+    Q4_CUDA(cudaMemsetAsync(m->b_lm_bt + (size_t)3 * SP * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
+    m->b_lm_ones_sp = SP;
+  }
+  auto q = std::make_unique<LmShardPlan>();
+  q->acts = acts;
+  q->n_act = n_act;
+  q->row_begin = row_begin;
+  q->row_end = row_end;
+  q->scales = m->semb + (size_t)row_begin * (kHidden / kGroup);
+  q->bt = m->b_lm_bt;
+  q->partial = m->b_lm_shard_part;
+  q->best_score = best_score;
+  q->best_row = best_row;
+  q->err = m->b_err;
+  if ((rc = q4gpu_encode_u8_map(&q->amap, m->b_emb8 + (size_t)row_begin * kHidden, kHidden,
+                                (uint64_t)(row_end - row_begin), 128)) ||
+      (rc = q4gpu_encode_u8_map(&q->bmap, m->b_lm_bt, kHidden, (uint64_t)q4gpu_batch_limb_rows(SP),
+                                (uint32_t)q4gpu_batch_box_rows(SP))))
+    return rc;
+  return q4gpu_enqueue_lm_shard(*q, m->stream);
+}
+
+int q4gpu_batch_commit(q4gpu_model* m, int32_t first_slot, int32_t n_seq, const int64_t* tokens,
+                       const int64_t* scores) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (!tokens || !scores) return q4gpu_fail(Q4GPU_ERR_ARG, "null tokens/scores");
+  if ((rc = batch_prepare(m))) return rc;
+  auto pp = std::make_unique<BatchPlan>();
+  if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
+  return q4gpu_enqueue_batch_commit(*pp, tokens, scores, m->stream);
 }
 
 int q4gpu_batch_set_position(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t position, int32_t lm_from) {

@@ -184,6 +184,25 @@ class Q4Model:
                                                     _ptr(sc)), "q4gpu_batch_run_step")
         return out.astype(np.int64), sc
 
+    # -- vocabulary-sharded LM head -----------------------------------------
+    def batch_forward_hidden(self, n_seq: int, out, first_slot: int = 0) -> None:
+        """One position of slots [first_slot, first_slot + n_seq) up to the final RMSNorm;
+        `out`: int32 CUDA tensor [n_seq, 1024] receiving the normed vectors (async)."""
+        _native.check(self.lib.q4gpu_batch_forward_hidden(self.handle, first_slot, n_seq, out.data_ptr()),
+                      "q4gpu_batch_forward_hidden")
+
+    def lm_head_shard(self, acts, row_begin: int, row_end: int, best_score, best_row) -> None:
+        """LM head over vocabulary rows [row_begin, row_end) for acts (int32 CUDA [n, 1024]);
+        best_score / best_row: int64 CUDA [n] (async)."""
+        _native.check(self.lib.q4gpu_lm_head_shard(self.handle, acts.data_ptr(), acts.shape[0], row_begin, row_end,
+                                                   best_score.data_ptr(), best_row.data_ptr()),
+                      "q4gpu_lm_head_shard")
+
+    def batch_commit(self, tokens, scores, first_slot: int = 0) -> None:
+        """Store tokens / scores (int64 CUDA [n]) at each slot's position + 1 and advance (async)."""
+        _native.check(self.lib.q4gpu_batch_commit(self.handle, first_slot, tokens.shape[0], tokens.data_ptr(),
+                                                  scores.data_ptr()), "q4gpu_batch_commit")
+
     def batch_time_kernels(self, n_seq: int, reps: int = 2, first_slot: int = 0) -> dict[str, tuple[float, int]]:
         """Mean device ms per launch and launches per step of each batched kernel
         (kernels serialised by events; advances the positions by `reps`)."""

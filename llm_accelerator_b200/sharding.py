@@ -77,3 +77,60 @@ def max_over_ranks(x: float, device=None, group=None) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
     return float(t.item())
+
+
+def reduce_winners_device(scores, rows):
+    """Device-side twin of combine_argmax: scores / rows int64 tensors [shards, n]
+    -> (score, row) [n], highest score then lowest row, without a host round trip."""
+    import torch
+
+    best = scores.max(dim=0).values
+    big = torch.iinfo(torch.int64).max
+    row = torch.where(scores == best.unsqueeze(0), rows, torch.full_like(rows, big)).min(dim=0).values
+    return best, row
+
+
+class VocabShardedDecoder:
+    """Greedy decode steps with the tied LM head split over the ranks of a
+    process group (one GPU each).  Every rank decodes `n_local` sequences of
+    its own (slots 0..n_local-1 of `model`); per step the ranks exchange the
+    final normed vectors (all_gather), each scores its vocabulary shard for all
+    of them, and the (score, row) winners are exchanged and reduced with the
+    reference's rule.  The result equals an unsharded LM head bit for bit."""
+
+    def __init__(self, model, n_local: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.m, self.n, self.group = model, n_local, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.v0, self.v1 = vocab_shard(model.vocab, self.world, self.rank)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.stream = torch.cuda.ExternalStream(model.stream)
+        self.acts = torch.empty((n_local, 1024), dtype=torch.int32, device=dev)
+        self.all_acts = torch.empty((self.world * n_local, 1024), dtype=torch.int32, device=dev)
+        self.bs = torch.empty(self.world * n_local, dtype=torch.int64, device=dev)
+        self.br = torch.empty(self.world * n_local, dtype=torch.int64, device=dev)
+        self.win = torch.empty((self.world, 2, self.world * n_local), dtype=torch.int64, device=dev)
+
+    def step(self) -> None:
+        """One decode position for this rank's sequences (asynchronous on the model stream)."""
+        import torch
+        import torch.distributed as dist
+
+        with torch.cuda.stream(self.stream):
+            self.m.batch_forward_hidden(self.n, self.acts)
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.all_acts, self.acts, group=self.group)
+            else:
+                self.all_acts.copy_(self.acts)
+            self.m.lm_head_shard(self.all_acts, self.v0, self.v1, self.bs, self.br)
+            mine = torch.stack([self.bs, self.br])
+            if self.world > 1:
+                dist.all_gather_into_tensor(self.win, mine, group=self.group)
+            else:
+                self.win.copy_(mine.unsqueeze(0))
+            score, row = reduce_winners_device(self.win[:, 0, :], self.win[:, 1, :])
+            lo = self.rank * self.n
+            self.m.batch_commit(row[lo:lo + self.n].contiguous(), score[lo:lo + self.n].contiguous())
