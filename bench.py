@@ -417,6 +417,80 @@ def run_ours(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------
+# Config 5 (opt-in, --cfg5): 8 sequences with 8192-token prompts, decode at
+# context 8192..; the 8 sequences are split over the ranks and, for N > 1, the
+# LM head is vocabulary-sharded with an NCCL exchange of the (score, row)
+# winners.  Prints its own JSON line (rank 0).
+# ---------------------------------------------------------------------------
+CFG5_SEQS, CFG5_PROMPT, CFG5_GEN = 8, 8192, 512
+
+
+def run_cfg5(args, ws, rank, local):
+    import torch
+
+    from llm_accelerator_b200.model import Q4Model
+    from llm_accelerator_b200.sharding import VocabShardedDecoder, max_over_ranks, shard_range
+
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if CFG5_SEQS % ws:
+        raise SystemExit("config 5 needs a GPU count dividing 8")
+    a, b = shard_range(CFG5_SEQS, ws, rank)
+    n_local = b - a
+    prompts = [np.random.default_rng(50_000 + i).integers(0, VOCAB, CFG5_PROMPT).tolist() for i in range(a, b)]
+    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=CFG5_PROMPT + CFG5_GEN, max_seqs=n_local, device=local)
+    m.init_synthetic(seed=0)
+    stream = torch.cuda.ExternalStream(m.stream)
+    t0 = time.perf_counter()
+    m.decode_batch(prompts, 1)  # serial prefill; the first generated token of each sequence
+    prefill_s = max_over_ranks(time.perf_counter() - t0, device=torch.device("cuda", local))
+    steps = min(args.steps, CFG5_GEN - 1)
+    dec = VocabShardedDecoder(m, n_local) if ws > 1 else None
+
+    def run(n):
+        for _ in range(n):
+            if dec is not None:
+                dec.step()
+            else:
+                m.batch_steps(1, n_local)
+
+    run(min(args.warmup, 4))
+    m.batch_set_position(CFG5_PROMPT, n_local)
+    m.sync()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    run(steps)
+    e1.record(stream)
+    e1.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1), device=torch.device("cuda", local))
+    toks = m.read_tokens(CFG5_PROMPT, 4, slot=0)[0].tolist()
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/sec (config 5: batch 8, context 8192..)", "value": round(CFG5_SEQS * steps / (ms / 1000), 2),
+            "unit": UNIT, "n_gpus": ws, "steps": steps, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+            "scaling": "strong", "dtype": "int64", "data": "synthetic",
+            "config": {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (serial batched prefill), greedy "
+                                   "decode from position 8192", "sequences_per_gpu": n_local,
+                       "lm_head": f"vocabulary-sharded over {ws} GPUs, NCCL all_gather of vectors and (score, row) "
+                                  "winners" if ws > 1 else "full vocabulary on one GPU"},
+            "prefill_s": round(prefill_s, 2), "first_tokens_seq0": toks,
+        }
+        print(json.dumps(line), flush=True)
+    m.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -425,12 +499,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cfg5", action="store_true", help="run config 5 (long context, sharded LM head) instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     ws, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, ws, rank)
+    elif args.cfg5:
+        run_cfg5(args, ws, rank, local)
     else:
         run_ours(args, ws, rank, local)
 
