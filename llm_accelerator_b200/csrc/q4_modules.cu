@@ -2,6 +2,9 @@
 // reference's fixed-point decode path, exposed through the C ABI in
 // include/q4gpu.h so each stage can be checked bit-exactly on its own.
 // The decode-step kernels (q4_decode.cu) fuse these same stages.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "q4_gemv.cuh"
@@ -606,6 +609,422 @@ __global__ void __launch_bounds__(kGvThreads) gemv_stream_kernel(GemvArgs g) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Tensor-core Q4 GEMV (batch 1).  Weight rows stream into a ring of shared-
+// memory slots by TMA (producer warp); consumer warps take the row sums from
+// mma.sync m16n8k32 (u8 x u8 -> s32).
+//
+// A slot holds one unit: a block of up to 64 rows (four 16-row tiles) x 1024
+// columns as four 128-byte-wide boxes with the 128-byte swizzle (16-byte
+// chunk index XOR row % 8, so the eight rows one load instruction touches
+// sit in different banks), and the block's scales for those columns.  A
+// consumer warp claims one 16-row tile at a time from a shared counter (its
+// K / 1024 units), so faster warps take more tiles.
+//
+// MMA operands: A = 16 rows of biased nibbles u = w + 8; B = the six 4-bit
+// limbs n_j of c = a + 2^23 (columns 0..5) and a column of ones (column 6).
+// Thread t of a row holds packed words t and t + 4 of each 64-column group.
+// The group's first MMA takes their low nibbles as u with B = 16 n_j, the
+// second their high nibbles in place (16 u) with B = n_j, so both add 16 u n_j
+// and no shift is needed.  Per row and group the accumulator columns are
+// D_j = 16 P_j (P_j = sum u n_j) and D_6 = 16 U (U = sum u), and
+//   16 sum w * a = sum_j 16^j D_j - 2^23 D_6 - 128 sum(a).
+// Lane t holds columns 2t, 2t + 1 and forms x_t = D_2t + 16 D_2t+1, started
+// from the bias split -128 sum(a) = r - 2^23 Q' (0 <= r < 2^23): the MMA
+// accumulator starts at r in column 0 (lane 0) and at Q' in column 6 (lane 3).
+// Lane t accumulates x_t times the scale (exact int32 x exact int64) and the
+// tile's row sum is (acc_0 + 2^8 acc_1 + 2^16 acc_2 - 2^23 acc_3) / 16, an
+// exact division.
+constexpr int kMvWarps = 15;  // consumer warps; one more issues the copies (16 warps: 128 registers each)
+constexpr int kMvThreads = (kMvWarps + 1) * 32;
+constexpr int kMvBox = 64 * 128;                     // one 64-row x 128-byte box
+constexpr int kMvSlot = 4 * kMvBox + 64 * 32;        // 1024 columns of 64 rows + their scales
+
+template <int K>
+struct MvCfg {
+  static constexpr int KS = K / 1024;                // units per block
+  static constexpr int NS = K <= 2048 ? 6 : 5;       // ring slots
+  static constexpr size_t SMEM =
+      1024 + (size_t)NS * kMvSlot + (size_t)K * 8 + (size_t)(K / 16) * 4 + 2 * NS * 8 + NS * 4;  // ring, bf, bq, bars
+};
+
+// W and S as 3-D u8 tensors [count][rows][bytes]: 64- and 16-row boxes
+struct MvMaps {
+  CUtensorMap w64, w16, s64, s16;
+};
+
+__device__ __forceinline__ void mma_u8(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// first MMA of a group: the accumulator starts at {ci, 0, ci, 0}
+__device__ __forceinline__ void mma_u8_init(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1, int32_t ci) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(ci), "r"(0));
+}
+
+// Nibble masks and biases held in registers: a three-register LOP3 then
+// unpacks a word in one instruction (an immediate takes only one operand slot).
+struct MvMasks {
+  uint32_t mlo, blo, mhi, bhi;
+  __device__ __forceinline__ MvMasks() {
+    asm volatile("mov.b32 %0, 0x0F0F0F0F;" : "=r"(mlo));
+    asm volatile("mov.b32 %0, 0x08080808;" : "=r"(blo));
+    asm volatile("mov.b32 %0, 0xF0F0F0F0;" : "=r"(mhi));
+    asm volatile("mov.b32 %0, 0x80808080;" : "=r"(bhi));
+  }
+  __device__ __forceinline__ uint32_t lo(uint32_t v) const { return (v & mlo) ^ blo; }  // u
+  __device__ __forceinline__ uint32_t hi(uint32_t v) const { return (v & mhi) ^ bhi; }  // 16 u
+};
+
+__device__ __forceinline__ void mv_tma3(void* dst, const CUtensorMap* m, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"((uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"((uint32_t)__cvta_generic_to_shared(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mv_arrive_n(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(b)), "r"(n)
+               : "memory");
+}
+
+// bounded wait (about 0.2 s) until the producer has issued unit u into the slot
+__device__ __forceinline__ bool mv_wait_tag(volatile int* tag, int u) {
+  if (*tag == u) return true;
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(200);  // the unit is at least one slot turn away: leave the issue slots to working warps
+    if (*tag == u) return true;
+    if ((it & 255u) == 0) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (t - t0 > 200000000ull) return false;
+    }
+  }
+}
+
+// bounded wait (about 0.2 s) on an mbarrier phase; each try suspends the
+// thread in hardware (up to 0.1 ms) until the phase completes, so waiting
+// warps take no issue slots
+__device__ __forceinline__ bool mv_wait(uint64_t* b, unsigned parity) {
+  const uint32_t addr = (uint32_t)__cvta_generic_to_shared(b);
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(addr), "r"(parity), "r"(100000u)
+        : "memory");
+    if (ok) return true;
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > 200000000ull) return false;
+  }
+}
+
+__device__ __forceinline__ void mv_consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kMvWarps * 32) : "memory");
+}
+
+// B fragments and accumulator starts of K activations.  bf[G][lane] (g =
+// lane / 4, t = lane % 4) = {lo b0, lo b1, hi b0, hi b1}: lo b0 holds
+// 16 n_g(c) at columns 64 G + 8 t + {0, 2, 4, 6}, lo b1 the same + 32, hi b0
+// and b1 n_g(c) at those columns + 1 (g = 6: ones, 16 for lo; g = 7: zeros).
+// bq[G / 4][t][G % 4] = r (t = 0), Q' (t = 3), 0 otherwise, with
+// -128 sum(a) = r - 2^23 Q'.
+__device__ __forceinline__ uint32_t mv_limbs4(const int32_t (&v)[8], int h, int g, uint32_t mul) {
+  uint32_t r = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t c = (uint32_t)(v[2 * i + h] + (1 << 23));
+    const uint32_t n = g < 6 ? (c >> (4 * g)) & 15u : (g == 6 ? 1u : 0u);
+    r |= (n * mul) << (8 * i);
+  }
+  return r;
+}
+
+// One warp per group G and pass: lane (g, t) reads the 16 activations of its
+// fragment (two 8-column runs), and the quad g = 0 sums the group for bq.
+// nthreads is a multiple of 32, so each warp's lanes share one G.
+__device__ __forceinline__ void mv_stage_b(const int32_t* __restrict__ act, int K, uint4* bf, int32_t* bq, int tid,
+                                           int nthreads) {
+  for (int e = tid; e < K / 2; e += nthreads) {
+    const int G = e >> 5, gq = (e & 31) >> 2, t = e & 3;
+    const int4* a = reinterpret_cast<const int4*>(act + 64 * G + 8 * t);
+    const int4 p0 = a[0], p1 = a[1], p2 = a[8], p3 = a[9];
+    const int32_t lo[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    const int32_t hi[8] = {p2.x, p2.y, p2.z, p2.w, p3.x, p3.y, p3.z, p3.w};
+    bf[e] = make_uint4(mv_limbs4(lo, 0, gq, 16), mv_limbs4(hi, 0, gq, 16), mv_limbs4(lo, 1, gq, 1),
+                       mv_limbs4(hi, 1, gq, 1));
+    int64_t sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum += (int64_t)lo[i] + hi[i];
+    sum += shfl_xor_i64(sum, 1);
+    sum += shfl_xor_i64(sum, 2);
+    if (gq == 0) {
+      const int64_t nb = -128 * sum;  // |nb| <= 2^36
+      bq[((G >> 2) * 4 + t) * 4 + (G & 3)] =
+          t == 0 ? (int32_t)(nb & ((1 << 23) - 1)) : (t == 3 ? (int32_t)(-(nb >> 23)) : 0);
+    }
+  }
+}
+
+// The CTA's tiles [t0, t1) form blocks of up to four consecutive tiles of one
+// matrix: in matrix m they start at max(t0, m * tpm) + 4 k.
+struct MvBlocks {
+  int t0, t1, tpm, m0, nb0, bpm;
+  __device__ MvBlocks(int a, int b, int tiles_per_matrix, int count) : t0(a), t1(b), tpm(tiles_per_matrix) {
+    m0 = count == 1 ? 0 : t0 / tpm;
+    const int e0 = (m0 + 1) * tpm;
+    nb0 = ((t1 < e0 ? t1 : e0) - t0 + 3) / 4;
+    bpm = (tpm + 3) / 4;
+  }
+  // matrix, block ordinal and index inside the block of tile t
+  __device__ void locate(int t, int count, int& m, int& ord, int& j) const {
+    m = count == 1 ? 0 : t / tpm;
+    const int sm = m == m0 ? t0 : m * tpm;
+    const int k = (t - sm) >> 2;
+    j = t - sm - 4 * k;
+    ord = m == m0 ? k : nb0 + (m - m0 - 1) * bpm + k;
+  }
+};
+
+template <int K, int MODE>
+__global__ void __launch_bounds__(kMvThreads, 1) gemv_mma_kernel(const __grid_constant__ MvMaps maps, GemvArgs g) {
+  using C = MvCfg<K>;
+  constexpr int KS = C::KS, NS = C::NS;
+  extern __shared__ __align__(1024) unsigned char mv_smem_raw[];
+  // the 128-byte swizzle repeats every 1024 bytes: slots start on that boundary
+  uint8_t* slots = reinterpret_cast<uint8_t*>(((uintptr_t)mv_smem_raw + 1023) & ~(uintptr_t)1023);
+  uint4* bf = reinterpret_cast<uint4*>(slots + NS * kMvSlot);
+  int32_t* bq = reinterpret_cast<int32_t*>(bf + K / 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(bq + K / 16);
+  uint64_t* empty = full + NS;
+  // tag[s]: the unit last issued into slot s.  A consumer that claimed a tile
+  // far ahead waits for its unit's tag before the parity wait, so the parity
+  // it waits on is never two phases away.
+  volatile int* tag = reinterpret_cast<volatile int*>(empty + NS);
+  __shared__ ArgBest wbest[kMvWarps + 1];
+  __shared__ bool last;
+  __shared__ int next_tile;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tg = lane & 3;
+  const int tpm = (g.rows + 15) >> 4;  // 16-row tiles per matrix (count * tpm < 2^31)
+  const int64_t total = (int64_t)tpm * g.count;
+  const int t0 = (int)(total * blockIdx.x / gridDim.x), t1 = (int)(total * (blockIdx.x + 1) / gridDim.x);
+  const int ntile = t1 - t0;
+  const MvBlocks blocks(t0, t1, tpm, g.count);
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      gv_bar_init(full + s);
+      gv_bar_init_n(empty + s, 4);
+      tag[s] = -1;
+    }
+    next_tile = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  int64_t best_s = INT64_MIN;
+  int32_t best_i = INT32_MAX;
+  if (warp == kMvWarps) {
+    // producer: the blocks in order, one unit (1024 columns) at a time
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.w64)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.s64)) : "memory");
+      int ord = 0;
+      bool ok = true;
+      for (int tb = t0; ok && tb < t1; ++ord) {
+        const int m = g.count == 1 ? 0 : tb / tpm;
+        const int me = (m + 1) * tpm;
+        const int n = min(4, (t1 < me ? t1 : me) - tb);
+        const int row0 = (tb - m * tpm) * 16;
+        for (int c = 0; c < KS; ++c) {
+          const int u = ord * KS + c, s = u % NS;
+          if (u >= NS && !mv_wait(empty + s, ((u / NS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = slots + s * kMvSlot;
+          tag[s] = u;
+          if (n == 4) {
+            gv_expect(full + s, kMvSlot);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) mv_tma3(dst + b * kMvBox, &maps.w64, c * 512 + b * 128, row0, m, full + s);
+            mv_tma3(dst + 4 * kMvBox, &maps.s64, c * 32, row0, m, full + s);
+          } else {
+            gv_expect(full + s, (uint32_t)n * (4 * 2048 + 512));
+            for (int j = 0; j < n; ++j) {
+#pragma unroll
+              for (int b = 0; b < 4; ++b)
+                mv_tma3(dst + b * kMvBox + j * 2048, &maps.w16, c * 512 + b * 128, row0 + 16 * j, m, full + s);
+              mv_tma3(dst + 4 * kMvBox + j * 512, &maps.s16, c * 32, row0 + 16 * j, m, full + s);
+            }
+            mv_arrive_n(empty + s, 4 - n);  // the block's missing tiles
+          }
+        }
+        tb += n;
+      }
+    }
+  } else {
+    mv_stage_b(g.act, K, bf, bq, tid, kMvWarps * 32);
+    mv_consumer_sync();
+    const MvMasks mk;
+    // swizzled byte offsets of words t (ox0) and t + 4 (ox1) of group G, G % 4 = G4, in row gid of a box
+    uint32_t ox0[4], ox1[4];
+#pragma unroll
+    for (int G4 = 0; G4 < 4; ++G4) {
+      ox0[G4] = (uint32_t)(gid * 128 + (((2 * G4) ^ gid) << 4) + 4 * tg);
+      ox1[G4] = (uint32_t)(gid * 128 + (((2 * G4 + 1) ^ gid) << 4) + 4 * tg);
+    }
+    for (;;) {
+      int ti = 0;
+      if (lane == 0) ti = atomicAdd(&next_tile, 1);
+      ti = __shfl_sync(0xFFFFFFFFu, ti, 0);
+      if (ti >= ntile) break;
+      const int tile = t0 + ti;
+      int m, ord, j;
+      blocks.locate(tile, g.count, m, ord, j);
+      const int row0 = (tile - m * tpm) * 16;
+      int64_t acc0 = 0, acc1 = 0;  // rows row0 + gid, row0 + gid + 8
+#pragma unroll 1
+      for (int c = 0; c < KS; ++c) {
+        const int u = ord * KS + c, s = u % NS;
+        const bool ok = mv_wait_tag(tag + s, u) && mv_wait(full + s, (u / NS) & 1);
+        // this tile's words and scales into registers, then the slot goes back
+        const uint8_t* st = slots + s * kMvSlot + j * 2048;
+        const uint8_t* sc = slots + s * kMvSlot + 4 * kMvBox + (16 * j + gid) * 32;
+        uint32_t xw[16][4];
+        uint4 sv[4];
+#pragma unroll
+        for (int GG = 0; GG < 16; ++GG) {
+          const uint8_t* bx = st + (GG >> 2) * kMvBox;
+          xw[GG][0] = *reinterpret_cast<const uint32_t*>(bx + ox0[GG & 3]);
+          xw[GG][1] = *reinterpret_cast<const uint32_t*>(bx + ox1[GG & 3]);
+          xw[GG][2] = *reinterpret_cast<const uint32_t*>(bx + 1024 + ox0[GG & 3]);
+          xw[GG][3] = *reinterpret_cast<const uint32_t*>(bx + 1024 + ox1[GG & 3]);
+        }
+        sv[0] = *reinterpret_cast<const uint4*>(sc);
+        sv[1] = *reinterpret_cast<const uint4*>(sc + 16);
+        sv[2] = *reinterpret_cast<const uint4*>(sc + 8 * 32);
+        sv[3] = *reinterpret_cast<const uint4*>(sc + 8 * 32 + 16);
+        __syncwarp();
+        if (lane == 0) gv_arrive(empty + s);
+        if (!ok) continue;
+        const uint4* bsm = bf + c * 512 + lane;
+        const int4* bqs = reinterpret_cast<const int4*>(bq + c * 64) + tg;
+#pragma unroll
+        for (int GG = 0; GG < 16; ++GG) {
+          const uint4 b = bsm[GG * 32];
+          const int4 q4 = bqs[(GG >> 2) * 4];
+          const int32_t q = (GG & 3) == 0 ? q4.x : (GG & 3) == 1 ? q4.y : (GG & 3) == 2 ? q4.z : q4.w;
+          int32_t d[4];
+          mma_u8_init(d, mk.lo(xw[GG][0]), mk.lo(xw[GG][2]), mk.lo(xw[GG][1]), mk.lo(xw[GG][3]), b.x, b.y, q);
+          mma_u8(d, mk.hi(xw[GG][0]), mk.hi(xw[GG][2]), mk.hi(xw[GG][1]), mk.hi(xw[GG][3]), b.z, b.w);
+          const uint32_t w0 = reinterpret_cast<const uint32_t*>(&sv[GG >> 3])[(GG >> 1) & 3];
+          const uint32_t w1 = reinterpret_cast<const uint32_t*>(&sv[2 + (GG >> 3)])[(GG >> 1) & 3];
+          const int32_t sa = (int32_t)((GG & 1) ? (w0 >> 16) : (w0 & 0xFFFFu));
+          const int32_t sb = (int32_t)((GG & 1) ? (w1 >> 16) : (w1 & 0xFFFFu));
+          acc0 = mad_wide(d[0] + 16 * d[1], sa, acc0);
+          acc1 = mad_wide(d[2] + 16 * d[3], sb, acc1);
+        }
+      }
+      // lane weights 1, 2^8, 2^16, -2^23; the sum over the quad is 16 x the row sum
+      acc0 <<= 8 * tg - (tg == 3);
+      acc1 <<= 8 * tg - (tg == 3);
+      if (tg == 3) {
+        acc0 = -acc0;
+        acc1 = -acc1;
+      }
+      acc0 += shfl_xor_i64(acc0, 1);
+      acc1 += shfl_xor_i64(acc1, 1);
+      acc0 += shfl_xor_i64(acc0, 2);
+      acc1 += shfl_xor_i64(acc1, 2);
+      if (tg == 0) {
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int row = row0 + gid + 8 * r;
+          const int64_t v = (r ? acc1 : acc0) >> 4;
+          if (row < g.rows) {
+            if constexpr (MODE == 0) {
+              g.out[m * g.out_stride + row] = v;
+              if (g.out12) g.out12[m * g.out_stride + row] = sat24c(v >> 14, g.sat);
+            } else {
+              if (g.out) g.out[row] = v;
+              if (better(v, row, best_s, best_i)) {
+                best_s = v;
+                best_i = row;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  if constexpr (MODE == 1) {
+    auto warp_best = [&](int64_t& bs, int32_t& bi) {
+#pragma unroll
+      for (int msk = 1; msk < 32; msk <<= 1) {
+        const int64_t os = shfl_xor_i64(bs, msk);
+        const int32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, msk);
+        if (better(os, oi, bs, bi)) {
+          bs = os;
+          bi = oi;
+        }
+      }
+    };
+    __syncwarp();
+    warp_best(best_s, best_i);
+    if (lane == 0) wbest[warp] = ArgBest{best_s, best_i, 0};
+    __syncthreads();
+    if (tid == 0) {
+      ArgBest b = wbest[0];
+      for (int w = 1; w <= kMvWarps; ++w)
+        if (better(wbest[w].score, wbest[w].idx, b.score, b.idx)) b = wbest[w];
+      g.partial[blockIdx.x] = b;
+      __threadfence();
+      const unsigned int done = atomicAdd(g.counter, 1u);
+      last = (done == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (last) {  // the last CTA reduces all partials, every thread a strided share
+      __threadfence();
+      int64_t bs = INT64_MIN;
+      int32_t bi = INT32_MAX;
+      for (int i = tid; i < (int)gridDim.x; i += kMvThreads) {
+        const int64_t cs = *((volatile int64_t*)&g.partial[i].score);
+        const int32_t ci = *((volatile int32_t*)&g.partial[i].idx);
+        if (better(cs, ci, bs, bi)) {
+          bs = cs;
+          bi = ci;
+        }
+      }
+      warp_best(bs, bi);
+      __syncthreads();
+      if (lane == 0) wbest[warp] = ArgBest{bs, bi, 0};
+      __syncthreads();
+      if (tid == 0) {
+        ArgBest b = wbest[0];
+        for (int w = 1; w <= kMvWarps; ++w)
+          if (better(wbest[w].score, wbest[w].idx, b.score, b.idx)) b = wbest[w];
+        *g.out_tok = b.idx;
+        *g.out_score = b.score;
+        *g.counter = 0;  // ready for the next launch
+      }
+    }
+  }
+}
+
 // Scratch of q4gpu_lm_head_argmax_noalloc: the per-CTA best (score, row) of
 // the LM-head grid and its completion counter, 444 * 16 + 16 = 7120 bytes,
 // resident on every device that loads this library.
@@ -651,8 +1070,88 @@ int q4gpu_quantize_q4(const float* w, int64_t rows, int32_t cols, uint8_t* packe
 
 namespace {
 
+// 3-D u8 tensor map [count][rows][inner bytes] with a box of box_inner x box_rows x 1
+int mv_encode(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t count, uint64_t row_stride,
+              uint64_t mat_stride, uint32_t box_inner, uint32_t box_rows, bool swizzle) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !encode)
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  }
+  const cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)count};
+  const cuuint64_t strides[2] = {(cuuint64_t)row_stride, (cuuint64_t)mat_stride};
+  const cuuint32_t box[3] = {box_inner, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q4GPU_OK;
+}
+
+// Tensor maps of one GEMV operand set, cached by its pointers and shape (a
+// model's GEMVs repeat every token).
+int mv_maps(const GemvArgs& g, int K, MvMaps* out) {
+  struct Entry {
+    const void* W;
+    const void* S;
+    int K, rows, count;
+    int64_t ws, ss;
+    MvMaps maps;
+  };
+  static Entry cache[32];
+  static int n_used = 0, next = 0;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n_used; ++i) {
+    const Entry& e = cache[i];
+    if (e.W == g.W && e.S == g.S && e.K == K && e.rows == g.rows && e.count == g.count && e.ws == g.w_stride &&
+        e.ss == g.s_stride) {
+      *out = e.maps;
+      return Q4GPU_OK;
+    }
+  }
+  Entry e{g.W, g.S, K, g.rows, g.count, g.w_stride, g.s_stride, {}};
+  const uint64_t wrow = (uint64_t)K / 2, srow = (uint64_t)K / 32;
+  const uint64_t wmat = g.count > 1 ? (uint64_t)g.w_stride : wrow * g.rows;
+  const uint64_t smat = g.count > 1 ? (uint64_t)g.s_stride * 2 : srow * g.rows;
+  int rc = mv_encode(&e.maps.w64, g.W, wrow, g.rows, g.count, wrow, wmat, 128, 64, true);
+  if (rc == Q4GPU_OK) rc = mv_encode(&e.maps.w16, g.W, wrow, g.rows, g.count, wrow, wmat, 128, 16, true);
+  if (rc == Q4GPU_OK) rc = mv_encode(&e.maps.s64, g.S, srow, g.rows, g.count, srow, smat, 32, 64, false);
+  if (rc == Q4GPU_OK) rc = mv_encode(&e.maps.s16, g.S, srow, g.rows, g.count, srow, smat, 32, 16, false);
+  if (rc != Q4GPU_OK) return rc;
+  cache[next] = e;
+  next = (next + 1) % 32;
+  if (n_used < 32) ++n_used;
+  *out = e.maps;
+  return Q4GPU_OK;
+}
+
+template <int K, int MODE>
+int mv_launch(const GemvArgs& g, int grid_cap, cudaStream_t s) {
+  using C = MvCfg<K>;
+  static_assert(C::SMEM <= 227 * 1024 - 512, "GEMV slot ring too large");
+  MvMaps maps;
+  const int rc = mv_maps(g, K, &maps);
+  if (rc != Q4GPU_OK) return rc;
+  const cudaError_t e =
+      cudaFuncSetAttribute(gemv_mma_kernel<K, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "GEMV shared memory: %s", cudaGetErrorString(e));
+  const int64_t tiles = (int64_t)((g.rows + 15) / 16) * g.count;
+  const int grid = (int)std::min<int64_t>(tiles, std::min(grid_cap, 148));
+  gemv_mma_kernel<K, MODE><<<grid, kMvThreads, C::SMEM, s>>>(maps, g);
+  return q4gpu_check_launch();
+}
+
 template <int K, int MODE>
 int gv_launch(const GemvArgs& g, int grid_cap, cudaStream_t s) {
+  // tensor-core path when the scale rows can travel by bulk copy (16-byte aligned)
+  if (((uintptr_t)g.S & 15) == 0 && ((g.s_stride * 2) & 15) == 0 && (g.act_stride == 0 || g.count == 1))
+    return mv_launch<K, MODE>(g, grid_cap, s);
   using C = GvCfg<K>;
   static_assert(C::SMEM < 227 * 1024, "GEMV stage ring too large");
   // scales ride with the weights when every stage's scale rows start 16-byte aligned
