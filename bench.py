@@ -270,6 +270,81 @@ def batch1_secondary(device: int, steps: int) -> dict:
                     "d2h_bytes_per_step": 12, "api": "q4gpu_run_token (qot_session_runner_fn)"}}
 
 
+def gemv_secondary(device: int, peak_gbs: float) -> dict:
+    """Config 1: the 3072 x 1024 Q4 GEMV over 160 distinct rotated weight copies
+    (~267 MB, above L2), one q4gpu_gemv_q26_strided launch with the shared
+    activation; plus the same 160 GEMVs as separate launches in one CUDA graph
+    and one LM-head-sized (151936 x 1024) GEMV.  Packed bytes and scales are
+    uniform random: the kernels' time does not depend on the values."""
+    import torch
+
+    from llm_accelerator_b200 import _native
+
+    lib = _native.load()
+    dev = torch.device("cuda", device)
+    g = torch.Generator(device=dev).manual_seed(1)
+    K, R, N, RB = 1024, 3072, 160, 151936
+    act = torch.randint(-(1 << 23), 1 << 23, (K,), dtype=torch.int32, device=dev, generator=g)
+    W = torch.randint(0, 256, (N, R, K // 2), dtype=torch.uint8, device=dev, generator=g)
+    S = torch.randint(0, 1 << 15, (N, R, K // 64), dtype=torch.int16, device=dev, generator=g)
+    out = torch.empty((N, R), dtype=torch.int64, device=dev)
+    o12 = torch.empty((N, R), dtype=torch.int32, device=dev)
+    per = R * K // 2 + R * K // 32 + K * 4 + R * 12  # packed + scales + activation + outputs (8 + 4 B)
+    st = torch.cuda.Stream(device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed(fn, reps):
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                fn()
+            e0.record(st)
+            for _ in range(reps):
+                fn()
+            e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def strided():
+        _native.check(lib.q4gpu_gemv_q26_strided(act.data_ptr(), 0, K, W.data_ptr(), R * K // 2, S.data_ptr(),
+                                                 R * K // 64, R, N, out.data_ptr(), o12.data_ptr(), R, None,
+                                                 st.cuda_stream), "q4gpu_gemv_q26_strided")
+
+    def separate():
+        for i in range(N):
+            _native.check(lib.q4gpu_gemv_q26(act.data_ptr(), K, W[i].data_ptr(), S[i].data_ptr(), R,
+                                             out[i].data_ptr(), o12[i].data_ptr(), None, st.cuda_stream),
+                          "q4gpu_gemv_q26")
+
+    ms_strided = timed(strided, 10)
+    with torch.cuda.stream(st):
+        separate()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            separate()
+    ms_graph = timed(graph.replay, 5)
+    del graph, W, S, out, o12
+    Wb = torch.randint(0, 256, (RB, K // 2), dtype=torch.uint8, device=dev, generator=g)
+    Sb = torch.randint(0, 1 << 15, (RB, K // 64), dtype=torch.int16, device=dev, generator=g)
+    ob = torch.empty(RB, dtype=torch.int64, device=dev)
+
+    def big():
+        _native.check(lib.q4gpu_gemv_q26(act.data_ptr(), K, Wb.data_ptr(), Sb.data_ptr(), RB, ob.data_ptr(), None,
+                                         None, st.cuda_stream), "q4gpu_gemv_q26")
+
+    ms_big = timed(big, 20)
+    big_bytes = RB * (K // 2 + K // 32) + K * 4 + RB * 8
+    gbs = N * per / ms_strided / 1e6
+    return {"workload": "cfg1: 3072x1024 Q4 GEMV x 160 distinct weight copies (267 MB > L2), shared activation, "
+                        "one q4gpu_gemv_q26_strided launch (tensor-core mma.sync u8 path)",
+            "bytes_per_gemv": per, "us_per_gemv": round(ms_strided * 1000 / N, 3), "gbs": round(gbs, 1),
+            "frac": round(gbs / peak_gbs, 4), "peak": peak_gbs,
+            "separate_launches_in_graph": {"us_per_gemv": round(ms_graph * 1000 / N, 3),
+                                           "gbs": round(N * per / ms_graph / 1e6, 1)},
+            "lm_head_sized": {"rows": RB, "us": round(ms_big * 1000, 2),
+                              "gbs": round(big_bytes / ms_big / 1e6, 1),
+                              "frac": round(big_bytes / ms_big / 1e6 / peak_gbs, 4)}}
+
+
 def run_ours(args, ws, rank, local):
     import torch
 
@@ -400,6 +475,7 @@ def run_ours(args, ws, rank, local):
         }
         if ws == 1:
             line["batch1"] = batch1_secondary(local, 128)
+            line["gemv"] = gemv_secondary(local, peaks["hbm_gbs"])
             if not args.no_cpu_baseline:
                 c = cpu_decode(args.cpu_steps, 2)
                 line["cpu_baseline"] = {

@@ -96,11 +96,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity, int* err
   return false;
 }
 
-// Grid-wide barrier: arrivals count in bar[0]; the last CTA to arrive resets
-// it and bumps the generation word bar[1], which the others poll (acquire).
-// `hook` runs on warp 1 between arrival and release (work that needs no
-// result of this stage, e.g. L2 prefetches).  Returns false when the wait ran
-// out or another CTA reported an error; the caller then returns.
+// Grid-wide barrier on one monotonic arrival counter bar[0] (zeroed by the
+// host before each launch): barrier i of a launch releases when the counter
+// reaches (i + 1) x gridDim.x.  The arrival is one release add, the wait an
+// acquire poll of the same word, so the release costs a single trip to L2.
 struct Barrier {
   unsigned* bar;
   int* err;
@@ -120,25 +119,17 @@ __device__ __forceinline__ bool grid_sync(Barrier& b, Hook hook = Hook()) {
   const unsigned idx = b.index++;
   if (threadIdx.x == 0) {
     if (b.trace && (int)idx < b.trace_cap) atomicMax(&b.trace[2 * idx], globaltimer());
-    const unsigned gen = ld_acquire_u32(b.bar + 1);
-    __threadfence();
-    const unsigned arrived = atomicAdd(b.bar, 1u);
+    const unsigned target = (idx + 1) * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(b.bar) : "memory");
     int ok = 1;
-    if (arrived == gridDim.x - 1) {
-      atomicExch(b.bar, 0u);
-      __threadfence();
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(b.bar + 1), "r"(gen + 1) : "memory");
-    } else {
-      uint32_t it = 0;
-      while (ld_acquire_u32(b.bar + 1) == gen) {
-        if (++it > kSpinLimit || ((it & 255) == 0 && *((volatile int*)b.err) != 0)) {
-          atomicCAS(b.err, 0, 1);
-          ok = 0;
-          break;
-        }
+    uint32_t it = 0;
+    while (ld_acquire_u32(b.bar) < target) {
+      if (++it > kSpinLimit || ((it & 255) == 0 && *((volatile int*)b.err) != 0)) {
+        atomicCAS(b.err, 0, 1);
+        ok = 0;
+        break;
       }
     }
-    __threadfence();
     if (b.trace && blockIdx.x == 0 && (int)idx < b.trace_cap) b.trace[2 * idx + 1] = globaltimer();
     *b.s_flag = ok;
   } else if (threadIdx.x == 32) {

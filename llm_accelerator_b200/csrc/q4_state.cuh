@@ -81,7 +81,7 @@ struct PersistArgs {
   const int32_t* sig_lut;
   int32_t* qkv;        // [4096] raw projections of the current layer
   ArgBestD* lm_part;   // [gridDim.x]
-  unsigned int* bar;   // [2]: arrivals, generation
+  unsigned int* bar;   // [2]: grid barrier arrival counter (monotonic within a launch), spare
   int* err;            // 0 = ok
   int n_steps;
   int lm_from;         // the LM head runs at positions p with p + 1 >= lm_from
