@@ -155,13 +155,25 @@ __device__ __forceinline__ void stage_limbs_par(const int32_t* act, int K, uint3
   if (c < K / 8 && (c & 3) == 0) bias8[c >> 2] = 8 * s;
 }
 
+// This thread's two hidden-size gamma values (elements t and t + 512), loaded
+// at a stage's start so the read overlaps the stage's input read.
+struct Gamma2 {
+  int32_t v[2];
+  __device__ __forceinline__ explicit Gamma2(const int32_t* __restrict__ g) {
+    v[0] = __ldg(g + threadIdx.x);
+    v[1] = __ldg(g + threadIdx.x + kPThreads);
+  }
+};
+static_assert(2 * kPThreads == kHidden, "two hidden elements per thread");
+
 // Hidden-size RMSNorm of act[] in place (Q14.10 -> Q12.12).
-__device__ __forceinline__ void hidden_norm_inplace(int32_t* act, const int32_t* __restrict__ gamma, int64_t* red) {
-  int64_t ss = 0;
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) ss += (int64_t)act[i] * act[i];
-  ss = block_sum_i64(ss, red);
+__device__ __forceinline__ void hidden_norm_inplace(int32_t* act, const Gamma2& gamma, int64_t* red) {
+  const int i0 = threadIdx.x, i1 = threadIdx.x + kPThreads;
+  const int32_t x0 = act[i0], x1 = act[i1];
+  const int64_t ss = block_sum_i64((int64_t)x0 * x0 + (int64_t)x1 * x1, red);
   const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) act[i] = norm_apply(act[i], inv, gamma[i], kHiddenNorm);
+  act[i0] = norm_apply(x0, inv, gamma.v[0], kHiddenNorm);
+  act[i1] = norm_apply(x1, inv, gamma.v[1], kHiddenNorm);
 }
 
 // Block-wide max (and sum) of two int64 values at once; red needs 32 slots.
@@ -280,6 +292,9 @@ struct PSmem {
   uint64_t* mbar;     // [5]: KV copy completion, then 4 LM-head ring slots
   int32_t* own;       // [16]: this CTA's rows of hidden (0..7) and post (8..15)
   int* flag;
+  int32_t* exp_lut;   // [257] softmax LUT
+  int32_t* sig_lut;   // [1025] sigmoid LUT
+  int32_t* rope;      // [256]: cos, sin rows of the step's position
 };
 
 constexpr int kLmChunkRows = 64;  // LM-head rows per ring slot (32 KB + 2 KB)
@@ -387,12 +402,13 @@ __device__ __forceinline__ void preload_down(const LayerW& w, PreDown& pre) {
 __device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm, bool first_layer,
                           const PreQkv& pre) {
   const int G = gridDim.x, cta = blockIdx.x;
+  const Gamma2 gamma(w.g_in);
   // the layer input: the embedding (already in act) or the previous layer's output
   if (!first_layer)
     for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
       *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
   __syncthreads();
-  hidden_norm_inplace(sm.act, w.g_in, sm.red);
+  hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
   stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
   __syncthreads();
@@ -415,10 +431,11 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
   int32_t* kc = sm.hv + 2 * kHeadDim;
   int32_t* vc = sm.hv + 3 * kHeadDim;
   // raw q (2 heads), k, v of this KV head; then per-head norm and RoPE
-  int32_t raw = 0;
+  int32_t raw = 0, gam = 0;
   if (t < 3 * kHeadDim) {
     const int which = t / kHeadDim, d = t % kHeadDim;
     const int row = which < 2 ? (2 * h + which) * kHeadDim + d : kQRows + h * kHeadDim + d;
+    gam = __ldg((which < 2 ? w.g_q : w.g_k) + d);
     raw = ldcg(a.qkv + row);
   } else if (t < 4 * kHeadDim) {
     vc[t - 3 * kHeadDim] = ldcg(a.qkv + kQRows + kKvRows + h * kHeadDim + (t - 3 * kHeadDim));
@@ -431,8 +448,7 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     const int which = t / kHeadDim, d = t % kHeadDim;
     const int64_t ss = sm.red[which * 4] + sm.red[which * 4 + 1] + sm.red[which * 4 + 2] + sm.red[which * 4 + 3];
     const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
-    const int32_t* gamma = which < 2 ? w.g_q : w.g_k;
-    sm.hv[which * kHeadDim + d] = norm_apply(raw, inv, gamma[d], kHeadNorm);
+    sm.hv[which * kHeadDim + d] = norm_apply(raw, inv, gam, kHeadNorm);
   }
   __syncthreads();
   int32_t rot_v = 0;
@@ -440,7 +456,7 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     const int which = t / kHeadDim, d = t % kHeadDim;
     const int32_t* x = sm.hv + which * kHeadDim;
     const int64_t rot = d < 64 ? -(int64_t)x[d + 64] : (int64_t)x[d - 64];
-    rot_v = sat24(((int64_t)x[d] * a.cos_tab[pos * kHeadDim + d] + rot * a.sin_tab[pos * kHeadDim + d]) >> 15);
+    rot_v = sat24(((int64_t)x[d] * sm.rope[d] + rot * sm.rope[kHeadDim + d]) >> 15);
   }
   __syncthreads();
   if (t < 3 * kHeadDim) sm.hv[t] = rot_v;
@@ -505,13 +521,13 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
       const int i0 = lut_index(m0, s0[p]), i1 = lut_index(m1, s1[p]);
       s0[p] = i0;
       s1[p] = i1;
-      e0 += a.exp_lut[i0];
-      e1 += a.exp_lut[i1];
+      e0 += sm.exp_lut[i0];
+      e1 += sm.exp_lut[i1];
     }
     block_sum2(e0, e1, sm.red);
     for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
       const int hh = i / kExpLut, k = i % kExpLut;
-      sm.probtab[i] = ((uint64_t)a.exp_lut[k] << 16) / (uint64_t)(hh ? e1 : e0);
+      sm.probtab[i] = ((uint64_t)sm.exp_lut[k] << 16) / (uint64_t)(hh ? e1 : e0);
     }
   }
   __syncthreads();
@@ -558,10 +574,11 @@ __device__ void stage_oproj(const PersistArgs& a, const PSmem& sm, const PreO& p
 
 __device__ void stage_gateup(const PersistArgs& a, const LayerW& w, const PSmem& sm, const PreGU& pre) {
   const int G = gridDim.x, cta = blockIdx.x;
+  const Gamma2 gamma(w.g_post);
   for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
     *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.post + i);
   __syncthreads();
-  hidden_norm_inplace(sm.act, w.g_post, sm.red);
+  hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
   stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
   __syncthreads();
@@ -573,7 +590,7 @@ __device__ void stage_gateup(const PersistArgs& a, const LayerW& w, const PSmem&
     const int32_t gc = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
     int ix = (gc + 32768 + 32) >> 6;
     ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
-    const int32_t silu = sat24(((int64_t)g * a.sig_lut[ix]) >> 16);
+    const int32_t silu = sat24(((int64_t)g * sm.sig_lut[ix]) >> 16);
     a.st.mlp[r0 + i] = sat24(((int64_t)silu * u) >> 12);
   }
 }
@@ -604,10 +621,11 @@ __device__ void stage_down(const PersistArgs& a, const PSmem& sm, const PreDown&
 __device__ void stage_lmhead(const PersistArgs& a, const PSmem& sm, unsigned& ring_phase) {
   const int G = gridDim.x, cta = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Gamma2 gamma(a.g_final);
   for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
     *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
   __syncthreads();
-  hidden_norm_inplace(sm.act, a.g_final, sm.red);
+  hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
   stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
   __syncthreads();
@@ -736,7 +754,13 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
     sm.own = reinterpret_cast<int32_t*>(take(16 * 4));
     sm.flag = reinterpret_cast<int*>(take(16));
     sm.sc = reinterpret_cast<int64_t*>(take((size_t)2 * a.score_cap * 8));
+    sm.exp_lut = reinterpret_cast<int32_t*>(take(kExpLut * 4));
+    sm.sig_lut = reinterpret_cast<int32_t*>(take(kSigLut * 4));
+    sm.rope = reinterpret_cast<int32_t*>(take(2 * kHeadDim * 4));
   }
+  // the lookup tables stay in shared memory for the whole launch
+  for (int i = threadIdx.x; i < kExpLut; i += blockDim.x) sm.exp_lut[i] = a.exp_lut[i];
+  for (int i = threadIdx.x; i < kSigLut; i += blockDim.x) sm.sig_lut[i] = a.sig_lut[i];
   const int G = gridDim.x, cta = blockIdx.x;
   const bool attn_cta = cta < kKvHeads * kAttnSplit;
   if (threadIdx.x == 0) {
@@ -762,6 +786,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
     }
     const bool lm = pos + 1 >= a.lm_from;
     const int tok = next_tok >= 0 ? next_tok : ldcg(a.st.tokens + pos);
+    // this position's RoPE rows, read by the attention stage of every layer
+    if (attn_cta && threadIdx.x < 2 * kHeadDim)
+      sm.rope[threadIdx.x] = threadIdx.x < kHeadDim ? a.cos_tab[pos * kHeadDim + threadIdx.x]
+                                                    : a.sin_tab[pos * kHeadDim + threadIdx.x - kHeadDim];
     // tied embedding: the whole vector for the first norm, and this CTA's
     // rows of the residual stream
     {
@@ -832,7 +860,7 @@ size_t persistent_smem_bytes(int score_cap) {
   return r((size_t)kKvWindow * kHeadDim * 4) + r((size_t)kKvWindow * kSliceDims * 4) + r(kInter * 4) +
          r(limb_words(kInter) * 4) + r((kInter / 32) * 8) + r(256 * 8) + r(32 * 8) + r(2 * kExpLut * 8) +
          r(4 * kHeadDim * 4) + r((size_t)kPThreads * 2 * 8) + r(64) + r(64) + r(16) + r((size_t)2 * score_cap * 8) +
-         128;
+         r(kExpLut * 4) + r(kSigLut * 4) + r(2 * kHeadDim * 4) + 128;
 }
 
 }  // namespace q4
