@@ -289,10 +289,86 @@ enum {
  * `scale` its uint16 [rows, cols/64] scales; for gammas/tables `data` is
  * int32 and `scale` is NULL.  `layer` is ignored for model-wide tensors.
  * RoPE tables are int32 [max_context, 128] Q1.15. */
+/* The configuration the context was created with. */
+int q4gpu_model_get_config(q4gpu_model *m, q4gpu_model_config *cfg);
+
 int q4gpu_model_set_tensor(q4gpu_model *m, int32_t layer, int32_t which, const void *data,
                            size_t data_bytes, const uint16_t *scale, size_t scale_bytes);
 int q4gpu_model_get_tensor(q4gpu_model *m, int32_t layer, int32_t which, void *data,
                            size_t data_bytes, uint16_t *scale, size_t scale_bytes);
+
+/* =======================================================================
+ * QMAP v1 blob consumption (Source/QMAP_FORMAT.md).  The reference's
+ * PL-DDR image (61 segments, init/q4_runtime_assets.json) is copied into one
+ * host arena whose byte 0 sits at physical address arena_base
+ * (0x4_0000_0000); the walker reads the per-layer runtime packets and binds
+ * the tensors their descriptors point at.
+ * ======================================================================= */
+
+/* 256-byte QMAP header (QMAP_FORMAT.md:142-157), as stored (little-endian). */
+typedef struct q4gpu_qmap_header {
+    uint32_t magic, version, header_bytes, descriptor_bytes, descriptor_count, descriptor_capacity;
+    uint64_t descriptor_table_addr, payload_base_addr, image_base_addr, image_bytes;
+    uint32_t flags, checksum32;
+} q4gpu_qmap_header;
+
+/* 128-byte tensor descriptor (QMAP_FORMAT.md:193-214), as stored. */
+typedef struct q4gpu_qmap_descriptor {
+    uint32_t tensor_id, role, dtype, rank, flags, element_bits, group_size, scale_tensor_id;
+    uint64_t base_addr, nbytes;
+    uint32_t dims[4];
+    uint64_t strides_bytes[4];
+    uint32_t aux[4];
+    uint32_t checksum32;
+    uint32_t reserved[3];
+} q4gpu_qmap_descriptor;
+
+/* Where the packets are: per layer the ten bases of qot_layer_qmap_bases_t
+ * (qmap_one_token_runtime.h:31-42: qkv, input_norm, attn_frontend,
+ * attn_score_value, o_proj, post_attn_norm, mlp_gate_up, mlp_silu_mul,
+ * mlp_down, mlp_residual_add) and the final-tail packet
+ * (QOT_MODEL_FINAL_TAIL_QMAP_BASE).  The RoPE and embedding bases are
+ * optional cross-checks (0 = take them from the descriptors). */
+typedef struct q4gpu_qmap_layout {
+    uint64_t arena_base;
+    uint64_t final_tail_qmap_base;
+    uint64_t rope_cos_base, rope_sin_base;
+    uint64_t embed_weight_base, embed_scale_base;
+    int32_t n_layers;
+    int32_t reserved;
+    const uint64_t *layer_bases; /* [n_layers][10] */
+} q4gpu_qmap_layout;
+
+/* One bound model tensor (Q4GPU_T_* `which`; layer -1 = model-wide) as arena
+ * offsets.  Q4 weights: packed rows (rows x cols / 2 bytes) and their u16
+ * scales.  Vectors: rows values of elem_stride bytes each. */
+enum { Q4GPU_QMAP_PACKED_Q4 = 0, Q4GPU_QMAP_S16 = 1, Q4GPU_QMAP_U16 = 2, Q4GPU_QMAP_U32 = 3 };
+typedef struct q4gpu_qmap_tensor {
+    int32_t layer, which;
+    uint64_t data_offset, data_bytes;
+    uint64_t scale_offset, scale_bytes;
+    int32_t rows, cols;
+    int32_t elem_stride, elem_kind;
+} q4gpu_qmap_tensor;
+
+/* Decode and validate the packet at physical packet_addr (magic, version 1,
+ * 256/128-byte header/descriptors, count <= capacity, image_base_addr =
+ * packet_addr, table inside the arena).  Returns the descriptor count (up to
+ * desc_cap copied) or a negative Q4GPU_ERR_*.  Host only. */
+int q4gpu_qmap_read_packet(const uint8_t *arena, uint64_t arena_base, uint64_t arena_bytes, uint64_t packet_addr,
+                           q4gpu_qmap_header *header, q4gpu_qmap_descriptor *desc, int32_t desc_cap);
+/* Bind every model tensor of the image (11 per layer, then the RoPE planes,
+ * exp / sigmoid LUTs, tied embedding and final gamma).  Weights are found by
+ * role and matrix id (aux0), vectors by role, dtype and length; the LUTs must
+ * agree across layers and the score scale must be 189812531.  With cap 0 only
+ * *n_out is set.  Host only. */
+int q4gpu_qmap_bind(const uint8_t *arena, uint64_t arena_bytes, const q4gpu_qmap_layout *layout,
+                    q4gpu_qmap_tensor *out, int32_t cap, int32_t *n_out);
+/* A bound vector as int32 values (16-bit values extended from their slots). */
+int q4gpu_qmap_vector(const uint8_t *arena, const q4gpu_qmap_tensor *t, int32_t *out, int64_t count);
+/* Bind and upload the whole image into the context (q4gpu_model_set_tensor). */
+int q4gpu_model_load_qmap(q4gpu_model *m, const uint8_t *arena, uint64_t arena_bytes,
+                          const q4gpu_qmap_layout *layout);
 
 /* Runner with the exact signature of qot_session_runner_fn
  * (FPGA_Project/software/qmap_prompt_demo/qot_session.h:51-58; default runner

@@ -63,6 +63,35 @@ class ModelConfig(C.Structure):
                 ("max_seqs", C.c_int32), ("device", C.c_int32), ("reserved", C.c_int32 * 3)]
 
 
+class QmapHeader(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("magic", "version", "header_bytes", "descriptor_bytes",
+                                           "descriptor_count", "descriptor_capacity")] + \
+               [(n, C.c_uint64) for n in ("descriptor_table_addr", "payload_base_addr", "image_base_addr",
+                                           "image_bytes")] + [("flags", C.c_uint32), ("checksum32", C.c_uint32)]
+
+
+class QmapDescriptor(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("tensor_id", "role", "dtype", "rank", "flags", "element_bits",
+                                           "group_size", "scale_tensor_id")] + \
+               [("base_addr", C.c_uint64), ("nbytes", C.c_uint64), ("dims", C.c_uint32 * 4),
+                ("strides_bytes", C.c_uint64 * 4), ("aux", C.c_uint32 * 4), ("checksum32", C.c_uint32),
+                ("reserved", C.c_uint32 * 3)]
+
+
+class QmapLayout(C.Structure):
+    _fields_ = [("arena_base", C.c_uint64), ("final_tail_qmap_base", C.c_uint64), ("rope_cos_base", C.c_uint64),
+                ("rope_sin_base", C.c_uint64), ("embed_weight_base", C.c_uint64), ("embed_scale_base", C.c_uint64),
+                ("n_layers", C.c_int32), ("reserved", C.c_int32), ("layer_bases", C.POINTER(C.c_uint64))]
+
+
+class QmapTensor(C.Structure):
+    _fields_ = [("layer", C.c_int32), ("which", C.c_int32), ("data_offset", C.c_uint64),
+                ("data_bytes", C.c_uint64), ("scale_offset", C.c_uint64), ("scale_bytes", C.c_uint64),
+                ("rows", C.c_int32), ("cols", C.c_int32), ("elem_stride", C.c_int32), ("elem_kind", C.c_int32)]
+
+
+QMAP_PACKED_Q4, QMAP_S16, QMAP_U16, QMAP_U32 = range(4)
+
 P = C.c_void_p
 I32, I64, U32, U64, SZ = C.c_int32, C.c_int64, C.c_uint32, C.c_uint64, C.c_size_t
 
@@ -119,6 +148,11 @@ SIGNATURES = {
     "q4gpu_model_set_position": (C.c_int, [P, C.c_size_t, I32]),
     "q4gpu_model_read_tokens": (C.c_int, [P, C.c_size_t, I32, I32, P, P, P]),
     "q4gpu_model_time_kernels": (C.c_int, [P, C.c_size_t, I32, P, P]),
+    "q4gpu_model_get_config": (C.c_int, [P, C.POINTER(ModelConfig)]),
+    "q4gpu_qmap_read_packet": (C.c_int, [P, U64, U64, U64, C.POINTER(QmapHeader), C.POINTER(QmapDescriptor), I32]),
+    "q4gpu_qmap_bind": (C.c_int, [P, U64, C.POINTER(QmapLayout), C.POINTER(QmapTensor), I32, C.POINTER(I32)]),
+    "q4gpu_qmap_vector": (C.c_int, [P, C.POINTER(QmapTensor), P, I64]),
+    "q4gpu_model_load_qmap": (C.c_int, [P, P, U64, C.POINTER(QmapLayout)]),
 }
 
 _lib = None

@@ -18,7 +18,7 @@ REPO = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB = LIB_DIR / "libq4gpu.so"
-SOURCES = ["q4_modules.cu", "q4_decode.cu", "q4_persistent.cu", "q4_batch.cu"]
+SOURCES = ["q4_modules.cu", "q4_decode.cu", "q4_persistent.cu", "q4_batch.cu", "q4_qmap.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1271,6 +1271,12 @@ static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, s
   }
 }
 
+int q4gpu_model_get_config(q4gpu_model* m, q4gpu_model_config* cfg) {
+  if (!m || !cfg) return q4gpu_fail(Q4GPU_ERR_ARG, "null model/config");
+  *cfg = m->cfg;
+  return Q4GPU_OK;
+}
+
 int q4gpu_model_set_tensor(q4gpu_model* m, int32_t layer, int32_t which, const void* data, size_t data_bytes,
                            const uint16_t* scale, size_t scale_bytes) {
   return tensor_io(m, layer, which, const_cast<void*>(data), data_bytes, const_cast<uint16_t*>(scale), scale_bytes,
