@@ -526,7 +526,8 @@ int32_t q4gpu_model_get_mode(q4gpu_model *m);
 /* Diagnostics: run n_steps persistent decode steps of slot `base` (the LM head
  * where p + 1 >= lm_from) and return, for each of the first n_barriers grid
  * barriers, {last CTA's arrival, release} in %globaltimer ns (uint64 [n_barriers, 2]).
- * Per step there are 5 barriers per layer, then one after the LM head. */
+ * Per step there are 3 barriers per layer (after QKV, after attention + o_proj
+ * partial sums, after gate/up + down partial sums), then one after the LM head. */
 int q4gpu_model_trace_persistent(q4gpu_model *m, uintptr_t base, int32_t n_steps, int32_t lm_from,
                                  uint64_t *stamps, int32_t n_barriers);
 

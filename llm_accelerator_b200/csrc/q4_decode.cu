@@ -464,6 +464,7 @@ struct q4gpu_model {
   size_t p_smem = 0;
   LayerW* layers_dev = nullptr;
   int32_t* p_qkv = nullptr;
+  int64_t* p_acc = nullptr;
   ArgBestD* p_lm_part = nullptr;
   unsigned int* p_bar = nullptr;
   int* p_err = nullptr;
@@ -490,6 +491,9 @@ struct q4gpu_model {
   CUtensorMap b_mlm{};       // TMA map of b_emb8
   BatchLayerW b_layers[kMaxLayers]{};
   bool b_stale = true;  // int8 copies out of date with the Q4 weights
+  bool p_stale = true;  // the persistent kernel's o_proj slices out of date
+  uint8_t* p_wo_sl = nullptr;
+  uint16_t* p_so_sl = nullptr;
   int b_ones_sp = 0;    // SP whose ones rows the B matrices hold
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> b_graphs;  // (first slot, S, hidden-only)
   int32_t* b_final_act = nullptr;   // [64, 1024] final-norm vectors of a hidden-only step
@@ -708,6 +712,11 @@ int encode_kv_map(q4gpu_model* m, int64_t n_pages) {
 int run_persistent(q4gpu_model* m, int slot, int n_steps, int lm_from, unsigned long long* trace = nullptr,
                    int trace_cap = 0) {
   if (n_steps <= 0) return Q4GPU_OK;
+  if (m->p_stale) {
+    const int rc = q4gpu_persistent_relayout(m->layers_dev, m->cfg.n_layers, m->stream);
+    if (rc != Q4GPU_OK) return rc;
+    m->p_stale = false;
+  }
   PersistArgs a{};
   a.vmap = m->vmap;
   a.st = m->slots[slot];
@@ -722,6 +731,7 @@ int run_persistent(q4gpu_model* m, int slot, int n_steps, int lm_from, unsigned 
   a.exp_lut = m->exp_lut;
   a.sig_lut = m->sig_lut;
   a.qkv = m->p_qkv;
+  a.acc = m->p_acc;
   a.lm_part = m->p_lm_part;
   a.bar = m->p_bar;
   a.err = m->p_err;
@@ -730,14 +740,15 @@ int run_persistent(q4gpu_model* m, int slot, int n_steps, int lm_from, unsigned 
   a.score_cap = m->cfg.max_context;
   a.trace = trace;
   a.trace_cap = trace_cap;
-  // the arrival counter of one launch counts (5 L + 1) G per step: split very
+  // the arrival counter of one launch counts (3 L + 1) G per step: split very
   // long runs so it stays below 2^32
   const int per_launch = (int)std::min<int64_t>(
-      (int64_t)0xF0000000 / ((int64_t)m->p_grid * (5 * m->cfg.n_layers + 1)), 1 << 20);
+      (int64_t)0xF0000000 / ((int64_t)m->p_grid * (3 * m->cfg.n_layers + 1)), 1 << 20);
   int rc = Q4GPU_OK;
   for (int done = 0; done < n_steps && rc == Q4GPU_OK; done += per_launch) {
     a.n_steps = std::min(per_launch, n_steps - done);
     Q4_CUDA(cudaMemsetAsync(m->p_bar, 0, 2 * sizeof(unsigned int), m->stream));
+    Q4_CUDA(cudaMemsetAsync(m->p_acc, 0, 16 * kHidden * sizeof(int64_t), m->stream));
     rc = q4gpu_launch_persistent(a, m->p_grid, m->p_smem, m->stream);
     a.trace = nullptr;
   }
@@ -1036,8 +1047,12 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   if ((rc = m->alloc(&m->sin_tab, (size_t)cfg->max_context * kHeadDim))) return fail(rc);
   if ((rc = m->alloc(&m->exp_lut, kExpLut))) return fail(rc);
   if ((rc = m->alloc(&m->sig_lut, kSigLut))) return fail(rc);
+  if ((rc = m->alloc(&m->p_wo_sl, (size_t)L * 64 * kHidden * 16))) return fail(rc);
+  if ((rc = m->alloc(&m->p_so_sl, (size_t)L * 64 * kHidden * 2))) return fail(rc);
   for (int l = 0; l < L; ++l) {
     LayerW& w = m->layers[l];
+    w.wo_sl = m->p_wo_sl + (size_t)l * 64 * kHidden * 16;
+    w.so_sl = m->p_so_sl + (size_t)l * 64 * kHidden * 2;
     const TensorRef q = layer_tensor(m, l, Q4GPU_T_Q), o = layer_tensor(m, l, Q4GPU_T_O),
                     g = layer_tensor(m, l, Q4GPU_T_GATE), u = layer_tensor(m, l, Q4GPU_T_UP),
                     d = layer_tensor(m, l, Q4GPU_T_DOWN);
@@ -1134,6 +1149,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   if (cudaMemcpy(m->layers_dev, m->layers, sizeof(LayerW) * L, cudaMemcpyHostToDevice) != cudaSuccess)
     return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "layer table upload"));
   if ((rc = m->alloc(&m->p_qkv, (size_t)kQRows + 2 * kKvRows))) return fail(rc);
+  if ((rc = m->alloc(&m->p_acc, (size_t)16 * kHidden))) return fail(rc);
   if ((rc = m->alloc(&m->p_lm_part, 1024))) return fail(rc);
   if ((rc = m->alloc(&m->p_bar, 16))) return fail(rc);
   if ((rc = m->alloc(&m->p_err, 16))) return fail(rc);
@@ -1175,6 +1191,7 @@ int q4gpu_model_init_synthetic(q4gpu_model* m, uint64_t seed, float std_dev, flo
   Q4_CUDA(cudaMalloc(&err, sizeof(int32_t)));
   Q4_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), m->stream));
   m->b_stale = true;
+  m->p_stale = true;
   auto gen_quant = [&](uint64_t tid, const TensorRef& t) -> int {
     int r = q4gpu_synth_f32(seed, tid, 0, t.rows * t.cols, std_dev, 1, tmp, m->stream);
     if (r) return r;
@@ -1227,7 +1244,7 @@ static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, s
   int rc = set_device(m);
   if (rc) return rc;
   const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
-  if (to_device) m->b_stale = true;
+  if (to_device) m->b_stale = m->p_stale = true;
   auto cp = [&](void* dev, void* host, size_t n) -> int {
     Q4_CUDA(to_device ? cudaMemcpy(dev, host, n, kind) : cudaMemcpy(host, dev, n, kind));
     return Q4GPU_OK;

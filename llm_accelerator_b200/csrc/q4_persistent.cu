@@ -35,6 +35,8 @@ constexpr int kAttnSplit = 8;  // CTAs per KV head (head_dim slices of 16)
 constexpr int kSliceDims = kHeadDim / kAttnSplit;
 constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr int kKvWindow = 256;  // cached positions staged in shared memory
+constexpr int kAttnCtas = kKvHeads * kAttnSplit;  // CTAs [0, 64): attention + o_proj partial sums
+constexpr int kGuCtas = kInter / kGroup;          // CTAs [64, 112): 64 gate/up rows each + down partial sums
 
 // ---- memory-model helpers ---------------------------------------------------
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -290,7 +292,8 @@ struct PSmem {
   int32_t* kwin;      // [kKvWindow * 128]: cached K rows of the attention head
   int32_t* vwin;      // [kKvWindow * kSliceDims]: cached V of this CTA's dims
   uint64_t* mbar;     // [5]: KV copy completion, then 4 LM-head ring slots
-  int32_t* own;       // [16]: this CTA's rows of hidden (0..7) and post (8..15)
+  int32_t* hid;       // [1024]: the layer's input hidden state (Q14.10), every CTA a full copy
+  int32_t* post;      // [1024]: the post-attention hidden state (Q14.10), every CTA a full copy
   int* flag;
   int32_t* exp_lut;   // [257] softmax LUT
   int32_t* sig_lut;   // [1025] sigmoid LUT
@@ -363,9 +366,6 @@ __device__ __forceinline__ void issue_lm_chunk(const PersistArgs& a, const PSmem
 
 // ---- stages -----------------------------------------------------------------
 using PreQkv = Pre<kHidden, 2>;
-using PreO = Pre<2 * kHidden, 1>;
-using PreGU = Pre<kHidden, 3>;
-using PreDown = Pre<kInter, 2>;
 
 __device__ __forceinline__ void preload_qkv(const LayerW& w, PreQkv& pre) {
   const int r0 = part_of(4096, blockIdx.x, gridDim.x), r1 = part_of(4096, blockIdx.x + 1, gridDim.x);
@@ -374,39 +374,130 @@ __device__ __forceinline__ void preload_qkv(const LayerW& w, PreQkv& pre) {
     S = w.sqkv + (size_t)(r0 + r) * 16;
   }, pre);
 }
-__device__ __forceinline__ void preload_oproj(const LayerW& w, PreO& pre) {
-  const int r0 = part_of(kHidden, blockIdx.x, gridDim.x), r1 = part_of(kHidden, blockIdx.x + 1, gridDim.x);
-  preload_items((r1 - r0) * 2, [&](int r, const uint8_t*& W, const uint16_t*& S) {
-    W = w.wo + (size_t)(r0 + r) * 1024;
-    S = w.so + (size_t)(r0 + r) * 32;
-  }, pre);
+
+__device__ __forceinline__ int32_t nibble(uint32_t w, int k) { return (int32_t)(w << (28 - 4 * k)) >> 28; }
+__device__ __forceinline__ void red_add_i64(int64_t* p, int64_t v) {
+  atomicAdd(reinterpret_cast<unsigned long long*>(p), (unsigned long long)v);
 }
-__device__ __forceinline__ void preload_gateup(const LayerW& w, PreGU& pre) {
-  const int r0 = part_of(kInter, blockIdx.x, gridDim.x), r1 = part_of(kInter, blockIdx.x + 1, gridDim.x);
-  const int n = r1 - r0;
-  preload_items(2 * n, [&](int r, const uint8_t*& W, const uint16_t*& S) {
-    const bool up = r >= n;
-    const int row = r0 + (up ? r - n : r);
-    W = (up ? w.wup : w.wgate) + (size_t)row * 512;
-    S = (up ? w.sup : w.sgate) + (size_t)row * 16;
-  }, pre);
+__device__ __forceinline__ int64_t ldcg64(const int64_t* p) {
+  return (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
 }
-__device__ __forceinline__ void preload_down(const LayerW& w, PreDown& pre) {
-  const int r0 = part_of(kHidden, blockIdx.x, gridDim.x), r1 = part_of(kHidden, blockIdx.x + 1, gridDim.x);
-  preload_items((r1 - r0) * 3, [&](int r, const uint8_t*& W, const uint16_t*& S) {
-    W = w.wdown + (size_t)(r0 + r) * 1536;
-    S = w.sdown + (size_t)(r0 + r) * 48;
-  }, pre);
+// split-K partial sums of the layer with parity `par`: o_proj in buffer par,
+// down in buffer 2 + par; each row's sum owns a 32-byte sector (kAccStride
+// int64) so the atomic adds of the contributing CTAs spread over more L2 lines
+constexpr int kAccStride = 4;
+__device__ __forceinline__ int64_t* acc_row(const PersistArgs& a, int buf, int row) {
+  return a.acc + ((size_t)buf * kHidden + row) * kAccStride;
 }
 
-__device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm, bool first_layer,
+// o_proj columns fed by attention CTA (h, slice): for rows t and t + 512, the 16
+// columns (8 bytes) of each of its two q heads and the scale of their group
+// (16 columns starting at a multiple of 16 never straddle a 64-column group),
+// read from the regrouped copy (LayerW::wo_sl) with coalesced 16-byte loads.
+struct OSlice {
+  uint2 w[2][2];
+  uint32_t s[2][2];
+};
+__device__ __forceinline__ void preload_oslice(const LayerW& w, OSlice& o) {
+  const uint4* src = reinterpret_cast<const uint4*>(w.wo_sl) + (size_t)blockIdx.x * kHidden;
+  const uint32_t* ss = reinterpret_cast<const uint32_t*>(w.so_sl) + (size_t)blockIdx.x * kHidden;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = threadIdx.x + r * kPThreads;
+    const uint4 v = __ldg(src + row);
+    const uint32_t s2 = __ldg(ss + row);
+    o.w[r][0] = make_uint2(v.x, v.y);
+    o.w[r][1] = make_uint2(v.z, v.w);
+    o.s[r][0] = s2 & 0xFFFFu;
+    o.s[r][1] = s2 >> 16;
+  }
+}
+
+// Regroup every layer's o_proj columns into the attention CTAs' slices (run
+// whenever the weights change): grid (64 slices, layers).
+__global__ void oslice_layout_kernel(const LayerW* __restrict__ layers) {
+  const LayerW w = layers[blockIdx.y];
+  const int c = blockIdx.x, h = c / kAttnSplit, d0 = (c % kAttnSplit) * kSliceDims;
+  uint4* dst = reinterpret_cast<uint4*>(const_cast<uint8_t*>(w.wo_sl)) + (size_t)c * kHidden;
+  uint32_t* ds = reinterpret_cast<uint32_t*>(const_cast<uint16_t*>(w.so_sl)) + (size_t)c * kHidden;
+  for (int row = threadIdx.x; row < kHidden; row += blockDim.x) {
+    uint2 v[2];
+    uint32_t sc[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int col = (2 * h + hh) * kHeadDim + d0;
+      v[hh] = *reinterpret_cast<const uint2*>(w.wo + (size_t)row * kHidden + col / 2);
+      sc[hh] = w.so[(size_t)row * (2 * kHidden / kGroup) + col / kGroup];
+    }
+    dst[row] = make_uint4(v[0].x, v[0].y, v[1].x, v[1].y);
+    ds[row] = sc[0] | (sc[1] << 16);
+  }
+}
+
+// down columns [64 gc, 64 gc + 64) (this gate/up CTA's rows, one scale group)
+// of every row and their scales, staged in the CTA's K-window buffer (gate/up
+// CTAs run no attention): 32 bytes per row, then the 1024 scales.
+__device__ __forceinline__ uint4* dslice_w(const PSmem& sm) { return reinterpret_cast<uint4*>(sm.kwin); }
+__device__ __forceinline__ uint32_t* dslice_s(const PSmem& sm) {
+  return reinterpret_cast<uint32_t*>(sm.kwin + 2 * kHidden * 4);
+}
+// gate/up CTA gc owns gate and up rows [64 gc, 64 gc + 64) (items 0..63 gate,
+// 64..127 up); their packed rows sit in the K-window buffer after the down
+// slice: item it, lane l -> 16 bytes at gu_w[32 it + l], its half-group scale at gu_s[32 it + l].
+constexpr int kGuItems = 2 * kGroup;
+constexpr int kGuWOffset = 2 * kHidden * 16 + kHidden * 4;
+__device__ __forceinline__ uint4* gu_w(const PSmem& sm) {
+  return reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sm.kwin) + kGuWOffset);
+}
+__device__ __forceinline__ uint32_t* gu_s(const PSmem& sm) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sm.kwin) + kGuWOffset + kGuItems * 32 * 16);
+}
+static_assert(kGuWOffset + kGuItems * 32 * 20 <= kKvWindow * kHeadDim * 4, "gate/up staging exceeds the K window");
+__device__ __forceinline__ void preload_gateup(const LayerW& w, int gc, const PSmem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < kGuItems / kPWarps; ++j) {
+    const int it = warp + j * kPWarps;
+    const bool up = it >= kGroup;
+    const int row = gc * kGroup + (up ? it - kGroup : it);
+    const uint8_t* W = (up ? w.wup : w.wgate) + (size_t)row * 512;
+    const uint16_t* S = (up ? w.sup : w.sgate) + (size_t)row * 16;
+    const uint4 v = ldg_stream(W + lane * 16);
+    const uint32_t sc = __ldg(S + (lane >> 1));
+    gu_w(sm)[it * 32 + lane] = v;
+    gu_s(sm)[it * 32 + lane] = sc;
+  }
+}
+
+__device__ __forceinline__ void preload_dslice(const LayerW& w, int gc, const PSmem& sm) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = threadIdx.x + r * kPThreads;
+    const uint4* p = reinterpret_cast<const uint4*>(w.wdown + (size_t)row * (kInter / 2) + gc * (kGroup / 2));
+    const uint4 w0 = __ldg(p), w1 = __ldg(p + 1);
+    const uint32_t sc = __ldg(w.sdown + (size_t)row * (kInter / kGroup) + gc);
+    dslice_w(sm)[2 * row] = w0;
+    dslice_w(sm)[2 * row + 1] = w1;
+    dslice_s(sm)[row] = sc;
+  }
+}
+
+// Layer input hidden state, every CTA the whole vector: the embedding (layer 0,
+// already in hid) or post + (down >> 2) of the previous layer from its partial sums.
+__device__ __forceinline__ void build_hidden(const PersistArgs& a, const PSmem& sm, int par_prev) {
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    const int32_t dn = sat24(ldcg64(acc_row(a, 2 + par_prev, i)) >> 14);
+    sm.hid[i] = sat24((int64_t)sm.post[i] + (dn >> 2));
+  }
+}
+
+__device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm, bool first_layer, int par_prev,
                           const PreQkv& pre) {
   const int G = gridDim.x, cta = blockIdx.x;
   const Gamma2 gamma(w.g_in);
-  // the layer input: the embedding (already in act) or the previous layer's output
-  if (!first_layer)
-    for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
-      *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
+  if (!first_layer) build_hidden(a, sm, par_prev);
+  __syncthreads();
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) sm.act[i] = sm.hid[i];
   __syncthreads();
   hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
@@ -419,10 +510,18 @@ __device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm
 }
 
 // returns false on a copy timeout
-__device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSmem& sm, int layer, int pos,
-                                unsigned& mbar_phase) {
+__device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSmem& sm, int layer, int pos, int par,
+                                unsigned& mbar_phase, const OSlice& os) {
   const int cta = blockIdx.x;
-  if (cta >= kKvHeads * kAttnSplit) return true;
+  if (cta == (int)gridDim.x - 1) {
+    // the other parity's partial sums are free now (last read before this
+    // layer's first barrier, next written after this stage's barrier)
+    for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+      __stcg(reinterpret_cast<long long*>(acc_row(a, par ^ 1, i)), 0ll);
+      __stcg(reinterpret_cast<long long*>(acc_row(a, 2 + (par ^ 1), i)), 0ll);
+    }
+  }
+  if (cta >= kAttnCtas) return true;
   const int h = cta / kAttnSplit, sl = cta % kAttnSplit, d0 = sl * kSliceDims;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int ctx = pos + 1;
@@ -544,73 +643,94 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     sm.vacc[(pl * kSliceDims + dl) * 2 + 1] = acc1;
   }
   __syncthreads();
-  if (t < 2 * kSliceDims) {
+  if (t < 2 * kSliceDims) {  // this CTA's 32 attention outputs (q heads 2h, 2h + 1; dims d0..d0+15)
     const int dl = t % kSliceDims, hh = t / kSliceDims;
     int64_t acc = 0;
     for (int pl = 0; pl < kPThreads / kSliceDims; ++pl) acc += sm.vacc[(pl * kSliceDims + dl) * 2 + hh];
-    a.st.attn[(2 * h + hh) * kHeadDim + d0 + dl] = sat24(acc >> 16);
+    q0[hh * kSliceDims + dl] = sat24(acc >> 16);
+  }
+  __syncthreads();
+  // o_proj partial sums of those 32 inputs for every output row
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    int64_t v = 0;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      int32_t dot = 0;  // 16 terms: |dot| < 2^30
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        dot += nibble(os.w[r][hh].x, k) * q0[hh * kSliceDims + k];
+        dot += nibble(os.w[r][hh].y, k) * q0[hh * kSliceDims + 8 + k];
+      }
+      v += (int64_t)dot * os.s[r][hh];
+    }
+    red_add_i64(acc_row(a, par, t + r * kPThreads), v);
   }
   return true;
 }
 
-__device__ void stage_oproj(const PersistArgs& a, const PSmem& sm, const PreO& pre) {
-  const int G = gridDim.x, cta = blockIdx.x;
-  constexpr int K = 2 * kHidden;
-  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
-    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.attn + i);
-  __syncthreads();
-  stage_limbs_par(sm.act, K, sm.limbs, sm.bias8);
-  __syncthreads();
-  const int r0 = part_of(kHidden, cta, G), r1 = part_of(kHidden, cta + 1, G);
-  compute_items((r1 - r0) * 2, pre, sm.limbs, sm.bias8, sm.part);
-  __syncthreads();
-  for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) {
-    const int32_t o = sat24((sm.part[2 * i] + sm.part[2 * i + 1]) >> 14);
-    const int32_t post = sat24((int64_t)sm.own[i] + (o >> 2));
-    a.st.post[r0 + i] = post;
-    sm.own[8 + i] = post;
-  }
-}
-
-__device__ void stage_gateup(const PersistArgs& a, const LayerW& w, const PSmem& sm, const PreGU& pre) {
-  const int G = gridDim.x, cta = blockIdx.x;
+// post = hidden + (o_proj >> 2) from the o_proj partial sums (every CTA, whole
+// vector); gate/up CTAs then run their 64 gate and 64 up rows, SwiGLU, and add
+// their down partial sums (64 columns of K = one scale group) for every row.
+__device__ void stage_gateup_down(const PersistArgs& a, const LayerW& w, const PSmem& sm, int par) {
+  const int gc = (int)blockIdx.x - kAttnCtas;
+  const bool gu = gc >= 0 && gc < kGuCtas;
   const Gamma2 gamma(w.g_post);
-  for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
-    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.post + i);
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    const int32_t o = sat24(ldcg64(acc_row(a, par, i)) >> 14);
+    const int32_t post = sat24((int64_t)sm.hid[i] + (o >> 2));
+    sm.post[i] = post;
+    sm.act[i] = post;
+  }
+  if (!gu) return;
   __syncthreads();
   hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
   stage_limbs_par(sm.act, kHidden, sm.limbs, sm.bias8);
   __syncthreads();
-  const int r0 = part_of(kInter, cta, G), r1 = part_of(kInter, cta + 1, G), n = r1 - r0;
-  compute_items(2 * n, pre, sm.limbs, sm.bias8, sm.part);
+  {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint32_t l24[24];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) {
+      const uint4 t = reinterpret_cast<const uint4*>(sm.limbs + lane * kLimbStride)[i];
+      l24[4 * i] = t.x;
+      l24[4 * i + 1] = t.y;
+      l24[4 * i + 2] = t.z;
+      l24[4 * i + 3] = t.w;
+    }
+    const int64_t b8 = sm.bias8[lane];
+#pragma unroll 4
+    for (int j = 0; j < kGuItems / kPWarps; ++j) {
+      const int it = warp + j * kPWarps;
+      const int64_t v = warp_sum_i64(lane_span(gu_w(sm)[it * 32 + lane], l24, b8, gu_s(sm)[it * 32 + lane]));
+      if (lane == 0) sm.part[it] = v;
+    }
+  }
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int32_t g = sat24(sm.part[i] >> 14), u = sat24(sm.part[n + i] >> 14);
-    const int32_t gc = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
-    int ix = (gc + 32768 + 32) >> 6;
+  if (threadIdx.x < kGroup) {
+    const int32_t g = sat24(sm.part[threadIdx.x] >> 14), u = sat24(sm.part[kGroup + threadIdx.x] >> 14);
+    const int32_t gcl = g < -32768 ? -32768 : (g > 32768 ? 32768 : g);
+    int ix = (gcl + 32768 + 32) >> 6;
     ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
     const int32_t silu = sat24(((int64_t)g * sm.sig_lut[ix]) >> 16);
-    a.st.mlp[r0 + i] = sat24(((int64_t)silu * u) >> 12);
+    sm.hv[threadIdx.x] = sat24(((int64_t)silu * u) >> 12);
   }
-}
-
-__device__ void stage_down(const PersistArgs& a, const PSmem& sm, const PreDown& pre) {
-  const int G = gridDim.x, cta = blockIdx.x;
-  constexpr int K = kInter;
-  for (int i = threadIdx.x * 4; i < K; i += blockDim.x * 4)
-    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.mlp + i);
   __syncthreads();
-  stage_limbs_par(sm.act, K, sm.limbs, sm.bias8);
-  __syncthreads();
-  const int r0 = part_of(kHidden, cta, G), r1 = part_of(kHidden, cta + 1, G);
-  compute_items((r1 - r0) * 3, pre, sm.limbs, sm.bias8, sm.part);
-  __syncthreads();
-  for (int i = threadIdx.x; i < r1 - r0; i += blockDim.x) {
-    const int32_t dn = sat24((sm.part[3 * i] + sm.part[3 * i + 1] + sm.part[3 * i + 2]) >> 14);
-    const int32_t hid = sat24((int64_t)sm.own[8 + i] + (dn >> 2));
-    a.st.hidden[r0 + i] = hid;
-    sm.own[i] = hid;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = threadIdx.x + r * kPThreads;
+    const uint4 w0 = dslice_w(sm)[2 * row], w1 = dslice_w(sm)[2 * row + 1];
+    const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    int64_t dot = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 16 terms per int32 chunk: |sum| < 2^30
+      int32_t part = 0;
+#pragma unroll
+      for (int k = 0; k < 16; ++k) part += nibble(wv[2 * q + k / 8], k % 8) * sm.hv[16 * q + k];
+      dot += part;
+    }
+    red_add_i64(acc_row(a, 2 + par, row), dot * (int64_t)dslice_s(sm)[row]);
   }
 }
 
@@ -622,8 +742,7 @@ __device__ void stage_lmhead(const PersistArgs& a, const PSmem& sm, unsigned& ri
   const int G = gridDim.x, cta = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Gamma2 gamma(a.g_final);
-  for (int i = threadIdx.x * 4; i < kHidden; i += blockDim.x * 4)
-    *reinterpret_cast<int4*>(sm.act + i) = ldcg4(a.st.hidden + i);
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) sm.act[i] = sm.hid[i];  // the final hidden state
   __syncthreads();
   hidden_norm_inplace(sm.act, gamma, sm.red);
   __syncthreads();
@@ -751,7 +870,8 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
     sm.hv = reinterpret_cast<int32_t*>(take(4 * kHeadDim * 4));
     sm.vacc = reinterpret_cast<int64_t*>(take((size_t)kPThreads * 2 * 8));
     sm.mbar = reinterpret_cast<uint64_t*>(take(8 * 8));
-    sm.own = reinterpret_cast<int32_t*>(take(16 * 4));
+    sm.hid = reinterpret_cast<int32_t*>(take(kHidden * 4));
+    sm.post = reinterpret_cast<int32_t*>(take(kHidden * 4));
     sm.flag = reinterpret_cast<int*>(take(16));
     sm.sc = reinterpret_cast<int64_t*>(take((size_t)2 * a.score_cap * 8));
     sm.exp_lut = reinterpret_cast<int32_t*>(take(kExpLut * 4));
@@ -762,7 +882,9 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
   for (int i = threadIdx.x; i < kExpLut; i += blockDim.x) sm.exp_lut[i] = a.exp_lut[i];
   for (int i = threadIdx.x; i < kSigLut; i += blockDim.x) sm.sig_lut[i] = a.sig_lut[i];
   const int G = gridDim.x, cta = blockIdx.x;
-  const bool attn_cta = cta < kKvHeads * kAttnSplit;
+  const bool attn_cta = cta < kAttnCtas;
+  const int gc = cta - kAttnCtas;
+  const bool gu_cta = gc >= 0 && gc < kGuCtas;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 1 + kLmRing; ++i) mbar_init(sm.mbar + i, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -773,12 +895,10 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
   unsigned ring_phase = 0;
   int pos = ldcg(a.st.pos);
   int next_tok = -1;
-  const int h0 = part_of(kHidden, cta, G), h1 = part_of(kHidden, cta + 1, G);
+  int par = 0;  // parity of the partial-sum buffers of the current layer (host zeroes parity 0)
   const int v0 = part_of(a.vocab, cta, G), v1 = part_of(a.vocab, cta + 1, G);
   PreQkv pq;
-  PreO po;
-  PreGU pg;
-  PreDown pd;
+  OSlice os;
   for (int step = 0; step < a.n_steps; ++step) {
     if (pos >= a.st.max_ctx) {  // every CTA sees the same pos: all stop here
       if (cta == 0 && threadIdx.x == 0) atomicCAS(a.err, 0, 2);
@@ -790,44 +910,42 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
     if (attn_cta && threadIdx.x < 2 * kHeadDim)
       sm.rope[threadIdx.x] = threadIdx.x < kHeadDim ? a.cos_tab[pos * kHeadDim + threadIdx.x]
                                                     : a.sin_tab[pos * kHeadDim + threadIdx.x - kHeadDim];
-    // tied embedding: the whole vector for the first norm, and this CTA's
-    // rows of the residual stream
+    // tied embedding: layer 0's input hidden state, every CTA the whole vector
     {
       const uint8_t* row = a.emb + (size_t)tok * (kHidden / 2);
       const uint16_t* sc = a.semb + (size_t)tok * (kHidden / kGroup);
       for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
         const uint8_t b = row[i >> 1];
         const int q = (int)((i & 1) ? (b >> 4) : (b & 0xF));
-        sm.act[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
-      }
-      __syncthreads();
-      for (int i = threadIdx.x; i < h1 - h0; i += blockDim.x) {
-        a.st.hidden[h0 + i] = sm.act[h0 + i];
-        sm.own[i] = sm.act[h0 + i];
+        sm.hid[i] = ((q >= 8 ? q - 16 : q) * (int32_t)sc[i / kGroup]) >> 4;
       }
     }
     preload_qkv(a.layers[0], pq);
     for (int l = 0; l < a.n_layers; ++l) {
       const LayerW w = a.layers[l];
       const bool last = l + 1 == a.n_layers;
-      if (attn_cta) issue_kv_copies(a, sm, l, pos);
-      preload_oproj(w, po);
-      stage_qkv(a, w, sm, l == 0, pq);
+      // layer 0's K/V window streams in during its QKV stage; later layers'
+      // windows were issued after the previous attention stage (the attention
+      // CTAs have no gate/up work), so the copies overlap that stage instead
+      if (attn_cta && l == 0) issue_kv_copies(a, sm, l, pos);
+      stage_qkv(a, w, sm, l == 0, par ^ 1, pq);
+      // issued here, not at the layer start: outstanding loads hold scoreboard
+      // slots that the QKV stage would wait on; the barrier hides their latency
+      if (attn_cta) preload_oslice(w, os);
       // L2 prefetch of the next layer's weight slices while waiting
       if (!grid_sync(bar, [&] {
             if (!last) prefetch_layer(a.layers[l + 1], cta, G);
           }))
         return;
-      if (!stage_attention(a, w, sm, l, pos, mbar_phase)) return;
+      if (!stage_attention(a, w, sm, l, pos, par, mbar_phase, os)) return;
+      if (attn_cta && !last) issue_kv_copies(a, sm, l + 1, pos);
+      if (gu_cta) {  // not attention CTAs: these loads overlap the barrier wait
+        preload_gateup(w, gc, sm);
+        preload_dslice(w, gc, sm);
+      }
       if (!grid_sync(bar)) return;
-      preload_gateup(w, pg);
-      stage_oproj(a, sm, po);
-      if (!grid_sync(bar)) return;
-      preload_down(w, pd);
-      stage_gateup(a, w, sm, pg);
-      if (!grid_sync(bar)) return;
+      stage_gateup_down(a, w, sm, par);
       if (!last) preload_qkv(a.layers[l + 1], pq);
-      stage_down(a, sm, pd);
       if (last && lm) {
         // the first LM-head chunks stream in while the layer barrier resolves
         fence_proxy_async();
@@ -836,7 +954,13 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
           for (int j = 0; j < kLmRing; ++j) issue_lm_chunk(a, sm, v0, v1, j);
       }
       if (!grid_sync(bar)) return;
+      par ^= 1;
     }
+    // the final hidden state (every CTA; CTA 0 also keeps it in the slot state)
+    build_hidden(a, sm, par ^ 1);
+    __syncthreads();
+    if (cta == 0)
+      for (int i = threadIdx.x; i < kHidden; i += blockDim.x) a.st.hidden[i] = sm.hid[i];
     next_tok = -1;
     if (lm) {
       stage_lmhead(a, sm, ring_phase);
@@ -848,7 +972,7 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
       }
       next_tok = (int)sm.part[0];
       __syncthreads();
-      // lm_part is rewritten only after the next step's 5 x layers barriers
+      // lm_part is rewritten only after the next step's 3 x layers barriers
     }
     ++pos;
   }
@@ -859,7 +983,8 @@ size_t persistent_smem_bytes(int score_cap) {
   auto r = [](size_t b) { return (b + 127) & ~(size_t)127; };
   return r((size_t)kKvWindow * kHeadDim * 4) + r((size_t)kKvWindow * kSliceDims * 4) + r(kInter * 4) +
          r(limb_words(kInter) * 4) + r((kInter / 32) * 8) + r(256 * 8) + r(32 * 8) + r(2 * kExpLut * 8) +
-         r(4 * kHeadDim * 4) + r((size_t)kPThreads * 2 * 8) + r(64) + r(64) + r(16) + r((size_t)2 * score_cap * 8) +
+         r(4 * kHeadDim * 4) + r((size_t)kPThreads * 2 * 8) + r(64) + 2 * r(kHidden * 4) + r(16) +
+         r((size_t)2 * score_cap * 8) +
          r(kExpLut * 4) + r(kSigLut * 4) + r(2 * kHeadDim * 4) + 128;
 }
 
@@ -871,6 +996,13 @@ int q4gpu_launch_persistent(const q4::PersistArgs& args, int grid, size_t smem, 
   const cudaError_t e = cudaLaunchCooperativeKernel((const void*)q4::decode_persistent_kernel, dim3(grid),
                                                     dim3(q4::kPThreads), params, smem, stream);
   if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "persistent launch: %s", cudaGetErrorString(e));
+  return Q4GPU_OK;
+}
+
+int q4gpu_persistent_relayout(const q4::LayerW* layers_dev, int n_layers, cudaStream_t stream) {
+  q4::oslice_layout_kernel<<<dim3(q4::kAttnCtas, n_layers), 256, 0, stream>>>(layers_dev);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "o_proj slice layout: %s", cudaGetErrorString(e));
   return Q4GPU_OK;
 }
 

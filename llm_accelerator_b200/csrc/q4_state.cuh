@@ -56,6 +56,11 @@ struct LayerW {
   const int32_t* g_post;
   const int32_t* g_q;
   const int32_t* g_k;
+  // o_proj columns regrouped for the persistent kernel's attention CTAs:
+  // slice c (KV head c / 8, head dims 16 (c % 8) ..) holds, per output row, the
+  // 16 columns of each of the head pair (16 B) and their two scales (u16 x 2)
+  const uint8_t* wo_sl;   // [64][1024][16]
+  const uint16_t* so_sl;  // [64][1024][2]
 };
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
@@ -80,6 +85,7 @@ struct PersistArgs {
   const int32_t* exp_lut;
   const int32_t* sig_lut;
   int32_t* qkv;        // [4096] raw projections of the current layer
+  int64_t* acc;        // [4][1024][4]: o_proj partial sums (layer parity 0, 1), then down (0, 1); one 32-B sector per row
   ArgBestD* lm_part;   // [gridDim.x]
   unsigned int* bar;   // [2]: grid barrier arrival counter (monotonic within a launch), spare
   int* err;            // 0 = ok
@@ -95,5 +101,6 @@ struct PersistArgs {
 }  // namespace q4
 
 // Launch / set-up of the persistent kernel (q4_persistent.cu).
+int q4gpu_persistent_relayout(const q4::LayerW* layers_dev, int n_layers, cudaStream_t stream);
 int q4gpu_launch_persistent(const q4::PersistArgs& args, int grid, size_t smem, cudaStream_t stream);
 int q4gpu_persistent_setup(int score_cap, size_t* smem, int* grid);
