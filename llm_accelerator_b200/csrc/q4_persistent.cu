@@ -253,28 +253,75 @@ __device__ __forceinline__ void preload_items(int n_items, RowFn row_of, Pre<K, 
   }
 }
 
+// Sum over the warp of R per-lane values at once (R = 2, 8): halving exchanges
+// leave lane l with the total of value (l >> 2) % R ... for R = 8, (l >> 4) % 2
+// for R = 2; returns it.
+template <int R>
+__device__ __forceinline__ int64_t warp_sum_multi(int64_t (&v)[R], int lane) {
+  if constexpr (R == 8) {
+    const bool h = lane & 16, g = lane & 8, b = lane & 4;
+    int64_t x[4], y[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = (h ? v[i + 4] : v[i]) + shfl_xor_i64(h ? v[i] : v[i + 4], 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) y[i] = (g ? x[i + 2] : x[i]) + shfl_xor_i64(g ? x[i] : x[i + 2], 8);
+    int64_t z = (b ? y[1] : y[0]) + shfl_xor_i64(b ? y[0] : y[1], 4);
+    z += shfl_xor_i64(z, 2);
+    z += shfl_xor_i64(z, 1);
+    return z;
+  } else {
+    static_assert(R == 2, "R = 2 or 8");
+    const bool h = lane & 16;
+    int64_t z = (h ? v[1] : v[0]) + shfl_xor_i64(h ? v[0] : v[1], 16);
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) z += shfl_xor_i64(z, m);
+    return z;
+  }
+}
+
 template <int K, int RMAX>
 __device__ __forceinline__ void compute_items(int n_items, const Pre<K, RMAX>& pre, const uint32_t* limbs,
                                               const int64_t* bias8, int64_t* part) {
   constexpr int KS = K / 1024;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if constexpr (RMAX == 2 && KS == 1) {
+    // one half-group of limbs serves both items; both sums leave one butterfly
+    const uint32_t* l = limbs + lane * kLimbStride;
+    uint32_t l24[24];
 #pragma unroll
-  for (int j = 0; j < RMAX; ++j) {
-    const int it = warp + j * kPWarps;
-    if (it < n_items) {
-      const int hg = (it % KS) * 32 + lane;
-      const uint32_t* l = limbs + hg * kLimbStride;
-      uint32_t l24[24];
+    for (int i = 0; i < 6; ++i) {
+      const uint4 t = reinterpret_cast<const uint4*>(l)[i];
+      l24[4 * i] = t.x;
+      l24[4 * i + 1] = t.y;
+      l24[4 * i + 2] = t.z;
+      l24[4 * i + 3] = t.w;
+    }
+    int64_t v[2];
 #pragma unroll
-      for (int i = 0; i < 6; ++i) {
-        const uint4 t = reinterpret_cast<const uint4*>(l)[i];
-        l24[4 * i] = t.x;
-        l24[4 * i + 1] = t.y;
-        l24[4 * i + 2] = t.z;
-        l24[4 * i + 3] = t.w;
+    for (int j = 0; j < 2; ++j)
+      v[j] = warp + j * kPWarps < n_items ? lane_span(pre.w[j], l24, bias8[lane], pre.sc[j]) : 0;
+    const int64_t tot = warp_sum_multi<2>(v, lane);
+    const int it = warp + ((lane >> 4) & 1) * kPWarps;
+    if ((lane & 15) == 0 && it < n_items) part[it] = tot;
+  } else {
+#pragma unroll
+    for (int j = 0; j < RMAX; ++j) {
+      const int it = warp + j * kPWarps;
+      if (it < n_items) {
+        const int hg = (it % KS) * 32 + lane;
+        const uint32_t* l = limbs + hg * kLimbStride;
+        uint32_t l24[24];
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+          const uint4 t = reinterpret_cast<const uint4*>(l)[i];
+          l24[4 * i] = t.x;
+          l24[4 * i + 1] = t.y;
+          l24[4 * i + 2] = t.z;
+          l24[4 * i + 3] = t.w;
+        }
+        const int64_t v = warp_sum_i64(lane_span(pre.w[j], l24, bias8[hg], pre.sc[j]));
+        if (lane == 0) part[it] = v;
       }
-      const int64_t v = warp_sum_i64(lane_span(pre.w[j], l24, bias8[hg], pre.sc[j]));
-      if (lane == 0) part[it] = v;
     }
   }
 }
@@ -643,11 +690,14 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     sm.vacc[(pl * kSliceDims + dl) * 2 + 1] = acc1;
   }
   __syncthreads();
-  if (t < 2 * kSliceDims) {  // this CTA's 32 attention outputs (q heads 2h, 2h + 1; dims d0..d0+15)
-    const int dl = t % kSliceDims, hh = t / kSliceDims;
-    int64_t acc = 0;
-    for (int pl = 0; pl < kPThreads / kSliceDims; ++pl) acc += sm.vacc[(pl * kSliceDims + dl) * 2 + hh];
-    q0[hh * kSliceDims + dl] = sat24(acc >> 16);
+  {  // this CTA's 32 attention outputs (q heads 2h, 2h + 1; dims d0..d0+15): warp w
+     // sums outputs 2w, 2w + 1 over the 32 position lanes (16 lanes each, 2 partials a lane)
+    static_assert(kPThreads / kSliceDims == 32 && kPWarps * 2 == 2 * kSliceDims, "reduction layout");
+    const int o = 2 * warp + (lane >> 4), dl = o % kSliceDims, hh = o / kSliceDims, pl = 2 * (lane & 15);
+    int64_t acc = sm.vacc[(pl * kSliceDims + dl) * 2 + hh] + sm.vacc[((pl + 1) * kSliceDims + dl) * 2 + hh];
+#pragma unroll
+    for (int m = 8; m > 0; m >>= 1) acc += shfl_xor_i64(acc, m);
+    if ((lane & 15) == 0) q0[hh * kSliceDims + dl] = sat24(acc >> 16);
   }
   __syncthreads();
   // o_proj partial sums of those 32 inputs for every output row
@@ -700,12 +750,15 @@ __device__ void stage_gateup_down(const PersistArgs& a, const LayerW& w, const P
       l24[4 * i + 3] = t.w;
     }
     const int64_t b8 = sm.bias8[lane];
-#pragma unroll 4
-    for (int j = 0; j < kGuItems / kPWarps; ++j) {
+    constexpr int J = kGuItems / kPWarps;  // 8 items per warp
+    int64_t v[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
       const int it = warp + j * kPWarps;
-      const int64_t v = warp_sum_i64(lane_span(gu_w(sm)[it * 32 + lane], l24, b8, gu_s(sm)[it * 32 + lane]));
-      if (lane == 0) sm.part[it] = v;
+      v[j] = lane_span(gu_w(sm)[it * 32 + lane], l24, b8, gu_s(sm)[it * 32 + lane]);
     }
+    const int64_t tot = warp_sum_multi<J>(v, lane);
+    if ((lane & 3) == 0) sm.part[warp + ((lane >> 2) & 7) * kPWarps] = tot;
   }
   __syncthreads();
   if (threadIdx.x < kGroup) {
@@ -938,12 +991,12 @@ __global__ void __launch_bounds__(kPThreads, 1) decode_persistent_kernel(const _
           }))
         return;
       if (!stage_attention(a, w, sm, l, pos, par, mbar_phase, os)) return;
-      if (attn_cta && !last) issue_kv_copies(a, sm, l + 1, pos);
       if (gu_cta) {  // not attention CTAs: these loads overlap the barrier wait
         preload_gateup(w, gc, sm);
         preload_dslice(w, gc, sm);
       }
       if (!grid_sync(bar)) return;
+      if (attn_cta && !last) issue_kv_copies(a, sm, l + 1, pos);
       stage_gateup_down(a, w, sm, par);
       if (!last) preload_qkv(a.layers[l + 1], pq);
       if (last && lm) {
