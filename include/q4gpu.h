@@ -517,7 +517,8 @@ int q4gpu_decode_steps(q4gpu_model *m, uintptr_t base, int32_t n_steps);
 /* Execution mode of q4gpu_decode_steps / q4gpu_decode_token_ids / decode_batch:
  * 0 = one CUDA graph of per-stage kernels per step (PDL-chained);
  * 1 = the persistent cooperative kernel, many steps per launch (default when
- *     its shared memory fits; q4gpu_run_token always uses mode 0).
+ *     its shared memory fits; q4gpu_run_token uses it for full-model calls
+ *     with the embedding, one step per call, and mode 0 for layer ranges).
  * A persistent launch whose grid barrier wait runs out reports through
  * q4gpu_model_sync (Q4GPU_ERR_CUDA) or QOT_ERR_TIMEOUT from the decode API. */
 int q4gpu_model_set_mode(q4gpu_model *m, int32_t mode);

@@ -1327,10 +1327,14 @@ int q4gpu_run_token(void* runner_context, uintptr_t base, const qot_run_config_t
   if (set_device(m)) return QOT_ERR_STATUS;
   const int slot = (int)base;
   if (slot_busy(m, slot)) return QOT_ERR_BUSY;
-  cudaGraphExec_t g;
-  if (get_graph(m, GraphKey{slot, (int)config->layer_start, (int)config->layer_count,
-                            config->embedding_enable ? 1 : 0, 1},
-                &g) != Q4GPU_OK)
+  // a full-model call with the embedding runs as one step of the persistent
+  // kernel (mode 1); layer ranges run the per-stage graph
+  const bool persistent = m->mode == 1 && m->p_grid > 0 && config->layer_start == 0u &&
+                          (int)config->layer_count == m->cfg.n_layers && config->embedding_enable;
+  cudaGraphExec_t g = nullptr;
+  if (!persistent && get_graph(m, GraphKey{slot, (int)config->layer_start, (int)config->layer_count,
+                                           config->embedding_enable ? 1 : 0, 1},
+                               &g) != Q4GPU_OK)
     return QOT_ERR_STATUS;
   const SlotState& st = m->slots[slot];
   int32_t* hin = m->h_in + 2 * slot;
@@ -1339,7 +1343,8 @@ int q4gpu_run_token(void* runner_context, uintptr_t base, const qot_run_config_t
   HostResult* hr = m->h_res + slot;
   if (cudaMemcpyAsync(st.tokens + position, &hin[0], 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess ||
       cudaMemcpyAsync(st.pos, &hin[1], 4, cudaMemcpyHostToDevice, m->stream) != cudaSuccess ||
-      cudaGraphLaunch(g, m->stream) != cudaSuccess ||
+      (persistent ? run_persistent(m, slot, 1, (int)position) != Q4GPU_OK
+                  : cudaGraphLaunch(g, m->stream) != cudaSuccess) ||
       cudaMemcpyAsync(&hr->token, st.tokens + position + 1, 4, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess ||
       cudaMemcpyAsync(&hr->score, st.scores + position + 1, 8, cudaMemcpyDeviceToHost, m->stream) != cudaSuccess ||
       cudaEventRecord(m->done[slot], m->stream) != cudaSuccess) {
@@ -1350,6 +1355,7 @@ int q4gpu_run_token(void* runner_context, uintptr_t base, const qot_run_config_t
   memset(result, 0, sizeof(*result));
   rc = poll_slot(m, slot, max_polls);
   if (rc != QOT_OK) return rc;
+  if (persistent && check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
   result->status = 1u;  // done
   result->token_id = (uint32_t)hr->token;
   result->score_q26 = hr->score;
