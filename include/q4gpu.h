@@ -413,6 +413,22 @@ int q4gpu_decode_batch(q4gpu_model *m, int32_t n_seq, const uint32_t *prompts,
  * advances the position.  Asynchronous on the model stream. */
 int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t n_steps);
 
+/* Batched exact prefill (no reference counterpart: the reference runs a
+ * prompt one position at a time).  Stores each prompt in its slot's token
+ * array (prompts concatenated, prompt_lens[n_seq], 1 <= len <= max_context),
+ * runs positions 0 .. len - 2 of all n_seq sequences (1 <= n_seq <= 64, slots
+ * [first_slot, first_slot + n_seq)) through every layer as columns of batched
+ * passes (64 columns per tcgen05 GEMM, 32-position query tiles per attention
+ * CTA), and leaves each slot at position len - 1 with lm_from = len: the K/V
+ * cache equals the one serial decode steps leave, bit for bit, and
+ * q4gpu_batch_steps continues from the last prompt token.  Asynchronous on
+ * the model stream. */
+int q4gpu_batch_prefill(q4gpu_model *m, int32_t first_slot, int32_t n_seq, const uint32_t *prompts,
+                        const uint32_t *prompt_lens);
+/* How q4gpu_decode_batch runs the prompts: 1 = q4gpu_batch_prefill (default),
+ * 0 = serial batched steps from position 0 (the reference's order). */
+int q4gpu_model_set_prefill(q4gpu_model *m, int32_t mode);
+
 /* Vocabulary-sharded LM head (no reference counterpart; the reference scans the
  * whole vocabulary on one device).  A step becomes: q4gpu_batch_forward_hidden
  * on each rank's own sequences -> exchange of the final vectors -> each rank's

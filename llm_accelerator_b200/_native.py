@@ -126,6 +126,8 @@ SIGNATURES = {
                                          C.POINTER(U32), C.POINTER(QotResult)]),
     "q4gpu_decode_batch": (C.c_int, [P, I32, P, P, U32, P, P]),
     "q4gpu_batch_steps": (C.c_int, [P, I32, I32, I32]),
+    "q4gpu_batch_prefill": (C.c_int, [P, I32, I32, P, P]),
+    "q4gpu_model_set_prefill": (C.c_int, [P, I32]),
     "q4gpu_batch_forward_hidden": (C.c_int, [P, I32, I32, P]),
     "q4gpu_lm_head_shard": (C.c_int, [P, P, I32, I32, I32, P, P]),
     "q4gpu_batch_commit": (C.c_int, [P, I32, I32, P, P]),

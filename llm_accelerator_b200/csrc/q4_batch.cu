@@ -1114,6 +1114,300 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Batched exact prefill.  The prompt positions of the sequences become the
+// columns of batched passes, column = (sequence, position) in sequence-major
+// order: 64 columns per GEMM (the batched-step GEMMs, unchanged), a block of
+// up to kPfBlock columns per attention launch.  Blocks run through all layers
+// in column order, so the keys and values a column attends to are in the
+// cache when its attention runs: earlier positions of the same sequence were
+// written by earlier blocks (every layer) or, in this block, by the q/k
+// kernel that runs before the attention.  Each column computes exactly what
+// a decode step at its position computes, so the K/V cache it leaves equals
+// the serial one bit for bit.
+//
+// Attention (prefill_attn_kernel): one CTA per (KV head, query tile of up to
+// 32 consecutive positions of one sequence), 64 query rows (the two heads of
+// the group).  The exact LUT softmax is done in three passes over 64-key
+// chunks staged in shared memory (padded rows, cp.async):
+//   1. scaled scores -> row maxima;
+//   2. scores again -> LUT indices (kept in a u16 scratch) and exp sums;
+//      then a probability table per row, prob[e] = (lut[e] << 16) / sum;
+//   3. values: sum over keys of prob[idx] * v in int64, then sat24(>> 16)
+//      as limbs of the o_proj input.
+// ---------------------------------------------------------------------------
+constexpr int kPfStride = kHeadDim + 4;  // padded shared-memory row (words): conflict-free 16-byte reads
+constexpr int kPfRows = 2 * kPfTileQ;    // query rows of a CTA
+constexpr int kPfChunkWords = kPfKeys * kPfStride;
+constexpr int kPfPbStride = kPfKeys + 4;
+constexpr size_t kPfTabBytes = (size_t)kPfRows * kExpLut * 4;  // >= the q rows' kPfRows * kPfStride * 4
+constexpr size_t kPfSmem = kPfTabBytes + 2 * (size_t)kPfChunkWords * 4 + (size_t)kPfRows * kPfPbStride * 4;
+static_assert((size_t)kPfRows * kPfStride * 4 <= kPfTabBytes, "q rows alias the probability table");
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// q (kind 0) or k (kind 1) head row -> RMSNorm (head constants) -> RoPE at
+// `pos`, by one warp: lane owns elements 4 lane .. 4 lane + 3, the rotation
+// partner d +- 64 sits 16 lanes away.  Same arithmetic as the decode kernels.
+__device__ __forceinline__ int4 head_norm_rope(const int32_t* row, const int32_t* gamma, const int32_t* cos_tab,
+                                               const int32_t* sin_tab, int pos, int lane) {
+  const int4 x = *reinterpret_cast<const int4*>(row + 4 * lane);
+  const int4 cs = *reinterpret_cast<const int4*>(cos_tab + (size_t)pos * kHeadDim + 4 * lane);
+  const int4 sn = *reinterpret_cast<const int4*>(sin_tab + (size_t)pos * kHeadDim + 4 * lane);
+  const int4 gm = *reinterpret_cast<const int4*>(gamma + 4 * lane);
+  const int32_t xs[4] = {x.x, x.y, x.z, x.w}, cv[4] = {cs.x, cs.y, cs.z, cs.w}, sv[4] = {sn.x, sn.y, sn.z, sn.w};
+  const int32_t gv[4] = {gm.x, gm.y, gm.z, gm.w};
+  int64_t ss = 0;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ss = mad_wide(xs[e], xs[e], ss);
+  ss = warp_sum_i64(ss);
+  const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
+  int32_t o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int32_t n = norm_apply(xs[e], inv, gv[e], kHeadNorm);
+    const int32_t partner = __shfl_xor_sync(0xFFFFFFFFu, n, 16);
+    const int64_t rot = lane < 16 ? -(int64_t)partner : (int64_t)partner;
+    o[e] = sat24(((int64_t)n * cv[e] + rot * sv[e]) >> 15);
+  }
+  return make_int4(o[0], o[1], o[2], o[3]);
+}
+
+// Per (KV head, column): q heads 2 kv, 2 kv + 1 normed and roped in place in
+// qkv, k normed and roped into the cache, v copied into the cache.
+__global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __restrict__ col_slots,
+                                                         const int32_t* __restrict__ col_pos4, int32_t* qkv,
+                                                         int layer, const int32_t* __restrict__ g_q,
+                                                         const int32_t* __restrict__ g_k,
+                                                         const int32_t* __restrict__ cos_tab,
+                                                         const int32_t* __restrict__ sin_tab) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int kv = blockIdx.x, m = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int pos = col_pos4[4 * m];
+  const KvView kvv = col_slots[m].kv;
+  int32_t* raw = qkv + (size_t)m * (kQRows + 2 * kKvRows);
+  if (warp < 2) {
+    int32_t* row = raw + (2 * kv + warp) * kHeadDim;
+    const int4 o = head_norm_rope(row, g_q, cos_tab, sin_tab, pos, lane);
+    reinterpret_cast<int4*>(row)[lane] = o;
+  } else if (warp == 2) {
+    const int4 o = head_norm_rope(raw + kQRows + kv * kHeadDim, g_k, cos_tab, sin_tab, pos, lane);
+    reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = o;
+  } else {
+    const int4 v = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
+    reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v;
+  }
+}
+
+__global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
+  extern __shared__ __align__(16) uint8_t pf_smem[];
+  int32_t* qs = reinterpret_cast<int32_t*>(pf_smem);     // [64][kPfStride] q rows (passes 1-2)
+  uint32_t* ptab = reinterpret_cast<uint32_t*>(pf_smem);  // [64][257] probability table (pass 3)
+  int32_t* ring = reinterpret_cast<int32_t*>(pf_smem + kPfTabBytes);  // 2 x [64][kPfStride]
+  uint32_t* pb = reinterpret_cast<uint32_t*>(pf_smem + kPfTabBytes + 2 * (size_t)kPfChunkWords * 4);
+  __shared__ int32_t elut[kExpLut];
+  __shared__ int64_t rmax[kPfRows], rsum[kPfRows];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int kv = blockIdx.x;
+  const PfTile tl = a.tiles[blockIdx.y];
+  const int t = threadIdx.x, rg = t >> 4, kg = t & 15;
+  const KvView kvv = a.col_slots[tl.col0].kv;
+  const int kend = tl.pos0 + tl.nq;  // keys 0 .. kend - 1
+  const int nch = (kend + kPfKeys - 1) / kPfKeys;
+
+  // chunk c of K (kind 0) or V (kind 1) into ring buffer c & 1; one commit
+  // group per call, empty past the end, so wait_group 1 always means "chunk c
+  // has landed" when chunks c and c + 1 were the last two issued
+  auto issue = [&](int kind, int c) {
+    if (c < nch) {
+      const int j0 = c * kPfKeys;
+      const int n = kend - j0 < kPfKeys ? kend - j0 : kPfKeys;
+      const int32_t* src = kvv.at(a.layer, kind, kv, j0);  // a 64-aligned chunk is one page
+      int32_t* dst = ring + (c & 1) * kPfChunkWords;
+      for (int i = t; i < n * (kHeadDim / 4); i += 256) {
+        const int j = i >> 5, d4 = i & 31;
+        cp_async16(dst + j * kPfStride + 4 * d4, src + (size_t)j * kHeadDim + 4 * d4);
+      }
+    }
+    cp_async_commit();
+  };
+  issue(0, 0);
+  issue(0, 1);
+  for (int i = t; i < kPfRows * (kHeadDim / 4); i += 256) {
+    const int r = i >> 5, d4 = i & 31, hh = r / kPfTileQ, qi = r % kPfTileQ;
+    int4 v = make_int4(0, 0, 0, 0);
+    if (qi < tl.nq)
+      v = *reinterpret_cast<const int4*>(a.qkv + (size_t)(tl.col0 + qi) * (kQRows + 2 * kKvRows) +
+                                         (2 * kv + hh) * kHeadDim + 4 * d4);
+    *reinterpret_cast<int4*>(qs + r * kPfStride + 4 * d4) = v;
+  }
+  for (int i = t; i < kExpLut; i += 256) elut[i] = a.exp_lut[i];
+
+  // scores of this thread's rows 4 rg + e and keys kg + 16 u of a staged chunk
+  auto scores = [&](const int32_t* kb, int64_t (&acc)[4][4]) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[e][u] = 0;
+#pragma unroll 2
+    for (int d = 0; d < kHeadDim; d += 4) {
+      int4 q[4], k[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) q[e] = *reinterpret_cast<const int4*>(qs + (4 * rg + e) * kPfStride + d);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) k[u] = *reinterpret_cast<const int4*>(kb + (kg + 16 * u) * kPfStride + d);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          int64_t s = acc[e][u];
+          s = mad_wide(q[e].x, k[u].x, s);
+          s = mad_wide(q[e].y, k[u].y, s);
+          s = mad_wide(q[e].z, k[u].z, s);
+          s = mad_wide(q[e].w, k[u].w, s);
+          acc[e][u] = s;
+        }
+    }
+  };
+  // row r = hh * 32 + qi is query position pos0 + qi; key j is valid for it when j <= pos0 + qi
+  auto valid = [&](int e, int j) {
+    const int qi = (4 * rg + e) % kPfTileQ;
+    return qi < tl.nq && j <= tl.pos0 + qi;
+  };
+
+  // pass 1: row maxima
+  int64_t mx[4] = {INT64_MIN, INT64_MIN, INT64_MIN, INT64_MIN};
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait1();
+    __syncthreads();
+    int64_t acc[4][4];
+    scores(ring + (c & 1) * kPfChunkWords, acc);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (valid(e, c * kPfKeys + kg + 16 * u)) {
+          const int64_t s = scale_score(acc[e][u], kScoreScale);
+          mx[e] = s > mx[e] ? s : mx[e];
+        }
+    __syncthreads();
+    issue(0, c + 2);
+  }
+  issue(0, 0);  // pass 2 streams K again
+  issue(0, 1);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int msk = 1; msk < 16; msk <<= 1) {
+      const int64_t o = shfl_xor_i64(mx[e], msk);
+      mx[e] = o > mx[e] ? o : mx[e];
+    }
+    if (kg == 0) rmax[4 * rg + e] = mx[e];
+  }
+  __syncthreads();
+  // pass 2: LUT indices and exp sums
+  int64_t sm[4] = {0, 0, 0, 0};
+  const int64_t rmx[4] = {rmax[4 * rg], rmax[4 * rg + 1], rmax[4 * rg + 2], rmax[4 * rg + 3]};
+  uint16_t* idx_row[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = 4 * rg + e, hh = r / kPfTileQ, qi = r % kPfTileQ;
+    const int col = tl.col0 + (qi < tl.nq ? qi : 0);
+    idx_row[e] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.max_ctx;
+  }
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait1();
+    __syncthreads();
+    int64_t acc[4][4];
+    scores(ring + (c & 1) * kPfChunkWords, acc);
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = c * kPfKeys + kg + 16 * u;
+        if (valid(e, j)) {
+          const int ix = lut_index(rmx[e], scale_score(acc[e][u], kScoreScale));
+          sm[e] += elut[ix];
+          idx_row[e][j] = (uint16_t)ix;
+        }
+      }
+    __syncthreads();
+    issue(0, c + 2);
+  }
+  issue(1, 0);  // pass 3 streams V
+  issue(1, 1);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int msk = 1; msk < 16; msk <<= 1) sm[e] += shfl_xor_i64(sm[e], msk);
+    if (kg == 0) rsum[4 * rg + e] = sm[e];
+  }
+  __syncthreads();  // q rows are dead: the table takes their place
+  for (int i = t; i < kPfRows * kExpLut; i += 256) {
+    const int r = i / kExpLut, e = i - r * kExpLut;
+    const int64_t s = rsum[r];
+    ptab[i] = s > 0 ? (uint32_t)udiv_exact((uint64_t)elut[e] << 16, (uint64_t)s) : 0u;
+  }
+  // pass 3: probability-weighted values.  Thread (rg, kg) owns output rows
+  // 4 rg + e and dims 4 kg + f, 64 + 4 kg + f.
+  int64_t o[4][8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+#pragma unroll
+    for (int f = 0; f < 8; ++f) o[e][f] = 0;
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait1();
+    __syncthreads();  // also orders the table writes before the first lookups
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = kg + 16 * u, j = c * kPfKeys + jj;
+        uint32_t p = 0;
+        if (valid(e, j)) p = ptab[(4 * rg + e) * kExpLut + idx_row[e][j]];
+        pb[(4 * rg + e) * kPfPbStride + jj] = p;
+      }
+    __syncthreads();
+    const int32_t* vb = ring + (c & 1) * kPfChunkWords;
+    const int n = kend - c * kPfKeys < kPfKeys ? kend - c * kPfKeys : kPfKeys;
+#pragma unroll 2
+    for (int jj = 0; jj < n; ++jj) {
+      const int4 v0 = *reinterpret_cast<const int4*>(vb + jj * kPfStride + 4 * kg);
+      const int4 v1 = *reinterpret_cast<const int4*>(vb + jj * kPfStride + 64 + 4 * kg);
+      const int32_t vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int32_t p = (int32_t)pb[(4 * rg + e) * kPfPbStride + jj];
+#pragma unroll
+        for (int f = 0; f < 8; ++f) o[e][f] = mad_wide(p, vv[f], o[e][f]);
+      }
+    }
+    __syncthreads();
+    issue(1, c + 2);
+  }
+  // outputs as limbs of the o_proj input (64-column sub-batches, SP = 64)
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int r = 4 * rg + e, hh = r / kPfTileQ, qi = r % kPfTileQ;
+    if (qi >= tl.nq) continue;
+    const int col = tl.col0 + qi;
+    uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
+#pragma unroll
+    for (int f = 0; f < 8; ++f) {
+      const int d = (f < 4 ? 4 * kg + f : 64 + 4 * kg + f - 4);
+      write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d, sat24(o[e][f] >> 16));
+    }
+  }
+}
+
 }  // namespace q4
 
 // ===========================================================================
@@ -1330,6 +1624,57 @@ int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
   BQ((launch_gemm<SP, kGemmLm>(q.amap, q.bmap, c, q.scales, rows, kHidden, 1, nullptr, q.partial, s)));
   shard_argmax_kernel<<<q.n_act, 256, 0, s>>>(q.partial, (rows + 127) / 128, q.row_begin, q.best_score, q.best_row);
   BQ(cudaGetLastError());
+  return Q4GPU_OK;
+}
+
+int q4gpu_prefill_setup() {
+  int rc;
+  if ((rc = set_smem<kPfSub, kGemmQkv>()) || (rc = set_smem<kPfSub, kGemmO>()) ||
+      (rc = set_smem<kPfSub, kGemmGu>()) || (rc = set_smem<kPfSub, kGemmDown>()))
+    return rc;
+  BQ(cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmem));
+  return Q4GPU_OK;
+}
+
+int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
+  if (p.n_cols < 1 || p.n_cols > kPfBlock || p.n_tiles < 1 || p.n_tiles > kPfBlock)
+    return q4gpu_fail(Q4GPU_ERR_SHAPE, "prefill block of %d columns / %d tiles", p.n_cols, p.n_tiles);
+  constexpr int kRow = kQRows + 2 * kKvRows;
+  const size_t bt2_sub = (size_t)q4gpu_batch_limb_rows(kPfSub) * 2 * kHidden;
+  const int nsub = (p.n_cols + kPfSub - 1) / kPfSub;
+  auto ctx = [&](int sub) {
+    const int c0 = sub * kPfSub;
+    const int S = p.n_cols - c0 < kPfSub ? p.n_cols - c0 : kPfSub;
+    return BatchCtx{p.col_slots + c0, S, kPfSub, p.qkv + (size_t)c0 * kRow, p.bt1, p.bt2 + (size_t)sub * bt2_sub,
+                    p.bt3, nullptr, p.err, p.col_pos4 + 4 * c0, p.hidden + (size_t)c0 * kHidden,
+                    p.post + (size_t)c0 * kHidden, p.max_ctx, nullptr};
+  };
+  for (int sub = 0; sub < nsub; ++sub) {
+    const BatchCtx c = ctx(sub);
+    BQ(launch_pdl(batch_embed_kernel, dim3(c.S), dim3(256), 0, s, c, p.emb, p.semb));
+  }
+  for (int l = 0; l < p.n_layers; ++l) {
+    const BatchLayerW& w = p.layers[l];
+    for (int sub = 0; sub < nsub; ++sub) {
+      const BatchCtx c = ctx(sub);
+      BQ(launch_pdl(batch_norm_limbs_kernel, dim3(c.S), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
+      BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kRow, kHidden, kSplitQkv, nullptr, nullptr, s)));
+    }
+    BQ(launch_pdl(prefill_qk_kernel, dim3(kKvHeads, p.n_cols), dim3(128), 0, s, p.col_slots, p.col_pos4, p.qkv, l,
+                  w.g_q, w.g_k, p.cos_tab, p.sin_tab));
+    const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, bt2_sub, p.lut_idx, p.max_ctx, l, p.exp_lut, p.err};
+    BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(256), kPfSmem, s, a));
+    for (int sub = 0; sub < nsub; ++sub) {
+      const BatchCtx c = ctx(sub);
+      BQ((launch_gemm<kPfSub, kGemmO>(w.mo, p.mb2[sub], c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr,
+                                      s)));
+      BQ(launch_pdl(batch_norm_limbs_kernel, dim3(c.S), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
+      BQ((launch_gemm<kPfSub, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr,
+                                       s)));
+      BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr,
+                                         s)));
+    }
+  }
   return Q4GPU_OK;
 }
 

@@ -90,6 +90,58 @@ struct LmShardPlan {
   int* err;
 };
 
+// Batched exact prefill: prompt positions as columns (sequence-major).
+constexpr int kPfSub = 64;     // columns per GEMM (padded batch 64)
+constexpr int kPfBlock = 512;  // columns per attention launch (and per enqueued block)
+constexpr int kPfTileQ = 32;   // query positions per attention CTA (one sequence)
+constexpr int kPfKeys = 64;    // keys per staged attention chunk (one KV page)
+
+// Query tile of an attention launch: block columns [col0, col0 + nq), all of
+// one sequence, at positions pos0 .. pos0 + nq - 1.
+struct PfTile {
+  int32_t col0, nq, pos0, pad;
+};
+
+struct PfAttn {
+  const PfTile* tiles;
+  const SlotState* col_slots;  // [block columns] the column's sequence state
+  const int32_t* qkv;          // [block columns][4096]; q rows normed and roped
+  uint8_t* bt2;                // [block columns / 64][3 * 64 + 8][2048] limbs of the attention output
+  size_t bt2_sub;              // bytes per 64-column sub-batch of bt2
+  uint16_t* lut_idx;           // [block columns][16][max_ctx] exp-LUT indices (scratch)
+  int max_ctx;
+  int layer;
+  const int32_t* exp_lut;
+  int* err;
+};
+
+struct PrefillPlan {
+  alignas(64) CUtensorMap mb1;          // bt1 / bt3 (SP 64)
+  CUtensorMap mb3;
+  CUtensorMap mb2[kPfBlock / kPfSub];  // bt2 of each 64-column sub-batch
+  const SlotState* col_slots;  // [n_cols] this block's columns
+  const int32_t* col_pos4;     // [n_cols][4], position at [4 c]
+  const PfTile* tiles;         // [n_tiles], block-relative columns
+  int n_cols, n_tiles;
+  int32_t* hidden;  // [kPfBlock][1024]
+  int32_t* post;    // [kPfBlock][1024]
+  int32_t* qkv;     // [kPfBlock][4096]
+  uint8_t* bt1;     // [3 * 64 + 8][1024]
+  uint8_t* bt2;     // [kPfBlock / 64][3 * 64 + 8][2048]
+  uint8_t* bt3;     // [3 * 64 + 8][3072]
+  uint16_t* lut_idx;  // [kPfBlock][16][max_ctx]
+  const uint8_t* emb;
+  const uint16_t* semb;
+  const BatchLayerW* layers;
+  int n_layers;
+  int max_ctx;
+  const int32_t* cos_tab;
+  const int32_t* sin_tab;
+  const int32_t* exp_lut;
+  const int32_t* sig_lut;
+  int* err;
+};
+
 constexpr int kGemmTraceCtas = 1200;  // CTAs one GEMM launch can record (the LM head has 1187)
 
 }  // namespace q4
@@ -122,5 +174,11 @@ int q4gpu_batch_gather(const q4::SlotState* slots, int S, const int32_t* in, int
 int q4gpu_batch_set_positions(const q4::SlotState* slots, int S, int pos, int32_t* lm_from, int lm_value,
                               cudaStream_t s);
 int q4gpu_enqueue_lm_shard(const q4::LmShardPlan& q, cudaStream_t s);
+// kernel attributes of the prefill launches (once per process)
+int q4gpu_prefill_setup();
+// One block of prefill columns through every layer (embedding .. down_proj):
+// K/V of every column written to its sequence's cache.
+int q4gpu_enqueue_prefill_block(const q4::PrefillPlan& p, cudaStream_t s);
+
 // tokens / scores: device int64 [S]; stores them at position + 1 and advances positions
 int q4gpu_enqueue_batch_commit(const q4::BatchPlan& p, const int64_t* tokens, const int64_t* scores, cudaStream_t s);

@@ -500,6 +500,13 @@ struct q4gpu_model {
   uint8_t* b_lm_bt = nullptr;       // limb matrix of a vocabulary-shard LM head
   ArgBestD* b_lm_shard_part = nullptr;
   int b_lm_ones_sp = 0;
+  // batched exact prefill (q4gpu_batch_prefill)
+  int prefill_mode = 1;          // 1: batched prefill in q4gpu_decode_batch; 0: serial, position by position
+  PrefillPlan* pf = nullptr;     // buffers and TMA maps; per-block fields set per launch
+  SlotState* pf_cols = nullptr;  // [pf_cap] column -> its sequence's state
+  int32_t* pf_pos4 = nullptr;    // [pf_cap][4]
+  PfTile* pf_tiles = nullptr;    // [pf_tile_cap]
+  size_t pf_cap = 0, pf_tile_cap = 0;
 
   template <class T>
   int alloc(T** p, size_t count) {
@@ -954,6 +961,116 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   return Q4GPU_OK;
 }
 
+// Prefill buffers and maps, once per model (64-column GEMMs; ones rows at 3 * 64).
+int prefill_prepare(q4gpu_model* m) {
+  if (m->pf) return Q4GPU_OK;
+  int rc;
+  static bool attrs = false;
+  if (!attrs) {
+    if ((rc = q4gpu_prefill_setup())) return rc;
+    attrs = true;
+  }
+  auto p = std::make_unique<PrefillPlan>();
+  const size_t rows = (size_t)q4gpu_batch_limb_rows(kPfSub);
+  const uint32_t box = (uint32_t)q4gpu_batch_box_rows(kPfSub);
+  constexpr int nsub = kPfBlock / kPfSub;
+  if ((rc = m->alloc(&p->hidden, (size_t)kPfBlock * kHidden)) || (rc = m->alloc(&p->post, (size_t)kPfBlock * kHidden)) ||
+      (rc = m->alloc(&p->qkv, (size_t)kPfBlock * (kQRows + 2 * kKvRows))) ||
+      (rc = m->alloc(&p->bt1, rows * kHidden)) || (rc = m->alloc(&p->bt2, nsub * rows * 2 * kHidden)) ||
+      (rc = m->alloc(&p->bt3, rows * kInter)) ||
+      (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * m->cfg.max_context)))
+    return rc;
+  Q4_CUDA(cudaMemset(p->bt1 + 3 * kPfSub * kHidden, 1, (size_t)kBatchOnes * kHidden));
+  Q4_CUDA(cudaMemset(p->bt3 + 3 * kPfSub * kInter, 1, (size_t)kBatchOnes * kInter));
+  for (int sub = 0; sub < nsub; ++sub)
+    Q4_CUDA(cudaMemset(p->bt2 + (sub * rows + 3 * kPfSub) * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden));
+  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, rows, box)) ||
+      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, rows, box)))
+    return rc;
+  for (int sub = 0; sub < nsub; ++sub)
+    if ((rc = q4gpu_encode_u8_map(&p->mb2[sub], p->bt2 + sub * rows * 2 * kHidden, 2 * kHidden, rows, box)))
+      return rc;
+  p->emb = m->emb;
+  p->semb = m->semb;
+  p->layers = m->b_layers;
+  p->n_layers = m->cfg.n_layers;
+  p->max_ctx = m->cfg.max_context;
+  p->cos_tab = m->cos_tab;
+  p->sin_tab = m->sin_tab;
+  p->exp_lut = m->exp_lut;
+  p->sig_lut = m->sig_lut;
+  p->err = m->b_err;
+  m->pf = p.release();
+  return Q4GPU_OK;
+}
+
+// Prefill of slots [first, first + S): the tokens at positions 0 .. len - 2 of
+// each slot (already in the slot's token array) go through every layer as
+// columns of batched passes, leaving the K/V cache exactly as serial decode
+// steps over those positions would.  Positions are set to len - 1, so the next
+// batched step runs the last prompt token.  Stream-ordered on the model stream.
+int batch_prefill(q4gpu_model* m, int first, int S, const uint32_t* lens) {
+  int rc;
+  if ((rc = batch_prepare(m)) || (rc = prefill_prepare(m))) return rc;
+  std::vector<SlotState> cols;
+  std::vector<int32_t> pos4;
+  for (int i = 0; i < S; ++i) {
+    if (lens[i] < 1u || lens[i] > (uint32_t)m->cfg.max_context)
+      return q4gpu_fail(Q4GPU_ERR_ARG, "prefill length %u of slot %d", lens[i], first + i);
+    for (uint32_t q = 0; q + 1 < lens[i]; ++q) {
+      cols.push_back(m->slots[first + i]);
+      pos4.insert(pos4.end(), {(int32_t)q, 0, 0, 0});
+    }
+  }
+  const size_t n = cols.size();
+  // query tiles: runs of one sequence inside a block, at most kPfTileQ long
+  std::vector<PfTile> tiles;
+  std::vector<size_t> tile0;  // first tile of each block
+  for (size_t b0 = 0; b0 < n; b0 += kPfBlock) {
+    tile0.push_back(tiles.size());
+    const size_t b1 = std::min(n, b0 + (size_t)kPfBlock);
+    for (size_t c = b0; c < b1;) {
+      size_t e = c + 1;
+      while (e < b1 && e - c < (size_t)kPfTileQ && cols[e].tokens == cols[c].tokens) ++e;
+      tiles.push_back(PfTile{(int32_t)(c - b0), (int32_t)(e - c), pos4[4 * c], 0});
+      c = e;
+    }
+  }
+  tile0.push_back(tiles.size());
+  if (n > 0) {
+    if (n > m->pf_cap) {
+      size_t cap = std::max(n, (size_t)4096);
+      if ((rc = m->alloc(&m->pf_cols, cap)) || (rc = m->alloc(&m->pf_pos4, 4 * cap))) return rc;
+      m->pf_cap = cap;
+    }
+    if (tiles.size() > m->pf_tile_cap) {
+      size_t cap = std::max(tiles.size(), (size_t)1024);
+      if ((rc = m->alloc(&m->pf_tiles, cap))) return rc;
+      m->pf_tile_cap = cap;
+    }
+    // pageable sources: each copy returns once its data is staged
+    Q4_CUDA(cudaMemcpyAsync(m->pf_cols, cols.data(), n * sizeof(SlotState), cudaMemcpyHostToDevice, m->stream));
+    Q4_CUDA(cudaMemcpyAsync(m->pf_pos4, pos4.data(), 4 * n * sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+    Q4_CUDA(cudaMemcpyAsync(m->pf_tiles, tiles.data(), tiles.size() * sizeof(PfTile), cudaMemcpyHostToDevice,
+                            m->stream));
+    PrefillPlan& p = *m->pf;
+    for (size_t b = 0; b + 1 < tile0.size(); ++b) {
+      const size_t c0 = b * kPfBlock;
+      p.col_slots = m->pf_cols + c0;
+      p.col_pos4 = m->pf_pos4 + 4 * c0;
+      p.tiles = m->pf_tiles + tile0[b];
+      p.n_cols = (int)std::min((size_t)kPfBlock, n - c0);
+      p.n_tiles = (int)(tile0[b + 1] - tile0[b]);
+      if ((rc = q4gpu_enqueue_prefill_block(p, m->stream))) return rc;
+    }
+  }
+  for (int i = 0; i < S; ++i) {
+    const int32_t pos = (int32_t)lens[i] - 1;
+    Q4_CUDA(cudaMemcpyAsync(m->slots[first + i].pos, &pos, sizeof(int32_t), cudaMemcpyHostToDevice, m->stream));
+  }
+  return Q4GPU_OK;
+}
+
 int batch_check_error(q4gpu_model* m) {
   if (!m->b_err) return Q4GPU_OK;
   int e = 0;
@@ -1172,6 +1289,7 @@ void q4gpu_model_destroy(q4gpu_model* m) {
   for (auto e : m->done)
     if (e) cudaEventDestroy(e);
   for (void* p : m->allocs) cudaFree(p);
+  delete m->pf;
   if (m->h_res) cudaFreeHost(m->h_res);
   if (m->h_in) cudaFreeHost(m->h_in);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -1472,9 +1590,17 @@ int q4gpu_decode_batch(q4gpu_model* m, int32_t n_seq, const uint32_t* prompts, c
     }
     ok = ok &&
          cudaMemcpyAsync(m->b_lm_from + first, lm.data(), (size_t)S * 4, cudaMemcpyHostToDevice, m->stream) ==
-             cudaSuccess &&
-         q4gpu_batch_set_positions(m->b_slots + first, S, 0, m->b_lm_from + first, -1, m->stream) == Q4GPU_OK;
-    const uint32_t steps = longest + max_new_tokens - 1u;
+             cudaSuccess;
+    uint32_t steps;
+    if (m->prefill_mode == 1) {
+      // prompt positions 0 .. len - 2 as batched columns; then every sequence
+      // steps from its last prompt token
+      if (ok && batch_prefill(m, first, S, prompt_lens + first) != Q4GPU_OK) return QOT_ERR_STATUS;
+      steps = max_new_tokens;
+    } else {
+      ok = ok && q4gpu_batch_set_positions(m->b_slots + first, S, 0, m->b_lm_from + first, -1, m->stream) == Q4GPU_OK;
+      steps = longest + max_new_tokens - 1u;
+    }
     for (uint32_t i = 0; ok && i < steps; ++i) ok = cudaGraphLaunch(g, m->stream) == cudaSuccess;
     for (int i = 0; ok && i < S; ++i) {
       const int s = first + i;
@@ -1502,6 +1628,36 @@ int q4gpu_batch_steps(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t
   cudaGraphExec_t g;
   if ((rc = batch_graph(m, first_slot, n_seq, &g))) return rc;
   for (int i = 0; i < n_steps; ++i) Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  return Q4GPU_OK;
+}
+
+int q4gpu_batch_prefill(q4gpu_model* m, int32_t first_slot, int32_t n_seq, const uint32_t* prompts,
+                        const uint32_t* prompt_lens) {
+  if (!prompts || !prompt_lens) return q4gpu_fail(Q4GPU_ERR_ARG, "null prompts");
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  std::vector<int32_t> lm(n_seq);
+  size_t off = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    const uint32_t len = prompt_lens[i];
+    if (len < 1u || len > (uint32_t)m->cfg.max_context)
+      return q4gpu_fail(Q4GPU_ERR_ARG, "prompt %d: length %u outside 1..max_context", i, len);
+    for (uint32_t j = 0; j < len; ++j)
+      if (prompts[off + j] >= (uint32_t)m->cfg.vocab) return q4gpu_fail(Q4GPU_ERR_ARG, "prompt %d: bad token", i);
+    Q4_CUDA(cudaMemcpyAsync(m->slots[first_slot + i].tokens, prompts + off, (size_t)len * 4, cudaMemcpyHostToDevice,
+                            m->stream));
+    lm[i] = (int32_t)len;
+    off += len;
+  }
+  if ((rc = batch_prepare(m))) return rc;
+  Q4_CUDA(cudaMemcpyAsync(m->b_lm_from + first_slot, lm.data(), (size_t)n_seq * 4, cudaMemcpyHostToDevice,
+                          m->stream));
+  return batch_prefill(m, first_slot, n_seq, prompt_lens);
+}
+
+int q4gpu_model_set_prefill(q4gpu_model* m, int32_t mode) {
+  if (!m || mode < 0 || mode > 1) return q4gpu_fail(Q4GPU_ERR_ARG, "prefill mode must be 0 or 1");
+  m->prefill_mode = mode;
   return Q4GPU_OK;
 }
 

@@ -60,6 +60,7 @@ class Q4Model:
         _native.check(self.lib.q4gpu_model_create(C.byref(cfg), C.byref(h)), "q4gpu_model_create")
         self.handle = h
         self.n_layers, self.vocab, self.max_context, self.max_seqs = n_layers, vocab, max_context, max_seqs
+        self._prefill_mode = 1
         self.install_rope_tables()
 
     # -- lifecycle ---------------------------------------------------------
@@ -169,6 +170,25 @@ class Q4Model:
     def batch_steps(self, n_steps: int, n_seq: int, first_slot: int = 0) -> None:
         """Enqueue n batched steps for slots [first_slot, first_slot + n_seq) (async)."""
         _native.check(self.lib.q4gpu_batch_steps(self.handle, first_slot, n_seq, n_steps), "q4gpu_batch_steps")
+
+    def batch_prefill(self, prompts, first_slot: int = 0) -> None:
+        """Store the prompts in slots [first_slot, first_slot + len(prompts)) and prefill
+        positions 0 .. len - 2 of each as batched columns; every slot is left at its last
+        prompt token (position len - 1, lm_from len) for batch_steps (async)."""
+        lens = np.asarray([len(p) for p in prompts], dtype=np.uint32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.uint32) for p in prompts]))
+        _native.check(self.lib.q4gpu_batch_prefill(self.handle, first_slot, len(prompts), _ptr(flat), _ptr(lens)),
+                      "q4gpu_batch_prefill")
+
+    @property
+    def prefill_mode(self) -> int:
+        """How decode_batch runs prompts: 1 batched prefill (default), 0 serial steps."""
+        return self._prefill_mode
+
+    @prefill_mode.setter
+    def prefill_mode(self, value: int) -> None:
+        _native.check(self.lib.q4gpu_model_set_prefill(self.handle, value), "q4gpu_model_set_prefill")
+        self._prefill_mode = int(value)
 
     def batch_set_position(self, position: int, n_seq: int, first_slot: int = 0, lm_from: int = -1) -> None:
         _native.check(self.lib.q4gpu_batch_set_position(self.handle, first_slot, n_seq, position, lm_from),
