@@ -1130,26 +1130,36 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
 // Attention (prefill_attn_kernel): one CTA per (KV head, query tile of up to
 // 32 consecutive positions of one sequence), 64 query rows (the two heads of
 // the group).  The exact LUT softmax is done in three passes over 64-key
-// chunks staged in shared memory (padded rows, cp.async):
+// chunks of the cache (cp.async into a staging buffer, then converted to
+// double in padded shared-memory rows):
 //   1. scaled scores -> row maxima;
 //   2. scores again -> LUT indices (kept in a u16 scratch) and exp sums;
 //      then a probability table per row, prob[e] = (lut[e] << 16) / sum;
-//   3. values: sum over keys of prob[idx] * v in int64, then sat24(>> 16)
-//      as limbs of the o_proj input.
+//   3. values: sum over keys of prob[idx] * v, then sat24(>> 16) as limbs of
+//      the o_proj input.
+// The dot products run as double fused multiply-adds, which are exact here:
+// q, k and v are signed 24-bit (|x| <= 2^23), so every q k product is an
+// integer of magnitude <= 2^46 and a 128-term sum stays <= 2^53, where every
+// integer is a double and no fused multiply-add rounds; every p v product is
+// <= 2^39 in magnitude and the probabilities of a row sum to at most 2^16, so
+// the value sums stay <= 2^39.  The results are the integers the int64
+// decode kernels compute.
 // ---------------------------------------------------------------------------
-constexpr int kPfStride = kHeadDim + 4;  // padded shared-memory row (words): conflict-free 16-byte reads
-constexpr int kPfRows = 2 * kPfTileQ;    // query rows of a CTA
-constexpr int kPfChunkWords = kPfKeys * kPfStride;
-constexpr int kPfPbStride = kPfKeys + 4;
-constexpr size_t kPfTabBytes = (size_t)kPfRows * kExpLut * 4;  // >= the q rows' kPfRows * kPfStride * 4
-constexpr size_t kPfSmem = kPfTabBytes + 2 * (size_t)kPfChunkWords * 4 + (size_t)kPfRows * kPfPbStride * 4;
-static_assert((size_t)kPfRows * kPfStride * 4 <= kPfTabBytes, "q rows alias the probability table");
+constexpr int kPfStride = kHeadDim + 4;   // staged int32 key row (words): 16-byte aligned rows
+constexpr int kPfDStride = kHeadDim + 2;  // double row: consecutive rows 4 banks apart
+constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA
+constexpr int kPfPbStride = kPfKeys + 2;  // double row of the staged probabilities
+constexpr size_t kPfRowsBytes = (size_t)kPfRows * kPfDStride * 8;   // q rows; the probability table in pass 3
+constexpr size_t kPfKeysBytes = (size_t)kPfKeys * kPfDStride * 8;   // one chunk of keys or values as double
+constexpr size_t kPfStageBytes = (size_t)kPfKeys * kPfStride * 4;   // one chunk as staged int32
+constexpr size_t kPfSmem = kPfRowsBytes + kPfKeysBytes + kPfStageBytes + (size_t)kPfRows * kPfPbStride * 8;
+static_assert((size_t)kPfRows * kExpLut * 4 <= kPfRowsBytes, "the probability table aliases the q rows");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // q (kind 0) or k (kind 1) head row -> RMSNorm (head constants) -> RoPE at
 // `pos`, by one warp: lane owns elements 4 lane .. 4 lane + 3, the rotation
@@ -1208,10 +1218,11 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
 
 __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   extern __shared__ __align__(16) uint8_t pf_smem[];
-  int32_t* qs = reinterpret_cast<int32_t*>(pf_smem);     // [64][kPfStride] q rows (passes 1-2)
+  double* qd = reinterpret_cast<double*>(pf_smem);        // [64][kPfDStride] q rows (passes 1-2)
   uint32_t* ptab = reinterpret_cast<uint32_t*>(pf_smem);  // [64][257] probability table (pass 3)
-  int32_t* ring = reinterpret_cast<int32_t*>(pf_smem + kPfTabBytes);  // 2 x [64][kPfStride]
-  uint32_t* pb = reinterpret_cast<uint32_t*>(pf_smem + kPfTabBytes + 2 * (size_t)kPfChunkWords * 4);
+  double* kd = reinterpret_cast<double*>(pf_smem + kPfRowsBytes);  // [64][kPfDStride] keys / values
+  int32_t* stg = reinterpret_cast<int32_t*>(pf_smem + kPfRowsBytes + kPfKeysBytes);  // [64][kPfStride]
+  double* pb = reinterpret_cast<double*>(pf_smem + kPfRowsBytes + kPfKeysBytes + kPfStageBytes);  // [64][kPfPbStride]
   __shared__ int32_t elut[kExpLut];
   __shared__ int64_t rmax[kPfRows], rsum[kPfRows];
   grid_dep_wait();
@@ -1222,60 +1233,67 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   const KvView kvv = a.col_slots[tl.col0].kv;
   const int kend = tl.pos0 + tl.nq;  // keys 0 .. kend - 1
   const int nch = (kend + kPfKeys - 1) / kPfKeys;
+  auto keys_in = [&](int c) { return kend - c * kPfKeys < kPfKeys ? kend - c * kPfKeys : kPfKeys; };
 
-  // chunk c of K (kind 0) or V (kind 1) into ring buffer c & 1; one commit
-  // group per call, empty past the end, so wait_group 1 always means "chunk c
-  // has landed" when chunks c and c + 1 were the last two issued
-  auto issue = [&](int kind, int c) {
+  // chunk c of K (kind 0) or V (kind 1) into the staging buffer (one commit group)
+  auto stage = [&](int kind, int c) {
     if (c < nch) {
-      const int j0 = c * kPfKeys;
-      const int n = kend - j0 < kPfKeys ? kend - j0 : kPfKeys;
-      const int32_t* src = kvv.at(a.layer, kind, kv, j0);  // a 64-aligned chunk is one page
-      int32_t* dst = ring + (c & 1) * kPfChunkWords;
+      const int n = keys_in(c);
+      const int32_t* src = kvv.at(a.layer, kind, kv, c * kPfKeys);  // a 64-aligned chunk is one page
       for (int i = t; i < n * (kHeadDim / 4); i += 256) {
         const int j = i >> 5, d4 = i & 31;
-        cp_async16(dst + j * kPfStride + 4 * d4, src + (size_t)j * kHeadDim + 4 * d4);
+        cp_async16(stg + j * kPfStride + 4 * d4, src + (size_t)j * kHeadDim + 4 * d4);
       }
     }
     cp_async_commit();
   };
-  issue(0, 0);
-  issue(0, 1);
+  // staged chunk c -> doubles in kd
+  auto convert = [&](int c) {
+    const int n = keys_in(c);
+    for (int i = t; i < n * (kHeadDim / 4); i += 256) {
+      const int j = i >> 5, d4 = i & 31;
+      const int4 v = *reinterpret_cast<const int4*>(stg + j * kPfStride + 4 * d4);
+      double2* dst = reinterpret_cast<double2*>(kd + j * kPfDStride + 4 * d4);
+      dst[0] = make_double2((double)v.x, (double)v.y);
+      dst[1] = make_double2((double)v.z, (double)v.w);
+    }
+  };
+  stage(0, 0);
   for (int i = t; i < kPfRows * (kHeadDim / 4); i += 256) {
     const int r = i >> 5, d4 = i & 31, hh = r / kPfTileQ, qi = r % kPfTileQ;
     int4 v = make_int4(0, 0, 0, 0);
     if (qi < tl.nq)
       v = *reinterpret_cast<const int4*>(a.qkv + (size_t)(tl.col0 + qi) * (kQRows + 2 * kKvRows) +
                                          (2 * kv + hh) * kHeadDim + 4 * d4);
-    *reinterpret_cast<int4*>(qs + r * kPfStride + 4 * d4) = v;
+    double2* dst = reinterpret_cast<double2*>(qd + r * kPfDStride + 4 * d4);
+    dst[0] = make_double2((double)v.x, (double)v.y);
+    dst[1] = make_double2((double)v.z, (double)v.w);
   }
   for (int i = t; i < kExpLut; i += 256) elut[i] = a.exp_lut[i];
 
-  // scores of this thread's rows 4 rg + e and keys kg + 16 u of a staged chunk
-  auto scores = [&](const int32_t* kb, int64_t (&acc)[4][4]) {
+  // raw scores of this thread's rows 4 rg + e and keys kg + 16 u of the chunk in kd
+  auto scores = [&](int64_t (&raw)[4][4]) {
+    double acc[4][4];
 #pragma unroll
     for (int e = 0; e < 4; ++e)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) acc[e][u] = 0;
-#pragma unroll 2
-    for (int d = 0; d < kHeadDim; d += 4) {
-      int4 q[4], k[4];
+      for (int u = 0; u < 4; ++u) acc[e][u] = 0.0;
+#pragma unroll 4
+    for (int d = 0; d < kHeadDim; d += 2) {
+      double2 q[4], k[4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) q[e] = *reinterpret_cast<const int4*>(qs + (4 * rg + e) * kPfStride + d);
+      for (int e = 0; e < 4; ++e) q[e] = *reinterpret_cast<const double2*>(qd + (4 * rg + e) * kPfDStride + d);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) k[u] = *reinterpret_cast<const int4*>(kb + (kg + 16 * u) * kPfStride + d);
+      for (int u = 0; u < 4; ++u) k[u] = *reinterpret_cast<const double2*>(kd + (kg + 16 * u) * kPfDStride + d);
 #pragma unroll
       for (int e = 0; e < 4; ++e)
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          int64_t s = acc[e][u];
-          s = mad_wide(q[e].x, k[u].x, s);
-          s = mad_wide(q[e].y, k[u].y, s);
-          s = mad_wide(q[e].z, k[u].z, s);
-          s = mad_wide(q[e].w, k[u].w, s);
-          acc[e][u] = s;
-        }
+        for (int u = 0; u < 4; ++u) acc[e][u] = fma(q[e].y, k[u].y, fma(q[e].x, k[u].x, acc[e][u]));
     }
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) raw[e][u] = (int64_t)acc[e][u];
   };
   // row r = hh * 32 + qi is query position pos0 + qi; key j is valid for it when j <= pos0 + qi
   auto valid = [&](int e, int j) {
@@ -1286,23 +1304,23 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   // pass 1: row maxima
   int64_t mx[4] = {INT64_MIN, INT64_MIN, INT64_MIN, INT64_MIN};
   for (int c = 0; c < nch; ++c) {
-    cp_async_wait1();
+    cp_async_wait0();
+    __syncthreads();  // chunk c staged; the previous chunk's scores are done
+    convert(c);
     __syncthreads();
-    int64_t acc[4][4];
-    scores(ring + (c & 1) * kPfChunkWords, acc);
+    stage(0, c + 1);
+    int64_t raw[4][4];
+    scores(raw);
 #pragma unroll
     for (int e = 0; e < 4; ++e)
 #pragma unroll
       for (int u = 0; u < 4; ++u)
         if (valid(e, c * kPfKeys + kg + 16 * u)) {
-          const int64_t s = scale_score(acc[e][u], kScoreScale);
+          const int64_t s = scale_score(raw[e][u], kScoreScale);
           mx[e] = s > mx[e] ? s : mx[e];
         }
-    __syncthreads();
-    issue(0, c + 2);
   }
-  issue(0, 0);  // pass 2 streams K again
-  issue(0, 1);
+  stage(0, 0);  // pass 2 streams K again
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
 #pragma unroll
@@ -1324,26 +1342,26 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     idx_row[e] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.max_ctx;
   }
   for (int c = 0; c < nch; ++c) {
-    cp_async_wait1();
+    cp_async_wait0();
     __syncthreads();
-    int64_t acc[4][4];
-    scores(ring + (c & 1) * kPfChunkWords, acc);
+    convert(c);
+    __syncthreads();
+    stage(0, c + 1);
+    int64_t raw[4][4];
+    scores(raw);
 #pragma unroll
     for (int e = 0; e < 4; ++e)
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int j = c * kPfKeys + kg + 16 * u;
         if (valid(e, j)) {
-          const int ix = lut_index(rmx[e], scale_score(acc[e][u], kScoreScale));
+          const int ix = lut_index(rmx[e], scale_score(raw[e][u], kScoreScale));
           sm[e] += elut[ix];
           idx_row[e][j] = (uint16_t)ix;
         }
       }
-    __syncthreads();
-    issue(0, c + 2);
   }
-  issue(1, 0);  // pass 3 streams V
-  issue(1, 1);
+  stage(1, 0);  // pass 3 streams V
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
 #pragma unroll
@@ -1357,15 +1375,16 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     ptab[i] = s > 0 ? (uint32_t)udiv_exact((uint64_t)elut[e] << 16, (uint64_t)s) : 0u;
   }
   // pass 3: probability-weighted values.  Thread (rg, kg) owns output rows
-  // 4 rg + e and dims 4 kg + f, 64 + 4 kg + f.
-  int64_t o[4][8];
+  // 4 rg + e and dims 32 i + 2 kg + {0, 1}, i = 0..3.
+  double o[4][8];
 #pragma unroll
   for (int e = 0; e < 4; ++e)
 #pragma unroll
-    for (int f = 0; f < 8; ++f) o[e][f] = 0;
+    for (int f = 0; f < 8; ++f) o[e][f] = 0.0;
   for (int c = 0; c < nch; ++c) {
-    cp_async_wait1();
+    cp_async_wait0();
     __syncthreads();  // also orders the table writes before the first lookups
+    convert(c);
 #pragma unroll
     for (int e = 0; e < 4; ++e)
 #pragma unroll
@@ -1373,25 +1392,23 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
         const int jj = kg + 16 * u, j = c * kPfKeys + jj;
         uint32_t p = 0;
         if (valid(e, j)) p = ptab[(4 * rg + e) * kExpLut + idx_row[e][j]];
-        pb[(4 * rg + e) * kPfPbStride + jj] = p;
+        pb[(4 * rg + e) * kPfPbStride + jj] = (double)p;
       }
     __syncthreads();
-    const int32_t* vb = ring + (c & 1) * kPfChunkWords;
-    const int n = kend - c * kPfKeys < kPfKeys ? kend - c * kPfKeys : kPfKeys;
+    stage(1, c + 1);
+    const int n = keys_in(c);
 #pragma unroll 2
     for (int jj = 0; jj < n; ++jj) {
-      const int4 v0 = *reinterpret_cast<const int4*>(vb + jj * kPfStride + 4 * kg);
-      const int4 v1 = *reinterpret_cast<const int4*>(vb + jj * kPfStride + 64 + 4 * kg);
-      const int32_t vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      const double2* vrow = reinterpret_cast<const double2*>(kd + jj * kPfDStride);
+      const double2 v0 = vrow[kg], v1 = vrow[16 + kg], v2 = vrow[32 + kg], v3 = vrow[48 + kg];
+      const double vv[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int32_t p = (int32_t)pb[(4 * rg + e) * kPfPbStride + jj];
+        const double p = pb[(4 * rg + e) * kPfPbStride + jj];
 #pragma unroll
-        for (int f = 0; f < 8; ++f) o[e][f] = mad_wide(p, vv[f], o[e][f]);
+        for (int f = 0; f < 8; ++f) o[e][f] = fma(p, vv[f], o[e][f]);
       }
     }
-    __syncthreads();
-    issue(1, c + 2);
   }
   // outputs as limbs of the o_proj input (64-column sub-batches, SP = 64)
 #pragma unroll
@@ -1402,8 +1419,9 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
 #pragma unroll
     for (int f = 0; f < 8; ++f) {
-      const int d = (f < 4 ? 4 * kg + f : 64 + 4 * kg + f - 4);
-      write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d, sat24(o[e][f] >> 16));
+      const int d = 32 * (f >> 1) + 2 * kg + (f & 1);
+      write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d,
+                  sat24((int64_t)o[e][f] >> 16));
     }
   }
 }
