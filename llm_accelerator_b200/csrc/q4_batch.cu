@@ -1130,34 +1130,66 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
 // Attention (prefill_attn_kernel): one CTA per (KV head, query tile of up to
 // 32 consecutive positions of one sequence), 64 query rows (the two heads of
 // the group).  The exact LUT softmax is done in three passes over 64-key
-// chunks of the cache (cp.async into a staging buffer, then converted to
-// double in padded shared-memory rows):
+// chunks of the cache (cp.async into a staging buffer, then re-laid out in
+// padded shared-memory rows):
 //   1. scaled scores -> row maxima;
 //   2. scores again -> LUT indices (kept in a u16 scratch) and exp sums;
 //      then a probability table per row, prob[e] = (lut[e] << 16) / sum;
 //   3. values: sum over keys of prob[idx] * v, then sat24(>> 16) as limbs of
 //      the o_proj input.
-// The dot products run as double fused multiply-adds, which are exact here:
-// q, k and v are signed 24-bit (|x| <= 2^23), so every q k product is an
-// integer of magnitude <= 2^46 and a 128-term sum stays <= 2^53, where every
-// integer is a double and no fused multiply-add rounds; every p v product is
-// <= 2^39 in magnitude and the probabilities of a row sum to at most 2^16, so
-// the value sums stay <= 2^39.  The results are the integers the int64
-// decode kernels compute.
+// Scores run on the tensor cores (mma.sync m16n8k32, 8-bit): q and k are
+// signed 24-bit, split into byte limbs x = x0 + 2^8 x1 + 2^16 x2 (x0, x1
+// unsigned, x2 signed), and
+//   q k = sum_{a,b} 2^(8 (a + b)) qa kb
+// takes nine limb products per tile, accumulated by shift into five int32
+// sums (each below 3 * 128 * 255^2 in magnitude) and combined in int64.
+// Values likewise: p (0 .. 2^16) = p0 + 2^8 p1 + 2^16 p2 with p2 in {0, 1}
+// (its three products are skipped for chunks where no p reaches 2^16), v in
+// byte limbs, five int32 sums per 64-key chunk folded into int64.  The
+// results are the integers the int64 decode kernels compute.
 // ---------------------------------------------------------------------------
 constexpr int kPfStride = kHeadDim + 4;   // staged int32 key row (words): 16-byte aligned rows
-constexpr int kPfDStride = kHeadDim + 2;  // double row: consecutive rows 4 banks apart
 constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA
-constexpr int kPfPbStride = kPfKeys + 2;  // double row of the staged probabilities
-constexpr size_t kPfRowsBytes = (size_t)kPfRows * kPfDStride * 8;   // q rows; the probability table in pass 3
-constexpr size_t kPfKeysBytes = (size_t)kPfKeys * kPfDStride * 8;   // one chunk of keys or values as double
+constexpr int kPfLStride = kHeadDim + 16;  // byte-limb row: rows 4 banks apart for the fragment loads
+constexpr size_t kPfLimbBytes = (size_t)3 * 64 * kPfLStride;       // three limb planes of 64 rows
+constexpr size_t kPfRowsBytes = (size_t)kPfRows * kExpLut * 4;      // q and key limbs (passes 1-2) / probability table
+constexpr int kPfTStride = kPfKeys + 16;  // byte-limb row of the transposed values / probabilities (20 words)
+constexpr size_t kPfVtBytes = (size_t)3 * kHeadDim * kPfTStride;  // value limbs [3][128 dims][64 keys]
+constexpr size_t kPfPlBytes = (size_t)3 * kPfRows * kPfTStride;   // probability limbs [3][64 rows][64 keys]
 constexpr size_t kPfStageBytes = (size_t)kPfKeys * kPfStride * 4;   // one chunk as staged int32
-constexpr size_t kPfSmem = kPfRowsBytes + kPfKeysBytes + kPfStageBytes + (size_t)kPfRows * kPfPbStride * 8;
-static_assert((size_t)kPfRows * kExpLut * 4 <= kPfRowsBytes, "the probability table aliases the q rows");
+constexpr size_t kPfSmem = kPfRowsBytes + kPfVtBytes + kPfPlBytes + kPfStageBytes;
+static_assert(2 * kPfLimbBytes <= kPfRowsBytes, "q and key limbs share the probability table's space");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
 }
+// D += A B, mma.sync m16n8k32 on 8-bit operands, signed (s8) or unsigned (u8) per operand
+template <bool SA, bool SB>
+__device__ __forceinline__ void mma_limb(int32_t (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+#define PF_MMA(TA, TB)                                                                                     \
+  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB ".s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, " \
+               "{%8,%9}, {%0,%1,%2,%3};"                                                                   \
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])                                            \
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]))
+  if constexpr (!SA && !SB)
+    PF_MMA("u8", "u8");
+  else if constexpr (!SA && SB)
+    PF_MMA("u8", "s8");
+  else if constexpr (SA && !SB)
+    PF_MMA("s8", "u8");
+  else
+    PF_MMA("s8", "s8");
+#undef PF_MMA
+}
+
+// byte `l` of each of four words, packed (the limb l of four elements)
+__device__ __forceinline__ uint32_t limb_word(int4 v, int l) {
+  const uint32_t sel = (uint32_t)l | ((uint32_t)(l + 4) << 4);
+  const uint32_t lo = __byte_perm((uint32_t)v.x, (uint32_t)v.y, sel);
+  const uint32_t hi = __byte_perm((uint32_t)v.z, (uint32_t)v.w, sel);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
@@ -1218,18 +1250,20 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
 
 __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   extern __shared__ __align__(16) uint8_t pf_smem[];
-  double* qd = reinterpret_cast<double*>(pf_smem);        // [64][kPfDStride] q rows (passes 1-2)
+  uint8_t* qL = pf_smem;                                  // [3][64][kPfLStride] q limbs (passes 1-2)
+  uint8_t* kL = pf_smem + kPfLimbBytes;                   // [3][64][kPfLStride] key limbs (passes 1-2)
   uint32_t* ptab = reinterpret_cast<uint32_t*>(pf_smem);  // [64][257] probability table (pass 3)
-  double* kd = reinterpret_cast<double*>(pf_smem + kPfRowsBytes);  // [64][kPfDStride] keys / values
-  int32_t* stg = reinterpret_cast<int32_t*>(pf_smem + kPfRowsBytes + kPfKeysBytes);  // [64][kPfStride]
-  double* pb = reinterpret_cast<double*>(pf_smem + kPfRowsBytes + kPfKeysBytes + kPfStageBytes);  // [64][kPfPbStride]
+  uint8_t* vT = pf_smem + kPfRowsBytes;                    // [3][128][kPfTStride] value limbs, key-contiguous (pass 3)
+  uint8_t* pL = pf_smem + kPfRowsBytes + kPfVtBytes;       // [3][64][kPfTStride] probability limbs (pass 3)
+  int32_t* stg = reinterpret_cast<int32_t*>(pf_smem + kPfRowsBytes + kPfVtBytes + kPfPlBytes);  // [64][kPfStride]
   __shared__ int32_t elut[kExpLut];
+  __shared__ int64_t rred[2][kPfRows];  // per key half: row maxima, then row sums
   __shared__ int64_t rmax[kPfRows], rsum[kPfRows];
   grid_dep_wait();
   grid_dep_launch();
   const int kv = blockIdx.x;
   const PfTile tl = a.tiles[blockIdx.y];
-  const int t = threadIdx.x, rg = t >> 4, kg = t & 15;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const KvView kvv = a.col_slots[tl.col0].kv;
   const int kend = tl.pos0 + tl.nq;  // keys 0 .. kend - 1
   const int nch = (kend + kPfKeys - 1) / kPfKeys;
@@ -1247,17 +1281,6 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     }
     cp_async_commit();
   };
-  // staged chunk c -> doubles in kd
-  auto convert = [&](int c) {
-    const int n = keys_in(c);
-    for (int i = t; i < n * (kHeadDim / 4); i += 256) {
-      const int j = i >> 5, d4 = i & 31;
-      const int4 v = *reinterpret_cast<const int4*>(stg + j * kPfStride + 4 * d4);
-      double2* dst = reinterpret_cast<double2*>(kd + j * kPfDStride + 4 * d4);
-      dst[0] = make_double2((double)v.x, (double)v.y);
-      dst[1] = make_double2((double)v.z, (double)v.w);
-    }
-  };
   stage(0, 0);
   for (int i = t; i < kPfRows * (kHeadDim / 4); i += 256) {
     const int r = i >> 5, d4 = i & 31, hh = r / kPfTileQ, qi = r % kPfTileQ;
@@ -1265,164 +1288,269 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     if (qi < tl.nq)
       v = *reinterpret_cast<const int4*>(a.qkv + (size_t)(tl.col0 + qi) * (kQRows + 2 * kKvRows) +
                                          (2 * kv + hh) * kHeadDim + 4 * d4);
-    double2* dst = reinterpret_cast<double2*>(qd + r * kPfDStride + 4 * d4);
-    dst[0] = make_double2((double)v.x, (double)v.y);
-    dst[1] = make_double2((double)v.z, (double)v.w);
+#pragma unroll
+    for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(qL + (l * 64 + r) * kPfLStride + 4 * d4) = limb_word(v, l);
   }
   for (int i = t; i < kExpLut; i += 256) elut[i] = a.exp_lut[i];
 
-  // raw scores of this thread's rows 4 rg + e and keys kg + 16 u of the chunk in kd
-  auto scores = [&](int64_t (&raw)[4][4]) {
-    double acc[4][4];
+  // Scores: warp (mt, kh) takes rows 16 mt .. +15 and keys 32 kh .. +31 of the
+  // chunk (four 8-key MMA tiles).  Lane (g, tig) ends up with rows
+  // ra = 16 mt + g and ra + 8, keys 32 kh + 8 nt + 2 tig + h (nt 0..3, h 0..1).
+  const int mt = warp & 3, kh = warp >> 2, g = lane >> 2, tig = lane & 3;
+  const int ra = 16 * mt + g;
+  auto key_of = [&](int nt, int h) { return 32 * kh + 8 * nt + 2 * tig + h; };
+  auto scores = [&](int64_t (&raw)[2][8]) {
+    int32_t acc[5][4][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+    for (int s = 0; s < 5; ++s)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) acc[e][u] = 0.0;
-#pragma unroll 4
-    for (int d = 0; d < kHeadDim; d += 2) {
-      double2 q[4], k[4];
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) q[e] = *reinterpret_cast<const double2*>(qd + (4 * rg + e) * kPfDStride + d);
+        for (int i = 0; i < 4; ++i) acc[s][nt][i] = 0;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) k[u] = *reinterpret_cast<const double2*>(kd + (kg + 16 * u) * kPfDStride + d);
+    for (int ks = 0; ks < kHeadDim / 32; ++ks) {
+      const int k0 = 32 * ks + 4 * tig;
+      uint32_t A[3][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
+      for (int l = 0; l < 3; ++l) {
+        const uint8_t* q0 = qL + (l * 64 + ra) * kPfLStride + k0;
+        A[l][0] = *reinterpret_cast<const uint32_t*>(q0);
+        A[l][1] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride);
+        A[l][2] = *reinterpret_cast<const uint32_t*>(q0 + 16);
+        A[l][3] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride + 16);
+      }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) acc[e][u] = fma(q[e].y, k[u].y, fma(q[e].x, k[u].x, acc[e][u]));
+      for (int nt = 0; nt < 4; ++nt) {
+        uint32_t B[3][2];
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+          const uint8_t* k = kL + (l * 64 + 32 * kh + 8 * nt + g) * kPfLStride + k0;
+          B[l][0] = *reinterpret_cast<const uint32_t*>(k);
+          B[l][1] = *reinterpret_cast<const uint32_t*>(k + 16);
+        }
+        mma_limb<false, false>(acc[0][nt], A[0], B[0]);
+        mma_limb<false, false>(acc[1][nt], A[0], B[1]);
+        mma_limb<false, false>(acc[1][nt], A[1], B[0]);
+        mma_limb<false, true>(acc[2][nt], A[0], B[2]);
+        mma_limb<false, false>(acc[2][nt], A[1], B[1]);
+        mma_limb<true, false>(acc[2][nt], A[2], B[0]);
+        mma_limb<false, true>(acc[3][nt], A[1], B[2]);
+        mma_limb<true, false>(acc[3][nt], A[2], B[1]);
+        mma_limb<true, true>(acc[4][nt], A[2], B[2]);
+      }
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+    for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) raw[e][u] = (int64_t)acc[e][u];
+      for (int i = 0; i < 4; ++i)
+        raw[i >> 1][2 * nt + (i & 1)] = (int64_t)acc[0][nt][i] + (int64_t)acc[1][nt][i] * 256 +
+                                        (int64_t)acc[2][nt][i] * 65536 + (int64_t)acc[3][nt][i] * 16777216 +
+                                        (int64_t)acc[4][nt][i] * 4294967296LL;
+  };
+  // staged chunk -> key limbs
+  auto key_limbs = [&](int c) {
+    const int n = keys_in(c);
+    for (int i = t; i < n * (kHeadDim / 4); i += 256) {
+      const int j = i >> 5, d4 = i & 31;
+      const int4 v = *reinterpret_cast<const int4*>(stg + j * kPfStride + 4 * d4);
+#pragma unroll
+      for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(kL + (l * 64 + j) * kPfLStride + 4 * d4) = limb_word(v, l);
+    }
   };
   // row r = hh * 32 + qi is query position pos0 + qi; key j is valid for it when j <= pos0 + qi
-  auto valid = [&](int e, int j) {
-    const int qi = (4 * rg + e) % kPfTileQ;
+  auto valid = [&](int r, int j) {
+    const int qi = r % kPfTileQ;
     return qi < tl.nq && j <= tl.pos0 + qi;
   };
 
   // pass 1: row maxima
-  int64_t mx[4] = {INT64_MIN, INT64_MIN, INT64_MIN, INT64_MIN};
+  int64_t mx[2] = {INT64_MIN, INT64_MIN};
   for (int c = 0; c < nch; ++c) {
     cp_async_wait0();
     __syncthreads();  // chunk c staged; the previous chunk's scores are done
-    convert(c);
+    key_limbs(c);
     __syncthreads();
     stage(0, c + 1);
-    int64_t raw[4][4];
+    int64_t raw[2][8];
     scores(raw);
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (valid(e, c * kPfKeys + kg + 16 * u)) {
-          const int64_t s = scale_score(raw[e][u], kScoreScale);
-          mx[e] = s > mx[e] ? s : mx[e];
-        }
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          if (valid(ra + 8 * i, c * kPfKeys + key_of(nt, h))) {
+            const int64_t s = scale_score(raw[i][2 * nt + h], kScoreScale);
+            mx[i] = s > mx[i] ? s : mx[i];
+          }
   }
   stage(0, 0);  // pass 2 streams K again
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
+  for (int i = 0; i < 2; ++i) {
 #pragma unroll
-    for (int msk = 1; msk < 16; msk <<= 1) {
-      const int64_t o = shfl_xor_i64(mx[e], msk);
-      mx[e] = o > mx[e] ? o : mx[e];
+    for (int msk = 1; msk < 4; msk <<= 1) {
+      const int64_t o = shfl_xor_i64(mx[i], msk);
+      mx[i] = o > mx[i] ? o : mx[i];
     }
-    if (kg == 0) rmax[4 * rg + e] = mx[e];
+    if (tig == 0) rred[kh][ra + 8 * i] = mx[i];
   }
   __syncthreads();
+  if (t < kPfRows) rmax[t] = rred[0][t] > rred[1][t] ? rred[0][t] : rred[1][t];
+  __syncthreads();
   // pass 2: LUT indices and exp sums
-  int64_t sm[4] = {0, 0, 0, 0};
-  const int64_t rmx[4] = {rmax[4 * rg], rmax[4 * rg + 1], rmax[4 * rg + 2], rmax[4 * rg + 3]};
-  uint16_t* idx_row[4];
+  int64_t sm[2] = {0, 0};
+  const int64_t rmx[2] = {rmax[ra], rmax[ra + 8]};
+  uint16_t* idx_row[2];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int r = 4 * rg + e, hh = r / kPfTileQ, qi = r % kPfTileQ;
+  for (int i = 0; i < 2; ++i) {
+    const int r = ra + 8 * i, hh = r / kPfTileQ, qi = r % kPfTileQ;
     const int col = tl.col0 + (qi < tl.nq ? qi : 0);
-    idx_row[e] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.max_ctx;
+    idx_row[i] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.max_ctx;
   }
   for (int c = 0; c < nch; ++c) {
     cp_async_wait0();
     __syncthreads();
-    convert(c);
+    key_limbs(c);
     __syncthreads();
     stage(0, c + 1);
-    int64_t raw[4][4];
+    int64_t raw[2][8];
     scores(raw);
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+    for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = c * kPfKeys + kg + 16 * u;
-        if (valid(e, j)) {
-          const int ix = lut_index(rmx[e], scale_score(raw[e][u], kScoreScale));
-          sm[e] += elut[ix];
-          idx_row[e][j] = (uint16_t)ix;
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = c * kPfKeys + key_of(nt, h);
+          if (valid(ra + 8 * i, j)) {
+            const int ix = lut_index(rmx[i], scale_score(raw[i][2 * nt + h], kScoreScale));
+            sm[i] += elut[ix];
+            idx_row[i][j] = (uint16_t)ix;
+          }
         }
-      }
   }
   stage(1, 0);  // pass 3 streams V
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
+  for (int i = 0; i < 2; ++i) {
 #pragma unroll
-    for (int msk = 1; msk < 16; msk <<= 1) sm[e] += shfl_xor_i64(sm[e], msk);
-    if (kg == 0) rsum[4 * rg + e] = sm[e];
+    for (int msk = 1; msk < 4; msk <<= 1) sm[i] += shfl_xor_i64(sm[i], msk);
+    if (tig == 0) rred[kh][ra + 8 * i] = sm[i];
   }
-  __syncthreads();  // q rows are dead: the table takes their place
+  __syncthreads();  // the limbs are dead: the table takes their place
+  if (t < kPfRows) rsum[t] = rred[0][t] + rred[1][t];
+  __syncthreads();
   for (int i = t; i < kPfRows * kExpLut; i += 256) {
     const int r = i / kExpLut, e = i - r * kExpLut;
     const int64_t s = rsum[r];
     ptab[i] = s > 0 ? (uint32_t)udiv_exact((uint64_t)elut[e] << 16, (uint64_t)s) : 0u;
   }
-  // pass 3: probability-weighted values.  Thread (rg, kg) owns output rows
-  // 4 rg + e and dims 32 i + 2 kg + {0, 1}, i = 0..3.
-  double o[4][8];
+  // pass 3: probability-weighted values.  Warp (mt, dh) takes output rows
+  // 16 mt .. +15 and dims 64 dh .. +63 (eight 8-dim MMA tiles, two batches of
+  // four); lane (g, tig) holds rows ra, ra + 8 and dims 64 dh + 8 n + 2 tig + {0, 1}.
+  const int dh = kh;
+  int64_t tot[8][4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e)
+  for (int n = 0; n < 8; ++n)
 #pragma unroll
-    for (int f = 0; f < 8; ++f) o[e][f] = 0.0;
+    for (int i = 0; i < 4; ++i) tot[n][i] = 0;
   for (int c = 0; c < nch; ++c) {
     cp_async_wait0();
-    __syncthreads();  // also orders the table writes before the first lookups
-    convert(c);
+    __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
+    // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
+    for (int i = t; i < kHeadDim * (kPfKeys / 4); i += 256) {
+      const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;  // 8 dims x 4 key groups per warp
+      const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
+      const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
+                               stg[(4 * jg + 2) * kPfStride + dd], stg[(4 * jg + 3) * kPfStride + dd]);
 #pragma unroll
-    for (int e = 0; e < 4; ++e)
+      for (int l = 0; l < 3; ++l)
+        *reinterpret_cast<uint32_t*>(vT + (l * kHeadDim + dd) * kPfTStride + 4 * jg) = limb_word(v, l);
+    }
+    // probability limbs of this thread's (row, key) pairs of the score layout
+    int big = 0;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int jj = kg + 16 * u, j = c * kPfKeys + jj;
-        uint32_t p = 0;
-        if (valid(e, j)) p = ptab[(4 * rg + e) * kExpLut + idx_row[e][j]];
-        pb[(4 * rg + e) * kPfPbStride + jj] = (double)p;
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
+        uint32_t p0 = 0, p1 = 0;
+        if (valid(r, j)) p0 = ptab[r * kExpLut + idx_row[i][j]];
+        if (valid(r, j + 1)) p1 = ptab[r * kExpLut + idx_row[i][j + 1]];
+        big |= (int)((p0 | p1) >> 16);
+#pragma unroll
+        for (int l = 0; l < 3; ++l)
+          *reinterpret_cast<uint16_t*>(pL + (l * kPfRows + r) * kPfTStride + jj) =
+              (uint16_t)(((p0 >> (8 * l)) & 0xFF) | (((p1 >> (8 * l)) & 0xFF) << 8));
       }
-    __syncthreads();
+    const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
     stage(1, c + 1);
-    const int n = keys_in(c);
-#pragma unroll 2
-    for (int jj = 0; jj < n; ++jj) {
-      const double2* vrow = reinterpret_cast<const double2*>(kd + jj * kPfDStride);
-      const double2 v0 = vrow[kg], v1 = vrow[16 + kg], v2 = vrow[32 + kg], v3 = vrow[48 + kg];
-      const double vv[8] = {v0.x, v0.y, v1.x, v1.y, v2.x, v2.y, v3.x, v3.y};
+    uint32_t A[2][3][4];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const double p = pb[(4 * rg + e) * kPfPbStride + jj];
+    for (int ks = 0; ks < 2; ++ks)
 #pragma unroll
-        for (int f = 0; f < 8; ++f) o[e][f] = fma(p, vv[f], o[e][f]);
+      for (int l = 0; l < 3; ++l) {
+        const uint8_t* p = pL + (l * kPfRows + ra) * kPfTStride + 32 * ks + 4 * tig;
+        A[ks][l][0] = *reinterpret_cast<const uint32_t*>(p);
+        A[ks][l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
+        A[ks][l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
+        A[ks][l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
       }
+#pragma unroll
+    for (int sb = 0; sb < 2; ++sb) {
+      int32_t acc[5][4][4];
+#pragma unroll
+      for (int s5 = 0; s5 < 5; ++s5)
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          uint32_t B[3][2];
+#pragma unroll
+          for (int l = 0; l < 3; ++l) {
+            const uint8_t* v = vT + (l * kHeadDim + 64 * dh + 8 * (4 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
+            B[l][0] = *reinterpret_cast<const uint32_t*>(v);
+            B[l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
+          }
+          mma_limb<false, false>(acc[0][n], A[ks][0], B[0]);
+          mma_limb<false, false>(acc[1][n], A[ks][0], B[1]);
+          mma_limb<false, false>(acc[1][n], A[ks][1], B[0]);
+          mma_limb<false, true>(acc[2][n], A[ks][0], B[2]);
+          mma_limb<false, false>(acc[2][n], A[ks][1], B[1]);
+          mma_limb<false, true>(acc[3][n], A[ks][1], B[2]);
+          if (any2) {
+            mma_limb<false, false>(acc[2][n], A[ks][2], B[0]);
+            mma_limb<false, false>(acc[3][n], A[ks][2], B[1]);
+            mma_limb<false, true>(acc[4][n], A[ks][2], B[2]);
+          }
+        }
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          tot[4 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
+                                (int64_t)acc[2][n][i] * 65536 + (int64_t)acc[3][n][i] * 16777216 +
+                                (int64_t)acc[4][n][i] * 4294967296LL;
     }
   }
   // outputs as limbs of the o_proj input (64-column sub-batches, SP = 64)
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int r = 4 * rg + e, hh = r / kPfTileQ, qi = r % kPfTileQ;
+  for (int i = 0; i < 2; ++i) {
+    const int r = ra + 8 * i, hh = r / kPfTileQ, qi = r % kPfTileQ;
     if (qi >= tl.nq) continue;
     const int col = tl.col0 + qi;
     uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
 #pragma unroll
-    for (int f = 0; f < 8; ++f) {
-      const int d = 32 * (f >> 1) + 2 * kg + (f & 1);
-      write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d,
-                  sat24((int64_t)o[e][f] >> 16));
-    }
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int d = 64 * dh + 8 * n + 2 * tig + h;
+        write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d,
+                    sat24(tot[n][2 * i + h] >> 16));
+      }
   }
 }
 

@@ -101,3 +101,23 @@ def test_prefill_errors(gm):
         gm.batch_prefill([[1]] * 4, first_slot=14)
     with pytest.raises(_native.Q4GpuError):
         gm.prefill_mode = 2
+
+
+def test_prefill_sharp_attention_matches_serial():
+    """q/k head-norm gammas of 8.0 make most attention rows put their whole
+    probability (2^16) on one key, so the chunks that need the probabilities'
+    third limb (p >> 16) run their extra products; the K/V cache, tokens and
+    scores still equal the serial path's."""
+    rng = np.random.default_rng(13)
+    prompts = [rng.integers(0, VOCAB, n).tolist() for n in (130, 65, 3)]
+    with Q4Model(n_layers=L, vocab=VOCAB, max_context=256, max_seqs=3) as m:
+        m.init_synthetic(seed=SEED, std=0.02, gamma_std=GAMMA)
+        for layer in range(L):
+            for which in (_native.T_Q_GAMMA, _native.T_K_GAMMA):
+                m.set_table(which, np.full(128, 8 * 128, dtype=np.int32), layer=layer)
+        g1, s1, kv1 = _run(m, prompts, 4, 1)
+        g0, s0, kv0 = _run(m, prompts, 4, 0)
+    assert g1.tolist() == g0.tolist() and s1.tolist() == s0.tolist()
+    for i in range(len(prompts)):
+        for a, b in zip(kv1[i], kv0[i]):
+            assert np.array_equal(a, b), i
