@@ -41,6 +41,11 @@ struct BatchCtx {
   // optional timeline (nullptr = off): attention CTA (m, kv) of layer l writes
   // %globaltimer stamps at its phase boundaries to trace[((l * S + m) * 8 + kv) * 8 + k]
   unsigned long long* trace;
+  // Columns beyond SP (prefill): column m belongs to sub-batch m / SP, whose
+  // limb matrices start bt_sub1 / bt_sub3 bytes after the previous one's in
+  // bt1 / bt3 (0 when S <= SP).
+  size_t bt_sub1;
+  size_t bt_sub3;
 };
 
 __device__ __forceinline__ void attn_stamp(const BatchCtx& c, int layer, int m, int kv, int k) {
@@ -148,6 +153,8 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
   grid_dep_wait();
   grid_dep_launch();
   const int m = blockIdx.x, k = 4 * threadIdx.x;
+  const int sub = m / c.SP, ms = m - sub * c.SP;
+  uint8_t* bt = c.bt1 + (size_t)sub * c.bt_sub1;
   const int4 x = *reinterpret_cast<const int4*>((which == 0 ? c.hidden0 : c.post0) + (size_t)m * kHidden + k);
   const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
   int64_t ss = (int64_t)x.x * x.x + (int64_t)x.y * x.y + (int64_t)x.z * x.z + (int64_t)x.w * x.w;
@@ -165,7 +172,7 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
     const int sh = 8 * limb;
     const uint32_t word = ((u0 >> sh) & 0xFF) | (((u1 >> sh) & 0xFF) << 8) | (((u2 >> sh) & 0xFF) << 16) |
                           (((u3 >> sh) & 0xFF) << 24);
-    *reinterpret_cast<uint32_t*>(c.bt1 + (size_t)(limb * c.SP + m) * kHidden + k) = word;
+    *reinterpret_cast<uint32_t*>(bt + (size_t)(limb * c.SP + ms) * kHidden + k) = word;
   }
 }
 
@@ -748,6 +755,18 @@ __global__ void __launch_bounds__(kUThreads, 1)
   const int nkt = g.kt_per_split, kt0 = split * nkt;
   const int row0 = tile * 128;
   const int G = g.K / 64;
+  // sub-batch z = blockIdx.z: columns SP z .. SP z + SP - 1 (B rows from NB z)
+  const int z = blockIdx.z;
+  BatchCtx c = g.c;
+  if (z) {
+    const size_t m0 = (size_t)SP * z;
+    c.qkv_raw += m0 * (kQRows + 2 * kKvRows);
+    c.pos0 += 4 * m0;
+    c.hidden0 += m0 * kHidden;
+    c.post0 += m0 * kHidden;
+    c.bt3 += z * c.bt_sub3;
+  }
+  c.S = c.S - SP * z < SP ? c.S - SP * z : SP;
 
   if (threadIdx.x == 0) gemm_stamp(g, 0);
   if (threadIdx.x == 0) {
@@ -775,7 +794,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   grid_dep_launch();
   auto fail = [&]() {
     *abort_flag = 1;
-    atomicExch(g.c.err, 3);
+    atomicExch(c.err, 3);
   };
 
   if (warp == 0) {
@@ -790,7 +809,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
       grid_dep_wait();
       gemm_stamp(g, 2);
       for (int kt = 0; kt < pre; ++kt)
-        umma::tma_load(sm + kt * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, 0, full + kt);
+        umma::tma_load(sm + kt * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, C::NB * z, full + kt);
       for (int kt = pre; kt < nkt && !*abort_flag; ++kt) {
         const int s = kt % kUStages;
         if (!umma::bar_wait(empty + s, ((kt / kUStages) & 1) ^ 1)) {
@@ -799,7 +818,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         }
         umma::bar_expect_tx(full + s, C::STAGE);
         umma::tma_load(sm + s * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + s);
-        umma::tma_load(sm + s * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, 0, full + s);
+        umma::tma_load(sm + s * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, C::NB * z, full + s);
       }
     } else {
       grid_dep_wait();
@@ -809,7 +828,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
     if (lane != 0) {
       // which sequences take part in this step (the epilogues that update slot state)
       if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
-        for (int m = lane - 1; m < SP; m += 31) live[m] = m < g.c.S && g.c.pos0[4 * m] < g.c.max_ctx;
+        for (int m = lane - 1; m < SP; m += 31) live[m] = m < c.S && c.pos0[4 * m] < c.max_ctx;
     } else {
       for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
         const int s = kt % kUStages;
@@ -922,8 +941,8 @@ __global__ void __launch_bounds__(kUThreads, 1)
     if constexpr (KIND == kGemmQkv) {
       for (int i = et; i < nl * SP; i += kUThreads) {
         const int local = i % nl, m = i / nl;
-        if (m < g.c.S)
-          g.c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
+        if (m < c.S)
+          c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
       }
     } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
       for (int i = et; i < nl * SP; i += kUThreads) {
@@ -932,9 +951,9 @@ __global__ void __launch_bounds__(kUThreads, 1)
         const size_t at = (size_t)m * kHidden + row0 + row_of(local);
         const int32_t o = sat24(sum_of(local, m) >> 14);
         if (KIND == kGemmO)
-          g.c.post0[at] = sat24((int64_t)g.c.hidden0[at] + (o >> 2));
+          c.post0[at] = sat24((int64_t)c.hidden0[at] + (o >> 2));
         else
-          g.c.hidden0[at] = sat24((int64_t)g.c.post0[at] + (o >> 2));
+          c.hidden0[at] = sat24((int64_t)c.post0[at] + (o >> 2));
       }
     } else if constexpr (KIND == kGemmGu) {
       // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
@@ -947,7 +966,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
         ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
         const int32_t silu = sat24(((int64_t)gv * g.sig_lut[ix]) >> 16);
         const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
-        write_limbs(g.c.bt3, SP, kInter, m, tile * 64 + split * rows_per + j, hv);
+        write_limbs(c.bt3, SP, kInter, m, tile * 64 + split * rows_per + j, hv);
       }
     } else {
       // LM head (no split): best (score, row) of each sequence over the tile
@@ -1167,7 +1186,7 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 template <bool SA, bool SB>
 __device__ __forceinline__ void mma_limb(int32_t (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
 #define PF_MMA(TA, TB)                                                                                     \
-  asm volatile("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB ".s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, " \
+  asm("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB ".s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "          \
                "{%8,%9}, {%0,%1,%2,%3};"                                                                   \
                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])                                            \
                : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]))
@@ -1319,25 +1338,35 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
         A[l][2] = *reinterpret_cast<const uint32_t*>(q0 + 16);
         A[l][3] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride + 16);
       }
+      uint32_t B[4][3][2];
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-        uint32_t B[3][2];
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int l = 0; l < 3; ++l) {
           const uint8_t* k = kL + (l * 64 + 32 * kh + 8 * nt + g) * kPfLStride + k0;
-          B[l][0] = *reinterpret_cast<const uint32_t*>(k);
-          B[l][1] = *reinterpret_cast<const uint32_t*>(k + 16);
+          B[nt][l][0] = *reinterpret_cast<const uint32_t*>(k);
+          B[nt][l][1] = *reinterpret_cast<const uint32_t*>(k + 16);
         }
-        mma_limb<false, false>(acc[0][nt], A[0], B[0]);
-        mma_limb<false, false>(acc[1][nt], A[0], B[1]);
-        mma_limb<false, false>(acc[1][nt], A[1], B[0]);
-        mma_limb<false, true>(acc[2][nt], A[0], B[2]);
-        mma_limb<false, false>(acc[2][nt], A[1], B[1]);
-        mma_limb<true, false>(acc[2][nt], A[2], B[0]);
-        mma_limb<false, true>(acc[3][nt], A[1], B[2]);
-        mma_limb<true, false>(acc[3][nt], A[2], B[1]);
-        mma_limb<true, true>(acc[4][nt], A[2], B[2]);
-      }
+      // limb pairs outer, tiles inner: four independent accumulators between
+      // two products into the same one
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[0][nt], A[0], B[nt][0]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[1][nt], A[0], B[nt][1]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, true>(acc[2][nt], A[0], B[nt][2]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, true>(acc[3][nt], A[1], B[nt][2]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<true, true>(acc[4][nt], A[2], B[nt][2]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[1][nt], A[1], B[nt][0]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[2][nt], A[1], B[nt][1]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<true, false>(acc[3][nt], A[2], B[nt][1]);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) mma_limb<true, false>(acc[2][nt], A[2], B[nt][0]);
     }
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
@@ -1405,7 +1434,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   for (int i = 0; i < 2; ++i) {
     const int r = ra + 8 * i, hh = r / kPfTileQ, qi = r % kPfTileQ;
     const int col = tl.col0 + (qi < tl.nq ? qi : 0);
-    idx_row[i] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.max_ctx;
+    idx_row[i] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.idx_ld;
   }
   for (int c = 0; c < nch; ++c) {
     cp_async_wait0();
@@ -1453,7 +1482,24 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   for (int n = 0; n < 8; ++n)
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[n][i] = 0;
+  // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded
+  // a chunk ahead; the scratch rows are 64-aligned, so a pair is one 4-byte word
+  auto idx_pairs = [&](int c, uint32_t (&w)[2][4]) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+        w[i][nt] = *reinterpret_cast<const uint32_t*>(idx_row[i] + c * kPfKeys + key_of(nt, 0));
+  };
+  uint32_t nidx[2][4];
+  idx_pairs(0, nidx);
   for (int c = 0; c < nch; ++c) {
+    uint32_t cidx[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) cidx[i][nt] = nidx[i][nt];
+    if (c + 1 < nch) idx_pairs(c + 1, nidx);
     cp_async_wait0();
     __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
     // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
@@ -1474,8 +1520,8 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
       for (int nt = 0; nt < 4; ++nt) {
         const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
         uint32_t p0 = 0, p1 = 0;
-        if (valid(r, j)) p0 = ptab[r * kExpLut + idx_row[i][j]];
-        if (valid(r, j + 1)) p1 = ptab[r * kExpLut + idx_row[i][j + 1]];
+        if (valid(r, j)) p0 = ptab[r * kExpLut + (cidx[i][nt] & 0xFFFFu)];
+        if (valid(r, j + 1)) p1 = ptab[r * kExpLut + (cidx[i][nt] >> 16)];
         big |= (int)((p0 | p1) >> 16);
 #pragma unroll
         for (int l = 0; l < 3; ++l)
@@ -1505,28 +1551,37 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks)
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t B[4][3][2];
 #pragma unroll
-        for (int n = 0; n < 4; ++n) {
-          uint32_t B[3][2];
+        for (int n = 0; n < 4; ++n)
 #pragma unroll
           for (int l = 0; l < 3; ++l) {
             const uint8_t* v = vT + (l * kHeadDim + 64 * dh + 8 * (4 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
-            B[l][0] = *reinterpret_cast<const uint32_t*>(v);
-            B[l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
+            B[n][l][0] = *reinterpret_cast<const uint32_t*>(v);
+            B[n][l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
           }
-          mma_limb<false, false>(acc[0][n], A[ks][0], B[0]);
-          mma_limb<false, false>(acc[1][n], A[ks][0], B[1]);
-          mma_limb<false, false>(acc[1][n], A[ks][1], B[0]);
-          mma_limb<false, true>(acc[2][n], A[ks][0], B[2]);
-          mma_limb<false, false>(acc[2][n], A[ks][1], B[1]);
-          mma_limb<false, true>(acc[3][n], A[ks][1], B[2]);
-          if (any2) {
-            mma_limb<false, false>(acc[2][n], A[ks][2], B[0]);
-            mma_limb<false, false>(acc[3][n], A[ks][2], B[1]);
-            mma_limb<false, true>(acc[4][n], A[ks][2], B[2]);
-          }
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[0][n], A[ks][0], B[n][0]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[1][n], A[ks][0], B[n][1]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[2][n], A[ks][0], B[n][2]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[3][n], A[ks][1], B[n][2]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[1][n], A[ks][1], B[n][0]);
+#pragma unroll
+        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[2][n], A[ks][1], B[n][1]);
+        if (any2) {
+#pragma unroll
+          for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[4][n], A[ks][2], B[n][2]);
+#pragma unroll
+          for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[3][n], A[ks][2], B[n][1]);
+#pragma unroll
+          for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[2][n], A[ks][2], B[n][0]);
         }
+      }
 #pragma unroll
       for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -1600,13 +1655,15 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStr
 
 // K splits of each batched GEMM (a cluster of that many CTAs per row tile)
 constexpr int kSplitQkv = 4, kSplitO = 8, kSplitGu = 2, kSplitDown = 8;
+// prefill launches cover up to 8 sub-batches each, so they need fewer splits to fill the GPU
+constexpr int kPfSplitQkv = 1, kPfSplitO = 2, kPfSplitGu = 1, kPfSplitDown = 4;
 
 template <int SP, int KIND>
 cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const BatchCtx& c, const uint16_t* scales,
                         int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s,
-                        unsigned long long* trace = nullptr) {
+                        unsigned long long* trace = nullptr, int subs = 1) {
   UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial, trace};
-  const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)splits);
+  const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)splits, (unsigned)subs);
   return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
 }
 
@@ -1786,40 +1843,30 @@ int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
   if (p.n_cols < 1 || p.n_cols > kPfBlock || p.n_tiles < 1 || p.n_tiles > kPfBlock)
     return q4gpu_fail(Q4GPU_ERR_SHAPE, "prefill block of %d columns / %d tiles", p.n_cols, p.n_tiles);
   constexpr int kRow = kQRows + 2 * kKvRows;
-  const size_t bt2_sub = (size_t)q4gpu_batch_limb_rows(kPfSub) * 2 * kHidden;
+  constexpr size_t nb = (size_t)UCfg<kPfSub>::NB;  // rows of one sub-batch's limb matrix (ones rows, zero padding)
   const int nsub = (p.n_cols + kPfSub - 1) / kPfSub;
-  auto ctx = [&](int sub) {
-    const int c0 = sub * kPfSub;
-    const int S = p.n_cols - c0 < kPfSub ? p.n_cols - c0 : kPfSub;
-    return BatchCtx{p.col_slots + c0, S, kPfSub, p.qkv + (size_t)c0 * kRow, p.bt1, p.bt2 + (size_t)sub * bt2_sub,
-                    p.bt3, nullptr, p.err, p.col_pos4 + 4 * c0, p.hidden + (size_t)c0 * kHidden,
-                    p.post + (size_t)c0 * kHidden, p.max_ctx, nullptr};
-  };
-  for (int sub = 0; sub < nsub; ++sub) {
-    const BatchCtx c = ctx(sub);
-    BQ(launch_pdl(batch_embed_kernel, dim3(c.S), dim3(256), 0, s, c, p.emb, p.semb));
-  }
+  // all columns of the block in one context: the GEMMs take sub-batch z from blockIdx.z
+  const BatchCtx c{p.col_slots, p.n_cols, kPfSub, p.qkv,      p.bt1,         p.bt2,  p.bt3,
+                   nullptr,     p.err,    p.col_pos4, p.hidden, p.post,        p.max_ctx, nullptr,
+                   nb * kHidden, nb * kInter};
+  BQ(launch_pdl(batch_embed_kernel, dim3(p.n_cols), dim3(256), 0, s, c, p.emb, p.semb));
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
-    for (int sub = 0; sub < nsub; ++sub) {
-      const BatchCtx c = ctx(sub);
-      BQ(launch_pdl(batch_norm_limbs_kernel, dim3(c.S), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
-      BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kRow, kHidden, kSplitQkv, nullptr, nullptr, s)));
-    }
+    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
+    BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kRow, kHidden, kPfSplitQkv, nullptr, nullptr, s,
+                                      nullptr, nsub)));
     BQ(launch_pdl(prefill_qk_kernel, dim3(kKvHeads, p.n_cols), dim3(128), 0, s, p.col_slots, p.col_pos4, p.qkv, l,
                   w.g_q, w.g_k, p.cos_tab, p.sin_tab));
-    const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, bt2_sub, p.lut_idx, p.max_ctx, l, p.exp_lut, p.err};
+    const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, nb * 2 * kHidden, p.lut_idx, (p.max_ctx + 63) / 64 * 64, l,
+                   p.exp_lut, p.err};
     BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(256), kPfSmem, s, a));
-    for (int sub = 0; sub < nsub; ++sub) {
-      const BatchCtx c = ctx(sub);
-      BQ((launch_gemm<kPfSub, kGemmO>(w.mo, p.mb2[sub], c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr,
-                                      s)));
-      BQ(launch_pdl(batch_norm_limbs_kernel, dim3(c.S), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
-      BQ((launch_gemm<kPfSub, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr,
-                                       s)));
-      BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr,
-                                         s)));
-    }
+    BQ((launch_gemm<kPfSub, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kPfSplitO, nullptr, nullptr, s,
+                                    nullptr, nsub)));
+    BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
+    BQ((launch_gemm<kPfSub, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kPfSplitGu, p.sig_lut, nullptr, s,
+                                     nullptr, nsub)));
+    BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kPfSplitDown, nullptr, nullptr,
+                                       s, nullptr, nsub)));
   }
   return Q4GPU_OK;
 }

@@ -106,19 +106,22 @@ struct PfAttn {
   const PfTile* tiles;
   const SlotState* col_slots;  // [block columns] the column's sequence state
   const int32_t* qkv;          // [block columns][4096]; q rows normed and roped
-  uint8_t* bt2;                // [block columns / 64][3 * 64 + 8][2048] limbs of the attention output
+  uint8_t* bt2;                // [block columns / 64][208][2048] limbs of the attention output
   size_t bt2_sub;              // bytes per 64-column sub-batch of bt2
-  uint16_t* lut_idx;           // [block columns][16][max_ctx] exp-LUT indices (scratch)
-  int max_ctx;
+  uint16_t* lut_idx;           // [block columns][16][idx_ld] exp-LUT indices (scratch)
+  int idx_ld;                  // max_ctx rounded up to 64
   int layer;
   const int32_t* exp_lut;
   int* err;
 };
 
+// Limb matrices of the prefill hold kPfBlock / 64 sub-batches of
+// q4gpu_batch_box_rows(64) = 208 rows each (3 * 64 limb rows, 8 ones rows, 8
+// zero rows); a GEMM's sub-batch z reads B rows 208 z .. 208 z + 207.
 struct PrefillPlan {
-  alignas(64) CUtensorMap mb1;          // bt1 / bt3 (SP 64)
+  alignas(64) CUtensorMap mb1;  // TMA maps of bt1 / bt2 / bt3, 208-row boxes
+  CUtensorMap mb2;
   CUtensorMap mb3;
-  CUtensorMap mb2[kPfBlock / kPfSub];  // bt2 of each 64-column sub-batch
   const SlotState* col_slots;  // [n_cols] this block's columns
   const int32_t* col_pos4;     // [n_cols][4], position at [4 c]
   const PfTile* tiles;         // [n_tiles], block-relative columns
@@ -126,10 +129,10 @@ struct PrefillPlan {
   int32_t* hidden;  // [kPfBlock][1024]
   int32_t* post;    // [kPfBlock][1024]
   int32_t* qkv;     // [kPfBlock][4096]
-  uint8_t* bt1;     // [3 * 64 + 8][1024]
-  uint8_t* bt2;     // [kPfBlock / 64][3 * 64 + 8][2048]
-  uint8_t* bt3;     // [3 * 64 + 8][3072]
-  uint16_t* lut_idx;  // [kPfBlock][16][max_ctx]
+  uint8_t* bt1;     // [kPfBlock / 64][208][1024]
+  uint8_t* bt2;     // [kPfBlock / 64][208][2048]
+  uint8_t* bt3;     // [kPfBlock / 64][208][3072]
+  uint16_t* lut_idx;  // [kPfBlock][16][max_ctx rounded up to 64]
   const uint8_t* emb;
   const uint16_t* semb;
   const BatchLayerW* layers;

@@ -971,25 +971,23 @@ int prefill_prepare(q4gpu_model* m) {
     attrs = true;
   }
   auto p = std::make_unique<PrefillPlan>();
-  const size_t rows = (size_t)q4gpu_batch_limb_rows(kPfSub);
-  const uint32_t box = (uint32_t)q4gpu_batch_box_rows(kPfSub);
+  const size_t rows = (size_t)q4gpu_batch_box_rows(kPfSub);  // 208: limb rows, ones rows, zero rows
   constexpr int nsub = kPfBlock / kPfSub;
   if ((rc = m->alloc(&p->hidden, (size_t)kPfBlock * kHidden)) || (rc = m->alloc(&p->post, (size_t)kPfBlock * kHidden)) ||
       (rc = m->alloc(&p->qkv, (size_t)kPfBlock * (kQRows + 2 * kKvRows))) ||
-      (rc = m->alloc(&p->bt1, rows * kHidden)) || (rc = m->alloc(&p->bt2, nsub * rows * 2 * kHidden)) ||
-      (rc = m->alloc(&p->bt3, rows * kInter)) ||
-      (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * m->cfg.max_context)))
+      (rc = m->alloc(&p->bt1, nsub * rows * kHidden)) || (rc = m->alloc(&p->bt2, nsub * rows * 2 * kHidden)) ||
+      (rc = m->alloc(&p->bt3, nsub * rows * kInter)) ||
+      (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * ((m->cfg.max_context + 63) / 64 * 64))))
     return rc;
-  Q4_CUDA(cudaMemset(p->bt1 + 3 * kPfSub * kHidden, 1, (size_t)kBatchOnes * kHidden));
-  Q4_CUDA(cudaMemset(p->bt3 + 3 * kPfSub * kInter, 1, (size_t)kBatchOnes * kInter));
-  for (int sub = 0; sub < nsub; ++sub)
+  for (int sub = 0; sub < nsub; ++sub) {
+    Q4_CUDA(cudaMemset(p->bt1 + (sub * rows + 3 * kPfSub) * kHidden, 1, (size_t)kBatchOnes * kHidden));
     Q4_CUDA(cudaMemset(p->bt2 + (sub * rows + 3 * kPfSub) * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden));
-  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, rows, box)) ||
-      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, rows, box)))
+    Q4_CUDA(cudaMemset(p->bt3 + (sub * rows + 3 * kPfSub) * kInter, 1, (size_t)kBatchOnes * kInter));
+  }
+  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)rows)) ||
+      (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)rows)) ||
+      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, nsub * rows, (uint32_t)rows)))
     return rc;
-  for (int sub = 0; sub < nsub; ++sub)
-    if ((rc = q4gpu_encode_u8_map(&p->mb2[sub], p->bt2 + sub * rows * 2 * kHidden, 2 * kHidden, rows, box)))
-      return rc;
   p->emb = m->emb;
   p->semb = m->semb;
   p->layers = m->b_layers;
