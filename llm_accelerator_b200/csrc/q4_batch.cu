@@ -730,7 +730,7 @@ __device__ __forceinline__ void gemm_stamp(const UGemm& g, int k) {
   if (g.trace) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + k] = t;
+    g.trace[((size_t)blockIdx.y * gridDim.z + blockIdx.z) * 8 + k] = t;
   }
 }
 
@@ -751,12 +751,14 @@ __global__ void __launch_bounds__(kUThreads, 1)
   int* live = reinterpret_cast<int*>(tmem_slot + 2);  // [64]: sequence m takes part in this step
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y, splits = gridDim.y;
+  // grid (sub-batches, K splits, row tiles): the sub-batches of one weight
+  // tile are adjacent in launch order and share its reads through L2
+  const int tile = blockIdx.z, split = blockIdx.y, splits = gridDim.y;
   const int nkt = g.kt_per_split, kt0 = split * nkt;
   const int row0 = tile * 128;
   const int G = g.K / 64;
-  // sub-batch z = blockIdx.z: columns SP z .. SP z + SP - 1 (B rows from NB z)
-  const int z = blockIdx.z;
+  // sub-batch z: columns SP z .. SP z + SP - 1 (B rows from NB z)
+  const int z = blockIdx.x;
   BatchCtx c = g.c;
   if (z) {
     const size_t m0 = (size_t)SP * z;
@@ -1663,7 +1665,7 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
                         int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s,
                         unsigned long long* trace = nullptr, int subs = 1) {
   UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial, trace};
-  const dim3 grid((unsigned)((rows + 127) / 128), (unsigned)splits, (unsigned)subs);
+  const dim3 grid((unsigned)subs, (unsigned)splits, (unsigned)((rows + 127) / 128));
   return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
 }
 
