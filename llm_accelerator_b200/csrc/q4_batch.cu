@@ -1171,6 +1171,8 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
 // ---------------------------------------------------------------------------
 constexpr int kPfStride = kHeadDim + 4;   // staged int32 key row (words): 16-byte aligned rows
 constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA
+constexpr int kPfThreads = 512;           // 16 warps: 4 row tiles x 4 key (or dim) quarters
+constexpr int kPfQuarters = 4;
 constexpr int kPfLStride = kHeadDim + 16;  // byte-limb row: rows 4 banks apart for the fragment loads
 constexpr size_t kPfLimbBytes = (size_t)3 * 64 * kPfLStride;       // three limb planes of 64 rows
 constexpr size_t kPfRowsBytes = (size_t)kPfRows * kExpLut * 4;      // q and key limbs (passes 1-2) / probability table
@@ -1269,7 +1271,7 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
   }
 }
 
-__global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
   extern __shared__ __align__(16) uint8_t pf_smem[];
   uint8_t* qL = pf_smem;                                  // [3][64][kPfLStride] q limbs (passes 1-2)
   uint8_t* kL = pf_smem + kPfLimbBytes;                   // [3][64][kPfLStride] key limbs (passes 1-2)
@@ -1278,8 +1280,9 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   uint8_t* pL = pf_smem + kPfRowsBytes + kPfVtBytes;       // [3][64][kPfTStride] probability limbs (pass 3)
   int32_t* stg = reinterpret_cast<int32_t*>(pf_smem + kPfRowsBytes + kPfVtBytes + kPfPlBytes);  // [64][kPfStride]
   __shared__ int32_t elut[kExpLut];
-  __shared__ int64_t rred[2][kPfRows];  // per key half: row maxima, then row sums
-  __shared__ int64_t rmax[kPfRows], rsum[kPfRows];
+  __shared__ int64_t rred[kPfQuarters][kPfRows];  // per key quarter: row maxima, then row sums
+  __shared__ int64_t rmax[kPfRows];
+  __shared__ uint64_t rsum[kPfRows], rrcp[kPfRows];  // row sums and floor((2^64 - 1) / sum)
   grid_dep_wait();
   grid_dep_launch();
   const int kv = blockIdx.x;
@@ -1295,7 +1298,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     if (c < nch) {
       const int n = keys_in(c);
       const int32_t* src = kvv.at(a.layer, kind, kv, c * kPfKeys);  // a 64-aligned chunk is one page
-      for (int i = t; i < n * (kHeadDim / 4); i += 256) {
+      for (int i = t; i < n * (kHeadDim / 4); i += kPfThreads) {
         const int j = i >> 5, d4 = i & 31;
         cp_async16(stg + j * kPfStride + 4 * d4, src + (size_t)j * kHeadDim + 4 * d4);
       }
@@ -1303,7 +1306,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     cp_async_commit();
   };
   stage(0, 0);
-  for (int i = t; i < kPfRows * (kHeadDim / 4); i += 256) {
+  for (int i = t; i < kPfRows * (kHeadDim / 4); i += kPfThreads) {
     const int r = i >> 5, d4 = i & 31, hh = r / kPfTileQ, qi = r % kPfTileQ;
     int4 v = make_int4(0, 0, 0, 0);
     if (qi < tl.nq)
@@ -1312,26 +1315,26 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
 #pragma unroll
     for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(qL + (l * 64 + r) * kPfLStride + 4 * d4) = limb_word(v, l);
   }
-  for (int i = t; i < kExpLut; i += 256) elut[i] = a.exp_lut[i];
+  for (int i = t; i < kExpLut; i += kPfThreads) elut[i] = a.exp_lut[i];
 
-  // Scores: warp (mt, kh) takes rows 16 mt .. +15 and keys 32 kh .. +31 of the
-  // chunk (four 8-key MMA tiles).  Lane (g, tig) ends up with rows
-  // ra = 16 mt + g and ra + 8, keys 32 kh + 8 nt + 2 tig + h (nt 0..3, h 0..1).
-  const int mt = warp & 3, kh = warp >> 2, g = lane >> 2, tig = lane & 3;
+  // Scores: warp (mt, kq) takes rows 16 mt .. +15 and keys 16 kq .. +15 of the
+  // chunk (two 8-key MMA tiles).  Lane (g, tig) ends up with rows ra = 16 mt + g
+  // and ra + 8, keys 16 kq + 8 nt + 2 tig + h (nt, h = 0, 1).
+  const int mt = warp & 3, kq = warp >> 2, g = lane >> 2, tig = lane & 3;
   const int ra = 16 * mt + g;
-  auto key_of = [&](int nt, int h) { return 32 * kh + 8 * nt + 2 * tig + h; };
-  auto scores = [&](int64_t (&raw)[2][8]) {
-    int32_t acc[5][4][4];
+  auto key_of = [&](int nt, int h) { return 16 * kq + 8 * nt + 2 * tig + h; };
+  auto scores = [&](int64_t (&raw)[2][4]) {
+    int32_t acc[5][2][4];
 #pragma unroll
     for (int s = 0; s < 5; ++s)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[s][nt][i] = 0;
 #pragma unroll
     for (int ks = 0; ks < kHeadDim / 32; ++ks) {
       const int k0 = 32 * ks + 4 * tig;
-      uint32_t A[3][4];
+      uint32_t A[3][4], B[2][3][2];
 #pragma unroll
       for (int l = 0; l < 3; ++l) {
         const uint8_t* q0 = qL + (l * 64 + ra) * kPfLStride + k0;
@@ -1340,38 +1343,37 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
         A[l][2] = *reinterpret_cast<const uint32_t*>(q0 + 16);
         A[l][3] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride + 16);
       }
-      uint32_t B[4][3][2];
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int l = 0; l < 3; ++l) {
-          const uint8_t* k = kL + (l * 64 + 32 * kh + 8 * nt + g) * kPfLStride + k0;
+          const uint8_t* k = kL + (l * 64 + 16 * kq + 8 * nt + g) * kPfLStride + k0;
           B[nt][l][0] = *reinterpret_cast<const uint32_t*>(k);
           B[nt][l][1] = *reinterpret_cast<const uint32_t*>(k + 16);
         }
-      // limb pairs outer, tiles inner: four independent accumulators between
-      // two products into the same one
+      // limb pairs outer, tiles inner: independent accumulators between two
+      // products into the same one
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[0][nt], A[0], B[nt][0]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[0][nt], A[0], B[nt][0]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[1][nt], A[0], B[nt][1]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[1][nt], A[0], B[nt][1]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, true>(acc[2][nt], A[0], B[nt][2]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, true>(acc[2][nt], A[0], B[nt][2]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, true>(acc[3][nt], A[1], B[nt][2]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, true>(acc[3][nt], A[1], B[nt][2]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<true, true>(acc[4][nt], A[2], B[nt][2]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<true, true>(acc[4][nt], A[2], B[nt][2]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[1][nt], A[1], B[nt][0]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[1][nt], A[1], B[nt][0]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<false, false>(acc[2][nt], A[1], B[nt][1]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[2][nt], A[1], B[nt][1]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<true, false>(acc[3][nt], A[2], B[nt][1]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<true, false>(acc[3][nt], A[2], B[nt][1]);
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) mma_limb<true, false>(acc[2][nt], A[2], B[nt][0]);
+      for (int nt = 0; nt < 2; ++nt) mma_limb<true, false>(acc[2][nt], A[2], B[nt][0]);
     }
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
+    for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i)
         raw[i >> 1][2 * nt + (i & 1)] = (int64_t)acc[0][nt][i] + (int64_t)acc[1][nt][i] * 256 +
@@ -1381,7 +1383,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
   // staged chunk -> key limbs
   auto key_limbs = [&](int c) {
     const int n = keys_in(c);
-    for (int i = t; i < n * (kHeadDim / 4); i += 256) {
+    for (int i = t; i < n * (kHeadDim / 4); i += kPfThreads) {
       const int j = i >> 5, d4 = i & 31;
       const int4 v = *reinterpret_cast<const int4*>(stg + j * kPfStride + 4 * d4);
 #pragma unroll
@@ -1394,7 +1396,8 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     return qi < tl.nq && j <= tl.pos0 + qi;
   };
 
-  // pass 1: row maxima
+  // pass 1: row maxima of the raw scores (the scaling is monotonic, so the
+  // maximum scaled score is the scaled maximum)
   int64_t mx[2] = {INT64_MIN, INT64_MIN};
   for (int c = 0; c < nch; ++c) {
     cp_async_wait0();
@@ -1402,18 +1405,15 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     key_limbs(c);
     __syncthreads();
     stage(0, c + 1);
-    int64_t raw[2][8];
+    int64_t raw[2][4];
     scores(raw);
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int h = 0; h < 2; ++h)
-          if (valid(ra + 8 * i, c * kPfKeys + key_of(nt, h))) {
-            const int64_t s = scale_score(raw[i][2 * nt + h], kScoreScale);
-            mx[i] = s > mx[i] ? s : mx[i];
-          }
+          if (valid(ra + 8 * i, c * kPfKeys + key_of(nt, h))) mx[i] = raw[i][2 * nt + h] > mx[i] ? raw[i][2 * nt + h] : mx[i];
   }
   stage(0, 0);  // pass 2 streams K again
 #pragma unroll
@@ -1423,10 +1423,15 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
       const int64_t o = shfl_xor_i64(mx[i], msk);
       mx[i] = o > mx[i] ? o : mx[i];
     }
-    if (tig == 0) rred[kh][ra + 8 * i] = mx[i];
+    if (tig == 0) rred[kq][ra + 8 * i] = mx[i];
   }
   __syncthreads();
-  if (t < kPfRows) rmax[t] = rred[0][t] > rred[1][t] ? rred[0][t] : rred[1][t];
+  if (t < kPfRows) {
+    int64_t m = rred[0][t];
+#pragma unroll
+    for (int q = 1; q < kPfQuarters; ++q) m = rred[q][t] > m ? rred[q][t] : m;
+    rmax[t] = m == INT64_MIN ? m : scale_score(m, kScoreScale);
+  }
   __syncthreads();
   // pass 2: LUT indices and exp sums
   int64_t sm[2] = {0, 0};
@@ -1444,68 +1449,90 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     key_limbs(c);
     __syncthreads();
     stage(0, c + 1);
-    int64_t raw[2][8];
+    int64_t raw[2][4];
     scores(raw);
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt) {
+        const int j = c * kPfKeys + key_of(nt, 0);
+        uint32_t pair = 0;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int j = c * kPfKeys + key_of(nt, h);
-          if (valid(ra + 8 * i, j)) {
+        for (int h = 0; h < 2; ++h)
+          if (valid(ra + 8 * i, j + h)) {
             const int ix = lut_index(rmx[i], scale_score(raw[i][2 * nt + h], kScoreScale));
             sm[i] += elut[ix];
-            idx_row[i][j] = (uint16_t)ix;
+            pair |= (uint32_t)ix << (16 * h);
           }
-        }
+        // rows are 64-aligned, so (j, j + 1), j even, is one 4-byte word; rows
+        // past the tile's queries alias its first row and store nothing
+        if ((ra + 8 * i) % kPfTileQ < tl.nq) *reinterpret_cast<uint32_t*>(idx_row[i] + j) = pair;
+      }
   }
   stage(1, 0);  // pass 3 streams V
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
 #pragma unroll
     for (int msk = 1; msk < 4; msk <<= 1) sm[i] += shfl_xor_i64(sm[i], msk);
-    if (tig == 0) rred[kh][ra + 8 * i] = sm[i];
+    if (tig == 0) rred[kq][ra + 8 * i] = sm[i];
   }
   __syncthreads();  // the limbs are dead: the table takes their place
-  if (t < kPfRows) rsum[t] = rred[0][t] + rred[1][t];
-  __syncthreads();
-  for (int i = t; i < kPfRows * kExpLut; i += 256) {
-    const int r = i / kExpLut, e = i - r * kExpLut;
-    const int64_t s = rsum[r];
-    ptab[i] = s > 0 ? (uint32_t)udiv_exact((uint64_t)elut[e] << 16, (uint64_t)s) : 0u;
-  }
-  // pass 3: probability-weighted values.  Warp (mt, dh) takes output rows
-  // 16 mt .. +15 and dims 64 dh .. +63 (eight 8-dim MMA tiles, two batches of
-  // four); lane (g, tig) holds rows ra, ra + 8 and dims 64 dh + 8 n + 2 tig + {0, 1}.
-  const int dh = kh;
-  int64_t tot[8][4];
+  if (t < kPfRows) {
+    uint64_t s = 0;
 #pragma unroll
-  for (int n = 0; n < 8; ++n)
+    for (int q = 0; q < kPfQuarters; ++q) s += (uint64_t)rred[q][t];
+    rsum[t] = s;
+    rrcp[t] = s > 0 ? ~0ULL / s : 0;
+  }
+  __syncthreads();
+  // prob[e] = floor((lut[e] << 16) / sum) by a Barrett reciprocal: with
+  // R = floor((2^64 - 1) / sum) and n < 2^37, q = mulhi(n, R) is at most two
+  // below the quotient, and the remainder test fixes it exactly
+  for (int i = t; i < kPfRows * kExpLut; i += kPfThreads) {
+    const int r = i / kExpLut, e = i - r * kExpLut;
+    const uint64_t s = rsum[r], n = (uint64_t)elut[e] << 16;
+    uint32_t p = 0;
+    if (s > 0) {
+      uint64_t q = __umul64hi(n, rrcp[r]);
+      uint64_t rem = n - q * s;
+      if (rem >= s) {
+        ++q;
+        rem -= s;
+      }
+      if (rem >= s) ++q;
+      p = (uint32_t)q;
+    }
+    ptab[i] = p;
+  }
+  // pass 3: probability-weighted values.  Warp (mt, kq) takes output rows
+  // 16 mt .. +15 and dims 32 kq .. +31 (four 8-dim MMA tiles, two at a time);
+  // lane (g, tig) holds rows ra, ra + 8 and dims 32 kq + 8 n + 2 tig + {0, 1}.
+  int64_t tot[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
 #pragma unroll
     for (int i = 0; i < 4; ++i) tot[n][i] = 0;
-  // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded
-  // a chunk ahead; the scratch rows are 64-aligned, so a pair is one 4-byte word
-  auto idx_pairs = [&](int c, uint32_t (&w)[2][4]) {
+  // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded a chunk ahead
+  auto idx_pairs = [&](int c, uint32_t (&w)[2][2]) {
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 2; ++nt)
         w[i][nt] = *reinterpret_cast<const uint32_t*>(idx_row[i] + c * kPfKeys + key_of(nt, 0));
   };
-  uint32_t nidx[2][4];
+  uint32_t nidx[2][2];
   idx_pairs(0, nidx);
   for (int c = 0; c < nch; ++c) {
-    uint32_t cidx[2][4];
+    uint32_t cidx[2][2];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) cidx[i][nt] = nidx[i][nt];
+      for (int nt = 0; nt < 2; ++nt) cidx[i][nt] = nidx[i][nt];
     if (c + 1 < nch) idx_pairs(c + 1, nidx);
     cp_async_wait0();
     __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
     // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
-    for (int i = t; i < kHeadDim * (kPfKeys / 4); i += 256) {
+    for (int i = t; i < kHeadDim * (kPfKeys / 4); i += kPfThreads) {
       const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;  // 8 dims x 4 key groups per warp
       const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
       const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
@@ -1519,7 +1546,7 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
+      for (int nt = 0; nt < 2; ++nt) {
         const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
         uint32_t p0 = 0, p1 = 0;
         if (valid(r, j)) p0 = ptab[r * kExpLut + (cidx[i][nt] & 0xFFFFu)];
@@ -1532,63 +1559,60 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
       }
     const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
     stage(1, c + 1);
-    uint32_t A[2][3][4];
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-      for (int l = 0; l < 3; ++l) {
-        const uint8_t* p = pL + (l * kPfRows + ra) * kPfTStride + 32 * ks + 4 * tig;
-        A[ks][l][0] = *reinterpret_cast<const uint32_t*>(p);
-        A[ks][l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
-        A[ks][l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
-        A[ks][l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
-      }
 #pragma unroll
     for (int sb = 0; sb < 2; ++sb) {
-      int32_t acc[5][4][4];
+      int32_t acc[5][2][4];
 #pragma unroll
       for (int s5 = 0; s5 < 5; ++s5)
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int n = 0; n < 2; ++n)
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
-        uint32_t B[4][3][2];
+        uint32_t A[3][4], B[2][3][2];
 #pragma unroll
-        for (int n = 0; n < 4; ++n)
+        for (int l = 0; l < 3; ++l) {
+          const uint8_t* p = pL + (l * kPfRows + ra) * kPfTStride + 32 * ks + 4 * tig;
+          A[l][0] = *reinterpret_cast<const uint32_t*>(p);
+          A[l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
+          A[l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
+          A[l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
 #pragma unroll
           for (int l = 0; l < 3; ++l) {
-            const uint8_t* v = vT + (l * kHeadDim + 64 * dh + 8 * (4 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
+            const uint8_t* v = vT + (l * kHeadDim + 32 * kq + 8 * (2 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
             B[n][l][0] = *reinterpret_cast<const uint32_t*>(v);
             B[n][l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
           }
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[0][n], A[ks][0], B[n][0]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[0][n], A[0], B[n][0]);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[1][n], A[ks][0], B[n][1]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[0], B[n][1]);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[2][n], A[ks][0], B[n][2]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[2][n], A[0], B[n][2]);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[3][n], A[ks][1], B[n][2]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[3][n], A[1], B[n][2]);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[1][n], A[ks][1], B[n][0]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[1], B[n][0]);
 #pragma unroll
-        for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[2][n], A[ks][1], B[n][1]);
+        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[1], B[n][1]);
         if (any2) {
 #pragma unroll
-          for (int n = 0; n < 4; ++n) mma_limb<false, true>(acc[4][n], A[ks][2], B[n][2]);
+          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[4][n], A[2], B[n][2]);
 #pragma unroll
-          for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[3][n], A[ks][2], B[n][1]);
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[3][n], A[2], B[n][1]);
 #pragma unroll
-          for (int n = 0; n < 4; ++n) mma_limb<false, false>(acc[2][n], A[ks][2], B[n][0]);
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[2], B[n][0]);
         }
       }
 #pragma unroll
-      for (int n = 0; n < 4; ++n)
+      for (int n = 0; n < 2; ++n)
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          tot[4 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
+          tot[2 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
                                 (int64_t)acc[2][n][i] * 65536 + (int64_t)acc[3][n][i] * 16777216 +
                                 (int64_t)acc[4][n][i] * 4294967296LL;
     }
@@ -1601,10 +1625,10 @@ __global__ void __launch_bounds__(256, 1) prefill_attn_kernel(PfAttn a) {
     const int col = tl.col0 + qi;
     uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int d = 64 * dh + 8 * n + 2 * tig + h;
+        const int d = 32 * kq + 8 * n + 2 * tig + h;
         write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d,
                     sat24(tot[n][2 * i + h] >> 16));
       }
@@ -1861,7 +1885,7 @@ int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
                   w.g_q, w.g_k, p.cos_tab, p.sin_tab));
     const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, nb * 2 * kHidden, p.lut_idx, (p.max_ctx + 63) / 64 * 64, l,
                    p.exp_lut, p.err};
-    BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(256), kPfSmem, s, a));
+    BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(kPfThreads), kPfSmem, s, a));
     BQ((launch_gemm<kPfSub, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kPfSplitO, nullptr, nullptr, s,
                                     nullptr, nsub)));
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
