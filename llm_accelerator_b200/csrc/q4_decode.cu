@@ -410,6 +410,13 @@ int q4gpu_check_launch() {
     if (e_ != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
   } while (0)
 
+struct q4gpu_model;
+// A host <-> device copy that the model stream's kernels depend on: ordered on
+// that stream and finished before returning.  (A plain cudaMemcpy runs on the
+// legacy stream, which does not order against the non-blocking model stream,
+// and a pageable host-to-device cudaMemcpy may return before its DMA lands.)
+int stream_copy(q4gpu_model* m, void* dst, const void* src, size_t n, cudaMemcpyKind kind);
+
 namespace {
 
 constexpr int kMaxLayers = 28;
@@ -512,12 +519,21 @@ struct q4gpu_model {
   int alloc(T** p, size_t count) {
     void* v = nullptr;
     Q4_CUDA(cudaMalloc(&v, count * sizeof(T) + 256));
-    Q4_CUDA(cudaMemset(v, 0, count * sizeof(T) + 256));
+    // zeroed on the model stream (a plain cudaMemset runs on the legacy
+    // stream, which does not order against the non-blocking model stream)
+    Q4_CUDA(cudaMemsetAsync(v, 0, count * sizeof(T) + 256, stream));
+    Q4_CUDA(cudaStreamSynchronize(stream));
     allocs.push_back(v);
     *p = reinterpret_cast<T*>(v);
     return Q4GPU_OK;
   }
 };
+
+int stream_copy(q4gpu_model* m, void* dst, const void* src, size_t n, cudaMemcpyKind kind) {
+  Q4_CUDA(cudaMemcpyAsync(dst, src, n, kind, m->stream));
+  Q4_CUDA(cudaStreamSynchronize(m->stream));
+  return Q4GPU_OK;
+}
 
 namespace {
 
@@ -767,7 +783,7 @@ int check_persistent_error(q4gpu_model* m) {
   int e = 0;
   Q4_CUDA(cudaMemcpy(&e, m->p_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (e) {
-    cudaMemset(m->p_err, 0, sizeof(int));
+    cudaMemsetAsync(m->p_err, 0, sizeof(int), m->stream);
     return q4gpu_fail(Q4GPU_ERR_CUDA, e == 2 ? "persistent decode kernel: stepped past max_context"
                                              : "persistent decode kernel: a grid barrier wait ran out");
   }
@@ -857,7 +873,8 @@ int batch_prepare(q4gpu_model* m) {
     if ((rc = m->alloc(&m->b_bt2, (size_t)kBtRows * 2 * kHidden))) return rc;
     if ((rc = m->alloc(&m->b_bt3, (size_t)kBtRows * kInter))) return rc;
     if ((rc = m->alloc(&m->b_slots, m->slots.size()))) return rc;
-    Q4_CUDA(cudaMemcpy(m->b_slots, m->slots.data(), sizeof(SlotState) * m->slots.size(), cudaMemcpyHostToDevice));
+    if ((rc = stream_copy(m, m->b_slots, m->slots.data(), sizeof(SlotState) * m->slots.size(), cudaMemcpyHostToDevice)))
+      return rc;
     if ((rc = m->alloc(&m->b_lm_from, (size_t)m->cfg.max_seqs))) return rc;
     if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
     if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
@@ -873,7 +890,7 @@ int batch_prepare(q4gpu_model* m) {
     if ((rc = m->alloc(&m->b_att_cnt, (size_t)2 * kBatchSeqMax * kKvHeads))) return rc;
     {
       std::vector<int64_t> armed((size_t)kBatchSeqMax * kQHeads, INT64_MIN);
-      Q4_CUDA(cudaMemcpy(m->b_att_M, armed.data(), armed.size() * 8, cudaMemcpyHostToDevice));
+      if ((rc = stream_copy(m, m->b_att_M, armed.data(), armed.size() * 8, cudaMemcpyHostToDevice))) return rc;
     }
     Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
     for (int l = 0; l < L; ++l) {
@@ -980,9 +997,10 @@ int prefill_prepare(q4gpu_model* m) {
       (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * ((m->cfg.max_context + 63) / 64 * 64))))
     return rc;
   for (int sub = 0; sub < nsub; ++sub) {
-    Q4_CUDA(cudaMemset(p->bt1 + (sub * rows + 3 * kPfSub) * kHidden, 1, (size_t)kBatchOnes * kHidden));
-    Q4_CUDA(cudaMemset(p->bt2 + (sub * rows + 3 * kPfSub) * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden));
-    Q4_CUDA(cudaMemset(p->bt3 + (sub * rows + 3 * kPfSub) * kInter, 1, (size_t)kBatchOnes * kInter));
+    Q4_CUDA(cudaMemsetAsync(p->bt1 + (sub * rows + 3 * kPfSub) * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
+    Q4_CUDA(cudaMemsetAsync(p->bt2 + (sub * rows + 3 * kPfSub) * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden,
+                            m->stream));
+    Q4_CUDA(cudaMemsetAsync(p->bt3 + (sub * rows + 3 * kPfSub) * kInter, 1, (size_t)kBatchOnes * kInter, m->stream));
   }
   if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)rows)) ||
       (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)rows)) ||
@@ -1074,7 +1092,7 @@ int batch_check_error(q4gpu_model* m) {
   int e = 0;
   Q4_CUDA(cudaMemcpy(&e, m->b_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (e) {
-    cudaMemset(m->b_err, 0, sizeof(int));
+    cudaMemsetAsync(m->b_err, 0, sizeof(int), m->stream);
     return q4gpu_fail(Q4GPU_ERR_CUDA, "batched GEMM: a pipeline wait ran out");
   }
   return Q4GPU_OK;
@@ -1190,17 +1208,17 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   // default tables: gammas 1.0, LUTs, RoPE (float32 host build)
   {
     std::vector<int32_t> ones(kLayerGammas * L, 128), e(kExpLut), sg(kSigLut);
-    if (cudaMemcpy(m->gammas, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(m->g_final, ones.data(), kHidden * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (stream_copy(m, m->gammas, ones.data(), ones.size() * 4, cudaMemcpyHostToDevice) != Q4GPU_OK ||
+        stream_copy(m, m->g_final, ones.data(), kHidden * 4, cudaMemcpyHostToDevice) != Q4GPU_OK)
       return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "gamma init"));
     build_luts(e.data(), sg.data());
-    if (cudaMemcpy(m->exp_lut, e.data(), kExpLut * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(m->sig_lut, sg.data(), kSigLut * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (stream_copy(m, m->exp_lut, e.data(), kExpLut * 4, cudaMemcpyHostToDevice) != Q4GPU_OK ||
+        stream_copy(m, m->sig_lut, sg.data(), kSigLut * 4, cudaMemcpyHostToDevice) != Q4GPU_OK)
       return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "lut init"));
     std::vector<int32_t> c((size_t)cfg->max_context * kHeadDim), s(c.size());
     build_rope(cfg->max_context, c.data(), s.data());
-    if (cudaMemcpy(m->cos_tab, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemcpy(m->sin_tab, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (stream_copy(m, m->cos_tab, c.data(), c.size() * 4, cudaMemcpyHostToDevice) != Q4GPU_OK ||
+        stream_copy(m, m->sin_tab, s.data(), s.size() * 4, cudaMemcpyHostToDevice) != Q4GPU_OK)
       return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "rope init"));
   }
   // paged KV pool: every slot owns ceil(max_context / 64) pages
@@ -1212,7 +1230,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   {
     std::vector<int32_t> pt(n_pages);
     for (int64_t i = 0; i < n_pages; ++i) pt[i] = (int32_t)i;
-    if (cudaMemcpy(m->page_tables, pt.data(), n_pages * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+    if (stream_copy(m, m->page_tables, pt.data(), n_pages * 4, cudaMemcpyHostToDevice) != Q4GPU_OK)
       return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "page table init"));
   }
   // per-slot state
@@ -1261,7 +1279,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
     return fail(q4gpu_fail(Q4GPU_ERR_SHAPE, "max_context %d needs %zu B of shared memory", cfg->max_context, asmem));
   // persistent kernel: available when its shared memory fits (score buffer of max_context)
   if ((rc = m->alloc(&m->layers_dev, (size_t)L))) return fail(rc);
-  if (cudaMemcpy(m->layers_dev, m->layers, sizeof(LayerW) * L, cudaMemcpyHostToDevice) != cudaSuccess)
+  if (stream_copy(m, m->layers_dev, m->layers, sizeof(LayerW) * L, cudaMemcpyHostToDevice) != Q4GPU_OK)
     return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "layer table upload"));
   if ((rc = m->alloc(&m->p_qkv, (size_t)kQRows + 2 * kKvRows))) return fail(rc);
   if ((rc = m->alloc(&m->p_acc, (size_t)16 * kHidden))) return fail(rc);
@@ -1362,8 +1380,7 @@ static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, s
   const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
   if (to_device) m->b_stale = m->p_stale = true;
   auto cp = [&](void* dev, void* host, size_t n) -> int {
-    Q4_CUDA(to_device ? cudaMemcpy(dev, host, n, kind) : cudaMemcpy(host, dev, n, kind));
-    return Q4GPU_OK;
+    return to_device ? stream_copy(m, dev, host, n, kind) : stream_copy(m, host, dev, n, kind);
   };
   if (which >= Q4GPU_T_Q && which <= Q4GPU_T_DOWN) {
     if (layer < 0 || layer >= m->cfg.n_layers) return q4gpu_fail(Q4GPU_ERR_ARG, "bad layer");
@@ -1937,7 +1954,7 @@ static int kv_io(q4gpu_model* m, uintptr_t base, int32_t layer, int32_t kind, in
   int32_t* dev = nullptr;
   Q4_CUDA(cudaMalloc(&dev, n * 4));
   bool ok = true;
-  if (to_pool) ok = cudaMemcpy(dev, data, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (to_pool) ok = stream_copy(m, dev, data, n * 4, cudaMemcpyHostToDevice) == Q4GPU_OK;
   if (ok) {
     kv_copy_kernel<<<dim3(positions, kKvHeads), kHeadDim, 0, m->stream>>>(m->slots[base].kv, layer, kind, positions,
                                                                           dev, to_pool ? 1 : 0);
@@ -1963,7 +1980,7 @@ int q4gpu_model_write_hidden(q4gpu_model* m, uintptr_t base, const int32_t* hidd
   int rc = set_device(m);
   if (rc) return rc;
   Q4_CUDA(cudaStreamSynchronize(m->stream));
-  Q4_CUDA(cudaMemcpy(m->slots[base].hidden, hidden, kHidden * 4, cudaMemcpyHostToDevice));
+  return stream_copy(m, m->slots[base].hidden, hidden, kHidden * 4, cudaMemcpyHostToDevice);
   return Q4GPU_OK;
 }
 

@@ -163,7 +163,7 @@ class Q4Model:
         rc = self.lib.q4gpu_decode_batch(self.handle, len(prompts), _ptr(flat), _ptr(lens), max_new_tokens,
                                          _ptr(gen), _ptr(scores))
         if rc != 0:
-            raise QotError(rc, "q4gpu_decode_batch")
+            raise QotError(rc, "q4gpu_decode_batch: " + self.lib.q4gpu_last_error().decode(errors="replace"))
         return gen.astype(np.int64), scores
 
     # -- batched decode (up to 64 slots per step) ------------------------------
