@@ -1243,6 +1243,262 @@ __device__ __forceinline__ int4 head_norm_rope(const int32_t* row, const int32_t
   return make_int4(o[0], o[1], o[2], o[3]);
 }
 
+// ---------------------------------------------------------------------------
+// Cluster attention for small batches and long contexts: the 8 CTAs of a
+// thread-block cluster share one (KV head, sequence) pair, each streaming
+// one eighth of the context through a ring of 32-key chunks (K, then V).
+// The exact two-pass LUT softmax is resolved over DSMEM: every rank
+// publishes its row maxima, then its exp sums, and reads the others' after a
+// cluster barrier; the probability table uses a Barrett reciprocal of the
+// total (R = floor((2^64 - 1) / sum), q = mulhi(n, R) is at most one below
+// floor(n / sum) for n < 2^37 and a remainder test makes it exact); rank 0
+// adds the eight ranks' int64 value sums and writes the o_proj limbs.  No
+// global scratch, no atomics, no single-CTA tail over the whole context.
+// ---------------------------------------------------------------------------
+constexpr int kClRanks = 8;
+constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds (max_ctx <= 32768)
+
+__device__ __forceinline__ uint32_t barrett_div(uint64_t n, uint64_t d, uint64_t rcp) {
+  uint64_t q = __umul64hi(n, rcp);
+  uint64_t rem = n - q * d;
+  if (rem >= d) {
+    ++q;
+    rem -= d;
+  }
+  if (rem >= d) ++q;
+  return (uint32_t)q;
+}
+
+__global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
+                                                            const int32_t* __restrict__ g_k,
+                                                            const int32_t* __restrict__ cos_tab,
+                                                            const int32_t* __restrict__ sin_tab,
+                                                            const int32_t* __restrict__ exp_lut, int kpr_cap) {
+  extern __shared__ __align__(128) uint8_t cl_smem[];
+  int32_t* ring = reinterpret_cast<int32_t*>(cl_smem);                            // [2][32][128]
+  int64_t* sc = reinterpret_cast<int64_t*>(cl_smem + kAttnRing * kAttnChunkBytes);  // [2][kpr_cap]
+  __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v of the new position
+  __shared__ uint32_t probtab[2][kExpLut];
+  __shared__ int64_t red[2][8];
+  __shared__ int64_t xmax[2], xsum[2];       // published to the cluster
+  __shared__ int64_t part[2][kHeadDim];      // this rank's value sums, published to the cluster
+  __shared__ uint64_t bars[kAttnRing];
+  const int rank = blockIdx.x, kv = blockIdx.y, m = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  grid_dep_wait();
+  grid_dep_launch();
+  // every rank reaches every cluster barrier below: no early return
+  const int pos = c.pos0[4 * m];
+  const bool live = pos < c.max_ctx;
+  const int ctx = live ? pos + 1 : 0;
+  const int kpr = ((ctx + kClRanks - 1) / kClRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+  const int k0 = rank * kpr;
+  const int k1 = k0 + kpr < ctx ? k0 + kpr : ctx;  // this rank's keys [k0, k1)
+  const int nloc = k1 > k0 ? k1 - k0 : 0;
+  const KvView kvv = c.slots[m].kv;
+  const int nk = (nloc + kAttnChunk - 1) / kAttnChunk, total = 2 * nk;
+  const int kend = k1 < pos ? k1 : pos;  // cached keys of the range (the new position comes from shared memory)
+  auto issue = [&](int i) {
+    const int kind = i < nk ? 0 : 1, j = i < nk ? i : i - nk;
+    const int p0 = k0 + j * kAttnChunk;
+    int n = kend - p0;
+    n = n < 0 ? 0 : (n > kAttnChunk ? kAttnChunk : n);
+    uint64_t* b = bars + i % kAttnRing;
+    umma::bar_expect_tx(b, (uint32_t)n * kHeadDim * 4);
+    if (n > 0)
+      bulk_load(ring + (i % kAttnRing) * kAttnChunk * kHeadDim, kvv.at(layer, kind, kv, p0), (uint32_t)n * kHeadDim * 4,
+                b);
+  };
+  if (t == 0) {
+    for (int s = 0; s < kAttnRing; ++s) umma::bar_init(bars + s, 1);
+    umma::bar_init_fence();
+    for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
+  }
+  if (live) {
+    const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
+    const bool owner = pos >= k0 && pos < k1;  // the rank whose range holds the new position appends it
+    if (warp < 2) {
+      reinterpret_cast<int4*>(hv[warp])[lane] =
+          head_norm_rope(raw + (2 * kv + warp) * kHeadDim, g_q, cos_tab, sin_tab, pos, lane);
+    } else if (warp == 2) {
+      const int4 k4 = head_norm_rope(raw + kQRows + kv * kHeadDim, g_k, cos_tab, sin_tab, pos, lane);
+      reinterpret_cast<int4*>(hv[2])[lane] = k4;
+      if (owner) reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = k4;
+    } else if (warp == 3) {
+      const int4 v4 = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
+      reinterpret_cast<int4*>(hv[3])[lane] = v4;
+      if (owner) reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
+    }
+  }
+  __syncthreads();
+  bool ok = true;
+  // scores of the range: 32 keys per chunk, 4 per warp, 8 lanes per key
+  int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
+  {
+    const int sub = lane & 7, quad = lane >> 3;
+    int32_t q0[16], q1[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int4 a = *reinterpret_cast<const int4*>(&hv[0][4 * (sub + 8 * j)]);
+      const int4 b = *reinterpret_cast<const int4*>(&hv[1][4 * (sub + 8 * j)]);
+      q0[4 * j] = a.x; q0[4 * j + 1] = a.y; q0[4 * j + 2] = a.z; q0[4 * j + 3] = a.w;
+      q1[4 * j] = b.x; q1[4 * j + 1] = b.y; q1[4 * j + 2] = b.z; q1[4 * j + 3] = b.w;
+    }
+    for (int i = 0; i < nk; ++i) {
+      if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+      const int lp = i * kAttnChunk + warp * 4 + quad, p = k0 + lp;
+      const int32_t* krow = p == pos ? hv[2] : ring + ((i % kAttnRing) * kAttnChunk + warp * 4 + quad) * kHeadDim;
+      int64_t s0 = 0, s1 = 0;
+      if (p < k1) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * (sub + 8 * j));
+          const int32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            s0 = mad_wide(q0[4 * j + e], kk[e], s0);
+            s1 = mad_wide(q1[4 * j + e], kk[e], s1);
+          }
+        }
+      }
+#pragma unroll
+      for (int msk = 1; msk < 8; msk <<= 1) {
+        s0 += shfl_xor_i64(s0, msk);
+        s1 += shfl_xor_i64(s1, msk);
+      }
+      if (p < k1) {
+        const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
+        if (sub == 0) {
+          sc[lp] = v0;
+          sc[kpr_cap + lp] = v1;
+        }
+        mx0 = v0 > mx0 ? v0 : mx0;
+        mx1 = v1 > mx1 ? v1 : mx1;
+      }
+      __syncthreads();  // slot i % 2 is free again
+      if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+    }
+  }
+#pragma unroll
+  for (int msk = 8; msk < 32; msk <<= 1) {
+    const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
+    mx0 = o0 > mx0 ? o0 : mx0;
+    mx1 = o1 > mx1 ? o1 : mx1;
+  }
+  if (lane == 0) {
+    red[0][warp] = mx0;
+    red[1][warp] = mx1;
+  }
+  __syncthreads();
+  if (t < 2) {
+    int64_t b = red[t][0];
+    for (int w = 1; w < 8; ++w) b = red[t][w] > b ? red[t][w] : b;
+    xmax[t] = b;
+  }
+  umma::cluster_sync();  // every rank's maxima are published
+  mx0 = INT64_MIN;
+  mx1 = INT64_MIN;
+#pragma unroll
+  for (int r = 0; r < kClRanks; ++r) {
+    const int64_t o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[0]), (uint32_t)r));
+    const int64_t o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[1]), (uint32_t)r));
+    mx0 = o0 > mx0 ? o0 : mx0;
+    mx1 = o1 > mx1 ? o1 : mx1;
+  }
+  // LUT indices and exp sums of the range
+  int64_t sum0 = 0, sum1 = 0;
+  for (int lp = t; lp < nloc; lp += blockDim.x) {
+    const int i0 = lut_index(mx0, sc[lp]), i1 = lut_index(mx1, sc[kpr_cap + lp]);
+    sc[lp] = i0;
+    sc[kpr_cap + lp] = i1;
+    sum0 += exp_lut[i0];
+    sum1 += exp_lut[i1];
+  }
+  sum0 = warp_sum_i64(sum0);
+  sum1 = warp_sum_i64(sum1);
+  __syncthreads();  // red reused
+  if (lane == 0) {
+    red[0][warp] = sum0;
+    red[1][warp] = sum1;
+  }
+  __syncthreads();
+  if (t < 2) {
+    int64_t b = 0;
+    for (int w = 0; w < 8; ++w) b += red[t][w];
+    xsum[t] = b;
+  }
+  umma::cluster_sync();  // every rank's sums are published
+  sum0 = 0;
+  sum1 = 0;
+#pragma unroll
+  for (int r = 0; r < kClRanks; ++r) {
+    sum0 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[0]), (uint32_t)r));
+    sum1 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[1]), (uint32_t)r));
+  }
+  if (live) {
+    const uint64_t d0 = (uint64_t)sum0, d1 = (uint64_t)sum1, r0 = ~0ULL / d0, r1 = ~0ULL / d1;
+    for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
+      const int h = i >= kExpLut, e = i - h * kExpLut;
+      probtab[h][e] = barrett_div((uint64_t)exp_lut[e] << 16, h ? d1 : d0, h ? r1 : r0);
+    }
+  }
+  __syncthreads();
+  for (int lp = t; lp < nloc; lp += blockDim.x) {
+    sc[lp] = probtab[0][(int)sc[lp]];
+    sc[kpr_cap + lp] = probtab[1][(int)sc[kpr_cap + lp]];
+  }
+  __syncthreads();
+  // values of the range: thread (warp, lane) accumulates dims 4 lane .. +3 of
+  // the chunk's keys warp, warp + 8, warp + 16, warp + 24 for both heads
+  int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
+  for (int i = nk; i < total; ++i) {
+    if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+    const int base = (i - nk) * kAttnChunk;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int lp = base + warp + 8 * u, p = k0 + lp;
+      if (p < k1) {
+        const int32_t* vrow = p == pos ? hv[3] : ring + ((i % kAttnRing) * kAttnChunk + warp + 8 * u) * kHeadDim;
+        const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
+        const int32_t p0 = (int32_t)sc[lp], p1 = (int32_t)sc[kpr_cap + lp];
+        const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          a0[e] = mad_wide(p0, vv[e], a0[e]);
+          a1[e] = mad_wide(p1, vv[e], a1[e]);
+        }
+      }
+    }
+    __syncthreads();
+    if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+  }
+  if (!ok) atomicExch(c.err, 4);
+  // cross-warp sums through the idle ring [8][2][128], then published
+  int64_t* wpart = reinterpret_cast<int64_t*>(cl_smem);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    wpart[(warp * 2 + 0) * kHeadDim + 4 * lane + e] = a0[e];
+    wpart[(warp * 2 + 1) * kHeadDim + 4 * lane + e] = a1[e];
+  }
+  __syncthreads();
+  {
+    const int h = t >> 7, d = t & (kHeadDim - 1);
+    int64_t acc = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc += wpart[(w * 2 + h) * kHeadDim + d];
+    part[h][d] = acc;
+  }
+  umma::cluster_sync();  // every rank's value sums are published
+  if (rank == 0 && live) {
+    const int h = t >> 7, d = t & (kHeadDim - 1);
+    int64_t acc = 0;
+#pragma unroll
+    for (int r = 0; r < kClRanks; ++r) acc += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&part[h][d]), (uint32_t)r));
+    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
+  }
+  umma::cluster_sync();  // no rank leaves while rank 0 still reads its shared memory
+}
+
 // Per (KV head, column): q heads 2 kv, 2 kv + 1 normed and roped in place in
 // qkv, k normed and roped into the cache, v copied into the cache.
 __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __restrict__ col_slots,
@@ -1668,6 +1924,27 @@ cudaError_t launch_ex(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStre
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// PDL launch with thread-block clusters of `cluster_x` CTAs along x
+template <typename... KArgs, typename... Args>
+cudaError_t launch_cluster_x(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, int cluster_x,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g;
+  cfg.blockDim = b;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, Args... args) {
   return launch_ex(k, g, b, smem, s, 1, args...);
@@ -1694,6 +1971,14 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
 }
 
 bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
+// keys per cluster rank the score buffer must hold, and whether the cluster kernel covers max_ctx
+int attn_cl_kpr(const BatchPlan& p) {
+  return ((p.max_ctx + kClRanks - 1) / kClRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+}
+bool attn_cluster(const BatchPlan& p) { return !attn_one_cta_per_head(p) && attn_cl_kpr(p) <= kClKprMax; }
+size_t attn_cl_smem(const BatchPlan& p) {
+  return (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * attn_cl_kpr(p) * 8;
+}
 
 template <int SP>
 int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
@@ -1734,6 +2019,9 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
                     p.sin_tab, p.exp_lut));
+    } else if (attn_cluster(p)) {
+      BQ(launch_cluster_x(batch_attn_cl_kernel, dim3(kClRanks, kKvHeads, p.S), dim3(256), attn_cl_smem(p), s,
+                          kClRanks, c, l, w.g_q, w.g_k, p.cos_tab, p.sin_tab, p.exp_lut, attn_cl_kpr(p)));
     } else {
       BQ(launch_pdl(batch_attn_scores_kernel, attn_grid, dim3(256), 0, s, c, as, l, w.g_q, w.g_k, p.cos_tab,
                     p.sin_tab, p.exp_lut));
@@ -1778,6 +2066,8 @@ int setup_t(const BatchPlan& p) {
   if ((rc = set_smem<SP, kGemmQkv>()) || (rc = set_smem<SP, kGemmO>()) || (rc = set_smem<SP, kGemmGu>()) ||
       (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
     return rc;
+  if (attn_cluster(p))
+    BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_cl_smem(p)));
   if (attn_one_cta_per_head(p))
     BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
