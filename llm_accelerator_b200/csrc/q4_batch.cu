@@ -619,9 +619,12 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     sum0 += red[0][w];
     sum1 += red[1][w];
   }
-  for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
-    const int h = i >= kExpLut, e = i - h * kExpLut;
-    probtab[h][e] = (uint32_t)udiv_exact((uint64_t)exp_lut[e] << 16, (uint64_t)(h ? sum1 : sum0));
+  {
+    const uint64_t d0 = (uint64_t)sum0, d1 = (uint64_t)sum1, r0 = ~0ULL / d0, r1 = ~0ULL / d1;
+    for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
+      const int h = i >= kExpLut, e = i - h * kExpLut;
+      probtab[h][e] = barrett_div((uint64_t)exp_lut[e] << 16, h ? d1 : d0, h ? r1 : r0);
+    }
   }
   __syncthreads();
   // per-position probabilities of both heads, packed over the index array
@@ -1258,17 +1261,6 @@ __device__ __forceinline__ int4 head_norm_rope(const int32_t* row, const int32_t
 constexpr int kClRanks = 8;
 constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds (max_ctx <= 32768)
 
-__device__ __forceinline__ uint32_t barrett_div(uint64_t n, uint64_t d, uint64_t rcp) {
-  uint64_t q = __umul64hi(n, rcp);
-  uint64_t rem = n - q * d;
-  if (rem >= d) {
-    ++q;
-    rem -= d;
-  }
-  if (rem >= d) ++q;
-  return (uint32_t)q;
-}
-
 __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
                                                             const int32_t* __restrict__ cos_tab,
@@ -1741,24 +1733,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
     rrcp[t] = s > 0 ? ~0ULL / s : 0;
   }
   __syncthreads();
-  // prob[e] = floor((lut[e] << 16) / sum) by a Barrett reciprocal: with
-  // R = floor((2^64 - 1) / sum) and n < 2^37, q = mulhi(n, R) is at most two
-  // below the quotient, and the remainder test fixes it exactly
+  // prob[e] = floor((lut[e] << 16) / sum) by the row's Barrett reciprocal
   for (int i = t; i < kPfRows * kExpLut; i += kPfThreads) {
     const int r = i / kExpLut, e = i - r * kExpLut;
-    const uint64_t s = rsum[r], n = (uint64_t)elut[e] << 16;
-    uint32_t p = 0;
-    if (s > 0) {
-      uint64_t q = __umul64hi(n, rrcp[r]);
-      uint64_t rem = n - q * s;
-      if (rem >= s) {
-        ++q;
-        rem -= s;
-      }
-      if (rem >= s) ++q;
-      p = (uint32_t)q;
-    }
-    ptab[i] = p;
+    const uint64_t s = rsum[r];
+    ptab[i] = s > 0 ? barrett_div((uint64_t)elut[e] << 16, s, rrcp[r]) : 0u;
   }
   // pass 3: probability-weighted values.  Warp (mt, kq) takes output rows
   // 16 mt .. +15 and dims 32 kq .. +31 (four 8-dim MMA tiles, two at a time);

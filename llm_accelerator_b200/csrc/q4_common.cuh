@@ -154,6 +154,16 @@ __device__ __forceinline__ uint64_t udiv_exact(uint64_t n, uint64_t d) {
   return q;
 }
 
+// floor(n / d) (a quotient below 2^32) with a precomputed Barrett reciprocal
+// rcp = floor((2^64 - 1) / d), d > 0 (Barrett, 1986): rcp >= (2^64 - d) / d, so
+// n rcp / 2^64 > n / d - n / 2^64 > n / d - 1 and q = mulhi(n, rcp) is the
+// quotient or one below it; one remainder test makes it exact.
+__device__ __forceinline__ uint32_t barrett_div(uint64_t n, uint64_t d, uint64_t rcp) {
+  uint64_t q = __umul64hi(n, rcp);
+  if (n - q * d >= d) ++q;
+  return (uint32_t)q;
+}
+
 __device__ __forceinline__ int64_t shfl_xor_i64(int64_t v, int m) {
   return (int64_t)__shfl_xor_sync(0xFFFFFFFFu, (unsigned long long)v, m);
 }
