@@ -1247,19 +1247,19 @@ __device__ __forceinline__ int4 head_norm_rope(const int32_t* row, const int32_t
 }
 
 // ---------------------------------------------------------------------------
-// Cluster attention for small batches and long contexts: the 8 CTAs of a
-// thread-block cluster share one (KV head, sequence) pair, each streaming
-// one eighth of the context through a ring of 32-key chunks (K, then V).
+// Cluster attention for small batches and long contexts: the R CTAs of a
+// thread-block cluster (R = gridDim.x: 8, or 16 for batches of up to four
+// sequences) share one (KV head, sequence) pair, each streaming 1/R of the
+// context through a ring of 32-key chunks (K, then V).
 // The exact two-pass LUT softmax is resolved over DSMEM: every rank
 // publishes its row maxima, then its exp sums, and reads the others' after a
 // cluster barrier; the probability table uses a Barrett reciprocal of the
 // total (R = floor((2^64 - 1) / sum), q = mulhi(n, R) is at most one below
 // floor(n / sum) for n < 2^37 and a remainder test makes it exact); rank 0
-// adds the eight ranks' int64 value sums and writes the o_proj limbs.  No
+// adds the ranks' int64 value sums and writes the o_proj limbs.  No
 // global scratch, no atomics, no single-CTA tail over the whole context.
 // ---------------------------------------------------------------------------
-constexpr int kClRanks = 8;
-constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds (max_ctx <= 32768)
+constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds
 
 __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
@@ -1275,7 +1275,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   __shared__ int64_t xmax[2], xsum[2];       // published to the cluster
   __shared__ int64_t part[2][kHeadDim];      // this rank's value sums, published to the cluster
   __shared__ uint64_t bars[kAttnRing];
-  const int rank = blockIdx.x, kv = blockIdx.y, m = blockIdx.z;
+  const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   grid_dep_wait();
   grid_dep_launch();
@@ -1283,7 +1283,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   const int pos = c.pos0[4 * m];
   const bool live = pos < c.max_ctx;
   const int ctx = live ? pos + 1 : 0;
-  const int kpr = ((ctx + kClRanks - 1) / kClRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+  const int kpr = ((ctx + nranks - 1) / nranks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
   const int k0 = rank * kpr;
   const int k1 = k0 + kpr < ctx ? k0 + kpr : ctx;  // this rank's keys [k0, k1)
   const int nloc = k1 > k0 ? k1 - k0 : 0;
@@ -1390,8 +1390,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   umma::cluster_sync();  // every rank's maxima are published
   mx0 = INT64_MIN;
   mx1 = INT64_MIN;
-#pragma unroll
-  for (int r = 0; r < kClRanks; ++r) {
+  for (int r = 0; r < nranks; ++r) {
     const int64_t o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[0]), (uint32_t)r));
     const int64_t o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[1]), (uint32_t)r));
     mx0 = o0 > mx0 ? o0 : mx0;
@@ -1422,8 +1421,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   umma::cluster_sync();  // every rank's sums are published
   sum0 = 0;
   sum1 = 0;
-#pragma unroll
-  for (int r = 0; r < kClRanks; ++r) {
+  for (int r = 0; r < nranks; ++r) {
     sum0 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[0]), (uint32_t)r));
     sum1 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[1]), (uint32_t)r));
   }
@@ -1484,8 +1482,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   if (rank == 0 && live) {
     const int h = t >> 7, d = t & (kHeadDim - 1);
     int64_t acc = 0;
-#pragma unroll
-    for (int r = 0; r < kClRanks; ++r) acc += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&part[h][d]), (uint32_t)r));
+    for (int r = 0; r < nranks; ++r) acc += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&part[h][d]), (uint32_t)r));
     write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
   }
   umma::cluster_sync();  // no rank leaves while rank 0 still reads its shared memory
@@ -1950,9 +1947,12 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const 
 }
 
 bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
-// keys per cluster rank the score buffer must hold, and whether the cluster kernel covers max_ctx
+// cluster size of the cluster attention (16 CTAs for batches of up to 4 sequences), the keys per
+// rank its score buffer must hold, and whether it covers max_ctx
+int attn_cl_ranks(const BatchPlan& p) { return p.S <= 4 ? 16 : 8; }
 int attn_cl_kpr(const BatchPlan& p) {
-  return ((p.max_ctx + kClRanks - 1) / kClRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+  const int r = attn_cl_ranks(p);
+  return ((p.max_ctx + r - 1) / r + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
 }
 bool attn_cluster(const BatchPlan& p) { return !attn_one_cta_per_head(p) && attn_cl_kpr(p) <= kClKprMax; }
 size_t attn_cl_smem(const BatchPlan& p) {
@@ -1999,8 +1999,8 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
                     p.sin_tab, p.exp_lut));
     } else if (attn_cluster(p)) {
-      BQ(launch_cluster_x(batch_attn_cl_kernel, dim3(kClRanks, kKvHeads, p.S), dim3(256), attn_cl_smem(p), s,
-                          kClRanks, c, l, w.g_q, w.g_k, p.cos_tab, p.sin_tab, p.exp_lut, attn_cl_kpr(p)));
+      BQ(launch_cluster_x(batch_attn_cl_kernel, dim3(attn_cl_ranks(p), kKvHeads, p.S), dim3(256), attn_cl_smem(p),
+                          s, attn_cl_ranks(p), c, l, w.g_q, w.g_k, p.cos_tab, p.sin_tab, p.exp_lut, attn_cl_kpr(p)));
     } else {
       BQ(launch_pdl(batch_attn_scores_kernel, attn_grid, dim3(256), 0, s, c, as, l, w.g_q, w.g_k, p.cos_tab,
                     p.sin_tab, p.exp_lut));
@@ -2045,8 +2045,10 @@ int setup_t(const BatchPlan& p) {
   if ((rc = set_smem<SP, kGemmQkv>()) || (rc = set_smem<SP, kGemmO>()) || (rc = set_smem<SP, kGemmGu>()) ||
       (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
     return rc;
-  if (attn_cluster(p))
+  if (attn_cluster(p)) {
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_cl_smem(p)));
+    BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  }
   if (attn_one_cta_per_head(p))
     BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                             (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
