@@ -15,8 +15,11 @@ a cycle replays the same tokens).  Per step the weights (420 MB of int8
 copies) and the KV cache of 64 sequences (~5.6 GB at the mean context 384)
 stream from HBM: far larger than L2, so no flush is needed.
 
-Secondary: batch 1, prompt 128, decode positions
-128..255, on the persistent cooperative kernel.
+Secondary (one GPU only): `batch1`: batch 1, prompt 128,
+decode positions 128..255, on the persistent cooperative kernel; `gemv`
+(config 1); `cfg5` (config 5 on one GPU: 8 x 8192-token prompts through the
+batched exact prefill, decode from position 8192).  `--cfg5` runs config 5
+alone, on N GPUs with the vocabulary-sharded LM head.
 
 N > 1 (torchrun, one rank per GPU): every rank decodes its own 64 sequences
 (prompt seeds depend on the rank); no collective on the data path; value is
@@ -57,6 +60,7 @@ CYCLE = GEN - 1  # decode steps of one generation: positions 256..510
 WORKLOAD = ("cfg4: Qwen3-0.6B 28-layer Q4 (int4 + Q2.14 group scales) greedy decode, 64 sequences per GPU, "
             "prompt 256 uniform ids each, 256 generated tokens, context up to 512, decode positions 256..510 cycled")
 B1_PROMPT, B1_CYCLE = 128, 128
+CFG5_SEQS, CFG5_PROMPT, CFG5_GEN = 8, 8192, 512
 HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 
 
@@ -269,6 +273,47 @@ def batch1_secondary(device: int, steps: int) -> dict:
             "steps": steps, "mode": "persistent cooperative kernel" if mode == 1 else "per-stage CUDA graphs",
             "e2e": {"value": round(n_e2e / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 12, "api": "q4gpu_run_token (qot_session_runner_fn)"}}
+
+
+def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16) -> dict:
+    """Config 5 on one GPU: 8 sequences with 8192-token prompts (batched exact
+    prefill), greedy decode from position 8192; the attention kernel's K/V bytes
+    against HBM at that context."""
+    import torch
+
+    from llm_accelerator_b200.model import Q4Model
+
+    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=CFG5_PROMPT + CFG5_GEN, max_seqs=CFG5_SEQS, device=device)
+    m.init_synthetic(seed=0)
+    prompts = [np.random.default_rng(50_000 + i).integers(0, VOCAB, CFG5_PROMPT).tolist() for i in range(CFG5_SEQS)]
+    m.decode_batch([prompts[0][:2]], 1)  # int8 copies and prefill buffers
+    t0 = time.perf_counter()
+    m.decode_batch(prompts, 1)
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.ExternalStream(m.stream)
+    m.batch_steps(3, CFG5_SEQS)
+    m.batch_set_position(CFG5_PROMPT, CFG5_SEQS)
+    m.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    m.batch_steps(steps, CFG5_SEQS)
+    e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks = m.read_tokens(CFG5_PROMPT, 4, slot=0)[0].tolist()
+    kt = m.batch_time_kernels(CFG5_SEQS, reps=2)
+    ctx = CFG5_PROMPT + steps + 2
+    m.close()
+    att_ms = kt["attention"][0]
+    gbs = batch_kernel_bytes("attention", CFG5_SEQS, ctx) / (att_ms * 1e-3) / 1e9
+    return {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (seeds 50000..), batched exact prefill, "
+                        "greedy decode from position 8192, full vocabulary on one GPU",
+            "value": round(CFG5_SEQS * steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
+            "steps": steps, "prefill_s": round(prefill_s, 3),
+            "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
+            "attention": {"kernel": "batch_attn_cl_kernel (8-CTA clusters)", "ms_per_launch": round(att_ms, 5),
+                          "context": ctx, "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)},
+            "first_tokens_seq0": toks}
 
 
 def gemv_secondary(device: int, peak_gbs: float) -> dict:
@@ -494,6 +539,7 @@ def run_ours(args, ws, rank, local):
         if ws == 1:
             line["batch1"] = batch1_secondary(local, 128)
             line["gemv"] = gemv_secondary(local, peaks["hbm_gbs"])
+            line["cfg5"] = cfg5_secondary(local, peaks["hbm_gbs"])
             if not args.no_cpu_baseline:
                 c = cpu_decode(args.cpu_steps, 2)
                 line["cpu_baseline"] = {
@@ -517,7 +563,6 @@ def run_ours(args, ws, rank, local):
 # LM head is vocabulary-sharded with an NCCL exchange of the (score, row)
 # winners.  Prints its own JSON line (rank 0).
 # ---------------------------------------------------------------------------
-CFG5_SEQS, CFG5_PROMPT, CFG5_GEN = 8, 8192, 512
 
 
 def run_cfg5(args, ws, rank, local):
