@@ -192,7 +192,6 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
 // Integer sums are order independent, so the result equals the serial one.
 // ---------------------------------------------------------------------------
 constexpr int kPage = kKvPage;  // 64 positions per unit
-constexpr int kPageBytes = kPage * kHeadDim * 4;
 
 struct AttnScratch {
   int64_t* S;         // [64 seqs][16 heads][max_ctx] scaled scores
