@@ -121,3 +121,20 @@ def test_prefill_sharp_attention_matches_serial():
     for i in range(len(prompts)):
         for a, b in zip(kv1[i], kv0[i]):
             assert np.array_equal(a, b), i
+
+
+def test_long_prompt_matches_c_oracle():
+    """A 2050-token prompt (one layer): prefill query tiles over 33 KV pages and
+    batched decode steps through the 16-CTA cluster attention (160 keys per
+    rank, several chunks each) give the C oracle's tokens and scores."""
+    L1, V1, ctx, n_gen = 1, 256, 2064, 3
+    prompt = np.random.default_rng(17).integers(0, V1, 2050).tolist()
+    with Q4Model(n_layers=L1, vocab=V1, max_context=ctx, max_seqs=1) as m:
+        m.init_synthetic(seed=SEED, std=0.02, gamma_std=GAMMA)
+        gen, scores = m.decode_batch([prompt], n_gen)
+    cm = CModel(L1, V1, ctx, seed=SEED, std=0.02, gamma_std=GAMMA)
+    try:
+        ref, ref_scores = cm.decode(prompt, n_gen)
+    finally:
+        cm.close()
+    assert gen[0].tolist() == ref and scores[0].tolist() == ref_scores
