@@ -257,12 +257,38 @@ class Q4Model:
         _native.check(self.lib.q4gpu_model_set_mode(self.handle, value), "q4gpu_model_set_mode")
 
     def trace_persistent(self, n_steps: int, lm_from: int = 0, slot: int = 0) -> np.ndarray:
-        """[barriers, 2] (last arrival, release) ns of a persistent run."""
-        n = n_steps * (5 * self.n_layers + 1)
+        """[barriers, 2] (last arrival, release) ns of a persistent run: per step
+        3 grid barriers per layer (after QKV, after attention + o_proj, after
+        gate/up + down) and one after the LM head."""
+        n = n_steps * (3 * self.n_layers + 1)
         st = np.zeros((n, 2), dtype=np.uint64)
         _native.check(self.lib.q4gpu_model_trace_persistent(self.handle, slot, n_steps, lm_from, _ptr(st), n),
                       "q4gpu_model_trace_persistent")
         return st
+
+    def persistent_stage_times(self, n_steps: int = 4, slot: int = 0) -> dict:
+        """Mean µs per stage of the persistent decode kernel from its barrier
+        timeline over steps 2..n_steps of a run from the slot's position:
+        {stage: [work (previous release -> last arrival), barrier (last arrival
+        -> release)]} for qkv, attn_o, gateup_down and lm, plus step_us."""
+        st = self.trace_persistent(n_steps, slot=slot).astype(np.int64)
+        per_step = 3 * self.n_layers + 1
+        names = ["qkv", "attn_o", "gateup_down"]
+        work = {k: [] for k in names + ["lm"]}
+        bar = {k: [] for k in names + ["lm"]}
+        for s in range(1, n_steps):
+            base = s * per_step
+            prev = st[base - 1, 1]
+            for i in range(per_step):
+                arr, rel = st[base + i]
+                k = "lm" if i == per_step - 1 else names[i % 3]
+                work[k].append(arr - prev)
+                bar[k].append(rel - arr)
+                prev = rel
+        out = {"step_us": round(float(st[n_steps * per_step - 1, 1] - st[per_step - 1, 1]) / (n_steps - 1) / 1e3, 1)}
+        for k in names + ["lm"]:
+            out[k] = [round(float(np.mean(work[k])) / 1e3, 2), round(float(np.mean(bar[k])) / 1e3, 2)]
+        return out
 
     def set_position(self, position: int, slot: int = 0) -> None:
         _native.check(self.lib.q4gpu_model_set_position(self.handle, slot, position), "q4gpu_model_set_position")
