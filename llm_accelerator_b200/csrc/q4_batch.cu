@@ -1151,39 +1151,41 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
 // the serial one bit for bit.
 //
 // Attention (prefill_attn_kernel): one CTA per (KV head, query tile of up to
-// 32 consecutive positions of one sequence), 64 query rows (the two heads of
+// 64 consecutive positions of one sequence), 128 query rows (the two heads of
 // the group).  The exact LUT softmax is done in three passes over 64-key
-// chunks of the cache (cp.async into a staging buffer, then re-laid out in
-// padded shared-memory rows):
-//   1. scaled scores -> row maxima;
+// chunks of the cache (cp.async into a staging buffer, then re-laid out):
+//   1. scores -> row maxima;
 //   2. scores again -> LUT indices (kept in a u16 scratch) and exp sums;
 //      then a probability table per row, prob[e] = (lut[e] << 16) / sum;
-//   3. values: sum over keys of prob[idx] * v, then sat24(>> 16) as limbs of
-//      the o_proj input.
-// Scores run on the tensor cores (mma.sync m16n8k32, 8-bit): q and k are
-// signed 24-bit, split into byte limbs x = x0 + 2^8 x1 + 2^16 x2 (x0, x1
-// unsigned, x2 signed), and
-//   q k = sum_{a,b} 2^(8 (a + b)) qa kb
-// takes nine limb products per tile, accumulated by shift into five int32
-// sums (each below 3 * 128 * 255^2 in magnitude) and combined in int64.
-// Values likewise: p (0 .. 2^16) = p0 + 2^8 p1 + 2^16 p2 with p2 in {0, 1}
-// (its three products are skipped for chunks where no p reaches 2^16), v in
-// byte limbs, five int32 sums per 64-key chunk folded into int64.  The
-// results are the integers the int64 decode kernels compute.
+//   3. values, one head at a time: sum over keys of prob[idx] * v, then
+//      sat24(>> 16) as limbs of the o_proj input.
+// q and k are signed 24-bit, split into byte limbs x = x0 + 2^8 x1 + 2^16 x2
+// (x0, x1 unsigned, x2 signed), and
+//   q k = sum_{a,b} 2^(8 (a + b)) qa kb.
+// Scores run on the 5th-generation tensor cores: the limb planes sit in
+// shared memory as 128-byte-swizzled K-major UMMA operands (q: M = 128 rows,
+// keys: N = 64), one thread issues tcgen05.mma kind::i8 for the nine limb
+// products (u8 / s8 per operand) into five TMEM accumulators, one per shift
+// (each below 3 * 128 * 255^2 in magnitude), and all 16 warps read them back
+// with tcgen05.ld and combine them in int64.  Values use mma.sync m16n8k32 on
+// byte limbs likewise: p (0 .. 2^16) = p0 + 2^8 p1 + 2^16 p2 with p2 in
+// {0, 1} (its three products are skipped for chunks where no p reaches 2^16),
+// five int32 sums per 64-key chunk folded into int64.  The results are the
+// integers the int64 decode kernels compute.
 // ---------------------------------------------------------------------------
 constexpr int kPfStride = kHeadDim + 4;   // staged int32 key row (words): 16-byte aligned rows
-constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA
-constexpr int kPfThreads = 512;           // 16 warps: 4 row tiles x 4 key (or dim) quarters
-constexpr int kPfQuarters = 4;
-constexpr int kPfLStride = kHeadDim + 16;  // byte-limb row: rows 4 banks apart for the fragment loads
-constexpr size_t kPfLimbBytes = (size_t)3 * 64 * kPfLStride;       // three limb planes of 64 rows
-constexpr size_t kPfRowsBytes = (size_t)kPfRows * kExpLut * 4;      // q and key limbs (passes 1-2) / probability table
+constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA: the UMMA M of the score products
+constexpr int kPfThreads = 512;           // 16 warps: 4 row tiles x 4 dim quarters in the value pass
+constexpr size_t kPfQlBytes = (size_t)3 * kPfRows * 128;   // q limbs: three 128-byte-swizzled K-major planes
+constexpr size_t kPfKlBytes = (size_t)3 * kPfKeys * 128;   // key limbs of a chunk, same layout
+constexpr size_t kPfTabBytes = (size_t)kPfTileQ * kExpLut * 4;  // one head's probability table (value pass)
+constexpr size_t kPfRegionA = kPfQlBytes + kPfKlBytes > kPfTabBytes ? kPfQlBytes + kPfKlBytes : kPfTabBytes;
 constexpr int kPfTStride = kPfKeys + 16;  // byte-limb row of the transposed values / probabilities (20 words)
 constexpr size_t kPfVtBytes = (size_t)3 * kHeadDim * kPfTStride;  // value limbs [3][128 dims][64 keys]
-constexpr size_t kPfPlBytes = (size_t)3 * kPfRows * kPfTStride;   // probability limbs [3][64 rows][64 keys]
+constexpr size_t kPfPlBytes = (size_t)3 * kPfTileQ * kPfTStride;  // probability limbs [3][64 rows][64 keys]
 constexpr size_t kPfStageBytes = (size_t)kPfKeys * kPfStride * 4;   // one chunk as staged int32
-constexpr size_t kPfSmem = kPfRowsBytes + kPfVtBytes + kPfPlBytes + kPfStageBytes;
-static_assert(2 * kPfLimbBytes <= kPfRowsBytes, "q and key limbs share the probability table's space");
+constexpr size_t kPfSmem = 1024 + kPfRegionA + kPfVtBytes + kPfPlBytes + kPfStageBytes;  // + alignment slack
+static_assert(kPfRows == 128 && kPfKeys == 64, "score MMAs are M = 128, N = 64");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
@@ -1516,17 +1518,21 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
-  extern __shared__ __align__(16) uint8_t pf_smem[];
-  uint8_t* qL = pf_smem;                                  // [3][64][kPfLStride] q limbs (passes 1-2)
-  uint8_t* kL = pf_smem + kPfLimbBytes;                   // [3][64][kPfLStride] key limbs (passes 1-2)
-  uint32_t* ptab = reinterpret_cast<uint32_t*>(pf_smem);  // [64][257] probability table (pass 3)
-  uint8_t* vT = pf_smem + kPfRowsBytes;                    // [3][128][kPfTStride] value limbs, key-contiguous (pass 3)
-  uint8_t* pL = pf_smem + kPfRowsBytes + kPfVtBytes;       // [3][64][kPfTStride] probability limbs (pass 3)
-  int32_t* stg = reinterpret_cast<int32_t*>(pf_smem + kPfRowsBytes + kPfVtBytes + kPfPlBytes);  // [64][kPfStride]
+  extern __shared__ uint8_t pf_raw[];
+  const uint32_t raw_addr = umma::smem_addr(pf_raw);
+  uint8_t* base = pf_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);  // 1024-byte aligned: swizzle atoms
+  uint8_t* qL = base;                                   // [3][128 rows][128 B] q limbs, UMMA A (passes 1-2)
+  uint8_t* kL = base + kPfQlBytes;                      // [3][64 keys][128 B] key limbs, UMMA B (passes 1-2)
+  uint32_t* ptab = reinterpret_cast<uint32_t*>(base);   // [64][257] one head's probability table (pass 3)
+  uint8_t* vT = base + kPfRegionA;                      // [3][128 dims][kPfTStride] value limbs, key-contiguous
+  uint8_t* pL = vT + kPfVtBytes;                        // [3][64 rows][kPfTStride] probability limbs
+  int32_t* stg = reinterpret_cast<int32_t*>(pL + kPfPlBytes);  // [64][kPfStride] staged keys / values
   __shared__ int32_t elut[kExpLut];
-  __shared__ int64_t rred[kPfQuarters][kPfRows];  // per key quarter: row maxima, then row sums
+  __shared__ int64_t rred[4][kPfRows];  // per column quarter: row maxima, then row sums
   __shared__ int64_t rmax[kPfRows];
   __shared__ uint64_t rsum[kPfRows], rrcp[kPfRows];  // row sums and floor((2^64 - 1) / sum)
+  __shared__ uint64_t mbar;                           // the score MMAs of a chunk are done
+  __shared__ uint32_t tmem_slot;
   grid_dep_wait();
   grid_dep_launch();
   const int kv = blockIdx.x;
@@ -1549,7 +1555,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
     }
     cp_async_commit();
   };
+  // 4 limb bytes of dims 4 d4 .. +3 of row r in a 128-byte-swizzled K-major plane
+  auto put_sw = [](uint8_t* plane, int r, int d4, uint32_t w) {
+    *reinterpret_cast<uint32_t*>(plane + r * 128 + ((((d4 >> 2) ^ (r & 7))) << 4) + ((d4 & 3) << 2)) = w;
+  };
+  if (t == 0) {
+    umma::bar_init(&mbar, 1);
+    umma::bar_init_fence();
+  }
+  if (warp == 0) umma::tmem_alloc(&tmem_slot, 512);
   stage(0, 0);
+  // q limbs: row r = hh * 64 + qi is head 2 kv + hh at position pos0 + qi
   for (int i = t; i < kPfRows * (kHeadDim / 4); i += kPfThreads) {
     const int r = i >> 5, d4 = i & 31, hh = r / kPfTileQ, qi = r % kPfTileQ;
     int4 v = make_int4(0, 0, 0, 0);
@@ -1557,73 +1573,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
       v = *reinterpret_cast<const int4*>(a.qkv + (size_t)(tl.col0 + qi) * (kQRows + 2 * kKvRows) +
                                          (2 * kv + hh) * kHeadDim + 4 * d4);
 #pragma unroll
-    for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(qL + (l * 64 + r) * kPfLStride + 4 * d4) = limb_word(v, l);
+    for (int l = 0; l < 3; ++l) put_sw(qL + l * (kPfRows * 128), r, d4, limb_word(v, l));
   }
   for (int i = t; i < kExpLut; i += kPfThreads) elut[i] = a.exp_lut[i];
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // limbs written here, read by the tensor cores
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
 
-  // Scores: warp (mt, kq) takes rows 16 mt .. +15 and keys 16 kq .. +15 of the
-  // chunk (two 8-key MMA tiles).  Lane (g, tig) ends up with rows ra = 16 mt + g
-  // and ra + 8, keys 16 kq + 8 nt + 2 tig + h (nt, h = 0, 1).
-  const int mt = warp & 3, kq = warp >> 2, g = lane >> 2, tig = lane & 3;
-  const int ra = 16 * mt + g;
-  auto key_of = [&](int nt, int h) { return 16 * kq + 8 * nt + 2 * tig + h; };
-  auto scores = [&](int64_t (&raw)[2][4]) {
-    int32_t acc[5][2][4];
-#pragma unroll
-    for (int s = 0; s < 5; ++s)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[s][nt][i] = 0;
-#pragma unroll
-    for (int ks = 0; ks < kHeadDim / 32; ++ks) {
-      const int k0 = 32 * ks + 4 * tig;
-      uint32_t A[3][4], B[2][3][2];
-#pragma unroll
-      for (int l = 0; l < 3; ++l) {
-        const uint8_t* q0 = qL + (l * 64 + ra) * kPfLStride + k0;
-        A[l][0] = *reinterpret_cast<const uint32_t*>(q0);
-        A[l][1] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride);
-        A[l][2] = *reinterpret_cast<const uint32_t*>(q0 + 16);
-        A[l][3] = *reinterpret_cast<const uint32_t*>(q0 + 8 * kPfLStride + 16);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-          const uint8_t* k = kL + (l * 64 + 16 * kq + 8 * nt + g) * kPfLStride + k0;
-          B[nt][l][0] = *reinterpret_cast<const uint32_t*>(k);
-          B[nt][l][1] = *reinterpret_cast<const uint32_t*>(k + 16);
-        }
-      // limb pairs outer, tiles inner: independent accumulators between two
-      // products into the same one
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[0][nt], A[0], B[nt][0]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[1][nt], A[0], B[nt][1]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, true>(acc[2][nt], A[0], B[nt][2]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, true>(acc[3][nt], A[1], B[nt][2]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<true, true>(acc[4][nt], A[2], B[nt][2]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[1][nt], A[1], B[nt][0]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<false, false>(acc[2][nt], A[1], B[nt][1]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<true, false>(acc[3][nt], A[2], B[nt][1]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) mma_limb<true, false>(acc[2][nt], A[2], B[nt][0]);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        raw[i >> 1][2 * nt + (i & 1)] = (int64_t)acc[0][nt][i] + (int64_t)acc[1][nt][i] * 256 +
-                                        (int64_t)acc[2][nt][i] * 65536 + (int64_t)acc[3][nt][i] * 16777216 +
-                                        (int64_t)acc[4][nt][i] * 4294967296LL;
-  };
   // staged chunk -> key limbs
   auto key_limbs = [&](int c) {
     const int n = keys_in(c);
@@ -1631,238 +1589,276 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
       const int j = i >> 5, d4 = i & 31;
       const int4 v = *reinterpret_cast<const int4*>(stg + j * kPfStride + 4 * d4);
 #pragma unroll
-      for (int l = 0; l < 3; ++l) *reinterpret_cast<uint32_t*>(kL + (l * 64 + j) * kPfLStride + 4 * d4) = limb_word(v, l);
+      for (int l = 0; l < 3; ++l) put_sw(kL + l * (kPfKeys * 128), j, d4, limb_word(v, l));
     }
   };
-  // row r = hh * 32 + qi is query position pos0 + qi; key j is valid for it when j <= pos0 + qi
-  auto valid = [&](int r, int j) {
-    const int qi = r % kPfTileQ;
-    return qi < tl.nq && j <= tl.pos0 + qi;
+  // Scores of a chunk on the tensor cores: D_g[128 rows][64 keys] (TMEM
+  // columns 64 g) for the five shift groups g of the nine limb products,
+  // 4 MMAs of K = 32 bytes each (one thread issues).
+  auto issue_scores = [&]() {
+    const uint32_t qa = umma::smem_addr(qL), ka = umma::smem_addr(kL);
+    constexpr int pa[9] = {0, 0, 1, 0, 1, 2, 1, 2, 2}, pb[9] = {0, 1, 0, 2, 1, 0, 2, 1, 2};
+    constexpr int pg[9] = {0, 1, 1, 2, 2, 2, 3, 3, 4};
+    constexpr bool first[9] = {true, true, false, true, false, false, true, false, true};
+#pragma unroll
+    for (int q = 0; q < 9; ++q) {
+      const uint32_t idesc = umma::i8_idesc_ab(kPfRows, kPfKeys, pa[q] == 2, pb[q] == 2);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_i8(tmem + (uint32_t)(pg[q] * kPfKeys),
+                     umma::sw128_desc(qa + (uint32_t)(pa[q] * kPfRows * 128 + 32 * ks)),
+                     umma::sw128_desc(ka + (uint32_t)(pb[q] * kPfKeys * 128 + 32 * ks)), idesc,
+                     (first[q] && ks == 0) ? 0u : 1u);
+    }
+    umma::mma_commit(&mbar);
   };
-
-  // pass 1: row maxima of the raw scores (the scaling is monotonic, so the
-  // maximum scaled score is the scaled maximum)
-  int64_t mx[2] = {INT64_MIN, INT64_MIN};
-  for (int c = 0; c < nch; ++c) {
-    cp_async_wait0();
-    __syncthreads();  // chunk c staged; the previous chunk's scores are done
-    key_limbs(c);
-    __syncthreads();
-    stage(0, c + 1);
-    int64_t raw[2][4];
-    scores(raw);
+  // TMEM read-out: warp (sp, cq) reads lanes 32 sp .. +31 (rows) and the
+  // chunk's columns 16 cq .. +15 (keys); lane = row r = 32 sp + lane
+  const int sp = warp & 3, cq = warp >> 2;
+  const int er = 32 * sp + lane;
+  const int eqi = er % kPfTileQ;
+  const bool erow = eqi < tl.nq;
+  bool ok = true;
+  uint32_t phase = 0;
+  auto scores_of = [&](int cb, int64_t (&raw)[8]) {
+    int32_t v[5][8];
+    const uint32_t lb = tmem + ((uint32_t)(32 * sp) << 16) + (uint32_t)cb;
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int g = 0; g < 5; ++g) umma::tmem_ld<8>(lb + (uint32_t)(g * kPfKeys), v[g]);
+    umma::tmem_ld_wait();
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+    for (int i = 0; i < 8; ++i)
+      raw[i] = (int64_t)v[0][i] + (int64_t)v[1][i] * 256 + (int64_t)v[2][i] * 65536 + (int64_t)v[3][i] * 16777216 +
+               (int64_t)v[4][i] * 4294967296LL;
+  };
+  // one pass over the K chunks; body(c, cb, raw) for every 8 keys of the warp's column quarter
+  auto k_pass = [&](auto&& body) {
+    for (int c = 0; c < nch; ++c) {
+      cp_async_wait0();
+      __syncthreads();  // chunk c staged; the previous chunk's TMEM reads are done
+      key_limbs(c);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      umma::fence_before_sync();
+      __syncthreads();
+      umma::fence_after_sync();
+      stage(0, c + 1);
+      if (t == 0) issue_scores();
+      if (!umma::bar_wait(&mbar, phase)) ok = false;
+      umma::fence_after_sync();
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
-          if (valid(ra + 8 * i, c * kPfKeys + key_of(nt, h))) mx[i] = raw[i][2 * nt + h] > mx[i] ? raw[i][2 * nt + h] : mx[i];
-  }
+      for (int cb = 16 * cq; cb < 16 * cq + 16; cb += 8) {
+        int64_t raw[8];
+        scores_of(cb, raw);
+        body(c, cb, raw);
+      }
+      umma::fence_before_sync();
+      phase ^= 1u;
+    }
+  };
+  // pass 1: row maxima of the raw scores (the score scaling is monotonic, so
+  // the maximum scaled score is the scaled maximum)
+  int64_t mx = INT64_MIN;
+  k_pass([&](int c, int cb, const int64_t (&raw)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = c * kPfKeys + cb + i;
+      if (erow && j <= tl.pos0 + eqi) mx = raw[i] > mx ? raw[i] : mx;
+    }
+  });
   stage(0, 0);  // pass 2 streams K again
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-#pragma unroll
-    for (int msk = 1; msk < 4; msk <<= 1) {
-      const int64_t o = shfl_xor_i64(mx[i], msk);
-      mx[i] = o > mx[i] ? o : mx[i];
-    }
-    if (tig == 0) rred[kq][ra + 8 * i] = mx[i];
-  }
+  rred[cq][er] = mx;
   __syncthreads();
   if (t < kPfRows) {
     int64_t m = rred[0][t];
 #pragma unroll
-    for (int q = 1; q < kPfQuarters; ++q) m = rred[q][t] > m ? rred[q][t] : m;
+    for (int q = 1; q < 4; ++q) m = rred[q][t] > m ? rred[q][t] : m;
     rmax[t] = m == INT64_MIN ? m : scale_score(m, kScoreScale);
   }
   __syncthreads();
-  // pass 2: LUT indices and exp sums
-  int64_t sm[2] = {0, 0};
-  const int64_t rmx[2] = {rmax[ra], rmax[ra + 8]};
-  uint16_t* idx_row[2];
+  // pass 2: LUT indices (kept in the u16 scratch, one 16-byte store per 8 keys) and exp sums
+  const int64_t rmx = rmax[er];
+  uint16_t* erow_idx =
+      a.lut_idx + ((size_t)(tl.col0 + (erow ? eqi : 0)) * kQHeads + 2 * kv + er / kPfTileQ) * a.idx_ld;
+  int64_t esum = 0;
+  k_pass([&](int c, int cb, const int64_t (&raw)[8]) {
+    uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int r = ra + 8 * i, hh = r / kPfTileQ, qi = r % kPfTileQ;
-    const int col = tl.col0 + (qi < tl.nq ? qi : 0);
-    idx_row[i] = a.lut_idx + ((size_t)col * kQHeads + 2 * kv + hh) * a.idx_ld;
-  }
-  for (int c = 0; c < nch; ++c) {
-    cp_async_wait0();
-    __syncthreads();
-    key_limbs(c);
-    __syncthreads();
-    stage(0, c + 1);
-    int64_t raw[2][4];
-    scores(raw);
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int j = c * kPfKeys + key_of(nt, 0);
-        uint32_t pair = 0;
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          if (valid(ra + 8 * i, j + h)) {
-            const int ix = lut_index(rmx[i], scale_score(raw[i][2 * nt + h], kScoreScale));
-            sm[i] += elut[ix];
-            pair |= (uint32_t)ix << (16 * h);
-          }
-        // rows are 64-aligned, so (j, j + 1), j even, is one 4-byte word; rows
-        // past the tile's queries alias its first row and store nothing
-        if ((ra + 8 * i) % kPfTileQ < tl.nq) *reinterpret_cast<uint32_t*>(idx_row[i] + j) = pair;
+    for (int i = 0; i < 8; ++i) {
+      const int j = c * kPfKeys + cb + i;
+      if (erow && j <= tl.pos0 + eqi) {
+        const int ix = lut_index(rmx, scale_score(raw[i], kScoreScale));
+        esum += elut[ix];
+        w[i >> 1] |= (uint32_t)ix << (16 * (i & 1));
       }
-  }
-  stage(1, 0);  // pass 3 streams V
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-#pragma unroll
-    for (int msk = 1; msk < 4; msk <<= 1) sm[i] += shfl_xor_i64(sm[i], msk);
-    if (tig == 0) rred[kq][ra + 8 * i] = sm[i];
-  }
-  __syncthreads();  // the limbs are dead: the table takes their place
+    }
+    if (erow) *reinterpret_cast<uint4*>(erow_idx + c * kPfKeys + cb) = make_uint4(w[0], w[1], w[2], w[3]);
+  });
+  rred[cq][er] = esum;
+  __syncthreads();
   if (t < kPfRows) {
-    uint64_t s = 0;
-#pragma unroll
-    for (int q = 0; q < kPfQuarters; ++q) s += (uint64_t)rred[q][t];
+    const uint64_t s = (uint64_t)(rred[0][t] + rred[1][t] + rred[2][t] + rred[3][t]);
     rsum[t] = s;
     rrcp[t] = s > 0 ? ~0ULL / s : 0;
   }
-  __syncthreads();
-  // prob[e] = floor((lut[e] << 16) / sum) by the row's Barrett reciprocal
-  for (int i = t; i < kPfRows * kExpLut; i += kPfThreads) {
-    const int r = i / kExpLut, e = i - r * kExpLut;
-    const uint64_t s = rsum[r];
-    ptab[i] = s > 0 ? barrett_div((uint64_t)elut[e] << 16, s, rrcp[r]) : 0u;
-  }
-  // pass 3: probability-weighted values.  Warp (mt, kq) takes output rows
-  // 16 mt .. +15 and dims 32 kq .. +31 (four 8-dim MMA tiles, two at a time);
-  // lane (g, tig) holds rows ra, ra + 8 and dims 32 kq + 8 n + 2 tig + {0, 1}.
-  int64_t tot[4][4];
-#pragma unroll
-  for (int n = 0; n < 4; ++n)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) tot[n][i] = 0;
-  // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded a chunk ahead
-  auto idx_pairs = [&](int c, uint32_t (&w)[2][2]) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-        w[i][nt] = *reinterpret_cast<const uint32_t*>(idx_row[i] + c * kPfKeys + key_of(nt, 0));
-  };
-  uint32_t nidx[2][2];
-  idx_pairs(0, nidx);
-  for (int c = 0; c < nch; ++c) {
-    uint32_t cidx[2][2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) cidx[i][nt] = nidx[i][nt];
-    if (c + 1 < nch) idx_pairs(c + 1, nidx);
-    cp_async_wait0();
-    __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
-    // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
-    for (int i = t; i < kHeadDim * (kPfKeys / 4); i += kPfThreads) {
-      const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;  // 8 dims x 4 key groups per warp
-      const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
-      const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
-                               stg[(4 * jg + 2) * kPfStride + dd], stg[(4 * jg + 3) * kPfStride + dd]);
-#pragma unroll
-      for (int l = 0; l < 3; ++l)
-        *reinterpret_cast<uint32_t*>(vT + (l * kHeadDim + dd) * kPfTStride + 4 * jg) = limb_word(v, l);
+  if (!ok) atomicExch(a.err, 5);
+  // pass 3, one query head at a time: probability-weighted values.  Warp
+  // (mt, kq) takes rows 16 mt .. +15 of the head and dims 32 kq .. +31 (four
+  // 8-dim MMA tiles, two at a time); lane (g, tig) holds rows ra, ra + 8 and
+  // dims 32 kq + 8 n + 2 tig + {0, 1}; its probabilities are those of keys
+  // 16 kq + 8 nt + 2 tig + {0, 1}.
+  const int mt = warp & 3, kq = warp >> 2, g = lane >> 2, tig = lane & 3;
+  const int ra = 16 * mt + g;
+  auto key_of = [&](int nt, int h) { return 16 * kq + 8 * nt + 2 * tig + h; };
+  auto valid = [&](int qi, int j) { return qi < tl.nq && j <= tl.pos0 + qi; };
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    stage(1, 0);      // the staging buffer is free: the last K chunk / the other head's last V chunk is converted
+    __syncthreads();  // every score MMA has completed (all warps waited for them): the limbs, or the other
+                      // head's table, are dead and the table takes their place
+    for (int i = t; i < kPfTileQ * kExpLut; i += kPfThreads) {
+      const int r = i / kExpLut, e = i - r * kExpLut;
+      const uint64_t s = rsum[hf * kPfTileQ + r];
+      ptab[i] = s > 0 ? barrett_div((uint64_t)elut[e] << 16, s, rrcp[hf * kPfTileQ + r]) : 0u;
     }
-    // probability limbs of this thread's (row, key) pairs of the score layout
-    int big = 0;
+    uint16_t* idx_row[2];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
-        uint32_t p0 = 0, p1 = 0;
-        if (valid(r, j)) p0 = ptab[r * kExpLut + (cidx[i][nt] & 0xFFFFu)];
-        if (valid(r, j + 1)) p1 = ptab[r * kExpLut + (cidx[i][nt] >> 16)];
-        big |= (int)((p0 | p1) >> 16);
-#pragma unroll
-        for (int l = 0; l < 3; ++l)
-          *reinterpret_cast<uint16_t*>(pL + (l * kPfRows + r) * kPfTStride + jj) =
-              (uint16_t)(((p0 >> (8 * l)) & 0xFF) | (((p1 >> (8 * l)) & 0xFF) << 8));
-      }
-    const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
-    stage(1, c + 1);
-#pragma unroll
-    for (int sb = 0; sb < 2; ++sb) {
-      int32_t acc[5][2][4];
-#pragma unroll
-      for (int s5 = 0; s5 < 5; ++s5)
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        uint32_t A[3][4], B[2][3][2];
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-          const uint8_t* p = pL + (l * kPfRows + ra) * kPfTStride + 32 * ks + 4 * tig;
-          A[l][0] = *reinterpret_cast<const uint32_t*>(p);
-          A[l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
-          A[l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
-          A[l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
-        }
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-          for (int l = 0; l < 3; ++l) {
-            const uint8_t* v = vT + (l * kHeadDim + 32 * kq + 8 * (2 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
-            B[n][l][0] = *reinterpret_cast<const uint32_t*>(v);
-            B[n][l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
-          }
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[0][n], A[0], B[n][0]);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[0], B[n][1]);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[2][n], A[0], B[n][2]);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[3][n], A[1], B[n][2]);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[1], B[n][0]);
-#pragma unroll
-        for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[1], B[n][1]);
-        if (any2) {
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[4][n], A[2], B[n][2]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[3][n], A[2], B[n][1]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[2], B[n][0]);
-        }
-      }
-#pragma unroll
-      for (int n = 0; n < 2; ++n)
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          tot[2 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
-                                (int64_t)acc[2][n][i] * 65536 + (int64_t)acc[3][n][i] * 16777216 +
-                                (int64_t)acc[4][n][i] * 4294967296LL;
+    for (int i = 0; i < 2; ++i) {
+      const int qi = ra + 8 * i;
+      idx_row[i] = a.lut_idx + ((size_t)(tl.col0 + (qi < tl.nq ? qi : 0)) * kQHeads + 2 * kv + hf) * a.idx_ld;
     }
-  }
-  // outputs as limbs of the o_proj input (64-column sub-batches, SP = 64)
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int r = ra + 8 * i, hh = r / kPfTileQ, qi = r % kPfTileQ;
-    if (qi >= tl.nq) continue;
-    const int col = tl.col0 + qi;
-    uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
+    int64_t tot[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int d = 32 * kq + 8 * n + 2 * tig + h;
-        write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hh) * kHeadDim + d,
-                    sat24(tot[n][2 * i + h] >> 16));
+      for (int i = 0; i < 4; ++i) tot[n][i] = 0;
+    // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded a chunk ahead
+    auto idx_pairs = [&](int c, uint32_t (&w)[2][2]) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          w[i][nt] = *reinterpret_cast<const uint32_t*>(idx_row[i] + c * kPfKeys + key_of(nt, 0));
+    };
+    uint32_t nidx[2][2];
+    idx_pairs(0, nidx);
+    for (int c = 0; c < nch; ++c) {
+      uint32_t cidx[2][2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) cidx[i][nt] = nidx[i][nt];
+      if (c + 1 < nch) idx_pairs(c + 1, nidx);
+      cp_async_wait0();
+      __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
+      // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
+      for (int i = t; i < kHeadDim * (kPfKeys / 4); i += kPfThreads) {
+        const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;  // 8 dims x 4 key groups per warp
+        const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
+        const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
+                                 stg[(4 * jg + 2) * kPfStride + dd], stg[(4 * jg + 3) * kPfStride + dd]);
+#pragma unroll
+        for (int l = 0; l < 3; ++l)
+          *reinterpret_cast<uint32_t*>(vT + (l * kHeadDim + dd) * kPfTStride + 4 * jg) = limb_word(v, l);
       }
+      // probability limbs of this thread's (row, key) pairs
+      int big = 0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
+          uint32_t p0 = 0, p1 = 0;
+          if (valid(r, j)) p0 = ptab[r * kExpLut + (cidx[i][nt] & 0xFFFFu)];
+          if (valid(r, j + 1)) p1 = ptab[r * kExpLut + (cidx[i][nt] >> 16)];
+          big |= (int)((p0 | p1) >> 16);
+#pragma unroll
+          for (int l = 0; l < 3; ++l)
+            *reinterpret_cast<uint16_t*>(pL + (l * kPfTileQ + r) * kPfTStride + jj) =
+                (uint16_t)(((p0 >> (8 * l)) & 0xFF) | (((p1 >> (8 * l)) & 0xFF) << 8));
+        }
+      const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
+      stage(1, c + 1);
+#pragma unroll
+      for (int sb = 0; sb < 2; ++sb) {
+        int32_t acc[5][2][4];
+#pragma unroll
+        for (int s5 = 0; s5 < 5; ++s5)
+#pragma unroll
+          for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
+#pragma unroll
+        for (int ks = 0; ks < 2; ++ks) {
+          uint32_t A[3][4], B[2][3][2];
+#pragma unroll
+          for (int l = 0; l < 3; ++l) {
+            const uint8_t* p = pL + (l * kPfTileQ + ra) * kPfTStride + 32 * ks + 4 * tig;
+            A[l][0] = *reinterpret_cast<const uint32_t*>(p);
+            A[l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
+            A[l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
+            A[l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
+          }
+#pragma unroll
+          for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+              const uint8_t* v =
+                  vT + (l * kHeadDim + 32 * kq + 8 * (2 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
+              B[n][l][0] = *reinterpret_cast<const uint32_t*>(v);
+              B[n][l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
+            }
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[0][n], A[0], B[n][0]);
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[0], B[n][1]);
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[2][n], A[0], B[n][2]);
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[3][n], A[1], B[n][2]);
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[1], B[n][0]);
+#pragma unroll
+          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[1], B[n][1]);
+          if (any2) {
+#pragma unroll
+            for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[4][n], A[2], B[n][2]);
+#pragma unroll
+            for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[3][n], A[2], B[n][1]);
+#pragma unroll
+            for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[2], B[n][0]);
+          }
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            tot[2 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
+                                  (int64_t)acc[2][n][i] * 65536 + (int64_t)acc[3][n][i] * 16777216 +
+                                  (int64_t)acc[4][n][i] * 4294967296LL;
+      }
+    }
+    // outputs of head 2 kv + hf as limbs of the o_proj input (64-column sub-batches, SP = 64)
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int qi = ra + 8 * i;
+      if (qi >= tl.nq) continue;
+      const int col = tl.col0 + qi;
+      uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int d = 32 * kq + 8 * n + 2 * tig + h;
+          write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hf) * kHeadDim + d,
+                      sat24(tot[n][2 * i + h] >> 16));
+        }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, 512);
   }
 }
 

@@ -92,8 +92,8 @@ struct LmShardPlan {
 
 // Batched exact prefill: prompt positions as columns (sequence-major).
 constexpr int kPfSub = 64;     // columns per GEMM (padded batch 64)
-constexpr int kPfBlock = 512;  // columns per attention launch (and per enqueued block)
-constexpr int kPfTileQ = 32;   // query positions per attention CTA (one sequence)
+constexpr int kPfBlock = 1024;  // columns per attention launch (and per enqueued block)
+constexpr int kPfTileQ = 64;    // query positions per attention CTA (one sequence): 128 rows with both heads
 constexpr int kPfKeys = 64;    // keys per staged attention chunk (one KV page)
 
 // Query tile of an attention launch: block columns [col0, col0 + nq), all of

@@ -144,6 +144,12 @@ __host__ __device__ constexpr uint32_t i8_idesc(int M, int N) {
   return (2u << 4) | (1u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// The same with the signedness of each operand chosen (u8 or s8).
+__host__ __device__ constexpr uint32_t i8_idesc_ab(int M, int N, bool a_signed, bool b_signed) {
+  return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
 // D[tmem] (+)= A[smem] x B[smem]^T, issued by one thread.
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                        uint32_t accumulate) {
