@@ -1701,158 +1701,141 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
     rrcp[t] = s > 0 ? ~0ULL / s : 0;
   }
   if (!ok) atomicExch(a.err, 5);
-  // pass 3, one query head at a time: probability-weighted values.  Warp
-  // (mt, kq) takes rows 16 mt .. +15 of the head and dims 32 kq .. +31 (four
-  // 8-dim MMA tiles, two at a time); lane (g, tig) holds rows ra, ra + 8 and
-  // dims 32 kq + 8 n + 2 tig + {0, 1}; its probabilities are those of keys
-  // 16 kq + 8 nt + 2 tig + {0, 1}.
-  const int mt = warp & 3, kq = warp >> 2, g = lane >> 2, tig = lane & 3;
-  const int ra = 16 * mt + g;
-  auto key_of = [&](int nt, int h) { return 16 * kq + 8 * nt + 2 * tig + h; };
-  auto valid = [&](int qi, int j) { return qi < tl.nq && j <= tl.pos0 + qi; };
-#pragma unroll 1
-  for (int hf = 0; hf < 2; ++hf) {
-    stage(1, 0);      // the staging buffer is free: the last K chunk / the other head's last V chunk is converted
-    __syncthreads();  // every score MMA has completed (all warps waited for them): the limbs, or the other
-                      // head's table, are dead and the table takes their place
-    for (int i = t; i < kPfTileQ * kExpLut; i += kPfThreads) {
-      const int r = i / kExpLut, e = i - r * kExpLut;
-      const uint64_t s = rsum[hf * kPfTileQ + r];
-      ptab[i] = s > 0 ? barrett_div((uint64_t)elut[e] << 16, s, rrcp[hf * kPfTileQ + r]) : 0u;
+  // pass 3: probability-weighted values on tcgen05, both heads at once, in
+  // 128-key chunks (two 64-key stagings).  A = probability limbs [3][128 rows]
+  // [128 keys], B = value limbs [3][128 dims][128 keys] (both 128-byte-swizzled
+  // K-major, in the score operands' space), D = five TMEM accumulators per
+  // 64-dim half (the halves run one after the other), folded into int64 after
+  // every chunk, so no int32 sum spans more than 128 keys.  Probabilities come
+  // from the row's Barrett reciprocal: prob = (lut[idx] << 16) / sum.
+  uint8_t* pLt = base;                      // [3][128][128] probability limbs
+  uint8_t* vTt = base + 3 * kPfRows * 128;  // [3][128][128] value limbs
+  constexpr int kPvKeys = 2 * kPfKeys;
+  const int nch2 = (kend + kPvKeys - 1) / kPvKeys;
+  int64_t tot[2][16];  // dims 64 h + 16 cq + i of row er
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tot[h][i] = 0;
+  // the LUT-index scratch row of this thread's probability items
+  auto idx_base = [&](int r) {
+    const int qi = r % kPfTileQ;
+    return a.lut_idx + ((size_t)(tl.col0 + (qi < tl.nq ? qi : 0)) * kQHeads + 2 * kv + r / kPfTileQ) * a.idx_ld;
+  };
+  // staged 64 keys -> value limbs at keys 64 half .. (lane (d % 8, j4) packs keys 4 j4 .. +3 of dim d)
+  auto value_limbs = [&](int half) {
+    for (int i = t; i < kHeadDim * (kPfKeys / 4); i += kPfThreads) {
+      const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;
+      const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
+      const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
+                               stg[(4 * jg + 2) * kPfStride + dd], stg[(4 * jg + 3) * kPfStride + dd]);
+#pragma unroll
+      for (int l = 0; l < 3; ++l) put_sw(vTt + l * (kHeadDim * 128), dd, 16 * half + jg, limb_word(v, l));
     }
-    uint16_t* idx_row[2];
+  };
+  auto issue_values = [&](int h, bool any2) {
+    const uint32_t pa = umma::smem_addr(pLt), va = umma::smem_addr(vTt);
+    constexpr int ppa[9] = {0, 0, 1, 0, 1, 1, 2, 2, 2}, ppb[9] = {0, 1, 0, 2, 1, 2, 0, 1, 2};
+    constexpr int ppg[9] = {0, 1, 1, 2, 2, 3, 2, 3, 4};
+    constexpr bool first[9] = {true, true, false, true, false, true, false, false, true};
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int qi = ra + 8 * i;
-      idx_row[i] = a.lut_idx + ((size_t)(tl.col0 + (qi < tl.nq ? qi : 0)) * kQHeads + 2 * kv + hf) * a.idx_ld;
+    for (int q = 0; q < 9; ++q) {
+      if (ppa[q] == 2 && !any2) continue;  // p2 = 0 in every row of the chunk: group 4 stays unused
+      const uint32_t idesc = umma::i8_idesc_ab(kPfRows, 64, false, ppb[q] == 2);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma::mma_i8(tmem + (uint32_t)(ppg[q] * 64),
+                     umma::sw128_desc(pa + (uint32_t)(ppa[q] * kPfRows * 128 + 32 * ks)),
+                     umma::sw128_desc(va + (uint32_t)(ppb[q] * kHeadDim * 128 + h * 64 * 128 + 32 * ks)), idesc,
+                     (first[q] && ks == 0) ? 0u : 1u);
     }
-    int64_t tot[4][4];
+    umma::mma_commit(&mbar);
+  };
+  stage(1, 0);  // the staging buffer is free: the last K chunk was converted
+  constexpr int kPvItems = kPfRows * (kPvKeys / 4) / kPfThreads;  // (row, 4 keys) items per thread
+  for (int c2 = 0; c2 < nch2; ++c2) {
+    // this thread's LUT indices of the chunk, loaded first so that the loads
+    // overlap the first value conversion
+    uint2 ixw[kPvItems];
 #pragma unroll
-    for (int n = 0; n < 4; ++n)
+    for (int u = 0; u < kPvItems; ++u) {
+      const int i = t + u * kPfThreads, r = i >> 5, k4 = i & 31, qi = r % kPfTileQ;
+      const int j0 = c2 * kPvKeys + 4 * k4;
+      ixw[u] = make_uint2(0, 0);
+      if (qi < tl.nq && j0 <= tl.pos0 + qi) ixw[u] = *reinterpret_cast<const uint2*>(idx_base(r) + j0);
+    }
+    cp_async_wait0();
+    __syncthreads();  // keys 128 c2 .. +63 staged; the previous chunk's TMEM reads are done
+    value_limbs(0);
+    __syncthreads();
+    stage(1, 2 * c2 + 1);
+    // probability limbs: item (row r, keys 4 k4 .. +3) -> one word per limb plane
+    int big = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tot[n][i] = 0;
-    // LUT-index pairs (keys 2 tig + {0, 1} of each tile) of the next chunk, loaded a chunk ahead
-    auto idx_pairs = [&](int c, uint32_t (&w)[2][2]) {
+    for (int u = 0; u < kPvItems; ++u) {
+      const int i = t + u * kPfThreads, r = i >> 5, k4 = i & 31, qi = r % kPfTileQ;
+      const int j0 = c2 * kPvKeys + 4 * k4;
+      uint32_t pw[3] = {0, 0, 0};
+      if (qi < tl.nq && j0 <= tl.pos0 + qi) {
+        const uint2 ix = ixw[u];
+        const uint32_t ixs[4] = {ix.x & 0xFFFFu, ix.x >> 16, ix.y & 0xFFFFu, ix.y >> 16};
+        const uint64_t s = rsum[r], rc = rrcp[r];
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+        for (int e = 0; e < 4; ++e)
+          if (j0 + e <= tl.pos0 + qi) {
+            const uint32_t p = barrett_div((uint64_t)elut[ixs[e]] << 16, s, rc);
+            big |= (int)(p >> 16);
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-          w[i][nt] = *reinterpret_cast<const uint32_t*>(idx_row[i] + c * kPfKeys + key_of(nt, 0));
-    };
-    uint32_t nidx[2][2];
-    idx_pairs(0, nidx);
-    for (int c = 0; c < nch; ++c) {
-      uint32_t cidx[2][2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) cidx[i][nt] = nidx[i][nt];
-      if (c + 1 < nch) idx_pairs(c + 1, nidx);
-      cp_async_wait0();
-      __syncthreads();  // chunk c staged; the previous chunk's MMAs are done; orders the table writes
-      // value limbs, transposed: lane (d % 8, j4) of a warp packs keys 4 j4 .. +3 of dim d
-      for (int i = t; i < kHeadDim * (kPfKeys / 4); i += kPfThreads) {
-        const int d = (i & 7) | ((i >> 5) << 3), j4 = (i >> 3) & 3;  // 8 dims x 4 key groups per warp
-        const int dd = d & (kHeadDim - 1), jg = j4 + 4 * (d >> 7);
-        const int4 v = make_int4(stg[(4 * jg + 0) * kPfStride + dd], stg[(4 * jg + 1) * kPfStride + dd],
-                                 stg[(4 * jg + 2) * kPfStride + dd], stg[(4 * jg + 3) * kPfStride + dd]);
-#pragma unroll
-        for (int l = 0; l < 3; ++l)
-          *reinterpret_cast<uint32_t*>(vT + (l * kHeadDim + dd) * kPfTStride + 4 * jg) = limb_word(v, l);
-      }
-      // probability limbs of this thread's (row, key) pairs
-      int big = 0;
-#pragma unroll
-      for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const int r = ra + 8 * i, jj = key_of(nt, 0), j = c * kPfKeys + jj;
-          uint32_t p0 = 0, p1 = 0;
-          if (valid(r, j)) p0 = ptab[r * kExpLut + (cidx[i][nt] & 0xFFFFu)];
-          if (valid(r, j + 1)) p1 = ptab[r * kExpLut + (cidx[i][nt] >> 16)];
-          big |= (int)((p0 | p1) >> 16);
-#pragma unroll
-          for (int l = 0; l < 3; ++l)
-            *reinterpret_cast<uint16_t*>(pL + (l * kPfTileQ + r) * kPfTStride + jj) =
-                (uint16_t)(((p0 >> (8 * l)) & 0xFF) | (((p1 >> (8 * l)) & 0xFF) << 8));
-        }
-      const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
-      stage(1, c + 1);
-#pragma unroll
-      for (int sb = 0; sb < 2; ++sb) {
-        int32_t acc[5][2][4];
-#pragma unroll
-        for (int s5 = 0; s5 < 5; ++s5)
-#pragma unroll
-          for (int n = 0; n < 2; ++n)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[s5][n][i] = 0;
-#pragma unroll
-        for (int ks = 0; ks < 2; ++ks) {
-          uint32_t A[3][4], B[2][3][2];
-#pragma unroll
-          for (int l = 0; l < 3; ++l) {
-            const uint8_t* p = pL + (l * kPfTileQ + ra) * kPfTStride + 32 * ks + 4 * tig;
-            A[l][0] = *reinterpret_cast<const uint32_t*>(p);
-            A[l][1] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride);
-            A[l][2] = *reinterpret_cast<const uint32_t*>(p + 16);
-            A[l][3] = *reinterpret_cast<const uint32_t*>(p + 8 * kPfTStride + 16);
+            for (int l = 0; l < 3; ++l) pw[l] |= ((p >> (8 * l)) & 0xFFu) << (8 * e);
           }
-#pragma unroll
-          for (int n = 0; n < 2; ++n)
-#pragma unroll
-            for (int l = 0; l < 3; ++l) {
-              const uint8_t* v =
-                  vT + (l * kHeadDim + 32 * kq + 8 * (2 * sb + n) + g) * kPfTStride + 32 * ks + 4 * tig;
-              B[n][l][0] = *reinterpret_cast<const uint32_t*>(v);
-              B[n][l][1] = *reinterpret_cast<const uint32_t*>(v + 16);
-            }
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[0][n], A[0], B[n][0]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[0], B[n][1]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[2][n], A[0], B[n][2]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[3][n], A[1], B[n][2]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[1][n], A[1], B[n][0]);
-#pragma unroll
-          for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[1], B[n][1]);
-          if (any2) {
-#pragma unroll
-            for (int n = 0; n < 2; ++n) mma_limb<false, true>(acc[4][n], A[2], B[n][2]);
-#pragma unroll
-            for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[3][n], A[2], B[n][1]);
-#pragma unroll
-            for (int n = 0; n < 2; ++n) mma_limb<false, false>(acc[2][n], A[2], B[n][0]);
-          }
-        }
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            tot[2 * sb + n][i] += (int64_t)acc[0][n][i] + (int64_t)acc[1][n][i] * 256 +
-                                  (int64_t)acc[2][n][i] * 65536 + (int64_t)acc[3][n][i] * 16777216 +
-                                  (int64_t)acc[4][n][i] * 4294967296LL;
       }
+#pragma unroll
+      for (int l = 0; l < 3; ++l) put_sw(pLt + l * (kPfRows * 128), r, k4, pw[l]);
     }
-    // outputs of head 2 kv + hf as limbs of the o_proj input (64-column sub-batches, SP = 64)
+    const bool any2 = __syncthreads_or(big) != 0;  // some p = 2^16 in this chunk: its limb-2 products count
+    cp_async_wait0();
+    __syncthreads();  // keys 128 c2 + 64 .. +63 staged
+    value_limbs(1);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+    stage(1, 2 * c2 + 2);
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int qi = ra + 8 * i;
-      if (qi >= tl.nq) continue;
-      const int col = tl.col0 + qi;
-      uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
+    for (int h = 0; h < 2; ++h) {
+      if (t == 0) issue_values(h, any2);
+      if (!umma::bar_wait(&mbar, phase)) ok = false;
+      phase ^= 1u;
+      umma::fence_after_sync();
 #pragma unroll
-      for (int n = 0; n < 4; ++n)
+      for (int cb = 0; cb < 16; cb += 8) {
+        int32_t v[5][8];
+        const uint32_t lb = tmem + ((uint32_t)(32 * sp) << 16) + (uint32_t)(16 * cq + cb);
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int d = 32 * kq + 8 * n + 2 * tig + h;
-          write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + hf) * kHeadDim + d,
-                      sat24(tot[n][2 * i + h] >> 16));
-        }
+        for (int g5 = 0; g5 < 4; ++g5) umma::tmem_ld<8>(lb + (uint32_t)(g5 * 64), v[g5]);
+        if (any2) umma::tmem_ld<8>(lb + 4u * 64u, v[4]);
+        umma::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          tot[h][cb + i] += (int64_t)v[0][i] + (int64_t)v[1][i] * 256 + (int64_t)v[2][i] * 65536 +
+                            (int64_t)v[3][i] * 16777216 + (any2 ? (int64_t)v[4][i] * 4294967296LL : 0);
+      }
+      umma::fence_before_sync();
+      __syncthreads();  // TMEM read before the next MMAs overwrite it
+      umma::fence_after_sync();
     }
+  }
+  if (!ok) atomicExch(a.err, 5);
+  // outputs of row er (head 2 kv + er / 64, position pos0 + er % 64) as limbs of the o_proj input
+  if (erow) {
+    const int col = tl.col0 + eqi;
+    uint8_t* bt = a.bt2 + (size_t)(col / kPfSub) * a.bt2_sub;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        write_limbs(bt, kPfSub, 2 * kHidden, col % kPfSub, (2 * kv + er / kPfTileQ) * kHeadDim + 64 * h + 16 * cq + i,
+                    sat24(tot[h][i] >> 16));
   }
   umma::fence_before_sync();
   __syncthreads();
