@@ -1156,59 +1156,40 @@ __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ par
 // chunks of the cache (cp.async into a staging buffer, then re-laid out):
 //   1. scores -> row maxima;
 //   2. scores again -> LUT indices (kept in a u16 scratch) and exp sums;
-//      then a probability table per row, prob[e] = (lut[e] << 16) / sum;
-//   3. values, one head at a time: sum over keys of prob[idx] * v, then
+//   3. values in 128-key chunks: sum over keys of prob * v with
+//      prob = (lut[idx] << 16) / sum by the row's Barrett reciprocal, then
 //      sat24(>> 16) as limbs of the o_proj input.
 // q and k are signed 24-bit, split into byte limbs x = x0 + 2^8 x1 + 2^16 x2
 // (x0, x1 unsigned, x2 signed), and
 //   q k = sum_{a,b} 2^(8 (a + b)) qa kb.
-// Scores run on the 5th-generation tensor cores: the limb planes sit in
-// shared memory as 128-byte-swizzled K-major UMMA operands (q: M = 128 rows,
-// keys: N = 64), one thread issues tcgen05.mma kind::i8 for the nine limb
-// products (u8 / s8 per operand) into five TMEM accumulators, one per shift
-// (each below 3 * 128 * 255^2 in magnitude), and all 16 warps read them back
-// with tcgen05.ld and combine them in int64.  Values use mma.sync m16n8k32 on
-// byte limbs likewise: p (0 .. 2^16) = p0 + 2^8 p1 + 2^16 p2 with p2 in
-// {0, 1} (its three products are skipped for chunks where no p reaches 2^16),
-// five int32 sums per 64-key chunk folded into int64.  The results are the
-// integers the int64 decode kernels compute.
+// Both products run on the 5th-generation tensor cores (tcgen05.mma kind::i8,
+// u8 / s8 per operand in the instruction descriptor, one issuing thread, the
+// operands in shared memory as 128-byte-swizzled K-major tiles written by the
+// threads, accumulators in TMEM read back by all 16 warps with tcgen05.ld):
+//   scores: A = q limbs (M = 128 rows), B = key limbs (N = 64 keys), nine
+//     limb products into five accumulators, one per shift (each below
+//     3 * 128 * 255^2 in magnitude), combined in int64;
+//   values: A = probability limbs (128 rows x 128 keys), B = value limbs
+//     (dims x 128 keys), p (0 .. 2^16) = p0 + 2^8 p1 + 2^16 p2 with p2 in
+//     {0, 1} (its three products are skipped for chunks where no p reaches
+//     2^16), two N = 64 halves of the dims per chunk, folded into int64
+//     after every 128-key chunk.
+// The results are the integers the int64 decode kernels compute.
 // ---------------------------------------------------------------------------
 constexpr int kPfStride = kHeadDim + 4;   // staged int32 key row (words): 16-byte aligned rows
 constexpr int kPfRows = 2 * kPfTileQ;     // query rows of a CTA: the UMMA M of the score products
 constexpr int kPfThreads = 512;           // 16 warps: 4 row tiles x 4 dim quarters in the value pass
 constexpr size_t kPfQlBytes = (size_t)3 * kPfRows * 128;   // q limbs: three 128-byte-swizzled K-major planes
 constexpr size_t kPfKlBytes = (size_t)3 * kPfKeys * 128;   // key limbs of a chunk, same layout
-constexpr size_t kPfTabBytes = (size_t)kPfTileQ * kExpLut * 4;  // one head's probability table (value pass)
-constexpr size_t kPfRegionA = kPfQlBytes + kPfKlBytes > kPfTabBytes ? kPfQlBytes + kPfKlBytes : kPfTabBytes;
-constexpr int kPfTStride = kPfKeys + 16;  // byte-limb row of the transposed values / probabilities (20 words)
-constexpr size_t kPfVtBytes = (size_t)3 * kHeadDim * kPfTStride;  // value limbs [3][128 dims][64 keys]
-constexpr size_t kPfPlBytes = (size_t)3 * kPfTileQ * kPfTStride;  // probability limbs [3][64 rows][64 keys]
+constexpr size_t kPfPvBytes = (size_t)3 * kPfRows * 128 + (size_t)3 * kHeadDim * 128;  // probability + value limbs
+constexpr size_t kPfOperands = kPfQlBytes + kPfKlBytes > kPfPvBytes ? kPfQlBytes + kPfKlBytes : kPfPvBytes;
 constexpr size_t kPfStageBytes = (size_t)kPfKeys * kPfStride * 4;   // one chunk as staged int32
-constexpr size_t kPfSmem = 1024 + kPfRegionA + kPfVtBytes + kPfPlBytes + kPfStageBytes;  // + alignment slack
+constexpr size_t kPfSmem = 1024 + kPfOperands + kPfStageBytes;       // + alignment slack
 static_assert(kPfRows == 128 && kPfKeys == 64, "score MMAs are M = 128, N = 64");
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
 }
-// D += A B, mma.sync m16n8k32 on 8-bit operands, signed (s8) or unsigned (u8) per operand
-template <bool SA, bool SB>
-__device__ __forceinline__ void mma_limb(int32_t (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
-#define PF_MMA(TA, TB)                                                                                     \
-  asm("mma.sync.aligned.m16n8k32.row.col.s32." TA "." TB ".s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "          \
-               "{%8,%9}, {%0,%1,%2,%3};"                                                                   \
-               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])                                            \
-               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]))
-  if constexpr (!SA && !SB)
-    PF_MMA("u8", "u8");
-  else if constexpr (!SA && SB)
-    PF_MMA("u8", "s8");
-  else if constexpr (SA && !SB)
-    PF_MMA("s8", "u8");
-  else
-    PF_MMA("s8", "s8");
-#undef PF_MMA
-}
-
 // byte `l` of each of four words, packed (the limb l of four elements)
 __device__ __forceinline__ uint32_t limb_word(int4 v, int l) {
   const uint32_t sel = (uint32_t)l | ((uint32_t)(l + 4) << 4);
@@ -1521,12 +1502,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
   extern __shared__ uint8_t pf_raw[];
   const uint32_t raw_addr = umma::smem_addr(pf_raw);
   uint8_t* base = pf_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);  // 1024-byte aligned: swizzle atoms
-  uint8_t* qL = base;                                   // [3][128 rows][128 B] q limbs, UMMA A (passes 1-2)
-  uint8_t* kL = base + kPfQlBytes;                      // [3][64 keys][128 B] key limbs, UMMA B (passes 1-2)
-  uint32_t* ptab = reinterpret_cast<uint32_t*>(base);   // [64][257] one head's probability table (pass 3)
-  uint8_t* vT = base + kPfRegionA;                      // [3][128 dims][kPfTStride] value limbs, key-contiguous
-  uint8_t* pL = vT + kPfVtBytes;                        // [3][64 rows][kPfTStride] probability limbs
-  int32_t* stg = reinterpret_cast<int32_t*>(pL + kPfPlBytes);  // [64][kPfStride] staged keys / values
+  uint8_t* qL = base;                  // [3][128 rows][128 B] q limbs, UMMA A (passes 1-2)
+  uint8_t* kL = base + kPfQlBytes;     // [3][64 keys][128 B] key limbs, UMMA B (passes 1-2)
+  int32_t* stg = reinterpret_cast<int32_t*>(base + kPfOperands);  // [64][kPfStride] staged keys / values
   __shared__ int32_t elut[kExpLut];
   __shared__ int64_t rred[4][kPfRows];  // per column quarter: row maxima, then row sums
   __shared__ int64_t rmax[kPfRows];
