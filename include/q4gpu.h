@@ -425,8 +425,11 @@ int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t
  * the model stream. */
 int q4gpu_batch_prefill(q4gpu_model *m, int32_t first_slot, int32_t n_seq, const uint32_t *prompts,
                         const uint32_t *prompt_lens);
-/* How q4gpu_decode_batch runs the prompts: 1 = q4gpu_batch_prefill (default),
- * 0 = serial batched steps from position 0 (the reference's order). */
+/* How prompts run: 1 = batched exact prefill (default): q4gpu_decode_batch uses
+ * q4gpu_batch_prefill, and q4gpu_decode_token_ids (full model, from position 0,
+ * persistent mode) prefills positions 0 .. len - 2 the same way before the
+ * persistent kernel continues from the last prompt token; 0 = serial, one
+ * step per prompt position (the reference's order).  Results are identical. */
 int q4gpu_model_set_prefill(q4gpu_model *m, int32_t mode);
 
 /* Vocabulary-sharded LM head (no reference counterpart; the reference scans the

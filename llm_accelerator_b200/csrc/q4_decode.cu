@@ -1537,7 +1537,19 @@ int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_
   bool ok = cudaMemcpyAsync(st.tokens + cfg->position, toks.data(), toks.size() * 4, cudaMemcpyHostToDevice,
                             m->stream) == cudaSuccess &&
             cudaMemcpyAsync(st.pos, &hin[1], 4, cudaMemcpyHostToDevice, m->stream) == cudaSuccess;
-  if (m->mode == 1) {
+  const bool full_model = cfg->layer_start == 0u && cfg->layer_count == (uint32_t)m->cfg.n_layers;
+  if (m->prefill_mode == 1 && cfg->position == 0u && prompt_token_count >= 2u && full_model && m->cfg.vocab >= 64) {
+    // prompt positions 0 .. len - 2 as batched prefill columns (the same K/V
+    // cache as the serial runs), then max_new_tokens decode runs from the last
+    // prompt token (persistent kernel or step graphs) instead of
+    // len + max_new_tokens - 1
+    const uint32_t len = prompt_token_count;
+    ok = ok && batch_prefill(m, slot, 1, &len) == Q4GPU_OK;
+    if (m->mode == 1)
+      ok = ok && run_persistent(m, slot, (int)max_new_tokens, (int)len) == Q4GPU_OK;
+    else
+      for (uint32_t i = 0; ok && i < max_new_tokens; ++i) ok = cudaGraphLaunch(gstep, m->stream) == cudaSuccess;
+  } else if (m->mode == 1) {
     ok = ok && run_persistent(m, slot, (int)run_count, (int)(cfg->position + prompt_token_count)) == Q4GPU_OK;
   } else {
     for (uint32_t i = 0; ok && i + 1 < prompt_token_count; ++i) ok = cudaGraphLaunch(gpre, m->stream) == cudaSuccess;
