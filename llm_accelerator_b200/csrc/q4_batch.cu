@@ -1573,8 +1573,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
   // Scores of a chunk on the tensor cores: D_g[128 rows][64 keys] (TMEM
   // columns 64 g) for the five shift groups g of the nine limb products,
   // 4 MMAs of K = 32 bytes each (one thread issues).
+  const uint64_t qdesc = umma::sw128_desc(umma::smem_addr(qL)), kdesc = umma::sw128_desc(umma::smem_addr(kL));
   auto issue_scores = [&]() {
-    const uint32_t qa = umma::smem_addr(qL), ka = umma::smem_addr(kL);
     constexpr int pa[9] = {0, 0, 1, 0, 1, 2, 1, 2, 2}, pb[9] = {0, 1, 0, 2, 1, 0, 2, 1, 2};
     constexpr int pg[9] = {0, 1, 1, 2, 2, 2, 3, 3, 4};
     constexpr bool first[9] = {true, true, false, true, false, false, true, false, true};
@@ -1582,11 +1582,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
     for (int q = 0; q < 9; ++q) {
       const uint32_t idesc = umma::i8_idesc_ab(kPfRows, kPfKeys, pa[q] == 2, pb[q] == 2);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_i8(tmem + (uint32_t)(pg[q] * kPfKeys),
-                     umma::sw128_desc(qa + (uint32_t)(pa[q] * kPfRows * 128 + 32 * ks)),
-                     umma::sw128_desc(ka + (uint32_t)(pb[q] * kPfKeys * 128 + 32 * ks)), idesc,
-                     (first[q] && ks == 0) ? 0u : 1u);
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint64_t ad = qdesc + (uint64_t)((pa[q] * kPfRows * 128 + 32 * ks) >> 4);
+        const uint64_t bd = kdesc + (uint64_t)((pb[q] * kPfKeys * 128 + 32 * ks) >> 4);
+        const uint32_t d = tmem + (uint32_t)(pg[q] * kPfKeys);
+        if (first[q] && ks == 0)
+          umma::mma_i8_init(d, ad, bd, idesc);
+        else
+          umma::mma_i8_acc(d, ad, bd, idesc);
+      }
     }
     umma::mma_commit(&mbar);
   };
@@ -1711,8 +1715,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
       for (int l = 0; l < 3; ++l) put_sw(vTt + l * (kHeadDim * 128), dd, 16 * half + jg, limb_word(v, l));
     }
   };
+  const uint64_t pdesc = umma::sw128_desc(umma::smem_addr(pLt)), vdesc = umma::sw128_desc(umma::smem_addr(vTt));
   auto issue_values = [&](int h, bool any2) {
-    const uint32_t pa = umma::smem_addr(pLt), va = umma::smem_addr(vTt);
     constexpr int ppa[9] = {0, 0, 1, 0, 1, 1, 2, 2, 2}, ppb[9] = {0, 1, 0, 2, 1, 2, 0, 1, 2};
     constexpr int ppg[9] = {0, 1, 1, 2, 2, 3, 2, 3, 4};
     constexpr bool first[9] = {true, true, false, true, false, true, false, false, true};
@@ -1721,11 +1725,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(PfAttn a) {
       if (ppa[q] == 2 && !any2) continue;  // p2 = 0 in every row of the chunk: group 4 stays unused
       const uint32_t idesc = umma::i8_idesc_ab(kPfRows, 64, false, ppb[q] == 2);
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma::mma_i8(tmem + (uint32_t)(ppg[q] * 64),
-                     umma::sw128_desc(pa + (uint32_t)(ppa[q] * kPfRows * 128 + 32 * ks)),
-                     umma::sw128_desc(va + (uint32_t)(ppb[q] * kHeadDim * 128 + h * 64 * 128 + 32 * ks)), idesc,
-                     (first[q] && ks == 0) ? 0u : 1u);
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint64_t ad = pdesc + (uint64_t)((ppa[q] * kPfRows * 128 + 32 * ks) >> 4);
+        const uint64_t bd = vdesc + (uint64_t)((ppb[q] * kHeadDim * 128 + h * 64 * 128 + 32 * ks) >> 4);
+        const uint32_t d = tmem + (uint32_t)(ppg[q] * 64);
+        if (first[q] && ks == 0)
+          umma::mma_i8_init(d, ad, bd, idesc);
+        else
+          umma::mma_i8_acc(d, ad, bd, idesc);
+      }
     }
     umma::mma_commit(&mbar);
   };

@@ -159,6 +159,24 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
       : "memory");
 }
+// The same with the accumulate flag fixed: D = A B (init) or D += A B (acc).
+// A descriptor's start-address field is (address >> 4) in its low 14 bits, so
+// the descriptor of a tile at a 16-byte multiple `off` past another is that
+// descriptor + off / 16 (shared-memory addresses stay below 2^18).
+__device__ __forceinline__ void mma_i8_init(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, 0, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%4, %4, %4, %4}, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
+      : "memory");
+}
+__device__ __forceinline__ void mma_i8_acc(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.eq.b32 p, 0, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%4, %4, %4, %4}, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(0)
+      : "memory");
+}
 // Arrive on bar once every tcgen05 operation this thread issued so far is done.
 __device__ __forceinline__ void mma_commit(uint64_t* b) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(b))
