@@ -466,9 +466,11 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   __shared__ uint64_t bars[kAttnRing];
   const int kv = blockIdx.x, m = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  grid_dep_wait();
-  grid_dep_launch();
   attn_stamp(c, layer, m, kv, 0);
+  // The cached K/V rows (positions < pos, written by earlier steps) and the
+  // position itself (advanced at the end of the previous step) do not depend
+  // on the kernels of this step: the first chunks load before the wait for
+  // the q/k/v projections.
   const int pos = c.pos0[4 * m];
   if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
@@ -490,6 +492,8 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     umma::bar_init_fence();
     for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
   }
+  grid_dep_wait();
+  grid_dep_launch();
   const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
   // warp 0: q head 2kv, warp 1: q head 2kv+1, warp 2: k (normed, roped);
   // warp 3: v.  A lane owns dims 4 lane .. 4 lane + 3; the RoPE partner
@@ -1259,9 +1263,9 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   __shared__ uint64_t bars[kAttnRing];
   const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  grid_dep_wait();
-  grid_dep_launch();
-  // every rank reaches every cluster barrier below: no early return
+  // every rank reaches every cluster barrier below: no early return.  The
+  // cached K/V rows and the position come from earlier steps, so the first
+  // chunks load before the wait for this step's q/k/v projections.
   const int pos = c.pos0[4 * m];
   const bool live = pos < c.max_ctx;
   const int ctx = live ? pos + 1 : 0;
@@ -1288,6 +1292,8 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
     umma::bar_init_fence();
     for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
   }
+  grid_dep_wait();
+  grid_dep_launch();
   if (live) {
     const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
     const bool owner = pos >= k0 && pos < k1;  // the rank whose range holds the new position appends it
