@@ -418,8 +418,8 @@ int q4gpu_batch_steps(q4gpu_model *m, int32_t first_slot, int32_t n_seq, int32_t
  * array (prompts concatenated, prompt_lens[n_seq], 1 <= len <= max_context),
  * runs positions 0 .. len - 2 of all n_seq sequences (1 <= n_seq <= 64, slots
  * [first_slot, first_slot + n_seq)) through every layer as columns of batched
- * passes (64 columns per tcgen05 GEMM, 32-position query tiles per attention
- * CTA), and leaves each slot at position len - 1 with lm_from = len: the K/V
+ * passes (64 columns per tcgen05 GEMM sub-batch, 1024 columns per block,
+ * query tiles of up to 64 positions of one sequence per attention CTA), and leaves each slot at position len - 1 with lm_from = len: the K/V
  * cache equals the one serial decode steps leave, bit for bit, and
  * q4gpu_batch_steps continues from the last prompt token.  Asynchronous on
  * the model stream. */

@@ -38,9 +38,9 @@ def _run(m, prompts, n_gen, mode):
 
 
 def test_prefill_matches_serial_across_blocks_and_tiles(gm):
-    """Ragged prompts (1 .. 700 tokens): 1228 prefill columns over three
-    512-column blocks, query tiles cut at 32 positions, at sequence changes and
-    at block edges; tokens, scores and the whole K/V cache of both layers equal
+    """Ragged prompts (1 .. 700 tokens): 1227 prefill columns over two
+    1024-column blocks (the 700-token prompt straddles the edge), query tiles
+    cut at 64 positions, at sequence changes and at block edges; tokens, scores and the whole K/V cache of both layers equal
     the serial path's."""
     rng = np.random.default_rng(5)
     lens = [1, 2, 31, 32, 33, 64, 65, 300, 700, 9]
