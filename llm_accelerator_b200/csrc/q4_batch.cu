@@ -150,13 +150,14 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
                                                                const int32_t* __restrict__ gamma,
                                                                int32_t* __restrict__ out_act) {
   __shared__ int64_t red[32];
+  const int m = blockIdx.x, k = 4 * threadIdx.x;
+  // the norm weights do not depend on earlier kernels: load them before the wait
+  const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
   grid_dep_wait();
   grid_dep_launch();
-  const int m = blockIdx.x, k = 4 * threadIdx.x;
   const int sub = m / c.SP, ms = m - sub * c.SP;
   uint8_t* bt = c.bt1 + (size_t)sub * c.bt_sub1;
   const int4 x = *reinterpret_cast<const int4*>((which == 0 ? c.hidden0 : c.post0) + (size_t)m * kHidden + k);
-  const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
   int64_t ss = (int64_t)x.x * x.x + (int64_t)x.y * x.y + (int64_t)x.z * x.z + (int64_t)x.w * x.w;
   ss = block_sum_i64(ss, red);
   const int64_t inv = inv_rms_from_ss(ss, kHiddenNorm);
@@ -209,6 +210,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                "l"(src), "r"(bytes), "r"(umma::smem_addr(bar))
                : "memory");
 }
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ int64_t ld_cg64(const int64_t* p) {
   return (int64_t)__ldcg(reinterpret_cast<const long long*>(p));
@@ -535,6 +545,7 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
   {
     const int sub = lane & 7, quad = lane >> 3;
+    const bool hi = (sub & 4) != 0;
     int32_t q0[16], q1[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -560,28 +571,30 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
           }
         }
       }
-#pragma unroll
-      for (int msk = 1; msk < 8; msk <<= 1) {
-        s0 += shfl_xor_i64(s0, msk);
-        s1 += shfl_xor_i64(s1, msk);
-      }
+      // the 8 lanes' partial sums: one exchange splits the heads (lanes
+      // sub < 4 keep head 0, sub >= 4 head 1), two more finish each sum, so
+      // every lane scales one score
+      int64_t sh = hi ? s1 : s0;
+      sh += shfl_xor_i64(hi ? s0 : s1, 4);
+      sh += shfl_xor_i64(sh, 2);
+      sh += shfl_xor_i64(sh, 1);
       if (p < ctx) {
-        const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
-        if (sub == 0) {
-          sc[p] = v0;
-          sc[ctx + p] = v1;
-        }
-        mx0 = v0 > mx0 ? v0 : mx0;
-        mx1 = v1 > mx1 ? v1 : mx1;
+        const int64_t v = scale_score(sh, kScoreScale);
+        if ((sub & 3) == 0) sc[hi ? ctx + p : p] = v;
+        if (hi)
+          mx1 = v > mx1 ? v : mx1;
+        else
+          mx0 = v > mx0 ? v : mx0;
       }
       __syncthreads();  // slot i % 3 is free again
       if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
     }
   }
   attn_stamp(c, layer, m, kv, 2);
-  // maxima of both heads (one block reduction)
+  // maxima of both heads (one block reduction; head 0's sit in lanes with
+  // sub < 4, head 1's in the others)
 #pragma unroll
-  for (int msk = 8; msk < 32; msk <<= 1) {
+  for (int msk = 4; msk < 32; msk <<= 1) {
     const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
     mx0 = o0 > mx0 ? o0 : mx0;
     mx1 = o1 > mx1 ? o1 : mx1;
@@ -623,11 +636,10 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     sum1 += red[1][w];
   }
   {
-    const uint64_t d0 = (uint64_t)sum0, d1 = (uint64_t)sum1, r0 = ~0ULL / d0, r1 = ~0ULL / d1;
-    for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
-      const int h = i >= kExpLut, e = i - h * kExpLut;
-      probtab[h][e] = barrett_div((uint64_t)exp_lut[e] << 16, h ? d1 : d0, h ? r1 : r0);
-    }
+    // warps 0-3 build head 0's table, warps 4-7 head 1's: one reciprocal each
+    const int h = t >> 7;
+    const uint64_t d = (uint64_t)(h ? sum1 : sum0), rc = ~0ULL / d;
+    for (int e = t & 127; e < kExpLut; e += 128) probtab[h][e] = barrett_div((uint64_t)exp_lut[e] << 16, d, rc);
   }
   __syncthreads();
   // per-position probabilities of both heads, packed over the index array
@@ -714,9 +726,19 @@ struct UCfg {
   static constexpr int TCOLS = 2 * NB <= 32 ? 32 : 2 * NB <= 64 ? 64 : 2 * NB <= 128 ? 128 : 2 * NB <= 256 ? 256 : 512;
   static constexpr int BUF = TCOLS / 2;  // TMEM columns of one accumulator buffer
   static constexpr int RED_BYTES = 128 * SP * 8;
-  static constexpr size_t SMEM = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 512;
+  // operands of the final epilogue staged during the K loop: the residual
+  // rows a CTA owns (O / down, splits >= 2: at most 64 rows x SP) or the
+  // sigmoid table (gate/up)
+  static constexpr int STG_BYTES = 64 * SP * 4 > 4 * kSigLut ? 64 * SP * 4 : (4 * kSigLut + 15) / 16 * 16;
+  static constexpr size_t SMEM_BASE = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 512;
   static constexpr uint32_t IDESC = umma::i8_idesc(128, NB);
 };
+// dynamic shared memory of a GEMM kind: O (1), gate/up (2) and down (3)
+// stage their final-epilogue operands
+template <int SP, int KIND>
+constexpr size_t gemm_smem() {
+  return UCfg<SP>::SMEM_BASE + (KIND == 1 || KIND == 2 || KIND == 3 ? UCfg<SP>::STG_BYTES : 0);
+}
 
 struct UGemm {
   BatchCtx c;
@@ -731,7 +753,8 @@ struct UGemm {
 
 // GEMM timeline points: 0 entry, 1 set-up done, 2 dependency released (TMA
 // warp), 3 first accumulator ready, 4 last group folded, 5 partial sums
-// exchanged, 6 epilogue done (epilogue warp 2 records 3-4, thread 0 the rest)
+// exchanged, 6 epilogue done, 7 last K tile landed (epilogue warp 2 records
+// 3-4, the MMA thread 7, thread 0 the rest)
 __device__ __forceinline__ void gemm_stamp(const UGemm& g, int k) {
   if (g.trace) {
     unsigned long long t;
@@ -755,6 +778,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* live = reinterpret_cast<int*>(tmem_slot + 2);  // [64]: sequence m takes part in this step
+  int32_t* stg = reinterpret_cast<int32_t*>(sm + kUStages * C::STAGE + C::RED_BYTES + 512);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // grid (sub-batches, K splits, row tiles): the sub-batches of one weight
@@ -833,17 +857,14 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
   } else if (warp == 1) {
     grid_dep_wait();
-    if (lane != 0) {
-      // which sequences take part in this step (the epilogues that update slot state)
-      if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
-        for (int m = lane - 1; m < SP; m += 31) live[m] = m < c.S && c.pos0[4 * m] < c.max_ctx;
-    } else {
+    if (lane == 0) {
       for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
         const int s = kt % kUStages;
         if (!umma::bar_wait(full + s, (kt / kUStages) & 1)) {
           fail();
           break;
         }
+        if (kt == nkt - 1) gemm_stamp(g, 7);
         umma::fence_after_sync();
         const uint32_t a0 = umma::smem_addr(sm + s * C::STAGE), b0 = a0 + C::A_BYTES;
         for (int h = 0; h < 2; ++h) {
@@ -865,6 +886,34 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
   } else {
     grid_dep_wait();
+    // Before the K loop, without waiting on the loads: stage what the final
+    // epilogue reads from global memory (written by kernels this one waited
+    // for) by cp.async, the residual of each owned (row, sequence) item
+    // (O / down) or the sigmoid table (gate/up), and fetch the positions
+    // that say which sequences take part in this step.
+    const int et2 = threadIdx.x - 64;
+    int pos_m = INT_MAX;
+    if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
+      if (et2 < SP && et2 < c.S) pos_m = c.pos0[4 * et2];
+    if constexpr (KIND == kGemmO || KIND == kGemmDown) {
+      // items i .. i + 3 (i a multiple of 4) are 4 consecutive rows of one
+      // sequence: rows_per = 64 / splits >= 8
+      const int32_t* res = KIND == kGemmO ? c.hidden0 : c.post0;
+      const int lsp = __ffs(splits) - 1, lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
+      for (int i = 4 * et2; i < nl * SP; i += 4 * (kUThreads - 64)) {
+        const int local = i & (nl - 1), m = i >> lnl;
+        const int row = ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
+        if (m < c.S) cp_async16(stg + i, res + (size_t)m * kHidden + row0 + row);
+      }
+    } else if constexpr (KIND == kGemmGu) {
+      if ((reinterpret_cast<uintptr_t>(g.sig_lut) & 15) == 0) {
+        for (int e4 = et2; e4 < kSigLut / 4; e4 += kUThreads - 64) cp_async16(stg + 4 * e4, g.sig_lut + 4 * e4);
+        for (int e = kSigLut / 4 * 4 + et2; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
+      } else {
+        for (int e = et2; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
+      }
+    }
+    cp_async_commit();
     // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (its sub-partition);
     // the four warps of one sub-partition take a quarter of the sequences each
     const int sp = warp & 3, q = (warp - 2) >> 2;
@@ -912,12 +961,17 @@ __global__ void __launch_bounds__(kUThreads, 1)
       }
     }
     if (warp == 2 && lane == 0) gemm_stamp(g, 4);
+    cp_async_wait0();
+    if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
+      if (et2 < SP) live[et2] = pos_m < c.max_ctx;
     // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
-    // so each owner holds matching rows of both 64-row halves (gate and up)
-    const int rows_per = 64 / splits;
-    const int owner = (r & 63) / rows_per;
-    const int local = (r >> 6) * rows_per + (r & 63) % rows_per;
-    const int nl = 128 / splits;
+    // so each owner holds matching rows of both 64-row halves (gate and up);
+    // splits is a power of two (1, 2, 4 or 8), so these are shifts and masks
+    const int lsp = __ffs(splits) - 1;
+    const int rows_per = 64 >> lsp;
+    const int owner = (r & 63) >> (6 - lsp);
+    const int local = (r >> 6) * rows_per + (r & (rows_per - 1));
+    const int nl = 128 >> lsp;
     // red[src][m][local]: a warp's 32 rows land contiguously
     int64_t* dst = red + ((size_t)split * SP + q * C::Q) * nl + local;
     if (splits == 1) {
@@ -936,10 +990,14 @@ __global__ void __launch_bounds__(kUThreads, 1)
     __syncthreads();
   if (threadIdx.x == 0) gemm_stamp(g, 5);
 
-  // final epilogue over the rows this CTA owns
-  const int rows_per = 64 / splits, nl = 128 / splits;
+  // final epilogue over the rows this CTA owns (local row l, sequence m: item
+  // l + nl m; rows_per and nl are powers of two)
+  const int lsp = __ffs(splits) - 1;
+  const int lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
   const int et = threadIdx.x;
-  auto row_of = [&](int local) { return (local / rows_per) * 64 + split * rows_per + local % rows_per; };
+  auto row_of = [&](int local) {
+    return ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
+  };
   auto sum_of = [&](int local, int m) {
     int64_t v = 0;
     for (int src = 0; src < splits; ++src) v += red[((size_t)src * SP + m) * nl + local];
@@ -948,31 +1006,29 @@ __global__ void __launch_bounds__(kUThreads, 1)
   if (!*abort_flag) {
     if constexpr (KIND == kGemmQkv) {
       for (int i = et; i < nl * SP; i += kUThreads) {
-        const int local = i % nl, m = i / nl;
+        const int local = i & (nl - 1), m = i >> lnl;
         if (m < c.S)
           c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
       }
     } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
+      // residual (staged in stg) + o_proj / down output >> 2
+      int32_t* __restrict__ out = KIND == kGemmO ? c.post0 : c.hidden0;
       for (int i = et; i < nl * SP; i += kUThreads) {
-        const int local = i % nl, m = i / nl;
+        const int local = i & (nl - 1), m = i >> lnl;
         if (!live[m]) continue;
-        const size_t at = (size_t)m * kHidden + row0 + row_of(local);
         const int32_t o = sat24(sum_of(local, m) >> 14);
-        if (KIND == kGemmO)
-          c.post0[at] = sat24((int64_t)c.hidden0[at] + (o >> 2));
-        else
-          c.hidden0[at] = sat24((int64_t)c.post0[at] + (o >> 2));
+        out[(size_t)m * kHidden + row0 + row_of(local)] = sat24((int64_t)stg[i] + (o >> 2));
       }
     } else if constexpr (KIND == kGemmGu) {
       // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
       for (int i = et; i < rows_per * SP; i += kUThreads) {
-        const int j = i % rows_per, m = i / rows_per;
+        const int j = i & (rows_per - 1), m = i >> lrp;
         if (!live[m]) continue;
         const int32_t gv = sat24(sum_of(j, m) >> 14), uv = sat24(sum_of(rows_per + j, m) >> 14);
         const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
         int ix = (gc + 32768 + 32) >> 6;
         ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
-        const int32_t silu = sat24(((int64_t)gv * g.sig_lut[ix]) >> 16);
+        const int32_t silu = sat24(((int64_t)gv * stg[ix]) >> 16);
         const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
         write_limbs(c.bt3, SP, kInter, m, tile * 64 + split * rows_per + j, hv);
       }
@@ -1191,9 +1247,6 @@ constexpr size_t kPfStageBytes = (size_t)kPfKeys * kPfStride * 4;   // one chunk
 constexpr size_t kPfSmem = 1024 + kPfOperands + kPfStageBytes;       // + alignment slack
 static_assert(kPfRows == 128 && kPfKeys == 64, "score MMAs are M = 128, N = 64");
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(umma::smem_addr(dst)), "l"(src) : "memory");
-}
 // byte `l` of each of four words, packed (the limb l of four elements)
 __device__ __forceinline__ uint32_t limb_word(int4 v, int l) {
   const uint32_t sel = (uint32_t)l | ((uint32_t)(l + 4) << 4);
@@ -1202,8 +1255,6 @@ __device__ __forceinline__ uint32_t limb_word(int4 v, int l) {
   return __byte_perm(lo, hi, 0x5410);
 }
 
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // q (kind 0) or k (kind 1) head row -> RMSNorm (head constants) -> RoPE at
 // `pos`, by one warp: lane owns elements 4 lane .. 4 lane + 3, the rotation
@@ -1911,9 +1962,13 @@ template <int SP, int KIND>
 cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const BatchCtx& c, const uint16_t* scales,
                         int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s,
                         unsigned long long* trace = nullptr, int subs = 1) {
+  // the epilogue's row bookkeeping uses shifts: splits must be 1, 2, 4 or 8
+  if (splits < 1 || splits > 8 || (splits & (splits - 1)) || K % (128 * splits)) return cudaErrorInvalidValue;
+  // O / down stage their residual rows (128 / splits of them) in 64 rows' room
+  if ((KIND == kGemmO || KIND == kGemmDown) && splits < 2) return cudaErrorInvalidValue;
   UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial, trace};
   const dim3 grid((unsigned)subs, (unsigned)splits, (unsigned)((rows + 127) / 128));
-  return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), UCfg<SP>::SMEM, s, splits, amap, bmap, g);
+  return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), gemm_smem<SP, KIND>(), s, splits, amap, bmap, g);
 }
 
 bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
@@ -2005,7 +2060,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
 template <int SP, int KIND>
 int set_smem() {
   BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)UCfg<SP>::SMEM));
+                          (int)gemm_smem<SP, KIND>()));
   return Q4GPU_OK;
 }
 
@@ -2089,7 +2144,7 @@ int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
   act_limbs_kernel<<<q.n_act, 256, 0, s>>>(q.acts, q.bt, SP);
   BQ(cudaGetLastError());
   BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, kGemmLm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)UCfg<SP>::SMEM));
+                          (int)gemm_smem<SP, kGemmLm>()));
   const int rows = q.row_end - q.row_begin;
   BQ((launch_gemm<SP, kGemmLm>(q.amap, q.bmap, c, q.scales, rows, kHidden, 1, nullptr, q.partial, s)));
   shard_argmax_kernel<<<q.n_act, 256, 0, s>>>(q.partial, (rows + 127) / 128, q.row_begin, q.best_score, q.best_row);

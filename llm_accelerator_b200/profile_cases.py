@@ -4,10 +4,11 @@
     python -m llm_accelerator_b200.profile_cases gemv --rows 151936 --k 1024 --reps 3
     python -m llm_accelerator_b200.profile_cases lmhead --rows 151936 --reps 3
 
-`batch`: the full 28-layer, 151936-vocabulary synthetic model (seed 0), `seqs`
-sequences set to `position` and advanced `steps` batched decode steps (200
-kernel launches per step: embed, 28 x [norm, qkv GEMM, attention, o_proj GEMM,
-norm, gate/up GEMM, down GEMM], norm, LM-head GEMM, argmax).
+`batch`: the 151936-vocabulary synthetic model (seed 0; 28 layers, or `--layers`
+for a smaller capture: the per-layer launches do not depend on the layer count),
+`seqs` sequences set to `position` and advanced `steps` batched decode steps
+(4 + 7 L kernel launches per step: embed, L x [norm, qkv GEMM, attention,
+o_proj GEMM, norm, gate/up GEMM, down GEMM], norm, LM-head GEMM, argmax).
 `gemv` / `lmhead`: `reps` calls of q4gpu_gemv_q26 / q4gpu_lm_head_argmax on a
 random packed matrix (a few hundred MB of device memory at most).
 """
@@ -16,10 +17,10 @@ from __future__ import annotations
 import argparse
 
 
-def batch_case(seqs: int, position: int, steps: int, max_context: int) -> None:
+def batch_case(seqs: int, position: int, steps: int, max_context: int, layers: int = 28) -> None:
     from .model import Q4Model
 
-    with Q4Model(n_layers=28, vocab=151936, max_context=max_context, max_seqs=seqs) as m:
+    with Q4Model(n_layers=layers, vocab=151936, max_context=max_context, max_seqs=seqs) as m:
         m.init_synthetic(seed=0)
         m.batch_set_position(position, seqs, lm_from=0)
         m.batch_steps(steps, seqs)
@@ -62,6 +63,7 @@ def main() -> None:
     b.add_argument("--position", type=int, default=383)
     b.add_argument("--steps", type=int, default=2)
     b.add_argument("--max-context", type=int, default=512)
+    b.add_argument("--layers", type=int, default=28)
     for name in ("gemv", "lmhead"):
         p = sub.add_parser(name)
         p.add_argument("--rows", type=int, default=151936)
@@ -69,7 +71,7 @@ def main() -> None:
         p.add_argument("--reps", type=int, default=3)
     a = ap.parse_args()
     if a.case == "batch":
-        batch_case(a.seqs, a.position, a.steps, a.max_context)
+        batch_case(a.seqs, a.position, a.steps, a.max_context, a.layers)
     else:
         gemv_case(a.rows, a.k if a.case == "gemv" else 1024, a.reps, a.case == "lmhead")
     print("ok")
