@@ -456,8 +456,10 @@ __global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, Attn
 // bulk copies, contiguous inside a KV page); the current position's K/V row
 // is taken from shared memory.  The score maxima are kept while the scores
 // are made, so the softmax is one pass over the (shared-memory) scores.
-// Used when the batch has enough (KV head, sequence) pairs to fill the GPU;
-// small batches and long contexts use the split-KV kernels above.
+// Used when the batch has enough (KV head, sequence) pairs to fill the GPU
+// and contexts up to 1024; smaller batches and longer contexts use the
+// cluster kernel (batch_attn_cl_kernel), the longest ones the split-KV
+// kernels above.
 constexpr int kAttnChunk = 32;
 constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
 constexpr int kAttnRing = 2;
@@ -468,7 +470,7 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
                                                             const int32_t* __restrict__ sin_tab,
                                                             const int32_t* __restrict__ exp_lut) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
-  int32_t* ring = reinterpret_cast<int32_t*>(attn_smem);                            // [3][32][128]
+  int32_t* ring = reinterpret_cast<int32_t*>(attn_smem);                            // [kAttnRing][32][128]
   int64_t* sc = reinterpret_cast<int64_t*>(attn_smem + kAttnRing * kAttnChunkBytes);  // [2][ctx]
   __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v
   __shared__ uint32_t probtab[2][kExpLut];
@@ -586,7 +588,7 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
         else
           mx0 = v > mx0 ? v : mx0;
       }
-      __syncthreads();  // slot i % 3 is free again
+      __syncthreads();  // slot i % kAttnRing is free again
       if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
     }
   }
