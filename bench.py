@@ -10,16 +10,21 @@ prefilled as columns of batched passes (q4gpu_batch_prefill; the serial
 position-by-position prefill, the reference's order, is timed beside it and
 must give the same first tokens).  One timed step = one batched decode step: 64
 tokens, one per sequence (embedding, 28 layers, final norm, LM head,
-argmax), at decode positions cycling through 256..510 (the generated half;
-a cycle replays the same tokens).  Per step the weights (420 MB of int8
-copies) and the KV cache of 64 sequences (~5.6 GB at the mean context 384)
-stream from HBM: far larger than L2, so no flush is needed.
+argmax), at decode positions in 256..510 (the generated half; a cycle replays
+the same tokens).  The timed window of --steps steps is centred in that cycle,
+so its mean context is the cycle's (384); the per-kernel roofline is taken at
+the same mean context.  Per step the weights (317 MB of Q4) and the KV cache
+of 64 sequences (~5.6 GB at context 384) stream from HBM: far larger than L2,
+so no flush is needed.
 
 Secondary (one GPU only): `batch1`: batch 1, prompt 128,
-decode positions 128..255, on the persistent cooperative kernel; `gemv`
-(config 1); `cfg5` (config 5 on one GPU: 8 x 8192-token prompts through the
-batched exact prefill, decode from position 8192).  `--cfg5` runs config 5
-alone, on N GPUs with the vocabulary-sharded LM head.
+decode positions 128..255, on the persistent cooperative kernel; `cfg2` (one
+decoder layer at batch 1, context 513); `gemv` (config 1); `cfg5` (config 5 on
+one GPU: 8 x 8192-token prompts through the batched exact prefill, decode from
+position 8192).  Each decode secondary carries a `parity` field from the C
+oracle (config 3: every token and score of the timed run; config 5: sampled
+positions re-run on top of the GPU's cache).  `--cfg5` runs config 5 alone,
+on N GPUs with the vocabulary-sharded LM head.
 
 N > 1 (torchrun, one rank per GPU): every rank decodes its own 64 sequences
 (prompt seeds depend on the rank); no collective on the data path; value is
@@ -58,7 +63,8 @@ GEN = 256
 MAX_CTX = 512
 CYCLE = GEN - 1  # decode steps of one generation: positions 256..510
 WORKLOAD = ("cfg4: Qwen3-0.6B 28-layer Q4 (int4 + Q2.14 group scales) greedy decode, 64 sequences per GPU, "
-            "prompt 256 uniform ids each, 256 generated tokens, context up to 512, decode positions 256..510 cycled")
+            "prompt 256 uniform ids each, 256 generated tokens, context up to 512, timed window centred in decode "
+            "positions 256..510")
 B1_PROMPT, B1_CYCLE = 128, 128
 CFG5_SEQS, CFG5_PROMPT, CFG5_GEN = 8, 8192, 512
 HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
@@ -69,27 +75,63 @@ HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 # attention at context `ctx`): what the kernel must move at least
 # ---------------------------------------------------------------------------
 def batch_kernel_bytes(kind: str, S: int, ctx: int) -> int:
+    """Algorithmic bytes of one launch: weights counted as Q4 (packed nibbles +
+    u16 scales), K/V at the reference's 4 B per element."""
     limbs = 3 * S  # limb rows of a B matrix (u8)
+
+    def q4(rows: int, k: int) -> int:
+        return rows * k // 2 + rows * k // 32
+
     if kind == "embed":
         return S * (512 + 32 + 4 * HIDDEN)
     if kind == "norm_limbs":
         return S * (4 * HIDDEN + limbs // S * HIDDEN) + 4 * HIDDEN
     if kind == "qkv_gemm":
-        return QKV_ROWS * HIDDEN + QKV_ROWS * 32 + limbs * HIDDEN + S * QKV_ROWS * 4
+        return q4(QKV_ROWS, HIDDEN) + limbs * HIDDEN + S * QKV_ROWS * 4
     if kind == "attention":
         kv_read = 8 * 2 * (ctx - 1) * 128 * 4
         return S * (kv_read + 8 * 2 * 128 * 4 + QKV_ROWS * 4 + 3 * 2 * HIDDEN)
     if kind == "o_proj_gemm":
-        return HIDDEN * 2 * HIDDEN + HIDDEN * 64 + limbs * 2 * HIDDEN + S * 3 * HIDDEN * 4
+        return q4(HIDDEN, 2 * HIDDEN) + limbs * 2 * HIDDEN + S * 3 * HIDDEN * 4
     if kind == "gate_up_gemm":
-        return 2 * INTER * HIDDEN + 2 * INTER * 32 + limbs * HIDDEN + limbs * INTER
+        return q4(2 * INTER, HIDDEN) + limbs * HIDDEN + limbs * INTER
     if kind == "down_gemm":
-        return HIDDEN * INTER + HIDDEN * 96 + limbs * INTER + S * 3 * HIDDEN * 4
+        return q4(HIDDEN, INTER) + limbs * INTER + S * 3 * HIDDEN * 4
     if kind == "lm_head_gemm":
-        return VOCAB * HIDDEN + VOCAB * 32 + limbs * HIDDEN + (VOCAB + 127) // 128 * 64 * 16
+        return q4(VOCAB, HIDDEN) + limbs * HIDDEN + (VOCAB + 127) // 128 * 64 * 16
     if kind == "argmax":
         return S * ((VOCAB + 127) // 128 * 16 + 16)
     return 0
+
+
+def timed_window(steps: int) -> int:
+    """First decode position of a timed window of `steps` steps: centred in the
+    cycle 256..510 so that the window's mean context is the cycle's (384)."""
+    return PROMPT if steps >= CYCLE else PROMPT + (CYCLE - steps) // 2
+
+
+def window_positions(start: int, steps: int) -> list[int]:
+    """Decode positions of `steps` steps from `start`, wrapping to 256 after 510."""
+    out, p = [], start
+    for _ in range(steps):
+        if p >= PROMPT + CYCLE:
+            p = PROMPT
+        out.append(p)
+        p += 1
+    return out
+
+
+def host_cpu() -> dict:
+    """CPU model and logical core count of this host."""
+    model = "unknown"
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count()}
 
 
 def measured_peaks() -> dict:
@@ -181,36 +223,48 @@ def prompts_for(rank: int) -> list[list[int]]:
 # ---------------------------------------------------------------------------
 # CPU arm: the C restatement of the reference path, one sequence at a time
 # ---------------------------------------------------------------------------
-def cpu_decode(n_steps: int, warmup: int, threads: int = 0) -> dict:
-    """Sequence 0 of rank 0: serial prefill of its 256-token prompt, then
-    warm-up + n_steps greedy decode steps (one token each) from position 256."""
+def cpu_decode(n_steps: int, warmup: int, threads: int = 0, cm=None) -> dict:
+    """Sequence 0 of rank 0 on the C oracle: serial prefill of its 256-token
+    prompt, greedy decode up to the GPU's timed window (timed_window), then
+    warm-up + n_steps steps (one token each) timed over that window's positions."""
     from oracle import c_oracle as CO
     cores = CO.set_threads(threads)
-    m = CO.CModel(LAYERS, VOCAB, MAX_CTX, seed=0)
+    own = cm is None
+    if own:
+        cm = CO.CModel(LAYERS, VOCAB, MAX_CTX, seed=0)
     prompt = prompts_for(0)[0]
     tok = 0
     for p, t in enumerate(prompt):
-        tok, _ = m.run_token(t, p, want_logits=(p == PROMPT - 1))
-    first = tok
-    toks = []
+        tok, _ = cm.run_token(t, p, want_logits=(p == PROMPT - 1))
+    ring = {PROMPT: tok}  # token at each decode position
+    start = timed_window(n_steps)
     pos = PROMPT
-
-    def step():
-        nonlocal tok, pos
-        if pos >= PROMPT + CYCLE:
-            pos, tok = PROMPT, first
-        tok, _ = m.run_token(tok, pos)
-        toks.append(tok)
+    while pos < start:  # the tokens leading into the window (untimed)
+        ring[pos + 1], _ = cm.run_token(ring[pos], pos)
         pos += 1
+    positions = window_positions(start, warmup) + window_positions(start, n_steps)
 
-    for _ in range(warmup):
-        step()
+    def step(p):
+        ring[p + 1], _ = cm.run_token(ring[p], p)
+
+    for p in positions[:warmup]:
+        step(p)
     t0 = time.perf_counter()
-    for _ in range(n_steps):
-        step()
+    for p in positions[warmup:]:
+        step(p)
     dt = time.perf_counter() - t0
-    m.close()
-    return {"value": n_steps / dt, "cores": cores, "seconds": dt, "tokens": [first] + toks}
+    if own:
+        cm.close()
+    return {"value": n_steps / dt, "cores": cores, "seconds": dt, "start": start,
+            "tokens": [ring[p] for p in range(PROMPT, PROMPT + 17) if p in ring]}
+
+
+def cpu_sample_text(steps: int, warm: int, start: int) -> str:
+    return (f"sequence 0 of the config-4 workload: {steps} decode steps (one token each) at positions "
+            f"{start}..{start + steps - 1} (the GPU's timed window) after {warm} warm-up steps, its serial "
+            "256-token prefill and the steps leading to the window; C restatement of the reference's Python Q4 "
+            "path (oracle/q4_oracle.c), OpenMP over all host threads.  Extrapolated: the CPU decodes one sequence "
+            "at a time, so its tokens/s on this sample stands for the 64-sequence workload")
 
 
 def run_reference(args, ws, rank):
@@ -223,11 +277,10 @@ def run_reference(args, ws, rank):
         "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 * r["seconds"] / steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
         "config": {"workload": WORKLOAD, "batch": BATCH, "prompt": PROMPT, "generate": GEN,
+                   "timed_positions": [r["start"], r["start"] + steps - 1],
                    "parallelism": "host CPU, one sequence at a time"},
         "cpu_baseline": {"value": round(r["value"], 3), "unit": UNIT, "cores": r["cores"], "kind": "port",
-                         "sample": f"sequence 0: {steps} decode steps (one token each) after {warm} warm-up steps "
-                                   "and the serial 256-token prefill, C restatement of the reference's Python Q4 "
-                                   "path (oracle/q4_oracle.c), OpenMP over all host threads"},
+                         "sample": cpu_sample_text(steps, warm, r["start"]), **host_cpu()},
         "e2e": {"value": round(r["value"], 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -236,8 +289,10 @@ def run_reference(args, ws, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def batch1_secondary(device: int, steps: int) -> dict:
-    """Config 3 on the persistent kernel: batch 1, prompt 128, positions 128..255."""
+def batch1_secondary(device: int, steps: int, cm=None) -> dict:
+    """Config 3 on the persistent kernel: batch 1, prompt 128, positions 128..255;
+    with `cm` (a C-oracle model) every generated token and score of the run is
+    compared with a serial oracle decode of the same prompt."""
     import torch
 
     from llm_accelerator_b200.model import Q4Model
@@ -259,6 +314,7 @@ def batch1_secondary(device: int, steps: int) -> dict:
     e1.record(stream)
     e1.synchronize()
     ms = e0.elapsed_time(e1)
+    toks, scores, _ = m.read_tokens(B1_PROMPT, steps + 1, slot=slot)
     n_e2e = 32
     tok, pos = first, B1_PROMPT
     t0 = time.perf_counter()
@@ -268,17 +324,63 @@ def batch1_secondary(device: int, steps: int) -> dict:
     e2e_s = time.perf_counter() - t0
     mode = m.mode
     m.close()
-    return {"workload": "cfg3: batch 1, prompt 128 uniform ids, decode positions 128..255",
-            "value": round(steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
-            "steps": steps, "mode": "persistent cooperative kernel" if mode == 1 else "per-stage CUDA graphs",
-            "e2e": {"value": round(n_e2e / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
-                    "d2h_bytes_per_step": 12, "api": "q4gpu_run_token (qot_session_runner_fn)"}}
+    out = {"workload": "cfg3: batch 1, prompt 128 uniform ids, decode positions 128..255",
+           "value": round(steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
+           "steps": steps, "mode": "persistent cooperative kernel" if mode == 1 else "per-stage CUDA graphs",
+           "e2e": {"value": round(n_e2e / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 8,
+                   "d2h_bytes_per_step": 12, "api": "q4gpu_run_token (qot_session_runner_fn)"}}
+    if cm is not None:
+        want, want_scores = cm.decode(prompt, steps + 1)
+        same = toks.tolist() == want and scores.tolist() == want_scores
+        out["parity"] = (f"identical: all {steps + 1} generated tokens and Q26 scores equal a serial C-oracle decode"
+                         if same else f"MISMATCH gpu={toks.tolist()[:8]} oracle={want[:8]}")
+    return out
 
 
-def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16) -> dict:
+def cfg2_secondary(device: int, peak_gbs: float) -> dict:
+    """Config 2: one decoder layer at batch 1, single decode step at position 512
+    (context 513) with the KV cache pre-filled with seeded N(0, 1) Q12.12 values.
+    The model has 28 distinct layers, so every layer's 8.4 MB of Q4 weights and
+    4.2 MB of K/V come from HBM (234 MB + 117 MB per step, above L2); the layer
+    time is the sum of its five kernels' mean device times (per-kernel events)."""
+    from llm_accelerator_b200.model import Q4Model
+
+    ctx = 513
+    m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=ctx + 7, max_seqs=1, device=device)
+    m.init_synthetic(seed=0)
+    rng = np.random.default_rng(2)
+    for layer in range(LAYERS):
+        for kind in (0, 1):
+            kv = np.clip(np.rint(rng.standard_normal((ctx - 1, 8, 128)) * 4096), -(1 << 23), (1 << 23) - 1)
+            m.write_kv(layer, kind, kv.astype(np.int32))
+    h = np.clip(np.rint(rng.standard_normal(1024) * 1024), -(1 << 23), (1 << 23) - 1).astype(np.int32)
+    m.write_hidden(h)
+    reps = 5
+    tot = {}
+    for _ in range(reps):
+        m.set_position(ctx - 1)
+        for k, (ms, n) in m.time_kernels(reps=1).items():
+            tot.setdefault(k, []).append((ms, n))
+    m.close()
+    layer_kinds = ("qkv_norm_rope_kv", "attention", "o_proj_residual", "post_norm_gate_up_swiglu", "down_residual")
+    per = {k: float(np.median([x[0] for x in v])) for k, v in tot.items()}
+    us = 1000.0 * sum(per[k] for k in layer_kinds if k in per)
+    layer_bytes = 8_355_840 + 4_194_304 + 24_576  # Q4 weights + K/V read + activations / K/V write
+    gbs = layer_bytes / (us * 1e-6) / 1e9
+    return {"workload": "cfg2: one Qwen3-0.6B layer, batch 1, decode step at position 512 (context 513), KV "
+                        "pre-filled with seeded N(0,1) Q12.12, per-stage decode kernels",
+            "us_per_layer": round(us, 2), "kernels_us": {k: round(1000.0 * per[k], 2) for k in layer_kinds if k in per},
+            "bytes_per_layer": layer_bytes, "gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4),
+            "peak": peak_gbs}
+
+
+def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16, check: bool = True) -> dict:
     """Config 5 on one GPU: 8 sequences with 8192-token prompts (batched exact
     prefill), greedy decode from position 8192; the attention kernel's K/V bytes
-    against HBM at that context."""
+    against HBM at that context.  With `check`, sequence 0's cache is loaded into
+    the C oracle and sampled positions (prompt positions, the last prompt
+    position and the timed decode steps) are re-run there: K/V rows, tokens and
+    scores must be identical."""
     import torch
 
     from llm_accelerator_b200.model import Q4Model
@@ -286,7 +388,7 @@ def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16) -> dict:
     m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=CFG5_PROMPT + CFG5_GEN, max_seqs=CFG5_SEQS, device=device)
     m.init_synthetic(seed=0)
     prompts = [np.random.default_rng(50_000 + i).integers(0, VOCAB, CFG5_PROMPT).tolist() for i in range(CFG5_SEQS)]
-    m.decode_batch([prompts[0][:2]], 1)  # int8 copies and prefill buffers
+    m.decode_batch([prompts[0][:2]], 1)  # batched-path buffers and prefill buffers
     t0 = time.perf_counter()
     m.decode_batch(prompts, 1)
     prefill_s = time.perf_counter() - t0
@@ -303,17 +405,36 @@ def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16) -> dict:
     toks = m.read_tokens(CFG5_PROMPT, 4, slot=0)[0].tolist()
     kt = m.batch_time_kernels(CFG5_SEQS, reps=2)
     ctx = CFG5_PROMPT + steps + 2
+    parity = None
+    if check:
+        from oracle.c_oracle import CModel
+        from oracle.long_context import sampled_parity
+        m.batch_set_position(CFG5_PROMPT, CFG5_SEQS)  # re-run the timed steps: the ring ends at 8192 + steps
+        m.batch_steps(steps, CFG5_SEQS)
+        m.sync()
+        n_cached = CFG5_PROMPT + steps
+        sample = [0, 1023, 1024, 4096, CFG5_PROMPT - 2, CFG5_PROMPT - 1, CFG5_PROMPT, CFG5_PROMPT + 1,
+                  n_cached - 1]
+        cm = CModel(LAYERS, VOCAB, CFG5_PROMPT + CFG5_GEN, seed=0)
+        bad = sampled_parity(cm, m, 0, sample, n_cached=n_cached, logits_from=CFG5_PROMPT - 1)
+        cm.close()
+        parity = (f"identical: sequence 0 re-run by the C oracle on the GPU's cache at positions {sample}: K/V rows "
+                  "of all 28 layers, and tokens and Q26 scores from the last prompt position on"
+                  if not bad else f"MISMATCH {bad[:4]}")
     m.close()
     att_ms = kt["attention"][0]
     gbs = batch_kernel_bytes("attention", CFG5_SEQS, ctx) / (att_ms * 1e-3) / 1e9
-    return {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (seeds 50000..), batched exact prefill, "
-                        "greedy decode from position 8192, full vocabulary on one GPU",
-            "value": round(CFG5_SEQS * steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
-            "steps": steps, "prefill_s": round(prefill_s, 3),
-            "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
-            "attention": {"kernel": "batch_attn_cl_kernel (8-CTA clusters)", "ms_per_launch": round(att_ms, 5),
-                          "context": ctx, "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)},
-            "first_tokens_seq0": toks}
+    out = {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (seeds 50000..), batched exact prefill, "
+                       "greedy decode from position 8192, full vocabulary on one GPU",
+           "value": round(CFG5_SEQS * steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
+           "steps": steps, "prefill_s": round(prefill_s, 3),
+           "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
+           "attention": {"kernel": "batch_attn_cl_kernel (8-CTA clusters)", "ms_per_launch": round(att_ms, 5),
+                         "context": ctx, "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)},
+           "first_tokens_seq0": toks}
+    if parity is not None:
+        out["parity"] = parity
+    return out
 
 
 def gemv_secondary(device: int, peak_gbs: float) -> dict:
@@ -454,10 +575,19 @@ def run_ours(args, ws, rank, local):
             n -= k
         return resets
 
+    # one full pass over the cycle fills every sequence's token ring and cache
+    # for positions 256..510; the timed window (centred in the cycle) and its
+    # warm-up then replay positions whose tokens are known
     state = {"pos": PROMPT}
+    enqueue(CYCLE, state)
+    start = timed_window(steps)
+    positions = window_positions(start, steps)
+    ctx_mean = float(np.mean(positions)) + 1.0  # context of a step at position p is p + 1
+    m.batch_set_position(start, BATCH)
+    state["pos"] = start
     enqueue(warm, state)
-    m.batch_set_position(PROMPT, BATCH)
-    state["pos"] = PROMPT
+    m.batch_set_position(start, BATCH)
+    state["pos"] = start
     m.sync()
 
     sampler = ClockSampler(local)
@@ -479,10 +609,11 @@ def run_ours(args, ws, rank, local):
     toks0 = m.read_tokens(PROMPT, n_check + 1, slot=0)[0].tolist()
 
     # end to end through the public C ABI with host buffers: per step the host
-    # sends (token, position) of every sequence and reads back (token, score)
-    e2e_steps = min(steps, CYCLE)
-    tok = first.copy()
-    pos = np.full(BATCH, PROMPT, dtype=np.int64)
+    # sends (token, position) of every sequence and reads back (token, score),
+    # over the same window of positions
+    e2e_steps = min(steps, PROMPT + CYCLE - start)
+    tok = np.array([m.read_tokens(start, 1, slot=i)[0][0] for i in range(BATCH)], dtype=np.int64)
+    pos = np.full(BATCH, start, dtype=np.int64)
     barrier()
     t0 = time.perf_counter()
     for _ in range(e2e_steps):
@@ -491,20 +622,22 @@ def run_ours(args, ws, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     e2e = ws * BATCH * e2e_steps / e2e_s
 
-    # per-kernel device times at the middle of the cycle (kernels serialised by events)
-    mid = PROMPT + CYCLE // 2
+    # per-kernel device times (kernels serialised by events) at the timed
+    # window's mean context: `reps` steps from position mid run at contexts
+    # mid + 1 .. mid + reps
+    reps = 3
+    mid = int(round(ctx_mean - (reps + 1) / 2.0))
     m.batch_set_position(mid, BATCH)
     m.sync()
-    reps = 3
     kt = m.batch_time_kernels(BATCH, reps=reps)
-    ctx_mean = mid + (reps + 1) / 2.0
+    kt_ctx = mid + (reps + 1) / 2.0
     share = {k: v[0] * v[1] for k, v in kt.items()}
     tot = sum(share.values())
     dom = max(share, key=share.get)
     peaks = measured_peaks()
 
     def gbs(kind: str) -> float:
-        return batch_kernel_bytes(kind, BATCH, int(round(ctx_mean))) / (kt[kind][0] * 1e-3) / 1e9
+        return batch_kernel_bytes(kind, BATCH, int(round(kt_ctx))) / (kt[kind][0] * 1e-3) / 1e9
 
     launches_per_step = sum(v[1] for v in kt.values())
 
@@ -514,17 +647,18 @@ def run_ours(args, ws, rank, local):
             "warmup": warm, "ms_per_step": round(ms_max / steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
             "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "prompt": PROMPT, "generate": GEN,
-                       "max_context": MAX_CTX,
+                       "max_context": MAX_CTX, "timed_positions": [positions[0], positions[-1]],
+                       "ctx_mean": round(ctx_mean, 2),
                        "parallelism": f"independent sequences, {BATCH} per GPU x{ws}" if ws > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (420 MB int8 weights + ~5.6 GB KV cache per step)"},
+                       "l2": "inputs larger than L2 (317 MB Q4 weights + ~5.6 GB KV cache per step)"},
             "e2e": {"value": round(e2e, 2), "unit": UNIT, "h2d_bytes_per_step": BATCH * 8,
                     "d2h_bytes_per_step": BATCH * 16,
                     "api": "q4gpu_batch_run_step: host (token, position) in, host (token, score) out, every step"},
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(gbs(dom), 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs(dom) / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"], "traffic": profiled_traffic(dom),
-                         "bytes_per_launch": batch_kernel_bytes(dom, BATCH, int(round(ctx_mean))),
-                         "ms_per_launch": round(kt[dom][0], 5), "context": round(ctx_mean, 1)},
+                         "bytes_per_launch": batch_kernel_bytes(dom, BATCH, int(round(kt_ctx))),
+                         "ms_per_launch": round(kt[dom][0], 5), "context": round(kt_ctx, 1)},
             "kernels": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
                             "share": round(share[k] / tot, 4), "gbs": round(gbs(k), 1)} for k, v in kt.items()},
             "prefill_s": round(prefill_s, 3),
@@ -536,22 +670,25 @@ def run_ours(args, ws, rank, local):
             "gpu_launches": launches_per_step * steps + resets,
             "clocks": clocks,
         }
+    m.close()
+    if rank == 0:
         if ws == 1:
-            line["batch1"] = batch1_secondary(local, 128)
+            from oracle import c_oracle as CO
+            cm = None if args.no_cpu_baseline else CO.CModel(LAYERS, VOCAB, MAX_CTX, seed=0)
+            line["batch1"] = batch1_secondary(local, 128, cm)
+            line["cfg2"] = cfg2_secondary(local, peaks["hbm_gbs"])
             line["gemv"] = gemv_secondary(local, peaks["hbm_gbs"])
-            line["cfg5"] = cfg5_secondary(local, peaks["hbm_gbs"])
-            if not args.no_cpu_baseline:
-                c = cpu_decode(args.cpu_steps, 2)
+            line["cfg5"] = cfg5_secondary(local, peaks["hbm_gbs"], check=not args.no_cpu_baseline)
+            if cm is not None:
+                c = cpu_decode(args.cpu_steps, 2, cm=cm)
+                cm.close()
                 line["cpu_baseline"] = {
                     "value": round(c["value"], 3), "unit": UNIT, "cores": c["cores"], "kind": "port",
-                    "sample": f"sequence 0: {args.cpu_steps} decode steps at positions 258.. after its serial "
-                              "256-token prefill, C restatement of the reference's Python Q4 path "
-                              "(oracle/q4_oracle.c), all host threads"}
+                    "sample": cpu_sample_text(args.cpu_steps, 2, c["start"]), **host_cpu()}
                 n = min(len(c["tokens"]), len(toks0))
                 line["parity"] = "sequence 0 tokens identical to the CPU oracle" if c["tokens"][:n] == toks0[:n] \
                     else f"MISMATCH gpu={toks0[:n]} cpu={c['tokens'][:n]}"
         print(json.dumps(line), flush=True)
-    m.close()
     if dist is not None:
         barrier()
         dist.destroy_process_group()

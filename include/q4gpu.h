@@ -149,7 +149,10 @@ int q4gpu_embedding(const int32_t *tokens, int32_t n_tokens, const uint8_t *pack
  * strict '>' in ascending row order, lowest index wins ties.
  * act: int32 [1024] Q12.12 (already final-normed).  logits (optional): int64 [rows].
  * workspace: device scratch of q4gpu_lm_head_workspace_bytes(rows) bytes.
- * out_token (int32) / out_score (int64) are device pointers. */
+ * out_token (int32) / out_score (int64) are device pointers.
+ * Returns Q4GPU_OK, Q4GPU_ERR_ARG / _WORKSPACE / _ALIGN (activation, packed and
+ * workspace 16-byte aligned, scales 2-byte aligned) before any device work, or
+ * the launch's error; q4gpu_last_error() holds the message. */
 size_t q4gpu_lm_head_workspace_bytes(int32_t rows);
 int q4gpu_lm_head_argmax(const int32_t *act, const uint8_t *packed, const uint16_t *scale,
                          int32_t rows, int64_t *logits, void *workspace, size_t workspace_bytes,
@@ -167,9 +170,13 @@ int q4gpu_lm_head_argmax(const int32_t *act, const uint8_t *packed, const uint16
  * device pointers, as above).
  * - rows must be 1..Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS; anything else returns
  *   Q4GPU_ERR_ARG before any device work.
- * - The first call on a device looks up the scratch's device address with that
- *   device current (cudaGetSymbolAddress); make that first call before any
- *   stream capture.
+ * - The scratch exists once per CUDA context.  The first call in a context
+ *   (a device's primary context, or the caller's own driver-API context made
+ *   current) looks up its address there (cudaGetSymbolAddress) and caches it
+ *   under the context's unique id; make that first call before any stream
+ *   capture.
+ * - Errors are reported as by q4gpu_lm_head_argmax (same codes, message in
+ *   q4gpu_last_error), so the two entry points can replace each other.
  * - Every call on a device shares the one scratch array and it keeps the last
  *   call's contents (the completion counter is cleared on each call): calls
  *   that overlap on the GPU race with each other and must be serialised by

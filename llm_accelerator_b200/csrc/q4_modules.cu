@@ -6,6 +6,8 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "q4_gemv.cuh"
 #include "q4gpu_internal.h"
@@ -1306,13 +1308,20 @@ size_t q4gpu_lm_head_workspace_bytes(int32_t rows) {
 int q4gpu_lm_head_argmax(const int32_t* act, const uint8_t* packed, const uint16_t* scale, int32_t rows,
                          int64_t* logits, void* workspace, size_t workspace_bytes, int32_t* out_token,
                          int64_t* out_score, void* stream) {
-  if (!act || !packed || !scale || rows <= 0 || !workspace || !out_token || !out_score) return Q4GPU_ERR_ARG;
-  if (workspace_bytes < q4gpu_lm_head_workspace_bytes(rows)) return Q4GPU_ERR_WORKSPACE;
-  if ((((uintptr_t)packed) & 15) || (((uintptr_t)workspace) & 15) || (((uintptr_t)act) & 15)) return Q4GPU_ERR_ALIGN;
+  if (!act || !packed || !scale || !workspace || !out_token || !out_score)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "null argument");
+  if (rows <= 0) return q4gpu_fail(Q4GPU_ERR_ARG, "rows %d must be positive", rows);
+  if (workspace_bytes < q4gpu_lm_head_workspace_bytes(rows))
+    return q4gpu_fail(Q4GPU_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", workspace_bytes,
+                      q4gpu_lm_head_workspace_bytes(rows));
+  if ((((uintptr_t)packed) & 15) || (((uintptr_t)workspace) & 15) || (((uintptr_t)act) & 15))
+    return q4gpu_fail(Q4GPU_ERR_ALIGN, "activation, packed weights and workspace must be 16-byte aligned");
+  if (((uintptr_t)scale) & 1) return q4gpu_fail(Q4GPU_ERR_ALIGN, "scales must be 2-byte aligned");
   ArgBest* partial = reinterpret_cast<ArgBest*>(workspace);
   unsigned int* counter =
       reinterpret_cast<unsigned int*>(reinterpret_cast<char*>(workspace) + Q4GPU_LM_HEAD_BLOCKS * sizeof(ArgBest));
-  cudaMemsetAsync(counter, 0, sizeof(unsigned int), as_stream(stream));
+  const cudaError_t ce = cudaMemsetAsync(counter, 0, sizeof(unsigned int), as_stream(stream));
+  if (ce != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "workspace clear: %s", cudaGetErrorString(ce));
   GemvArgs g{};
   g.act = act;
   g.W = packed;
@@ -1324,28 +1333,60 @@ int q4gpu_lm_head_argmax(const int32_t* act, const uint8_t* packed, const uint16
   g.counter = counter;
   g.out_tok = out_token;
   g.out_score = out_score;
-  return gv_dispatch<1>(kHidden, g, gv_grid_cap(kHidden), as_stream(stream)) == Q4GPU_OK ? Q4GPU_OK : Q4GPU_ERR_CUDA;
+  return gv_dispatch<1>(kHidden, g, gv_grid_cap(kHidden), as_stream(stream));
 }
 
-// Device address of g_lm_head_static_scratch, looked up once per device (with
-// that device current) on the first no-alloc call there.  In host code the
-// symbol itself is only a host-side stand-in; kernels get this address.
+// Device address of g_lm_head_static_scratch in the calling thread's current
+// CUDA context.  A __device__ symbol exists once per context (the primary
+// context of a device, or a caller's own driver-API context), so the address
+// is looked up with cudaGetSymbolAddress, with that context current, the first
+// time each context calls, and cached under the context's unique id
+// (cuCtxGetId: ids are never reused, so a reset device or a destroyed and
+// re-created context gets a fresh lookup).  In host code the symbol itself is
+// only a host-side stand-in; kernels get this address.
 static int lm_head_static_scratch(q4::LmHeadStaticScratch** out) {
   static std::mutex mu;
-  static q4::LmHeadStaticScratch* addr[Q4GPU_MAX_DEVICES] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= Q4GPU_MAX_DEVICES) return q4gpu_fail(Q4GPU_ERR_ARG, "device ordinal %d too large", dev);
+  static std::vector<std::pair<unsigned long long, void*>> by_ctx;
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, q4::g_lm_head_static_scratch);
+  if (!get_current || !get_id) {
+    cudaDriverEntryPointQueryResult q1, q2;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", reinterpret_cast<void**>(&get_current), cudaEnableDefault, &q1) !=
+            cudaSuccess ||
+        q1 != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPoint("cuCtxGetId", reinterpret_cast<void**>(&get_id), cudaEnableDefault, &q2) !=
+            cudaSuccess ||
+        q2 != cudaDriverEntryPointSuccess) {
+      get_current = nullptr;
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId unavailable");
+    }
+  }
+  void* p = nullptr;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuCtxGetCurrent failed");
+  if (!ctx) {
+    // no context current yet on this thread: the runtime call makes the
+    // device's primary context current
+    const cudaError_t e = cudaGetSymbolAddress(&p, q4::g_lm_head_static_scratch);
     if (e != cudaSuccess)
       return q4gpu_fail(Q4GPU_ERR_CUDA, "cudaGetSymbolAddress(lm-head scratch): %s", cudaGetErrorString(e));
-    addr[dev] = static_cast<q4::LmHeadStaticScratch*>(p);
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx) return q4gpu_fail(Q4GPU_ERR_CUDA, "no current CUDA context");
   }
-  *out = addr[dev];
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuCtxGetId failed");
+  for (const auto& e : by_ctx)
+    if (e.first == id) {
+      *out = static_cast<q4::LmHeadStaticScratch*>(e.second);
+      return Q4GPU_OK;
+    }
+  if (!p) {
+    const cudaError_t e = cudaGetSymbolAddress(&p, q4::g_lm_head_static_scratch);
+    if (e != cudaSuccess)
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cudaGetSymbolAddress(lm-head scratch): %s", cudaGetErrorString(e));
+  }
+  by_ctx.emplace_back(id, p);
+  *out = static_cast<q4::LmHeadStaticScratch*>(p);
   return Q4GPU_OK;
 }
 
@@ -1357,6 +1398,7 @@ int q4gpu_lm_head_argmax_noalloc(const int32_t* act, const uint8_t* packed, cons
                       Q4GPU_LM_HEAD_NOALLOC_MAX_ROWS);
   if ((((uintptr_t)packed) & 15) || (((uintptr_t)act) & 15))
     return q4gpu_fail(Q4GPU_ERR_ALIGN, "activation and packed weights must be 16-byte aligned");
+  if (((uintptr_t)scale) & 1) return q4gpu_fail(Q4GPU_ERR_ALIGN, "scales must be 2-byte aligned");
   q4::LmHeadStaticScratch* sc = nullptr;
   int rc = lm_head_static_scratch(&sc);
   if (rc) return rc;

@@ -322,11 +322,13 @@ class Q4Model:
         h = np.ascontiguousarray(np.asarray(hidden, dtype=np.int32))
         _native.check(self.lib.q4gpu_model_write_hidden(self.handle, slot, _ptr(h)), "q4gpu_model_write_hidden")
 
-    def read_kv(self, layer: int, kind: int, positions: int, slot: int = 0) -> np.ndarray:
+    def read_kv(self, layer: int, kind: int, positions: int, slot: int = 0, raw: bool = False) -> np.ndarray:
+        """K (kind 0) or V (kind 1) rows [positions, 8, 128] of a layer in the reference's
+        order; int64 like the reference's arrays, or the stored int32 words with raw=True."""
         out = np.empty((positions, 8, 128), dtype=np.int32)
         _native.check(self.lib.q4gpu_model_read_kv(self.handle, slot, layer, kind, positions, _ptr(out)),
                       "q4gpu_model_read_kv")
-        return out.astype(np.int64)
+        return out if raw else out.astype(np.int64)
 
     def write_kv(self, layer: int, kind: int, data, slot: int = 0) -> None:
         d = np.ascontiguousarray(np.asarray(data, dtype=np.int32))

@@ -2,6 +2,9 @@
 
     python -m oracle.build_ref [--reference <reference root>]
 
+The reference root comes from --reference, else $Q4_REFERENCE_ROOT, else a
+`reference` checkout beside this repository.
+
 `session_seam`: the reference's own session state machine
 (FPGA_Project/software/qmap_prompt_demo/qot_session.c), compiled with gcc from
 the reference sources where they lie, linked with oracle/session_seam_main.c
@@ -23,7 +26,14 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent
 OUT = HERE / "_ref"
 LIB_DIR = REPO / "llm_accelerator_b200" / "_lib"
-DEFAULT_REF = Path(os.environ.get("Q4_REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_root() -> Path | None:
+    """The reference checkout: $Q4_REFERENCE_ROOT, else a `reference` directory
+    beside this repository's; None when neither exists."""
+    env = os.environ.get("Q4_REFERENCE_ROOT")
+    cand = Path(env) if env else REPO.parent / "reference"
+    return cand if cand.is_dir() else None
 
 
 def build_session_seam(ref: Path) -> Path | None:
@@ -46,9 +56,10 @@ def build_session_seam(ref: Path) -> Path | None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=DEFAULT_REF)
+    ap.add_argument("--reference", type=Path, default=None)
     a = ap.parse_args()
-    exe = build_session_seam(a.reference)
+    ref = a.reference or reference_root()
+    exe = build_session_seam(ref) if ref else None
     print(exe if exe else "reference sources or libq4gpu.so missing: nothing built", file=sys.stderr)
 
 

@@ -33,6 +33,8 @@ def lib() -> C.CDLL:
             "orc_run_token": (C.c_int, [P, C.c_int, C.c_int, C.c_int, P, P]),
             "orc_decode": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
             "orc_read_hidden": (None, [P, P]),
+            "orc_set_kv": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.c_int, P]),
+            "orc_get_kv": (C.c_int, [P, C.c_int, C.c_int, C.c_int, C.c_int, P]),
             "orc_set_threads": (C.c_int, [C.c_int]),
         }
         for n, (r, a) in sig.items():
@@ -115,6 +117,18 @@ class CModel:
         h = np.ascontiguousarray(hidden, dtype=np.int32).copy()
         self.L.orc_layer_step(self.h, layer, pos, _p(h))
         return h.astype(np.int64)
+
+    def set_kv(self, layer: int, kind: int, pos0: int, rows) -> None:
+        """Load K (kind 0) or V (kind 1) rows [n, 8, 128] at positions pos0.. of a layer."""
+        r = np.ascontiguousarray(rows, dtype=np.int32)
+        if self.L.orc_set_kv(self.h, layer, kind, pos0, r.shape[0], _p(r)):
+            raise ValueError("K/V rows out of range")
+
+    def get_kv(self, layer: int, kind: int, pos0: int, n: int) -> np.ndarray:
+        out = np.empty((n, 8, 128), dtype=np.int32)
+        if self.L.orc_get_kv(self.h, layer, kind, pos0, n, _p(out)):
+            raise ValueError("K/V rows out of range")
+        return out
 
     def decode(self, prompt, max_new: int) -> tuple[list, list]:
         p = np.ascontiguousarray(prompt, dtype=np.int32)

@@ -418,6 +418,26 @@ int orc_decode(orc_model *m, const int32_t *prompt, int n_prompt, int max_new, i
 
 void orc_read_hidden(const orc_model *m, int32_t *out) { memcpy(out, m->hidden, sizeof(m->hidden)); }
 
+/* K (kind 0) or V (kind 1) cache rows of one layer, positions [pos0, pos0 + n),
+ * each [8 heads][128] Q12.12 as the decode path stores them.  Loading a
+ * cache lets a check re-run single positions teacher-forced on top of a
+ * cache some other implementation built (the long-prompt parity checks). */
+int orc_set_kv(orc_model *m, int layer, int kind, int pos0, int n, const int32_t *rows) {
+  if (layer < 0 || layer >= m->n_layers || kind < 0 || kind > 1 || pos0 < 0 || n < 0 || pos0 + n > m->max_ctx)
+    return -1;
+  int32_t *c = (kind ? m->v_cache : m->k_cache) + ((size_t)layer * m->max_ctx + pos0) * KVROWS;
+  memcpy(c, rows, (size_t)n * KVROWS * sizeof(int32_t));
+  return 0;
+}
+
+int orc_get_kv(const orc_model *m, int layer, int kind, int pos0, int n, int32_t *rows) {
+  if (layer < 0 || layer >= m->n_layers || kind < 0 || kind > 1 || pos0 < 0 || n < 0 || pos0 + n > m->max_ctx)
+    return -1;
+  const int32_t *c = (kind ? m->v_cache : m->k_cache) + ((size_t)layer * m->max_ctx + pos0) * KVROWS;
+  memcpy(rows, c, (size_t)n * KVROWS * sizeof(int32_t));
+  return 0;
+}
+
 int orc_set_threads(int n) {
 #ifdef _OPENMP
   if (n > 0) omp_set_num_threads(n);

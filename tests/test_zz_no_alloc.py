@@ -29,14 +29,15 @@ def _case_inputs(act, packed, scale):
     return a, w, s
 
 
-def _with_workspace(lib, a, w, s, rows, stream):
+def _with_workspace(lib, a, w, s, rows, stream, scale_ptr=None, want_logits=True):
     ws_bytes = lib.q4gpu_lm_head_workspace_bytes(rows)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
-    logits = torch.empty(rows, dtype=torch.int64, device="cuda")
+    logits = torch.empty(rows, dtype=torch.int64, device="cuda") if want_logits else None
     tok = torch.empty(1, dtype=torch.int32, device="cuda")
     score = torch.empty(1, dtype=torch.int64, device="cuda")
-    rc = lib.q4gpu_lm_head_argmax(a.data_ptr(), w.data_ptr(), s.data_ptr(), rows, logits.data_ptr(), ws.data_ptr(),
-                                  ws_bytes, tok.data_ptr(), score.data_ptr(), stream)
+    rc = lib.q4gpu_lm_head_argmax(a.data_ptr(), w.data_ptr(), s.data_ptr() if scale_ptr is None else scale_ptr, rows,
+                                  logits.data_ptr() if want_logits else None, ws.data_ptr(), ws_bytes,
+                                  tok.data_ptr(), score.data_ptr(), stream)
     assert rc == 0, lib.q4gpu_last_error()
     return logits, tok, score
 
@@ -72,6 +73,36 @@ def test_noalloc_matches_workspace_entry_two_calls(kat):
         assert int(tok.item()) == int(ref_tok.item()) and int(score.item()) == int(ref_score.item())
     # the reference's own scan window result for the first case
     assert (int(outs[0][1].item()), int(outs[0][2].item())) == (264, 1365150750)
+
+
+def test_noalloc_unaligned_scales_without_logits():
+    """Scales that start 2 bytes past a 16-byte boundary take the library's
+    CUDA-core GEMV kernel instead of the tensor-core one; it writes the same
+    static scratch.  No logits are requested.  Two calls in a row, each checked
+    against the workspace entry point on the same pointers."""
+    lib = _native.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    rng = np.random.default_rng(77)
+    for rows in (4099, 1536):
+        act = rng.integers(-(1 << 23), 1 << 23, 1024)
+        packed = rng.integers(0, 256, (rows, 512)).astype(np.uint8)
+        scale = rng.integers(0, 1 << 16, rows * 16 + 1).astype(np.uint16)  # one spare u16 in front
+        a, w, s = _case_inputs(act, packed, scale)
+        sp = s.data_ptr() + 2
+        assert sp % 16 == 2
+        tok = torch.empty(1, dtype=torch.int32, device="cuda")
+        score = torch.empty(1, dtype=torch.int64, device="cuda")
+        rc = lib.q4gpu_lm_head_argmax_noalloc(a.data_ptr(), w.data_ptr(), sp, rows, None, tok.data_ptr(),
+                                              score.data_ptr(), stream)
+        assert rc == 0, lib.q4gpu_last_error()
+        _, ref_tok, ref_score = _with_workspace(lib, a, w, s, rows, stream, scale_ptr=sp, want_logits=False)
+        torch.cuda.synchronize()
+        assert (int(tok.item()), int(score.item())) == (int(ref_tok.item()), int(ref_score.item()))
+        # and the tensor-core path on the aligned copy of the same scales agrees
+        s2 = torch.from_numpy(scale[1:].copy().view(np.int16)).cuda()
+        _, al_tok, al_score = _with_workspace(lib, a, w, s2, rows, stream, want_logits=False)
+        torch.cuda.synchronize()
+        assert (int(al_tok.item()), int(al_score.item())) == (int(tok.item()), int(score.item()))
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
