@@ -2,17 +2,17 @@
 // per step together, sharing every weight read.
 //
 // GEMMs run on the tensor cores (tcgen05.mma, kind::i8) with exact integer
-// arithmetic.  Weights are expanded once to int8 (row-major [rows, K]).  Each
-// sequence's activation a (signed 24-bit) is fed as the three unsigned byte
-// limbs of a + 2^23, and eight B rows of ones yield sum(w) per row and
-// 64-group, so that per scale group
-//     sum(w * a) = P0 + 256 P1 + 65536 P2 - 2^23 W1
-// with every Pj an exact int32 tensor-core sum (|Pj| < 2^17).
+// arithmetic, reading the Q4 weights as the model stores them: the group
+// scales are split into 4-bit digits and each digit's weight plane (w * s_j,
+// a signed byte) is built in shared memory next to the MMA (see the GEMM
+// section below).  Each sequence's activation a (signed 24-bit) is fed as the
+// three unsigned byte limbs of a + 2^23.
 //
 // B ("limb") matrices are stored as Bt[n][k] u8 with n = limb * SP + m
-// (SP = padded sequence count) and n = 3 SP .. 3 SP + 7 the ones rows.
-// Producers write them directly: a norm kernel for the norm-fed GEMMs, the
-// attention epilogue for o_proj, the SwiGLU epilogue for down.
+// (SP = padded sequence count) and n = 3 SP .. 3 SP + 7 zero rows (the MMA's
+// N is 3 SP rounded up to 16).  Producers write them directly: a norm kernel
+// for the norm-fed GEMMs, the attention epilogue for o_proj, the SwiGLU
+// epilogue for down.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -67,34 +67,6 @@ __device__ __forceinline__ void write_limbs(uint8_t* bt, int SP, int K, int m, i
 // ---------------------------------------------------------------------------
 // Kernels
 // ---------------------------------------------------------------------------
-__global__ void expand_int4_kernel(const uint8_t* __restrict__ packed, int64_t n_bytes, int8_t* __restrict__ out) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_bytes; i += (int64_t)gridDim.x * blockDim.x) {
-    const uint8_t b = packed[i];
-    const int lo = b & 0xF, hi = b >> 4;
-    out[2 * i] = (int8_t)(lo >= 8 ? lo - 16 : lo);
-    out[2 * i + 1] = (int8_t)(hi >= 8 ? hi - 16 : hi);
-  }
-}
-
-// gate [3072, 1024] and up [3072, 1024] (packed, with scales) -> int8 [6144,
-// 1024] in 64-row blocks: out rows 128 b .. 128 b + 63 = gate rows 64 b ..,
-// out rows 128 b + 64 .. 128 b + 127 = up rows 64 b ..
-__global__ void expand_gu_kernel(const uint8_t* __restrict__ gate, const uint8_t* __restrict__ up,
-                                 const uint16_t* __restrict__ sg, const uint16_t* __restrict__ su,
-                                 int8_t* __restrict__ out, uint16_t* __restrict__ sout) {
-  constexpr int64_t kBytes = (int64_t)2 * kInter * (kHidden / 2);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < kBytes; i += (int64_t)gridDim.x * blockDim.x) {
-    const int r = (int)(i / (kHidden / 2)), col = (int)(i % (kHidden / 2));
-    const int src = 64 * (r / 128) + (r & 63);
-    const bool is_up = (r & 64) != 0;
-    const uint8_t b = (is_up ? up : gate)[(size_t)src * (kHidden / 2) + col];
-    const int lo = b & 0xF, hi = b >> 4;
-    out[2 * i] = (int8_t)(lo >= 8 ? lo - 16 : lo);
-    out[2 * i + 1] = (int8_t)(hi >= 8 ? hi - 16 : hi);
-    if (col < kHidden / kGroup) sout[(size_t)r * (kHidden / kGroup) + col] = (is_up ? su : sg)[(size_t)src * 16 + col];
-  }
-}
-
 // Per-sequence step inputs [S][2] = (token, position): store the token at its
 // position, set the position, and make the argmax land for every position.
 __global__ void batch_load_kernel(const SlotState* __restrict__ slots, int S, const int32_t* __restrict__ in,
@@ -698,126 +670,227 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
 }
 
 // ---------------------------------------------------------------------------
-// Exact batched GEMM on the 5th-generation tensor cores.
+// Exact batched GEMM on the 5th-generation tensor cores, reading the Q4
+// weights as stored (packed nibbles + u16 Q2.14 group scales).
 //
-// CTA tile: 128 weight rows x NB limb columns (NB = 3 SP + 8 rounded up to
-// 16), K streamed in 128-byte tiles (two 64-column scale groups) through a
-// 3-stage TMA ring.  Warp 0 issues the TMA loads, warp 1 owns TMEM and issues
-// tcgen05.mma (kind::i8, s8 x u8 -> s32), warps 2-17 are the epilogue.  Each
-// scale group accumulates into its own TMEM buffer (two, alternating), so the
-// MMAs of one group overlap the epilogue of the previous: the epilogue reads
-// the limb sums P0, P1, P2 and the weight sum W1 of (row, sequence) with
-// tcgen05.ld and folds them into an int64 accumulator exactly,
-//     sum(w a) s = (P0 + 256 P1) s + (2 P2 - 256 W1) (s << 15),
-// two 32 x 32 -> 64-bit multiply-adds per (row, sequence, group).
+//   out[r][m] = sum_k w[r][k] s[r][k / 64] a[m][k]     (exact, int64)
+//
+// with w the int4 weight, s its group scale and a the signed 24-bit
+// activation of sequence m.  The scale is split into 4-bit digits
+// s = sum_j 16^j s_j, so every w s_j lies in [-120, 105] and fits a signed
+// byte: "plane" j of the A operand holds w s_j for every weight.  The
+// activation enters as the three unsigned byte limbs c_i of c = a + 2^23
+// (the B limb matrix, rows limb * SP + m).  Then
+//   sum_k w s a = sum_{j,i} 16^j 256^i T[j][i] - 2^23 sum_k w s,
+//   T[j][i][r][m] = sum_k (w s_j)[r][k] c_i[m][k],
+// and each T is one int32 tensor-core accumulator over the CTA's whole K
+// range (|T| < 120 * 255 * K): TMEM is read once per tile, not once per
+// 64-column scale group.
+//
+// CTA tile: 128 weight rows x SN sequences (a chunk of the SP columns of the
+// limb matrix: MMA N = 3 SN rounded up to 16, zero rows past 3 SN), K in
+// 128-wide tiles.  Reading TMEM back runs at about 56 bytes per clock per SM,
+// so a CTA's accumulators (128 x 6 SN int32) and its share of a split-K
+// exchange are kept small by splitting the sequences over CTAs first and K
+// only where a matrix has few row tiles (o_proj, down).  Warp 0 issues the
+// TMA loads (packed weights into a 4-slot ring, the three limb boxes of the
+// chunk into a limb ring), warp 1 owns TMEM and issues tcgen05.mma (kind::i8,
+// s8 x u8 -> s32), and warps 2-17 first build the planes of each K tile in
+// shared memory, then read the accumulators and run the epilogue.
+// Building a plane: u = w + 8 (nibble ^ 8) times s_j plus 128 - 8 s_j in
+// each byte stays within [8, 233] (one IMAD per four weights, no carry
+// between bytes), and XOR 0x80 turns it into the signed byte w s_j; the bytes
+// go to the 128-byte-swizzled K-major layout the MMA descriptor expects.
+// One pass covers two digits (2p, 2p + 1, accumulators T[2p..2p+1] at TMEM
+// columns [0, N) and [N, 2N)); tiles whose scales all fit in 8 bits (the
+// usual case) need one pass, others a second with the loads repeated and the
+// accumulators read out in between.  The weight tiles and planes do not
+// depend on earlier kernels, so the first ones are loaded and built before
+// griddepcontrol.wait.
 // K may be split over the CTAs of a cluster (gridDim.y = splits <= 8); the
 // partial sums then meet in the owning CTA's shared memory over DSMEM.
 // ---------------------------------------------------------------------------
 enum GemmKind { kGemmQkv = 0, kGemmO = 1, kGemmGu = 2, kGemmDown = 3, kGemmLm = 4 };
 
 constexpr int kUThreads = 576;  // 18 warps
-constexpr int kUStages = 3;
+constexpr int kUMaxKt = 8;      // K tiles per CTA (K / splits <= 1024)
 
-template <int SP>
+template <int SN, int KIND>
 struct UCfg {
-  static constexpr int NB = (3 * SP + kBatchOnes + 15) / 16 * 16;
-  static constexpr int Q = SP / 4;  // sequences per epilogue thread
-  static constexpr int A_BYTES = 128 * 128;
-  static constexpr int B_BYTES = NB * 128;
-  static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int TCOLS = 2 * NB <= 32 ? 32 : 2 * NB <= 64 ? 64 : 2 * NB <= 128 ? 128 : 2 * NB <= 256 ? 256 : 512;
-  static constexpr int BUF = TCOLS / 2;  // TMEM columns of one accumulator buffer
-  static constexpr int RED_BYTES = 128 * SP * 8;
+  static constexpr int NM = (3 * SN + 15) / 16 * 16;  // MMA N: three limb blocks of SN columns
+  static constexpr int Q = SN / 4;                    // sequences per epilogue thread
+  static constexpr int A_PK = 128 * 64;               // packed weights of one 128-wide K tile
+  static constexpr int PLANE = 128 * 128;             // one plane of a K tile
+  static constexpr int B_BYTES = NM * 128;            // limb tile (3 boxes of SN rows + zero rows)
+  static constexpr int SA = 4;                        // packed-weight tiles in flight
+  static constexpr int SB = KIND == kGemmLm && SN == 64 ? 4 : SN == 64 ? 2 : 3;  // limb tiles in flight
+  static constexpr int SPL = 2;                       // plane pairs in flight
+  static constexpr int TCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128 : 2 * NM <= 256 ? 256 : 512;
+  // per-row partial sums [splits][SN][rows]; the LM head never splits K and
+  // keeps them in the plane slots, free once its MMAs are done
+  static constexpr bool RED_IN_PLANES = KIND == kGemmLm;
+  static constexpr int RED_BYTES = 128 * SN * 8;
   // operands of the final epilogue staged during the K loop: the residual
-  // rows a CTA owns (O / down, splits >= 2: at most 64 rows x SP) or the
+  // rows a CTA owns (O / down, splits >= 2: at most 64 rows x SN) or the
   // sigmoid table (gate/up)
-  static constexpr int STG_BYTES = 64 * SP * 4 > 4 * kSigLut ? 64 * SP * 4 : (4 * kSigLut + 15) / 16 * 16;
-  static constexpr size_t SMEM_BASE = 1024 + (size_t)kUStages * STAGE + RED_BYTES + 512;
-  static constexpr uint32_t IDESC = umma::i8_idesc(128, NB);
+  static constexpr int STG_BYTES = KIND == kGemmO || KIND == kGemmDown ? 64 * SN * 4
+                                   : KIND == kGemmGu                   ? (4 * kSigLut + 15) / 16 * 16
+                                                                       : 0;
+  static constexpr size_t OFF_B = (size_t)SPL * 2 * PLANE;
+  static constexpr size_t OFF_A = OFF_B + (size_t)SB * B_BYTES;
+  static constexpr size_t OFF_RED = RED_IN_PLANES ? 0 : OFF_A + (size_t)SA * A_PK;
+  static constexpr size_t OFF_RB = (RED_IN_PLANES ? OFF_A + (size_t)SA * A_PK : OFF_RED + RED_BYTES);
+  static constexpr size_t OFF_BAR = OFF_RB + 1024;  // barriers, TMEM slot, flags, live[64]
+  static constexpr size_t OFF_STG = OFF_BAR + 512;
+  static constexpr size_t SMEM = 1024 + OFF_STG + STG_BYTES;
+  static constexpr uint32_t IDESC = umma::i8_idesc(128, NM);
+  static_assert(2 * NM <= 512, "two accumulator sets must fit TMEM");
+  static_assert(B_BYTES % 1024 == 0 && SN % 8 == 0, "limb boxes stay on 1024-byte swizzle atoms");
+  static_assert(!RED_IN_PLANES || RED_BYTES <= OFF_B, "row sums fit the plane slots");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
 };
-// dynamic shared memory of a GEMM kind: O (1), gate/up (2) and down (3)
-// stage their final-epilogue operands
-template <int SP, int KIND>
-constexpr size_t gemm_smem() {
-  return UCfg<SP>::SMEM_BASE + (KIND == 1 || KIND == 2 || KIND == 3 ? UCfg<SP>::STG_BYTES : 0);
-}
 
 struct UGemm {
   BatchCtx c;
-  const uint16_t* scales;  // [rows, K / 64]
-  int rows;                // rows of A (the LM head's may end inside the last tile)
+  const uint16_t* scales;   // [rows, K / 64]; gate/up: the gate rows' scales
+  const uint16_t* scales2;  // gate/up: the up rows' scales ([3072, 16])
+  int rows;                 // rows of A (the LM head's may end inside the last tile)
   int K;
-  int kt_per_split;        // 128-wide K tiles each CTA of a cluster covers
+  int kt_per_split;         // 128-wide K tiles each CTA of a cluster covers (<= kUMaxKt)
+  int SP;                   // padded sequences of the limb matrix (its rows are limb * SP + m)
+  int chunks;               // sequence chunks of SN per sub-batch (SP / SN)
+  int b_sub_rows;           // limb-matrix rows between consecutive sub-batches (prefill)
   const int32_t* sig_lut;
-  ArgBestD* partial;       // LM head: [tiles, 64]
+  ArgBestD* partial;        // LM head: [tiles, 64]
   unsigned long long* trace;  // optional: [CTA][8] %globaltimer stamps of this launch (nullptr = off)
 };
 
 // GEMM timeline points: 0 entry, 1 set-up done, 2 dependency released (TMA
-// warp), 3 first accumulator ready, 4 last group folded, 5 partial sums
-// exchanged, 6 epilogue done, 7 last K tile landed (epilogue warp 2 records
-// 3-4, the MMA thread 7, thread 0 the rest)
+// warp), 3 accumulators ready, 4 accumulators read, 5 partial sums exchanged,
+// 6 epilogue done, 7 last K tile issued (epilogue warp 2 records 3-4, the MMA
+// thread 7, thread 0 the rest)
 __device__ __forceinline__ void gemm_stamp(const UGemm& g, int k) {
   if (g.trace) {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    g.trace[((size_t)blockIdx.y * gridDim.z + blockIdx.z) * 8 + k] = t;
+    g.trace[(((size_t)blockIdx.y * gridDim.z + blockIdx.z) * gridDim.x + blockIdx.x) * 8 + k] = t;
   }
 }
 
-template <int SP, int KIND>
+// 16 packed weights (8 bytes, k order) -> four words of biased weights
+// u = w + 8 in [0, 15], one per byte, U[t] holding k = 4t .. 4t + 3.
+__device__ __forceinline__ void unpack16_biased(uint2 x, uint32_t* U) {
+  const uint32_t l0 = (x.x ^ 0x88888888u) & 0x0F0F0F0Fu;         // k 0, 2, 4, 6
+  const uint32_t h0 = ((x.x >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;  // k 1, 3, 5, 7
+  const uint32_t l1 = (x.y ^ 0x88888888u) & 0x0F0F0F0Fu;
+  const uint32_t h1 = ((x.y >> 4) ^ 0x08080808u) & 0x0F0F0F0Fu;
+  U[0] = __byte_perm(l0, h0, 0x5140);
+  U[1] = __byte_perm(l0, h0, 0x7362);
+  U[2] = __byte_perm(l1, h1, 0x5140);
+  U[3] = __byte_perm(l1, h1, 0x7362);
+}
+
+// Signed bytes w * d (d a 4-bit scale digit) of four biased weights.
+__device__ __forceinline__ uint32_t plane_word(uint32_t u4, uint32_t d, uint32_t bias) {
+  return (u4 * d + bias) ^ 0x80808080u;
+}
+
+template <int SN, int KIND>
 __global__ void __launch_bounds__(kUThreads, 1)
-    umma_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap bmap, UGemm g) {
-  using C = UCfg<SP>;
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap amap2,
+                     const __grid_constant__ CUtensorMap bmap, UGemm g) {
+  using C = UCfg<SN, KIND>;
+  constexpr int SA = C::SA, SB = C::SB, SPL = C::SPL;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = umma::smem_addr(smem_raw);
   uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  int64_t* red = reinterpret_cast<int64_t*>(sm + kUStages * C::STAGE);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + kUStages * C::STAGE + C::RED_BYTES);
-  uint64_t* empty = full + kUStages;
-  uint64_t* tfull = empty + kUStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint8_t* planes = sm;
+  uint8_t* bstage = sm + C::OFF_B;
+  uint8_t* astage = sm + C::OFF_A;
+  int64_t* red = reinterpret_cast<int64_t*>(sm + C::OFF_RED);
+  int64_t* rbs = reinterpret_cast<int64_t*>(sm + C::OFF_RB);
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
+  uint64_t* empty_a = full_a + SA;
+  uint64_t* full_b = empty_a + SA;
+  uint64_t* empty_b = full_b + SB;
+  uint64_t* full_p = empty_b + SB;
+  uint64_t* empty_p = full_p + SPL;
+  uint64_t* tfull = empty_p + SPL;
+  uint64_t* tempty = tfull + 1;
+  uint64_t* scales_in = tempty + 1;  // the builders know whether a second pass is needed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(scales_in + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* live = reinterpret_cast<int*>(tmem_slot + 2);  // [64]: sequence m takes part in this step
-  int32_t* stg = reinterpret_cast<int32_t*>(sm + kUStages * C::STAGE + C::RED_BYTES + 512);
+  int* wide_any = reinterpret_cast<int*>(tmem_slot + 2);
+  int* live = reinterpret_cast<int*>(tmem_slot + 4);  // [64]: sequence m of the chunk takes part in this step
+  int32_t* stg = reinterpret_cast<int32_t*>(sm + C::OFF_STG);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // grid (sub-batches, K splits, row tiles): the sub-batches of one weight
-  // tile are adjacent in launch order and share its reads through L2
+  // grid (sub-batch x sequence chunk, K splits, row tiles): the CTAs of one
+  // weight tile are adjacent in launch order and share its reads through L2
   const int tile = blockIdx.z, split = blockIdx.y, splits = gridDim.y;
   const int nkt = g.kt_per_split, kt0 = split * nkt;
   const int row0 = tile * 128;
   const int G = g.K / 64;
-  // sub-batch z: columns SP z .. SP z + SP - 1 (B rows from NB z)
-  const int z = blockIdx.x;
+  const int SP = g.SP;
+  const int z = blockIdx.x / g.chunks, n0 = (blockIdx.x - z * g.chunks) * SN;
+  // this CTA's sequences: columns SP z + n0 .. + SN - 1 of the batch
   BatchCtx c = g.c;
-  if (z) {
-    const size_t m0 = (size_t)SP * z;
+  {
+    const size_t m0 = (size_t)SP * z + n0;
     c.qkv_raw += m0 * (kQRows + 2 * kKvRows);
     c.pos0 += 4 * m0;
     c.hidden0 += m0 * kHidden;
     c.post0 += m0 * kHidden;
     c.bt3 += z * c.bt_sub3;
+    const int rem = c.S - SP * z - n0;
+    c.S = rem < 0 ? 0 : (rem < SN ? rem : SN);
   }
-  c.S = c.S - SP * z < SP ? c.S - SP * z : SP;
+  // weight rows of this tile: 128 consecutive rows, or for gate/up 64 gate
+  // rows then the matching 64 up rows (amap2)
+  const int arow0 = KIND == kGemmGu ? tile * 64 : row0;
+  const int arow1 = KIND == kGemmGu ? tile * 64 : row0 + 64;
 
   if (threadIdx.x == 0) gemm_stamp(g, 0);
+  const int pre_a = nkt < SA ? nkt : SA;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kUStages; ++s) {
-      umma::bar_init(full + s, 1);
-      umma::bar_init(empty + s, 1);
+    for (int s = 0; s < SA; ++s) {
+      umma::bar_init(full_a + s, 1);
+      umma::bar_init(empty_a + s, 16);
     }
-    for (int h = 0; h < 2; ++h) {
-      umma::bar_init(tfull + h, 1);
-      umma::bar_init(tempty + h, 16);
+    for (int s = 0; s < SB; ++s) {
+      umma::bar_init(full_b + s, 1);
+      umma::bar_init(empty_b + s, 1);
     }
+    for (int s = 0; s < SPL; ++s) {
+      umma::bar_init(full_p + s, 16);
+      umma::bar_init(empty_p + s, 1);
+    }
+    umma::bar_init(tfull, 1);
+    umma::bar_init(tempty, 16);
+    umma::bar_init(scales_in, 16);
     *abort_flag = 0;
+    *wide_any = 0;
     umma::bar_init_fence();
     umma::prefetch_map(&amap);
     umma::prefetch_map(&bmap);
+    if (KIND == kGemmGu) umma::prefetch_map(&amap2);
+    // the weights do not depend on earlier kernels: their first tiles
+    // stream in while those finish
+    for (int kt = 0; kt < pre_a; ++kt) {
+      umma::bar_expect_tx(full_a + kt, C::A_PK);
+      umma::tma_load(astage + kt * C::A_PK, &amap, (kt0 + kt) * 64, arow0, full_a + kt);
+      umma::tma_load(astage + kt * C::A_PK + C::A_PK / 2, KIND == kGemmGu ? &amap2 : &amap, (kt0 + kt) * 64, arow1,
+                     full_a + kt);
+    }
   }
   if (warp == 1) umma::tmem_alloc(tmem_slot, C::TCOLS);
+  if constexpr (C::NM > 3 * SN) {
+    // limb-tile rows past the chunk's 3 SN are read by the MMA: zeros
+    constexpr int pad = (C::NM - 3 * SN) * 128 / 16;
+    for (int i = threadIdx.x; i < SB * pad; i += kUThreads)
+      *reinterpret_cast<uint4*>(bstage + (i / pad) * C::B_BYTES + 3 * SN * 128 + (i % pad) * 16) = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
@@ -830,29 +903,45 @@ __global__ void __launch_bounds__(kUThreads, 1)
     *abort_flag = 1;
     atomicExch(c.err, 3);
   };
+  // a second pass (scale digits 2 and 3) once the builders have seen every scale
+  auto passes = [&]() -> int {
+    if (!umma::bar_wait(scales_in, 0)) {
+      fail();
+      return 1;
+    }
+    return *reinterpret_cast<volatile int*>(wide_any) ? 2 : 1;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
-      // the weights do not depend on the previous kernel: their first tiles
-      // stream in while it finishes
-      const int pre = nkt < kUStages ? nkt : kUStages;
-      for (int kt = 0; kt < pre; ++kt) {
-        umma::bar_expect_tx(full + kt, C::STAGE);
-        umma::tma_load(sm + kt * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + kt);
-      }
       grid_dep_wait();
       gemm_stamp(g, 2);
-      for (int kt = 0; kt < pre; ++kt)
-        umma::tma_load(sm + kt * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, C::NB * z, full + kt);
-      for (int kt = pre; kt < nkt && !*abort_flag; ++kt) {
-        const int s = kt % kUStages;
-        if (!umma::bar_wait(empty + s, ((kt / kUStages) & 1) ^ 1)) {
+      int nv = nkt;
+      for (int v = 0; v < nv && !*abort_flag; ++v) {
+        if (v == nkt - 1) nv = passes() * nkt;
+        const int kt = v % nkt;
+        if (v >= pre_a) {
+          const int s = v % SA;
+          if (!umma::bar_wait(empty_a + s, ((v / SA) & 1) ^ 1)) {
+            fail();
+            break;
+          }
+          umma::bar_expect_tx(full_a + s, C::A_PK);
+          umma::tma_load(astage + s * C::A_PK, &amap, (kt0 + kt) * 64, arow0, full_a + s);
+          umma::tma_load(astage + s * C::A_PK + C::A_PK / 2, KIND == kGemmGu ? &amap2 : &amap, (kt0 + kt) * 64,
+                         arow1, full_a + s);
+        }
+        const int sb = v % SB;
+        if (!umma::bar_wait(empty_b + sb, ((v / SB) & 1) ^ 1)) {
           fail();
           break;
         }
-        umma::bar_expect_tx(full + s, C::STAGE);
-        umma::tma_load(sm + s * C::STAGE, &amap, (kt0 + kt) * 128, row0, full + s);
-        umma::tma_load(sm + s * C::STAGE + C::A_BYTES, &bmap, (kt0 + kt) * 128, C::NB * z, full + s);
+        umma::bar_expect_tx(full_b + sb, 3 * SN * 128);
+        uint8_t* bdst = bstage + sb * C::B_BYTES;
+        const int y0 = g.b_sub_rows * z + n0;
+#pragma unroll
+        for (int limb = 0; limb < 3; ++limb)
+          umma::tma_load(bdst + limb * SN * 128, &bmap, (kt0 + kt) * 128, y0 + limb * SP, full_b + sb);
       }
     } else {
       grid_dep_wait();
@@ -860,112 +949,226 @@ __global__ void __launch_bounds__(kUThreads, 1)
   } else if (warp == 1) {
     grid_dep_wait();
     if (lane == 0) {
-      for (int kt = 0; kt < nkt && !*abort_flag; ++kt) {
-        const int s = kt % kUStages;
-        if (!umma::bar_wait(full + s, (kt / kUStages) & 1)) {
+      int nv = nkt;
+      for (int v = 0; v < nv && !*abort_flag; ++v) {
+        const int pass = v / nkt, kt = v - pass * nkt;
+        if (pass == 1 && kt == 0 && !umma::bar_wait(tempty, 0)) {  // the first pass's accumulators are read
           fail();
           break;
         }
-        if (kt == nkt - 1) gemm_stamp(g, 7);
-        umma::fence_after_sync();
-        const uint32_t a0 = umma::smem_addr(sm + s * C::STAGE), b0 = a0 + C::A_BYTES;
-        for (int h = 0; h < 2; ++h) {
-          if (!umma::bar_wait(tempty + h, (kt & 1) ^ 1)) {
-            fail();
-            break;
-          }
-          umma::fence_after_sync();
-          const uint32_t d = tmem + (uint32_t)(h * C::BUF);
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint32_t off = (uint32_t)(64 * h + 32 * j);
-            umma::mma_i8(d, umma::sw128_desc(a0 + off), umma::sw128_desc(b0 + off), C::IDESC, (uint32_t)j);
-          }
-          umma::mma_commit(tfull + h);
+        const int sb = v % SB, sp = v % SPL;
+        if (!umma::bar_wait(full_b + sb, (v / SB) & 1) || !umma::bar_wait(full_p + sp, (v / SPL) & 1)) {
+          fail();
+          break;
         }
-        umma::mma_commit(empty + s);
+        umma::fence_after_sync();
+        const uint32_t a0 = umma::smem_addr(planes + sp * 2 * C::PLANE), b0 = umma::smem_addr(bstage + sb * C::B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (kt | kk) != 0;
+          umma::mma_i8(tmem, umma::sw128_desc(a0 + 32 * kk), umma::sw128_desc(b0 + 32 * kk), C::IDESC, acc);
+          umma::mma_i8(tmem + C::NM, umma::sw128_desc(a0 + C::PLANE + 32 * kk), umma::sw128_desc(b0 + 32 * kk),
+                       C::IDESC, acc);
+        }
+        umma::mma_commit(empty_p + sp);
+        umma::mma_commit(empty_b + sb);
+        if (kt == nkt - 1) {
+          umma::mma_commit(tfull);
+          if (pass == 0) nv = passes() * nkt;
+          if (v == nv - 1) gemm_stamp(g, 7);
+        }
       }
     }
   } else {
-    grid_dep_wait();
-    // Before the K loop, without waiting on the loads: stage what the final
-    // epilogue reads from global memory (written by kernels this one waited
-    // for) by cp.async, the residual of each owned (row, sequence) item
-    // (O / down) or the sigmoid table (gate/up), and fetch the positions
-    // that say which sequences take part in this step.
-    const int et2 = threadIdx.x - 64;
-    int pos_m = INT_MAX;
-    if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
-      if (et2 < SP && et2 < c.S) pos_m = c.pos0[4 * et2];
-    if constexpr (KIND == kGemmO || KIND == kGemmDown) {
-      // items i .. i + 3 (i a multiple of 4) are 4 consecutive rows of one
-      // sequence: rows_per = 64 / splits >= 8
-      const int32_t* res = KIND == kGemmO ? c.hidden0 : c.post0;
-      const int lsp = __ffs(splits) - 1, lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
-      for (int i = 4 * et2; i < nl * SP; i += 4 * (kUThreads - 64)) {
-        const int local = i & (nl - 1), m = i >> lnl;
-        const int row = ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
-        if (m < c.S) cp_async16(stg + i, res + (size_t)m * kHidden + row0 + row);
-      }
-    } else if constexpr (KIND == kGemmGu) {
-      if ((reinterpret_cast<uintptr_t>(g.sig_lut) & 15) == 0) {
-        for (int e4 = et2; e4 < kSigLut / 4; e4 += kUThreads - 64) cp_async16(stg + 4 * e4, g.sig_lut + 4 * e4);
-        for (int e = kSigLut / 4 * 4 + et2; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
+    // ---- plane builders (warps 2-17), then the epilogue ---------------------
+    // builder et takes chunk cc (16 K values) of rows r0 and r0 + 64 in every
+    // K tile; their group scales, all K tiles, in registers
+    const int et = threadIdx.x - 64;
+    const int r0 = et >> 3, cc = et & 7;
+    uint32_t sc2[kUMaxKt];  // scale of row r0 (low half) and r0 + 64 (high half) per K tile
+    {
+      const uint16_t* s_lo;
+      const uint16_t* s_hi;
+      if constexpr (KIND == kGemmGu) {
+        s_lo = g.scales + (size_t)(tile * 64 + r0) * G;
+        s_hi = g.scales2 + (size_t)(tile * 64 + r0) * G;
       } else {
-        for (int e = et2; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
+        const int ga = row0 + r0 < g.rows ? row0 + r0 : g.rows - 1;
+        const int gb = row0 + r0 + 64 < g.rows ? row0 + r0 + 64 : g.rows - 1;
+        s_lo = g.scales + (size_t)ga * G;
+        s_hi = g.scales + (size_t)gb * G;
       }
-    }
-    cp_async_commit();
-    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. (its sub-partition);
-    // the four warps of one sub-partition take a quarter of the sequences each
-    const int sp = warp & 3, q = (warp - 2) >> 2;
-    const int r = 32 * sp + lane;
-    const int grow = row0 + r < g.rows ? row0 + r : g.rows - 1;
-    const uint16_t* srow = g.scales + (size_t)grow * G + 2 * kt0;
-    uint32_t s2all[8];  // this row's scale pairs for the CTA's K tiles (nkt <= 8)
+      const int gq = 2 * kt0 + (cc >> 2);
+      bool wide = false;  // a scale of this tile needs more than 8 bits
 #pragma unroll
-    for (int kt = 0; kt < 8; ++kt) s2all[kt] = kt < nkt ? *reinterpret_cast<const uint32_t*>(srow + 2 * kt) : 0u;
+      for (int kt = 0; kt < kUMaxKt; ++kt) {
+        const uint32_t a = kt < nkt ? s_lo[gq + 2 * kt] : 0u, b = kt < nkt ? s_hi[gq + 2 * kt] : 0u;
+        sc2[kt] = a | (b << 16);
+        wide |= (a | b) > 255u;
+      }
+      if (__any_sync(0xFFFFFFFFu, wide) && lane == 0) atomicOr(wide_any, 1);
+      __syncwarp();
+      if (lane == 0) umma::bar_arrive(scales_in);
+    }
+    int64_t rbp0 = 0, rbp1 = 0;  // sum_k w s of rows r0, r0 + 64 over this thread's chunks
+    const int sp_e = warp & 3, q = (warp - 2) >> 2;
+    const int r = 32 * sp_e + lane;  // the tile row (TMEM lane) this thread reads back
+    const uint32_t lane_base = tmem + ((uint32_t)(32 * sp_e) << 16);
     int64_t acc[C::Q];
 #pragma unroll
     for (int j = 0; j < C::Q; ++j) acc[j] = 0;
-    const uint32_t lane_base = tmem + ((uint32_t)(32 * sp) << 16);
-#pragma unroll 1
-    for (int kt = 0; kt < nkt; ++kt) {
-      uint32_t s2 = s2all[0];
-#pragma unroll
-      for (int i = 1; i < 8; ++i) s2 = kt == i ? s2all[i] : s2;
-      for (int h = 0; h < 2; ++h) {
-        if (!umma::bar_wait(tfull + h, kt & 1)) {
-          fail();
-          kt = nkt;
-          break;
+    int pos_m = INT_MAX;
+    bool dep_done = false;
+    // After the dependency wait: stage what the final epilogue reads from
+    // global memory (written by kernels this one waited for) by cp.async, the
+    // residual of each owned (row, sequence) item (O / down) or the sigmoid
+    // table (gate/up), and fetch the positions that say which sequences take
+    // part in this step.
+    auto dependent_loads = [&]() {
+      grid_dep_wait();
+      dep_done = true;
+      if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
+        if (et < c.S) pos_m = c.pos0[4 * et];
+      if constexpr (KIND == kGemmO || KIND == kGemmDown) {
+        // items i .. i + 3 (i a multiple of 4) are 4 consecutive rows of one
+        // sequence: rows_per = 64 / splits >= 8
+        const int32_t* res = KIND == kGemmO ? c.hidden0 : c.post0;
+        const int lsp = __ffs(splits) - 1, lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
+        for (int i = 4 * et; i < nl * SN; i += 4 * (kUThreads - 64)) {
+          const int local = i & (nl - 1), m = i >> lnl;
+          const int row = ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
+          if (m < c.S) cp_async16(stg + i, res + (size_t)m * kHidden + row0 + row);
         }
-        umma::fence_after_sync();
-        if (kt == 0 && h == 0 && warp == 2 && lane == 0) gemm_stamp(g, 3);
-        int32_t d0[C::Q], d1[C::Q], d2[C::Q], w1[1];
-        const uint32_t ta = lane_base + (uint32_t)(h * C::BUF + q * C::Q);
-        umma::tmem_ld_any<C::Q>(ta, d0);
-        umma::tmem_ld_any<C::Q>(ta + SP, d1);
-        umma::tmem_ld_any<C::Q>(ta + 2 * SP, d2);
-        umma::tmem_ld<1>(lane_base + (uint32_t)(h * C::BUF + 3 * SP), w1);
-        umma::tmem_ld_wait();
-        umma::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) umma::bar_arrive(tempty + h);
-        const int32_t s = (int32_t)(h ? (s2 >> 16) : (s2 & 0xFFFFu));
-        const int32_t s15 = s << 15, w256 = w1[0] * 256;
-#pragma unroll
-        for (int j = 0; j < C::Q; ++j) {
-          const int32_t lo = d0[j] + d1[j] * 256;
-          const int32_t t2 = 2 * d2[j] - w256;
-          acc[j] = mad_wide(lo, s, mad_wide(t2, s15, acc[j]));
+      } else if constexpr (KIND == kGemmGu) {
+        if ((reinterpret_cast<uintptr_t>(g.sig_lut) & 15) == 0) {
+          for (int e4 = et; e4 < kSigLut / 4; e4 += kUThreads - 64) cp_async16(stg + 4 * e4, g.sig_lut + 4 * e4);
+          for (int e = kSigLut / 4 * 4 + et; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
+        } else {
+          for (int e = et; e < kSigLut; e += kUThreads - 64) cp_async4(stg + e, g.sig_lut + e);
         }
       }
+      cp_async_commit();
+    };
+    // planes of (pass, K tile) step v into plane slot v % SPL
+    auto build = [&](int v) -> bool {
+      const int pass = v / nkt, kt = v - pass * nkt;
+      if (!umma::bar_wait(full_a + v % SA, (v / SA) & 1) || !umma::bar_wait(empty_p + v % SPL, ((v / SPL) & 1) ^ 1))
+        return false;
+      uint32_t s2 = sc2[0];
+#pragma unroll
+      for (int i = 1; i < kUMaxKt; ++i) s2 = kt == i ? sc2[i] : s2;
+      const uint8_t* pk = astage + (v % SA) * C::A_PK;
+      uint8_t* pl = planes + (v % SPL) * 2 * C::PLANE;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = r0 + 64 * h;
+        const uint32_t s = h ? (s2 >> 16) : (s2 & 0xFFFFu);
+        const uint2 x = *reinterpret_cast<const uint2*>(pk + row * 64 + cc * 8);
+        uint32_t U[4];
+        unpack16_biased(x, U);
+        if (pass == 0) {
+          const uint32_t su = U[0] + U[1] + U[2] + U[3];                  // byte sums <= 60: no carries
+          const int32_t sw = (int32_t)dp4a_uu(su, 0x01010101u, 0u) - 128;  // sum of the 16 weights
+          if (h)
+            rbp1 += (int64_t)sw * (int32_t)s;
+          else
+            rbp0 += (int64_t)sw * (int32_t)s;
+        }
+        // chunk cc of the row: 16-byte unit cc ^ (row % 8) of its 128-byte line
+        const uint32_t off = (uint32_t)row * 128u + ((uint32_t)(cc ^ (row & 7)) << 4);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t d = (s >> (8 * pass + 4 * j)) & 15u;
+          const uint32_t bias = (128u - 8u * d) * 0x01010101u;
+          uint4 o;
+          o.x = plane_word(U[0], d, bias);
+          o.y = plane_word(U[1], d, bias);
+          o.z = plane_word(U[2], d, bias);
+          o.w = plane_word(U[3], d, bias);
+          *reinterpret_cast<uint4*>(pl + j * C::PLANE + off) = o;
+        }
+      }
+      // plane bytes written by these threads are read by the tensor cores
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        umma::bar_arrive(full_p + v % SPL);
+        umma::bar_arrive(empty_a + v % SA);
+      }
+      return true;
+    };
+    // the accumulators of one pass: wait for its last MMAs, add T[j][i] << (8 pass + 4 j + 8 i)
+    auto read_pass = [&](int pass, int npass) -> bool {
+      if (!umma::bar_wait(tfull, pass)) return false;
+      umma::fence_after_sync();
+      if (pass == 0 && warp == 2 && lane == 0) gemm_stamp(g, 3);
+      // |T| < 120 * 255 * 1024 < 2^25 (K <= 1024 per CTA), so the two digits
+      // of a limb combine in int32, X_i = T[0][i] + 16 T[1][i] (< 2^30), and
+      // the row sum is X_0 + 2^8 X_1 + 2^16 X_2: two widening multiply-adds
+      int32_t x0[C::Q], x1[C::Q];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        int32_t d0[C::Q], d1[C::Q];
+        const uint32_t ta = lane_base + (uint32_t)(i * SN + q * C::Q);
+        umma::tmem_ld_any<C::Q>(ta, d0);
+        umma::tmem_ld_any<C::Q>(ta + C::NM, d1);
+        umma::tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < C::Q; ++j) {
+          const int32_t x = d0[j] + 16 * d1[j];
+          if (i == 0) {
+            x0[j] = x;
+          } else if (i == 1) {
+            x1[j] = x;
+          } else {
+            const int64_t t = mad_wide(x, 65536, mad_wide(x1[j], 256, (int64_t)x0[j]));
+            acc[j] += pass ? t * 256 : t;
+          }
+        }
+      }
+      if (pass + 1 < npass) {
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) umma::bar_arrive(tempty);
+      }
+      return true;
+    };
+    // the first plane slots fill before the dependency wait (weights only)
+    const int early = nkt < SPL ? nkt : SPL;
+    int nv = nkt;
+    bool ok = true;
+    for (int v = 0; v < nv && ok; ++v) {
+      if (v == early && !dep_done) dependent_loads();
+      ok = build(v);
+      const int pass = v / nkt;
+      if (ok && v - pass * nkt == nkt - 1) {
+        if (!dep_done) dependent_loads();
+        const int npass = passes();
+        nv = npass * nkt;
+        ok = read_pass(pass, npass);
+      }
     }
+    if (!ok) fail();
+    if (!dep_done) dependent_loads();
     if (warp == 2 && lane == 0) gemm_stamp(g, 4);
+    // sum_k w s of each row (the 2^23 offset of the activation limbs): the
+    // eight builders of a row add their chunks, the epilogue subtracts it
+#pragma unroll
+    for (int msk = 1; msk < 8; msk <<= 1) {
+      rbp0 += shfl_xor_i64(rbp0, msk);
+      rbp1 += shfl_xor_i64(rbp1, msk);
+    }
+    if (cc == 0) {
+      rbs[r0] = rbp0;
+      rbs[r0 + 64] = rbp1;
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kUThreads - 64) : "memory");
+    const int64_t rb = rbs[r];
+#pragma unroll
+    for (int j = 0; j < C::Q; ++j) acc[j] -= rb * (1LL << 23);
     cp_async_wait0();
     if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
-      if (et2 < SP) live[et2] = pos_m < c.max_ctx;
+      if (et < SN) live[et] = pos_m < c.max_ctx;
     // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
     // so each owner holds matching rows of both 64-row halves (gate and up);
     // splits is a power of two (1, 2, 4 or 8), so these are shifts and masks
@@ -975,8 +1178,10 @@ __global__ void __launch_bounds__(kUThreads, 1)
     const int local = (r >> 6) * rows_per + (r & (rows_per - 1));
     const int nl = 128 >> lsp;
     // red[src][m][local]: a warp's 32 rows land contiguously
-    int64_t* dst = red + ((size_t)split * SP + q * C::Q) * nl + local;
+    int64_t* dst = red + ((size_t)split * SN + q * C::Q) * nl + local;
     if (splits == 1) {
+      // (the LM head's row sums overwrite plane slots: every builder finished
+      // them before its MMAs, whose completion every thread here waited for)
 #pragma unroll
       for (int j = 0; j < C::Q; ++j) dst[(size_t)j * nl] = acc[j];
     } else {
@@ -992,22 +1197,22 @@ __global__ void __launch_bounds__(kUThreads, 1)
     __syncthreads();
   if (threadIdx.x == 0) gemm_stamp(g, 5);
 
-  // final epilogue over the rows this CTA owns (local row l, sequence m: item
-  // l + nl m; rows_per and nl are powers of two)
+  // final epilogue over the rows this CTA owns (local row l, sequence m of the
+  // chunk: item l + nl m; rows_per and nl are powers of two)
   const int lsp = __ffs(splits) - 1;
   const int lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
-  const int et = threadIdx.x;
+  const int ft = threadIdx.x;
   auto row_of = [&](int local) {
     return ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
   };
   auto sum_of = [&](int local, int m) {
     int64_t v = 0;
-    for (int src = 0; src < splits; ++src) v += red[((size_t)src * SP + m) * nl + local];
+    for (int src = 0; src < splits; ++src) v += red[((size_t)src * SN + m) * nl + local];
     return v;
   };
   if (!*abort_flag) {
     if constexpr (KIND == kGemmQkv) {
-      for (int i = et; i < nl * SP; i += kUThreads) {
+      for (int i = ft; i < nl * SN; i += kUThreads) {
         const int local = i & (nl - 1), m = i >> lnl;
         if (m < c.S)
           c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
@@ -1015,30 +1220,30 @@ __global__ void __launch_bounds__(kUThreads, 1)
     } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
       // residual (staged in stg) + o_proj / down output >> 2
       int32_t* __restrict__ out = KIND == kGemmO ? c.post0 : c.hidden0;
-      for (int i = et; i < nl * SP; i += kUThreads) {
+      for (int i = ft; i < nl * SN; i += kUThreads) {
         const int local = i & (nl - 1), m = i >> lnl;
-        if (!live[m]) continue;
+        if (m >= c.S || !live[m]) continue;
         const int32_t o = sat24(sum_of(local, m) >> 14);
         out[(size_t)m * kHidden + row0 + row_of(local)] = sat24((int64_t)stg[i] + (o >> 2));
       }
     } else if constexpr (KIND == kGemmGu) {
       // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
-      for (int i = et; i < rows_per * SP; i += kUThreads) {
+      for (int i = ft; i < rows_per * SN; i += kUThreads) {
         const int j = i & (rows_per - 1), m = i >> lrp;
-        if (!live[m]) continue;
+        if (m >= c.S || !live[m]) continue;
         const int32_t gv = sat24(sum_of(j, m) >> 14), uv = sat24(sum_of(rows_per + j, m) >> 14);
         const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
         int ix = (gc + 32768 + 32) >> 6;
         ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
         const int32_t silu = sat24(((int64_t)gv * stg[ix]) >> 16);
         const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
-        write_limbs(c.bt3, SP, kInter, m, tile * 64 + split * rows_per + j, hv);
+        write_limbs(c.bt3, SP, kInter, n0 + m, tile * 64 + split * rows_per + j, hv);
       }
     } else {
       // LM head (no split): best (score, row) of each sequence over the tile
-      ArgBestD* cand = reinterpret_cast<ArgBestD*>(sm);  // the TMA stages are free now
-      constexpr int kParts = kUThreads / SP;
-      for (int i = et; i < kParts * SP; i += kUThreads) {
+      ArgBestD* cand = reinterpret_cast<ArgBestD*>(bstage);  // the limb ring is free now
+      constexpr int kParts = kUThreads / SN;
+      for (int i = ft; i < kParts * SN; i += kUThreads) {
         const int part = i % kParts, m = i / kParts;
         int64_t bs = INT64_MIN;
         int32_t bi = INT32_MAX;
@@ -1051,16 +1256,16 @@ __global__ void __launch_bounds__(kUThreads, 1)
             bi = row;
           }
         }
-        cand[part * SP + m] = ArgBestD{bs, bi, 0};
+        cand[part * SN + m] = ArgBestD{bs, bi, 0};
       }
       __syncthreads();
-      for (int m = et; m < SP; m += kUThreads) {
+      for (int m = ft; m < SN; m += kUThreads) {
         ArgBestD b = cand[m];
         for (int part = 1; part < kParts; ++part) {
-          const ArgBestD o = cand[part * SP + m];
+          const ArgBestD o = cand[part * SN + m];
           if (o.score > b.score || (o.score == b.score && o.idx < b.idx)) b = o;
         }
-        g.partial[(size_t)tile * kBatchSeqMax + m] = b;
+        g.partial[(size_t)tile * kBatchSeqMax + n0 + m] = b;
       }
     }
   }
@@ -1956,22 +2161,45 @@ cudaError_t launch_pdl(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStr
   } while (0)
 
 // K splits of each batched GEMM (a cluster of that many CTAs per row tile)
-constexpr int kSplitQkv = 4, kSplitO = 8, kSplitGu = 2, kSplitDown = 8;
-// prefill launches cover up to 8 sub-batches each, so they need fewer splits to fill the GPU
-constexpr int kPfSplitQkv = 1, kPfSplitO = 2, kPfSplitGu = 1, kPfSplitDown = 4;
-
-template <int SP, int KIND>
-cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& bmap, const BatchCtx& c, const uint16_t* scales,
-                        int rows, int K, int splits, const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s,
-                        unsigned long long* trace = nullptr, int subs = 1) {
-  // the epilogue's row bookkeeping uses shifts: splits must be 1, 2, 4 or 8
-  if (splits < 1 || splits > 8 || (splits & (splits - 1)) || K % (128 * splits)) return cudaErrorInvalidValue;
+template <int SN, int KIND>
+cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& amap2, const CUtensorMap& bmap, const BatchCtx& c,
+                        const uint16_t* scales, const uint16_t* scales2, int rows, int K, int splits, int SP,
+                        const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s, unsigned long long* trace,
+                        int subs, int b_sub_rows) {
+  // the epilogue's row bookkeeping uses shifts: splits must be 1, 2, 4 or 8;
+  // a CTA holds the scales of at most kUMaxKt K tiles
+  if (splits < 1 || splits > 8 || (splits & (splits - 1)) || K % (128 * splits) || K / splits > 128 * kUMaxKt ||
+      SP % SN || SP > kBatchSeqMax)
+    return cudaErrorInvalidValue;
   // O / down stage their residual rows (128 / splits of them) in 64 rows' room
   if ((KIND == kGemmO || KIND == kGemmDown) && splits < 2) return cudaErrorInvalidValue;
-  UGemm g{c, scales, rows, K, K / 128 / splits, sig_lut, partial, trace};
-  const dim3 grid((unsigned)subs, (unsigned)splits, (unsigned)((rows + 127) / 128));
-  return launch_ex(umma_gemm_kernel<SP, KIND>, grid, dim3(kUThreads), gemm_smem<SP, KIND>(), s, splits, amap, bmap, g);
+  UGemm g{c, scales, scales2, rows, K, K / 128 / splits, SP, SP / SN, b_sub_rows, sig_lut, partial, trace};
+  const dim3 grid((unsigned)(subs * (SP / SN)), (unsigned)splits, (unsigned)((rows + 127) / 128));
+  return launch_ex(umma_gemm_kernel<SN, KIND>, grid, dim3(kUThreads), UCfg<SN, KIND>::SMEM, s, splits, amap, amap2,
+                   bmap, g);
 }
+
+// The same with the chunk width chosen at run time.
+template <int KIND, typename... Args>
+cudaError_t launch_gemm_sn(int sn, Args... args) {
+  switch (sn) {
+    case 8: return launch_gemm<8, KIND>(args...);
+    case 16: return launch_gemm<16, KIND>(args...);
+    case 24: return launch_gemm<24, KIND>(args...);
+    case 32: return launch_gemm<32, KIND>(args...);
+    case 64: return launch_gemm<64, KIND>(args...);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+// K splits of each GEMM of a decode step (a cluster of that many CTAs per row
+// tile); prefill launches cover up to 16 sub-batches of 64 columns each, so
+// they need fewer splits to fill the GPU
+int decode_splits(int kind, int SP) {
+  (void)SP;
+  return kind == kGemmQkv ? 4 : kind == kGemmGu ? 2 : kind == kGemmLm ? 1 : 8;
+}
+constexpr int kPfSplitQkv = 1, kPfSplitO = 2, kPfSplitGu = 1, kPfSplitDown = 4;
 
 bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
 // cluster size of the cluster attention (16 CTAs for batches of up to 4 sequences), the keys per
@@ -2019,8 +2247,9 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
     BMARK(kBkNorm);
-    BQ((launch_gemm<SP, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kQRows + 2 * kKvRows, kHidden, kSplitQkv, nullptr,
-                                  nullptr, s, gtrace(4 * l + 0))));
+    BQ(launch_gemm_sn<kGemmQkv>(q4gpu_batch_gemm_chunk(kGemmQkv, SP), w.mqkv, w.mqkv, p.mb_qkv, c, w.sqkv,
+                                (const uint16_t*)nullptr, kQRows + 2 * kKvRows, kHidden, decode_splits(kGemmQkv, SP),
+                                SP, (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 0), 1, 0));
     BMARK(kBkQkv);
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
@@ -2034,23 +2263,27 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
       BQ(launch_pdl(batch_attn_values_kernel, attn_grid, dim3(256), 0, s, c, as, l));
     }
     BMARK(kBkAttn);
-    BQ((launch_gemm<SP, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kSplitO, nullptr, nullptr, s,
-                                gtrace(4 * l + 1))));
+    BQ(launch_gemm_sn<kGemmO>(q4gpu_batch_gemm_chunk(kGemmO, SP), w.mo, w.mo, p.mb_o, c, w.so,
+                              (const uint16_t*)nullptr, kHidden, 2 * kHidden, decode_splits(kGemmO, SP), SP,
+                              (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 1), 1, 0));
     BMARK(kBkO);
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
     BMARK(kBkNorm);
-    BQ((launch_gemm<SP, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kSplitGu, p.sig_lut, nullptr, s,
-                                 gtrace(4 * l + 2))));
+    BQ(launch_gemm_sn<kGemmGu>(q4gpu_batch_gemm_chunk(kGemmGu, SP), w.mgate, w.mup, p.mb_gu, c, w.sgate, w.sup,
+                               2 * kInter, kHidden, decode_splits(kGemmGu, SP), SP, p.sig_lut, (ArgBestD*)nullptr, s,
+                               gtrace(4 * l + 2), 1, 0));
     BMARK(kBkGu);
-    BQ((launch_gemm<SP, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kSplitDown, nullptr, nullptr, s,
-                                   gtrace(4 * l + 3))));
+    BQ(launch_gemm_sn<kGemmDown>(q4gpu_batch_gemm_chunk(kGemmDown, SP), w.mdown, w.mdown, p.mb_down, c, w.sdown,
+                                 (const uint16_t*)nullptr, kHidden, kInter, decode_splits(kGemmDown, SP), SP,
+                                 (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 3), 1, 0));
     BMARK(kBkDown);
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final, p.final_act));
   BMARK(kBkNorm);
   if (p.final_act) return Q4GPU_OK;  // hidden-only step: the LM head runs per vocabulary shard
-  BQ((launch_gemm<SP, kGemmLm>(p.mlm, p.mb1, c, p.semb, p.vocab, kHidden, 1, nullptr, p.lm_partial, s,
-                               gtrace(4 * p.n_layers))));
+  BQ(launch_gemm_sn<kGemmLm>(q4gpu_batch_gemm_chunk(kGemmLm, SP), p.mlm, p.mlm, p.mb_lm, c, p.semb,
+                             (const uint16_t*)nullptr, p.vocab, kHidden, 1, SP, (const int32_t*)nullptr, p.lm_partial,
+                             s, gtrace(4 * p.n_layers), 1, 0));
   BMARK(kBkLm);
   BQ(launch_pdl(batch_argmax_kernel, dim3(p.S), dim3(256), 0, s, c, (const ArgBestD*)p.lm_partial,
                 (p.vocab + 127) / 128));
@@ -2059,19 +2292,40 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   return Q4GPU_OK;
 }
 
-template <int SP, int KIND>
+template <int SN, int KIND>
 int set_smem() {
-  BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)gemm_smem<SP, KIND>()));
+  BQ(cudaFuncSetAttribute(umma_gemm_kernel<SN, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                          (int)UCfg<SN, KIND>::SMEM));
+  return Q4GPU_OK;
+}
+
+template <int SN>
+int set_smem_all_kinds() {
+  int rc;
+  if ((rc = set_smem<SN, kGemmQkv>()) || (rc = set_smem<SN, kGemmO>()) || (rc = set_smem<SN, kGemmGu>()) ||
+      (rc = set_smem<SN, kGemmDown>()) || (rc = set_smem<SN, kGemmLm>()))
+    return rc;
+  return Q4GPU_OK;
+}
+
+// shared-memory attributes of every GEMM instantiation, once per process and device
+int gemm_setup() {
+  static bool done[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return q4gpu_fail(Q4GPU_ERR_CUDA, "no device");
+  if (done[dev]) return Q4GPU_OK;
+  int rc;
+  if ((rc = set_smem_all_kinds<8>()) || (rc = set_smem_all_kinds<16>()) || (rc = set_smem_all_kinds<24>()) ||
+      (rc = set_smem_all_kinds<32>()) || (rc = set_smem_all_kinds<64>()))
+    return rc;
+  done[dev] = true;
   return Q4GPU_OK;
 }
 
 template <int SP>
 int setup_t(const BatchPlan& p) {
   int rc;
-  if ((rc = set_smem<SP, kGemmQkv>()) || (rc = set_smem<SP, kGemmO>()) || (rc = set_smem<SP, kGemmGu>()) ||
-      (rc = set_smem<SP, kGemmDown>()) || (rc = set_smem<SP, kGemmLm>()))
-    return rc;
+  if ((rc = gemm_setup())) return rc;
   if (attn_cluster(p)) {
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_cl_smem(p)));
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -2085,6 +2339,15 @@ int setup_t(const BatchPlan& p) {
 }  // namespace
 
 int q4gpu_batch_padded(int S) { return S <= 8 ? 8 : S <= 16 ? 16 : S <= 24 ? 24 : S <= 32 ? 32 : 64; }
+
+// One MMA costs about the same below N = 96 (M = 128, K = 32: ~46 cycles up
+// to N = 64, ~96 at N = 192), and every sequence chunk of a tile repeats the
+// tile's plane building, so decode GEMMs take all SP sequences per CTA and
+// reach the GPU's width by splitting K.
+int q4gpu_batch_gemm_chunk(int kind, int SP) {
+  (void)kind;
+  return SP;
+}
 
 int q4gpu_batch_setup(const BatchPlan& p) {
   switch (p.SP) {
@@ -2128,14 +2391,29 @@ int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes
   return Q4GPU_OK;
 }
 
-int q4gpu_batch_limb_rows(int SP) { return 3 * SP + kBatchOnes; }
-int q4gpu_batch_box_rows(int SP) { return (3 * SP + kBatchOnes + 15) / 16 * 16; }
-
-int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s) {
-  const int blocks = (int)std::min<int64_t>((n_bytes + 255) / 256, 148 * 32);
-  expand_int4_kernel<<<blocks, 256, 0, s>>>(packed, n_bytes, out);
-  return q4gpu_check_launch();
+int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", reinterpret_cast<void**>(&encode), cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !encode)
+      return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner_bytes & 15))
+    return q4gpu_fail(Q4GPU_ERR_ALIGN, "packed weights must start and have rows on 16-byte boundaries");
+  const cuuint64_t dims[2] = {(cuuint64_t)inner_bytes, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)inner_bytes};
+  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q4GPU_OK;
 }
+
+int q4gpu_batch_limb_rows(int SP) { return 3 * SP + kBatchPad; }
 
 template <int SP>
 int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
@@ -2145,10 +2423,11 @@ int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
   c.err = q.err;
   act_limbs_kernel<<<q.n_act, 256, 0, s>>>(q.acts, q.bt, SP);
   BQ(cudaGetLastError());
-  BQ(cudaFuncSetAttribute(umma_gemm_kernel<SP, kGemmLm>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                          (int)gemm_smem<SP, kGemmLm>()));
+  int rc;
+  if ((rc = gemm_setup())) return rc;
   const int rows = q.row_end - q.row_begin;
-  BQ((launch_gemm<SP, kGemmLm>(q.amap, q.bmap, c, q.scales, rows, kHidden, 1, nullptr, q.partial, s)));
+  BQ((launch_gemm<SP, kGemmLm>(q.amap, q.amap, q.bmap, c, q.scales, nullptr, rows, kHidden, 1, SP, nullptr, q.partial,
+                               s, nullptr, 1, 0)));
   shard_argmax_kernel<<<q.n_act, 256, 0, s>>>(q.partial, (rows + 127) / 128, q.row_begin, q.best_score, q.best_row);
   BQ(cudaGetLastError());
   return Q4GPU_OK;
@@ -2156,9 +2435,7 @@ int lm_shard_t(const LmShardPlan& q, cudaStream_t s) {
 
 int q4gpu_prefill_setup() {
   int rc;
-  if ((rc = set_smem<kPfSub, kGemmQkv>()) || (rc = set_smem<kPfSub, kGemmO>()) ||
-      (rc = set_smem<kPfSub, kGemmGu>()) || (rc = set_smem<kPfSub, kGemmDown>()))
-    return rc;
+  if ((rc = gemm_setup())) return rc;
   BQ(cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfSmem));
   return Q4GPU_OK;
 }
@@ -2167,7 +2444,7 @@ int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
   if (p.n_cols < 1 || p.n_cols > kPfBlock || p.n_tiles < 1 || p.n_tiles > kPfBlock)
     return q4gpu_fail(Q4GPU_ERR_SHAPE, "prefill block of %d columns / %d tiles", p.n_cols, p.n_tiles);
   constexpr int kRow = kQRows + 2 * kKvRows;
-  constexpr size_t nb = (size_t)UCfg<kPfSub>::NB;  // rows of one sub-batch's limb matrix (ones rows, zero padding)
+  constexpr size_t nb = (size_t)kPfSubRows;  // rows of one sub-batch's limb matrix
   const int nsub = (p.n_cols + kPfSub - 1) / kPfSub;
   // all columns of the block in one context: the GEMMs take sub-batch z from blockIdx.z
   const BatchCtx c{p.col_slots, p.n_cols, kPfSub, p.qkv,      p.bt1,         p.bt2,  p.bt3,
@@ -2177,20 +2454,20 @@ int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
-    BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, p.mb1, c, w.sqkv, kRow, kHidden, kPfSplitQkv, nullptr, nullptr, s,
-                                      nullptr, nsub)));
+    BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, w.mqkv, p.mb1, c, w.sqkv, nullptr, kRow, kHidden, kPfSplitQkv, kPfSub,
+                                      nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
     BQ(launch_pdl(prefill_qk_kernel, dim3(kKvHeads, p.n_cols), dim3(128), 0, s, p.col_slots, p.col_pos4, p.qkv, l,
                   w.g_q, w.g_k, p.cos_tab, p.sin_tab));
     const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, nb * 2 * kHidden, p.lut_idx, (p.max_ctx + 63) / 64 * 64, l,
                    p.exp_lut, p.err};
     BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(kPfThreads), kPfSmem, s, a));
-    BQ((launch_gemm<kPfSub, kGemmO>(w.mo, p.mb2, c, w.so, kHidden, 2 * kHidden, kPfSplitO, nullptr, nullptr, s,
-                                    nullptr, nsub)));
+    BQ((launch_gemm<kPfSub, kGemmO>(w.mo, w.mo, p.mb2, c, w.so, nullptr, kHidden, 2 * kHidden, kPfSplitO, kPfSub,
+                                    nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
-    BQ((launch_gemm<kPfSub, kGemmGu>(w.mgu, p.mb1, c, w.sgu, 2 * kInter, kHidden, kPfSplitGu, p.sig_lut, nullptr, s,
-                                     nullptr, nsub)));
-    BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, p.mb3, c, w.sdown, kHidden, kInter, kPfSplitDown, nullptr, nullptr,
-                                       s, nullptr, nsub)));
+    BQ((launch_gemm<kPfSub, kGemmGu>(w.mgate, w.mup, p.mb1, c, w.sgate, w.sup, 2 * kInter, kHidden, kPfSplitGu,
+                                     kPfSub, p.sig_lut, nullptr, s, nullptr, nsub, kPfSubRows)));
+    BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, w.mdown, p.mb3, c, w.sdown, nullptr, kHidden, kInter, kPfSplitDown,
+                                       kPfSub, nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
   }
   return Q4GPU_OK;
 }
@@ -2211,12 +2488,6 @@ int q4gpu_enqueue_batch_commit(const BatchPlan& p, const int64_t* tokens, const 
   c.S = p.S;
   c.lm_from = p.lm_from;
   batch_commit_kernel<<<(p.S + 63) / 64, 64, 0, s>>>(c, tokens, scores);
-  return q4gpu_check_launch();
-}
-
-int q4gpu_expand_gu(const uint8_t* gate, const uint8_t* up, const uint16_t* sg, const uint16_t* su, int8_t* out,
-                    uint16_t* sout, cudaStream_t s) {
-  expand_gu_kernel<<<148 * 8, 256, 0, s>>>(gate, up, sg, su, out, sout);
   return q4gpu_check_launch();
 }
 

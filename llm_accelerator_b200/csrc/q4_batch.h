@@ -7,25 +7,22 @@
 namespace q4 {
 
 constexpr int kBatchSeqMax = 64;  // sequences one batched step advances
-constexpr int kBatchOnes = 8;     // B rows of ones after the 3 SP limb rows
+constexpr int kBatchPad = 8;      // zero B rows after the 3 SP limb rows (the MMA's N rounds 3 SP up to 16)
 constexpr int kScoreScale = 189812531;  // round(128^-0.5 * 2^31)
 
-// int8 copies of one layer's Q4 matrices (row-major [rows, K], one byte per
-// weight), with the model's Q2.14 group scales.
+// TMA maps of one layer's Q4 matrices as the model stores them (packed
+// nibbles [rows, K / 2], 64-byte x 64-row boxes), with their Q2.14 scales.
 struct BatchLayerW {
-  // TMA maps of the int8 matrices (128-byte x 128-row boxes, 128-byte swizzle)
-  alignas(64) CUtensorMap mqkv;
-  CUtensorMap mo;
-  CUtensorMap mgu;
-  CUtensorMap mdown;
-  const int8_t* wqkv;  // [4096, 1024]: q, k, v rows
-  const uint16_t* sqkv;
-  const int8_t* wo;  // [1024, 2048]
-  const uint16_t* so;
-  const int8_t* wgu;  // [6144, 1024]: 128-row blocks, gate rows 64b.. then up rows 64b..
-  const uint16_t* sgu;  // [6144, 16], same row order
-  const int8_t* wdown;  // [1024, 3072]
-  const uint16_t* sdown;
+  alignas(64) CUtensorMap mqkv;  // [4096, 512]: q, k, v rows
+  CUtensorMap mo;                // [1024, 1024]
+  CUtensorMap mgate;             // [3072, 512]
+  CUtensorMap mup;               // [3072, 512]
+  CUtensorMap mdown;             // [1024, 1536]
+  const uint16_t* sqkv;          // [4096, 16]
+  const uint16_t* so;            // [1024, 32]
+  const uint16_t* sgate;         // [3072, 16]
+  const uint16_t* sup;           // [3072, 16]
+  const uint16_t* sdown;         // [1024, 48]
   const int32_t* g_in;
   const int32_t* g_post;
   const int32_t* g_q;
@@ -33,10 +30,14 @@ struct BatchLayerW {
 };
 
 struct BatchPlan {
-  alignas(64) CUtensorMap mb1;  // TMA maps of bt1 / bt2 / bt3 ([3 SP + 8] rows)
-  CUtensorMap mb2;
-  CUtensorMap mb3;
-  CUtensorMap mlm;  // int8 embedding (LM head)
+  // TMA maps of the limb matrices bt1 / bt2 / bt3 ([3 SP + 8] rows), one per
+  // GEMM: boxes of the GEMM's sequence chunk (q4gpu_batch_gemm_chunk rows)
+  alignas(64) CUtensorMap mb_qkv;  // bt1
+  CUtensorMap mb_o;                // bt2
+  CUtensorMap mb_gu;               // bt1
+  CUtensorMap mb_down;             // bt3
+  CUtensorMap mb_lm;               // bt1
+  CUtensorMap mlm;  // packed Q4 embedding (the tied LM head)
   const SlotState* slots;  // device array [S]: sequence m is slot m
   int S;                   // live sequences (1..64)
   int SP;                  // padded sequence count: 8, 16, 24, 32 or 64
@@ -47,7 +48,6 @@ struct BatchPlan {
   const int32_t* lm_from;  // [S] the argmax is stored at positions p with p + 1 >= lm_from
   const uint8_t* emb;      // packed Q4 embedding [vocab, 512]
   const uint16_t* semb;    // [vocab, 16]
-  const int8_t* emb8;      // int8 embedding [vocab, 1024] (LM head)
   const BatchLayerW* layers;  // host array [n_layers]
   int n_layers;
   int max_ctx;
@@ -77,8 +77,8 @@ struct BatchPlan {
 
 // LM head over one vocabulary shard [row_begin, row_end) for n_act vectors.
 struct LmShardPlan {
-  alignas(64) CUtensorMap amap;  // int8 embedding rows of the shard
-  CUtensorMap bmap;              // limbs of the vectors
+  alignas(64) CUtensorMap amap;  // packed Q4 embedding rows of the shard
+  CUtensorMap bmap;              // limbs of the vectors (boxes of SP rows)
   const int32_t* acts;           // [n_act, 1024] Q12.12
   int n_act;
   int row_begin, row_end;
@@ -106,7 +106,7 @@ struct PfAttn {
   const PfTile* tiles;
   const SlotState* col_slots;  // [block columns] the column's sequence state
   const int32_t* qkv;          // [block columns][4096]; q rows normed and roped
-  uint8_t* bt2;                // [block columns / 64][208][2048] limbs of the attention output
+  uint8_t* bt2;                // [block columns / 64][192][2048] limbs of the attention output
   size_t bt2_sub;              // bytes per 64-column sub-batch of bt2
   uint16_t* lut_idx;           // [block columns][16][idx_ld] exp-LUT indices (scratch)
   int idx_ld;                  // max_ctx rounded up to 64
@@ -115,11 +115,11 @@ struct PfAttn {
   int* err;
 };
 
-// Limb matrices of the prefill hold kPfBlock / 64 sub-batches of
-// q4gpu_batch_box_rows(64) = 208 rows each (3 * 64 limb rows, 8 ones rows, 8
-// zero rows); a GEMM's sub-batch z reads B rows 208 z .. 208 z + 207.
+// Limb matrices of the prefill hold kPfBlock / 64 sub-batches of kPfSubRows =
+// 192 limb rows each; a GEMM's sub-batch z reads B rows 192 z .. 192 z + 191.
+constexpr int kPfSubRows = 3 * kPfSub;
 struct PrefillPlan {
-  alignas(64) CUtensorMap mb1;  // TMA maps of bt1 / bt2 / bt3, 208-row boxes
+  alignas(64) CUtensorMap mb1;  // TMA maps of bt1 / bt2 / bt3, 64-row boxes (one limb of a sub-batch)
   CUtensorMap mb2;
   CUtensorMap mb3;
   const SlotState* col_slots;  // [n_cols] this block's columns
@@ -129,9 +129,9 @@ struct PrefillPlan {
   int32_t* hidden;  // [kPfBlock][1024]
   int32_t* post;    // [kPfBlock][1024]
   int32_t* qkv;     // [kPfBlock][4096]
-  uint8_t* bt1;     // [kPfBlock / 64][208][1024]
-  uint8_t* bt2;     // [kPfBlock / 64][208][2048]
-  uint8_t* bt3;     // [kPfBlock / 64][208][3072]
+  uint8_t* bt1;     // [kPfBlock / 64][192][1024]
+  uint8_t* bt2;     // [kPfBlock / 64][192][2048]
+  uint8_t* bt3;     // [kPfBlock / 64][192][3072]
   uint16_t* lut_idx;  // [kPfBlock][16][max_ctx rounded up to 64]
   const uint8_t* emb;
   const uint16_t* semb;
@@ -150,10 +150,14 @@ constexpr int kGemmTraceCtas = 1200;  // CTAs one GEMM launch can record (the LM
 }  // namespace q4
 
 int q4gpu_batch_padded(int S);
-int q4gpu_batch_limb_rows(int SP);  // rows of a limb matrix: 3 SP + 8
-int q4gpu_batch_box_rows(int SP);   // the same rounded up to the MMA's N granule (16)
+int q4gpu_batch_limb_rows(int SP);  // rows of a limb matrix: 3 SP + 8 (the last 8 zero)
+// Sequences per CTA (the limb-box rows) of a batched GEMM kind (q4_batch.cu
+// GemmKind: 0 q/k/v, 1 o_proj, 2 gate/up, 3 down, 4 LM head) at SP padded sequences.
+int q4gpu_batch_gemm_chunk(int kind, int SP);
 // 2-D TMA map of a row-major u8 matrix [rows, inner_bytes], 128 x box_rows boxes, 128-byte swizzle
 int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows);
+// 2-D TMA map of packed Q4 weights [rows, inner_bytes]: 64-byte x 64-row boxes (one 128-wide K tile of 64 rows)
+int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows);
 int q4gpu_batch_setup(const q4::BatchPlan& p);
 // Kernel kinds of a batched step (q4gpu.h Q4GPU_BK_*), for per-kernel timing.
 enum { kBkEmbed = 0, kBkNorm, kBkQkv, kBkAttn, kBkO, kBkGu, kBkDown, kBkLm, kBkArgmax, kBkCount };
@@ -164,11 +168,6 @@ struct BatchMarks {
 // One decode position for all S sequences (embedding .. argmax), stream-ordered.
 // With marks, an event is recorded after every launch (no overlap between kernels).
 int q4gpu_enqueue_batch_step(const q4::BatchPlan& p, cudaStream_t s, BatchMarks* marks = nullptr);
-// packed int4 (two per byte, even index in the low nibble) -> int8
-int q4gpu_expand_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, cudaStream_t s);
-// gate/up packed rows -> the interleaved int8 layout of BatchLayerW::wgu / sgu
-int q4gpu_expand_gu(const uint8_t* gate, const uint8_t* up, const uint16_t* sg, const uint16_t* su, int8_t* out,
-                    uint16_t* sout, cudaStream_t s);
 // in: device [S][2] (token, position); lm_from[m] = 0
 int q4gpu_batch_load(const q4::SlotState* slots, int S, const int32_t* in, int32_t* lm_from, cudaStream_t s);
 // out: device [S][4] int32 = (token, 0, score as int64) at position in[m][1] + 1

@@ -477,9 +477,7 @@ struct q4gpu_model {
   int* p_err = nullptr;
   CUtensorMap vmap{};
   // batched decode (q4_batch.cu), set up on first use
-  int8_t* b_w8 = nullptr;     // per layer: qkv [4096,1024], o [1024,2048], gate/up [6144,1024], down [1024,3072]
-  uint16_t* b_sgu = nullptr;  // per layer: gate/up scales [6144,16] in the interleaved row order
-  int8_t* b_emb8 = nullptr;   // [vocab, 1024]
+  bool b_ready = false;       // batched buffers and the TMA maps of the packed weights set up
   int32_t* b_qkv = nullptr;
   uint8_t* b_bt1 = nullptr;
   uint8_t* b_bt2 = nullptr;
@@ -495,18 +493,17 @@ struct q4gpu_model {
   int64_t* b_att_M = nullptr;
   int64_t* b_att_O = nullptr;
   unsigned* b_att_cnt = nullptr;  // [2][64][8]
-  CUtensorMap b_mlm{};       // TMA map of b_emb8
+  CUtensorMap b_mlm{};       // TMA map of the packed embedding (the tied LM head)
   BatchLayerW b_layers[kMaxLayers]{};
-  bool b_stale = true;  // int8 copies out of date with the Q4 weights
   bool p_stale = true;  // the persistent kernel's o_proj slices out of date
   uint8_t* p_wo_sl = nullptr;
   uint16_t* p_so_sl = nullptr;
-  int b_ones_sp = 0;    // SP whose ones rows the B matrices hold
+  int b_pad_sp = 0;     // SP whose zero padding rows the B matrices hold
   std::map<std::tuple<int, int, int>, cudaGraphExec_t> b_graphs;  // (first slot, S, hidden-only)
   int32_t* b_final_act = nullptr;   // [64, 1024] final-norm vectors of a hidden-only step
   uint8_t* b_lm_bt = nullptr;       // limb matrix of a vocabulary-shard LM head
   ArgBestD* b_lm_shard_part = nullptr;
-  int b_lm_ones_sp = 0;
+  int b_lm_pad_sp = 0;
   // batched exact prefill (q4gpu_batch_prefill)
   int prefill_mode = 1;          // 1: batched prefill in q4gpu_decode_batch; 0: serial, position by position
   PrefillPlan* pf = nullptr;     // buffers and TMA maps; per-block fields set per launch
@@ -849,88 +846,64 @@ uint64_t step_bytes(const q4gpu_model* m, int layers, int ctx, int tail) {
 }
 
 // ---- batched decode (q4_batch.cu) ------------------------------------------
-constexpr size_t kB8Qkv = (size_t)(kQRows + 2 * kKvRows) * kHidden;
-constexpr size_t kB8O = (size_t)kHidden * 2 * kHidden;
-constexpr size_t kB8Gu = (size_t)2 * kInter * kHidden;
-constexpr size_t kB8Down = (size_t)kHidden * kInter;
-constexpr size_t kB8Layer = kB8Qkv + kB8O + kB8Gu + kB8Down;
-constexpr int kBtRows = 3 * kBatchSeqMax + kBatchOnes;
+constexpr int kBtRows = 3 * kBatchSeqMax + kBatchPad;
 
 int batch_lm_ctas(int vocab) { return (vocab + 127) / 128; }
 
-// Allocate the batched-decode buffers once and refresh the int8 weight copies
-// when the Q4 weights changed since the last batched call.
+// Allocate the batched-decode buffers and encode the TMA maps of the packed
+// weights once (the maps address the model's own Q4 tensors, so later weight
+// uploads need nothing here).
 int batch_prepare(q4gpu_model* m) {
   if (m->cfg.vocab < 64) return q4gpu_fail(Q4GPU_ERR_SHAPE, "batched decode needs a vocabulary of at least 64");
+  if (m->b_ready) return Q4GPU_OK;
   const int L = m->cfg.n_layers;
   int rc;
-  if (!m->b_w8) {
-    if ((rc = m->alloc(&m->b_w8, kB8Layer * L))) return rc;
-    if ((rc = m->alloc(&m->b_sgu, (size_t)2 * kInter * (kHidden / kGroup) * L))) return rc;
-    if ((rc = m->alloc(&m->b_emb8, (size_t)m->cfg.vocab * kHidden))) return rc;
-    if ((rc = m->alloc(&m->b_qkv, (size_t)kBatchSeqMax * (kQRows + 2 * kKvRows)))) return rc;
-    if ((rc = m->alloc(&m->b_bt1, (size_t)kBtRows * kHidden))) return rc;
-    if ((rc = m->alloc(&m->b_bt2, (size_t)kBtRows * 2 * kHidden))) return rc;
-    if ((rc = m->alloc(&m->b_bt3, (size_t)kBtRows * kInter))) return rc;
-    if ((rc = m->alloc(&m->b_slots, m->slots.size()))) return rc;
-    if ((rc = stream_copy(m, m->b_slots, m->slots.data(), sizeof(SlotState) * m->slots.size(), cudaMemcpyHostToDevice)))
+  if ((rc = m->alloc(&m->b_qkv, (size_t)kBatchSeqMax * (kQRows + 2 * kKvRows)))) return rc;
+  if ((rc = m->alloc(&m->b_bt1, (size_t)kBtRows * kHidden))) return rc;
+  if ((rc = m->alloc(&m->b_bt2, (size_t)kBtRows * 2 * kHidden))) return rc;
+  if ((rc = m->alloc(&m->b_bt3, (size_t)kBtRows * kInter))) return rc;
+  if ((rc = m->alloc(&m->b_slots, m->slots.size()))) return rc;
+  if ((rc = stream_copy(m, m->b_slots, m->slots.data(), sizeof(SlotState) * m->slots.size(), cudaMemcpyHostToDevice)))
+    return rc;
+  if ((rc = m->alloc(&m->b_lm_from, (size_t)m->cfg.max_seqs))) return rc;
+  if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
+  if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
+  if ((rc = m->alloc(&m->b_err, 4))) return rc;
+  if ((rc = m->alloc(&m->b_final_act, (size_t)kBatchSeqMax * kHidden))) return rc;
+  if ((rc = m->alloc(&m->b_lm_bt, (size_t)kBtRows * kHidden))) return rc;
+  if ((rc = m->alloc(&m->b_lm_shard_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
+  const size_t sp = (size_t)kBatchSeqMax * kQHeads * m->cfg.max_context;
+  if ((rc = m->alloc(&m->b_att_S, sp))) return rc;
+  if ((rc = m->alloc(&m->b_att_P, sp))) return rc;
+  if ((rc = m->alloc(&m->b_att_M, (size_t)kBatchSeqMax * kQHeads))) return rc;
+  if ((rc = m->alloc(&m->b_att_O, (size_t)kBatchSeqMax * kQHeads * kHeadDim))) return rc;
+  if ((rc = m->alloc(&m->b_att_cnt, (size_t)2 * kBatchSeqMax * kKvHeads))) return rc;
+  {
+    std::vector<int64_t> armed((size_t)kBatchSeqMax * kQHeads, INT64_MIN);
+    if ((rc = stream_copy(m, m->b_att_M, armed.data(), armed.size() * 8, cudaMemcpyHostToDevice))) return rc;
+  }
+  Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
+  for (int l = 0; l < L; ++l) {
+    const LayerW& q = m->layers[l];
+    BatchLayerW& b = m->b_layers[l];
+    b.sqkv = q.sqkv;
+    b.so = q.so;
+    b.sgate = q.sgate;
+    b.sup = q.sup;
+    b.sdown = q.sdown;
+    b.g_in = q.g_in;
+    b.g_post = q.g_post;
+    b.g_q = q.g_q;
+    b.g_k = q.g_k;
+    if ((rc = q4gpu_encode_q4_map(&b.mqkv, q.wqkv, kHidden / 2, kQRows + 2 * kKvRows)) ||
+        (rc = q4gpu_encode_q4_map(&b.mo, q.wo, kHidden, kHidden)) ||
+        (rc = q4gpu_encode_q4_map(&b.mgate, q.wgate, kHidden / 2, kInter)) ||
+        (rc = q4gpu_encode_q4_map(&b.mup, q.wup, kHidden / 2, kInter)) ||
+        (rc = q4gpu_encode_q4_map(&b.mdown, q.wdown, kInter / 2, kHidden)))
       return rc;
-    if ((rc = m->alloc(&m->b_lm_from, (size_t)m->cfg.max_seqs))) return rc;
-    if ((rc = m->alloc(&m->b_lm_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
-    if ((rc = m->alloc(&m->b_io, (size_t)kBatchSeqMax * 6))) return rc;
-    if ((rc = m->alloc(&m->b_err, 4))) return rc;
-    if ((rc = m->alloc(&m->b_final_act, (size_t)kBatchSeqMax * kHidden))) return rc;
-    if ((rc = m->alloc(&m->b_lm_bt, (size_t)kBtRows * kHidden))) return rc;
-    if ((rc = m->alloc(&m->b_lm_shard_part, (size_t)batch_lm_ctas(m->cfg.vocab) * kBatchSeqMax))) return rc;
-    const size_t sp = (size_t)kBatchSeqMax * kQHeads * m->cfg.max_context;
-    if ((rc = m->alloc(&m->b_att_S, sp))) return rc;
-    if ((rc = m->alloc(&m->b_att_P, sp))) return rc;
-    if ((rc = m->alloc(&m->b_att_M, (size_t)kBatchSeqMax * kQHeads))) return rc;
-    if ((rc = m->alloc(&m->b_att_O, (size_t)kBatchSeqMax * kQHeads * kHeadDim))) return rc;
-    if ((rc = m->alloc(&m->b_att_cnt, (size_t)2 * kBatchSeqMax * kKvHeads))) return rc;
-    {
-      std::vector<int64_t> armed((size_t)kBatchSeqMax * kQHeads, INT64_MIN);
-      if ((rc = stream_copy(m, m->b_att_M, armed.data(), armed.size() * 8, cudaMemcpyHostToDevice))) return rc;
-    }
-    Q4_CUDA(cudaMallocHost(&m->h_bio, (size_t)kBatchSeqMax * 6 * sizeof(int32_t)));
-    for (int l = 0; l < L; ++l) {
-      int8_t* w = m->b_w8 + kB8Layer * l;
-      const LayerW& q = m->layers[l];
-      BatchLayerW& b = m->b_layers[l];
-      b.wqkv = w;
-      b.sqkv = q.sqkv;
-      b.wo = w + kB8Qkv;
-      b.so = q.so;
-      b.wgu = w + kB8Qkv + kB8O;
-      b.sgu = m->b_sgu + (size_t)2 * kInter * (kHidden / kGroup) * l;
-      b.wdown = w + kB8Qkv + kB8O + kB8Gu;
-      b.sdown = q.sdown;
-      b.g_in = q.g_in;
-      b.g_post = q.g_post;
-      b.g_q = q.g_q;
-      b.g_k = q.g_k;
-      if ((rc = q4gpu_encode_u8_map(&b.mqkv, b.wqkv, kHidden, kQRows + 2 * kKvRows, 128)) ||
-          (rc = q4gpu_encode_u8_map(&b.mo, b.wo, 2 * kHidden, kHidden, 128)) ||
-          (rc = q4gpu_encode_u8_map(&b.mgu, b.wgu, kHidden, 2 * kInter, 128)) ||
-          (rc = q4gpu_encode_u8_map(&b.mdown, b.wdown, kInter, kHidden, 128)))
-        return rc;
-    }
-    if ((rc = q4gpu_encode_u8_map(&m->b_mlm, m->b_emb8, kHidden, (uint64_t)m->cfg.vocab, 128))) return rc;
   }
-  if (m->b_stale) {
-    for (int l = 0; l < L; ++l) {
-      const LayerW& q = m->layers[l];
-      BatchLayerW& b = m->b_layers[l];
-      if ((rc = q4gpu_expand_int4(q.wqkv, (int64_t)kB8Qkv / 2, const_cast<int8_t*>(b.wqkv), m->stream))) return rc;
-      if ((rc = q4gpu_expand_int4(q.wo, (int64_t)kB8O / 2, const_cast<int8_t*>(b.wo), m->stream))) return rc;
-      if ((rc = q4gpu_expand_gu(q.wgate, q.wup, q.sgate, q.sup, const_cast<int8_t*>(b.wgu),
-                                const_cast<uint16_t*>(b.sgu), m->stream)))
-        return rc;
-      if ((rc = q4gpu_expand_int4(q.wdown, (int64_t)kB8Down / 2, const_cast<int8_t*>(b.wdown), m->stream))) return rc;
-    }
-    if ((rc = q4gpu_expand_int4(m->emb, (int64_t)m->cfg.vocab * (kHidden / 2), m->b_emb8, m->stream))) return rc;
-    m->b_stale = false;
-  }
+  if ((rc = q4gpu_encode_q4_map(&m->b_mlm, m->emb, kHidden / 2, (uint64_t)m->cfg.vocab))) return rc;
+  m->b_ready = true;
   return Q4GPU_OK;
 }
 
@@ -946,7 +919,6 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.lm_from = m->b_lm_from + first;
   p.emb = m->emb;
   p.semb = m->semb;
-  p.emb8 = m->b_emb8;
   p.layers = m->b_layers;
   p.n_layers = m->cfg.n_layers;
   p.max_ctx = m->cfg.max_context;
@@ -968,17 +940,20 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.att_cnt_s = m->b_att_cnt;
   p.att_cnt_v = m->b_att_cnt + kBatchSeqMax * kKvHeads;
   p.mlm = m->b_mlm;
+  // limb boxes of each GEMM's sequence chunk (kinds: 0 q/k/v, 1 o_proj, 2 gate/up, 3 down, 4 LM head)
   const uint64_t nrows = (uint64_t)q4gpu_batch_limb_rows(p.SP);
-  const uint32_t box = (uint32_t)q4gpu_batch_box_rows(p.SP);
+  auto box = [&](int kind) { return (uint32_t)q4gpu_batch_gemm_chunk(kind, p.SP); };
   int rc;
-  if ((rc = q4gpu_encode_u8_map(&p.mb1, p.bt1, kHidden, nrows, box)) ||
-      (rc = q4gpu_encode_u8_map(&p.mb2, p.bt2, 2 * kHidden, nrows, box)) ||
-      (rc = q4gpu_encode_u8_map(&p.mb3, p.bt3, kInter, nrows, box)))
+  if ((rc = q4gpu_encode_u8_map(&p.mb_qkv, p.bt1, kHidden, nrows, box(0))) ||
+      (rc = q4gpu_encode_u8_map(&p.mb_o, p.bt2, 2 * kHidden, nrows, box(1))) ||
+      (rc = q4gpu_encode_u8_map(&p.mb_gu, p.bt1, kHidden, nrows, box(2))) ||
+      (rc = q4gpu_encode_u8_map(&p.mb_down, p.bt3, kInter, nrows, box(3))) ||
+      (rc = q4gpu_encode_u8_map(&p.mb_lm, p.bt1, kHidden, nrows, box(4))))
     return rc;
   return Q4GPU_OK;
 }
 
-// Prefill buffers and maps, once per model (64-column GEMMs; ones rows at 3 * 64).
+// Prefill buffers and maps, once per model (64-column GEMMs, 192 limb rows per sub-batch).
 int prefill_prepare(q4gpu_model* m) {
   if (m->pf) return Q4GPU_OK;
   int rc;
@@ -988,7 +963,7 @@ int prefill_prepare(q4gpu_model* m) {
     attrs = true;
   }
   auto p = std::make_unique<PrefillPlan>();
-  const size_t rows = (size_t)q4gpu_batch_box_rows(kPfSub);  // 208: limb rows, ones rows, zero rows
+  const size_t rows = (size_t)kPfSubRows;  // 192 limb rows per 64-column sub-batch
   constexpr int nsub = kPfBlock / kPfSub;
   if ((rc = m->alloc(&p->hidden, (size_t)kPfBlock * kHidden)) || (rc = m->alloc(&p->post, (size_t)kPfBlock * kHidden)) ||
       (rc = m->alloc(&p->qkv, (size_t)kPfBlock * (kQRows + 2 * kKvRows))) ||
@@ -996,15 +971,10 @@ int prefill_prepare(q4gpu_model* m) {
       (rc = m->alloc(&p->bt3, nsub * rows * kInter)) ||
       (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * ((m->cfg.max_context + 63) / 64 * 64))))
     return rc;
-  for (int sub = 0; sub < nsub; ++sub) {
-    Q4_CUDA(cudaMemsetAsync(p->bt1 + (sub * rows + 3 * kPfSub) * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
-    Q4_CUDA(cudaMemsetAsync(p->bt2 + (sub * rows + 3 * kPfSub) * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden,
-                            m->stream));
-    Q4_CUDA(cudaMemsetAsync(p->bt3 + (sub * rows + 3 * kPfSub) * kInter, 1, (size_t)kBatchOnes * kInter, m->stream));
-  }
-  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)rows)) ||
-      (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)rows)) ||
-      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, nsub * rows, (uint32_t)rows)))
+  // boxes of one limb of one 64-column sub-batch
+  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)kPfSub)) ||
+      (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)kPfSub)) ||
+      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, nsub * rows, (uint32_t)kPfSub)))
     return rc;
   p->emb = m->emb;
   p->semb = m->semb;
@@ -1106,11 +1076,13 @@ int batch_graph(q4gpu_model* m, int first, int S, cudaGraphExec_t* out, bool hid
   auto pp = std::make_unique<BatchPlan>();
   BatchPlan& p = *pp;
   if ((rc = batch_plan(m, first, S, p))) return rc;
-  if (m->b_ones_sp != p.SP) {
-    Q4_CUDA(cudaMemsetAsync(m->b_bt1 + (size_t)3 * p.SP * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
-    Q4_CUDA(cudaMemsetAsync(m->b_bt2 + (size_t)3 * p.SP * 2 * kHidden, 1, (size_t)kBatchOnes * 2 * kHidden, m->stream));
-    Q4_CUDA(cudaMemsetAsync(m->b_bt3 + (size_t)3 * p.SP * kInter, 1, (size_t)kBatchOnes * kInter, m->stream));
-    m->b_ones_sp = p.SP;
+  if (m->b_pad_sp != p.SP) {
+    // rows 3 SP .. 3 SP + 7 may hold limbs of a wider batch: the GEMMs read
+    // them (N rounds 3 SP up to 16) and need zeros there
+    Q4_CUDA(cudaMemsetAsync(m->b_bt1 + (size_t)3 * p.SP * kHidden, 0, (size_t)kBatchPad * kHidden, m->stream));
+    Q4_CUDA(cudaMemsetAsync(m->b_bt2 + (size_t)3 * p.SP * 2 * kHidden, 0, (size_t)kBatchPad * 2 * kHidden, m->stream));
+    Q4_CUDA(cudaMemsetAsync(m->b_bt3 + (size_t)3 * p.SP * kInter, 0, (size_t)kBatchPad * kInter, m->stream));
+    m->b_pad_sp = p.SP;
   }
   if (hidden_only) p.final_act = m->b_final_act;
   const auto key = std::make_tuple(first, S, hidden_only ? 1 : 0);
@@ -1324,7 +1296,6 @@ int q4gpu_model_init_synthetic(q4gpu_model* m, uint64_t seed, float std_dev, flo
   Q4_CUDA(cudaMalloc(&tmp, max_elems * sizeof(float)));
   Q4_CUDA(cudaMalloc(&err, sizeof(int32_t)));
   Q4_CUDA(cudaMemsetAsync(err, 0, sizeof(int32_t), m->stream));
-  m->b_stale = true;
   m->p_stale = true;
   auto gen_quant = [&](uint64_t tid, const TensorRef& t) -> int {
     int r = q4gpu_synth_f32(seed, tid, 0, t.rows * t.cols, std_dev, 1, tmp, m->stream);
@@ -1378,7 +1349,7 @@ static int tensor_io(q4gpu_model* m, int32_t layer, int32_t which, void* data, s
   int rc = set_device(m);
   if (rc) return rc;
   const cudaMemcpyKind kind = to_device ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
-  if (to_device) m->b_stale = m->p_stale = true;
+  if (to_device) m->p_stale = true;
   auto cp = [&](void* dev, void* host, size_t n) -> int {
     return to_device ? stream_copy(m, dev, host, n, kind) : stream_copy(m, host, dev, n, kind);
   };
@@ -1710,9 +1681,9 @@ int q4gpu_lm_head_shard(q4gpu_model* m, const int32_t* acts, int32_t n_act, int3
   if (rc) return rc;
   if ((rc = batch_prepare(m))) return rc;
   const int SP = q4gpu_batch_padded(n_act);
-  if (m->b_lm_ones_sp != SP) {
-    Q4_CUDA(cudaMemsetAsync(m->b_lm_bt + (size_t)3 * SP * kHidden, 1, (size_t)kBatchOnes * kHidden, m->stream));
-    m->b_lm_ones_sp = SP;
+  if (m->b_lm_pad_sp != SP) {
+    Q4_CUDA(cudaMemsetAsync(m->b_lm_bt + (size_t)3 * SP * kHidden, 0, (size_t)kBatchPad * kHidden, m->stream));
+    m->b_lm_pad_sp = SP;
   }
   auto q = std::make_unique<LmShardPlan>();
   q->acts = acts;
@@ -1725,10 +1696,9 @@ int q4gpu_lm_head_shard(q4gpu_model* m, const int32_t* acts, int32_t n_act, int3
   q->best_score = best_score;
   q->best_row = best_row;
   q->err = m->b_err;
-  if ((rc = q4gpu_encode_u8_map(&q->amap, m->b_emb8 + (size_t)row_begin * kHidden, kHidden,
-                                (uint64_t)(row_end - row_begin), 128)) ||
-      (rc = q4gpu_encode_u8_map(&q->bmap, m->b_lm_bt, kHidden, (uint64_t)q4gpu_batch_limb_rows(SP),
-                                (uint32_t)q4gpu_batch_box_rows(SP))))
+  if ((rc = q4gpu_encode_q4_map(&q->amap, m->emb + (size_t)row_begin * (kHidden / 2), kHidden / 2,
+                                (uint64_t)(row_end - row_begin))) ||
+      (rc = q4gpu_encode_u8_map(&q->bmap, m->b_lm_bt, kHidden, (uint64_t)q4gpu_batch_limb_rows(SP), (uint32_t)SP)))
     return rc;
   return q4gpu_enqueue_lm_shard(*q, m->stream);
 }

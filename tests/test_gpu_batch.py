@@ -171,3 +171,40 @@ def test_batch_full_model_matches_reference_golden(refmodel):
         for i in (1, 5):
             single, res = gm.decode(prompts[i], n_gen, slot=i)
             assert gen[i].tolist() == single and scores[i][-1] == res.score_q26
+
+
+def test_batch_gemm_wide_scales_take_two_passes():
+    """Group scales of 256 and above: the batched GEMMs split each scale into
+    4-bit digits and need a second pass over the weights for digits 2 and 3.
+    Layer 0's matrices get scales x 3 (up to ~700: three digits), layer 1's
+    down_proj x 300 and the LM head's first rows x 150 (four digits).  Batched
+    decode must equal the numpy oracle with the same widened scales, and the
+    single-sequence GEMV path."""
+    seed, n_layers, vocab, ctx = 5, 2, 4096, 64
+    om = O.Model(layers=[O.synth_layer(seed, li) for li in range(n_layers)], embed_q=None, embed_s=None,
+                 final_gamma=O.quantize_signed(np.ones(1024), 16, 7)[0])
+    om.embed_q, om.embed_s = O.quantize_weight_q4(O.synth_f32(seed, O.TID_EMBED, (vocab, 1024), 0.02))
+    om.cos, om.sin = O.rope_tables(ctx)
+    names = {_native.T_Q: "q", _native.T_K: "k", _native.T_V: "v", _native.T_O: "o", _native.T_GATE: "gate",
+             _native.T_UP: "up", _native.T_DOWN: "down"}
+    widen = [(0, w, 3) for w in names] + [(1, _native.T_DOWN, 300)]
+    with Q4Model(n_layers=n_layers, vocab=vocab, max_context=ctx, max_seqs=8) as gm:
+        gm.init_synthetic(seed=seed)
+        for layer, which, f in widen:
+            packed, scale = gm.get_weight(layer, which)
+            wide = np.minimum(scale.astype(np.int64) * f, 65535).astype(np.uint16)
+            gm.set_weight(layer, which, packed, wide)
+            setattr(om.layers[layer], names[which] + "_s", wide)
+        packed, scale = gm.get_weight(0, _native.T_EMBED)
+        scale = scale.astype(np.int64)
+        scale[:300] = np.minimum(scale[:300] * 150, 65535)
+        gm.set_weight(0, _native.T_EMBED, packed, scale.astype(np.uint16))
+        om.embed_s = scale.astype(np.uint16)
+        assert om.layers[1].down_s.max() >= 4096 and om.layers[0].q_s.max() >= 256
+        prompts = [[1, 2, 3], [4000, 17], [250, 251, 7, 9]]
+        gen, scores = gm.decode_batch(prompts, 4)
+        for i, p in enumerate(prompts):
+            ref, ref_scores = O.greedy_decode(om, p, 4, max_ctx=ctx)
+            assert gen[i].tolist() == ref and scores[i].tolist() == ref_scores, i
+            single, res = gm.decode(p, 4, slot=7)
+            assert single == ref and res.score_q26 == ref_scores[-1], i
