@@ -176,11 +176,17 @@ struct AttnScratch {
   int max_ctx;
 };
 
+// Bulk copy global -> shared of K/V rows.  The cache streams through L2 once
+// per step (GBs against a 126 MB L2), so its lines are marked evict-first:
+// the weights the GEMMs prefetch into L2 stay there.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   umma::smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(umma::smem_addr(bar))
-               : "memory");
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          umma::smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(umma::smem_addr(bar)), "l"(pol)
+      : "memory");
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -750,6 +756,32 @@ struct UCfg {
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
+// Up to four byte ranges (16-byte aligned, sizes multiples of 16) that the
+// CTAs of a launch prefetch into L2 between them, marked evict-last.
+struct L2Prefetch {
+  const void* p[4];
+  uint32_t bytes[4];
+};
+
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  const uint32_t n = gridDim.x * gridDim.y * gridDim.z;
+  const uint32_t i = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    if (!pf.p[r]) continue;
+    const uint32_t chunk = ((pf.bytes[r] + n - 1) / n + 15u) & ~15u, off = i * chunk;
+    if (off < pf.bytes[r]) {
+      const uint32_t len = pf.bytes[r] - off < chunk ? pf.bytes[r] - off : chunk;
+      asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
+                       reinterpret_cast<const char*>(pf.p[r]) + off),
+                   "r"(len), "l"(pol)
+                   : "memory");
+    }
+  }
+}
+
 struct UGemm {
   BatchCtx c;
   const uint16_t* scales;   // [rows, K / 64]; gate/up: the gate rows' scales
@@ -763,6 +795,7 @@ struct UGemm {
   const int32_t* sig_lut;
   ArgBestD* partial;        // LM head: [tiles, 64]
   unsigned long long* trace;  // optional: [CTA][8] %globaltimer stamps of this launch (nullptr = off)
+  L2Prefetch pf;            // the next GEMM's weights, pulled into L2 while this one runs
 };
 
 // GEMM timeline points: 0 entry, 1 set-up done, 2 dependency released (TMA
@@ -884,6 +917,33 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
   }
   if (warp == 1) umma::tmem_alloc(tmem_slot, C::TCOLS);
+  // plane builders (warps 2-17): builder et takes chunk cc (16 K values) of
+  // rows r0 and r0 + 64 in every K tile; their group scales, all K tiles, load
+  // into registers now (they do not depend on earlier kernels)
+  const int et = threadIdx.x - 64;
+  const int r0 = (et >> 3) & 63, cc = et & 7;
+  uint32_t sc2[kUMaxKt];  // scale of row r0 (low half) and r0 + 64 (high half) per K tile
+  bool wide = false;      // a scale of this tile needs more than 8 bits
+  if (warp >= 2) {
+    const uint16_t* s_lo;
+    const uint16_t* s_hi;
+    if constexpr (KIND == kGemmGu) {
+      s_lo = g.scales + (size_t)(tile * 64 + r0) * G;
+      s_hi = g.scales2 + (size_t)(tile * 64 + r0) * G;
+    } else {
+      const int ga = row0 + r0 < g.rows ? row0 + r0 : g.rows - 1;
+      const int gb = row0 + r0 + 64 < g.rows ? row0 + r0 + 64 : g.rows - 1;
+      s_lo = g.scales + (size_t)ga * G;
+      s_hi = g.scales + (size_t)gb * G;
+    }
+    const int gq = 2 * kt0 + (cc >> 2);
+#pragma unroll
+    for (int kt = 0; kt < kUMaxKt; ++kt) {
+      const uint32_t a = kt < nkt ? s_lo[gq + 2 * kt] : 0u, b = kt < nkt ? s_hi[gq + 2 * kt] : 0u;
+      sc2[kt] = a | (b << 16);
+      wide |= (a | b) > 255u;
+    }
+  }
   if constexpr (C::NM > 3 * SN) {
     // limb-tile rows past the chunk's 3 SN are read by the MMA: zeros
     constexpr int pad = (C::NM - 3 * SN) * 128 / 16;
@@ -918,7 +978,6 @@ __global__ void __launch_bounds__(kUThreads, 1)
       gemm_stamp(g, 2);
       int nv = nkt;
       for (int v = 0; v < nv && !*abort_flag; ++v) {
-        if (v == nkt - 1) nv = passes() * nkt;
         const int kt = v % nkt;
         if (v >= pre_a) {
           const int s = v % SA;
@@ -942,6 +1001,8 @@ __global__ void __launch_bounds__(kUThreads, 1)
 #pragma unroll
         for (int limb = 0; limb < 3; ++limb)
           umma::tma_load(bdst + limb * SN * 128, &bmap, (kt0 + kt) * 128, y0 + limb * SP, full_b + sb);
+        // the first pass's loads are all issued: does the tile need a second?
+        if (v == nkt - 1) nv = passes() * nkt;
       }
     } else {
       grid_dep_wait();
@@ -978,34 +1039,12 @@ __global__ void __launch_bounds__(kUThreads, 1)
           if (v == nv - 1) gemm_stamp(g, 7);
         }
       }
+      // all MMAs issued: this thread is free to pull the next GEMM's weights into L2
+      l2_prefetch_share(g.pf);
     }
   } else {
     // ---- plane builders (warps 2-17), then the epilogue ---------------------
-    // builder et takes chunk cc (16 K values) of rows r0 and r0 + 64 in every
-    // K tile; their group scales, all K tiles, in registers
-    const int et = threadIdx.x - 64;
-    const int r0 = et >> 3, cc = et & 7;
-    uint32_t sc2[kUMaxKt];  // scale of row r0 (low half) and r0 + 64 (high half) per K tile
     {
-      const uint16_t* s_lo;
-      const uint16_t* s_hi;
-      if constexpr (KIND == kGemmGu) {
-        s_lo = g.scales + (size_t)(tile * 64 + r0) * G;
-        s_hi = g.scales2 + (size_t)(tile * 64 + r0) * G;
-      } else {
-        const int ga = row0 + r0 < g.rows ? row0 + r0 : g.rows - 1;
-        const int gb = row0 + r0 + 64 < g.rows ? row0 + r0 + 64 : g.rows - 1;
-        s_lo = g.scales + (size_t)ga * G;
-        s_hi = g.scales + (size_t)gb * G;
-      }
-      const int gq = 2 * kt0 + (cc >> 2);
-      bool wide = false;  // a scale of this tile needs more than 8 bits
-#pragma unroll
-      for (int kt = 0; kt < kUMaxKt; ++kt) {
-        const uint32_t a = kt < nkt ? s_lo[gq + 2 * kt] : 0u, b = kt < nkt ? s_hi[gq + 2 * kt] : 0u;
-        sc2[kt] = a | (b << 16);
-        wide |= (a | b) > 255u;
-      }
       if (__any_sync(0xFFFFFFFFu, wide) && lane == 0) atomicOr(wide_any, 1);
       __syncwarp();
       if (lane == 0) umma::bar_arrive(scales_in);
@@ -2165,7 +2204,7 @@ template <int SN, int KIND>
 cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& amap2, const CUtensorMap& bmap, const BatchCtx& c,
                         const uint16_t* scales, const uint16_t* scales2, int rows, int K, int splits, int SP,
                         const int32_t* sig_lut, ArgBestD* partial, cudaStream_t s, unsigned long long* trace,
-                        int subs, int b_sub_rows) {
+                        int subs, int b_sub_rows, L2Prefetch pf = L2Prefetch{}) {
   // the epilogue's row bookkeeping uses shifts: splits must be 1, 2, 4 or 8;
   // a CTA holds the scales of at most kUMaxKt K tiles
   if (splits < 1 || splits > 8 || (splits & (splits - 1)) || K % (128 * splits) || K / splits > 128 * kUMaxKt ||
@@ -2173,7 +2212,7 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& amap2, const
     return cudaErrorInvalidValue;
   // O / down stage their residual rows (128 / splits of them) in 64 rows' room
   if ((KIND == kGemmO || KIND == kGemmDown) && splits < 2) return cudaErrorInvalidValue;
-  UGemm g{c, scales, scales2, rows, K, K / 128 / splits, SP, SP / SN, b_sub_rows, sig_lut, partial, trace};
+  UGemm g{c, scales, scales2, rows, K, K / 128 / splits, SP, SP / SN, b_sub_rows, sig_lut, partial, trace, pf};
   const dim3 grid((unsigned)(subs * (SP / SN)), (unsigned)splits, (unsigned)((rows + 127) / 128));
   return launch_ex(umma_gemm_kernel<SN, KIND>, grid, dim3(kUThreads), UCfg<SN, KIND>::SMEM, s, splits, amap, amap2,
                    bmap, g);
@@ -2190,6 +2229,25 @@ cudaError_t launch_gemm_sn(int sn, Args... args) {
     case 64: return launch_gemm<64, KIND>(args...);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// The weights of a layer's GEMMs, for the L2 prefetch issued one GEMM ahead:
+// q/k/v prefetches o_proj (past the attention, whose K/V loads are
+// evict-first), o_proj gate/up, gate/up down, down the next layer's q/k/v.
+L2Prefetch pf_qkv(const BatchLayerW& w) {
+  return L2Prefetch{{w.wqkv, w.sqkv, nullptr, nullptr},
+                    {(uint32_t)(kQRows + 2 * kKvRows) * kHidden / 2, (uint32_t)(kQRows + 2 * kKvRows) * kHidden / 32, 0, 0}};
+}
+L2Prefetch pf_o(const BatchLayerW& w) {
+  return L2Prefetch{{w.wo, w.so, nullptr, nullptr}, {(uint32_t)kHidden * kHidden, (uint32_t)kHidden * kHidden / 16, 0, 0}};
+}
+L2Prefetch pf_gu(const BatchLayerW& w) {
+  return L2Prefetch{{w.wgate, w.wup, w.sgate, w.sup},
+                    {(uint32_t)kInter * kHidden / 2, (uint32_t)kInter * kHidden / 2, (uint32_t)kInter * kHidden / 32,
+                     (uint32_t)kInter * kHidden / 32}};
+}
+L2Prefetch pf_down(const BatchLayerW& w) {
+  return L2Prefetch{{w.wdown, w.sdown, nullptr, nullptr}, {(uint32_t)kHidden * kInter / 2, (uint32_t)kHidden * kInter / 32, 0, 0}};
 }
 
 // K splits of each GEMM of a decode step (a cluster of that many CTAs per row
@@ -2249,7 +2307,8 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BMARK(kBkNorm);
     BQ(launch_gemm_sn<kGemmQkv>(q4gpu_batch_gemm_chunk(kGemmQkv, SP), w.mqkv, w.mqkv, p.mb_qkv, c, w.sqkv,
                                 (const uint16_t*)nullptr, kQRows + 2 * kKvRows, kHidden, decode_splits(kGemmQkv, SP),
-                                SP, (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 0), 1, 0));
+                                SP, (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 0), 1, 0,
+                                pf_o(w)));
     BMARK(kBkQkv);
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
@@ -2265,17 +2324,18 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BMARK(kBkAttn);
     BQ(launch_gemm_sn<kGemmO>(q4gpu_batch_gemm_chunk(kGemmO, SP), w.mo, w.mo, p.mb_o, c, w.so,
                               (const uint16_t*)nullptr, kHidden, 2 * kHidden, decode_splits(kGemmO, SP), SP,
-                              (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 1), 1, 0));
+                              (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 1), 1, 0, pf_gu(w)));
     BMARK(kBkO);
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
     BMARK(kBkNorm);
     BQ(launch_gemm_sn<kGemmGu>(q4gpu_batch_gemm_chunk(kGemmGu, SP), w.mgate, w.mup, p.mb_gu, c, w.sgate, w.sup,
                                2 * kInter, kHidden, decode_splits(kGemmGu, SP), SP, p.sig_lut, (ArgBestD*)nullptr, s,
-                               gtrace(4 * l + 2), 1, 0));
+                               gtrace(4 * l + 2), 1, 0, pf_down(w)));
     BMARK(kBkGu);
     BQ(launch_gemm_sn<kGemmDown>(q4gpu_batch_gemm_chunk(kGemmDown, SP), w.mdown, w.mdown, p.mb_down, c, w.sdown,
                                  (const uint16_t*)nullptr, kHidden, kInter, decode_splits(kGemmDown, SP), SP,
-                                 (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 3), 1, 0));
+                                 (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 3), 1, 0,
+                                 l + 1 < p.n_layers ? pf_qkv(p.layers[l + 1]) : L2Prefetch{}));
     BMARK(kBkDown);
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final, p.final_act));
@@ -2455,19 +2515,20 @@ int q4gpu_enqueue_prefill_block(const PrefillPlan& p, cudaStream_t s) {
     const BatchLayerW& w = p.layers[l];
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
     BQ((launch_gemm<kPfSub, kGemmQkv>(w.mqkv, w.mqkv, p.mb1, c, w.sqkv, nullptr, kRow, kHidden, kPfSplitQkv, kPfSub,
-                                      nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
+                                      nullptr, nullptr, s, nullptr, nsub, kPfSubRows, pf_o(w))));
     BQ(launch_pdl(prefill_qk_kernel, dim3(kKvHeads, p.n_cols), dim3(128), 0, s, p.col_slots, p.col_pos4, p.qkv, l,
                   w.g_q, w.g_k, p.cos_tab, p.sin_tab));
     const PfAttn a{p.tiles, p.col_slots, p.qkv, p.bt2, nb * 2 * kHidden, p.lut_idx, (p.max_ctx + 63) / 64 * 64, l,
                    p.exp_lut, p.err};
     BQ(launch_pdl(prefill_attn_kernel, dim3(kKvHeads, p.n_tiles), dim3(kPfThreads), kPfSmem, s, a));
     BQ((launch_gemm<kPfSub, kGemmO>(w.mo, w.mo, p.mb2, c, w.so, nullptr, kHidden, 2 * kHidden, kPfSplitO, kPfSub,
-                                    nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
+                                    nullptr, nullptr, s, nullptr, nsub, kPfSubRows, pf_gu(w))));
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.n_cols), dim3(256), 0, s, c, 1, w.g_post, (int32_t*)nullptr));
     BQ((launch_gemm<kPfSub, kGemmGu>(w.mgate, w.mup, p.mb1, c, w.sgate, w.sup, 2 * kInter, kHidden, kPfSplitGu,
-                                     kPfSub, p.sig_lut, nullptr, s, nullptr, nsub, kPfSubRows)));
+                                     kPfSub, p.sig_lut, nullptr, s, nullptr, nsub, kPfSubRows, pf_down(w))));
     BQ((launch_gemm<kPfSub, kGemmDown>(w.mdown, w.mdown, p.mb3, c, w.sdown, nullptr, kHidden, kInter, kPfSplitDown,
-                                       kPfSub, nullptr, nullptr, s, nullptr, nsub, kPfSubRows)));
+                                       kPfSub, nullptr, nullptr, s, nullptr, nsub, kPfSubRows,
+                                       l + 1 < p.n_layers ? pf_qkv(p.layers[l + 1]) : L2Prefetch{})));
   }
   return Q4GPU_OK;
 }

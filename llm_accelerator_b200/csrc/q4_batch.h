@@ -18,6 +18,11 @@ struct BatchLayerW {
   CUtensorMap mgate;             // [3072, 512]
   CUtensorMap mup;               // [3072, 512]
   CUtensorMap mdown;             // [1024, 1536]
+  const uint8_t* wqkv;           // the packed matrices the maps address
+  const uint8_t* wo;
+  const uint8_t* wgate;
+  const uint8_t* wup;
+  const uint8_t* wdown;
   const uint16_t* sqkv;          // [4096, 16]
   const uint16_t* so;            // [1024, 32]
   const uint16_t* sgate;         // [3072, 16]

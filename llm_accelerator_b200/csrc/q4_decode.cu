@@ -886,6 +886,11 @@ int batch_prepare(q4gpu_model* m) {
   for (int l = 0; l < L; ++l) {
     const LayerW& q = m->layers[l];
     BatchLayerW& b = m->b_layers[l];
+    b.wqkv = q.wqkv;
+    b.wo = q.wo;
+    b.wgate = q.wgate;
+    b.wup = q.wup;
+    b.wdown = q.wdown;
     b.sqkv = q.sqkv;
     b.so = q.so;
     b.sgate = q.sgate;
