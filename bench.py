@@ -688,6 +688,13 @@ def run_ours(args, ws, rank, local):
                 n = min(len(c["tokens"]), len(toks0))
                 line["parity"] = "sequence 0 tokens identical to the CPU oracle" if c["tokens"][:n] == toks0[:n] \
                     else f"MISMATCH gpu={toks0[:n]} cpu={c['tokens'][:n]}"
+    if ws > 1:
+        # config 5 across the same process group: the one collective on this
+        # path (the vocabulary-sharded LM head's exchanges), measured per N
+        c5 = cfg5_sharded(ws, rank, local, 16, 3)
+        if rank == 0:
+            line["cfg5"] = c5
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
         barrier()
@@ -702,19 +709,20 @@ def run_ours(args, ws, rank, local):
 # ---------------------------------------------------------------------------
 
 
-def run_cfg5(args, ws, rank, local):
+def cfg5_sharded(ws: int, rank: int, local: int, steps: int, warmup: int) -> dict:
+    """Config 5 over the process group: the 8 sequences split over the ranks and,
+    for N > 1, the tied LM head vocabulary-sharded (llm_accelerator_b200.sharding:
+    NCCL all_gather of the final vectors and of the (score, row) winners, one
+    reduce-and-commit kernel), the whole step replayed as one CUDA graph.  Steps
+    are timed on the device, max over ranks; the two collectives alone are timed
+    the same way on the same buffers (`exchange_us_per_step`)."""
     import torch
+    import torch.distributed as dist
 
     from llm_accelerator_b200.model import Q4Model
     from llm_accelerator_b200.sharding import VocabShardedDecoder, max_over_ranks, shard_range
 
-    torch.cuda.set_device(local)
-    dist = None
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
     if CFG5_SEQS % ws:
         raise SystemExit("config 5 needs a GPU count dividing 8")
     a, b = shard_range(CFG5_SEQS, ws, rank)
@@ -723,11 +731,18 @@ def run_cfg5(args, ws, rank, local):
     m = Q4Model(n_layers=LAYERS, vocab=VOCAB, max_context=CFG5_PROMPT + CFG5_GEN, max_seqs=n_local, device=local)
     m.init_synthetic(seed=0)
     stream = torch.cuda.ExternalStream(m.stream)
+    if ws > 1:
+        dist.barrier()
     t0 = time.perf_counter()
     m.decode_batch(prompts, 1)  # batched prefill; the first generated token of each sequence
-    prefill_s = max_over_ranks(time.perf_counter() - t0, device=torch.device("cuda", local))
-    steps = min(args.steps, CFG5_GEN - 1)
+    prefill_s = max_over_ranks(time.perf_counter() - t0, device=dev)
+    steps = min(steps, CFG5_GEN - 1)
     dec = VocabShardedDecoder(m, n_local) if ws > 1 else None
+    graphed = False
+    if dec is not None:
+        dec.step()  # eager: communicators, buffers, the forward graph
+        m.sync()
+        graphed = dec.capture()
 
     def run(n):
         for _ in range(n):
@@ -736,10 +751,10 @@ def run_cfg5(args, ws, rank, local):
             else:
                 m.batch_steps(1, n_local)
 
-    run(min(args.warmup, 4))
+    run(max(warmup, 3))
     m.batch_set_position(CFG5_PROMPT, n_local)
     m.sync()
-    if dist is not None:
+    if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -747,23 +762,56 @@ def run_cfg5(args, ws, rank, local):
     run(steps)
     e1.record(stream)
     e1.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), device=torch.device("cuda", local))
+    ms = max_over_ranks(e0.elapsed_time(e1), device=dev)
     toks = m.read_tokens(CFG5_PROMPT, 4, slot=0)[0].tolist()
-    if rank == 0:
-        line = {
-            "metric": "decode tokens/sec (config 5: batch 8, context 8192..)", "value": round(CFG5_SEQS * steps / (ms / 1000), 2),
-            "unit": UNIT, "n_gpus": ws, "steps": steps, "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
-            "scaling": "strong", "dtype": "int64", "data": "synthetic",
-            "config": {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (batched exact prefill), greedy "
-                                   "decode from position 8192", "sequences_per_gpu": n_local,
-                       "lm_head": f"vocabulary-sharded over {ws} GPUs, NCCL all_gather of vectors and (score, row) "
-                                  "winners" if ws > 1 else "full vocabulary on one GPU"},
-            "prefill_s": round(prefill_s, 2),
-            "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
-            "first_tokens_seq0": toks,
-        }
-        print(json.dumps(line), flush=True)
+    exch_us = None
+    if dec is not None:
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                dist.all_gather_into_tensor(dec.all_acts, dec.acts)
+                dist.all_gather_into_tensor(dec.win, dec.mine)
+            x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            x0.record(stream)
+            for _ in range(20):
+                dist.all_gather_into_tensor(dec.all_acts, dec.acts)
+                dist.all_gather_into_tensor(dec.win, dec.mine)
+            x1.record(stream)
+        x1.synchronize()
+        exch_us = max_over_ranks(1000.0 * x0.elapsed_time(x1) / 20, device=dev)
+        dec.release()
     m.close()
+    out = {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (seeds 50000..), batched exact prefill, "
+                       "greedy decode from position 8192", "n_gpus": ws, "sequences_per_gpu": n_local,
+           "value": round(CFG5_SEQS * steps / (ms / 1000), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
+           "steps": steps, "scaling": "strong", "prefill_s": round(prefill_s, 3),
+           "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
+           "lm_head": (f"vocabulary-sharded over {ws} GPUs: NCCL all_gather of the final vectors and of the (score, "
+                       "row) winners, q4gpu_batch_commit_shards, step " + ("replayed as one CUDA graph" if graphed
+                                                                          else "enqueued eagerly"))
+           if ws > 1 else "full vocabulary on one GPU",
+           "first_tokens_seq0": toks}
+    if exch_us is not None:
+        out["exchange_us_per_step"] = round(exch_us, 2)
+    return out
+
+
+def run_cfg5(args, ws, rank, local):
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    r = cfg5_sharded(ws, rank, local, args.steps, args.warmup)
+    if rank == 0:
+        line = {"metric": "decode tokens/sec (config 5: batch 8, context 8192..)", "higher_is_better": True,
+                "dtype": "int64", "data": "synthetic", **r,
+                "config": {"workload": r["workload"], "sequences_per_gpu": r["sequences_per_gpu"],
+                           "lm_head": r["lm_head"]}}
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -459,6 +459,15 @@ int q4gpu_batch_forward_hidden(q4gpu_model *m, int32_t first_slot, int32_t n_seq
 int q4gpu_lm_head_shard(q4gpu_model *m, const int32_t *acts, int32_t n_act, int32_t row_begin,
                         int32_t row_end, int64_t *best_score, int64_t *best_row);
 
+/* The shard winners' reduction and the commit in one launch: winners is the
+ * device int64 array an all_gather of every rank's [2][stride] (scores, rows)
+ * buffer produces, [n_shards][2][stride]; sequence i of this rank reads column
+ * col0 + i of every shard.  Highest score wins, the lowest row on ties (the
+ * reference's rule, exact whatever the shard order); the winner is stored like
+ * q4gpu_batch_commit stores tokens.  No reference counterpart. */
+int q4gpu_batch_commit_shards(q4gpu_model *m, int32_t first_slot, int32_t n_seq, const int64_t *winners,
+                              int32_t n_shards, int32_t stride, int32_t col0);
+
 /* Store tokens[i] (with scores[i]; int64 [n_seq]) at position + 1 of slot
  * first_slot + i (from its lm_from on) and advance the positions. */
 int q4gpu_batch_commit(q4gpu_model *m, int32_t first_slot, int32_t n_seq, const int64_t *tokens,

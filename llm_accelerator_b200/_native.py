@@ -131,6 +131,7 @@ SIGNATURES = {
     "q4gpu_batch_forward_hidden": (C.c_int, [P, I32, I32, P]),
     "q4gpu_lm_head_shard": (C.c_int, [P, P, I32, I32, I32, P, P]),
     "q4gpu_batch_commit": (C.c_int, [P, I32, I32, P, P]),
+    "q4gpu_batch_commit_shards": (C.c_int, [P, I32, I32, P, I32, I32, I32]),
     "q4gpu_batch_set_position": (C.c_int, [P, I32, I32, I32, I32]),
     "q4gpu_batch_run_step": (C.c_int, [P, I32, I32, P, P, P, P]),
     "q4gpu_batch_time_kernels": (C.c_int, [P, I32, I32, I32, P, P]),

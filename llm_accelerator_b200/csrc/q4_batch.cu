@@ -538,18 +538,24 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
       if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
       const int p = i * kAttnChunk + warp * 4 + quad;
       const int32_t* krow = p == pos ? hv[2] : ring + ((i % kAttnRing) * kAttnChunk + warp * 4 + quad) * kHeadDim;
-      int64_t s0 = 0, s1 = 0;
+      // two independent chains per head (even / odd dimensions) halve the
+      // multiply-add dependency chains
+      int64_t s0 = 0, s1 = 0, t0 = 0, t1 = 0;
       if (p < ctx) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * (sub + 8 * j));
-          const int32_t kk[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            s0 = mad_wide(q0[4 * j + e], kk[e], s0);
-            s1 = mad_wide(q1[4 * j + e], kk[e], s1);
-          }
+          s0 = mad_wide(q0[4 * j], k4.x, s0);
+          s1 = mad_wide(q1[4 * j], k4.x, s1);
+          t0 = mad_wide(q0[4 * j + 1], k4.y, t0);
+          t1 = mad_wide(q1[4 * j + 1], k4.y, t1);
+          s0 = mad_wide(q0[4 * j + 2], k4.z, s0);
+          s1 = mad_wide(q1[4 * j + 2], k4.z, s1);
+          t0 = mad_wide(q0[4 * j + 3], k4.w, t0);
+          t1 = mad_wide(q1[4 * j + 3], k4.w, t1);
         }
+        s0 += t0;
+        s1 += t1;
       }
       // the 8 lanes' partial sums: one exchange splits the heads (lanes
       // sub < 4 keep head 0, sub >= 4 head 1), two more finish each sum, so
@@ -1143,26 +1149,21 @@ __global__ void __launch_bounds__(kUThreads, 1)
       if (pass == 0 && warp == 2 && lane == 0) gemm_stamp(g, 3);
       // |T| < 120 * 255 * 1024 < 2^25 (K <= 1024 per CTA), so the two digits
       // of a limb combine in int32, X_i = T[0][i] + 16 T[1][i] (< 2^30), and
-      // the row sum is X_0 + 2^8 X_1 + 2^16 X_2: two widening multiply-adds
-      int32_t x0[C::Q], x1[C::Q];
+      // each limb adds X_i * 2^(8 i + 8 pass) with one widening multiply-add
+      // (TMEM is read in pieces of at most 8 columns: fewer live registers)
+      constexpr int kPiece = C::Q > 8 ? 8 : C::Q;
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
-        int32_t d0[C::Q], d1[C::Q];
-        const uint32_t ta = lane_base + (uint32_t)(i * SN + q * C::Q);
-        umma::tmem_ld_any<C::Q>(ta, d0);
-        umma::tmem_ld_any<C::Q>(ta + C::NM, d1);
-        umma::tmem_ld_wait();
+        const int32_t w = 1 << (8 * i + 8 * pass);
 #pragma unroll
-        for (int j = 0; j < C::Q; ++j) {
-          const int32_t x = d0[j] + 16 * d1[j];
-          if (i == 0) {
-            x0[j] = x;
-          } else if (i == 1) {
-            x1[j] = x;
-          } else {
-            const int64_t t = mad_wide(x, 65536, mad_wide(x1[j], 256, (int64_t)x0[j]));
-            acc[j] += pass ? t * 256 : t;
-          }
+        for (int j0 = 0; j0 < C::Q; j0 += kPiece) {
+          int32_t d0[kPiece], d1[kPiece];
+          const uint32_t ta = lane_base + (uint32_t)(i * SN + q * C::Q + j0);
+          umma::tmem_ld_any<kPiece>(ta, d0);
+          umma::tmem_ld_any<kPiece>(ta + C::NM, d1);
+          umma::tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < kPiece; ++j) acc[j0 + j] = mad_wide(d0[j] + 16 * d1[j], w, acc[j0 + j]);
         }
       }
       if (pass + 1 < npass) {
@@ -1216,7 +1217,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
     const int owner = (r & 63) >> (6 - lsp);
     const int local = (r >> 6) * rows_per + (r & (rows_per - 1));
     const int nl = 128 >> lsp;
-    // red[src][m][local]: a warp's 32 rows land contiguously
+    // red[src][m][local]: a warp's 32 rows land contiguously (conflict-free)
     int64_t* dst = red + ((size_t)split * SN + q * C::Q) * nl + local;
     if (splits == 1) {
       // (the LM head's row sums overwrite plane slots: every builder finished
@@ -1236,47 +1237,81 @@ __global__ void __launch_bounds__(kUThreads, 1)
     __syncthreads();
   if (threadIdx.x == 0) gemm_stamp(g, 5);
 
-  // final epilogue over the rows this CTA owns (local row l, sequence m of the
-  // chunk: item l + nl m; rows_per and nl are powers of two)
+  // final epilogue over the rows this CTA owns: work item (four consecutive
+  // local rows 4 lq .. 4 lq + 3, sequence m), which are four consecutive
+  // weight rows (rows_per >= 8): the split-K partial sums of each source CTA
+  // are two 16-byte shared loads, outputs one 16-byte global store
   const int lsp = __ffs(splits) - 1;
   const int lrp = 6 - lsp, rows_per = 64 >> lsp, lnl = 7 - lsp, nl = 128 >> lsp;
+  const int lq_bits = lnl - 2, nq = nl >> 2;  // row quads of the owned rows
   const int ft = threadIdx.x;
   auto row_of = [&](int local) {
     return ((local >> lrp) << 6) + split * rows_per + (local & (rows_per - 1));
   };
-  auto sum_of = [&](int local, int m) {
-    int64_t v = 0;
-    for (int src = 0; src < splits; ++src) v += red[((size_t)src * SN + m) * nl + local];
-    return v;
+  auto sums4 = [&](int local, int m, int64_t* v) {
+    v[0] = v[1] = v[2] = v[3] = 0;
+    for (int src = 0; src < splits; ++src) {
+      const longlong2* p = reinterpret_cast<const longlong2*>(red + ((size_t)src * SN + m) * nl + local);
+      const longlong2 a = p[0], b = p[1];
+      v[0] += a.x;
+      v[1] += a.y;
+      v[2] += b.x;
+      v[3] += b.y;
+    }
   };
   if (!*abort_flag) {
     if constexpr (KIND == kGemmQkv) {
-      for (int i = ft; i < nl * SN; i += kUThreads) {
-        const int local = i & (nl - 1), m = i >> lnl;
-        if (m < c.S)
-          c.qkv_raw[(size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)] = sat24(sum_of(local, m) >> 14);
+      for (int i = ft; i < nq * SN; i += kUThreads) {
+        const int local = 4 * (i & (nq - 1)), m = i >> lq_bits;
+        if (m >= c.S) continue;
+        int64_t v[4];
+        sums4(local, m, v);
+        *reinterpret_cast<int4*>(c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows) + row0 + row_of(local)) =
+            make_int4(sat24(v[0] >> 14), sat24(v[1] >> 14), sat24(v[2] >> 14), sat24(v[3] >> 14));
       }
     } else if constexpr (KIND == kGemmO || KIND == kGemmDown) {
-      // residual (staged in stg) + o_proj / down output >> 2
+      // residual (staged in stg: item local + nl m) + o_proj / down output >> 2
       int32_t* __restrict__ out = KIND == kGemmO ? c.post0 : c.hidden0;
-      for (int i = ft; i < nl * SN; i += kUThreads) {
-        const int local = i & (nl - 1), m = i >> lnl;
+      for (int i = ft; i < nq * SN; i += kUThreads) {
+        const int local = 4 * (i & (nq - 1)), m = i >> lq_bits;
         if (m >= c.S || !live[m]) continue;
-        const int32_t o = sat24(sum_of(local, m) >> 14);
-        out[(size_t)m * kHidden + row0 + row_of(local)] = sat24((int64_t)stg[i] + (o >> 2));
+        int64_t v[4];
+        sums4(local, m, v);
+        const int4 r = *reinterpret_cast<const int4*>(stg + m * nl + local);
+        *reinterpret_cast<int4*>(out + (size_t)m * kHidden + row0 + row_of(local)) =
+            make_int4(sat24((int64_t)r.x + (sat24(v[0] >> 14) >> 2)), sat24((int64_t)r.y + (sat24(v[1] >> 14) >> 2)),
+                      sat24((int64_t)r.z + (sat24(v[2] >> 14) >> 2)), sat24((int64_t)r.w + (sat24(v[3] >> 14) >> 2)));
       }
     } else if constexpr (KIND == kGemmGu) {
       // local rows 0 .. rows_per - 1 are gate rows, rows_per .. are the matching up rows
-      for (int i = ft; i < rows_per * SN; i += kUThreads) {
-        const int j = i & (rows_per - 1), m = i >> lrp;
+      const int jq_bits = lrp - 2, njq = rows_per >> 2;
+      for (int i = ft; i < njq * SN; i += kUThreads) {
+        const int j = 4 * (i & (njq - 1)), m = i >> jq_bits;
         if (m >= c.S || !live[m]) continue;
-        const int32_t gv = sat24(sum_of(j, m) >> 14), uv = sat24(sum_of(rows_per + j, m) >> 14);
-        const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
-        int ix = (gc + 32768 + 32) >> 6;
-        ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
-        const int32_t silu = sat24(((int64_t)gv * stg[ix]) >> 16);
-        const int32_t hv = sat24(((int64_t)silu * uv) >> 12);
-        write_limbs(c.bt3, SP, kInter, n0 + m, tile * 64 + split * rows_per + j, hv);
+        int64_t gs[4], us[4];
+        sums4(j, m, gs);
+        sums4(rows_per + j, m, us);
+        int32_t hv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int32_t gv = sat24(gs[e] >> 14), uv = sat24(us[e] >> 14);
+          const int32_t gc = gv < -32768 ? -32768 : (gv > 32768 ? 32768 : gv);
+          int ix = (gc + 32768 + 32) >> 6;
+          ix = ix > kSigLut - 1 ? kSigLut - 1 : ix;
+          const int32_t silu = sat24(((int64_t)gv * stg[ix]) >> 16);
+          hv[e] = sat24(((int64_t)silu * uv) >> 12);
+        }
+        // four consecutive intermediate columns: one 4-byte store per limb
+        const int col = tile * 64 + split * rows_per + j;
+        const uint32_t u[4] = {(uint32_t)(hv[0] + (1 << 23)), (uint32_t)(hv[1] + (1 << 23)),
+                               (uint32_t)(hv[2] + (1 << 23)), (uint32_t)(hv[3] + (1 << 23))};
+#pragma unroll
+        for (int limb = 0; limb < 3; ++limb) {
+          const int sh = 8 * limb;
+          *reinterpret_cast<uint32_t*>(c.bt3 + (size_t)(limb * SP + n0 + m) * kInter + col) =
+              ((u[0] >> sh) & 0xFF) | (((u[1] >> sh) & 0xFF) << 8) | (((u[2] >> sh) & 0xFF) << 16) |
+              (((u[3] >> sh) & 0xFF) << 24);
+        }
       }
     } else {
       // LM head (no split): best (score, row) of each sequence over the tile
@@ -1389,6 +1424,34 @@ __global__ void batch_commit_kernel(BatchCtx c, const int64_t* __restrict__ toke
   if (pos + 1 >= c.lm_from[m]) {
     st.tokens[pos + 1] = (int32_t)tokens[m];
     st.scores[pos + 1] = scores[m];
+  }
+  *st.pos = pos + 1;
+}
+
+// Vocabulary-sharded LM head: every shard's (score, row) winner of sequence
+// m sits at win[(k * 2 + 0) * stride + col0 + m] / win[(k * 2 + 1) * stride +
+// col0 + m] (shards k = 0 .. n_shards - 1, as an all_gather of [2][stride]
+// per rank lays them out).  The global winner follows the reference's rule
+// (highest score, lowest row on ties; the order shards are visited does not
+// matter), is stored at position + 1 from lm_from on, and positions advance.
+__global__ void batch_commit_shards_kernel(BatchCtx c, const int64_t* __restrict__ win, int n_shards, int stride,
+                                           int col0) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= c.S) return;
+  int64_t bs = INT64_MIN, br = INT64_MAX;
+  for (int k = 0; k < n_shards; ++k) {
+    const int64_t sc = win[(size_t)(2 * k) * stride + col0 + m], row = win[(size_t)(2 * k + 1) * stride + col0 + m];
+    if (sc > bs || (sc == bs && row < br)) {
+      bs = sc;
+      br = row;
+    }
+  }
+  const SlotState& st = c.slots[m];
+  const int pos = *st.pos;
+  if (pos >= st.max_ctx) return;
+  if (pos + 1 >= c.lm_from[m]) {
+    st.tokens[pos + 1] = (int32_t)br;
+    st.scores[pos + 1] = bs;
   }
   *st.pos = pos + 1;
 }
@@ -2549,6 +2612,16 @@ int q4gpu_enqueue_batch_commit(const BatchPlan& p, const int64_t* tokens, const 
   c.S = p.S;
   c.lm_from = p.lm_from;
   batch_commit_kernel<<<(p.S + 63) / 64, 64, 0, s>>>(c, tokens, scores);
+  return q4gpu_check_launch();
+}
+
+int q4gpu_enqueue_batch_commit_shards(const BatchPlan& p, const int64_t* win, int n_shards, int stride, int col0,
+                                      cudaStream_t s) {
+  BatchCtx c{};
+  c.slots = p.slots;
+  c.S = p.S;
+  c.lm_from = p.lm_from;
+  batch_commit_shards_kernel<<<(p.S + 63) / 64, 64, 0, s>>>(c, win, n_shards, stride, col0);
   return q4gpu_check_launch();
 }
 

@@ -189,3 +189,6 @@ int q4gpu_enqueue_prefill_block(const q4::PrefillPlan& p, cudaStream_t s);
 
 // tokens / scores: device int64 [S]; stores them at position + 1 and advances positions
 int q4gpu_enqueue_batch_commit(const q4::BatchPlan& p, const int64_t* tokens, const int64_t* scores, cudaStream_t s);
+// the same from per-shard (score, row) winners: win[(2 k) * stride + col0 + m] / win[(2 k + 1) * stride + col0 + m]
+int q4gpu_enqueue_batch_commit_shards(const q4::BatchPlan& p, const int64_t* win, int n_shards, int stride, int col0,
+                                      cudaStream_t s);

@@ -395,6 +395,9 @@ int q4gpu_fail(int code, const char* fmt, ...) {
   vsnprintf(buf, sizeof(buf), fmt, ap);
   va_end(ap);
   g_last_error = buf;
+  // the failing runtime call is reported here: consume the runtime's record of
+  // it, so a later launch check does not report it again
+  if (code == Q4GPU_ERR_CUDA) (void)cudaGetLastError();
   return code;
 }
 
@@ -1670,7 +1673,19 @@ int q4gpu_batch_forward_hidden(q4gpu_model* m, int32_t first_slot, int32_t n_seq
   if (!final_act) return q4gpu_fail(Q4GPU_ERR_ARG, "null final_act");
   cudaGraphExec_t g;
   if ((rc = batch_graph(m, first_slot, n_seq, &g, true))) return rc;
-  Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  // inside a caller's stream capture (a whole sharded step recorded as one
+  // graph) the kernels are enqueued directly: an executable graph cannot be
+  // launched into a capturing stream
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  Q4_CUDA(cudaStreamIsCapturing(m->stream, &cs));
+  if (cs == cudaStreamCaptureStatusActive) {
+    auto pp = std::make_unique<BatchPlan>();
+    if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
+    pp->final_act = m->b_final_act;
+    if ((rc = q4gpu_enqueue_batch_step(*pp, m->stream))) return rc;
+  } else {
+    Q4_CUDA(cudaGraphLaunch(g, m->stream));
+  }
   Q4_CUDA(cudaMemcpyAsync(final_act, m->b_final_act, (size_t)n_seq * kHidden * 4, cudaMemcpyDeviceToDevice,
                           m->stream));
   return Q4GPU_OK;
@@ -1717,6 +1732,20 @@ int q4gpu_batch_commit(q4gpu_model* m, int32_t first_slot, int32_t n_seq, const 
   auto pp = std::make_unique<BatchPlan>();
   if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
   return q4gpu_enqueue_batch_commit(*pp, tokens, scores, m->stream);
+}
+
+int q4gpu_batch_commit_shards(q4gpu_model* m, int32_t first_slot, int32_t n_seq, const int64_t* winners,
+                              int32_t n_shards, int32_t stride, int32_t col0) {
+  int rc = batch_range_ok(m, first_slot, n_seq);
+  if (rc) return rc;
+  if (!winners) return q4gpu_fail(Q4GPU_ERR_ARG, "null winners");
+  if (n_shards < 1 || stride < 1 || col0 < 0 || col0 + n_seq > stride)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad winner layout: %d shards, stride %d, columns [%d, %d)", n_shards, stride, col0,
+                      col0 + n_seq);
+  if ((rc = batch_prepare(m))) return rc;
+  auto pp = std::make_unique<BatchPlan>();
+  if ((rc = batch_plan(m, first_slot, n_seq, *pp))) return rc;
+  return q4gpu_enqueue_batch_commit_shards(*pp, winners, n_shards, stride, col0, m->stream);
 }
 
 int q4gpu_batch_set_position(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t position, int32_t lm_from) {

@@ -223,6 +223,13 @@ class Q4Model:
         _native.check(self.lib.q4gpu_batch_commit(self.handle, first_slot, tokens.shape[0], tokens.data_ptr(),
                                                   scores.data_ptr()), "q4gpu_batch_commit")
 
+    def batch_commit_shards(self, winners, n_seq: int, col0: int, first_slot: int = 0) -> None:
+        """Reduce per-shard (score, row) winners (int64 CUDA [shards, 2, stride]) for
+        this model's sequences (columns col0 .. col0 + n_seq) and commit them (async)."""
+        _native.check(self.lib.q4gpu_batch_commit_shards(self.handle, first_slot, n_seq, winners.data_ptr(),
+                                                         winners.shape[0], winners.shape[2], col0),
+                      "q4gpu_batch_commit_shards")
+
     def batch_time_kernels(self, n_seq: int, reps: int = 2, first_slot: int = 0) -> dict[str, tuple[float, int]]:
         """Mean device ms per launch and launches per step of each batched kernel
         (kernels serialised by events; advances the positions by `reps`)."""

@@ -79,24 +79,16 @@ def max_over_ranks(x: float, device=None, group=None) -> float:
     return float(t.item())
 
 
-def reduce_winners_device(scores, rows):
-    """Device-side twin of combine_argmax: scores / rows int64 tensors [shards, n]
-    -> (score, row) [n], highest score then lowest row, without a host round trip."""
-    import torch
-
-    best = scores.max(dim=0).values
-    big = torch.iinfo(torch.int64).max
-    row = torch.where(scores == best.unsqueeze(0), rows, torch.full_like(rows, big)).min(dim=0).values
-    return best, row
-
-
 class VocabShardedDecoder:
     """Greedy decode steps with the tied LM head split over the ranks of a
     process group (one GPU each).  Every rank decodes `n_local` sequences of
     its own (slots 0..n_local-1 of `model`); per step the ranks exchange the
     final normed vectors (all_gather), each scores its vocabulary shard for all
-    of them, and the (score, row) winners are exchanged and reduced with the
-    reference's rule.  The result equals an unsharded LM head bit for bit."""
+    of them, the (score, row) winners are exchanged (all_gather) and one kernel
+    (q4gpu_batch_commit_shards) reduces them with the reference's rule and
+    commits this rank's tokens.  The result equals an unsharded LM head bit for
+    bit.  `capture()` records the whole step (the batched forward graph, both
+    collectives, the shard GEMM and the commit) as one CUDA graph."""
 
     def __init__(self, model, n_local: int, group=None):
         import torch
@@ -108,29 +100,60 @@ class VocabShardedDecoder:
         self.v0, self.v1 = vocab_shard(model.vocab, self.world, self.rank)
         dev = torch.device("cuda", torch.cuda.current_device())
         self.stream = torch.cuda.ExternalStream(model.stream)
+        cols = self.world * n_local
         self.acts = torch.empty((n_local, 1024), dtype=torch.int32, device=dev)
-        self.all_acts = torch.empty((self.world * n_local, 1024), dtype=torch.int32, device=dev)
-        self.bs = torch.empty(self.world * n_local, dtype=torch.int64, device=dev)
-        self.br = torch.empty(self.world * n_local, dtype=torch.int64, device=dev)
-        self.win = torch.empty((self.world, 2, self.world * n_local), dtype=torch.int64, device=dev)
+        self.all_acts = torch.empty((cols, 1024), dtype=torch.int32, device=dev)
+        # this rank's shard winners for every sequence of every rank: scores
+        # then rows, one contiguous [2, cols] block as the all_gather sends it
+        self.mine = torch.empty((2, cols), dtype=torch.int64, device=dev)
+        self.win = torch.empty((self.world, 2, cols), dtype=torch.int64, device=dev)
+        self.graph = None
+
+    def _enqueue(self) -> None:
+        import torch.distributed as dist
+
+        self.m.batch_forward_hidden(self.n, self.acts)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.all_acts, self.acts, group=self.group)
+        else:
+            self.all_acts.copy_(self.acts)
+        self.m.lm_head_shard(self.all_acts, self.v0, self.v1, self.mine[0], self.mine[1])
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.win, self.mine, group=self.group)
+        else:
+            self.win[0].copy_(self.mine)
+        self.m.batch_commit_shards(self.win, self.n, self.rank * self.n)
 
     def step(self) -> None:
         """One decode position for this rank's sequences (asynchronous on the model stream)."""
         import torch
-        import torch.distributed as dist
 
+        if self.graph is not None:
+            self.graph.replay()
+            return
         with torch.cuda.stream(self.stream):
-            self.m.batch_forward_hidden(self.n, self.acts)
-            if self.world > 1:
-                dist.all_gather_into_tensor(self.all_acts, self.acts, group=self.group)
-            else:
-                self.all_acts.copy_(self.acts)
-            self.m.lm_head_shard(self.all_acts, self.v0, self.v1, self.bs, self.br)
-            mine = torch.stack([self.bs, self.br])
-            if self.world > 1:
-                dist.all_gather_into_tensor(self.win, mine, group=self.group)
-            else:
-                self.win.copy_(mine.unsqueeze(0))
-            score, row = reduce_winners_device(self.win[:, 0, :], self.win[:, 1, :])
-            lo = self.rank * self.n
-            self.m.batch_commit(row[lo:lo + self.n].contiguous(), score[lo:lo + self.n].contiguous())
+            self._enqueue()
+
+    def capture(self) -> bool:
+        """Record one step as a CUDA graph; later steps replay it.  Run one eager
+        step first (buffers, communicators, the forward graph).  Returns False,
+        leaving the eager path, if this CUDA / NCCL build cannot capture it."""
+        import torch
+
+        from ._native import Q4GpuError
+
+        g = torch.cuda.CUDAGraph()
+        try:
+            # relaxed: the library's host-side set-up calls (device selection,
+            # tensor-map encoding) run during the capture without being captured
+            with torch.cuda.graph(g, stream=self.stream, capture_error_mode="relaxed"):
+                self._enqueue()
+        except (RuntimeError, Q4GpuError):
+            torch.cuda.synchronize()
+            return False
+        self.graph = g
+        return True
+
+    def release(self) -> None:
+        """Drop the captured graph (before the process group is destroyed)."""
+        self.graph = None

@@ -37,14 +37,17 @@ def test_sharded_lm_head_matches_full_decode():
         with torch.cuda.stream(stream):
             for _ in range(n_new):
                 gm.batch_forward_hidden(5, acts)
-                sc = torch.empty((3, 5), dtype=torch.int64, device=dev)
-                rw = torch.empty((3, 5), dtype=torch.int64, device=dev)
+                # shard winners as an all_gather lays them out: [shard][score | row][sequence]
+                win = torch.empty((3, 2, 5), dtype=torch.int64, device=dev)
                 for i, (a, b) in enumerate(shards):
-                    gm.lm_head_shard(acts, a, b, sc[i], rw[i])
-                score, row = SH.reduce_winners_device(sc, rw)
-                host = SH.combine_argmax(sc.cpu().numpy(), rw.cpu().numpy())
-                assert np.array_equal(score.cpu().numpy(), host[0]) and np.array_equal(row.cpu().numpy(), host[1])
-                gm.batch_commit(row, score)
+                    gm.lm_head_shard(acts, a, b, win[i, 0], win[i, 1])
+                host = SH.combine_argmax(win[:, 0].cpu().numpy(), win[:, 1].cpu().numpy())
+                before = gm.read_tokens(0, CTX, slot=0)[2]
+                gm.batch_commit_shards(win, 5, 0)
+                gm.sync()
+                for i in range(5):
+                    t, sc, _ = gm.read_tokens(before + 1, 1, slot=i)
+                    assert (int(t[0]), int(sc[0])) == (int(host[1][i]), int(host[0][i])), i
         gm.sync()
         for i in range(5):
             toks, scores, pos = gm.read_tokens(4, n_new, slot=i)
@@ -65,11 +68,16 @@ def test_single_rank_decoder_equals_full_lm_head():
         gm.decode_batch(prompts, 1)
         gm.batch_set_position(2, 4)
         dec = SH.VocabShardedDecoder(gm, 4)
-        for _ in range(4):
+        dec.step()  # eager
+        gm.sync()
+        captured = dec.capture()  # the same step as one CUDA graph (capture does not run it)
+        for _ in range(3):
             dec.step()
         gm.sync()
+        dec.release()
         for i in range(4):
-            assert gm.read_tokens(3, 4, slot=i)[0].tolist() == full[i].tolist()
+            assert gm.read_tokens(3, 4, slot=i)[0].tolist() == full[i].tolist(), (i, captured)
+        assert captured, "the sharded step should capture as a CUDA graph"
 
 
 def test_lm_head_shard_rejects_bad_ranges():
