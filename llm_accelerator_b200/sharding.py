@@ -128,11 +128,11 @@ class VocabShardedDecoder:
         """One decode position for this rank's sequences (asynchronous on the model stream)."""
         import torch
 
-        if self.graph is not None:
-            self.graph.replay()
-            return
         with torch.cuda.stream(self.stream):
-            self._enqueue()
+            if self.graph is not None:
+                self.graph.replay()  # replays on the current stream: the model's
+            else:
+                self._enqueue()
 
     def capture(self) -> bool:
         """Record one step as a CUDA graph; later steps replay it.  Run one eager
