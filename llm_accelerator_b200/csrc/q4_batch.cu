@@ -699,12 +699,13 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
 // range (|T| < 120 * 255 * K): TMEM is read once per tile, not once per
 // 64-column scale group.
 //
-// CTA tile: 128 weight rows x SN sequences (a chunk of the SP columns of the
-// limb matrix: MMA N = 3 SN rounded up to 16, zero rows past 3 SN), K in
-// 128-wide tiles.  Reading TMEM back runs at about 56 bytes per clock per SM,
-// so a CTA's accumulators (128 x 6 SN int32) and its share of a split-K
-// exchange are kept small by splitting the sequences over CTAs first and K
-// only where a matrix has few row tiles (o_proj, down).  Warp 0 issues the
+// CTA tile: 128 weight rows x SN sequences (SN = SP columns of the limb
+// matrix in decode: MMA N = 3 SN rounded up to 16, zero rows past 3 SN), K in
+// 128-wide tiles.  An M128 x K32 kind::i8 MMA costs about 46 clocks at
+// N <= 48 and 96 at N = 192, so chunks of fewer sequences buy nothing: a CTA
+// takes all of them and K is split over the CTAs of a cluster instead where
+// a matrix has few row tiles (q/k/v 4, gate/up 2, o_proj and down 8, the LM
+// head 1).  Warp 0 issues the
 // TMA loads (packed weights into a 4-slot ring, the three limb boxes of the
 // chunk into a limb ring), warp 1 owns TMEM and issues tcgen05.mma (kind::i8,
 // s8 x u8 -> s32), and warps 2-17 first build the planes of each K tile in
@@ -891,25 +892,30 @@ __global__ void __launch_bounds__(kUThreads, 1)
 
   if (threadIdx.x == 0) gemm_stamp(g, 0);
   const int pre_a = nkt < SA ? nkt : SA;
+  // barrier set-up spread over warp 0 (one barrier per lane): thread 0 issues
+  // the first weight loads right after
+  if (warp == 0) {
+    constexpr int kBars = 2 * SA + 2 * SB + 2 * SPL + 3;
+    static_assert(kBars <= 32, "one barrier per lane of warp 0");
+    if (lane < kBars) {
+      const int b = lane;
+      const unsigned count = b < SA                            ? 1u
+                             : b < 2 * SA                      ? 16u
+                             : b < 2 * SA + 2 * SB             ? 1u
+                             : b < 2 * SA + 2 * SB + SPL       ? 16u
+                             : b < 2 * SA + 2 * SB + 2 * SPL   ? 1u
+                             : b == 2 * SA + 2 * SB + 2 * SPL  ? 1u  // tfull
+                                                               : 16u;  // tempty, scales_in
+      umma::bar_init(full_a + b, count);
+      umma::bar_init_fence();
+    }
+    if (lane == 0) {
+      *abort_flag = 0;
+      *wide_any = 0;
+    }
+    __syncwarp();
+  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < SA; ++s) {
-      umma::bar_init(full_a + s, 1);
-      umma::bar_init(empty_a + s, 16);
-    }
-    for (int s = 0; s < SB; ++s) {
-      umma::bar_init(full_b + s, 1);
-      umma::bar_init(empty_b + s, 1);
-    }
-    for (int s = 0; s < SPL; ++s) {
-      umma::bar_init(full_p + s, 16);
-      umma::bar_init(empty_p + s, 1);
-    }
-    umma::bar_init(tfull, 1);
-    umma::bar_init(tempty, 16);
-    umma::bar_init(scales_in, 16);
-    *abort_flag = 0;
-    *wide_any = 0;
-    umma::bar_init_fence();
     umma::prefetch_map(&amap);
     umma::prefetch_map(&bmap);
     if (KIND == kGemmGu) umma::prefetch_map(&amap2);
