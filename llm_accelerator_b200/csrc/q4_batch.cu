@@ -1613,11 +1613,16 @@ __device__ __forceinline__ int4 head_norm_rope(const int32_t* row, const int32_t
 // ---------------------------------------------------------------------------
 constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds
 
-__global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
-                                                            const int32_t* __restrict__ g_k,
-                                                            const int32_t* __restrict__ cos_tab,
-                                                            const int32_t* __restrict__ sin_tab,
-                                                            const int32_t* __restrict__ exp_lut, int kpr_cap) {
+// STAGE = false: the batched decode step (sequence m = blockIdx.z of c; q/k/v
+// raw from the q/k/v GEMM, normed, roped and appended here; output the o_proj
+// limbs).  STAGE = true: one slot of the per-stage batch-1 path (q heads
+// already normed and roped in st.qrope, the new K/V row already in the cache;
+// output st.attn).
+template <bool STAGE>
+__device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState& st, int* err, int layer,
+                                             const int32_t* __restrict__ g_q, const int32_t* __restrict__ g_k,
+                                             const int32_t* __restrict__ cos_tab, const int32_t* __restrict__ sin_tab,
+                                             const int32_t* __restrict__ exp_lut, int kpr_cap) {
   extern __shared__ __align__(128) uint8_t cl_smem[];
   int32_t* ring = reinterpret_cast<int32_t*>(cl_smem);                            // [2][32][128]
   int64_t* sc = reinterpret_cast<int64_t*>(cl_smem + kAttnRing * kAttnChunkBytes);  // [2][kpr_cap]
@@ -1627,19 +1632,19 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   __shared__ int64_t xmax[2], xsum[2];       // published to the cluster
   __shared__ int64_t part[2][kHeadDim];      // this rank's value sums, published to the cluster
   __shared__ uint64_t bars[kAttnRing];
-  const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = blockIdx.z;
+  const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = STAGE ? 0 : blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   // every rank reaches every cluster barrier below: no early return.  The
   // cached K/V rows and the position come from earlier steps, so the first
   // chunks load before the wait for this step's q/k/v projections.
-  const int pos = c.pos0[4 * m];
-  const bool live = pos < c.max_ctx;
+  const int pos = STAGE ? *st.pos : c.pos0[4 * m];
+  const bool live = pos < (STAGE ? st.max_ctx : c.max_ctx);
   const int ctx = live ? pos + 1 : 0;
   const int kpr = ((ctx + nranks - 1) / nranks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
   const int k0 = rank * kpr;
   const int k1 = k0 + kpr < ctx ? k0 + kpr : ctx;  // this rank's keys [k0, k1)
   const int nloc = k1 > k0 ? k1 - k0 : 0;
-  const KvView kvv = c.slots[m].kv;
+  const KvView kvv = STAGE ? st.kv : c.slots[m].kv;
   const int nk = (nloc + kAttnChunk - 1) / kAttnChunk, total = 2 * nk;
   const int kend = k1 < pos ? k1 : pos;  // cached keys of the range (the new position comes from shared memory)
   auto issue = [&](int i) {
@@ -1660,7 +1665,13 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   }
   grid_dep_wait();
   grid_dep_launch();
-  if (live) {
+  if (STAGE && live) {
+    // q heads 2 kv, 2 kv + 1 as roped by the q/k/v stage, the new K/V row from the cache
+    if (warp < 2)
+      reinterpret_cast<int4*>(hv[warp])[lane] = reinterpret_cast<const int4*>(st.qrope + (2 * kv + warp) * kHeadDim)[lane];
+    else if (warp < 4)
+      reinterpret_cast<int4*>(hv[warp])[lane] = reinterpret_cast<const int4*>(kvv.at(layer, warp - 2, kv, pos))[lane];
+  } else if (live) {
     const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
     const bool owner = pos >= k0 && pos < k1;  // the rank whose range holds the new position appends it
     if (warp < 2) {
@@ -1742,14 +1753,28 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
     xmax[t] = b;
   }
   umma::cluster_sync();  // every rank's maxima are published
-  mx0 = INT64_MIN;
-  mx1 = INT64_MIN;
-  for (int r = 0; r < nranks; ++r) {
-    const int64_t o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[0]), (uint32_t)r));
-    const int64_t o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[1]), (uint32_t)r));
-    mx0 = o0 > mx0 ? o0 : mx0;
-    mx1 = o1 > mx1 ? o1 : mx1;
+  // lane r of warp 0 reads rank r's (one round trip for all ranks), a warp
+  // reduction combines them
+  if (warp == 0) {
+    int64_t o0 = INT64_MIN, o1 = INT64_MIN;
+    if (lane < nranks) {
+      o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[0]), (uint32_t)lane));
+      o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[1]), (uint32_t)lane));
+    }
+#pragma unroll
+    for (int msk = 1; msk < 32; msk <<= 1) {
+      const int64_t a = shfl_xor_i64(o0, msk), b = shfl_xor_i64(o1, msk);
+      o0 = a > o0 ? a : o0;
+      o1 = b > o1 ? b : o1;
+    }
+    if (lane == 0) {
+      red[0][0] = o0;
+      red[1][0] = o1;
+    }
   }
+  __syncthreads();
+  mx0 = red[0][0];
+  mx1 = red[1][0];
   // LUT indices and exp sums of the range
   int64_t sum0 = 0, sum1 = 0;
   for (int lp = t; lp < nloc; lp += blockDim.x) {
@@ -1773,12 +1798,22 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
     xsum[t] = b;
   }
   umma::cluster_sync();  // every rank's sums are published
-  sum0 = 0;
-  sum1 = 0;
-  for (int r = 0; r < nranks; ++r) {
-    sum0 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[0]), (uint32_t)r));
-    sum1 += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[1]), (uint32_t)r));
+  if (warp == 0) {
+    int64_t o0 = 0, o1 = 0;
+    if (lane < nranks) {
+      o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[0]), (uint32_t)lane));
+      o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[1]), (uint32_t)lane));
+    }
+    o0 = warp_sum_i64(o0);
+    o1 = warp_sum_i64(o1);
+    if (lane == 0) {
+      red[0][1] = o0;
+      red[1][1] = o1;
+    }
   }
+  __syncthreads();
+  sum0 = red[0][1];
+  sum1 = red[1][1];
   if (live) {
     const uint64_t d0 = (uint64_t)sum0, d1 = (uint64_t)sum1, r0 = ~0ULL / d0, r1 = ~0ULL / d1;
     for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
@@ -1816,7 +1851,7 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
     __syncthreads();
     if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
   }
-  if (!ok) atomicExch(c.err, 4);
+  if (!ok) atomicExch(err, 4);
   // cross-warp sums through the idle ring [8][2][128], then published
   int64_t* wpart = reinterpret_cast<int64_t*>(cl_smem);
 #pragma unroll
@@ -1833,13 +1868,40 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
     part[h][d] = acc;
   }
   umma::cluster_sync();  // every rank's value sums are published
-  if (rank == 0 && live) {
-    const int h = t >> 7, d = t & (kHeadDim - 1);
-    int64_t acc = 0;
-    for (int r = 0; r < nranks; ++r) acc += umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&part[h][d]), (uint32_t)r));
-    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
+  {
+    // rank r finishes outputs [r per, (r + 1) per) of the 2 x 128: thread
+    // (source rank src, output j) fetches one partial sum (one round trip),
+    // the sums over the sources meet in the idle ring
+    const int per = 2 * kHeadDim / nranks, j = t % per, src = t / per, o = rank * per + j;
+    int64_t* gsum = wpart;  // [nranks][per]
+    gsum[src * per + j] =
+        umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&part[o >> 7][o & (kHeadDim - 1)]), (uint32_t)src));
+    __syncthreads();
+    if (t < per && live) {
+      int64_t acc = 0;
+      for (int r = 0; r < nranks; ++r) acc += gsum[r * per + t];
+      const int oo = rank * per + t, h = oo >> 7, d = oo & (kHeadDim - 1);
+      if constexpr (STAGE)
+        st.attn[(2 * kv + h) * kHeadDim + d] = sat24(acc >> 16);
+      else
+        write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
+    }
   }
-  umma::cluster_sync();  // no rank leaves while rank 0 still reads its shared memory
+  umma::cluster_sync();  // no rank leaves while another still reads its shared memory
+}
+
+__global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
+                                                            const int32_t* __restrict__ g_k,
+                                                            const int32_t* __restrict__ cos_tab,
+                                                            const int32_t* __restrict__ sin_tab,
+                                                            const int32_t* __restrict__ exp_lut, int kpr_cap) {
+  attn_cl_body<false>(c, SlotState{}, c.err, layer, g_q, g_k, cos_tab, sin_tab, exp_lut, kpr_cap);
+}
+
+// Attention of the per-stage batch-1 path (grid: ranks x 8 KV heads, one cluster per head).
+__global__ void __launch_bounds__(256) stage_attn_cl_kernel(SlotState st, int* err, int layer,
+                                                            const int32_t* __restrict__ exp_lut, int kpr_cap) {
+  attn_cl_body<true>(BatchCtx{}, st, err, layer, nullptr, nullptr, nullptr, nullptr, exp_lut, kpr_cap);
 }
 
 // Per (KV head, column): q heads 2 kv, 2 kv + 1 normed and roped in place in
@@ -2466,6 +2528,29 @@ int setup_t(const BatchPlan& p) {
 }
 
 }  // namespace
+
+namespace {
+int stage_attn_kpr(int max_ctx) {
+  return ((max_ctx + kStageAttnRanks - 1) / kStageAttnRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+}
+size_t stage_attn_smem(int max_ctx) { return (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * stage_attn_kpr(max_ctx) * 8; }
+}  // namespace
+
+bool q4gpu_stage_attention_fits(int max_ctx) { return max_ctx > 0 && stage_attn_kpr(max_ctx) <= kClKprMax; }
+
+int q4gpu_stage_attention_setup(int max_ctx) {
+  if (!q4gpu_stage_attention_fits(max_ctx)) return q4gpu_fail(Q4GPU_ERR_SHAPE, "stage attention: max_ctx too large");
+  BQ(cudaFuncSetAttribute(stage_attn_cl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stage_attn_smem(max_ctx)));
+  BQ(cudaFuncSetAttribute(stage_attn_cl_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  return Q4GPU_OK;
+}
+
+int q4gpu_enqueue_stage_attention(const SlotState& st, int* err, int layer, const int32_t* exp_lut, int max_ctx,
+                                  cudaStream_t s) {
+  BQ(launch_cluster_x(stage_attn_cl_kernel, dim3(kStageAttnRanks, kKvHeads), dim3(256), stage_attn_smem(max_ctx), s,
+                      kStageAttnRanks, st, err, layer, exp_lut, stage_attn_kpr(max_ctx)));
+  return Q4GPU_OK;
+}
 
 int q4gpu_batch_padded(int S) { return S <= 8 ? 8 : S <= 16 ? 16 : S <= 24 ? 24 : S <= 32 ? 32 : 64; }
 

@@ -192,3 +192,13 @@ int q4gpu_enqueue_batch_commit(const q4::BatchPlan& p, const int64_t* tokens, co
 // the same from per-shard (score, row) winners: win[(2 k) * stride + col0 + m] / win[(2 k + 1) * stride + col0 + m]
 int q4gpu_enqueue_batch_commit_shards(const q4::BatchPlan& p, const int64_t* win, int n_shards, int stride, int col0,
                                       cudaStream_t s);
+
+// Attention of the per-stage batch-1 path (one slot): a cluster of
+// kStageAttnRanks CTAs per KV head splits the context (stage_attn_cl_kernel).
+// Usable when max_ctx fits the ranks' score buffers.
+constexpr int kStageAttnRanks = 16;
+bool q4gpu_stage_attention_fits(int max_ctx);
+int q4gpu_stage_attention_setup(int max_ctx);
+// err: set to 4 when a K/V copy wait runs out
+int q4gpu_enqueue_stage_attention(const q4::SlotState& st, int* err, int layer, const int32_t* exp_lut, int max_ctx,
+                                  cudaStream_t s);

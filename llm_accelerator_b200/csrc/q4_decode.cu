@@ -477,7 +477,8 @@ struct q4gpu_model {
   int64_t* p_acc = nullptr;
   ArgBestD* p_lm_part = nullptr;
   unsigned int* p_bar = nullptr;
-  int* p_err = nullptr;
+  int* p_err = nullptr;      // set by the persistent kernel or the stage path's cluster attention
+  bool stage_attn_cl = false;  // the per-stage path runs its attention on clusters (stage_attn_cl_kernel)
   CUtensorMap vmap{};
   // batched decode (q4_batch.cu), set up on first use
   bool b_ready = false;       // batched buffers and the TMA maps of the packed weights set up
@@ -688,8 +689,13 @@ int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int
     Q4_CUDA(launch_k(qkv_step_kernel, dim3(kQHeads + 2 * kKvHeads), dim3(256), 0, s, st, w, l,
                      (const int32_t*)m->cos_tab, (const int32_t*)m->sin_tab));
     if ((rc = mark(Q4GPU_K_ATTN))) return rc;
-    Q4_CUDA(launch_k(attn_step_kernel, dim3(kKvHeads), dim3(256), attn_smem(m->cfg.max_context), s, st, l,
-                     (const int32_t*)m->exp_lut, scale));
+    if (m->stage_attn_cl) {
+      if ((rc = q4gpu_enqueue_stage_attention(st, m->p_err, l, (const int32_t*)m->exp_lut, m->cfg.max_context, s)))
+        return rc;
+    } else {
+      Q4_CUDA(launch_k(attn_step_kernel, dim3(kKvHeads), dim3(256), attn_smem(m->cfg.max_context), s, st, l,
+                       (const int32_t*)m->exp_lut, scale));
+    }
     if ((rc = mark(Q4GPU_K_OPROJ))) return rc;
     Q4_CUDA(launch_k(oproj_step_kernel, dim3(kHidden / 8), dim3(256), 0, s, st, w));
     if ((rc = mark(Q4GPU_K_GATEUP))) return rc;
@@ -784,8 +790,9 @@ int check_persistent_error(q4gpu_model* m) {
   Q4_CUDA(cudaMemcpy(&e, m->p_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (e) {
     cudaMemsetAsync(m->p_err, 0, sizeof(int), m->stream);
-    return q4gpu_fail(Q4GPU_ERR_CUDA, e == 2 ? "persistent decode kernel: stepped past max_context"
-                                             : "persistent decode kernel: a grid barrier wait ran out");
+    return q4gpu_fail(Q4GPU_ERR_CUDA, e == 2   ? "persistent decode kernel: stepped past max_context"
+                                      : e == 4 ? "attention stage: a K/V copy wait ran out"
+                                               : "persistent decode kernel: a grid barrier wait ran out");
   }
   return Q4GPU_OK;
 }
@@ -1254,9 +1261,12 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   for (int i = 0; i < S; ++i)
     if (cudaEventCreateWithFlags(&m->done[i], cudaEventDisableTiming) != cudaSuccess)
       return fail(q4gpu_fail(Q4GPU_ERR_CUDA, "event create"));
-  const size_t asmem = attn_smem(cfg->max_context);
-  if (cudaFuncSetAttribute(attn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem) != cudaSuccess)
-    return fail(q4gpu_fail(Q4GPU_ERR_SHAPE, "max_context %d needs %zu B of shared memory", cfg->max_context, asmem));
+  m->stage_attn_cl = q4gpu_stage_attention_fits(cfg->max_context) && q4gpu_stage_attention_setup(cfg->max_context) == Q4GPU_OK;
+  if (!m->stage_attn_cl) {
+    const size_t asmem = attn_smem(cfg->max_context);
+    if (cudaFuncSetAttribute(attn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)asmem) != cudaSuccess)
+      return fail(q4gpu_fail(Q4GPU_ERR_SHAPE, "max_context %d needs %zu B of shared memory", cfg->max_context, asmem));
+  }
   // persistent kernel: available when its shared memory fits (score buffer of max_context)
   if ((rc = m->alloc(&m->layers_dev, (size_t)L))) return fail(rc);
   if (stream_copy(m, m->layers_dev, m->layers, sizeof(LayerW) * L, cudaMemcpyHostToDevice) != Q4GPU_OK)
@@ -1467,7 +1477,7 @@ int q4gpu_run_token(void* runner_context, uintptr_t base, const qot_run_config_t
   memset(result, 0, sizeof(*result));
   rc = poll_slot(m, slot, max_polls);
   if (rc != QOT_OK) return rc;
-  if (persistent && check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
+  if (check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
   result->status = 1u;  // done
   result->token_id = (uint32_t)hr->token;
   result->score_q26 = hr->score;
@@ -1551,7 +1561,7 @@ int q4gpu_decode_token_ids(q4gpu_model* m, uintptr_t base, const qot_run_config_
   rc = poll_slot(m, slot, (uint32_t)std::min<uint64_t>(polls, 0xFFFFFFFFull));
   memset(last_result, 0, sizeof(*last_result));
   if (rc != QOT_OK) return rc;
-  if (m->mode == 1 && check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
+  if (check_persistent_error(m) != Q4GPU_OK) return QOT_ERR_TIMEOUT;
   for (uint32_t i = 0; i < max_new_tokens; ++i) {
     if ((uint32_t)gen[i] >= (uint32_t)m->cfg.vocab) return QOT_ERR_BAD_TOKEN;
     generated_token_ids[i] = (uint32_t)gen[i];

@@ -192,9 +192,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void cluster_st64(uint32_t caddr, int64_t v) {
   asm volatile("st.shared::cluster.b64 [%0], %1;" ::"r"(caddr), "l"(v) : "memory");
 }
-__device__ __forceinline__ void cluster_st128(uint32_t caddr, int64_t a, int64_t b) {
-  asm volatile("st.shared::cluster.v2.b64 [%0], {%1, %2};" ::"r"(caddr), "l"(a), "l"(b) : "memory");
-}
 __device__ __forceinline__ int64_t cluster_ld64(uint32_t caddr) {
   int64_t v;
   asm volatile("ld.shared::cluster.b64 %0, [%1];" : "=l"(v) : "r"(caddr) : "memory");

@@ -122,28 +122,32 @@ def test_runner_timeout_then_busy(small):
         assert codes <= {_native.QOT_ERR_BUSY}
 
 
-def test_single_layer_long_context_matches_oracle():
-    """One layer at position 512 over a pre-filled context (the cfg-2 shape):
-    K/V of positions 0..511 are N(0,1) bf16 values in Q12.12."""
-    seed, ctx = 21, 520
+@pytest.mark.parametrize("ctx,pos", [(520, 512), (4104, 4100), (70, 33)])
+def test_single_layer_long_context_matches_oracle(ctx, pos):
+    """One layer at `pos` over a pre-filled context (512: the cfg-2 shape; 4100:
+    every rank of the per-stage cluster attention holds several 32-key chunks;
+    33: most ranks hold no key): K/V of positions 0..pos-1 are N(0,1) bf16
+    values in Q12.12."""
+    seed = 21
     gm = Q4Model(n_layers=1, vocab=256, max_context=ctx, max_seqs=1)
     try:
         gm.init_synthetic(seed=seed)
+        gm.mode = 0  # the per-stage kernels (the persistent kernel covers only short contexts)
         om = oracle_small(seed, 1, 256, ctx)
-        kpre = O.quantize_signed(O.synth_f32(seed, 901, (512, 8, 128), 1.0), 24, 12)[0]
-        vpre = O.quantize_signed(O.synth_f32(seed, 902, (512, 8, 128), 1.0), 24, 12)[0]
+        kpre = O.quantize_signed(O.synth_f32(seed, 901, (pos, 8, 128), 1.0), 24, 12)[0]
+        vpre = O.quantize_signed(O.synth_f32(seed, 902, (pos, 8, 128), 1.0), 24, 12)[0]
         hidden = O.quantize_signed(O.synth_f32(seed, 903, (1024,), 1.0), 24, 10)[0]
         gm.write_kv(0, 0, kpre)
         gm.write_kv(0, 1, vpre)
         gm.write_hidden(hidden)
-        r = gm.run_token(0, 512, embedding=False)
+        r = gm.run_token(0, pos, embedding=False)
         st = O.DecodeState(1, ctx)
-        st.k[0, :512], st.v[0, :512] = kpre, vpre
+        st.k[0, :pos], st.v[0, :pos] = kpre, vpre
         tr = {}
-        out = O.layer_step(om.layers[0], hidden, 512, st.k[0], st.v[0], om.cos, om.sin, om.exp_lut,
+        out = O.layer_step(om.layers[0], hidden, pos, st.k[0], st.v[0], om.cos, om.sin, om.exp_lut,
                            om.sigmoid_lut, trace=tr)
         assert np.array_equal(gm.read_hidden(), out)
-        assert np.array_equal(gm.read_kv(0, 0, 513)[512], tr["k_rope"])
+        assert np.array_equal(gm.read_kv(0, 0, pos + 1)[pos], tr["k_rope"])
         fn = O.rmsnorm(out, om.final_gamma)["output"]
         tok, score = O.lm_head_argmax(O.gemv_q26(fn, om.embed_q, om.embed_s))
         assert (r.token_id, r.score_q26) == (tok, score)
