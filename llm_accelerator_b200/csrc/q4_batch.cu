@@ -732,10 +732,10 @@ template <int SN, int KIND>
 struct UCfg {
   static constexpr int NM = (3 * SN + 15) / 16 * 16;  // MMA N: three limb blocks of SN columns
   static constexpr int Q = SN / 4;                    // sequences per epilogue thread
-  static constexpr int A_PK = 128 * 64;               // packed weights of one 128-wide K tile
+  static constexpr int A_PK = 128 * 128;              // packed weights of two 128-wide K tiles (one A stage)
   static constexpr int PLANE = 128 * 128;             // one plane of a K tile
   static constexpr int B_BYTES = NM * 128;            // limb tile (3 boxes of SN rows + zero rows)
-  static constexpr int SA = 4;                        // packed-weight tiles in flight
+  static constexpr int SA = 2;                        // packed-weight stages in flight (four K tiles)
   static constexpr int SB = KIND == kGemmLm && SN == 64 ? 4 : SN == 64 ? 2 : 3;  // limb tiles in flight
   static constexpr int SPL = 2;                       // plane pairs in flight
   static constexpr int TCOLS = 2 * NM <= 32 ? 32 : 2 * NM <= 64 ? 64 : 2 * NM <= 128 ? 128 : 2 * NM <= 256 ? 256 : 512;
@@ -891,7 +891,16 @@ __global__ void __launch_bounds__(kUThreads, 1)
   const int arow1 = KIND == kGemmGu ? tile * 64 : row0 + 64;
 
   if (threadIdx.x == 0) gemm_stamp(g, 0);
-  const int pre_a = nkt < SA ? nkt : SA;
+  // A stage u holds K tiles 2 (u % upp), + 1 of pass u / upp: one 128-row x
+  // 128-byte box (gate/up: a 64-row box of each matrix), 128-byte swizzled
+  const int upp = (nkt + 1) >> 1;
+  const int pre_a = upp < SA ? upp : SA;
+  auto issue_a = [&](int u) {
+    const int sa = u % SA, x = (kt0 + 2 * (u % upp)) * 64;
+    umma::bar_expect_tx(full_a + sa, C::A_PK);
+    umma::tma_load(astage + sa * C::A_PK, &amap, x, arow0, full_a + sa);
+    if (KIND == kGemmGu) umma::tma_load(astage + sa * C::A_PK + C::A_PK / 2, &amap2, x, arow1, full_a + sa);
+  };
   // barrier set-up spread over warp 0 (one barrier per lane): thread 0 issues
   // the first weight loads right after
   if (warp == 0) {
@@ -921,19 +930,17 @@ __global__ void __launch_bounds__(kUThreads, 1)
     if (KIND == kGemmGu) umma::prefetch_map(&amap2);
     // the weights do not depend on earlier kernels: their first tiles
     // stream in while those finish
-    for (int kt = 0; kt < pre_a; ++kt) {
-      umma::bar_expect_tx(full_a + kt, C::A_PK);
-      umma::tma_load(astage + kt * C::A_PK, &amap, (kt0 + kt) * 64, arow0, full_a + kt);
-      umma::tma_load(astage + kt * C::A_PK + C::A_PK / 2, KIND == kGemmGu ? &amap2 : &amap, (kt0 + kt) * 64, arow1,
-                     full_a + kt);
-    }
+    for (int u = 0; u < pre_a; ++u) issue_a(u);
   }
   if (warp == 1) umma::tmem_alloc(tmem_slot, C::TCOLS);
   // plane builders (warps 2-17): builder et takes chunk cc (16 K values) of
   // rows r0 and r0 + 64 in every K tile; their group scales, all K tiles, load
   // into registers now (they do not depend on earlier kernels)
   const int et = threadIdx.x - 64;
-  const int r0 = (et >> 3) & 63, cc = et & 7;
+  // warp w covers rows {b, b + 4, b + 1, b + 5} (b = 8 (w / 2) + 2 (w % 2)):
+  // their swizzled 64-byte halves of an A stage fall in both bank halves
+  const int wl = et >> 5, gq = (et >> 3) & 3;
+  const int r0 = 8 * (wl >> 1) + 2 * (wl & 1) + 4 * (gq & 1) + (gq >> 1), cc = et & 7;
   uint32_t sc2[kUMaxKt];  // scale of row r0 (low half) and r0 + 64 (high half) per K tile
   bool wide = false;      // a scale of this tile needs more than 8 bits
   if (warp >= 2) {
@@ -990,29 +997,23 @@ __global__ void __launch_bounds__(kUThreads, 1)
       gemm_stamp(g, 2);
       int nv = nkt;
       for (int v = 0; v < nv && !*abort_flag; ++v) {
-        const int kt = v % nkt;
-        if (v >= pre_a) {
-          const int s = v % SA;
-          if (!umma::bar_wait(empty_a + s, ((v / SA) & 1) ^ 1)) {
+        const int pass = v / nkt, kt = v - pass * nkt;
+        const int u = pass * upp + (kt >> 1);
+        if ((kt & 1) == 0 && u >= pre_a) {
+          if (!umma::bar_wait(empty_a + u % SA, ((u / SA) & 1) ^ 1)) {
             fail();
             break;
           }
-          umma::bar_expect_tx(full_a + s, C::A_PK);
-          umma::tma_load(astage + s * C::A_PK, &amap, (kt0 + kt) * 64, arow0, full_a + s);
-          umma::tma_load(astage + s * C::A_PK + C::A_PK / 2, KIND == kGemmGu ? &amap2 : &amap, (kt0 + kt) * 64,
-                         arow1, full_a + s);
+          issue_a(u);
         }
         const int sb = v % SB;
         if (!umma::bar_wait(empty_b + sb, ((v / SB) & 1) ^ 1)) {
           fail();
           break;
         }
+        // the chunk's three limb blocks are consecutive rows (SN = SP): one box
         umma::bar_expect_tx(full_b + sb, 3 * SN * 128);
-        uint8_t* bdst = bstage + sb * C::B_BYTES;
-        const int y0 = g.b_sub_rows * z + n0;
-#pragma unroll
-        for (int limb = 0; limb < 3; ++limb)
-          umma::tma_load(bdst + limb * SN * 128, &bmap, (kt0 + kt) * 128, y0 + limb * SP, full_b + sb);
+        umma::tma_load(bstage + sb * C::B_BYTES, &bmap, (kt0 + kt) * 128, g.b_sub_rows * z + n0, full_b + sb);
         // the first pass's loads are all issued: does the tile need a second?
         if (v == nkt - 1) nv = passes() * nkt;
       }
@@ -1103,18 +1104,20 @@ __global__ void __launch_bounds__(kUThreads, 1)
     // planes of (pass, K tile) step v into plane slot v % SPL
     auto build = [&](int v) -> bool {
       const int pass = v / nkt, kt = v - pass * nkt;
-      if (!umma::bar_wait(full_a + v % SA, (v / SA) & 1) || !umma::bar_wait(empty_p + v % SPL, ((v / SPL) & 1) ^ 1))
+      const int u = pass * upp + (kt >> 1), sa = u % SA;
+      if (!umma::bar_wait(full_a + sa, (u / SA) & 1) || !umma::bar_wait(empty_p + v % SPL, ((v / SPL) & 1) ^ 1))
         return false;
       uint32_t s2 = sc2[0];
 #pragma unroll
       for (int i = 1; i < kUMaxKt; ++i) s2 = kt == i ? sc2[i] : s2;
-      const uint8_t* pk = astage + (v % SA) * C::A_PK;
+      const uint8_t* pk = astage + sa * C::A_PK;
+      const int c16 = ((kt & 1) << 2) | (cc >> 1);  // 16-byte chunk of the row's 128-byte stage line
       uint8_t* pl = planes + (v % SPL) * 2 * C::PLANE;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int row = r0 + 64 * h;
         const uint32_t s = h ? (s2 >> 16) : (s2 & 0xFFFFu);
-        const uint2 x = *reinterpret_cast<const uint2*>(pk + row * 64 + cc * 8);
+        const uint2 x = *reinterpret_cast<const uint2*>(pk + row * 128 + ((c16 ^ (row & 7)) << 4) + ((cc & 1) << 3));
         uint32_t U[4];
         unpack16_biased(x, U);
         if (pass == 0) {
@@ -1144,7 +1147,7 @@ __global__ void __launch_bounds__(kUThreads, 1)
       __syncwarp();
       if (lane == 0) {
         umma::bar_arrive(full_p + v % SPL);
-        umma::bar_arrive(empty_a + v % SA);
+        if ((kt & 1) || kt == nkt - 1) umma::bar_arrive(empty_a + sa);  // both tiles of the stage are built
       }
       return true;
     };
@@ -2338,8 +2341,9 @@ cudaError_t launch_gemm(const CUtensorMap& amap, const CUtensorMap& amap2, const
                         int subs, int b_sub_rows, L2Prefetch pf = L2Prefetch{}) {
   // the epilogue's row bookkeeping uses shifts: splits must be 1, 2, 4 or 8;
   // a CTA holds the scales of at most kUMaxKt K tiles
+  // the limb box of a K tile spans the three limb blocks: SN = SP
   if (splits < 1 || splits > 8 || (splits & (splits - 1)) || K % (128 * splits) || K / splits > 128 * kUMaxKt ||
-      SP % SN || SP > kBatchSeqMax)
+      SN != SP || SP > kBatchSeqMax)
     return cudaErrorInvalidValue;
   // O / down stage their residual rows (128 / splits of them) in 64 rows' room
   if ((KIND == kGemmO || KIND == kGemmDown) && splits < 2) return cudaErrorInvalidValue;
@@ -2605,7 +2609,7 @@ int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes
   return Q4GPU_OK;
 }
 
-int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows) {
+int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     cudaDriverEntryPointQueryResult q;
@@ -2618,10 +2622,10 @@ int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes
     return q4gpu_fail(Q4GPU_ERR_ALIGN, "packed weights must start and have rows on 16-byte boundaries");
   const cuuint64_t dims[2] = {(cuuint64_t)inner_bytes, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)inner_bytes};
-  const cuuint32_t box[2] = {64, 64};
+  const cuuint32_t box[2] = {128, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return q4gpu_fail(Q4GPU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return Q4GPU_OK;

@@ -160,9 +160,11 @@ int q4gpu_batch_limb_rows(int SP);  // rows of a limb matrix: 3 SP + 8 (the last
 // GemmKind: 0 q/k/v, 1 o_proj, 2 gate/up, 3 down, 4 LM head) at SP padded sequences.
 int q4gpu_batch_gemm_chunk(int kind, int SP);
 // 2-D TMA map of a row-major u8 matrix [rows, inner_bytes], 128 x box_rows boxes, 128-byte swizzle
+// (limb matrices: box_rows = 3 x the GEMM's sequence chunk, the three limb blocks of a K tile)
 int q4gpu_encode_u8_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows);
-// 2-D TMA map of packed Q4 weights [rows, inner_bytes]: 64-byte x 64-row boxes (one 128-wide K tile of 64 rows)
-int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows);
+// 2-D TMA map of packed Q4 weights [rows, inner_bytes]: 128-byte x box_rows boxes (two 128-wide
+// K tiles), 128-byte swizzle; box_rows 128 (one weight tile) or 64 (a gate or up half tile)
+int q4gpu_encode_q4_map(CUtensorMap* map, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_rows);
 int q4gpu_batch_setup(const q4::BatchPlan& p);
 // Kernel kinds of a batched step (q4gpu.h Q4GPU_BK_*), for per-kernel timing.
 enum { kBkEmbed = 0, kBkNorm, kBkQkv, kBkAttn, kBkO, kBkGu, kBkDown, kBkLm, kBkArgmax, kBkCount };

@@ -910,14 +910,14 @@ int batch_prepare(q4gpu_model* m) {
     b.g_post = q.g_post;
     b.g_q = q.g_q;
     b.g_k = q.g_k;
-    if ((rc = q4gpu_encode_q4_map(&b.mqkv, q.wqkv, kHidden / 2, kQRows + 2 * kKvRows)) ||
-        (rc = q4gpu_encode_q4_map(&b.mo, q.wo, kHidden, kHidden)) ||
-        (rc = q4gpu_encode_q4_map(&b.mgate, q.wgate, kHidden / 2, kInter)) ||
-        (rc = q4gpu_encode_q4_map(&b.mup, q.wup, kHidden / 2, kInter)) ||
-        (rc = q4gpu_encode_q4_map(&b.mdown, q.wdown, kInter / 2, kHidden)))
+    if ((rc = q4gpu_encode_q4_map(&b.mqkv, q.wqkv, kHidden / 2, kQRows + 2 * kKvRows, 128)) ||
+        (rc = q4gpu_encode_q4_map(&b.mo, q.wo, kHidden, kHidden, 128)) ||
+        (rc = q4gpu_encode_q4_map(&b.mgate, q.wgate, kHidden / 2, kInter, 64)) ||
+        (rc = q4gpu_encode_q4_map(&b.mup, q.wup, kHidden / 2, kInter, 64)) ||
+        (rc = q4gpu_encode_q4_map(&b.mdown, q.wdown, kInter / 2, kHidden, 128)))
       return rc;
   }
-  if ((rc = q4gpu_encode_q4_map(&m->b_mlm, m->emb, kHidden / 2, (uint64_t)m->cfg.vocab))) return rc;
+  if ((rc = q4gpu_encode_q4_map(&m->b_mlm, m->emb, kHidden / 2, (uint64_t)m->cfg.vocab, 128))) return rc;
   m->b_ready = true;
   return Q4GPU_OK;
 }
@@ -955,9 +955,9 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.att_cnt_s = m->b_att_cnt;
   p.att_cnt_v = m->b_att_cnt + kBatchSeqMax * kKvHeads;
   p.mlm = m->b_mlm;
-  // limb boxes of each GEMM's sequence chunk (kinds: 0 q/k/v, 1 o_proj, 2 gate/up, 3 down, 4 LM head)
+  // limb boxes of each GEMM's sequence chunk, its three limb blocks (kinds: 0 q/k/v, 1 o_proj, 2 gate/up, 3 down, 4 LM head)
   const uint64_t nrows = (uint64_t)q4gpu_batch_limb_rows(p.SP);
-  auto box = [&](int kind) { return (uint32_t)q4gpu_batch_gemm_chunk(kind, p.SP); };
+  auto box = [&](int kind) { return (uint32_t)(3 * q4gpu_batch_gemm_chunk(kind, p.SP)); };
   int rc;
   if ((rc = q4gpu_encode_u8_map(&p.mb_qkv, p.bt1, kHidden, nrows, box(0))) ||
       (rc = q4gpu_encode_u8_map(&p.mb_o, p.bt2, 2 * kHidden, nrows, box(1))) ||
@@ -986,10 +986,10 @@ int prefill_prepare(q4gpu_model* m) {
       (rc = m->alloc(&p->bt3, nsub * rows * kInter)) ||
       (rc = m->alloc(&p->lut_idx, (size_t)kPfBlock * kQHeads * ((m->cfg.max_context + 63) / 64 * 64))))
     return rc;
-  // boxes of one limb of one 64-column sub-batch
-  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)kPfSub)) ||
-      (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)kPfSub)) ||
-      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, nsub * rows, (uint32_t)kPfSub)))
+  // boxes of the three limbs of one 64-column sub-batch
+  if ((rc = q4gpu_encode_u8_map(&p->mb1, p->bt1, kHidden, nsub * rows, (uint32_t)(3 * kPfSub))) ||
+      (rc = q4gpu_encode_u8_map(&p->mb2, p->bt2, 2 * kHidden, nsub * rows, (uint32_t)(3 * kPfSub))) ||
+      (rc = q4gpu_encode_u8_map(&p->mb3, p->bt3, kInter, nsub * rows, (uint32_t)(3 * kPfSub))))
     return rc;
   p->emb = m->emb;
   p->semb = m->semb;
@@ -1727,8 +1727,8 @@ int q4gpu_lm_head_shard(q4gpu_model* m, const int32_t* acts, int32_t n_act, int3
   q->best_row = best_row;
   q->err = m->b_err;
   if ((rc = q4gpu_encode_q4_map(&q->amap, m->emb + (size_t)row_begin * (kHidden / 2), kHidden / 2,
-                                (uint64_t)(row_end - row_begin))) ||
-      (rc = q4gpu_encode_u8_map(&q->bmap, m->b_lm_bt, kHidden, (uint64_t)q4gpu_batch_limb_rows(SP), (uint32_t)SP)))
+                                (uint64_t)(row_end - row_begin), 128)) ||
+      (rc = q4gpu_encode_u8_map(&q->bmap, m->b_lm_bt, kHidden, (uint64_t)q4gpu_batch_limb_rows(SP), (uint32_t)(3 * SP))))
     return rc;
   return q4gpu_enqueue_lm_shard(*q, m->stream);
 }
