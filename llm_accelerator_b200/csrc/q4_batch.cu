@@ -780,11 +780,14 @@ __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& pf) {
     if (!pf.p[r]) continue;
     const uint32_t chunk = ((pf.bytes[r] + n - 1) / n + 15u) & ~15u, off = i * chunk;
     if (off < pf.bytes[r]) {
-      const uint32_t len = pf.bytes[r] - off < chunk ? pf.bytes[r] - off : chunk;
-      asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
-                       reinterpret_cast<const char*>(pf.p[r]) + off),
-                   "r"(len), "l"(pol)
-                   : "memory");
+      const uint32_t end = pf.bytes[r] - off < chunk ? pf.bytes[r] : off + chunk;
+      for (uint32_t o = off; o < end; o += 65536u) {  // pieces of at most 64 KB
+        const uint32_t len = end - o < 65536u ? end - o : 65536u;
+        asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
+                         reinterpret_cast<const char*>(pf.p[r]) + o),
+                     "r"(len), "l"(pol)
+                     : "memory");
+      }
     }
   }
 }
@@ -1152,30 +1155,82 @@ __global__ void __launch_bounds__(kUThreads, 1)
       return true;
     };
     // the accumulators of one pass: wait for its last MMAs, add T[j][i] << (8 pass + 4 j + 8 i)
+    // sum_k w s of each row (the 2^23 offset of the activation limbs): the
+    // eight builders of a row add their chunks (every pass-0 plane is built
+    // when the last pass is read out), the read-out subtracts it.  Every
+    // builder thread reaches the named barrier exactly once.
+    bool rb_done = false;
+    auto row_bias = [&]() -> int64_t {
+      rb_done = true;
+#pragma unroll
+      for (int msk = 1; msk < 8; msk <<= 1) {
+        rbp0 += shfl_xor_i64(rbp0, msk);
+        rbp1 += shfl_xor_i64(rbp1, msk);
+      }
+      if (cc == 0) {
+        rbs[r0] = rbp0;
+        rbs[r0 + 64] = rbp1;
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kUThreads - 64) : "memory");
+      return rbs[r];
+    };
+    // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
+    // so each owner holds matching rows of both 64-row halves (gate and up);
+    // splits is a power of two (1, 2, 4 or 8), so these are shifts and masks
+    const int lsp = __ffs(splits) - 1;
+    const int rows_per = 64 >> lsp;
+    const int owner = (r & 63) >> (6 - lsp);
+    const int local = (r >> 6) * rows_per + (r & (rows_per - 1));
+    const int nl = 128 >> lsp;
+    // red[src][m][local]: a warp's 32 rows land contiguously (conflict-free)
+    int64_t* dst = red + ((size_t)split * SN + q * C::Q) * nl + local;
+    const uint32_t ca = splits > 1 ? umma::cluster_map(umma::smem_addr(dst), (uint32_t)owner) : 0u;
+    // the accumulators of one pass: wait for its last MMAs, add T[j][i] << (8 pass + 4 j + 8 i).
+    // The last pass sends each piece of sequences to its owner as soon as it
+    // is read, so the DSMEM stores (bound by the SM-to-SM network) overlap the
+    // remaining TMEM reads.
     auto read_pass = [&](int pass, int npass) -> bool {
       if (!umma::bar_wait(tfull, pass)) return false;
       umma::fence_after_sync();
       if (pass == 0 && warp == 2 && lane == 0) gemm_stamp(g, 3);
+      const bool last = pass + 1 == npass;
+      const int64_t bias = last ? row_bias() * (1LL << 23) : 0;
       // |T| < 120 * 255 * 1024 < 2^25 (K <= 1024 per CTA), so the two digits
       // of a limb combine in int32, X_i = T[0][i] + 16 T[1][i] (< 2^30), and
       // each limb adds X_i * 2^(8 i + 8 pass) with one widening multiply-add
-      // (TMEM is read in pieces of at most 8 columns: fewer live registers)
-      constexpr int kPiece = C::Q > 8 ? 8 : C::Q;
+      // pieces of kP sequences (a divisor of Q: 2, 3 or 4)
+      constexpr int kP = C::Q % 4 == 0 ? 4 : C::Q % 3 == 0 ? 3 : C::Q;
 #pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        const int32_t w = 1 << (8 * i + 8 * pass);
+      for (int j0 = 0; j0 < C::Q; j0 += kP) {
+        int32_t d[3][2][kP];
 #pragma unroll
-        for (int j0 = 0; j0 < C::Q; j0 += kPiece) {
-          int32_t d0[kPiece], d1[kPiece];
+        for (int i = 0; i < 3; ++i) {
           const uint32_t ta = lane_base + (uint32_t)(i * SN + q * C::Q + j0);
-          umma::tmem_ld_any<kPiece>(ta, d0);
-          umma::tmem_ld_any<kPiece>(ta + C::NM, d1);
-          umma::tmem_ld_wait();
+          umma::tmem_ld_any<kP>(ta, d[i][0]);
+          umma::tmem_ld_any<kP>(ta + C::NM, d[i][1]);
+        }
+        umma::tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < kPiece; ++j) acc[j0 + j] = mad_wide(d0[j] + 16 * d1[j], w, acc[j0 + j]);
+        for (int j = 0; j < kP; ++j) {
+          int64_t a = acc[j0 + j];
+#pragma unroll
+          for (int i = 0; i < 3; ++i) a = mad_wide(d[i][0][j] + 16 * d[i][1][j], 1 << (8 * i + 8 * pass), a);
+          acc[j0 + j] = a;
+        }
+        if (last) {
+#pragma unroll
+          for (int j = 0; j < kP; ++j) {
+            const int64_t v = acc[j0 + j] - bias;
+            // (the LM head's row sums overwrite plane slots: every builder
+            // finished them before its MMAs, whose completion was waited for)
+            if (splits == 1)
+              dst[(size_t)(j0 + j) * nl] = v;
+            else
+              umma::cluster_st64(ca + 8 * (j0 + j) * nl, v);
+          }
         }
       }
-      if (pass + 1 < npass) {
+      if (!last) {
         umma::fence_before_sync();
         __syncwarp();
         if (lane == 0) umma::bar_arrive(tempty);
@@ -1199,45 +1254,11 @@ __global__ void __launch_bounds__(kUThreads, 1)
     }
     if (!ok) fail();
     if (!dep_done) dependent_loads();
+    if (!rb_done) row_bias();
     if (warp == 2 && lane == 0) gemm_stamp(g, 4);
-    // sum_k w s of each row (the 2^23 offset of the activation limbs): the
-    // eight builders of a row add their chunks, the epilogue subtracts it
-#pragma unroll
-    for (int msk = 1; msk < 8; msk <<= 1) {
-      rbp0 += shfl_xor_i64(rbp0, msk);
-      rbp1 += shfl_xor_i64(rbp1, msk);
-    }
-    if (cc == 0) {
-      rbs[r0] = rbp0;
-      rbs[r0 + 64] = rbp1;
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kUThreads - 64) : "memory");
-    const int64_t rb = rbs[r];
-#pragma unroll
-    for (int j = 0; j < C::Q; ++j) acc[j] -= rb * (1LL << 23);
     cp_async_wait0();
     if constexpr (KIND == kGemmO || KIND == kGemmDown || KIND == kGemmGu)
       if (et < SN) live[et] = pos_m < c.max_ctx;
-    // partial sums to the owning CTA: owner of row r is (r % 64) / rows_per,
-    // so each owner holds matching rows of both 64-row halves (gate and up);
-    // splits is a power of two (1, 2, 4 or 8), so these are shifts and masks
-    const int lsp = __ffs(splits) - 1;
-    const int rows_per = 64 >> lsp;
-    const int owner = (r & 63) >> (6 - lsp);
-    const int local = (r >> 6) * rows_per + (r & (rows_per - 1));
-    const int nl = 128 >> lsp;
-    // red[src][m][local]: a warp's 32 rows land contiguously (conflict-free)
-    int64_t* dst = red + ((size_t)split * SN + q * C::Q) * nl + local;
-    if (splits == 1) {
-      // (the LM head's row sums overwrite plane slots: every builder finished
-      // them before its MMAs, whose completion every thread here waited for)
-#pragma unroll
-      for (int j = 0; j < C::Q; ++j) dst[(size_t)j * nl] = acc[j];
-    } else {
-      const uint32_t ca = umma::cluster_map(umma::smem_addr(dst), (uint32_t)owner);
-#pragma unroll
-      for (int j = 0; j < C::Q; ++j) umma::cluster_st64(ca + 8 * j * nl, acc[j]);
-    }
   }
   __syncwarp();
   if (splits > 1)
@@ -2376,6 +2397,16 @@ L2Prefetch pf_qkv(const BatchLayerW& w) {
 L2Prefetch pf_o(const BatchLayerW& w) {
   return L2Prefetch{{w.wo, w.so, nullptr, nullptr}, {(uint32_t)kHidden * kHidden, (uint32_t)kHidden * kHidden / 16, 0, 0}};
 }
+// the last layer's q/k/v GEMM also pulls the tied LM head (82.6 MB, fits L2
+// beside the streamed evict-first K/V) in, about 60 us before the LM head runs
+L2Prefetch pf_o_and_lm(const BatchLayerW& w, const uint8_t* emb, const uint16_t* semb, int vocab) {
+  L2Prefetch pf = pf_o(w);
+  pf.p[2] = emb;
+  pf.bytes[2] = (uint32_t)vocab * (kHidden / 2);
+  pf.p[3] = semb;
+  pf.bytes[3] = (uint32_t)vocab * (kHidden / kGroup) * 2;
+  return pf;
+}
 L2Prefetch pf_gu(const BatchLayerW& w) {
   return L2Prefetch{{w.wgate, w.wup, w.sgate, w.sup},
                     {(uint32_t)kInter * kHidden / 2, (uint32_t)kInter * kHidden / 2, (uint32_t)kInter * kHidden / 32,
@@ -2438,12 +2469,13 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   BMARK(kBkEmbed);
   for (int l = 0; l < p.n_layers; ++l) {
     const BatchLayerW& w = p.layers[l];
+    const bool last_layer = l + 1 == p.n_layers;
     BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, w.g_in, (int32_t*)nullptr));
     BMARK(kBkNorm);
     BQ(launch_gemm_sn<kGemmQkv>(q4gpu_batch_gemm_chunk(kGemmQkv, SP), w.mqkv, w.mqkv, p.mb_qkv, c, w.sqkv,
                                 (const uint16_t*)nullptr, kQRows + 2 * kKvRows, kHidden, decode_splits(kGemmQkv, SP),
                                 SP, (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 0), 1, 0,
-                                pf_o(w)));
+                                last_layer && !p.final_act ? pf_o_and_lm(w, p.emb, p.semb, p.vocab) : pf_o(w)));
     BMARK(kBkQkv);
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
@@ -2470,7 +2502,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     BQ(launch_gemm_sn<kGemmDown>(q4gpu_batch_gemm_chunk(kGemmDown, SP), w.mdown, w.mdown, p.mb_down, c, w.sdown,
                                  (const uint16_t*)nullptr, kHidden, kInter, decode_splits(kGemmDown, SP), SP,
                                  (const int32_t*)nullptr, (ArgBestD*)nullptr, s, gtrace(4 * l + 3), 1, 0,
-                                 l + 1 < p.n_layers ? pf_qkv(p.layers[l + 1]) : L2Prefetch{}));
+                                 last_layer ? L2Prefetch{} : pf_qkv(p.layers[l + 1])));
     BMARK(kBkDown);
   }
   BQ(launch_pdl(batch_norm_limbs_kernel, dim3(p.S), dim3(256), 0, s, c, 0, p.g_final, p.final_act));
