@@ -55,8 +55,10 @@ __device__ __forceinline__ int64_t inv_rms_from_ss(int64_t ss, NormConsts c) {
   const uint64_t rad = (uint64_t)(ss >> c.mean_shift) + (uint64_t)c.eps;
   const uint64_t rms = isqrt_u64(rad);
   if (rms == 0) return (1LL << 24) - 1;
-  const uint64_t q = (1ULL << c.div_shift) / rms;
-  return (int64_t)(q < (1ULL << 24) - 1 ? q : (1ULL << 24) - 1);
+  // rad < 2^47 (sums of at most 1024 squares of 24-bit values, shifted), so
+  // rms < 2^24 and both operands fit 32 bits: a 32-bit division, same quotient
+  const uint32_t q = (1u << c.div_shift) / (uint32_t)rms;
+  return (int64_t)(q < (1u << 24) - 1 ? q : (1u << 24) - 1);
 }
 
 __device__ __forceinline__ int32_t norm_apply(int32_t x, int64_t inv, int32_t gamma, NormConsts c) {

@@ -673,7 +673,7 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     block_sum2(e0, e1, sm.red);
     for (int i = t; i < 2 * kExpLut; i += blockDim.x) {
       const int hh = i / kExpLut, k = i % kExpLut;
-      sm.probtab[i] = ((uint64_t)sm.exp_lut[k] << 16) / (uint64_t)(hh ? e1 : e0);
+      sm.probtab[i] = udiv_exact((uint64_t)sm.exp_lut[k] << 16, (uint64_t)(hh ? e1 : e0));  // operands < 2^53
     }
   }
   __syncthreads();
