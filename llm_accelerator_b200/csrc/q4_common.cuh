@@ -176,31 +176,34 @@ __device__ __forceinline__ int64_t warp_sum_i64(int64_t v) {
   return v;
 }
 
-// Block-wide int64 sum; `red` needs blockDim/32 slots.  All threads get it.
+__device__ __forceinline__ int64_t warp_max_i64(int64_t v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const int64_t o = shfl_xor_i64(v, m);
+    v = o > v ? o : v;
+  }
+  return v;
+}
+
+// Block-wide int64 sum; `red` needs blockDim/32 slots.  All threads get it:
+// every warp combines the per-warp partials with shuffles (no serial chain of
+// shared-memory reads).
 __device__ __forceinline__ int64_t block_sum_i64(int64_t v, int64_t* red) {
   v = warp_sum_i64(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  int64_t t = 0;
-  for (int i = 0; i < nw; ++i) t += red[i];
-  return t;
+  return warp_sum_i64(lane < nw ? red[lane] : 0);
 }
 
 __device__ __forceinline__ int64_t block_max_i64(int64_t v, int64_t* red) {
-#pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    const int64_t o = shfl_xor_i64(v, m);
-    v = o > v ? o : v;
-  }
+  v = warp_max_i64(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  int64_t t = red[0];
-  for (int i = 1; i < nw; ++i) t = red[i] > t ? red[i] : t;
-  return t;
+  return warp_max_i64(lane < nw ? red[lane] : INT64_MIN);
 }
 
 // Programmatic dependent launch: wait for the producing grid's memory, and

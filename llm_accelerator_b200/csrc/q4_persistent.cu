@@ -179,13 +179,10 @@ __device__ __forceinline__ void hidden_norm_inplace(int32_t* act, const Gamma2& 
 }
 
 // Block-wide max (and sum) of two int64 values at once; red needs 32 slots.
+// Every warp finishes the per-warp partials with shuffles.
 __device__ __forceinline__ void block_max2(int64_t& x, int64_t& y, int64_t* red) {
-#pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    const int64_t ox = shfl_xor_i64(x, m), oy = shfl_xor_i64(y, m);
-    x = ox > x ? ox : x;
-    y = oy > y ? oy : y;
-  }
+  x = warp_max_i64(x);
+  y = warp_max_i64(y);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
   if (lane == 0) {
@@ -193,20 +190,13 @@ __device__ __forceinline__ void block_max2(int64_t& x, int64_t& y, int64_t* red)
     red[2 * warp + 1] = y;
   }
   __syncthreads();
-  x = red[0];
-  y = red[1];
-  for (int i = 1; i < nw; ++i) {
-    x = red[2 * i] > x ? red[2 * i] : x;
-    y = red[2 * i + 1] > y ? red[2 * i + 1] : y;
-  }
+  x = warp_max_i64(lane < nw ? red[2 * lane] : INT64_MIN);
+  y = warp_max_i64(lane < nw ? red[2 * lane + 1] : INT64_MIN);
 }
 
 __device__ __forceinline__ void block_sum2(int64_t& x, int64_t& y, int64_t* red) {
-#pragma unroll
-  for (int m = 16; m > 0; m >>= 1) {
-    x += shfl_xor_i64(x, m);
-    y += shfl_xor_i64(y, m);
-  }
+  x = warp_sum_i64(x);
+  y = warp_sum_i64(y);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   __syncthreads();
   if (lane == 0) {
@@ -214,12 +204,8 @@ __device__ __forceinline__ void block_sum2(int64_t& x, int64_t& y, int64_t* red)
     red[2 * warp + 1] = y;
   }
   __syncthreads();
-  x = 0;
-  y = 0;
-  for (int i = 0; i < nw; ++i) {
-    x += red[2 * i];
-    y += red[2 * i + 1];
-  }
+  x = warp_sum_i64(lane < nw ? red[2 * lane] : 0);
+  y = warp_sum_i64(lane < nw ? red[2 * lane + 1] : 0);
 }
 
 // ---- GEMV items with weights preloaded into registers -----------------------
