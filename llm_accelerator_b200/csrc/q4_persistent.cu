@@ -517,11 +517,12 @@ __device__ __forceinline__ void preload_dslice(const LayerW& w, int gc, const PS
 
 // Layer input hidden state, every CTA the whole vector: the embedding (layer 0,
 // already in hid) or post + (down >> 2) of the previous layer from its partial sums.
+// (two elements per thread, both partial sums requested before either is used)
 __device__ __forceinline__ void build_hidden(const PersistArgs& a, const PSmem& sm, int par_prev) {
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
-    const int32_t dn = sat24(ldcg64(acc_row(a, 2 + par_prev, i)) >> 14);
-    sm.hid[i] = sat24((int64_t)sm.post[i] + (dn >> 2));
-  }
+  const int i0 = threadIdx.x, i1 = threadIdx.x + kPThreads;
+  const int64_t d0 = ldcg64(acc_row(a, 2 + par_prev, i0)), d1 = ldcg64(acc_row(a, 2 + par_prev, i1));
+  sm.hid[i0] = sat24((int64_t)sm.post[i0] + (sat24(d0 >> 14) >> 2));
+  sm.hid[i1] = sat24((int64_t)sm.post[i1] + (sat24(d1 >> 14) >> 2));
 }
 
 __device__ void stage_qkv(const PersistArgs& a, const LayerW& w, const PSmem& sm, bool first_layer, int par_prev,
@@ -712,11 +713,15 @@ __device__ void stage_gateup_down(const PersistArgs& a, const LayerW& w, const P
   const int gc = (int)blockIdx.x - kAttnCtas;
   const bool gu = gc >= 0 && gc < kGuCtas;
   const Gamma2 gamma(w.g_post);
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
-    const int32_t o = sat24(ldcg64(acc_row(a, par, i)) >> 14);
-    const int32_t post = sat24((int64_t)sm.hid[i] + (o >> 2));
-    sm.post[i] = post;
-    sm.act[i] = post;
+  {
+    const int i0 = threadIdx.x, i1 = threadIdx.x + kPThreads;
+    const int64_t s0 = ldcg64(acc_row(a, par, i0)), s1 = ldcg64(acc_row(a, par, i1));
+    const int32_t p0 = sat24((int64_t)sm.hid[i0] + (sat24(s0 >> 14) >> 2));
+    const int32_t p1 = sat24((int64_t)sm.hid[i1] + (sat24(s1 >> 14) >> 2));
+    sm.post[i0] = p0;
+    sm.act[i0] = p0;
+    sm.post[i1] = p1;
+    sm.act[i1] = p1;
   }
   if (!gu) return;
   __syncthreads();
