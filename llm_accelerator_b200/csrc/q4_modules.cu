@@ -837,6 +837,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) gemv_mma_kernel(const __grid_co
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  // the weights do not depend on earlier kernels: the next launch may start
+  // its own weight loads now, and this one waits only before reading the
+  // activation (programmatic dependent launch)
+  grid_dep_launch();
   int64_t best_s = INT64_MIN;
   int32_t best_i = INT32_MAX;
   if (warp == kMvWarps) {
@@ -879,6 +883,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) gemv_mma_kernel(const __grid_co
       }
     }
   } else {
+    grid_dep_wait();
     mv_stage_b(g.act, K, bf, bq, tid, kMvWarps * 32);
     mv_consumer_sync();
     const MvMasks mk;
@@ -1144,8 +1149,21 @@ int mv_launch(const GemvArgs& g, int grid_cap, cudaStream_t s) {
       cudaFuncSetAttribute(gemv_mma_kernel<K, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
   if (e != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "GEMV shared memory: %s", cudaGetErrorString(e));
   const int64_t tiles = (int64_t)((g.rows + 15) / 16) * g.count;
-  const int grid = (int)std::min<int64_t>(tiles, std::min(grid_cap, 148));
-  gemv_mma_kernel<K, MODE><<<grid, kMvThreads, C::SMEM, s>>>(maps, g);
+  // at least two 16-row tiles per CTA: a small matrix leaves SMs free for the
+  // next launch, whose weight loads then overlap this one (PDL)
+  const int grid = (int)std::min<int64_t>((tiles + 1) / 2, std::min(grid_cap, 148));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kMvThreads);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, gemv_mma_kernel<K, MODE>, maps, g);
+  if (le != cudaSuccess) return q4gpu_fail(Q4GPU_ERR_CUDA, "GEMV launch: %s", cudaGetErrorString(le));
   return q4gpu_check_launch();
 }
 
