@@ -589,6 +589,16 @@ enum {
 int q4gpu_model_time_kernels(q4gpu_model *m, uintptr_t base, int32_t reps, double *ms_per_launch,
                              int32_t *launches_per_step);
 
+/* Mean device time of one decoder layer on the per-stage path at `position`
+ * for slot `base`: each layer of [layer_start, layer_start + layer_count) runs
+ * as its own CUDA graph (its five kernels PDL-chained, no embedding, no LM
+ * head) and is timed with events, the layers in turn for `reps` cycles after
+ * one warm-up cycle (so a layer's weights and K/V are not still in L2 from its
+ * previous replay when the range is large); the position is reset before every
+ * replay.  No reference counterpart (measurement). */
+int q4gpu_model_time_layers(q4gpu_model *m, uintptr_t base, int32_t layer_start, int32_t layer_count,
+                            int32_t position, int32_t reps, double *ms);
+
 /* Stream the context launches on (a cudaStream_t), for timing. */
 void *q4gpu_model_stream(q4gpu_model *m);
 

@@ -151,6 +151,7 @@ SIGNATURES = {
     "q4gpu_model_set_position": (C.c_int, [P, C.c_size_t, I32]),
     "q4gpu_model_read_tokens": (C.c_int, [P, C.c_size_t, I32, I32, P, P, P]),
     "q4gpu_model_time_kernels": (C.c_int, [P, C.c_size_t, I32, P, P]),
+    "q4gpu_model_time_layers": (C.c_int, [P, C.c_size_t, I32, I32, I32, I32, P]),
     "q4gpu_model_get_config": (C.c_int, [P, C.POINTER(ModelConfig)]),
     "q4gpu_qmap_read_packet": (C.c_int, [P, U64, U64, U64, C.POINTER(QmapHeader), C.POINTER(QmapDescriptor), I32]),
     "q4gpu_qmap_bind": (C.c_int, [P, U64, C.POINTER(QmapLayout), C.POINTER(QmapTensor), I32, C.POINTER(I32)]),

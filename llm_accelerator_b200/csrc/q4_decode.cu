@@ -1898,6 +1898,42 @@ int q4gpu_model_time_kernels(q4gpu_model* m, uintptr_t base, int32_t reps, doubl
   return Q4GPU_OK;
 }
 
+int q4gpu_model_time_layers(q4gpu_model* m, uintptr_t base, int32_t layer_start, int32_t layer_count,
+                            int32_t position, int32_t reps, double* ms) {
+  if (!m || base >= (uintptr_t)m->cfg.max_seqs || layer_start < 0 || layer_count <= 0 ||
+      layer_start + layer_count > m->cfg.n_layers || position < 0 || position >= m->cfg.max_context || reps <= 0 || !ms)
+    return q4gpu_fail(Q4GPU_ERR_ARG, "bad time_layers");
+  int rc = set_device(m);
+  if (rc) return rc;
+  std::vector<cudaGraphExec_t> g((size_t)layer_count);
+  for (int i = 0; i < layer_count; ++i)
+    if ((rc = get_graph(m, GraphKey{(int)base, layer_start + i, 1, 0, 0}, &g[(size_t)i]))) return rc;
+  cudaEvent_t e0, e1;
+  Q4_CUDA(cudaEventCreate(&e0));
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return q4gpu_fail(Q4GPU_ERR_CUDA, "event create");
+  }
+  double tot = 0.0;
+  for (int r = 0; r < reps + 1 && rc == Q4GPU_OK; ++r)  // the first cycle warms up
+    for (int i = 0; i < layer_count && rc == Q4GPU_OK; ++i) {
+      float t = 0.f;
+      const bool ok =
+          launch_k(set_pos_kernel, dim3(1), dim3(32), 0, m->stream, m->slots[base], (int)position) == cudaSuccess &&
+          cudaEventRecord(e0, m->stream) == cudaSuccess && cudaGraphLaunch(g[(size_t)i], m->stream) == cudaSuccess &&
+          cudaEventRecord(e1, m->stream) == cudaSuccess && cudaEventSynchronize(e1) == cudaSuccess &&
+          cudaEventElapsedTime(&t, e0, e1) == cudaSuccess;
+      if (!ok) rc = q4gpu_fail(Q4GPU_ERR_CUDA, "time_layers: %s", cudaGetErrorString(cudaGetLastError()));
+      if (r > 0) tot += t;
+    }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (rc) return rc;
+  if ((rc = check_persistent_error(m))) return rc;
+  *ms = tot / ((double)reps * layer_count);
+  return Q4GPU_OK;
+}
+
 int q4gpu_batch_time_kernels(q4gpu_model* m, int32_t first_slot, int32_t n_seq, int32_t reps, double* ms_per_launch,
                              int32_t* launches_per_step) {
   int rc = batch_range_ok(m, first_slot, n_seq);

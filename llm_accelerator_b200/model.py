@@ -311,6 +311,15 @@ class Q4Model:
                                                        C.byref(pos)), "q4gpu_model_read_tokens")
         return t[:n].astype(np.int64), s[:n], pos.value
 
+    def time_layers(self, layer_start: int, layer_count: int, position: int, reps: int = 3, slot: int = 0) -> float:
+        """Mean device ms of one per-stage layer at `position`: each layer of
+        [layer_start, +layer_count) as its own graph (PDL-chained kernels, no
+        embedding, no LM head), the layers timed in turn for `reps` cycles."""
+        ms = np.zeros(1, dtype=np.float64)
+        _native.check(self.lib.q4gpu_model_time_layers(self.handle, slot, layer_start, layer_count, position, reps,
+                                                       _ptr(ms)), "q4gpu_model_time_layers")
+        return float(ms[0])
+
     def time_kernels(self, reps: int = 3, slot: int = 0) -> dict[str, tuple[float, int]]:
         """Mean device ms per launch and launches per step of each kernel kind."""
         ms = np.zeros(8, dtype=np.float64)

@@ -155,6 +155,25 @@ def test_single_layer_long_context_matches_oracle(ctx, pos):
         gm.close()
 
 
+def test_time_layers_replays_the_layer_graphs():
+    """q4gpu_model_time_layers runs the one-layer graph of the per-stage path at
+    a reset position: after its warm-up and one timed replay the hidden state
+    is the oracle's layer applied twice at that position (zero cache before)."""
+    seed, ctx, pos = 21, 300, 270
+    with Q4Model(n_layers=1, vocab=256, max_context=ctx, max_seqs=1) as gm:
+        gm.init_synthetic(seed=seed)
+        gm.mode = 0
+        om = oracle_small(seed, 1, 256, ctx)
+        h = O.quantize_signed(O.synth_f32(seed, 903, (1024,), 1.0), 24, 10)[0]
+        gm.write_hidden(h)
+        assert gm.time_layers(0, 1, pos, reps=1) > 0
+        st = O.DecodeState(1, ctx)
+        x = h
+        for _ in range(2):
+            x = O.layer_step(om.layers[0], x, pos, st.k[0], st.v[0], om.cos, om.sin, om.exp_lut, om.sigmoid_lut)
+        assert np.array_equal(gm.read_hidden(), x)
+
+
 def test_full_model_matches_reference_golden(refmodel):
     """The 28-layer, 151936-vocabulary seed-0 model: every per-position argmax
     and score of the reference's own chained fixed-point functions, then the
