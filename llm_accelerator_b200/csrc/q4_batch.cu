@@ -441,6 +441,7 @@ __global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, Attn
 constexpr int kAttnChunk = 32;
 constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
 constexpr int kAttnRing = 2;
+constexpr int kStageAttnRing = 4;
 
 __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
@@ -1642,20 +1643,20 @@ constexpr int kClKprMax = 4096;  // keys per rank the score buffer holds
 // limbs).  STAGE = true: one slot of the per-stage batch-1 path (q heads
 // already normed and roped in st.qrope, the new K/V row already in the cache;
 // output st.attn).
-template <bool STAGE>
+template <bool STAGE, int RING>
 __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState& st, int* err, int layer,
                                              const int32_t* __restrict__ g_q, const int32_t* __restrict__ g_k,
                                              const int32_t* __restrict__ cos_tab, const int32_t* __restrict__ sin_tab,
                                              const int32_t* __restrict__ exp_lut, int kpr_cap) {
   extern __shared__ __align__(128) uint8_t cl_smem[];
   int32_t* ring = reinterpret_cast<int32_t*>(cl_smem);                            // [2][32][128]
-  int64_t* sc = reinterpret_cast<int64_t*>(cl_smem + kAttnRing * kAttnChunkBytes);  // [2][kpr_cap]
+  int64_t* sc = reinterpret_cast<int64_t*>(cl_smem + RING * kAttnChunkBytes);  // [2][kpr_cap]
   __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v of the new position
   __shared__ uint32_t probtab[2][kExpLut];
   __shared__ int64_t red[2][8];
   __shared__ int64_t xmax[2], xsum[2];       // published to the cluster
   __shared__ int64_t part[2][kHeadDim];      // this rank's value sums, published to the cluster
-  __shared__ uint64_t bars[kAttnRing];
+  __shared__ uint64_t bars[RING];
   const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = STAGE ? 0 : blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   // every rank reaches every cluster barrier below: no early return.  The
@@ -1676,16 +1677,16 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
     const int p0 = k0 + j * kAttnChunk;
     int n = kend - p0;
     n = n < 0 ? 0 : (n > kAttnChunk ? kAttnChunk : n);
-    uint64_t* b = bars + i % kAttnRing;
+    uint64_t* b = bars + i % RING;
     umma::bar_expect_tx(b, (uint32_t)n * kHeadDim * 4);
     if (n > 0)
-      bulk_load(ring + (i % kAttnRing) * kAttnChunk * kHeadDim, kvv.at(layer, kind, kv, p0), (uint32_t)n * kHeadDim * 4,
+      bulk_load(ring + (i % RING) * kAttnChunk * kHeadDim, kvv.at(layer, kind, kv, p0), (uint32_t)n * kHeadDim * 4,
                 b);
   };
   if (t == 0) {
-    for (int s = 0; s < kAttnRing; ++s) umma::bar_init(bars + s, 1);
+    for (int s = 0; s < RING; ++s) umma::bar_init(bars + s, 1);
     umma::bar_init_fence();
-    for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
+    for (int i = 0; i < total && i < RING; ++i) issue(i);
   }
   grid_dep_wait();
   grid_dep_launch();
@@ -1726,9 +1727,9 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
       q1[4 * j] = b.x; q1[4 * j + 1] = b.y; q1[4 * j + 2] = b.z; q1[4 * j + 3] = b.w;
     }
     for (int i = 0; i < nk; ++i) {
-      if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+      if (!umma::bar_wait(bars + i % RING, (i / RING) & 1)) ok = false;
       const int lp = i * kAttnChunk + warp * 4 + quad, p = k0 + lp;
-      const int32_t* krow = p == pos ? hv[2] : ring + ((i % kAttnRing) * kAttnChunk + warp * 4 + quad) * kHeadDim;
+      const int32_t* krow = p == pos ? hv[2] : ring + ((i % RING) * kAttnChunk + warp * 4 + quad) * kHeadDim;
       int64_t s0 = 0, s1 = 0;
       if (p < k1) {
 #pragma unroll
@@ -1757,7 +1758,7 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
         mx1 = v1 > mx1 ? v1 : mx1;
       }
       __syncthreads();  // slot i % 2 is free again
-      if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+      if (t == 0 && i + RING < total) issue(i + RING);
     }
   }
 #pragma unroll
@@ -1855,13 +1856,13 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
   // the chunk's keys warp, warp + 8, warp + 16, warp + 24 for both heads
   int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
   for (int i = nk; i < total; ++i) {
-    if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
+    if (!umma::bar_wait(bars + i % RING, (i / RING) & 1)) ok = false;
     const int base = (i - nk) * kAttnChunk;
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int lp = base + warp + 8 * u, p = k0 + lp;
       if (p < k1) {
-        const int32_t* vrow = p == pos ? hv[3] : ring + ((i % kAttnRing) * kAttnChunk + warp + 8 * u) * kHeadDim;
+        const int32_t* vrow = p == pos ? hv[3] : ring + ((i % RING) * kAttnChunk + warp + 8 * u) * kHeadDim;
         const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
         const int32_t p0 = (int32_t)sc[lp], p1 = (int32_t)sc[kpr_cap + lp];
         const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -1873,7 +1874,7 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
       }
     }
     __syncthreads();
-    if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+    if (t == 0 && i + RING < total) issue(i + RING);
   }
   if (!ok) atomicExch(err, 4);
   // cross-warp sums through the idle ring [8][2][128], then published
@@ -1919,13 +1920,15 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
                                                             const int32_t* __restrict__ cos_tab,
                                                             const int32_t* __restrict__ sin_tab,
                                                             const int32_t* __restrict__ exp_lut, int kpr_cap) {
-  attn_cl_body<false>(c, SlotState{}, c.err, layer, g_q, g_k, cos_tab, sin_tab, exp_lut, kpr_cap);
+  attn_cl_body<false, kAttnRing>(c, SlotState{}, c.err, layer, g_q, g_k, cos_tab, sin_tab, exp_lut, kpr_cap);
 }
 
 // Attention of the per-stage batch-1 path (grid: ranks x 8 KV heads, one cluster per head).
+// 128 CTAs leave room for a 4-slot ring: a rank's keys of a 513-position
+// context (2 K + 2 V chunks) are all in flight at once.
 __global__ void __launch_bounds__(256) stage_attn_cl_kernel(SlotState st, int* err, int layer,
                                                             const int32_t* __restrict__ exp_lut, int kpr_cap) {
-  attn_cl_body<true>(BatchCtx{}, st, err, layer, nullptr, nullptr, nullptr, nullptr, exp_lut, kpr_cap);
+  attn_cl_body<true, kStageAttnRing>(BatchCtx{}, st, err, layer, nullptr, nullptr, nullptr, nullptr, exp_lut, kpr_cap);
 }
 
 // Per (KV head, column): q heads 2 kv, 2 kv + 1 normed and roped in place in
@@ -2569,7 +2572,9 @@ namespace {
 int stage_attn_kpr(int max_ctx) {
   return ((max_ctx + kStageAttnRanks - 1) / kStageAttnRanks + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
 }
-size_t stage_attn_smem(int max_ctx) { return (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * stage_attn_kpr(max_ctx) * 8; }
+size_t stage_attn_smem(int max_ctx) {
+  return (size_t)kStageAttnRing * kAttnChunkBytes + (size_t)2 * stage_attn_kpr(max_ctx) * 8;
+}
 }  // namespace
 
 bool q4gpu_stage_attention_fits(int max_ctx) { return max_ctx > 0 && stage_attn_kpr(max_ctx) <= kClKprMax; }

@@ -60,7 +60,11 @@ __global__ void embed_step_kernel(SlotState st, const uint8_t* __restrict__ W, c
   }
 }
 
-// One CTA per head: 16 q heads, 8 k heads, 8 v heads (128 rows each).
+// A cluster of four CTAs per head (16 q heads, 8 k heads, 8 v heads; 128
+// rows each): CTA rank c computes dims [16 c, 16 c + 16) and their RoPE
+// partners [64 + 16 c, 64 + 16 c + 16), 32 rows, so the rotation stays in the
+// CTA; the per-head norm's sum of squares crosses the cluster over DSMEM.
+constexpr int kQkvRanks = 4;
 __global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, int layer,
                                                        const int32_t* __restrict__ cos_tab,
                                                        const int32_t* __restrict__ sin_tab) {
@@ -68,50 +72,74 @@ __global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, i
   __shared__ __align__(16) uint32_t limbs[limb_words(kHidden)];
   __shared__ int64_t bias8[kHidden / 32];
   __shared__ int64_t red[8];
-  __shared__ int32_t y[kHeadDim], z[kHeadDim];
-  const int head = blockIdx.x;
+  __shared__ int64_t part_ss;  // this CTA's sum of squares, read by the cluster
+  __shared__ int32_t y[2 * 16];
+  const int head = blockIdx.x / kQkvRanks, c = blockIdx.x % kQkvRanks;
   const int row0 = head * kHeadDim;
+  const int lo = 16 * c, hi = 64 + 16 * c;  // this CTA's two 16-dim runs
   if (threadIdx.x == 0) {
-    prefetch_l2(w.wqkv + (size_t)row0 * 512, kHeadDim * 512);
-    prefetch_l2(w.sqkv + (size_t)row0 * 16, kHeadDim * 32);
+    prefetch_l2(w.wqkv + (size_t)(row0 + lo) * 512, 16 * 512);
+    prefetch_l2(w.wqkv + (size_t)(row0 + hi) * 512, 16 * 512);
+    prefetch_l2(w.sqkv + (size_t)(row0 + lo) * 16, 16 * 32);
+    prefetch_l2(w.sqkv + (size_t)(row0 + hi) * 16, 16 * 32);
   }
   grid_dep_wait();
   grid_dep_launch();
-  if (*st.pos >= st.max_ctx) return;
-  hidden_norm_to(st.hidden, w.g_in, a, red);
-  __syncthreads();
-  stage_limbs(a, kHidden, limbs, bias8);
-  __syncthreads();
+  // every CTA of the cluster reaches both cluster barriers below: no early return
+  const bool live = *st.pos < st.max_ctx;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
+  if (live) {
+    hidden_norm_to(st.hidden, w.g_in, a, red);
+    __syncthreads();
+    stage_limbs(a, kHidden, limbs, bias8);
+    __syncthreads();
+    // warps 0-3: rows lo + 4 w .. + 3; warps 4-7: rows hi + 4 (w - 4) .. + 3
     int64_t acc[4] = {0, 0, 0, 0};
-    const int r0 = warp * 16 + pass * 4;
+    const int r0 = warp < 4 ? lo + 4 * warp : hi + 4 * (warp - 4);
     gemv_slice<kHidden, 4>(w.wqkv, w.sqkv, row0 + r0, kQRows + 2 * kKvRows, 0, limbs, bias8, acc);
     warp_reduce_rows<4>(acc);
-    if (lane < 4) y[r0 + lane] = sat24(acc[lane] >> 14);
+    if (lane < 4) y[4 * warp + lane] = sat24(acc[lane] >> 14);  // y[j]: dim lo + j (j < 16), hi + j - 16
   }
   __syncthreads();
-  const int pos = *st.pos;
-  const int d = threadIdx.x;
-  if (head < kQHeads + kKvHeads) {
-    const int32_t* gamma = head < kQHeads ? w.g_q : w.g_k;
-    int64_t ss = d < kHeadDim ? (int64_t)y[d] * y[d] : 0;
-    ss = block_sum_i64(ss, red);
-    const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
-    if (d < kHeadDim) z[d] = norm_apply(y[d], inv, gamma[d], kHeadNorm);
-    __syncthreads();
-    if (d < kHeadDim) {
-      const int64_t rot = d < 64 ? -(int64_t)z[d + 64] : (int64_t)z[d - 64];
-      const int32_t r = sat24(((int64_t)z[d] * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
+  const bool normed = head < kQHeads + kKvHeads;
+  const int t = threadIdx.x;
+  if (t < 32) {
+    int64_t ss = normed && live ? (int64_t)y[t] * y[t] : 0;
+    ss = warp_sum_i64(ss);
+    if (t == 0) part_ss = ss;
+  }
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  if (live && t < 32) {
+    const int pos = *st.pos;
+    const int d = t < 16 ? lo + t : hi + (t - 16);
+    if (normed) {
+      int64_t ss = 0;
+#pragma unroll
+      for (int r = 0; r < kQkvRanks; ++r) {
+        uint32_t addr;
+        int64_t v;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(addr) : "r"((uint32_t)__cvta_generic_to_shared(&part_ss)), "r"(r));
+        asm volatile("ld.shared::cluster.b64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+        ss += v;
+      }
+      const int32_t* gamma = head < kQHeads ? w.g_q : w.g_k;
+      const int64_t inv = inv_rms_from_ss(ss, kHeadNorm);
+      // z of this dim and of its RoPE partner (the other run, same offset)
+      const int tp = t < 16 ? t + 16 : t - 16, dp = t < 16 ? hi + t : lo + (t - 16);
+      const int32_t z = norm_apply(y[t], inv, gamma[d], kHeadNorm);
+      const int32_t zp = norm_apply(y[tp], inv, gamma[dp], kHeadNorm);
+      const int64_t rot = d < 64 ? -(int64_t)zp : (int64_t)zp;
+      const int32_t r = sat24(((int64_t)z * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
       if (head < kQHeads)
         st.qrope[head * kHeadDim + d] = r;
       else
         st.kv.at(layer, 0, head - kQHeads, pos)[d] = r;
+    } else {
+      st.kv.at(layer, 1, head - kQHeads - kKvHeads, pos)[d] = y[t];
     }
-  } else if (d < kHeadDim) {
-    st.kv.at(layer, 1, head - kQHeads - kKvHeads, pos)[d] = y[d];
   }
+  // no CTA leaves while another may still read its part_ss
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // One CTA per KV head (its two query heads) of one slot.  Exact two-pass
@@ -650,6 +678,26 @@ cudaError_t launch_k(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStrea
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
+// The same with thread-block clusters of cluster_x CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kc(void (*k)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t s, int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g;
+  cfg.blockDim = b;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
 size_t attn_smem(int max_ctx) { return (size_t)2 * max_ctx * sizeof(int64_t); }
 
 // Per-kernel event marks for q4gpu_model_time_kernels (kinds as in q4gpu.h).
@@ -686,8 +734,8 @@ int enqueue_step(q4gpu_model* m, int slot, int layer_start, int layer_count, int
   for (int l = layer_start; l < layer_start + layer_count; ++l) {
     const LayerW& w = m->layers[l];
     if ((rc = mark(Q4GPU_K_QKV))) return rc;
-    Q4_CUDA(launch_k(qkv_step_kernel, dim3(kQHeads + 2 * kKvHeads), dim3(256), 0, s, st, w, l,
-                     (const int32_t*)m->cos_tab, (const int32_t*)m->sin_tab));
+    Q4_CUDA(launch_kc(qkv_step_kernel, dim3((kQHeads + 2 * kKvHeads) * kQkvRanks), dim3(256), 0, s, kQkvRanks, st, w,
+                      l, (const int32_t*)m->cos_tab, (const int32_t*)m->sin_tab));
     if ((rc = mark(Q4GPU_K_ATTN))) return rc;
     if (m->stage_attn_cl) {
       if ((rc = q4gpu_enqueue_stage_attention(st, m->p_err, l, (const int32_t*)m->exp_lut, m->cfg.max_context, s)))
