@@ -100,8 +100,9 @@ __global__ void batch_set_pos_kernel(const SlotState* __restrict__ slots, int S,
 }
 
 __global__ void batch_embed_kernel(BatchCtx c, const uint8_t* __restrict__ W, const uint16_t* __restrict__ S) {
-  grid_dep_wait();
+  // the next kernel may start its own set-up now (it waits for this one before reading)
   grid_dep_launch();
+  grid_dep_wait();
   const int m = blockIdx.x;
   const int pos = c.pos0[4 * m];
   if (pos >= c.max_ctx) return;
@@ -125,8 +126,9 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
   const int m = blockIdx.x, k = 4 * threadIdx.x;
   // the norm weights do not depend on earlier kernels: load them before the wait
   const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
-  grid_dep_wait();
+  // the next kernel may start its own set-up now (it waits for this one before reading)
   grid_dep_launch();
+  grid_dep_wait();
   const int sub = m / c.SP, ms = m - sub * c.SP;
   uint8_t* bt = c.bt1 + (size_t)sub * c.bt_sub1;
   const int4 x = *reinterpret_cast<const int4*>((which == 0 ? c.hidden0 : c.post0) + (size_t)m * kHidden + k);
@@ -1492,8 +1494,9 @@ __global__ void batch_commit_shards_kernel(BatchCtx c, const int64_t* __restrict
 __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ partial, int n_parts) {
   __shared__ int64_t ss[32];
   __shared__ int32_t si[32];
-  grid_dep_wait();
+  // the next kernel may start its own set-up now (it waits for this one before reading)
   grid_dep_launch();
+  grid_dep_wait();
   const int m = blockIdx.x;
   const SlotState& st = c.slots[m];
   int64_t bs = INT64_MIN;
