@@ -100,9 +100,10 @@ __global__ void batch_set_pos_kernel(const SlotState* __restrict__ slots, int S,
 }
 
 __global__ void batch_embed_kernel(BatchCtx c, const uint8_t* __restrict__ W, const uint16_t* __restrict__ S) {
-  // the next kernel may start its own set-up now (it waits for this one before reading)
-  grid_dep_launch();
+  // released only after the wait: kernels later in the step read the
+  // positions (advanced by the previous step's argmax) before their own waits
   grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.x;
   const int pos = c.pos0[4 * m];
   if (pos >= c.max_ctx) return;
@@ -126,7 +127,11 @@ __global__ void __launch_bounds__(256) batch_norm_limbs_kernel(BatchCtx c, int w
   const int m = blockIdx.x, k = 4 * threadIdx.x;
   // the norm weights do not depend on earlier kernels: load them before the wait
   const int4 gm = *reinterpret_cast<const int4*>(gamma + k);
-  // the next kernel may start its own set-up now (it waits for this one before reading)
+  // the next GEMM may start its weight-only set-up now (it waits for this
+  // kernel before reading its output).  Safe here, inside a step: the first
+  // norm of a step starts only after the embedding's wait, so nothing that
+  // reads the positions before its own wait can start before the previous
+  // step's argmax has completed.
   grid_dep_launch();
   grid_dep_wait();
   const int sub = m / c.SP, ms = m - sub * c.SP;
@@ -1494,9 +1499,9 @@ __global__ void batch_commit_shards_kernel(BatchCtx c, const int64_t* __restrict
 __global__ void batch_argmax_kernel(BatchCtx c, const ArgBestD* __restrict__ partial, int n_parts) {
   __shared__ int64_t ss[32];
   __shared__ int32_t si[32];
-  // the next kernel may start its own set-up now (it waits for this one before reading)
-  grid_dep_launch();
+  // released only after the wait (see batch_embed_kernel)
   grid_dep_wait();
+  grid_dep_launch();
   const int m = blockIdx.x;
   const SlotState& st = c.slots[m];
   int64_t bs = INT64_MIN;
