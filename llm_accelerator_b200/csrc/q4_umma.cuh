@@ -36,26 +36,16 @@ __device__ __forceinline__ bool bar_try_wait(uint64_t* b, unsigned parity) {
       : "memory");
   return ok != 0;
 }
-// The same with a suspend-time hint: a thread whose phase is not complete is
-// suspended in hardware (no issue slots) until it completes or the hint runs out.
-__device__ __forceinline__ bool bar_try_wait_hint(uint64_t* b, unsigned parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_addr(b)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
 // Wait for the phase of the given parity; gives up after `limit_ns` and
-// returns false (the caller records the error and winds down).  Waiting
-// threads stay suspended, so they leave the issue slots to working warps.
+// returns false (the caller records the error and winds down).  (A variant
+// that passed a suspend-time hint to try_wait slowed the cluster attention's
+// ring by a quarter: the plain try_wait loop stays.)
 __device__ __forceinline__ bool bar_wait(uint64_t* b, unsigned parity, uint64_t limit_ns = 200000000ull) {
   if (bar_try_wait(b, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
-    if (bar_try_wait_hint(b, parity, 20000u)) return true;
-    if ((it & 15u) == 0 && global_ns() - t0 > limit_ns) return false;
+    if (bar_try_wait(b, parity)) return true;
+    if ((it & 255u) == 0 && global_ns() - t0 > limit_ns) return false;
   }
 }
 
