@@ -264,6 +264,7 @@ __global__ void __launch_bounds__(256) batch_attn_scores_kernel(BatchCtx c, Attn
     *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
     if (warp == 2) {
       reinterpret_cast<int4*>(kvv.at(layer, 0, h, pos))[lane] = o4;
+      kpl_put4(kvv, layer, h, pos, 4 * lane, o4);
       asm volatile("fence.proxy.async.global;" ::: "memory");  // later bulk copies read this row
     }
   } else if (warp == 3 && has_new) {
@@ -436,60 +437,102 @@ __global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, Attn
 
 // Attention for one (KV head, sequence): q/k head RMSNorm + RoPE, KV append,
 // exact two-pass LUT softmax for the two query heads of the group; writes the
-// output and its limbs (the o_proj B matrix).  256 threads.  K, then V, of the
-// earlier positions stream through a 2-slot ring of 32-position chunks (16 KB
-// bulk copies, contiguous inside a KV page); the current position's K/V row
-// is taken from shared memory.  The score maxima are kept while the scores
-// are made, so the softmax is one pass over the (shared-memory) scores.
-// Used when the batch has enough (KV head, sequence) pairs to fill the GPU
-// and contexts up to 1024; smaller batches and longer contexts use the
-// cluster kernel (batch_attn_cl_kernel), the longest ones the split-KV
-// kernels above.
+// output and its limbs (the o_proj B matrix).  256 threads.  Used when the
+// batch has enough (KV head, sequence) pairs to fill the GPU and contexts up
+// to 1024; smaller batches and longer contexts use the cluster kernel
+// (batch_attn_cl_kernel), the longest ones the split-KV kernels above.
+//
+// Scores on the tensor cores.  With the query split into the unsigned byte
+// limbs c_b of c = q + 2^23 and the cached key into its byte planes k_a
+// (k = sum_a 2^(8 a) k_a, k_2 signed; KvView::kpl),
+//   q . k = sum_a 2^(8 a) (sum_b 2^(8 b) D_a[b] - 2^23 D_a[ones]),
+//   D_a[x] = sum_d k_a[d] x[d]  (|D_a| < 2^23, exact in int32),
+// so a 128-key chunk takes one M128 x N16 x K128 kind::i8 product per plane:
+// A = the plane's 128 key rows as copied from the cache (two pages), B = 16
+// rows of query bytes (c_b of both heads, a row of ones, zero rows), D in
+// TMEM, read back by warps 0-3 (lane = key) and combined in int64.  The
+// current position's key comes from this kernel's own q/k/v row and is
+// scored on the CUDA cores.  Values stay on the CUDA cores (int64 products of
+// the int32 V rows).  One ring of two 16 KB slots carries first the chunks'
+// key planes (loads i = 0 .. 3 nch - 1, plane i % 3 of chunk i / 3, released
+// by the MMA's commit), then the V rows in 32-position chunks (released by a
+// block barrier); the first loads start before the dependency wait.
 constexpr int kAttnChunk = 32;
 constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
 constexpr int kAttnRing = 2;
 constexpr int kStageAttnRing = 4;
+constexpr int kTcKeys = 128;                  // keys per score chunk (the MMA's M)
+constexpr int kTcSlot = 16384;                // ring slot: one key plane of a chunk, or 32 V rows
+constexpr int kTcSmemFixed = 1024 + 2 * kTcSlot + 16 * 128;  // alignment slack, ring, query bytes
+constexpr uint32_t kTcCols = 64;              // TMEM columns: D of three planes x 16
 
 __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
                                                             const int32_t* __restrict__ cos_tab,
                                                             const int32_t* __restrict__ sin_tab,
                                                             const int32_t* __restrict__ exp_lut) {
-  extern __shared__ __align__(128) uint8_t attn_smem[];
-  int32_t* ring = reinterpret_cast<int32_t*>(attn_smem);                            // [kAttnRing][32][128]
-  int64_t* sc = reinterpret_cast<int64_t*>(attn_smem + kAttnRing * kAttnChunkBytes);  // [2][ctx]
+  extern __shared__ uint8_t attn_raw[];
+  // 128-byte-swizzled operand tiles need 1024-byte alignment
+  const uint32_t raw_addr = umma::smem_addr(attn_raw);
+  uint8_t* sbase = attn_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* slots = sbase;                                   // [2][16 KB]
+  uint8_t* qb = sbase + 2 * kTcSlot;                        // [16][128] query bytes
+  int64_t* sc = reinterpret_cast<int64_t*>(qb + 16 * 128);  // [2][ctx]
   __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v
   __shared__ uint32_t probtab[2][kExpLut];
   __shared__ int64_t red[2][8];
-  __shared__ uint64_t bars[kAttnRing];
+  __shared__ uint64_t full[2], empty[2], dfull, dempty, mdone;
+  __shared__ uint32_t tmem_slot;
   const int kv = blockIdx.x, m = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   attn_stamp(c, layer, m, kv, 0);
   // The cached K/V rows (positions < pos, written by earlier steps) and the
   // position itself (advanced at the end of the previous step) do not depend
-  // on the kernels of this step: the first chunks load before the wait for
+  // on the kernels of this step: the first loads start before the wait for
   // the q/k/v projections.
   const int pos = c.pos0[4 * m];
   if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
   const KvView kvv = c.slots[m].kv;
-  // chunks 0 .. nk-1: K, nk .. 2 nk-1: V, positions [32 j, min(32 j + 32, pos))
-  const int nk = (ctx + kAttnChunk - 1) / kAttnChunk, total = 2 * nk;
+  const int nch = (pos + kTcKeys - 1) / kTcKeys;       // score chunks of the cached keys [0, pos)
+  const int nkp = 3 * nch;                             // key-plane loads
+  const int nk = (ctx + kAttnChunk - 1) / kAttnChunk;  // V chunks of 32 positions
+  const int total = nkp + nk;
   auto issue = [&](int i) {
-    const int kind = i < nk ? 0 : 1, j = i < nk ? i : i - nk;
-    const int p0 = j * kAttnChunk;
-    const int n = (pos - p0) < kAttnChunk ? (pos - p0) : kAttnChunk;
-    uint64_t* b = bars + i % kAttnRing;
-    umma::bar_expect_tx(b, n > 0 ? (uint32_t)n * kHeadDim * 4 : 0u);
-    if (n > 0)
-      bulk_load(ring + (i % kAttnRing) * kAttnChunk * kHeadDim, kvv.at(layer, kind, kv, p0), (uint32_t)n * kHeadDim * 4,
-                b);
+    uint64_t* b = full + (i & 1);
+    uint8_t* dst = slots + (i & 1) * kTcSlot;
+    if (i < nkp) {
+      const int ch = i / 3, a = i - 3 * ch, k0 = ch * kTcKeys;
+      const int n0 = pos - k0 < kKvPage ? pos - k0 : kKvPage;  // >= 1
+      int n1 = pos - k0 - kKvPage;
+      n1 = n1 < 0 ? 0 : (n1 > kKvPage ? kKvPage : n1);
+      umma::bar_expect_tx(b, (uint32_t)(n0 + n1) * 128u);
+      bulk_load(dst, kvv.kplane(layer, kv, k0) + a * kKplPlane, (uint32_t)n0 * 128u, b);
+      if (n1 > 0)
+        bulk_load(dst + kKplPlane, kvv.kplane(layer, kv, k0 + kKvPage) + a * kKplPlane, (uint32_t)n1 * 128u, b);
+    } else {
+      const int p0 = (i - nkp) * kAttnChunk;
+      int n = pos - p0;
+      n = n < 0 ? 0 : (n > kAttnChunk ? kAttnChunk : n);
+      umma::bar_expect_tx(b, (uint32_t)n * kHeadDim * 4);
+      if (n > 0) bulk_load(dst, kvv.at(layer, 1, kv, p0), (uint32_t)n * kHeadDim * 4, b);
+    }
   };
   if (t == 0) {
-    for (int s = 0; s < kAttnRing; ++s) umma::bar_init(bars + s, 1);
+    umma::bar_init(full, 1);
+    umma::bar_init(full + 1, 1);
+    umma::bar_init(empty, 1);
+    umma::bar_init(empty + 1, 1);
+    umma::bar_init(&dfull, 1);
+    umma::bar_init(&dempty, 4);
+    umma::bar_init(&mdone, 1);
     umma::bar_init_fence();
-    for (int i = 0; i < total && i < kAttnRing; ++i) issue(i);
+    for (int i = 0; i < total && i < 2; ++i) issue(i);
   }
+  if (warp == 1) umma::tmem_alloc(&tmem_slot, kTcCols);
+  // the exp LUT into probtab[0] now, off the critical path: the softmax of
+  // every CTA would otherwise fetch the same few L2 lines at about the same time
+  for (int e = t; e < kExpLut; e += blockDim.x) probtab[0][e] = (uint32_t)exp_lut[e];
   grid_dep_wait();
   grid_dep_launch();
   const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
@@ -519,76 +562,133 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     }
     const int4 o4 = make_int4(o[0], o[1], o[2], o[3]);
     *reinterpret_cast<int4*>(&hv[warp][4 * lane]) = o4;
-    if (warp == 2) reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = o4;
+    if (warp == 2) {
+      reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = o4;
+      kpl_put4(kvv, layer, kv, pos, 4 * lane, o4);
+    }
   } else if (warp == 3) {
     const int4 v4 = *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim + 4 * lane);
     *reinterpret_cast<int4*>(&hv[3][4 * lane]) = v4;
     reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
   }
   __syncthreads();
+  // query bytes, 128-byte-swizzled K-major: thread (row r = t / 16, dims
+  // 8 (t % 16) .. +7); rows 3 h + b: byte b of q_h + 2^23, row 6: ones
+  {
+    const int r = t >> 4, d0 = 8 * (t & 15);
+    uint32_t w0 = 0, w1 = 0;
+    if (r < 6) {
+      const int h = r >= 3, b = r - 3 * h;
+      const int4 lo = *reinterpret_cast<const int4*>(&hv[h][d0]);
+      const int4 hi = *reinterpret_cast<const int4*>(&hv[h][d0 + 4]);
+      const int4 bl = make_int4(lo.x + (1 << 23), lo.y + (1 << 23), lo.z + (1 << 23), lo.w + (1 << 23));
+      const int4 bh = make_int4(hi.x + (1 << 23), hi.y + (1 << 23), hi.z + (1 << 23), hi.w + (1 << 23));
+      w0 = byte_plane_word(bl, b);
+      w1 = byte_plane_word(bh, b);
+    } else if (r == 6) {
+      w0 = w1 = 0x01010101u;
+    }
+    *reinterpret_cast<uint2*>(qb + kpl_off(r, d0)) = make_uint2(w0, w1);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the tensor cores
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
   attn_stamp(c, layer, m, kv, 1);
   bool ok = true;
-  // scores: chunk of 32 positions, 4 per warp, 8 lanes per position; lane
-  // `sub` holds dims 4 (sub + 8 j) .. +3, j = 0..3
   int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
-  {
-    const int sub = lane & 7, quad = lane >> 3;
-    const bool hi = (sub & 4) != 0;
-    int32_t q0[16], q1[16];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int4 a = *reinterpret_cast<const int4*>(&hv[0][4 * (sub + 8 * j)]);
-      const int4 b = *reinterpret_cast<const int4*>(&hv[1][4 * (sub + 8 * j)]);
-      q0[4 * j] = a.x; q0[4 * j + 1] = a.y; q0[4 * j + 2] = a.z; q0[4 * j + 3] = a.w;
-      q1[4 * j] = b.x; q1[4 * j + 1] = b.y; q1[4 * j + 2] = b.z; q1[4 * j + 3] = b.w;
+  // the current position's scores (warp 5)
+  if (warp == 5) {
+    const int4 k4 = *reinterpret_cast<const int4*>(&hv[2][4 * lane]);
+    const int4 qa = *reinterpret_cast<const int4*>(&hv[0][4 * lane]);
+    const int4 qc = *reinterpret_cast<const int4*>(&hv[1][4 * lane]);
+    int64_t s0 = 0, s1 = 0;
+    s0 = mad_wide(qa.x, k4.x, s0);
+    s0 = mad_wide(qa.y, k4.y, s0);
+    s0 = mad_wide(qa.z, k4.z, s0);
+    s0 = mad_wide(qa.w, k4.w, s0);
+    s1 = mad_wide(qc.x, k4.x, s1);
+    s1 = mad_wide(qc.y, k4.y, s1);
+    s1 = mad_wide(qc.z, k4.z, s1);
+    s1 = mad_wide(qc.w, k4.w, s1);
+    s0 = warp_sum_i64(s0);
+    s1 = warp_sum_i64(s1);
+    if (lane == 0) {
+      mx0 = scale_score(s0, kScoreScale);
+      mx1 = scale_score(s1, kScoreScale);
+      sc[pos] = mx0;
+      sc[ctx + pos] = mx1;
     }
-    for (int i = 0; i < nk; ++i) {
-      if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
-      const int p = i * kAttnChunk + warp * 4 + quad;
-      const int32_t* krow = p == pos ? hv[2] : ring + ((i % kAttnRing) * kAttnChunk + warp * 4 + quad) * kHeadDim;
-      // two independent chains per head (even / odd dimensions) halve the
-      // multiply-add dependency chains
-      int64_t s0 = 0, s1 = 0, t0 = 0, t1 = 0;
-      if (p < ctx) {
+  }
+  if (t == 128) {
+    // MMA issuer (warp 4): key plane i into D_(i % 3); chunk ch waits until
+    // the previous chunk's D is read
+    const uint64_t qdesc = umma::sw128_desc(umma::smem_addr(qb));
+    for (int i = 0; i < nkp && ok; ++i) {
+      const int ch = i / 3, a = i - 3 * ch;
+      if (a == 0 && ch > 0 && !umma::bar_wait(&dempty, (ch - 1) & 1)) ok = false;
+      if (ok && !umma::bar_wait(full + (i & 1), (i >> 1) & 1)) ok = false;
+      if (!ok) break;
+      umma::fence_after_sync();
+      const uint64_t kdesc = umma::sw128_desc(umma::smem_addr(slots + (i & 1) * kTcSlot));
+      const uint32_t idesc = umma::i8_idesc_ab(kTcKeys, 16, a == 2, false);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int4 k4 = *reinterpret_cast<const int4*>(krow + 4 * (sub + 8 * j));
-          s0 = mad_wide(q0[4 * j], k4.x, s0);
-          s1 = mad_wide(q1[4 * j], k4.x, s1);
-          t0 = mad_wide(q0[4 * j + 1], k4.y, t0);
-          t1 = mad_wide(q1[4 * j + 1], k4.y, t1);
-          s0 = mad_wide(q0[4 * j + 2], k4.z, s0);
-          s1 = mad_wide(q1[4 * j + 2], k4.z, s1);
-          t0 = mad_wide(q0[4 * j + 3], k4.w, t0);
-          t1 = mad_wide(q1[4 * j + 3], k4.w, t1);
+      for (int kk = 0; kk < 4; ++kk)
+        umma::mma_i8(tmem + 16u * a, kdesc + (uint64_t)(2 * kk), qdesc + (uint64_t)(2 * kk), idesc, kk > 0);
+      umma::mma_commit(empty + (i & 1));
+      if (a == 2) umma::mma_commit(&dfull);
+      if (i + 2 < total) {
+        // the slot's MMAs have read it: reload
+        if (!umma::bar_wait(empty + (i & 1), (i >> 1) & 1)) {
+          ok = false;
+          break;
         }
-        s0 += t0;
-        s1 += t1;
+        issue(i + 2);
       }
-      // the 8 lanes' partial sums: one exchange splits the heads (lanes
-      // sub < 4 keep head 0, sub >= 4 head 1), two more finish each sum, so
-      // every lane scales one score
-      int64_t sh = hi ? s1 : s0;
-      sh += shfl_xor_i64(hi ? s0 : s1, 4);
-      sh += shfl_xor_i64(sh, 2);
-      sh += shfl_xor_i64(sh, 1);
-      if (p < ctx) {
-        const int64_t v = scale_score(sh, kScoreScale);
-        if ((sub & 3) == 0) sc[hi ? ctx + p : p] = v;
-        if (hi)
-          mx1 = v > mx1 ? v : mx1;
-        else
-          mx0 = v > mx0 ? v : mx0;
+    }
+    // no MMA of this CTA is in flight past this point
+    umma::mma_commit(&mdone);
+    if (!umma::bar_wait(&mdone, 0)) ok = false;
+  }
+  // scores of each chunk: warp w < 4 reads D of the three planes for TMEM
+  // lanes (keys) 32 w .. 32 w + 31, both heads
+  for (int ch = 0; ch < nch && warp < 4; ++ch) {
+    if (!umma::bar_wait(&dfull, ch & 1)) {
+      ok = false;
+      break;
+    }
+    umma::fence_after_sync();
+    int32_t d[3][8];
+    const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16);
+#pragma unroll
+    for (int a = 0; a < 3; ++a) umma::tmem_ld<8>(lb + 16u * a, d[a]);
+    umma::tmem_ld_wait();
+    umma::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) umma::bar_arrive(&dempty);
+    const int key = ch * kTcKeys + 32 * warp + lane;
+    if (key < pos) {
+      int64_t s0 = 0, s1 = 0;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const int64_t bias = (int64_t)d[a][6] << 23;
+        const int64_t t0 = (int64_t)d[a][0] + ((int64_t)d[a][1] << 8) + ((int64_t)d[a][2] << 16) - bias;
+        const int64_t t1 = (int64_t)d[a][3] + ((int64_t)d[a][4] << 8) + ((int64_t)d[a][5] << 16) - bias;
+        s0 += t0 << (8 * a);
+        s1 += t1 << (8 * a);
       }
-      __syncthreads();  // slot i % kAttnRing is free again
-      if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+      const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
+      sc[key] = v0;
+      sc[ctx + key] = v1;
+      mx0 = v0 > mx0 ? v0 : mx0;
+      mx1 = v1 > mx1 ? v1 : mx1;
     }
   }
   attn_stamp(c, layer, m, kv, 2);
-  // maxima of both heads (one block reduction; head 0's sit in lanes with
-  // sub < 4, head 1's in the others)
+  // maxima of both heads (one block reduction)
 #pragma unroll
-  for (int msk = 4; msk < 32; msk <<= 1) {
+  for (int msk = 1; msk < 32; msk <<= 1) {
     const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
     mx0 = o0 > mx0 ? o0 : mx0;
     mx1 = o1 > mx1 ? o1 : mx1;
@@ -611,8 +711,8 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     const int i0 = lut_index(mx0, sc[p]), i1 = lut_index(mx1, sc[ctx + p]);
     sc[p] = i0;
     sc[ctx + p] = i1;
-    sum0 += exp_lut[i0];
-    sum1 += exp_lut[i1];
+    sum0 += probtab[0][i0];
+    sum1 += probtab[0][i1];
   }
   sum0 = warp_sum_i64(sum0);
   sum1 = warp_sum_i64(sum1);
@@ -630,10 +730,29 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     sum1 += red[1][w];
   }
   {
-    // warps 0-3 build head 0's table, warps 4-7 head 1's: one reciprocal each
-    const int h = t >> 7;
-    const uint64_t d = (uint64_t)(h ? sum1 : sum0), rc = ~0ULL / d;
-    for (int e = t & 127; e < kExpLut; e += 128) probtab[h][e] = barrett_div((uint64_t)exp_lut[e] << 16, d, rc);
+    // warps 4-7 build head 1's table from the LUT in probtab[0]; warps 0-3
+    // compute head 0's in registers and overwrite the LUT once every read of
+    // it is done: one reciprocal per thread
+    const int h = t >> 7, e0 = t & 127;
+    const uint64_t dd = (uint64_t)(h ? sum1 : sum0), rc = ~0ULL / dd;
+    uint32_t p0[3] = {0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int e = e0 + 128 * k;
+      if (e < kExpLut) {
+        const uint32_t v = barrett_div((uint64_t)probtab[0][e] << 16, dd, rc);
+        if (h)
+          probtab[1][e] = v;
+        else
+          p0[k] = v;
+      }
+    }
+    __syncthreads();
+    if (h == 0) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+        if (e0 + 128 * k < kExpLut) probtab[0][e0 + 128 * k] = p0[k];
+    }
   }
   __syncthreads();
   // per-position probabilities of both heads, packed over the index array
@@ -647,15 +766,16 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   // values: thread (warp, lane) accumulates dims 4 lane .. +3 of the chunk's
   // positions warp, warp + 8, warp + 16, warp + 24 for both heads
   int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-  for (int i = nk; i < total; ++i) {
-    if (!umma::bar_wait(bars + i % kAttnRing, (i / kAttnRing) & 1)) ok = false;
-    const int base = (i - nk) * kAttnChunk;
+  for (int j = 0; j < nk; ++j) {
+    const int i = nkp + j;
+    if (!umma::bar_wait(full + (i & 1), (i >> 1) & 1)) ok = false;
+    const int base = j * kAttnChunk;
+    const int32_t* ring = reinterpret_cast<const int32_t*>(slots + (i & 1) * kTcSlot);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int p = base + warp + 8 * u;
       if (p < ctx) {
-        const int32_t* vrow =
-            p == pos ? hv[3] : ring + ((i % kAttnRing) * kAttnChunk + warp + 8 * u) * kHeadDim;
+        const int32_t* vrow = p == pos ? hv[3] : ring + (warp + 8 * u) * kHeadDim;
         const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
         const int2 pr = prs[p];
         const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
@@ -667,12 +787,12 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
       }
     }
     __syncthreads();
-    if (t == 0 && i + kAttnRing < total) issue(i + kAttnRing);
+    if (t == 0 && i + 2 < total) issue(i + 2);
   }
   attn_stamp(c, layer, m, kv, 4);
   if (!ok) atomicExch(c.err, 4);
   // the ring is idle now: reuse it for the cross-warp sums [8][2][128]
-  int64_t* part = reinterpret_cast<int64_t*>(attn_smem);
+  int64_t* part = reinterpret_cast<int64_t*>(slots);
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
     part[(warp * 2 + 0) * kHeadDim + 4 * lane + e] = a0[e];
@@ -685,6 +805,10 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
 #pragma unroll
     for (int w = 0; w < 8; ++w) acc += part[(w * 2 + h) * kHeadDim + d];
     write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
+  }
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, kTcCols);
   }
   attn_stamp(c, layer, m, kv, 5);
 }
@@ -1713,7 +1837,10 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
     } else if (warp == 2) {
       const int4 k4 = head_norm_rope(raw + kQRows + kv * kHeadDim, g_k, cos_tab, sin_tab, pos, lane);
       reinterpret_cast<int4*>(hv[2])[lane] = k4;
-      if (owner) reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = k4;
+      if (owner) {
+        reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = k4;
+        kpl_put4(kvv, layer, kv, pos, 4 * lane, k4);
+      }
     } else if (warp == 3) {
       const int4 v4 = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
       reinterpret_cast<int4*>(hv[3])[lane] = v4;
@@ -1961,6 +2088,7 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
   } else if (warp == 2) {
     const int4 o = head_norm_rope(raw + kQRows + kv * kHeadDim, g_k, cos_tab, sin_tab, pos, lane);
     reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = o;
+    kpl_put4(kvv, layer, kv, pos, 4 * lane, o);
   } else {
     const int4 v = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
     reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v;
@@ -2437,6 +2565,11 @@ int decode_splits(int kind, int SP) {
 constexpr int kPfSplitQkv = 1, kPfSplitO = 2, kPfSplitGu = 1, kPfSplitDown = 4;
 
 bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 && p.max_ctx <= 1024; }
+// dynamic shared memory of batch_attn_kernel: alignment slack, ring, query
+// bytes, scores [2][max_ctx]; with its 4.3 KB static and 1 KB reserved, four
+// CTAs fit an SM up to max_ctx = 1024 (the occupancy calculator reports one
+// for a kernel that allocates TMEM; 64 columns per CTA leave room for four)
+size_t attn_tc_smem(const BatchPlan& p) { return (size_t)kTcSmemFixed + (size_t)2 * p.max_ctx * 8; }
 // cluster size of the cluster attention (16 CTAs for batches of up to 4 sequences), the keys per
 // rank its score buffer must hold, and whether it covers max_ctx
 int attn_cl_ranks(const BatchPlan& p) { return p.S <= 4 ? 16 : 8; }
@@ -2474,7 +2607,7 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
   // enough (KV head, sequence) pairs to fill the GPU in one wave: one CTA per
   // pair; otherwise split each pair's context over pages
   const bool one_cta_per_head = attn_one_cta_per_head(p);
-  const size_t ring_smem = (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8;
+  const size_t ring_smem = attn_tc_smem(p);
   BMARK(-1);
   BQ(launch_pdl(batch_embed_kernel, dim3(p.S), dim3(256), 0, s, c, p.emb, p.semb));
   BMARK(kBkEmbed);
@@ -2569,8 +2702,7 @@ int setup_t(const BatchPlan& p) {
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   }
   if (attn_one_cta_per_head(p))
-    BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            (int)((size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * p.max_ctx * 8)));
+    BQ(cudaFuncSetAttribute(batch_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_tc_smem(p)));
   return Q4GPU_OK;
 }
 

@@ -132,8 +132,10 @@ __global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, i
       const int32_t r = sat24(((int64_t)z * cos_tab[pos * kHeadDim + d] + rot * sin_tab[pos * kHeadDim + d]) >> 15);
       if (head < kQHeads)
         st.qrope[head * kHeadDim + d] = r;
-      else
+      else {
         st.kv.at(layer, 0, head - kQHeads, pos)[d] = r;
+        kpl_put1(st.kv, layer, head - kQHeads, pos, d, r);
+      }
     } else {
       st.kv.at(layer, 1, head - kQHeads - kKvHeads, pos)[d] = y[t];
     }
@@ -399,10 +401,12 @@ __global__ void kv_copy_kernel(KvView kv, int layer, int kind, int positions, in
   if (p >= positions) return;
   int32_t* slot = kv.at(layer, kind, h, p) + d;
   int32_t* f = flat + ((size_t)p * kKvHeads + h) * kHeadDim + d;
-  if (to_pool)
+  if (to_pool) {
     *slot = *f;
-  else
+    if (kind == 0) kpl_put1(kv, layer, h, p, d, *f);
+  } else {
     *f = *slot;
+  }
 }
 
 }  // namespace q4
@@ -487,6 +491,8 @@ struct q4gpu_model {
   // KV pool
   int32_t* kv_pool = nullptr;
   int64_t page_elems = 0;
+  uint8_t* kv_planes = nullptr;  // the keys as byte planes (KvView::kpl)
+  int64_t kpl_page_bytes = 0;
   int pages_per_seq = 0;
   int32_t* page_tables = nullptr;
   // slots
@@ -1261,6 +1267,8 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   m->pages_per_seq = (cfg->max_context + kKvPage - 1) / kKvPage;
   const int64_t n_pages = (int64_t)m->pages_per_seq * cfg->max_seqs;
   if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
+  m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
+  if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
   if ((rc = m->alloc(&m->page_tables, (size_t)n_pages))) return fail(rc);
   {
     std::vector<int32_t> pt(n_pages);
@@ -1297,7 +1305,8 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
     st.mlp = mlp + (size_t)i * kInter;
     st.lm_partial = part + (size_t)i * Q4GPU_LM_HEAD_BLOCKS;
     st.lm_counter = ctr + (size_t)i * 32;
-    st.kv = KvView{m->kv_pool, m->page_tables + (size_t)i * m->pages_per_seq, m->page_elems};
+    st.kv = KvView{m->kv_pool, m->page_tables + (size_t)i * m->pages_per_seq, m->page_elems, m->kv_planes,
+                   m->kpl_page_bytes};
     st.max_ctx = cfg->max_context;
     m->slots.push_back(st);
   }

@@ -598,7 +598,10 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
     a.st.kv.at(layer, 1, h, pos)[t - 3 * kHeadDim] = vc[t - 3 * kHeadDim];
   }
   __syncthreads();
-  if (sl == 0 && t < kHeadDim) a.st.kv.at(layer, 0, h, pos)[t] = kc[t];
+  if (sl == 0 && t < kHeadDim) {
+    a.st.kv.at(layer, 0, h, pos)[t] = kc[t];
+    kpl_put1(a.st.kv, layer, h, pos, t, kc[t]);
+  }
   // the cached K rows and V slice were copied into shared memory during QKV
   if (!mbar_wait(sm.mbar, mbar_phase, a.err)) return false;
   mbar_phase ^= 1u;

@@ -10,15 +10,58 @@ namespace q4 {
 // ---------------------------------------------------------------------------
 // Device-side views
 // ---------------------------------------------------------------------------
+// One byte plane of a KV page's keys for one (layer, head): 64 rows of 128
+// bytes; the three planes of a (layer, head) follow each other.
+constexpr int kKplPlane = kKvPage * kHeadDim;  // 8192
+constexpr int kKplHead = 3 * kKplPlane;        // 24576
+
 struct KvView {
   int32_t* pool;         // [n_pages][layers][2][8][64][128] int32
   const int32_t* pages;  // this slot's page table: logical page -> physical page
   int64_t page_elems;    // layers * 2 * 8 * 64 * 128
+  // The keys once more as byte planes, read by the tensor-core scores of the
+  // batched attention: per physical page [layers][8 heads][3 planes][64][128]
+  // bytes.  Plane a holds byte a of each 24-bit key element k = b0 + 2^8 b1 +
+  // 2^16 b2 (b0, b1 unsigned, b2 the signed top byte); each 128-byte row (one
+  // position) is swizzled like a 128-byte-swizzled K-major UMMA tile (16-byte
+  // unit u of row r stored at unit u ^ (r % 8)), so a bulk copy of a plane's
+  // rows is an operand as it lands.
+  uint8_t* kpl;
+  int64_t kpl_page_bytes;  // layers * 8 * kKplHead
   __device__ __forceinline__ int32_t* at(int layer, int kind, int head, int pos) const {
     return pool + (int64_t)pages[pos >> 6] * page_elems +
            ((((int64_t)layer * 2 + kind) * kKvHeads + head) * kKvPage + (pos & (kKvPage - 1))) * kHeadDim;
   }
+  // plane 0 of the (layer, head) block of the page holding pos (row 0 of the page)
+  __device__ __forceinline__ uint8_t* kplane(int layer, int head, int pos) const {
+    return kpl + (int64_t)pages[pos >> 6] * kpl_page_bytes + ((int64_t)layer * kKvHeads + head) * kKplHead;
+  }
 };
+
+// Byte offset of dims d .. d + 3 (d % 4 == 0) of row r in a swizzled plane.
+__device__ __forceinline__ uint32_t kpl_off(int r, int d) {
+  return (uint32_t)r * 128u + ((uint32_t)((d >> 4) ^ (r & 7)) << 4) + (uint32_t)(d & 15);
+}
+// Byte l of each of four 32-bit values, packed.
+__device__ __forceinline__ uint32_t byte_plane_word(int4 v, int l) {
+  const uint32_t sel = (uint32_t)l | ((uint32_t)(l + 4) << 4);
+  const uint32_t lo = __byte_perm((uint32_t)v.x, (uint32_t)v.y, sel);
+  const uint32_t hi = __byte_perm((uint32_t)v.z, (uint32_t)v.w, sel);
+  return __byte_perm(lo, hi, 0x5410);
+}
+// Key elements d .. d + 3 (d % 4 == 0) of position pos into the byte planes.
+__device__ __forceinline__ void kpl_put4(const KvView& kv, int layer, int head, int pos, int d, int4 v) {
+  uint8_t* b = kv.kplane(layer, head, pos) + kpl_off(pos & (kKvPage - 1), d);
+#pragma unroll
+  for (int a = 0; a < 3; ++a) *reinterpret_cast<uint32_t*>(b + a * kKplPlane) = byte_plane_word(v, a);
+}
+// One key element.
+__device__ __forceinline__ void kpl_put1(const KvView& kv, int layer, int head, int pos, int d, int32_t x) {
+  uint8_t* b = kv.kplane(layer, head, pos) + kpl_off(pos & (kKvPage - 1), d & ~3) + (d & 3);
+  b[0] = (uint8_t)x;
+  b[kKplPlane] = (uint8_t)(x >> 8);
+  b[2 * kKplPlane] = (uint8_t)(x >> 16);
+}
 
 struct ArgBestD {
   int64_t score;
