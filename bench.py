@@ -74,9 +74,12 @@ HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 # algorithmic bytes of one launch of each batched kernel (S sequences, the
 # attention at context `ctx`): what the kernel must move at least
 # ---------------------------------------------------------------------------
-def batch_kernel_bytes(kind: str, S: int, ctx: int) -> int:
+def batch_kernel_bytes(kind: str, S: int, ctx: int, key_planes: bool = False) -> int:
     """Algorithmic bytes of one launch: weights counted as Q4 (packed nibbles +
-    u16 scales), K/V at the reference's 4 B per element."""
+    u16 scales), K/V at the reference's 4 B per element; with
+    key_planes (the one-CTA-per-head attention of config 4) the cached keys are
+    read as their three byte planes (3 B per element) and the new key is
+    written both ways."""
     limbs = 3 * S  # limb rows of a B matrix (u8)
 
     def q4(rows: int, k: int) -> int:
@@ -89,8 +92,10 @@ def batch_kernel_bytes(kind: str, S: int, ctx: int) -> int:
     if kind == "qkv_gemm":
         return q4(QKV_ROWS, HIDDEN) + limbs * HIDDEN + S * QKV_ROWS * 4
     if kind == "attention":
-        kv_read = 8 * 2 * (ctx - 1) * 128 * 4
-        return S * (kv_read + 8 * 2 * 128 * 4 + QKV_ROWS * 4 + 3 * 2 * HIDDEN)
+        key_b = 3 if key_planes else 4
+        kv_read = 8 * (ctx - 1) * 128 * (key_b + 4)
+        new_rows = 8 * 128 * (2 * 4 + (3 if key_planes else 0))
+        return S * (kv_read + new_rows + QKV_ROWS * 4 + 3 * 2 * HIDDEN)
     if kind == "o_proj_gemm":
         return q4(HIDDEN, 2 * HIDDEN) + limbs * 2 * HIDDEN + S * 3 * HIDDEN * 4
     if kind == "gate_up_gemm":
@@ -652,7 +657,7 @@ def run_ours(args, ws, rank, local):
     peaks = measured_peaks()
 
     def gbs(kind: str) -> float:
-        return batch_kernel_bytes(kind, BATCH, int(round(kt_ctx))) / (kt[kind][0] * 1e-3) / 1e9
+        return batch_kernel_bytes(kind, BATCH, int(round(kt_ctx)), kind == "attention") / (kt[kind][0] * 1e-3) / 1e9
 
     launches_per_step = sum(v[1] for v in kt.values())
 
@@ -672,7 +677,7 @@ def run_ours(args, ws, rank, local):
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(gbs(dom), 1), "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": round(gbs(dom) / peaks["hbm_gbs"], 4),
                          "peak_source": peaks["source"], "traffic": profiled_traffic(dom),
-                         "bytes_per_launch": batch_kernel_bytes(dom, BATCH, int(round(kt_ctx))),
+                         "bytes_per_launch": batch_kernel_bytes(dom, BATCH, int(round(kt_ctx)), dom == "attention"),
                          "ms_per_launch": round(kt[dom][0], 5), "context": round(kt_ctx, 1)},
             "kernels": {k: {"ms_per_launch": round(v[0], 5), "launches_per_step": v[1],
                             "share": round(share[k] / tot, 4), "gbs": round(gbs(k), 1)} for k, v in kt.items()},
