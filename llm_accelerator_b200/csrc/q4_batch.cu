@@ -268,8 +268,9 @@ __global__ void __launch_bounds__(256) batch_attn_scores_kernel(BatchCtx c, Attn
       asm volatile("fence.proxy.async.global;" ::: "memory");  // later bulk copies read this row
     }
   } else if (warp == 3 && has_new) {
-    reinterpret_cast<int4*>(kvv.at(layer, 1, h, pos))[lane] =
-        *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + h * kHeadDim + 4 * lane);
+    const int4 v4 = *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + h * kHeadDim + 4 * lane);
+    reinterpret_cast<int4*>(kvv.at(layer, 1, h, pos))[lane] = v4;
+    vpl_put4(kvv, layer, h, pos, 4 * lane, v4);
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
   __syncthreads();
@@ -452,11 +453,18 @@ __global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, Attn
 // rows of query bytes (c_b of both heads, a row of ones, zero rows), D in
 // TMEM, read back by warps 0-3 (lane = key) and combined in int64.  The
 // current position's key comes from this kernel's own q/k/v row and is
-// scored on the CUDA cores.  Values stay on the CUDA cores (int64 products of
-// the int32 V rows).  One ring of two 16 KB slots carries first the chunks'
-// key planes (loads i = 0 .. 3 nch - 1, plane i % 3 of chunk i / 3, released
-// by the MMA's commit), then the V rows in 32-position chunks (released by a
-// block barrier); the first loads start before the dependency wait.
+// scored on the CUDA cores.  Values the same way round: with the
+// probability p <= 2^16 split into bytes p_b and the values into the
+// transposed byte planes v_a (dims x positions; KvView::vpl),
+//   sum_p p v[d] = sum_a 2^(8 a) sum_b 2^(8 b) E_a[d][b],
+//   E_a[d][b] = sum_p v_a[d][p] p_b[p]  (|E_a| < 2^26 for 1024 positions),
+// one M128 (dims) x N16 x K128 (positions) product per plane and chunk, A
+// = two 64-byte-swizzled page planes, B = 16 rows of probability bytes, E
+// accumulated in TMEM over the chunks; the current position's value is
+// added on the CUDA cores.  One ring of two 16 KB slots carries the chunks'
+// key planes (loads i = 0 .. 3 nch - 1, plane i % 3 of chunk i / 3), then
+// their value planes, each slot released by the MMA's commit; the first
+// loads start before the dependency wait.
 constexpr int kAttnChunk = 32;
 constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
 constexpr int kAttnRing = 2;
@@ -464,7 +472,15 @@ constexpr int kStageAttnRing = 4;
 constexpr int kTcKeys = 128;                  // keys per score chunk (the MMA's M)
 constexpr int kTcSlot = 16384;                // ring slot: one key plane of a chunk, or 32 V rows
 constexpr int kTcSmemFixed = 1024 + 2 * kTcSlot + 16 * 128;  // alignment slack, ring, query bytes
-constexpr uint32_t kTcCols = 64;              // TMEM columns: D of three planes x 16
+constexpr uint32_t kTcCols = 128;             // TMEM columns: D (scores) at 0, E (values) at 64, 3 planes x 16
+constexpr uint32_t kTcVal = 64;
+
+// Shared-memory descriptor of a K-major tile with 64-byte rows, 64-byte
+// swizzled (8-row atoms of 512 bytes).
+__device__ __forceinline__ uint64_t sw64_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(512 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)4 << 61);
+}
 
 __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
                                                             const int32_t* __restrict__ g_k,
@@ -477,12 +493,14 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   uint8_t* sbase = attn_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* slots = sbase;                                   // [2][16 KB]
   uint8_t* qb = sbase + 2 * kTcSlot;                        // [16][128] query bytes
-  int64_t* sc = reinterpret_cast<int64_t*>(qb + 16 * 128);  // [2][ctx]
+  int64_t* sc = reinterpret_cast<int64_t*>(qb + 16 * 128);  // [2][ctx]; later the probability bytes
+  uint8_t* pb = reinterpret_cast<uint8_t*>(sc);              // [nch][16][128] probability bytes
   __shared__ __align__(16) int32_t hv[4][kHeadDim];  // roped q0, q1, k; raw v
   __shared__ uint32_t probtab[2][kExpLut];
   __shared__ int64_t red[2][8];
-  __shared__ uint64_t full[2], empty[2], dfull, dempty, mdone;
+  __shared__ uint64_t full[2], empty[2], dfull, dempty, vdone;
   __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t ppos[2];  // the current position's probability per head
   const int kv = blockIdx.x, m = blockIdx.y;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   attn_stamp(c, layer, m, kv, 0);
@@ -494,10 +512,9 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
   const KvView kvv = c.slots[m].kv;
-  const int nch = (pos + kTcKeys - 1) / kTcKeys;       // score chunks of the cached keys [0, pos)
-  const int nkp = 3 * nch;                             // key-plane loads
-  const int nk = (ctx + kAttnChunk - 1) / kAttnChunk;  // V chunks of 32 positions
-  const int total = nkp + nk;
+  const int nch = (pos + kTcKeys - 1) / kTcKeys;  // chunks of the cached positions [0, pos)
+  const int nkp = 3 * nch;                        // key-plane loads, then as many value-plane loads
+  const int total = 2 * nkp;
   auto issue = [&](int i) {
     uint64_t* b = full + (i & 1);
     uint8_t* dst = slots + (i & 1) * kTcSlot;
@@ -511,11 +528,12 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
       if (n1 > 0)
         bulk_load(dst + kKplPlane, kvv.kplane(layer, kv, k0 + kKvPage) + a * kKplPlane, (uint32_t)n1 * 128u, b);
     } else {
-      const int p0 = (i - nkp) * kAttnChunk;
-      int n = pos - p0;
-      n = n < 0 ? 0 : (n > kAttnChunk ? kAttnChunk : n);
-      umma::bar_expect_tx(b, (uint32_t)n * kHeadDim * 4);
-      if (n > 0) bulk_load(dst, kvv.at(layer, 1, kv, p0), (uint32_t)n * kHeadDim * 4, b);
+      // whole page planes (positions past pos get probability 0)
+      const int j = i - nkp, ch = j / 3, a = j - 3 * ch, k0 = ch * kTcKeys;
+      const bool two = k0 + kKvPage < pos;
+      umma::bar_expect_tx(b, (two ? 2u : 1u) * kKplPlane);
+      bulk_load(dst, kvv.vplane(layer, kv, k0) + a * kKplPlane, kKplPlane, b);
+      if (two) bulk_load(dst + kKplPlane, kvv.vplane(layer, kv, k0 + kKvPage) + a * kKplPlane, kKplPlane, b);
     }
   };
   if (t == 0) {
@@ -525,7 +543,7 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     umma::bar_init(empty + 1, 1);
     umma::bar_init(&dfull, 1);
     umma::bar_init(&dempty, 4);
-    umma::bar_init(&mdone, 1);
+    umma::bar_init(&vdone, 1);
     umma::bar_init_fence();
     for (int i = 0; i < total && i < 2; ++i) issue(i);
   }
@@ -570,6 +588,7 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     const int4 v4 = *reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim + 4 * lane);
     *reinterpret_cast<int4*>(&hv[3][4 * lane]) = v4;
     reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
+    vpl_put4(kvv, layer, kv, pos, 4 * lane, v4);
   }
   __syncthreads();
   // query bytes, 128-byte-swizzled K-major: thread (row r = t / 16, dims
@@ -647,14 +666,12 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
         issue(i + 2);
       }
     }
-    // no MMA of this CTA is in flight past this point
-    umma::mma_commit(&mdone);
-    if (!umma::bar_wait(&mdone, 0)) ok = false;
   }
   // scores of each chunk: warp w < 4 reads D of the three planes for TMEM
   // lanes (keys) 32 w .. 32 w + 31, both heads
   for (int ch = 0; ch < nch && warp < 4; ++ch) {
-    if (!umma::bar_wait(&dfull, ch & 1)) {
+    // the warp agrees on the outcome: the TMEM loads below are warp-wide
+    if (!__all_sync(0xFFFFFFFFu, umma::bar_wait(&dfull, ch & 1))) {
       ok = false;
       break;
     }
@@ -755,57 +772,104 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
     }
   }
   __syncthreads();
-  // per-position probabilities of both heads, packed over the index array
-  int2* prs = reinterpret_cast<int2*>(sc);
-  for (int p = t; p < ctx; p += blockDim.x) {
-    const int i0 = (int)sc[p], i1 = (int)sc[ctx + p];
-    prs[p] = make_int2((int)probtab[0][i0], (int)probtab[1][i1]);
-  }
-  __syncthreads();
-  attn_stamp(c, layer, m, kv, 3);
-  // values: thread (warp, lane) accumulates dims 4 lane .. +3 of the chunk's
-  // positions warp, warp + 8, warp + 16, warp + 24 for both heads
-  int64_t a0[4] = {0, 0, 0, 0}, a1[4] = {0, 0, 0, 0};
-  for (int j = 0; j < nk; ++j) {
-    const int i = nkp + j;
-    if (!umma::bar_wait(full + (i & 1), (i >> 1) & 1)) ok = false;
-    const int base = j * kAttnChunk;
-    const int32_t* ring = reinterpret_cast<const int32_t*>(slots + (i & 1) * kTcSlot);
+  // probabilities of this thread's positions t + 256 j (ctx <= 1024) into
+  // registers, then the index array becomes the probability bytes: chunk c,
+  // row 3 h + b = byte b of head h's probability, 128-byte swizzled, zero for
+  // the current position (added below) and past it
+  uint32_t pr[4][2];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int p = base + warp + 8 * u;
-      if (p < ctx) {
-        const int32_t* vrow = p == pos ? hv[3] : ring + (warp + 8 * u) * kHeadDim;
-        const int4 v4 = *reinterpret_cast<const int4*>(vrow + 4 * lane);
-        const int2 pr = prs[p];
-        const int32_t vv[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          a0[e] = mad_wide(pr.x, vv[e], a0[e]);
-          a1[e] = mad_wide(pr.y, vv[e], a1[e]);
-        }
+  for (int j = 0; j < 4; ++j) {
+    const int p = t + 256 * j;
+    pr[j][0] = pr[j][1] = 0;
+    if (p < ctx) {
+      pr[j][0] = probtab[0][(int)sc[p]];
+      pr[j][1] = probtab[1][(int)sc[ctx + p]];
+      if (p == pos) {
+        ppos[0] = pr[j][0];
+        ppos[1] = pr[j][1];
       }
     }
-    __syncthreads();
-    if (t == 0 && i + 2 < total) issue(i + 2);
+  }
+  __syncthreads();
+  for (int i = t; i < nch * 128; i += blockDim.x) reinterpret_cast<uint4*>(pb)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int p = t + 256 * j;
+    if (p < pos) {
+      uint8_t* tile = pb + (p >> 7) * 2048;
+      const int k = p & 127;
+#pragma unroll
+      for (int r = 0; r < 6; ++r) {
+        const uint32_t v = pr[j][r >= 3] >> (8 * (r % 3));
+        if (v & 0xFFu) tile[r * 128 + (((k >> 4) ^ (r & 7)) << 4) + (k & 15)] = (uint8_t)v;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // read by the tensor cores
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  attn_stamp(c, layer, m, kv, 3);
+  if (t == 128) {
+    // value products: plane a of chunk ch into E_a, accumulated over the chunks
+    const uint64_t pdesc = umma::sw128_desc(umma::smem_addr(pb));
+    for (int j = 0; j < nkp && ok; ++j) {
+      const int i = nkp + j, ch = j / 3, a = j - 3 * ch;
+      if (!umma::bar_wait(full + (i & 1), (i >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      umma::fence_after_sync();
+      const uint32_t sa = umma::smem_addr(slots + (i & 1) * kTcSlot);
+      const uint32_t idesc = umma::i8_idesc_ab(kTcKeys, 16, a == 2, false);
+      const bool two = ch * kTcKeys + kKvPage < pos;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (kk >= 2 && !two) break;  // the second page holds no cached position
+        const uint64_t vdesc = sw64_desc(sa + (kk >> 1) * kKplPlane) + (uint64_t)(2 * (kk & 1));
+        const uint64_t bdesc = pdesc + (uint64_t)((ch * 2048 + 32 * kk) >> 4);
+        umma::mma_i8(tmem + kTcVal + 16u * a, vdesc, bdesc, idesc, (ch | kk) != 0);
+      }
+      umma::mma_commit(empty + (i & 1));
+      if (i + 2 < total) {
+        if (!umma::bar_wait(empty + (i & 1), (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        issue(i + 2);
+      }
+    }
+    umma::mma_commit(&vdone);  // every MMA of this CTA is done when it arrives
+  }
+  // outputs: warp w < 4 reads E for dims 32 w .. 32 w + 31 (TMEM lanes)
+  if (warp < 4) {
+    const int d = 32 * warp + lane;
+    int64_t o0 = 0, o1 = 0;
+    const bool got = __all_sync(0xFFFFFFFFu, umma::bar_wait(&vdone, 0));
+    if (!got) ok = false;
+    umma::fence_after_sync();
+    if (nch > 0 && got) {
+      int32_t e[3][8];
+      const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16) + kTcVal;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) umma::tmem_ld<8>(lb + 16u * a, e[a]);
+      umma::tmem_ld_wait();
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        o0 += ((int64_t)e[a][0] + ((int64_t)e[a][1] << 8) + ((int64_t)e[a][2] << 16)) << (8 * a);
+        o1 += ((int64_t)e[a][3] + ((int64_t)e[a][4] << 8) + ((int64_t)e[a][5] << 16)) << (8 * a);
+      }
+    }
+    o0 += (int64_t)ppos[0] * hv[3][d];
+    o1 += (int64_t)ppos[1] * hv[3][d];
+    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv) * kHeadDim + d, sat24(o0 >> 16));
+    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + 1) * kHeadDim + d, sat24(o1 >> 16));
   }
   attn_stamp(c, layer, m, kv, 4);
   if (!ok) atomicExch(c.err, 4);
-  // the ring is idle now: reuse it for the cross-warp sums [8][2][128]
-  int64_t* part = reinterpret_cast<int64_t*>(slots);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    part[(warp * 2 + 0) * kHeadDim + 4 * lane + e] = a0[e];
-    part[(warp * 2 + 1) * kHeadDim + 4 * lane + e] = a1[e];
-  }
+  umma::fence_before_sync();
   __syncthreads();
-  {
-    const int h = t >> 7, d = t & (kHeadDim - 1);
-    int64_t acc = 0;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) acc += part[(w * 2 + h) * kHeadDim + d];
-    write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
-  }
   if (warp == 1) {
     umma::fence_after_sync();
     umma::tmem_dealloc(tmem, kTcCols);
@@ -1844,7 +1908,10 @@ __device__ __forceinline__ void attn_cl_body(const BatchCtx& c, const SlotState&
     } else if (warp == 3) {
       const int4 v4 = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
       reinterpret_cast<int4*>(hv[3])[lane] = v4;
-      if (owner) reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
+      if (owner) {
+        reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
+        vpl_put4(kvv, layer, kv, pos, 4 * lane, v4);
+      }
     }
   }
   __syncthreads();
@@ -2092,6 +2159,7 @@ __global__ void __launch_bounds__(128) prefill_qk_kernel(const SlotState* __rest
   } else {
     const int4 v = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
     reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v;
+    vpl_put4(kvv, layer, kv, pos, 4 * lane, v);
   }
 }
 
@@ -2569,7 +2637,10 @@ bool attn_one_cta_per_head(const BatchPlan& p) { return p.S * kKvHeads >= 148 &&
 // bytes, scores [2][max_ctx]; with its 4.3 KB static and 1 KB reserved, four
 // CTAs fit an SM up to max_ctx = 1024 (the occupancy calculator reports one
 // for a kernel that allocates TMEM; 64 columns per CTA leave room for four)
-size_t attn_tc_smem(const BatchPlan& p) { return (size_t)kTcSmemFixed + (size_t)2 * p.max_ctx * 8; }
+size_t attn_tc_smem(const BatchPlan& p) {
+  const size_t scores = (size_t)2 * p.max_ctx * 8, pbytes = (size_t)(p.max_ctx + kTcKeys - 1) / kTcKeys * 2048;
+  return (size_t)kTcSmemFixed + (scores > pbytes ? scores : pbytes);
+}
 // cluster size of the cluster attention (16 CTAs for batches of up to 4 sequences), the keys per
 // rank its score buffer must hold, and whether it covers max_ctx
 int attn_cl_ranks(const BatchPlan& p) { return p.S <= 4 ? 16 : 8; }

@@ -138,6 +138,7 @@ __global__ void __launch_bounds__(256) qkv_step_kernel(SlotState st, LayerW w, i
       }
     } else {
       st.kv.at(layer, 1, head - kQHeads - kKvHeads, pos)[d] = y[t];
+      vpl_put1(st.kv, layer, head - kQHeads - kKvHeads, pos, d, y[t]);
     }
   }
   // no CTA leaves while another may still read its part_ss
@@ -403,7 +404,10 @@ __global__ void kv_copy_kernel(KvView kv, int layer, int kind, int positions, in
   int32_t* f = flat + ((size_t)p * kKvHeads + h) * kHeadDim + d;
   if (to_pool) {
     *slot = *f;
-    if (kind == 0) kpl_put1(kv, layer, h, p, d, *f);
+    if (kind == 0)
+      kpl_put1(kv, layer, h, p, d, *f);
+    else
+      vpl_put1(kv, layer, h, p, d, *f);
   } else {
     *f = *slot;
   }
@@ -492,6 +496,7 @@ struct q4gpu_model {
   int32_t* kv_pool = nullptr;
   int64_t page_elems = 0;
   uint8_t* kv_planes = nullptr;  // the keys as byte planes (KvView::kpl)
+  uint8_t* v_planes = nullptr;   // the values as transposed byte planes (KvView::vpl)
   int64_t kpl_page_bytes = 0;
   int pages_per_seq = 0;
   int32_t* page_tables = nullptr;
@@ -1269,6 +1274,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
   m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
   if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
+  if ((rc = m->alloc(&m->v_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
   if ((rc = m->alloc(&m->page_tables, (size_t)n_pages))) return fail(rc);
   {
     std::vector<int32_t> pt(n_pages);
@@ -1306,7 +1312,7 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
     st.lm_partial = part + (size_t)i * Q4GPU_LM_HEAD_BLOCKS;
     st.lm_counter = ctr + (size_t)i * 32;
     st.kv = KvView{m->kv_pool, m->page_tables + (size_t)i * m->pages_per_seq, m->page_elems, m->kv_planes,
-                   m->kpl_page_bytes};
+                   m->kpl_page_bytes, m->v_planes};
     st.max_ctx = cfg->max_context;
     m->slots.push_back(st);
   }

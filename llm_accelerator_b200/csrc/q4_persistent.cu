@@ -596,6 +596,7 @@ __device__ bool stage_attention(const PersistArgs& a, const LayerW& w, const PSm
   if (sl == 0 && t >= 3 * kHeadDim && t < 4 * kHeadDim) {
     // this position's V goes to the cache (K below, after RoPE is in smem)
     a.st.kv.at(layer, 1, h, pos)[t - 3 * kHeadDim] = vc[t - 3 * kHeadDim];
+    vpl_put1(a.st.kv, layer, h, pos, t - 3 * kHeadDim, vc[t - 3 * kHeadDim]);
   }
   __syncthreads();
   if (sl == 0 && t < kHeadDim) {

@@ -28,6 +28,12 @@ struct KvView {
   // rows is an operand as it lands.
   uint8_t* kpl;
   int64_t kpl_page_bytes;  // layers * 8 * kKplHead
+  // The values as byte planes the other way round, read by the tensor-core
+  // value products: per physical page [layers][8 heads][3 planes][128 dims]
+  // [64 positions] bytes (same sizes as kpl); each 64-byte row (one dim) is
+  // swizzled like a 64-byte-swizzled K-major UMMA tile (16-byte unit u of row
+  // d stored at unit u ^ ((d / 2) % 4)).
+  uint8_t* vpl;
   __device__ __forceinline__ int32_t* at(int layer, int kind, int head, int pos) const {
     return pool + (int64_t)pages[pos >> 6] * page_elems +
            ((((int64_t)layer * 2 + kind) * kKvHeads + head) * kKvPage + (pos & (kKvPage - 1))) * kHeadDim;
@@ -35,6 +41,10 @@ struct KvView {
   // plane 0 of the (layer, head) block of the page holding pos (row 0 of the page)
   __device__ __forceinline__ uint8_t* kplane(int layer, int head, int pos) const {
     return kpl + (int64_t)pages[pos >> 6] * kpl_page_bytes + ((int64_t)layer * kKvHeads + head) * kKplHead;
+  }
+  // plane 0 of the (layer, head) block of the V planes of the page holding pos
+  __device__ __forceinline__ uint8_t* vplane(int layer, int head, int pos) const {
+    return vpl + (int64_t)pages[pos >> 6] * kpl_page_bytes + ((int64_t)layer * kKvHeads + head) * kKplHead;
   }
 };
 
@@ -54,6 +64,24 @@ __device__ __forceinline__ void kpl_put4(const KvView& kv, int layer, int head, 
   uint8_t* b = kv.kplane(layer, head, pos) + kpl_off(pos & (kKvPage - 1), d);
 #pragma unroll
   for (int a = 0; a < 3; ++a) *reinterpret_cast<uint32_t*>(b + a * kKplPlane) = byte_plane_word(v, a);
+}
+// Byte offset of (dim d, position p % 64) in a swizzled V plane.
+__device__ __forceinline__ uint32_t vpl_off(int d, int p) {
+  return (uint32_t)d * 64u + ((uint32_t)(((p & 63) >> 4) ^ ((d >> 1) & 3)) << 4) + (uint32_t)(p & 15);
+}
+// One value element (dim d of position pos) into the V byte planes.
+__device__ __forceinline__ void vpl_put1(const KvView& kv, int layer, int head, int pos, int d, int32_t x) {
+  uint8_t* b = kv.vplane(layer, head, pos) + vpl_off(d, pos);
+  b[0] = (uint8_t)x;
+  b[kKplPlane] = (uint8_t)(x >> 8);
+  b[2 * kKplPlane] = (uint8_t)(x >> 16);
+}
+// Value elements d .. d + 3 of position pos.
+__device__ __forceinline__ void vpl_put4(const KvView& kv, int layer, int head, int pos, int d, int4 v) {
+  vpl_put1(kv, layer, head, pos, d, v.x);
+  vpl_put1(kv, layer, head, pos, d + 1, v.y);
+  vpl_put1(kv, layer, head, pos, d + 2, v.z);
+  vpl_put1(kv, layer, head, pos, d + 3, v.w);
 }
 // One key element.
 __device__ __forceinline__ void kpl_put1(const KvView& kv, int layer, int head, int pos, int d, int32_t x) {
