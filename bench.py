@@ -74,12 +74,12 @@ HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 # algorithmic bytes of one launch of each batched kernel (S sequences, the
 # attention at context `ctx`): what the kernel must move at least
 # ---------------------------------------------------------------------------
-def batch_kernel_bytes(kind: str, S: int, ctx: int, key_planes: bool = False) -> int:
+def batch_kernel_bytes(kind: str, S: int, ctx: int, planes: bool = False) -> int:
     """Algorithmic bytes of one launch: weights counted as Q4 (packed nibbles +
     u16 scales), K/V at the reference's 4 B per element; with
-    key_planes (the one-CTA-per-head attention of config 4) the cached keys are
-    read as their three byte planes (3 B per element) and the new key is
-    written both ways."""
+    planes (the one-CTA-per-head attention of config 4) the cached keys and
+    values are read as their three byte planes (3 B per element) and the new
+    key and value rows are written both ways."""
     limbs = 3 * S  # limb rows of a B matrix (u8)
 
     def q4(rows: int, k: int) -> int:
@@ -92,9 +92,9 @@ def batch_kernel_bytes(kind: str, S: int, ctx: int, key_planes: bool = False) ->
     if kind == "qkv_gemm":
         return q4(QKV_ROWS, HIDDEN) + limbs * HIDDEN + S * QKV_ROWS * 4
     if kind == "attention":
-        key_b = 3 if key_planes else 4
-        kv_read = 8 * (ctx - 1) * 128 * (key_b + 4)
-        new_rows = 8 * 128 * (2 * 4 + (3 if key_planes else 0))
+        elem_b = 3 if planes else 4
+        kv_read = 8 * (ctx - 1) * 128 * 2 * elem_b
+        new_rows = 8 * 128 * 2 * (4 + (3 if planes else 0))
         return S * (kv_read + new_rows + QKV_ROWS * 4 + 3 * 2 * HIDDEN)
     if kind == "o_proj_gemm":
         return q4(HIDDEN, 2 * HIDDEN) + limbs * 2 * HIDDEN + S * 3 * HIDDEN * 4

@@ -512,6 +512,10 @@ __global__ void __launch_bounds__(256, 4) batch_attn_kernel(BatchCtx c, int laye
   if (pos >= c.max_ctx) return;
   const int ctx = pos + 1;
   const KvView kvv = c.slots[m].kv;
+  if (!kvv.kpl || !kvv.vpl) {  // the model holds no byte planes (it allocates them where this kernel runs)
+    if (t == 0) atomicExch(c.err, 4);
+    return;
+  }
   const int nch = (pos + kTcKeys - 1) / kTcKeys;  // chunks of the cached positions [0, pos)
   const int nkp = 3 * nch;                        // key-plane loads, then as many value-plane loads
   const int total = 2 * nkp;

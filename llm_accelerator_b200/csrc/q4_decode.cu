@@ -1272,9 +1272,13 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   m->pages_per_seq = (cfg->max_context + kKvPage - 1) / kKvPage;
   const int64_t n_pages = (int64_t)m->pages_per_seq * cfg->max_seqs;
   if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
-  m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
-  if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
-  if ((rc = m->alloc(&m->v_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
+  // the byte-plane copies of K and V, for the batched attention that reads
+  // them (q4_batch.cu: attn_one_cta_per_head)
+  if (cfg->max_seqs * kKvHeads >= 148 && cfg->max_context <= 1024) {
+    m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
+    if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
+    if ((rc = m->alloc(&m->v_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
+  }
   if ((rc = m->alloc(&m->page_tables, (size_t)n_pages))) return fail(rc);
   {
     std::vector<int32_t> pt(n_pages);

@@ -26,6 +26,9 @@ struct KvView {
   // position) is swizzled like a 128-byte-swizzled K-major UMMA tile (16-byte
   // unit u of row r stored at unit u ^ (r % 8)), so a bulk copy of a plane's
   // rows is an operand as it lands.
+  // Both byte-plane copies exist only where the batched attention can read
+  // them (batches of at least 19 sequences, contexts up to 1024: null
+  // otherwise, and the writers skip them).
   uint8_t* kpl;
   int64_t kpl_page_bytes;  // layers * 8 * kKplHead
   // The values as byte planes the other way round, read by the tensor-core
@@ -61,6 +64,7 @@ __device__ __forceinline__ uint32_t byte_plane_word(int4 v, int l) {
 }
 // Key elements d .. d + 3 (d % 4 == 0) of position pos into the byte planes.
 __device__ __forceinline__ void kpl_put4(const KvView& kv, int layer, int head, int pos, int d, int4 v) {
+  if (!kv.kpl) return;
   uint8_t* b = kv.kplane(layer, head, pos) + kpl_off(pos & (kKvPage - 1), d);
 #pragma unroll
   for (int a = 0; a < 3; ++a) *reinterpret_cast<uint32_t*>(b + a * kKplPlane) = byte_plane_word(v, a);
@@ -71,6 +75,7 @@ __device__ __forceinline__ uint32_t vpl_off(int d, int p) {
 }
 // One value element (dim d of position pos) into the V byte planes.
 __device__ __forceinline__ void vpl_put1(const KvView& kv, int layer, int head, int pos, int d, int32_t x) {
+  if (!kv.vpl) return;
   uint8_t* b = kv.vplane(layer, head, pos) + vpl_off(d, pos);
   b[0] = (uint8_t)x;
   b[kKplPlane] = (uint8_t)(x >> 8);
@@ -78,6 +83,7 @@ __device__ __forceinline__ void vpl_put1(const KvView& kv, int layer, int head, 
 }
 // Value elements d .. d + 3 of position pos.
 __device__ __forceinline__ void vpl_put4(const KvView& kv, int layer, int head, int pos, int d, int4 v) {
+  if (!kv.vpl) return;
   vpl_put1(kv, layer, head, pos, d, v.x);
   vpl_put1(kv, layer, head, pos, d + 1, v.y);
   vpl_put1(kv, layer, head, pos, d + 2, v.z);
@@ -85,6 +91,7 @@ __device__ __forceinline__ void vpl_put4(const KvView& kv, int layer, int head, 
 }
 // One key element.
 __device__ __forceinline__ void kpl_put1(const KvView& kv, int layer, int head, int pos, int d, int32_t x) {
+  if (!kv.kpl) return;
   uint8_t* b = kv.kplane(layer, head, pos) + kpl_off(pos & (kKvPage - 1), d & ~3) + (d & 3);
   b[0] = (uint8_t)x;
   b[kKplPlane] = (uint8_t)(x >> 8);
