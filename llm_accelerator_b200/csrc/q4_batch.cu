@@ -2129,6 +2129,439 @@ __global__ void __launch_bounds__(256) batch_attn_cl_kernel(BatchCtx c, int laye
   attn_cl_body<false, kAttnRing>(c, SlotState{}, c.err, layer, g_q, g_k, cos_tab, sin_tab, exp_lut, kpr_cap);
 }
 
+// Cluster attention with tensor-core products (batched decode, models that
+// hold the K/V byte planes): the R CTAs of a cluster share one (KV head,
+// sequence) pair; rank r takes positions [r kpr, (r + 1) kpr) with kpr a
+// multiple of 128, scores and values them as batch_attn_kernel does (key and
+// value planes through a two-slot ring into M128 x N16 x K128 kind::i8
+// products, D and E in TMEM), and the exact softmax crosses the cluster as in
+// attn_cl_body: row maxima, then exp sums, then the int64 value sums of each
+// rank meet over DSMEM.  The rank whose range holds the current position
+// appends its K/V and scores it (and adds its value) on the CUDA cores.
+// Ranks take at most kClTcKprMax positions.
+constexpr int kClTcKprMax = 2048;
+__global__ void __launch_bounds__(256) batch_attn_cl_tc_kernel(BatchCtx c, int layer, const int32_t* __restrict__ g_q,
+                                                               const int32_t* __restrict__ g_k,
+                                                               const int32_t* __restrict__ cos_tab,
+                                                               const int32_t* __restrict__ sin_tab,
+                                                               const int32_t* __restrict__ exp_lut, int kpr_cap) {
+  extern __shared__ uint8_t cl_raw[];
+  const uint32_t raw_addr = umma::smem_addr(cl_raw);
+  uint8_t* sbase = cl_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* slots = sbase;                                   // [2][16 KB]
+  uint8_t* qb = sbase + 2 * kTcSlot;                        // [16][128] query bytes
+  int64_t* sc = reinterpret_cast<int64_t*>(qb + 16 * 128);  // [2][kpr_cap]; later the probability bytes
+  uint8_t* pb = reinterpret_cast<uint8_t*>(sc);
+  __shared__ __align__(16) int32_t hv[4][kHeadDim];
+  __shared__ uint32_t probtab[2][kExpLut];
+  __shared__ int64_t red[2][8];
+  __shared__ int64_t xmax[2], xsum[2];   // published to the cluster
+  __shared__ uint64_t full[2], empty[2], dfull, dempty, vdone;
+  __shared__ uint32_t tmem_slot;
+  __shared__ uint32_t ppos[2];
+  const int rank = blockIdx.x, nranks = gridDim.x, kv = blockIdx.y, m = blockIdx.z;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  // every rank reaches every cluster barrier below: no early return
+  const int pos = c.pos0[4 * m];
+  const KvView kvv = c.slots[m].kv;
+  const bool live = pos < c.max_ctx && kvv.kpl && kvv.vpl;
+  if (pos < c.max_ctx && !live && t == 0 && rank == 0) atomicExch(c.err, 4);
+  const int ctx = live ? pos + 1 : 0;
+  const int kpr = ((ctx + nranks - 1) / nranks + kTcKeys - 1) / kTcKeys * kTcKeys;
+  const int k0 = rank * kpr;
+  const int k1 = k0 + kpr < ctx ? k0 + kpr : ctx;  // this rank's positions [k0, k1)
+  const int nloc = k1 > k0 ? k1 - k0 : 0;
+  const int kend = k1 < pos ? k1 : pos;             // cached positions of the range
+  const int ncached = kend > k0 ? kend - k0 : 0;
+  const bool owner = live && pos >= k0 && pos < k1;
+  const int nch = (ncached + kTcKeys - 1) / kTcKeys;
+  const int nkp = 3 * nch, total = 2 * nkp;
+  auto issue = [&](int i) {
+    uint64_t* b = full + (i & 1);
+    uint8_t* dst = slots + (i & 1) * kTcSlot;
+    const int j = i < nkp ? i : i - nkp, ch = j / 3, a = j - 3 * ch, p0 = k0 + ch * kTcKeys;
+    if (i < nkp) {
+      const int n0 = kend - p0 < kKvPage ? kend - p0 : kKvPage;  // >= 1
+      int n1 = kend - p0 - kKvPage;
+      n1 = n1 < 0 ? 0 : (n1 > kKvPage ? kKvPage : n1);
+      umma::bar_expect_tx(b, (uint32_t)(n0 + n1) * 128u);
+      bulk_load(dst, kvv.kplane(layer, kv, p0) + a * kKplPlane, (uint32_t)n0 * 128u, b);
+      if (n1 > 0)
+        bulk_load(dst + kKplPlane, kvv.kplane(layer, kv, p0 + kKvPage) + a * kKplPlane, (uint32_t)n1 * 128u, b);
+    } else {
+      const bool two = p0 + kKvPage < kend;
+      umma::bar_expect_tx(b, (two ? 2u : 1u) * kKplPlane);
+      bulk_load(dst, kvv.vplane(layer, kv, p0) + a * kKplPlane, kKplPlane, b);
+      if (two) bulk_load(dst + kKplPlane, kvv.vplane(layer, kv, p0 + kKvPage) + a * kKplPlane, kKplPlane, b);
+    }
+  };
+  if (t == 0) {
+    umma::bar_init(full, 1);
+    umma::bar_init(full + 1, 1);
+    umma::bar_init(empty, 1);
+    umma::bar_init(empty + 1, 1);
+    umma::bar_init(&dfull, 1);
+    umma::bar_init(&dempty, 4);
+    umma::bar_init(&vdone, 1);
+    umma::bar_init_fence();
+    for (int i = 0; i < total && i < 2; ++i) issue(i);
+  }
+  if (warp == 1) umma::tmem_alloc(&tmem_slot, kTcCols);
+  for (int e = t; e < kExpLut; e += blockDim.x) probtab[0][e] = (uint32_t)exp_lut[e];
+  grid_dep_wait();
+  grid_dep_launch();
+  if (live) {
+    const int32_t* raw = c.qkv_raw + (size_t)m * (kQRows + 2 * kKvRows);
+    if (warp < 2) {
+      reinterpret_cast<int4*>(hv[warp])[lane] =
+          head_norm_rope(raw + (2 * kv + warp) * kHeadDim, g_q, cos_tab, sin_tab, pos, lane);
+    } else if (warp == 2) {
+      const int4 k4 = head_norm_rope(raw + kQRows + kv * kHeadDim, g_k, cos_tab, sin_tab, pos, lane);
+      reinterpret_cast<int4*>(hv[2])[lane] = k4;
+      if (owner) {
+        reinterpret_cast<int4*>(kvv.at(layer, 0, kv, pos))[lane] = k4;
+        kpl_put4(kvv, layer, kv, pos, 4 * lane, k4);
+      }
+    } else if (warp == 3) {
+      const int4 v4 = reinterpret_cast<const int4*>(raw + kQRows + kKvRows + kv * kHeadDim)[lane];
+      reinterpret_cast<int4*>(hv[3])[lane] = v4;
+      if (owner) {
+        reinterpret_cast<int4*>(kvv.at(layer, 1, kv, pos))[lane] = v4;
+        vpl_put4(kvv, layer, kv, pos, 4 * lane, v4);
+      }
+    }
+  }
+  __syncthreads();
+  {
+    const int r = t >> 4, d0 = 8 * (t & 15);
+    uint32_t w0 = 0, w1 = 0;
+    if (r < 6) {
+      const int h = r >= 3, b = r - 3 * h;
+      const int4 lo = *reinterpret_cast<const int4*>(&hv[h][d0]);
+      const int4 hi = *reinterpret_cast<const int4*>(&hv[h][d0 + 4]);
+      const int4 bl = make_int4(lo.x + (1 << 23), lo.y + (1 << 23), lo.z + (1 << 23), lo.w + (1 << 23));
+      const int4 bh = make_int4(hi.x + (1 << 23), hi.y + (1 << 23), hi.z + (1 << 23), hi.w + (1 << 23));
+      w0 = byte_plane_word(bl, b);
+      w1 = byte_plane_word(bh, b);
+    } else if (r == 6) {
+      w0 = w1 = 0x01010101u;
+    }
+    *reinterpret_cast<uint2*>(qb + kpl_off(r, d0)) = make_uint2(w0, w1);
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = tmem_slot;
+  bool ok = true;
+  int64_t mx0 = INT64_MIN, mx1 = INT64_MIN;
+  // the current position's scores (warp 5 of the owner); sc is indexed by p - k0
+  if (warp == 5 && owner) {
+    const int4 k4 = *reinterpret_cast<const int4*>(&hv[2][4 * lane]);
+    const int4 qa = *reinterpret_cast<const int4*>(&hv[0][4 * lane]);
+    const int4 qc = *reinterpret_cast<const int4*>(&hv[1][4 * lane]);
+    int64_t s0 = 0, s1 = 0;
+    s0 = mad_wide(qa.x, k4.x, s0);
+    s0 = mad_wide(qa.y, k4.y, s0);
+    s0 = mad_wide(qa.z, k4.z, s0);
+    s0 = mad_wide(qa.w, k4.w, s0);
+    s1 = mad_wide(qc.x, k4.x, s1);
+    s1 = mad_wide(qc.y, k4.y, s1);
+    s1 = mad_wide(qc.z, k4.z, s1);
+    s1 = mad_wide(qc.w, k4.w, s1);
+    s0 = warp_sum_i64(s0);
+    s1 = warp_sum_i64(s1);
+    if (lane == 0) {
+      mx0 = scale_score(s0, kScoreScale);
+      mx1 = scale_score(s1, kScoreScale);
+      sc[pos - k0] = mx0;
+      sc[kpr_cap + pos - k0] = mx1;
+    }
+  }
+  if (t == 128) {
+    const uint64_t qdesc = umma::sw128_desc(umma::smem_addr(qb));
+    for (int i = 0; i < nkp && ok; ++i) {
+      const int ch = i / 3, a = i - 3 * ch;
+      if (a == 0 && ch > 0 && !umma::bar_wait(&dempty, (ch - 1) & 1)) ok = false;
+      if (ok && !umma::bar_wait(full + (i & 1), (i >> 1) & 1)) ok = false;
+      if (!ok) break;
+      umma::fence_after_sync();
+      const uint64_t kdesc = umma::sw128_desc(umma::smem_addr(slots + (i & 1) * kTcSlot));
+      const uint32_t idesc = umma::i8_idesc_ab(kTcKeys, 16, a == 2, false);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        umma::mma_i8(tmem + 16u * a, kdesc + (uint64_t)(2 * kk), qdesc + (uint64_t)(2 * kk), idesc, kk > 0);
+      umma::mma_commit(empty + (i & 1));
+      if (a == 2) umma::mma_commit(&dfull);
+      if (i + 2 < total) {
+        if (!umma::bar_wait(empty + (i & 1), (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        issue(i + 2);
+      }
+    }
+  }
+  for (int ch = 0; ch < nch && warp < 4; ++ch) {
+    if (!__all_sync(0xFFFFFFFFu, umma::bar_wait(&dfull, ch & 1))) {
+      ok = false;
+      break;
+    }
+    umma::fence_after_sync();
+    int32_t d[3][8];
+    const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16);
+#pragma unroll
+    for (int a = 0; a < 3; ++a) umma::tmem_ld<8>(lb + 16u * a, d[a]);
+    umma::tmem_ld_wait();
+    umma::fence_before_sync();
+    __syncwarp();
+    if (lane == 0) umma::bar_arrive(&dempty);
+    const int lk = ch * kTcKeys + 32 * warp + lane;  // local index
+    if (lk < ncached) {
+      int64_t s0 = 0, s1 = 0;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        const int64_t bias = (int64_t)d[a][6] << 23;
+        const int64_t t0 = (int64_t)d[a][0] + ((int64_t)d[a][1] << 8) + ((int64_t)d[a][2] << 16) - bias;
+        const int64_t t1 = (int64_t)d[a][3] + ((int64_t)d[a][4] << 8) + ((int64_t)d[a][5] << 16) - bias;
+        s0 += t0 << (8 * a);
+        s1 += t1 << (8 * a);
+      }
+      const int64_t v0 = scale_score(s0, kScoreScale), v1 = scale_score(s1, kScoreScale);
+      sc[lk] = v0;
+      sc[kpr_cap + lk] = v1;
+      mx0 = v0 > mx0 ? v0 : mx0;
+      mx1 = v1 > mx1 ? v1 : mx1;
+    }
+  }
+  // maxima: block, then cluster
+#pragma unroll
+  for (int msk = 1; msk < 32; msk <<= 1) {
+    const int64_t o0 = shfl_xor_i64(mx0, msk), o1 = shfl_xor_i64(mx1, msk);
+    mx0 = o0 > mx0 ? o0 : mx0;
+    mx1 = o1 > mx1 ? o1 : mx1;
+  }
+  if (lane == 0) {
+    red[0][warp] = mx0;
+    red[1][warp] = mx1;
+  }
+  __syncthreads();
+  if (t < 2) {
+    int64_t b = red[t][0];
+    for (int w = 1; w < 8; ++w) b = red[t][w] > b ? red[t][w] : b;
+    xmax[t] = b;
+  }
+  umma::cluster_sync();  // every rank's maxima are published
+  if (warp == 0) {
+    int64_t o0 = INT64_MIN, o1 = INT64_MIN;
+    if (lane < nranks) {
+      o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[0]), (uint32_t)lane));
+      o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xmax[1]), (uint32_t)lane));
+    }
+#pragma unroll
+    for (int msk = 1; msk < 32; msk <<= 1) {
+      const int64_t a = shfl_xor_i64(o0, msk), b = shfl_xor_i64(o1, msk);
+      o0 = a > o0 ? a : o0;
+      o1 = b > o1 ? b : o1;
+    }
+    if (lane == 0) {
+      red[0][0] = o0;
+      red[1][0] = o1;
+    }
+  }
+  __syncthreads();
+  mx0 = red[0][0];
+  mx1 = red[1][0];
+  // LUT indices and exp sums of the range
+  int64_t sum0 = 0, sum1 = 0;
+  for (int lp = t; lp < nloc; lp += blockDim.x) {
+    const int i0 = lut_index(mx0, sc[lp]), i1 = lut_index(mx1, sc[kpr_cap + lp]);
+    sc[lp] = i0;
+    sc[kpr_cap + lp] = i1;
+    sum0 += probtab[0][i0];
+    sum1 += probtab[0][i1];
+  }
+  sum0 = warp_sum_i64(sum0);
+  sum1 = warp_sum_i64(sum1);
+  __syncthreads();  // red reused
+  if (lane == 0) {
+    red[0][warp] = sum0;
+    red[1][warp] = sum1;
+  }
+  __syncthreads();
+  if (t < 2) {
+    int64_t b = 0;
+    for (int w = 0; w < 8; ++w) b += red[t][w];
+    xsum[t] = b;
+  }
+  umma::cluster_sync();  // every rank's sums are published
+  if (warp == 0) {
+    int64_t o0 = 0, o1 = 0;
+    if (lane < nranks) {
+      o0 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[0]), (uint32_t)lane));
+      o1 = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(&xsum[1]), (uint32_t)lane));
+    }
+    o0 = warp_sum_i64(o0);
+    o1 = warp_sum_i64(o1);
+    if (lane == 0) {
+      red[0][1] = o0;
+      red[1][1] = o1;
+    }
+  }
+  __syncthreads();
+  sum0 = red[0][1];
+  sum1 = red[1][1];
+  if (live) {
+    // warps 4-7 build head 1's table from the LUT in probtab[0]; warps 0-3
+    // compute head 0's in registers and overwrite the LUT after the barrier
+    const int h = t >> 7, e0 = t & 127;
+    const uint64_t dd = (uint64_t)(h ? sum1 : sum0), rc = ~0ULL / dd;
+    uint32_t p0[3] = {0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int e = e0 + 128 * k;
+      if (e < kExpLut) {
+        const uint32_t v = barrett_div((uint64_t)probtab[0][e] << 16, dd, rc);
+        if (h)
+          probtab[1][e] = v;
+        else
+          p0[k] = v;
+      }
+    }
+    __syncthreads();
+    if (h == 0) {
+#pragma unroll
+      for (int k = 0; k < 3; ++k)
+        if (e0 + 128 * k < kExpLut) probtab[0][e0 + 128 * k] = p0[k];
+    }
+  } else {
+    __syncthreads();
+  }
+  __syncthreads();
+  // probabilities of the range into registers (nloc <= kClTcKprMax: 8 per
+  // thread), then the index array becomes the probability bytes (as
+  // batch_attn_kernel)
+  uint32_t pr[kClTcKprMax / 256][2];
+#pragma unroll
+  for (int j = 0; j < kClTcKprMax / 256; ++j) {
+    const int lp = t + 256 * j;
+    pr[j][0] = pr[j][1] = 0;
+    if (lp < nloc) {
+      pr[j][0] = probtab[0][(int)sc[lp]];
+      pr[j][1] = probtab[1][(int)sc[kpr_cap + lp]];
+      if (owner && lp == pos - k0) {
+        ppos[0] = pr[j][0];
+        ppos[1] = pr[j][1];
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = t; i < nch * 128; i += blockDim.x) reinterpret_cast<uint4*>(pb)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < kClTcKprMax / 256; ++j) {
+    const int lp = t + 256 * j;
+    if (lp < ncached) {
+      uint8_t* tile = pb + (lp >> 7) * 2048;
+      const int k = lp & 127;
+#pragma unroll
+      for (int r = 0; r < 6; ++r) {
+        const uint32_t v = pr[j][r >= 3] >> (8 * (r % 3));
+        if (v & 0xFFu) tile[r * 128 + (((k >> 4) ^ (r & 7)) << 4) + (k & 15)] = (uint8_t)v;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  if (t == 128) {
+    const uint64_t pdesc = umma::sw128_desc(umma::smem_addr(pb));
+    for (int j = 0; j < nkp && ok; ++j) {
+      const int i = nkp + j, ch = j / 3, a = j - 3 * ch;
+      if (!umma::bar_wait(full + (i & 1), (i >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      umma::fence_after_sync();
+      const uint32_t sa = umma::smem_addr(slots + (i & 1) * kTcSlot);
+      const uint32_t idesc = umma::i8_idesc_ab(kTcKeys, 16, a == 2, false);
+      const bool two = k0 + ch * kTcKeys + kKvPage < kend;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (kk >= 2 && !two) break;
+        const uint64_t vdesc = sw64_desc(sa + (kk >> 1) * kKplPlane) + (uint64_t)(2 * (kk & 1));
+        const uint64_t bdesc = pdesc + (uint64_t)((ch * 2048 + 32 * kk) >> 4);
+        umma::mma_i8(tmem + kTcVal + 16u * a, vdesc, bdesc, idesc, (ch | kk) != 0);
+      }
+      umma::mma_commit(empty + (i & 1));
+      if (i + 2 < total) {
+        if (!umma::bar_wait(empty + (i & 1), (i >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        issue(i + 2);
+      }
+    }
+    umma::mma_commit(&vdone);
+  }
+  // this rank's value sums (warps 0-3: dims 32 w .. +31), published from
+  // the ring, idle once the value MMAs are done
+  int64_t* part = reinterpret_cast<int64_t*>(slots);         // [2][128]
+  int64_t* gsum = reinterpret_cast<int64_t*>(slots) + 256;   // [nranks][per]
+  if (warp < 4) {
+    const int d = 32 * warp + lane;
+    int64_t o0 = 0, o1 = 0;
+    const bool got = __all_sync(0xFFFFFFFFu, umma::bar_wait(&vdone, 0));
+    if (!got) ok = false;
+    umma::fence_after_sync();
+    if (nch > 0 && got) {
+      int32_t e[3][8];
+      const uint32_t lb = tmem + ((uint32_t)(32 * warp) << 16) + kTcVal;
+#pragma unroll
+      for (int a = 0; a < 3; ++a) umma::tmem_ld<8>(lb + 16u * a, e[a]);
+      umma::tmem_ld_wait();
+#pragma unroll
+      for (int a = 0; a < 3; ++a) {
+        o0 += ((int64_t)e[a][0] + ((int64_t)e[a][1] << 8) + ((int64_t)e[a][2] << 16)) << (8 * a);
+        o1 += ((int64_t)e[a][3] + ((int64_t)e[a][4] << 8) + ((int64_t)e[a][5] << 16)) << (8 * a);
+      }
+    }
+    if (owner) {
+      o0 += (int64_t)ppos[0] * hv[3][d];
+      o1 += (int64_t)ppos[1] * hv[3][d];
+    }
+    part[d] = o0;
+    part[kHeadDim + d] = o1;
+  }
+  if (!ok) atomicExch(c.err, 4);
+  umma::fence_before_sync();
+  umma::cluster_sync();  // every rank's value sums are published
+  {
+    // rank r finishes outputs [r per, (r + 1) per) of the 2 x 128 (any
+    // cluster size): one DSMEM load per (source rank, output)
+    const int per = (2 * kHeadDim + nranks - 1) / nranks;
+    for (int i = t; i < nranks * per; i += blockDim.x) {
+      const int src = i / per, o = rank * per + (i - src * per);
+      if (o < 2 * kHeadDim) gsum[i] = umma::cluster_ld64(umma::cluster_map(umma::smem_addr(part + o), (uint32_t)src));
+    }
+    __syncthreads();
+    for (int j = t; j < per && live; j += blockDim.x) {
+      const int oo = rank * per + j;
+      if (oo >= 2 * kHeadDim) break;
+      int64_t acc = 0;
+      for (int r = 0; r < nranks; ++r) acc += gsum[r * per + j];
+      const int h = oo >> 7, d = oo & (kHeadDim - 1);
+      write_limbs(c.bt2, c.SP, 2 * kHidden, m, (2 * kv + h) * kHeadDim + d, sat24(acc >> 16));
+    }
+  }
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, kTcCols);
+  }
+  umma::cluster_sync();  // no rank leaves while another still reads its shared memory
+}
+
 // Attention of the per-stage batch-1 path (grid: ranks x 8 KV heads, one cluster per head).
 // 128 CTAs leave room for a 4-slot ring: a rank's keys of a 513-position
 // context (2 K + 2 V chunks) are all in flight at once.
@@ -2653,6 +3086,22 @@ int attn_cl_kpr(const BatchPlan& p) {
   return ((p.max_ctx + r - 1) / r + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
 }
 bool attn_cluster(const BatchPlan& p) { return !attn_one_cta_per_head(p) && attn_cl_kpr(p) <= kClKprMax; }
+// Tensor-core cluster attention (models with byte planes): positions per rank
+// (a multiple of 128) and dynamic shared memory for R ranks, and the largest
+// R <= 16 whose R x 8 x S CTAs fit the GPU at once (TMEM: 4 CTAs per SM;
+// shared memory: the kernel's 4.3 KB static, 1 KB reserved), 0 if none.
+int attn_cl_tc_kpr(const BatchPlan& p, int R) { return ((p.max_ctx + R - 1) / R + kTcKeys - 1) / kTcKeys * kTcKeys; }
+size_t attn_cl_tc_smem(const BatchPlan& p, int R) { return (size_t)kTcSmemFixed + (size_t)16 * attn_cl_tc_kpr(p, R); }
+int attn_cl_tc_ranks(const BatchPlan& p) {
+  if (!p.kv_planes || attn_one_cta_per_head(p)) return 0;
+  for (int R = 16; R >= 2; --R) {
+    if (attn_cl_tc_kpr(p, R) > kClTcKprMax) break;
+    const size_t per_cta = attn_cl_tc_smem(p, R) + 4608 + 1024;
+    const int by_smem = (int)(233472 / per_cta), per_sm = by_smem < 4 ? by_smem : 4;
+    if (R * kKvHeads * p.S <= 148 * per_sm) return R;
+  }
+  return 0;
+}
 size_t attn_cl_smem(const BatchPlan& p) {
   return (size_t)kAttnRing * kAttnChunkBytes + (size_t)2 * attn_cl_kpr(p) * 8;
 }
@@ -2699,6 +3148,10 @@ int enqueue_t(const BatchPlan& p, cudaStream_t s, BatchMarks* mk) {
     if (one_cta_per_head) {
       BQ(launch_pdl(batch_attn_kernel, dim3(kKvHeads, p.S), dim3(256), ring_smem, s, c, l, w.g_q, w.g_k, p.cos_tab,
                     p.sin_tab, p.exp_lut));
+    } else if (attn_cl_tc_ranks(p) > 0) {
+      const int R = attn_cl_tc_ranks(p);
+      BQ(launch_cluster_x(batch_attn_cl_tc_kernel, dim3(R, kKvHeads, p.S), dim3(256), attn_cl_tc_smem(p, R), s, R, c,
+                          l, w.g_q, w.g_k, p.cos_tab, p.sin_tab, p.exp_lut, attn_cl_tc_kpr(p, R)));
     } else if (attn_cluster(p)) {
       BQ(launch_cluster_x(batch_attn_cl_kernel, dim3(attn_cl_ranks(p), kKvHeads, p.S), dim3(256), attn_cl_smem(p),
                           s, attn_cl_ranks(p), c, l, w.g_q, w.g_k, p.cos_tab, p.sin_tab, p.exp_lut, attn_cl_kpr(p)));
@@ -2772,6 +3225,12 @@ template <int SP>
 int setup_t(const BatchPlan& p) {
   int rc;
   if ((rc = gemm_setup())) return rc;
+  if (attn_cl_tc_ranks(p) > 0) {
+    const int R = attn_cl_tc_ranks(p);
+    BQ(cudaFuncSetAttribute(batch_attn_cl_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            (int)attn_cl_tc_smem(p, R)));
+    BQ(cudaFuncSetAttribute(batch_attn_cl_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  }
   if (attn_cluster(p)) {
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_cl_smem(p)));
     BQ(cudaFuncSetAttribute(batch_attn_cl_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));

@@ -78,6 +78,7 @@ struct BatchPlan {
   unsigned long long* trace;  // optional attention timeline, [layers, S, 8, 8] (nullptr = off)
   unsigned long long* gemm_trace;  // optional GEMM timeline, [4 layers + 1, kGemmTraceCtas, 8]
   int32_t* final_act;    // hidden-only step when set: final-norm Q12.12 [S, 1024], no LM head / argmax
+  int kv_planes;         // the model holds K/V byte planes (KvView::kpl / vpl)
 };
 
 // LM head over one vocabulary shard [row_begin, row_end) for n_act vectors.

@@ -996,6 +996,7 @@ int batch_plan(q4gpu_model* m, int first, int S, BatchPlan& p) {
   p.layers = m->b_layers;
   p.n_layers = m->cfg.n_layers;
   p.max_ctx = m->cfg.max_context;
+  p.kv_planes = m->kv_planes != nullptr;
   p.vocab = m->cfg.vocab;
   p.cos_tab = m->cos_tab;
   p.sin_tab = m->sin_tab;
@@ -1272,9 +1273,10 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   m->pages_per_seq = (cfg->max_context + kKvPage - 1) / kKvPage;
   const int64_t n_pages = (int64_t)m->pages_per_seq * cfg->max_seqs;
   if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
-  // the byte-plane copies of K and V, for the batched attention that reads
-  // them (q4_batch.cu: attn_one_cta_per_head)
-  if (cfg->max_seqs * kKvHeads >= 148 && cfg->max_context <= 1024) {
+  // the byte-plane copies of K and V, for the batched attention kernels that
+  // read them (q4_batch.cu: batch_attn_kernel, batch_attn_cl_tc_kernel); a
+  // one-slot model decodes on the batch-1 paths, which do not
+  if (cfg->max_seqs >= 2) {
     m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
     if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
     if ((rc = m->alloc(&m->v_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);

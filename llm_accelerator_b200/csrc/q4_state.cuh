@@ -26,9 +26,9 @@ struct KvView {
   // position) is swizzled like a 128-byte-swizzled K-major UMMA tile (16-byte
   // unit u of row r stored at unit u ^ (r % 8)), so a bulk copy of a plane's
   // rows is an operand as it lands.
-  // Both byte-plane copies exist only where the batched attention can read
-  // them (batches of at least 19 sequences, contexts up to 1024: null
-  // otherwise, and the writers skip them).
+  // Both byte-plane copies exist only in models with two or more sequence
+  // slots, where the batched attention reads them (null otherwise, and the
+  // writers skip them).
   uint8_t* kpl;
   int64_t kpl_page_bytes;  // layers * 8 * kKplHead
   // The values as byte planes the other way round, read by the tensor-core
