@@ -438,13 +438,15 @@ def cfg5_secondary(device: int, peak_gbs: float, steps: int = 16, check: bool = 
                   if not bad else f"MISMATCH {bad[:4]}")
     m.close()
     att_ms = kt["attention"][0]
-    gbs = batch_kernel_bytes("attention", CFG5_SEQS, ctx) / (att_ms * 1e-3) / 1e9
+    gbs = batch_kernel_bytes("attention", CFG5_SEQS, ctx, True) / (att_ms * 1e-3) / 1e9
     out = {"workload": "cfg5: 8 sequences x 8192-token uniform prompts (seeds 50000..), batched exact prefill, "
                        "greedy decode from position 8192, full vocabulary on one GPU",
            "value": round(CFG5_SEQS * steps / (ms / 1000.0), 2), "unit": UNIT, "ms_per_step": round(ms / steps, 4),
            "steps": steps, "prefill_s": round(prefill_s, 3),
            "prefill_prompt_tokens_per_s": round(CFG5_SEQS * CFG5_PROMPT / prefill_s, 1),
-           "attention": {"kernel": "batch_attn_cl_kernel (8-CTA clusters)", "ms_per_launch": round(att_ms, 5),
+           "attention": {"kernel": "batch_attn_cl_tc_kernel (9-CTA clusters, tcgen05 products on the K/V byte "
+                                   "planes)", "ms_per_launch": round(att_ms, 5),
+                         "timing": "kernels serialised by events (q4gpu_batch_time_kernels)",
                          "context": ctx, "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)},
            "first_tokens_seq0": toks}
     if parity is not None:
