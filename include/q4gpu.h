@@ -275,7 +275,7 @@ typedef struct q4gpu_model_config {
 /* Create a context: allocates weights, the paged KV pool, activations and
  * workspace on `device`.  Weights start zeroed; fill them with
  * q4gpu_model_init_synthetic or q4gpu_model_set_tensor.  With max_seqs >= 2
- * the pool also holds K and V as byte planes for the batched attention's
+ * or max_context > 1024 the pool also holds K and V as byte planes for the batched attention's
  * tensor-core products: 0.75x the int32 cache's bytes more (28 layers, per 64
  * positions of a sequence slot: 14 MiB int32 + 10.5 MiB). */
 int q4gpu_model_create(const q4gpu_model_config *cfg, q4gpu_model **out);

@@ -1274,9 +1274,11 @@ int q4gpu_model_create(const q4gpu_model_config* cfg, q4gpu_model** out) {
   const int64_t n_pages = (int64_t)m->pages_per_seq * cfg->max_seqs;
   if ((rc = m->alloc(&m->kv_pool, (size_t)n_pages * m->page_elems))) return fail(rc);
   // the byte-plane copies of K and V, for the batched attention kernels that
-  // read them (q4_batch.cu: batch_attn_kernel, batch_attn_cl_tc_kernel); a
-  // one-slot model decodes on the batch-1 paths, which do not
-  if (cfg->max_seqs >= 2) {
+  // read them (q4_batch.cu: batch_attn_kernel, batch_attn_cl_tc_kernel): in
+  // multi-slot models and long contexts (the vocabulary-sharded long-context
+  // decode runs one sequence per GPU through the batched path); a one-slot
+  // model up to 1024 positions decodes on the batch-1 paths, which read none
+  if (cfg->max_seqs >= 2 || cfg->max_context > 1024) {
     m->kpl_page_bytes = (int64_t)L * kKvHeads * kKplHead;
     if ((rc = m->alloc(&m->kv_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);
     if ((rc = m->alloc(&m->v_planes, (size_t)n_pages * m->kpl_page_bytes))) return fail(rc);

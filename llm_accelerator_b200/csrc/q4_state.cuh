@@ -27,8 +27,8 @@ struct KvView {
   // unit u of row r stored at unit u ^ (r % 8)), so a bulk copy of a plane's
   // rows is an operand as it lands.
   // Both byte-plane copies exist only in models with two or more sequence
-  // slots, where the batched attention reads them (null otherwise, and the
-  // writers skip them).
+  // slots or more than 1024 positions, where the batched attention reads
+  // them (null otherwise, and the writers skip them).
   uint8_t* kpl;
   int64_t kpl_page_bytes;  // layers * 8 * kKplHead
   // The values as byte planes the other way round, read by the tensor-core
