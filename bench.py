@@ -76,7 +76,7 @@ HIDDEN, QKV_ROWS, INTER = 1024, 4096, 3072
 # ---------------------------------------------------------------------------
 def batch_kernel_bytes(kind: str, S: int, ctx: int, planes: bool = False) -> int:
     """Algorithmic bytes of one launch: weights counted as Q4 (packed nibbles +
-    u16 scales), K/V at the reference's 4 B per element; with
+    u16 scales, the reference's storage), K/V at the reference's 4 B per element; with
     planes (the one-CTA-per-head attention of config 4) the cached keys and
     values are read as their three byte planes (3 B per element) and the new
     key and value rows are written both ways."""
