@@ -440,8 +440,9 @@ __global__ void __launch_bounds__(256) batch_attn_values_kernel(BatchCtx c, Attn
 // exact two-pass LUT softmax for the two query heads of the group; writes the
 // output and its limbs (the o_proj B matrix).  256 threads.  Used when the
 // batch has enough (KV head, sequence) pairs to fill the GPU and contexts up
-// to 1024; smaller batches and longer contexts use the cluster kernel
-// (batch_attn_cl_kernel), the longest ones the split-KV kernels above.
+// to 1024; smaller batches and longer contexts use the cluster kernels
+// (batch_attn_cl_tc_kernel with byte planes, batch_attn_cl_kernel without),
+// the longest ones the split-KV kernels above.
 //
 // Scores on the tensor cores.  With the query split into the unsigned byte
 // limbs c_b of c = q + 2^23 and the cached key into its byte planes k_a
@@ -470,7 +471,7 @@ constexpr int kAttnChunkBytes = kAttnChunk * kHeadDim * 4;
 constexpr int kAttnRing = 2;
 constexpr int kStageAttnRing = 4;
 constexpr int kTcKeys = 128;                  // keys per score chunk (the MMA's M)
-constexpr int kTcSlot = 16384;                // ring slot: one key plane of a chunk, or 32 V rows
+constexpr int kTcSlot = 16384;                // ring slot: one key or value plane of a 128-position chunk
 constexpr int kTcSmemFixed = 1024 + 2 * kTcSlot + 16 * 128;  // alignment slack, ring, query bytes
 constexpr uint32_t kTcCols = 128;             // TMEM columns: D (scores) at 0, E (values) at 64, 3 planes x 16
 constexpr uint32_t kTcVal = 64;
